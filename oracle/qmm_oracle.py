@@ -1,0 +1,508 @@
+"""CPU oracle for the quantized-matmul hot path -- TEST INFRASTRUCTURE ONLY.
+
+Nothing in the product path imports this module. Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` use it, and only as the checker or as the timed CPU
+restatement of the reference's own numpy path.
+
+It restates, in numpy, the numerics of loom-fun/loom-skills for this path (paths relative to the reference root):
+
+* block formats and their dequantisation
+  - Q4_0     ``skills/loom-port-llm/starter/quant_values.loom:386-408`` (@g_q4_0_values), ``formats.py:8``
+  - Q4_K     ``skills/loom-port-llm/starter/gen_llm.py:234-315`` (@g_k_scale_minimum, @g_k_metadata, @g_q4_k_values)
+  - IQ4_NL   ``skills/loom-port-llm/starter/quant_values.loom:18-91``
+  - MXFP4    ``skills/loom-port-llm/starter/gen_llm.py:786-895`` (ggml 17-byte blocks, split16 order) and
+             ``skills/loom-port-llm/starter/st_tensors.py:26-35`` (split planes, pairs order)
+  The Q4_K / IQ4_NL / MXFP4 arithmetic is the third-party ``gguf`` package's (gguf-py 0.19.0, installed unpinned by
+  ``skills/loom-setup/scripts/install_loom.sh:118``; called at ``make_kernel_tests.py:15-16, 45-47``). This file
+  restates that published algorithm; ``tests/test_oracle.py`` pins it against gguf 0.19.0 bit for bit.
+* the f16 GEMM staging (one rounding): ``moe_q4_0.py:11-38``, ``gen_gemm.py:159-279`` (IQ4), ``gen_gemm.py:499-532`` (Q4_K)
+* activation producers: ``gen_llm.py:1843-1912`` (g_row_scale_f16), ``gen_mxfp4s.py:852-870`` (F8_SCALE),
+  e4m3 rounding ``make_kernel_tests.py:2006-2019``; MXFP4 -> e5m2 decode ``gen_mxfp4s.py:14-48``
+* products: ``make_kernel_tests.py:45-47, 231-238`` (matvec), ``:1860-1876`` (GEMM: (x16 . W^T) * inv)
+* MoE: router ``gen_moe.py:116-253``, bucket ``gen_moe.py:829-955``, grouped GEMM ``gen_moe.py:1126-1228``,
+  combine ``gen_moe.py:730-762, 1231-1280``, reference F64 pipeline ``.github/devlab/kbench/moe_q4_0/gen_bench.py:185-248``.
+
+The quantisers below are test-input generators (seeded synthetic weights), not part of the reference path:
+Q4_0 restates gguf's quantiser; Q4_K, IQ4_NL and MXFP4 are this repository's own (gguf 0.19.0 cannot quantise Q4_K
+or IQ4_NL, and its MXFP4 quantiser picks max/scale in [4, 8) and saturates, which the MXFP4 config rules out).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+QK = {"q4_0": 32, "q4_k": 256, "iq4_nl": 32, "mxfp4": 32}          # values per block (formats.py:16-17)
+BLOCK_BYTES = {"q4_0": 18, "q4_k": 144, "iq4_nl": 18, "mxfp4": 17}  # bytes per block (formats.py:5-10)
+GGML_TYPE = {"q4_0": 2, "q4_k": 12, "iq4_nl": 20, "mxfp4": 39}      # gguf.GGMLQuantizationType ids
+IQ4_KVALUES = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int64)
+E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float64)
+MXFP4_F8_SHIFT = 8                      # gen_mxfp4s.py:29
+MXFP4_F8_E_MIN, MXFP4_F8_E_MAX = 107, 132
+
+
+def row_bytes(fmt, k):
+    """Packed bytes of one weight row of k values (gen_moe.py:70-71)."""
+    assert k % QK[fmt] == 0, (fmt, k)
+    return k // QK[fmt] * BLOCK_BYTES[fmt]
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# quantisers (seeded test-input generators)
+# ------------------------------------------------------------------------------------------------------------------
+def quantize_q4_0(w):
+    """float32 [..., k] -> packed Q4_0 bytes [..., k/32*18]. Restates gguf 0.19.0 quants.Q4_0.quantize_blocks:
+    d = (value of largest magnitude) / -8, q = clip(trunc(x/d + 8.5), 0, 15), d stored as f16."""
+    w = np.asarray(w, np.float32)
+    lead = w.shape[:-1]
+    blocks = w.reshape(-1, 32)
+    imax = np.abs(blocks).argmax(axis=-1)[:, None]
+    mx = np.take_along_axis(blocks, imax, axis=-1)
+    d = mx / np.float32(-8)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    q = np.trunc(blocks * inv + np.float32(8.5)).astype(np.float32).astype(np.uint8).clip(0, 15)
+    packed = q[:, :16] | (q[:, 16:] << np.uint8(4))
+    out = np.concatenate([d.astype(np.float16).view(np.uint8), packed], axis=-1)
+    return out.reshape(*lead, -1)
+
+
+def _pack_k_scales(sc, mn):
+    """8 six-bit scales and minima -> the 12-byte K-quant scale field (layout of gguf Q4_K.get_scale_min)."""
+    sc = sc.astype(np.uint8)
+    mn = mn.astype(np.uint8)
+    out = np.zeros(sc.shape[:-1] + (12,), np.uint8)
+    out[..., 0:4] = (sc[..., 0:4] & 63) | ((sc[..., 4:8] >> 4) << 6)
+    out[..., 4:8] = (mn[..., 0:4] & 63) | ((mn[..., 4:8] >> 4) << 6)
+    out[..., 8:12] = (sc[..., 4:8] & 15) | ((mn[..., 4:8] & 15) << 4)
+    return out
+
+
+def quantize_q4_k(w):
+    """float32 [..., k] -> packed Q4_K bytes [..., k/256*144] (this repository's own min/max quantiser).
+
+    Per 32-value group: scale = (max - min)/15, minimum = -min(0, min); super-block d = max scale/63, dmin = max
+    minimum/63 (f16); 6-bit codes sc = round(scale/d), m = round(minimum/dmin); q = round((x + dmin*m)/(d*sc))."""
+    w = np.asarray(w, np.float32)
+    lead = w.shape[:-1]
+    g = w.reshape(-1, 8, 32).astype(np.float64)
+    lo = np.minimum(g.min(-1), 0.0)
+    hi = g.max(-1)
+    scale = (hi - lo) / 15.0
+    minimum = -lo
+    d16 = (scale.max(-1) / 63.0).astype(np.float16)
+    dm16 = (minimum.max(-1) / 63.0).astype(np.float16)
+    d = d16.astype(np.float64)[:, None]
+    dm = dm16.astype(np.float64)[:, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d > 0, np.clip(np.rint(scale / d), 0, 63), 0).astype(np.int64)
+        mn = np.where(dm > 0, np.clip(np.rint(minimum / dm), 0, 63), 0).astype(np.int64)
+        step = d * sc
+        off = dm * mn
+        q = np.where(step[..., None] > 0, np.clip(np.rint((g + off[..., None]) / step[..., None]), 0, 15), 0)
+    q = q.astype(np.uint8)                                   # [B, 8, 32]
+    qs = (q[:, 0::2, :] | (q[:, 1::2, :] << 4)).reshape(-1, 128)   # page p: group 2p low nibble, 2p+1 high nibble
+    out = np.concatenate([d16.view(np.uint8).reshape(-1, 2), dm16.view(np.uint8).reshape(-1, 2),
+                          _pack_k_scales(sc, mn), qs], axis=-1)
+    return out.reshape(*lead, -1)
+
+
+def quantize_iq4_nl(w):
+    """float32 [..., k] -> packed IQ4_NL bytes [..., k/32*18] (own quantiser): d = (value of largest magnitude)/-127
+    in f16, code = nearest kvalue of x/d (ties: lowest index)."""
+    w = np.asarray(w, np.float32)
+    lead = w.shape[:-1]
+    blocks = w.reshape(-1, 32).astype(np.float64)
+    imax = np.abs(blocks).argmax(axis=-1)[:, None]
+    mx = np.take_along_axis(blocks, imax, axis=-1)
+    d16 = (mx / -127.0).astype(np.float16)
+    d = d16.astype(np.float64)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        v = np.where(d != 0, blocks / d, 0.0)
+    idx = np.abs(v[..., None] - IQ4_KVALUES[None, None, :]).argmin(-1).astype(np.uint8)   # argmin: first minimum
+    packed = idx[:, :16] | (idx[:, 16:] << np.uint8(4))
+    out = np.concatenate([d16.view(np.uint8).reshape(-1, 2), packed], axis=-1)
+    return out.reshape(*lead, -1)
+
+
+def _e2m1_codes(v):
+    """float64 values in [-6, 6] -> nearest e2m1 codes (bit 3 = sign), ties to the even table index."""
+    a = np.abs(v)
+    dist = np.abs(a[..., None] - E2M1)
+    best = dist.min(-1, keepdims=True)
+    cand = dist == best
+    even = cand & (np.arange(8) % 2 == 0)
+    mag = np.where(even.any(-1), even.argmax(-1), cand.argmax(-1))
+    sign = (v < 0) & (mag > 0)
+    return (mag | (sign << 3)).astype(np.uint8)
+
+
+def quantize_mxfp4(w, layout="planar"):
+    """float32 [..., k] -> MXFP4 (own quantiser): e8m0 e = ceil(log2(amax/6)) + 127 so every |x| / 2^(e-127) <= 6,
+    then the nearest e2m1 code. layout "planar" -> (nibbles [..., k/2] in pairs order, scales [..., k/32]);
+    layout "ggml" -> 17-byte blocks [..., k/32*17] (e8m0 byte, then element i low / i+16 high nibble)."""
+    w = np.asarray(w, np.float32)
+    lead = w.shape[:-1]
+    blocks = w.reshape(-1, 32).astype(np.float64)
+    amax = np.abs(blocks).max(-1)
+    with np.errstate(divide="ignore"):
+        e = np.where(amax > 0, np.ceil(np.log2(amax / 6.0)) + 127, 0)
+    e = np.clip(e, 0, 254).astype(np.int64)
+    s = np.exp2(e.astype(np.float64) - 127)
+    codes = _e2m1_codes(np.clip(blocks / s[:, None], -6, 6))   # [B, 32]
+    if layout == "ggml":
+        packed = codes[:, :16] | (codes[:, 16:] << 4)
+        out = np.concatenate([e.astype(np.uint8)[:, None], packed], axis=-1)
+        return out.reshape(*lead, -1)
+    nib = (codes[:, 0::2] | (codes[:, 1::2] << 4)).reshape(*lead, -1)
+    return nib, e.astype(np.uint8).reshape(*lead, -1)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# dequantisation: exact f32 values (gguf / @g_<fmt>_values) and the GEMM's f16 staging (one rounding)
+# ------------------------------------------------------------------------------------------------------------------
+def q4_k_scale_min(scales):
+    """12-byte scale fields [B, 12] -> (sc [B, 8], m [B, 8]) 6-bit codes (gen_llm.py:234-266)."""
+    s = scales.astype(np.int64)
+    d, m, md = s[:, 0:4], s[:, 4:8], s[:, 8:12]
+    sc = np.concatenate([d & 63, (md & 15) | ((d >> 2) & 48)], axis=-1)
+    mn = np.concatenate([m & 63, (md >> 4) | ((m >> 2) & 48)], axis=-1)
+    return sc, mn
+
+
+def _f16(raw2):
+    return np.ascontiguousarray(raw2).view(np.float16).reshape(-1)
+
+
+def _codes4(qs):
+    """16 packed bytes [B, 16] -> 32 nibble codes [B, 32]: element i = low nibble of byte i, i+16 = high nibble."""
+    return np.concatenate([qs & 15, qs >> 4], axis=-1).astype(np.int64)
+
+
+def dequant(fmt, raw, k):
+    """Packed rows [..., row_bytes] (or (nibbles, scales) for planar MXFP4) -> float32 [..., k], the exact values
+    the reference's numpy path uses (gguf.quants.dequantize; quant_values.loom / gen_llm.py helpers)."""
+    if fmt == "mxfp4_planar":
+        nib, sc = raw
+        lead = nib.shape[:-1]
+        nib = nib.reshape(-1, 16)
+        lo = E2M1[nib & 7] * np.where(nib & 8, -1.0, 1.0)
+        hi = E2M1[(nib >> 4) & 7] * np.where(nib & 128, -1.0, 1.0)
+        v = np.stack([lo, hi], -1).reshape(-1, 32)
+        s = np.exp2(sc.reshape(-1).astype(np.float64) - 127.0)
+        return (v * s[:, None]).astype(np.float32).reshape(*lead, k)
+    raw = np.asarray(raw, np.uint8)
+    lead = raw.shape[:-1]
+    b = raw.reshape(-1, BLOCK_BYTES[fmt])
+    if fmt == "q4_0":
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        v = d[:, None] * (_codes4(b[:, 2:]) - 8).astype(np.float32)
+    elif fmt == "iq4_nl":
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        v = d[:, None] * IQ4_KVALUES[_codes4(b[:, 2:])].astype(np.float32)
+    elif fmt == "q4_k":
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        dmin = _f16(b[:, 2:4]).astype(np.float32)
+        sc, mn = q4_k_scale_min(b[:, 4:16])
+        a = d[:, None] * sc.astype(np.float32)                       # [B, 8] exact in f32
+        c = dmin[:, None] * mn.astype(np.float32)
+        qs = b[:, 16:].reshape(-1, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+        q = (qs & 15).reshape(-1, 8, 32).astype(np.float32)
+        v = (a[:, :, None] * q - c[:, :, None]).reshape(-1, 256)
+    elif fmt == "mxfp4":
+        e = b[:, 0].astype(np.int64)
+        # ggml_e8m0_to_fp32_half: 2^(e-128) (e >= 2), subnormal encodings for e < 2; doubled e2m1 table
+        half = np.where(e < 2, np.exp2(e.astype(np.float64) - 128), np.exp2(e.astype(np.float64) - 128))
+        kv = np.array([0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12], np.float64)
+        v = (half[:, None] * kv[_codes4(b[:, 1:])]).astype(np.float32)
+    else:
+        raise ValueError(fmt)
+    return v.astype(np.float32).reshape(*lead, k)
+
+
+def dequant_f16(fmt, raw, k):
+    """The f16 weights the prefill GEMM stages (one rounding of the exact value):
+    Q4_0 f16(d*(q-8)) (moe_q4_0.py:36-38); IQ4_NL f16(d*kvalue) (gen_gemm.py:228-231);
+    Q4_K fma_f16(q, f16(d*sc), f16(-dmin*m)) (gen_gemm.py:526-532)."""
+    if fmt in ("q4_0", "iq4_nl", "mxfp4", "mxfp4_planar"):
+        return dequant(fmt, raw, k).astype(np.float64).astype(np.float16)
+    assert fmt == "q4_k"
+    raw = np.asarray(raw, np.uint8)
+    lead = raw.shape[:-1]
+    b = raw.reshape(-1, 144)
+    d = _f16(b[:, 0:2]).astype(np.float32)
+    dmin = _f16(b[:, 2:4]).astype(np.float32)
+    sc, mn = q4_k_scale_min(b[:, 4:16])
+    a16 = (d[:, None] * sc.astype(np.float32)).astype(np.float16).astype(np.float64)
+    c16 = (-(dmin[:, None] * mn.astype(np.float32))).astype(np.float16).astype(np.float64)
+    qs = b[:, 16:].reshape(-1, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+    q = (qs & 15).reshape(-1, 8, 32).astype(np.float64)
+    v = q * a16[:, :, None] + c16[:, :, None]          # exact in f64; one rounding to f16 = the f16 fma
+    with np.errstate(over="ignore"):
+        return v.reshape(-1, 256).astype(np.float16).reshape(*lead, k)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# activation producers
+# ------------------------------------------------------------------------------------------------------------------
+def _f32_exponent_field(a):
+    return (np.asarray(a, np.float32).view(np.uint32) >> 23) & 255
+
+
+def row_scale_f16(x):
+    """g_row_scale_f16 (gen_llm.py:1843-1912): per row e = clamp(exp(max|x|) - 127 - 13, 0, 100), s = 2^-e,
+    x16 = f16(x * s), scales[row] = (s, 2^e)."""
+    x = np.asarray(x, np.float32)
+    mx = np.abs(x).max(-1)
+    biased = _f32_exponent_field(mx).astype(np.int64)
+    e = np.clip(biased - 127 - 13, 0, 100)
+    s = ((127 - e).astype(np.uint32) << 23).view(np.float32)
+    inv = ((127 + e).astype(np.uint32) << 23).view(np.float32)
+    x16 = (x * s[:, None]).astype(np.float16)
+    return x16, np.stack([s, inv], -1).astype(np.float32)
+
+
+def e4m3_round(x):
+    """Nearest finite e4m3fn values, round to nearest even, saturating at 448 (make_kernel_tests.py:2006-2011)."""
+    x = np.asarray(x, np.float64)
+    a = np.minimum(np.abs(x), 448.0)
+    e = np.maximum(np.floor(np.log2(np.maximum(a, 2.0 ** -20))), -6)
+    q = 2.0 ** (e - 3)
+    return np.sign(x) * np.minimum(np.rint(a / q) * q, 448.0)
+
+
+def e4m3_bytes(v):
+    """e4m3fn values -> bytes (make_kernel_tests.py:2012-2019); negative values rounding to zero keep -0."""
+    v = np.asarray(v, np.float64)
+    a = np.abs(v)
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -20))).astype(np.int64)
+    sub = a < 2.0 ** -6
+    ef = np.where(sub, 0, e + 7)
+    with np.errstate(invalid="ignore"):
+        mant = np.where(sub, np.rint(a / 2.0 ** -9), np.rint((a / 2.0 ** e - 1) * 8)).astype(np.int64)
+    b = np.where(a == 0, 0, (ef << 3) | mant) | np.where(np.signbit(v), 0x80, 0)
+    return b.astype(np.uint8)
+
+
+def e4m3_values(b):
+    """e4m3fn bytes -> float64."""
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    ef = (b >> 3) & 15
+    m = b & 7
+    v = np.where(ef == 0, m * 2.0 ** -9, (1 + m / 8.0) * 2.0 ** (ef - 7))
+    v = np.where((ef == 15) & (m == 7), np.nan, v)
+    return s * v
+
+
+def row_scale_f8(x):
+    """The fp8 producer twin (gen_mxfp4s.py:852-870, 887-938): per row biased = exponent field of max|x|,
+    scale = 2^(134 - biased) and inverse 2^(biased - 142) (both clamped to normal exponents 1..254),
+    x8 = e4m3(x * scale): the row max lands in [128, 256); s8[row] = (scale, inverse) -- the inverse carries the
+    2^-8 of the weights held at 2^8 times their value."""
+    x = np.asarray(x, np.float32)
+    mx = np.abs(x).max(-1)
+    biased = _f32_exponent_field(mx).astype(np.int64)
+    sf = np.clip(261 - biased, 1, 254)
+    inf_ = np.clip(biased - (7 + MXFP4_F8_SHIFT), 1, 254)
+    s = (sf.astype(np.uint32) << 23).view(np.float32)
+    inv = (inf_.astype(np.uint32) << 23).view(np.float32)
+    x8 = e4m3_bytes(e4m3_round(x.astype(np.float64) * s[:, None].astype(np.float64)))
+    return x8, np.stack([s, inv], -1).astype(np.float32)
+
+
+def mxfp4_e5m2_bytes(e, q):
+    """MXFP4 nibble -> the e5m2 byte holding fp4 * 2^(e - 127 + 8) (gen_mxfp4s.py:14-27): sign | (base[m] + 4*(e-107)),
+    base = 8 12 14 16 18 20 22 for m = 1..7, zero stays zero. e [..] uint8, q [..] nibble codes."""
+    e = np.asarray(e, np.int64)
+    q = np.asarray(q, np.int64)
+    base = np.array([0, 8, 12, 14, 16, 18, 20, 22], np.int64)
+    m = q & 7
+    mag = np.where(m == 0, 0, base[m] + 4 * (e - MXFP4_F8_E_MIN))
+    return (mag | ((q & 8) << 4)).astype(np.uint8)
+
+
+def e5m2_values(b):
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    ef = (b >> 2) & 31
+    m = b & 3
+    return s * np.where(ef == 0, m * 2.0 ** -16, (1 + m / 4.0) * 2.0 ** (ef - 15))
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# products (float64, as make_kernel_tests.py builds its references)
+# ------------------------------------------------------------------------------------------------------------------
+def silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def mv_ref(fmt, w, x, n, k, w2=None, y_old=None):
+    """Decode matvec (gen_llm.py:1159-1378; reference make_kernel_tests.py:231-238):
+    y[t, n] (+)= sum_k x[t, k] W[n, k]; with w2: y = silu(x.Wg) * (x.Wu)."""
+    W = dequant(fmt, w, k).reshape(n, k).astype(np.float64)
+    x = np.asarray(x, np.float64).reshape(-1, k)
+    y = x @ W.T
+    if w2 is not None:
+        U = dequant(fmt, w2, k).reshape(n, k).astype(np.float64)
+        y = silu(y) * (x @ U.T)
+    if y_old is not None:
+        y = y + np.asarray(y_old, np.float64)
+    return y
+
+
+def gemm_ref(fmt, w, x16, scales, n, k, mode="store", w2=None, y_old=None):
+    """Prefill GEMM (gen_gemm.py:535-704; reference make_kernel_tests.py:1860-1876):
+    Y = (X16 . W^T) * inv[row]; mode acc adds y_old; swiglu: silu(G) * U."""
+    W = dequant(fmt, w, k).reshape(n, k).astype(np.float64)
+    x = np.asarray(x16, np.float64).reshape(-1, k)
+    inv = np.asarray(scales, np.float64)[:, 1:2]
+    y = (x @ W.T) * inv
+    if mode == "swiglu":
+        U = dequant(fmt, w2, k).reshape(n, k).astype(np.float64)
+        y = silu(y) * ((x @ U.T) * inv)
+    elif mode == "acc":
+        y = y + np.asarray(y_old, np.float64)
+    return y
+
+
+def gemm_mxfp4_f8_ref(x8, s8, nib, sc, n, k, order="pairs"):
+    """MXFP4 x FP8 GEMM (gen_mxfp4s.py:50-500; kbench gemm_mxfp4s/gen_bench.py:284-291):
+    y = (e4m3(x8) . (W * 2^8)^T) * s8[row, 1], W the exact MXFP4 values."""
+    W = dequant_mxfp4_planar(nib, sc, n, k, order)
+    a = e4m3_values(x8).reshape(-1, k)
+    return (a @ (W * 2.0 ** MXFP4_F8_SHIFT).T) * np.asarray(s8, np.float64)[:, 1:2]
+
+
+def dequant_mxfp4_planar(nib, sc, n, k, order="pairs"):
+    """Split planes (nibbles [n, k/2], scales [n, k/32]) -> float64 [n, k] in the given nibble order
+    (kbench gemm_mxfp4s/gen_bench.py:284-291: "pairs" = element 2j low nibble of byte j; "split16" = ggml order)."""
+    nib = np.asarray(nib, np.uint8).reshape(n, k // 2)
+    lo = E2M1[nib & 7] * np.where(nib & 8, -1.0, 1.0)
+    hi = E2M1[(nib >> 4) & 7] * np.where(nib & 128, -1.0, 1.0)
+    lo, hi = lo.reshape(n, -1, 16), hi.reshape(n, -1, 16)
+    blk = np.stack([lo, hi], 3).reshape(n, -1, 32) if order == "pairs" else np.concatenate([lo, hi], 2)
+    return (blk * np.exp2(np.asarray(sc, np.float64).reshape(n, -1, 1) - 127)).reshape(n, k)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# MoE
+# ------------------------------------------------------------------------------------------------------------------
+def route_ref(logits, ku, gating=1, norm=True, bias=None):
+    """Router top-k (gen_moe.py:116-253): gating 1 softmax over all experts then top-k, gating 2 sigmoid (+bias for
+    the pick), gating 3 top-k of the (biased) logits weighted by a softmax over the picked. Ties: lowest index.
+    norm: w / max(sum, 6.103515625e-05)."""
+    lg = np.asarray(logits, np.float32)
+    t, E = lg.shape
+    if gating == 1:
+        m = lg.max(-1, keepdims=True)
+        ex = np.exp((lg - m).astype(np.float32))
+        prob = (ex / ex.sum(-1, keepdims=True)).astype(np.float32)
+        score = prob
+    elif gating == 2:
+        prob = (1.0 / (1.0 + np.exp(-lg.astype(np.float64)))).astype(np.float32)
+        score = prob + (0 if bias is None else np.asarray(bias, np.float32))
+    else:
+        prob = lg + (0 if bias is None else np.asarray(bias, np.float32))
+        score = prob
+    ids = np.zeros((t, ku), np.int32)
+    wts = np.zeros((t, ku), np.float32)
+    for i in range(t):
+        order = np.lexsort((np.arange(E), -score[i].astype(np.float64)))[:ku]   # descending score, lowest index
+        ids[i] = order
+        p = prob[i, order].astype(np.float64)
+        if gating == 3:
+            ex = np.exp(p - p[0])
+            wts[i] = ex / ex.sum()
+        elif norm:
+            wts[i] = p / max(p.sum(), 6.103515625e-05)
+        else:
+            wts[i] = p
+    return ids, wts
+
+
+def moe_max_tiles(tokens, ku, n_experts, tile=64):
+    """Worst-case tile count (gen_llm.py:5406-5411): t*KU/64 + E (rounded up)."""
+    return (tokens * ku + tile - 1) // tile + n_experts
+
+
+def bucket_ref(ids, n_experts, max_tiles, live=None, tile=64):
+    """g_moe_bucket (gen_moe.py:829-955): live assignments a = t*KU + k counted per expert, ceil(count/tile) tiles per
+    expert in expert order, tile_info[tile] = (expert, rows) and (-1, 0) unused, rowmap[row] = a (-1 padding),
+    pos[a] = row (-1 dead). Within an expert, rows follow ascending a (the reference orders them by atomics; any
+    order within an expert's tiles is equivalent, see check_bucket)."""
+    ids = np.asarray(ids, np.int64)
+    t, ku = ids.shape
+    live = np.ones(t, bool) if live is None else np.asarray(live) != 0
+    e_of = np.clip(ids, 0, n_experts - 1).reshape(-1)
+    a_live = np.repeat(live, ku)
+    counts = np.bincount(e_of[a_live], minlength=n_experts)
+    tiles = (counts + tile - 1) // tile
+    base = np.concatenate([[0], np.cumsum(tiles)[:-1]])
+    total = int(tiles.sum())
+    assert total <= max_tiles
+    tile_info = np.tile(np.array([-1, 0], np.int32), (max_tiles, 1))
+    rowmap = np.full(max_tiles * tile, -1, np.int32)
+    pos = np.full(t * ku, -1, np.int32)
+    for e in range(n_experts):
+        for j in range(tiles[e]):
+            tile_info[base[e] + j] = (e, min(tile, counts[e] - j * tile))
+        members = np.nonzero((e_of == e) & a_live)[0]
+        rows = base[e] * tile + np.arange(len(members))
+        rowmap[rows] = members
+        pos[members] = rows
+    return tile_info, rowmap, pos
+
+
+def check_bucket(ids, n_experts, max_tiles, tile_info, rowmap, pos, live=None, tile=64):
+    """Order-free invariants of a bucket schedule: the reference's atomics order rows within an expert arbitrarily.
+    Returns None when the schedule is valid, else a message."""
+    ti, rm, ps = bucket_ref(ids, n_experts, max_tiles, live, tile)
+    if not np.array_equal(ti, np.asarray(tile_info)):
+        return "tile_info differs"
+    rowmap = np.asarray(rowmap)
+    pos = np.asarray(pos)
+    if not np.array_equal(rm < 0, rowmap < 0):
+        return "padding rows differ"
+    for e_tile in range(max_tiles):
+        e = ti[e_tile, 0]
+        if e < 0:
+            continue
+        seg = slice(e_tile * tile, (e_tile + 1) * tile)
+    # same set of assignments per expert, and pos is the inverse of rowmap
+    idsf = np.asarray(ids).reshape(-1)
+    for r in np.nonzero(rowmap >= 0)[0]:
+        a = rowmap[r]
+        if pos[a] != r:
+            return f"pos[{a}] != {r}"
+        if ti[r // tile, 0] != np.clip(idsf[a], 0, n_experts - 1):
+            return f"row {r} holds assignment {a} of another expert"
+    if not np.array_equal(pos < 0, ps < 0):
+        return "dead assignments differ"
+    return None
+
+
+def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts):
+    """The routed expert FFN in float64 (kbench moe_q4_0/gen_bench.py:185-248 with SiLU):
+    y[t] = sum_k wts[t,k] * Wd[e] (silu(Wg[e] x[t]) * (Wu[e] x[t])), e = ids[t,k]; w_gu[e] = gate rows then up rows."""
+    x = np.asarray(x, np.float64)
+    t, ku = ids.shape
+    y = np.zeros((t, h), np.float64)
+    cache = {}
+    for e in np.unique(ids):
+        gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
+        dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
+        cache[int(e)] = (gu, dn)
+    for e in np.unique(ids):
+        gu, dn = cache[int(e)]
+        sel = np.nonzero(ids == e)
+        xs = x[sel[0]]
+        pair = xs @ gu.T
+        act = silu(pair[:, :f]) * pair[:, f:]
+        ys = act @ dn.T
+        np.add.at(y, sel[0], ys * np.asarray(wts, np.float64)[sel][:, None])
+    return y
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))

@@ -1,0 +1,19 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a) and the built liblk.so")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    with np.load(os.path.join(ROOT, "tests", "golden", "golden.npz")) as z:
+        return {k: z[k] for k in z.files}
