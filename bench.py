@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized-matmul hot path on B200 (the driver's bench contract).
+
+Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B-like projection shapes
+(K=4096: N=4096 q/o, N=1024 k/v, N=24576 fused gate+up; down K=12288, N=4096), bf16 activations. One STEP is one decode
+token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
+868 MB at 8 layers, exceed the 126 MB L2). `value` is the decode GEMV weight GB/s; the line also carries the prefill
+TFLOP/s at M=2048 over the same shapes, and a sweep over M in {1, 8, 64, 512, 2048}.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
+
+--gpus N > 1 runs under torchrun, one rank per GPU, each rank with its own replica of the workload (weak scaling;
+the decode step has no exchange). --impl reference times the reference's CPU path (the numpy dequant + float64
+matvec of make_kernel_tests.py, restated in oracle/) on the same metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode GEMV weight GB/s (% HBM peak); prefill TFLOPS (% tensor peak)"
+SHAPES = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096), ("gate_up", 4096, 24576),
+          ("down", 12288, 4096)]   # (name, K, N)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def rank_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.out = os.path.join("/tmp", f"lk_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.out, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        rows = []
+        for line in open(self.out):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 10 and (self.uuid is None or f[1] == self.uuid):
+                rows.append(f)
+        os.unlink(self.out)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's numpy path (restated in oracle/)
+# ------------------------------------------------------------------------------------------------------------------
+def cpu_decode_gbs(budget_s=10.0, rows=1024):
+    """Dequantise + float64 matvec of a `rows`-row slice of the gate_up projection, repeated for ~budget_s seconds."""
+    from oracle import qmm_oracle as O
+    k = 4096
+    rng = np.random.default_rng(1)
+    w = O.quantize_q4_k((rng.standard_normal((rows, k)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        O.mv_ref("q4_k", w, x, rows, k)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 10000:
+            break
+    gbs = reps * w.nbytes / el / 1e9
+    return gbs, {"kind": "port", "cores": os.cpu_count(),
+                 "sample": f"Q4_K {rows}x{k} slice of gate_up (numpy dequant + float64 matvec, OpenBLAS threads), "
+                           f"{reps} reps in {el:.1f} s"}
+
+
+def run_reference(args):
+    rank, _, world = rank_env()
+    if rank != 0:
+        return
+    # each step: a bounded sample of the decode workload on the host cores (~2 s)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, desc = cpu_decode_gbs(budget_s=2.0)
+        if i >= args.warmup:
+            vals.append(v)
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2000.0, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "configs[1] Q4_K decode, M=1, gate_up slice (CPU sample)"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", **desc},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------------------------
+def make_weights(torch, layers, seed=0):
+    """Q4_K weights for one layer (seeded N(0,0.02), quantised on the host), copied to `layers` distinct buffers."""
+    from oracle import qmm_oracle as O
+    rng = np.random.default_rng(seed)
+    base = {}
+    for name, k, n in SHAPES:
+        chunks = []
+        for r0 in range(0, n, 2048):
+            r1 = min(n, r0 + 2048)
+            chunks.append(O.quantize_q4_k((rng.standard_normal((r1 - r0, k)) * 0.02).astype(np.float32)))
+        base[name] = torch.from_numpy(np.concatenate(chunks)).cuda()
+    stack = []
+    for li in range(layers):
+        stack.append({name: (t if li == 0 else t.clone()) for name, t in base.items()})
+    return stack
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from loom_skills_b200 import ops
+
+    rank, local, world = rank_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    pk, pk_src = peaks()
+    wstack = make_weights(torch, args.layers, seed=rank)
+    torch.manual_seed(rank)
+    xs = {k: torch.randn(1, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
+    ys = [{name: torch.empty(1, n, device=dev) for name, _, n in SHAPES} for _ in range(args.layers)]
+    wbytes_layer = sum(t.numel() for t in wstack[0].values())
+    act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
+    stream = torch.cuda.current_stream()
+
+    def decode_step(ev=None):
+        for li in range(args.layers):
+            for name, k, n in SHAPES:
+                if ev is not None:
+                    ev[0].append(torch.cuda.Event(enable_timing=True))
+                    ev[0][-1].record(stream)
+                ops.mv("q4_k", wstack[li][name], xs[k], n, k, y=ys[li][name])
+                if ev is not None:
+                    ev[1].append(torch.cuda.Event(enable_timing=True))
+                    ev[1][-1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- decode: device-resident inputs
+    for _ in range(args.warmup):
+        decode_step()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    clk = Clocks(uuid)
+    barrier()
+    clk.start()
+    kev = ([], [])
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        decode_step(kev)
+    t1.record(stream)
+    barrier()
+    clocks = clk.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    launch_ms = [a.elapsed_time(b) for a, b in zip(*kev)]
+    launches_per_step = args.layers * len(SHAPES)
+    step_bytes = args.layers * wbytes_layer
+    value = world * step_bytes / (ms * 1e-3) / 1e9
+    # dominant kernel: the Q4_K matvec (every launch of the step); algorithmic bytes = weights + x + y
+    alg_per_launch = (step_bytes + args.layers * act_bytes) / launches_per_step
+    kavg = statistics.mean(launch_ms)
+    achieved = alg_per_launch / (kavg * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_source": pk_src,
+            "kernel": "k_mv<Q4_K, bf16> (lk_mv)"}
+
+    # ---- e2e through the public API: pinned host x in, every projection output back, each step
+    hx = {k: torch.empty(1, k, dtype=torch.bfloat16).pin_memory() for k in xs}
+    for k in hx:
+        hx[k].copy_(xs[k].cpu())
+    hy = [{name: torch.empty(1, n).pin_memory() for name, _, n in SHAPES} for _ in range(args.layers)]
+    h2d = sum(t.numel() * 2 for t in hx.values())
+    d2h = sum(t.numel() * 4 for d in hy for t in d.values())
+
+    def e2e_step():
+        for k in hx:
+            xs[k].copy_(hx[k], non_blocking=True)
+        decode_step()
+        for li in range(args.layers):
+            for name in ys[li]:
+                hy[li][name].copy_(ys[li][name], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    t1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    e2e = {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
+
+    # ---- prefill: M=2048 through the same shapes (row scale to f16 + tcgen05 GEMM), one layer
+    M = args.prefill_rows
+    xp = {k: torch.randn(M, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
+    yp = {name: torch.empty(M, n, device=dev) for name, _, n in SHAPES}
+    flops = sum(2.0 * M * n * k for _, k, n in SHAPES)
+
+    def prefill_step(ev=None):
+        x16 = {k: ops.row_scale_f16(xp[k]) for k in xp}
+        for name, k, n in SHAPES:
+            if ev is not None:
+                ev[0].append(torch.cuda.Event(enable_timing=True))
+                ev[0][-1].record(stream)
+            ops.gemm("q4_k", "store", x16[k][0], x16[k][1], wstack[0][name], n, y=yp[name])
+            if ev is not None:
+                ev[1].append(torch.cuda.Event(enable_timing=True))
+                ev[1][-1].record(stream)
+
+    for _ in range(args.warmup):
+        prefill_step()
+    barrier()
+    pev = ([], [])
+    t0.record(stream)
+    for _ in range(args.steps):
+        prefill_step(pev)
+    t1.record(stream)
+    barrier()
+    pms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    gms = statistics.mean(a.elapsed_time(b) for a, b in zip(*pev)) * len(SHAPES)
+    ptflops = flops / (pms * 1e-3) / 1e12
+    gemm_tf = flops / (gms * 1e-3) / 1e12
+    peak_tf = pk["bf16_tflops_sustained"]
+    prefill = {"rows": M, "tflops": round(world * ptflops, 1), "ms_per_step": round(pms, 4),
+               "roofline": {"bound": "tensor", "achieved": round(gemm_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                            "frac": round(gemm_tf / peak_tf, 4), "traffic": None, "peak_source": pk_src + " sustained",
+                            "kernel": "k_gemm<Q4_K> (tcgen05 kind::f16, lk_gemm)"}}
+
+    # ---- sweep over the config's token counts (one layer, per-step ms)
+    sweep = {}
+    if not args.no_sweep:
+        for m in (1, 8, 64, 512, 2048):
+            xm = {k: torch.randn(m, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
+            ym = {name: torch.empty(m, n, device=dev) for name, _, n in SHAPES}
+
+            def step_m():
+                if m < 64:
+                    for name, k, n in SHAPES:
+                        ops.mv("q4_k", wstack[0][name], xm[k], n, k, y=ym[name])
+                else:
+                    x16 = {k: ops.row_scale_f16(xm[k]) for k in xm}
+                    for name, k, n in SHAPES:
+                        ops.gemm("q4_k", "store", x16[k][0], x16[k][1], wstack[0][name], n, y=ym[name])
+            for _ in range(3):
+                step_m()
+            torch.cuda.synchronize()
+            reps = 10
+            t0.record(stream)
+            for _ in range(reps):
+                step_m()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            mms = t0.elapsed_time(t1) / reps
+            sweep[str(m)] = {"ms": round(mms, 4), "weight_gbs": round(wbytes_layer / (mms * 1e-3) / 1e9, 1),
+                             "tflops": round(sum(2.0 * m * n * k for _, k, n in SHAPES) / (mms * 1e-3) / 1e12, 2)}
+
+    if rank == 0:
+        cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k x bf16 (f16 tensor-core codes, f32 accumulate)",
+            "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K, N(0,1) bf16 activations",
+            "config": {"workload": "configs[1] Qwen3-8B-like Q4_K projections, decode M=1",
+                       "shapes_k_n": [[k, n] for _, k, n in SHAPES], "layers": args.layers,
+                       "weight_bytes_per_step": step_bytes,
+                       "l2": f"inputs larger than L2: {step_bytes / 1e6:.0f} MB of weights rotated over "
+                             f"{args.layers} layer copies",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
+            "gpu_launches": args.steps * launches_per_step, "clocks": clocks, "prefill": prefill, "sweep": sweep,
+            "hbm_frac": round(value / world / pk["hbm_gbs"], 4)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--prefill-rows", type=int, default=2048)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,150 @@
+/*
+ * liblk -- the B200 (sm_100a) quantized-matmul hot path of loom-fun/loom-skills behind a C ABI.
+ *
+ * Every entry point replaces one kernel family that the reference's Python generators emit as Loom IR; the comment on
+ * each names the reference interface (path:line relative to the loom-skills checkout) whose launch signature it keeps:
+ * the same operands in the same order, the same layouts (packed GGUF blocks, [rows][k] activations, [rows][n] f32
+ * outputs, [rows][2] (scale, inverse) row factors, MoE tile_info/rowmap/pos schedules).
+ *
+ * Conventions
+ *  - All pointers are device pointers (cudaMalloc'd or views of them); the caller owns every buffer, as the
+ *    reference's command programs do. Nothing here allocates device memory or synchronises.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ *  - Return 0 (LK_OK) or a negative LK_E* code after host-side validation of formats, shapes and alignment. The
+ *    reference has no runtime errors (its contracts are index.assume preconditions); violating one here is an error
+ *    code, not undefined behaviour. A CUDA launch error is LK_ECUDA.
+ *  - Weight formats use the ggml type ids (gguf.GGMLQuantizationType).
+ */
+#ifndef LK_H
+#define LK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* lk_stream_t;   /* == cudaStream_t */
+
+/* weight formats (ggml type ids); LK_MXFP4S = split planes (nibble plane + E8M0 scale plane), formats.py:11-14 */
+enum { LK_Q4_0 = 2, LK_Q4_K = 12, LK_IQ4_NL = 20, LK_MXFP4 = 39, LK_MXFP4S = 1039 };
+/* element types (ggml ids where ggml has one) */
+enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 30, LK_E4M3 = 1000 };
+/* GEMM epilogues (gen_gemm.py:535 `mode`): y = acc, y += acc, y = silu(acc_w) * acc_w2 */
+enum { LK_STORE = 0, LK_ACC = 1, LK_SWIGLU = 2 };
+/* MXFP4 nibble order inside a 32-value block (gen_mxfp4s.py:1-7): OCP pairs, or ggml split16 */
+enum { LK_ORDER_PAIRS = 0, LK_ORDER_SPLIT16 = 1 };
+
+#define LK_OK 0
+#define LK_EINVAL (-1)       /* unknown format / mode / dtype, bad shape, null pointer */
+#define LK_EALIGN (-2)       /* a pointer or row stride is not aligned as the kernel's loads require */
+#define LK_ECUDA (-3)        /* the launch failed (cudaGetLastError) */
+#define LK_EUNSUPPORTED (-4) /* a valid combination this build has no kernel for */
+#define LK_ERANGE (-5)       /* a size beyond a stated maximum */
+
+const char* lk_strerror(int code);
+int lk_version(void);
+/* Device-side status (synchronous; no reference counterpart): bit 0 = a kernel's bounded wait on an mbarrier gave
+ * up (its results are not valid). clear != 0 resets it. */
+unsigned int lk_device_status(int clear);
+/* packed bytes of one row of k values of `fmt` (gen_moe.py:70-71 row_bytes); -1 if k is not a block multiple */
+int64_t lk_row_bytes(int fmt, int64_t k);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Block dequantisation, standalone (bit-exact check and weight staging).
+ * Replaces the value helpers @g_q4_0_values / @g_iq4_nl_values (quant_values.loom:18-91, 386-408), @g_q4_k_values
+ * (gen_llm.py:288-315), MXFP4 / MXFP4S (gen_llm.py:786-895) and, for out_dtype LK_F16, the GEMM staging
+ * dequant16 (gen_gemm.py:281-532, moe_q4_0.py:11-38).
+ * out_dtype LK_F32: the exact values (== gguf.quants.dequantize); LK_F16: one rounding of the exact value, except Q4_K
+ * whose staging is fma_f16(q, f16(d*sc), f16(-dmin*m)) as gen_gemm.py:526-532.
+ * w_scales: the E8M0 scale plane for LK_MXFP4S (pairs order), else NULL. n_values % 32 == 0 (256 for Q4_K).
+ */
+int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,
+               lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Activation producers.
+ * lk_row_scale_f16: g_row_scale_f16 (gen_llm.py:1843-1912), launch(%rows, %k, %x, %scales, %x16):
+ *   e = clamp(exponent(max|x[row]|) - 127 - 13, 0, 100); scales[row] = (2^-e, 2^e); x16 = f16(x * 2^-e).
+ *   x_dtype LK_F32 or LK_BF16.
+ * lk_row_scale_f8: the fp8 producer twin g_row_scale_f16_f8_rdna4 (gen_mxfp4s.py:852-870, 887-938),
+ *   launch(..., %x16, %x8, %s8, %w16): additionally x8 = e4m3(x * 2^(134 - b)), s8 = (2^(134-b), 2^(b-142)),
+ *   b = biased exponent of the row max; x16/scales are written only when non-NULL (the %w16 flag).
+ */
+int lk_row_scale_f16(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, lk_stream_t stream);
+int lk_row_scale_f8(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
+                    lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Decode matvec (tokens < 64). Replaces g_mv_{fmt}_k{K}[_t{TG}][_r{R}] and its swiglu pair (gen_llm.py:1159-1378),
+ * launch(%n, %tokens, %accumulate, %x, %w [, %w2], %y): y[t][n] (+)= sum_k x[t][k] W[n][k];
+ * w2 != NULL: y[t][n] (+)= silu(x.Wg[n]) * (x.Wu[n]).  x: [tokens][k] of x_dtype (LK_F32, LK_F16 or LK_BF16),
+ * W: [n] packed rows. Formats Q4_0, Q4_K, IQ4_NL; k % 256 == 0; w 16-byte aligned.
+ */
+int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w,
+          const void* w2, float* y, lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Prefill GEMM (tcgen05 + TMEM). Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704,
+ * 706, 1224), launch(%rows, %k, %n, %x, %scales, %w [, %w2], %y):
+ *   Y[rows][n] (+)= (X16 . W16^T) * scales[row][1]; swiglu: silu(G) * U with G, U the two weights' products.
+ * x16: [rows][k] f16 (lk_row_scale_f16's output), scales: [rows][2] f32, y: [rows][n] f32.
+ * Formats Q4_0, Q4_K, IQ4_NL. k % 256 == 0, n % 16 == 0; x16, w 16-byte aligned. Any rows >= 1.
+ */
+int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
+            const void* w2, float* y, lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * MXFP4 (split planes) x FP8 GEMM. Replaces g_gemm_mxfp4s_{store,swiglu}_f8_m256_rdna4
+ * (gen_mxfp4s.py:50-500; signature test tests/test_mxfp4s_f8.py:150-160),
+ * launch(%rows, %k, %n, %x, %scales, %w, %ws [, %w2, %w2s], %y): y = (x8 . (W * 2^8)^T) * s8[row][1].
+ * x8: [rows][k] e4m3, s8: [rows][2] (lk_row_scale_f8), w: nibble plane [n][k/2], ws: E8M0 plane [n][k/32].
+ * k % 128 == 0, n % 16 == 0.
+ */
+int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8,
+                      const uint8_t* w, const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y,
+                      lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * MoE (gen_moe.py). Assignment a = t * ku + slot.
+ * lk_moe_route: g_moe_route / g_moe_route_tr (gen_moe.py:116-253, 255-470), launch(%tokens, %h, %router_w, %bias,
+ *   %ids, %wts). gating 1 softmax (+ top-k, renormalised when norm: w / max(sum, 6.1e-5)), 2 sigmoid (+ bias for the
+ *   pick), 3 top-k of logit+bias weighted by a softmax over the picked. Ties: lowest expert index. `scale` multiplies
+ *   the final weights (expert_weights_scale, gen_moe.py:111-113). router_w == NULL: x already holds the logits
+ *   [tokens][n_experts] (f32); else x is [tokens][h] f32 and router_w [n_experts][h] of w_dtype (LK_F32/LK_BF16).
+ *   n_experts <= 256, ku <= 8.
+ * lk_moe_bucket: g_moe_bucket (gen_moe.py:829-955), launch(%tokens, %max_tiles, %info, %ids, %tile_info, %rowmap,
+ *   %pos): 64-row tiles per expert in expert order; tile_info[max_tiles][2] = (expert, rows) or (-1, 0);
+ *   rowmap[max_tiles*64] = a or -1; pos[tokens*ku] = row or -1. info == NULL: every token live, else live =
+ *   info[t*4+2] != 0. Rows of one expert follow ascending a (deterministic; the reference orders them by atomics).
+ * lk_moe_grouped_gemm: g_moe_ggu_{fmt}[_fused]_k{H} / g_moe_gdn_{fmt}_k{F} (gen_moe.py:1126-1228), launch(%rows,
+ *   %k, %n, %xrows, %tile_info, %rowmap, %x, %scales, %w [, %w2], %y). mode LK_SWIGLU (gate/up): A rows gathered
+ *   from x16[rowmap[r] / ku] (rowmap < 0 -> zero row), y[r] = silu(g) * u with g, u scaled by scales[token][1];
+ *   fused: w holds per expert n gate rows then n up rows. mode LK_STORE (down): A = sorted rows x16[r],
+ *   y[r] = acc * scales[r][1]. Tiles with expert < 0 are skipped (their y rows are not written).
+ * lk_moe_combine_sorted: g_moe_combine_sorted (gen_moe.py:1231-1280), launch(%tokens, %rows, %ys, %pos, %wts, %y):
+ *   y[t] (+)= sum_k wts[t][k] * ys[pos[t][k]] (pos < 0 -> 0).
+ * lk_moe_expert_mv: decode expert matvecs g_moe_gu_{fmt} / g_moe_dn_{fmt} (gen_moe.py:535-727): mode 0 (gu):
+ *   y[a] = silu(Wg[e] x[a/ku]) * (Wu[e] x[a/ku]); mode 1 (dn): y[a] = Wd[e] x[a]; e = ids[a].
+ * lk_moe_combine: g_moe_combine (gen_moe.py:730-762): y[t] (+)= sum_k wts[t][k] ys[t*ku + k].
+ */
+int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
+                 const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, lk_stream_t stream);
+int lk_moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_t* info, const int32_t* ids,
+                  int32_t* tile_info, int32_t* rowmap, int32_t* pos, lk_stream_t stream);
+int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
+                        const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
+                        const void* w, const void* w2, float* y, lk_stream_t stream);
+int lk_moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
+                          const float* wts, float* y, lk_stream_t stream);
+int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                     const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
+                     lk_stream_t stream);
+int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
+                   lk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LK_H */

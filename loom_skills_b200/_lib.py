@@ -1,0 +1,63 @@
+"""ctypes binding of liblk.so (the C ABI declared in include/lk.h). No fallback: a missing library is an error."""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblk.so")
+
+# formats / dtypes / modes (include/lk.h)
+Q4_0, Q4_K, IQ4_NL, MXFP4, MXFP4S = 2, 12, 20, 39, 1039
+F32, F16, BF16, E4M3 = 0, 1, 30, 1000
+STORE, ACC, SWIGLU = 0, 1, 2
+ORDER_PAIRS, ORDER_SPLIT16 = 0, 1
+FMT_IDS = {"q4_0": Q4_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "mxfp4": MXFP4, "mxfp4s": MXFP4S}
+MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU}
+
+_P, _I, _L, _F, _U = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint
+
+# name -> (restype, argtypes); every symbol include/lk.h declares
+SIGNATURES = {
+    "lk_strerror": (ctypes.c_char_p, [_I]),
+    "lk_version": (_I, []),
+    "lk_row_bytes": (_L, [_I, _L]),
+    "lk_device_status": (_U, [_I]),
+    "lk_dequant": (_I, [_I, _P, _P, _L, _P, _I, _P]),
+    "lk_row_scale_f16": (_I, [_I, _I, _P, _I, _P, _P, _P]),
+    "lk_row_scale_f8": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _P]),
+    "lk_mv": (_I, [_I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
+    "lk_gemm": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "lk_gemm_mxfp4s_f8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "lk_moe_route": (_I, [_I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _P, _P, _P]),
+    "lk_moe_bucket": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
+    "lk_moe_grouped_gemm": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "lk_moe_combine_sorted": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "lk_moe_expert_mv": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
+    "lk_moe_combine": (_I, [_I, _I, _I, _I, _P, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def load():
+    """The loaded liblk.so with argument types declared. Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built (run loom_skills_b200/build.py or __graft_entry__.build())")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+class LkError(RuntimeError):
+    pass
+
+
+def check(rc, what):
+    if rc != 0:
+        raise LkError(f"{what}: {load().lk_strerror(rc).decode()} (code {rc})")
+    return rc

@@ -1,0 +1,220 @@
+// The C ABI of liblk: host-side validation, then the kernel launchers. See include/lk.h for the contract of each
+// entry point and the reference interface it replaces.
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+using namespace lk;
+
+namespace lk {
+unsigned int status_mv(bool clear);
+unsigned int status_gemm(bool clear);
+int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
+         const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
+         int n_experts, int64_t expert_stride, int64_t w2_offset);
+int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+                const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
+int moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
+              const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s);
+int moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_t* info, const int32_t* ids,
+               int32_t* tile_info, int32_t* rowmap, int32_t* pos, cudaStream_t s);
+int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
+                       const float* wts, float* y, cudaStream_t s);
+int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
+                cudaStream_t s);
+}  // namespace lk
+
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+static bool q4_family(int fmt) { return fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL; }
+
+extern "C" {
+
+const char* lk_strerror(int code) {
+  switch (code) {
+    case LK_OK: return "ok";
+    case LK_EINVAL: return "invalid argument (format, mode, dtype, shape or null pointer)";
+    case LK_EALIGN: return "misaligned pointer or row stride";
+    case LK_ECUDA: return "CUDA launch failed";
+    case LK_EUNSUPPORTED: return "no kernel for this combination";
+    case LK_ERANGE: return "size beyond the stated maximum";
+  }
+  return "unknown error";
+}
+
+int lk_version(void) { return 1; }
+
+int64_t lk_row_bytes(int fmt, int64_t k) {
+  int qk = 0, bb = 0;
+  switch (fmt) {
+    case LK_Q4_0: case LK_IQ4_NL: qk = 32; bb = 18; break;
+    case LK_Q4_K: qk = 256; bb = 144; break;
+    case LK_MXFP4: qk = 32; bb = 17; break;
+    case LK_MXFP4S: qk = 32; bb = 16; break;
+    default: return -1;
+  }
+  if (k <= 0 || k % qk) return -1;
+  return k / qk * bb;
+}
+
+// Reads (and optionally clears) the device-side status word: bit 0 = a kernel's bounded wait gave up. Synchronous.
+unsigned int lk_device_status(int clear) { return status_mv(clear != 0) | status_gemm(clear != 0); }
+
+int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,
+               lk_stream_t stream) {
+  if (!w || !out || n_values < 0) return LK_EINVAL;
+  if (lk_row_bytes(fmt, 256) < 0) return LK_EINVAL;
+  if (n_values % (fmt == LK_Q4_K ? 256 : 32)) return LK_EINVAL;
+  if (out_dtype != LK_F32 && out_dtype != LK_F16) return LK_EINVAL;
+  if (fmt == LK_MXFP4S && !w_scales) return LK_EINVAL;
+  if (!aligned(out, 16)) return LK_EALIGN;
+  if (n_values == 0) return LK_OK;
+  return dequant(fmt, w, w_scales, n_values, out, out_dtype, (cudaStream_t)stream);
+}
+
+int lk_row_scale_f16(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, lk_stream_t stream) {
+  if (rows < 0 || k <= 0 || !x || !scales || !x16) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  return row_scale(rows, k, x, x_dtype, scales, x16, nullptr, nullptr, (cudaStream_t)stream);
+}
+
+int lk_row_scale_f8(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
+                    lk_stream_t stream) {
+  if (rows < 0 || k <= 0 || !x || !x8 || !s8) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  return row_scale(rows, k, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
+}
+
+int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
+          float* y, lk_stream_t stream) {
+  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (n <= 0 || k <= 0 || tokens < 0 || !x || !w || !y) return LK_EINVAL;
+  if (k % 256) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
+  if (tokens == 0) return LK_OK;
+  MvArgs a{};
+  a.w = (const uint8_t*)w;
+  a.w2 = (const uint8_t*)w2;
+  a.x = x;
+  a.y = y;
+  a.n = n;
+  a.k = k;
+  a.tokens = tokens;
+  a.accumulate = accumulate;
+  a.x_dtype = x_dtype;
+  a.row_bytes = lk_row_bytes(fmt, k);
+  a.swiglu = w2 != nullptr;
+  return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
+}
+
+int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                     const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
+                     lk_stream_t stream) {
+  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0 || !ids || !x || !w || !y) return LK_EINVAL;
+  if (mode != 0 && mode != 1) return LK_EINVAL;
+  if (k % 256) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (mode == 0 && !fused && !w2) return LK_EINVAL;
+  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
+  if (assignments == 0) return LK_OK;
+  MvArgs a{};
+  a.w = (const uint8_t*)w;
+  a.w2 = (mode == 0 && !fused) ? (const uint8_t*)w2 : nullptr;
+  a.x = x;
+  a.y = y;
+  a.n = n;
+  a.k = k;
+  a.tokens = assignments;
+  a.x_dtype = x_dtype;
+  a.row_bytes = lk_row_bytes(fmt, k);
+  a.ids = ids;
+  a.x_div = mode == 0 ? ku : 1;
+  a.n_experts = n_experts;
+  a.expert_stride = a.row_bytes * n * ((mode == 0 && fused) ? 2 : 1);
+  a.w2_offset = a.row_bytes * n;
+  a.swiglu = mode == 0;
+  return mv(fmt, a, assignments, (cudaStream_t)stream);
+}
+
+int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
+            const void* w2, float* y, lk_stream_t stream) {
+  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (mode != LK_STORE && mode != LK_ACC && mode != LK_SWIGLU) return LK_EINVAL;
+  if (rows < 0 || k <= 0 || n <= 0 || !x16 || !scales || !w || !y) return LK_EINVAL;
+  if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
+  if (k % 256 || n % 16) return LK_EINVAL;
+  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
+  if (rows == 0) return LK_OK;
+  return gemm(fmt, mode, rows, k, n, x16, scales, w, w2, y, (cudaStream_t)stream, nullptr, nullptr, rows, 1, 1, 0, 0);
+}
+
+int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
+                        const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
+                        const void* w, const void* w2, float* y, lk_stream_t stream) {
+  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (!tile_info || !rowmap || !x16 || !scales || !w || !y) return LK_EINVAL;
+  if (mode == LK_SWIGLU && !fused && !w2) return LK_EINVAL;
+  if (k % 256 || n % 16) return LK_EINVAL;
+  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
+  if (rows == 0) return LK_OK;
+  int64_t rb = lk_row_bytes(fmt, k);
+  int64_t stride = rb * n * ((mode == LK_SWIGLU && fused) ? 2 : 1);
+  const void* w2e = (mode == LK_SWIGLU) ? (fused ? nullptr : w2) : nullptr;
+  return gemm(fmt, mode, rows, k, n, x16, scales, w, w2e, y, (cudaStream_t)stream, tile_info, rowmap, xrows, ku,
+              n_experts, stride, (mode == LK_SWIGLU && fused) ? rb * n : 0);
+}
+
+int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8,
+                      const uint8_t* w, const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y,
+                      lk_stream_t stream) {
+  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
+  if (rows < 0 || k <= 0 || n <= 0 || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
+  if (mode == LK_SWIGLU && (!w2 || !w2s)) return LK_EINVAL;
+  if (k % 128 || n % 16) return LK_EINVAL;
+  if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(ws, 16) || !aligned(y, 16)) return LK_EALIGN;
+  if (w2 && (!aligned(w2, 16) || !aligned(w2s, 16))) return LK_EALIGN;
+  if (rows == 0) return LK_OK;
+  return gemm_mxfp4s(mode, order, rows, k, n, x8, s8, w, ws, w2, w2s, y, (cudaStream_t)stream);
+}
+
+int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
+                 const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, lk_stream_t stream) {
+  if (tokens < 0 || n_experts <= 0 || n_experts > 256 || ku <= 0 || ku > 8 || ku > n_experts) return LK_EINVAL;
+  if (gating < 1 || gating > 3 || !x || !ids || !wts) return LK_EINVAL;
+  if (router_w && (h <= 0 || (w_dtype != LK_F32 && w_dtype != LK_BF16))) return LK_EINVAL;
+  if (gating == 1 && bias) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  return moe_route(tokens, h, n_experts, ku, gating, norm, scale, x, router_w, w_dtype, bias, ids, wts,
+                   (cudaStream_t)stream);
+}
+
+int lk_moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_t* info, const int32_t* ids,
+                  int32_t* tile_info, int32_t* rowmap, int32_t* pos, lk_stream_t stream) {
+  if (tokens < 0 || ku <= 0 || n_experts <= 0 || n_experts > 256 || max_tiles <= 0) return LK_EINVAL;
+  if (!ids || !tile_info || !rowmap || !pos) return LK_EINVAL;
+  // worst case (gen_llm.py:5406-5411): every live expert's last tile partly filled
+  int64_t a = int64_t(tokens) * ku;
+  if (int64_t(max_tiles) < (a + 63) / 64 + (a < n_experts ? a : n_experts)) return LK_ERANGE;
+  return moe_bucket(tokens, ku, n_experts, max_tiles, info, ids, tile_info, rowmap, pos, (cudaStream_t)stream);
+}
+
+int lk_moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
+                          const float* wts, float* y, lk_stream_t stream) {
+  if (tokens < 0 || rows <= 0 || h <= 0 || ku <= 0 || ku > 8 || !ys || !pos || !wts || !y) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  return moe_combine_sorted(tokens, rows, h, ku, accumulate, ys, pos, wts, y, (cudaStream_t)stream);
+}
+
+int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
+                   lk_stream_t stream) {
+  if (tokens < 0 || h <= 0 || ku <= 0 || ku > 8 || !ys || !wts || !y) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  return moe_combine(tokens, h, ku, accumulate, ys, wts, y, (cudaStream_t)stream);
+}
+
+}  // extern "C"

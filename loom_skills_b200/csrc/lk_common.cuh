@@ -1,0 +1,224 @@
+// Shared device helpers for liblk (sm_100a): format constants, f16/bf16 bit helpers, mbarrier + bulk-copy (TMA)
+// wrappers and the tcgen05 (5th-gen tensor core / TMEM) instruction wrappers used by the prefill GEMMs.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/lk.h"
+
+#define LK_DEV __device__ __forceinline__
+
+namespace lk {
+
+// ---------------------------------------------------------------------------------------------------------------
+// formats: values and bytes per block (formats.py:5-17)
+// ---------------------------------------------------------------------------------------------------------------
+__host__ __device__ constexpr int qk_of(int fmt) { return fmt == LK_Q4_K ? 256 : 32; }
+__host__ __device__ constexpr int block_bytes_of(int fmt) {
+  return fmt == LK_Q4_K ? 144 : (fmt == LK_MXFP4 ? 17 : (fmt == LK_MXFP4S ? 16 : 18));
+}
+// 256 values of Q4_0, IQ4_NL and Q4_K all take 144 bytes: the unit every streamed chunk is counted in
+constexpr int kChunkValues = 256;
+constexpr int kChunkBytes = 144;
+
+// IQ4_NL codebook (kvalues_iq4nl, quant_values.loom:18-36) biased by +128 so every entry is one unsigned byte
+// (1..241): four little-endian words for a byte-permute lookup
+constexpr uint32_t kIq4Biased0 = (1u) | (24u << 8) | (45u << 16) | (63u << 24);      // -127 -104 -83 -65
+constexpr uint32_t kIq4Biased1 = (79u) | (93u << 8) | (106u << 16) | (118u << 24);   // -49 -35 -22 -10
+constexpr uint32_t kIq4Biased2 = (129u) | (141u << 8) | (153u << 16) | (166u << 24); // 1 13 25 38
+constexpr uint32_t kIq4Biased3 = (181u) | (197u << 8) | (217u << 16) | (241u << 24); // 53 69 89 113
+
+LK_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// 4 nibble codes (bits 0-3 of each byte of `idx`) -> their biased IQ4 codebook bytes
+LK_DEV uint32_t iq4_lookup4(uint32_t idx) {
+  // byte i of the result = table[idx.byte_i]: low 3 bits pick within a half-table, bit 3 picks the half
+  uint32_t sel = (idx & 0x7u) | ((idx >> 4) & 0x70u) | ((idx >> 8) & 0x700u) | ((idx >> 12) & 0x7000u);
+  uint32_t lo = prmt(kIq4Biased0, kIq4Biased1, sel);
+  uint32_t hi = prmt(kIq4Biased2, kIq4Biased3, sel);
+  uint32_t hsel = 0x3210u | ((idx >> 1) & 0x4u) | ((idx >> 5) & 0x40u) | ((idx >> 9) & 0x400u) | ((idx >> 13) & 0x4000u);
+  return prmt(lo, hi, hsel);
+}
+
+LK_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+LK_DEV float bf2f(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+// Q4_K 6-bit (scale, minimum) of group j of a 12-byte scale field (gen_llm.py:234-266)
+LK_DEV void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    m = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// mbarrier + bulk async copies (TMA)
+// ---------------------------------------------------------------------------------------------------------------
+LK_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+LK_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+LK_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+LK_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+LK_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+LK_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+LK_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Device-side status word of this translation unit (bit 0: a bounded wait gave up). Each kernel file defines a
+// reader with LK_STATUS_READER; lk_device_status() ORs them.
+static __device__ unsigned int g_status;
+#define LK_STATUS_READER(name)                                   \
+  unsigned int name(bool clear) {                                \
+    unsigned int v = 0;                                          \
+    cudaMemcpyFromSymbol(&v, g_status, sizeof(v));               \
+    if (clear) {                                                 \
+      unsigned int z = 0;                                        \
+      cudaMemcpyToSymbol(g_status, &z, sizeof(z));               \
+    }                                                            \
+    return v;                                                    \
+  }
+
+// Bounded wait: gives up after kSpinLimit polls and returns false (the caller records the error in g_status and
+// carries on with uniform control flow), so a kernel never spins forever on a phase that will not complete.
+constexpr uint32_t kSpinLimit = 1u << 26;
+LK_DEV bool mbar_wait(uint64_t* bar, uint32_t phase) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, phase)) return true;
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completing on `bar` (both addresses and the size multiples of 16 bytes)
+LK_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 2-D tiled TMA load through a tensor map (no multicast), completing on `bar`
+LK_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+LK_DEV void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05: TMEM allocation, UMMA issue, commit, TMEM loads
+// ---------------------------------------------------------------------------------------------------------------
+LK_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+LK_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+LK_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+LK_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LK_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (f16 or bf16 inputs, f32 accumulate)
+LK_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// kind::f8f6f4 (8-bit e4m3/e5m2 inputs, f32 accumulate)
+LK_DEV void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` when every previously issued tcgen05.mma of this thread has completed
+LK_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle canonical layout: rows of 128 bytes,
+// 8-row groups 1024 bytes apart (SBO), the 16-byte chunks of row r XOR-ed with (r % 8); version 1 (sm_100).
+LK_DEV uint64_t sdesc_k128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFF);     // start address
+  d |= uint64_t(1) << 16;                       // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                       // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                       // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulate, A and B both `ab` (0 = f16, 1 = bf16), both K-major
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, int ab) {
+  return (1u << 4) | (uint32_t(ab) << 7) | (uint32_t(ab) << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+// Instruction descriptor, kind::f8f6f4: f32 accumulate, A format fa, B format fb (0 = e4m3, 1 = e5m2), K-major
+__host__ __device__ constexpr uint32_t idesc_f8(int m, int n, int fa, int fb) {
+  return (1u << 4) | (uint32_t(fa) << 7) | (uint32_t(fb) << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// 32 lanes x 32 consecutive f32 columns of TMEM into registers (warp w reads lanes 32*(w%4) .. +31)
+LK_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// true when `mask` already has the current device's bit; sets it (per-device one-time kernel attribute set-up)
+inline bool once_per_device(unsigned& mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  unsigned bit = 1u << (dev & 31);
+  if (mask & bit) return true;
+  mask |= bit;
+  return false;
+}
+
+LK_DEV float silu(float g) { return g / (1.0f + __expf(-g)); }
+
+}  // namespace lk

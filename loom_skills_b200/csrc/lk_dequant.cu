@@ -1,0 +1,194 @@
+// Standalone block dequantisation and the activation producers (row scale to f16, fp8 twin).
+//
+// lk_dequant   replaces the value helpers @g_<fmt>_values (quant_values.loom:18-91, 386-408; gen_llm.py:288-315,
+//              786-895) and the GEMM's f16 staging dequant16 (gen_gemm.py:281-532, moe_q4_0.py:11-38).
+// row scales   g_row_scale_f16 (gen_llm.py:1843-1912) and its fp8 twin (gen_mxfp4s.py:852-870, 887-938).
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+
+__constant__ float kE2M1[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+__constant__ int kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+// one thread = one 32-value group; writes 32 outputs
+template <int FMT, bool F16OUT>
+__global__ void k_dequant(const uint8_t* __restrict__ w, const uint8_t* __restrict__ ws, int64_t groups,
+                          void* __restrict__ out) {
+  int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= groups) return;
+  float v[32];
+  __half h[32];
+  if (FMT == LK_Q4_0 || FMT == LK_IQ4_NL) {
+    const uint8_t* b = w + gid * 18;
+    float d = h2f(uint16_t(b[0] | (b[1] << 8)));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int lo = b[2 + i] & 15, hi = b[2 + i] >> 4;
+      float cl = FMT == LK_Q4_0 ? float(lo - 8) : float(kIq4Values[lo]);
+      float ch = FMT == LK_Q4_0 ? float(hi - 8) : float(kIq4Values[hi]);
+      v[i] = d * cl;        // exact in f32 (f16 scale x small integer)
+      v[i + 16] = d * ch;
+    }
+    if (F16OUT)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);   // one rounding of the exact value
+  } else if (FMT == LK_Q4_K) {
+    int64_t sb = gid >> 3;
+    int j = int(gid & 7);
+    const uint8_t* b = w + sb * 144;
+    float d = h2f(uint16_t(b[0] | (b[1] << 8)));
+    float dmin = h2f(uint16_t(b[2] | (b[3] << 8)));
+    int sc, m;
+    q4k_scale_min(b + 4, j, sc, m);
+    float a = d * float(sc), c = dmin * float(m);
+    const uint8_t* qs = b + 16 + (j >> 1) * 32;
+    int shift = (j & 1) * 4;
+    __half a16 = __float2half_rn(a), c16 = __float2half_rn(-c);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      int q = (qs[i] >> shift) & 15;
+      v[i] = __fsub_rn(__fmul_rn(a, float(q)), c);   // gguf: d*sc*q - dmin*m, the product exact
+      if (F16OUT) h[i] = __hfma(__int2half_rn(q), a16, c16);   // gen_gemm.py:526-532: one f16 fma
+    }
+  } else if (FMT == LK_MXFP4) {
+    // ggml 17-byte block: E8M0 byte, element i low nibble / i+16 high nibble; value = kv2[q] * 2^(e-128)
+    const uint8_t* b = w + gid * 17;
+    int e = b[0];
+    uint32_t bits = e < 2 ? (0x00200000u << e) : (uint32_t(e - 1) << 23);
+    float half_scale = __uint_as_float(bits);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int lo = b[1 + i] & 15, hi = b[1 + i] >> 4;
+      float kl = 2.0f * kE2M1[lo & 7], kh = 2.0f * kE2M1[hi & 7];
+      // ggml's table holds integers: code 8 is +0, not -0
+      v[i] = half_scale * ((lo & 8) ? -kl : kl) + 0.0f;
+      v[i + 16] = half_scale * ((hi & 8) ? -kh : kh) + 0.0f;
+    }
+    if (F16OUT)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);
+  } else {  // LK_MXFP4S: nibble plane (pairs order: element 2i low nibble, 2i+1 high) + scale plane
+    const uint8_t* b = w + gid * 16;
+    int e = ws[gid];
+    float s = e >= 1 ? __uint_as_float(uint32_t(e) << 23) : __uint_as_float(0x00400000u);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int lo = b[i] & 15, hi = b[i] >> 4;
+      v[2 * i] = ((lo & 8) ? -kE2M1[lo & 7] : kE2M1[lo & 7]) * s;
+      v[2 * i + 1] = ((hi & 8) ? -kE2M1[hi & 7] : kE2M1[hi & 7]) * s;
+    }
+    if (F16OUT)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);
+  }
+  if (F16OUT) {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + gid * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = reinterpret_cast<uint4*>(h)[i];
+  } else {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + gid * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+}
+
+template <int FMT>
+static int launch_dequant(const void* w, const void* ws, int64_t groups, void* out, bool f16, cudaStream_t s) {
+  int threads = 128;
+  int64_t blocks = (groups + threads - 1) / threads;
+  if (f16)
+    k_dequant<FMT, true><<<unsigned(blocks), threads, 0, s>>>((const uint8_t*)w, (const uint8_t*)ws, groups, out);
+  else
+    k_dequant<FMT, false><<<unsigned(blocks), threads, 0, s>>>((const uint8_t*)w, (const uint8_t*)ws, groups, out);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+int dequant(int fmt, const void* w, const void* ws, int64_t n, void* out, int out_dtype, cudaStream_t s) {
+  int64_t groups = n / 32;
+  bool f16 = out_dtype == LK_F16;
+  switch (fmt) {
+    case LK_Q4_0: return launch_dequant<LK_Q4_0>(w, ws, groups, out, f16, s);
+    case LK_IQ4_NL: return launch_dequant<LK_IQ4_NL>(w, ws, groups, out, f16, s);
+    case LK_Q4_K: return launch_dequant<LK_Q4_K>(w, ws, groups, out, f16, s);
+    case LK_MXFP4: return launch_dequant<LK_MXFP4>(w, ws, groups, out, f16, s);
+    case LK_MXFP4S: return launch_dequant<LK_MXFP4S>(w, ws, groups, out, f16, s);
+  }
+  return LK_EINVAL;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// row scales: one 256-thread block per row
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16>
+LK_DEV float load_x(const void* x, int64_t i) {
+  if (BF16) return bf2f(static_cast<const uint16_t*>(x)[i]);
+  return static_cast<const float*>(x)[i];
+}
+
+LK_DEV float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < (blockDim.x >> 5) ? red[l] : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <bool BF16, bool F8>
+__global__ void __launch_bounds__(256) k_row_scale(int k, const void* __restrict__ x, float* __restrict__ scales,
+                                                   __half* __restrict__ x16, uint8_t* __restrict__ x8,
+                                                   float* __restrict__ s8) {
+  __shared__ float red[8];
+  int64_t row = blockIdx.x;
+  const int64_t base = row * k;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < k; i += 256) m = fmaxf(m, fabsf(load_x<BF16>(x, base + i)));
+  m = block_max(m, red);
+  int biased = int((__float_as_uint(m) >> 23) & 255);
+  int e = min(max(biased - 127 - 13, 0), 100);
+  float s = __uint_as_float(uint32_t(127 - e) << 23), inv = __uint_as_float(uint32_t(127 + e) << 23);
+  float fs = 0.0f, finv = 0.0f;
+  if (F8) {
+    fs = __uint_as_float(uint32_t(min(max(261 - biased, 1), 254)) << 23);
+    finv = __uint_as_float(uint32_t(min(max(biased - 15, 1), 254)) << 23);
+  }
+  for (int i = threadIdx.x; i < k; i += 256) {
+    float v = load_x<BF16>(x, base + i);
+    if (x16) x16[base + i] = __float2half_rn(v * s);
+    if (F8) {
+      // e4m3, round to nearest even, saturating finite (the fptrunc of the producer twin)
+      __nv_fp8_storage_t q = __nv_cvt_float_to_fp8(v * fs, __NV_SATFINITE, __NV_E4M3);
+      x8[base + i] = q;
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (scales) {
+      scales[2 * row] = s;
+      scales[2 * row + 1] = inv;
+    }
+    if (F8) {
+      s8[2 * row] = fs;
+      s8[2 * row + 1] = finv;
+    }
+  }
+}
+
+int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
+              cudaStream_t s) {
+  bool bf = x_dtype == LK_BF16;
+  __half* h = reinterpret_cast<__half*>(x16);
+  if (x8) {
+    if (bf) k_row_scale<true, true><<<rows, 256, 0, s>>>(k, x, scales, h, x8, s8);
+    else k_row_scale<false, true><<<rows, 256, 0, s>>>(k, x, scales, h, x8, s8);
+  } else {
+    if (bf) k_row_scale<true, false><<<rows, 256, 0, s>>>(k, x, scales, h, nullptr, nullptr);
+    else k_row_scale<false, false><<<rows, 256, 0, s>>>(k, x, scales, h, nullptr, nullptr);
+  }
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+}  // namespace lk

@@ -1,0 +1,489 @@
+// Prefill GEMM over GGUF block weights on the 5th-generation tensor cores (tcgen05 + TMEM), dense and MoE-grouped.
+//
+// Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704, 706, 1224; dispatch gen_llm.py:4568-4622)
+// and the grouped expert GEMMs g_moe_ggu_{fmt}[_fused]_k{H} / g_moe_gdn_{fmt}_k{F} (gen_moe.py:1126-1228,
+// moe_q4_0.py:126-146):  Y = (X16 . W16^T) * inv[row]  (+ y | silu(G) * U).
+//
+// One CTA computes a 128-row x BN-column output tile (BN = 256; swiglu: 128 columns of each of gate and up):
+//   warp 0      producer: A tiles of X16 by 2-D TMA (128 rows x 64 k, 128-byte swizzle; MoE gate/up: TMA gather4 of
+//               the routed token rows) and the weights' packed bytes by 1-D bulk copies (144 bytes per row per 256 k)
+//   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, M=128, N=256, K=16) from one lane
+//   warps 2-9   dequantise the packed bytes into f16 B tiles in the UMMA K-major 128-byte-swizzle layout -- the
+//               reference's one-rounding staging exactly (f16(d*(q-8)), f16(d*kvalue), fma_f16(q, f16(d*sc),
+//               f16(-dmin*m))) -- then run the epilogue: tcgen05.ld of the f32 accumulators, * inv[row], store.
+// Pipelines: A ring (4 x 16 KB), B ring (2 x 32 KB), packed-bytes ring (2 x 36 KB), each with full/empty mbarriers;
+// the tensor core reads shared memory the dequant warps wrote after a fence.proxy.async.
+#include <mutex>
+
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kSA = 4, kSB = 2, kSR = 2;
+constexpr int kDqWarps = 8;
+constexpr int kGemmThreads = (2 + kDqWarps) * 32;
+
+enum { kDense = 0, kGather = 1, kSorted = 2 };
+
+struct GemmArgs {
+  const uint8_t* w;     // packed weight rows (expert 0 for MoE)
+  const uint8_t* w2;    // second weight (swiglu, not fused) or nullptr
+  const float* scales;  // [rows or xrows][2]
+  float* y;             // [rows][n]
+  int rows, k, n;
+  int64_t row_bytes;
+  // MoE
+  const int32_t* tile_info;   // [max_tiles][2]
+  const int32_t* rowmap;      // [max_tiles*64]
+  int max_tiles;
+  int xrows, ku, n_experts;
+  int64_t expert_stride, w2_offset;
+};
+
+// 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
+LK_DEV uint32_t sw128(int r, int c) { return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+LK_DEV void tma_gather4(void* dst, const CUtensorMap* map, int x, int r0, int r1, int r2, int r3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+LK_DEV uint32_t hsub2u(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+LK_DEV uint32_t hmul2u(uint32_t a, __half2 b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), b);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+LK_DEV uint32_t hfma2u(uint32_t a, __half2 b, __half2 c) {
+  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), b, c);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// 8 codes (bytes of t0, t1; low nibble only) -> 8 f16 (1024 + code), natural k order
+LK_DEV void magic8(uint32_t t0, uint32_t t1, uint32_t (&h)[4]) {
+  h[0] = prmt(t0, 0x64646464u, 0x4140u);
+  h[1] = prmt(t0, 0x64646464u, 0x4342u);
+  h[2] = prmt(t1, 0x64646464u, 0x4140u);
+  h[3] = prmt(t1, 0x64646464u, 0x4342u);
+}
+
+// Dequantise one 32-value group of one weight row into 4 swizzled 16-byte chunks of the B tile.
+//   raw    : the row's 144-byte packed chunk (256 values) in shared memory
+//   j      : group within the chunk (0..7); b_tile: the B stage; r: tile row; c0: first 16-byte chunk (0 or 4)
+template <int FMT>
+LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int c0) {
+  uint32_t q[4];   // 16 packed bytes holding the group's 32 codes
+  __half2 scale, offset;
+  bool hi_half_is_next;   // Q4_0 / IQ4: values 16..31 are the high nibbles of the same 16 bytes
+  if (FMT == LK_Q4_K) {
+    const uint8_t* qs = raw + 16 + 32 * (j >> 1);
+    uint4 a = *reinterpret_cast<const uint4*>(qs);
+    uint4 b = *reinterpret_cast<const uint4*>(qs + 16);
+    uint32_t sh = (j & 1) * 4;
+    // 32 codes: byte l's nibble (low for even groups, high for odd) is value l
+    uint32_t c[8] = {(a.x >> sh) & 0x0F0F0F0Fu, (a.y >> sh) & 0x0F0F0F0Fu, (a.z >> sh) & 0x0F0F0F0Fu,
+                     (a.w >> sh) & 0x0F0F0F0Fu, (b.x >> sh) & 0x0F0F0F0Fu, (b.y >> sh) & 0x0F0F0F0Fu,
+                     (b.z >> sh) & 0x0F0F0F0Fu, (b.w >> sh) & 0x0F0F0F0Fu};
+    uint4 hd = *reinterpret_cast<const uint4*>(raw);
+    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hd);
+    float d = h2f(uint16_t(hd.x & 0xffff)), dmin = h2f(uint16_t(hd.x >> 16));
+    int sc, m;
+    q4k_scale_min(hb + 4, j, sc, m);
+    __half a16 = __float2half_rn(d * float(sc)), c16 = __float2half_rn(-(dmin * float(m)));
+    scale = __halves2half2(a16, a16);
+    offset = __halves2half2(c16, c16);
+    const uint32_t k1024 = 0x64006400u;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t h[4];
+      magic8(c[2 * cc], c[2 * cc + 1], h);
+      uint4 out;
+      out.x = hfma2u(hsub2u(h[0], k1024), scale, offset);
+      out.y = hfma2u(hsub2u(h[1], k1024), scale, offset);
+      out.z = hfma2u(hsub2u(h[2], k1024), scale, offset);
+      out.w = hfma2u(hsub2u(h[3], k1024), scale, offset);
+      *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
+    }
+    (void)hi_half_is_next;
+    return;
+  }
+  // Q4_0 / IQ4_NL: 18-byte block j at raw + 18j: f16 d, then 16 code bytes (2-byte aligned)
+  const uint8_t* blk = raw + 18 * j;
+  const uint16_t* p16 = reinterpret_cast<const uint16_t*>(blk);
+  float d = h2f(p16[0]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = uint32_t(p16[1 + 2 * i]) | (uint32_t(p16[2 + 2 * i]) << 16);
+  __half dh = __float2half_rn(d);
+  scale = __halves2half2(dh, dh);
+  const uint32_t koff = FMT == LK_Q4_0 ? 0x64086408u : 0x64806480u;   // f16 1032 (1024 + 8) | 1152 (1024 + 128)
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    // chunk cc: values 8cc .. 8cc+7 = (cc < 2 ? low : high) nibbles of bytes 8*(cc&1) .. +7
+    uint32_t w0 = q[2 * (cc & 1)], w1 = q[2 * (cc & 1) + 1];
+    uint32_t t0 = ((cc >= 2) ? (w0 >> 4) : w0) & 0x0F0F0F0Fu;
+    uint32_t t1 = ((cc >= 2) ? (w1 >> 4) : w1) & 0x0F0F0F0Fu;
+    if (FMT == LK_IQ4_NL) {
+      t0 = iq4_lookup4(t0);
+      t1 = iq4_lookup4(t1);
+    }
+    uint32_t h[4];
+    magic8(t0, t1, h);
+    uint4 out;
+    // exact centred code (q - 8, or the kvalue), then one f16 multiply by d: the reference's single rounding
+    out.x = hmul2u(hsub2u(h[0], koff), scale);
+    out.y = hmul2u(hsub2u(h[1], koff), scale);
+    out.z = hmul2u(hsub2u(h[2], koff), scale);
+    out.w = hmul2u(hsub2u(h[3], koff), scale);
+    *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
+  }
+  (void)offset;
+  (void)hi_half_is_next;
+}
+
+template <int FMT, int BN, int NW, int MODE, int GROUP>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap amap, const GemmArgs p) {
+  constexpr int kRowsB = BN * NW;                 // weight rows dequantised per stage (256)
+  constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+  constexpr int kBBytes = kRowsB * kBK * 2;       // 32 KB
+  constexpr int kRBytes = kRowsB * kChunkBytes;   // 36 KB
+  constexpr uint32_t kTmemCols = BN * NW;         // 256
+  static_assert(kRowsB == 2 * kDqWarps * 16 || kRowsB == kDqWarps * 16, "one or two rows per dequant thread");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kSA * kABytes;
+  uint8_t* sR = sB + kSB * kBBytes;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + kSR * kRBytes);
+  uint64_t* empty_a = full_a + kSA;
+  uint64_t* full_b = empty_a + kSA;
+  uint64_t* empty_b = full_b + kSB;
+  uint64_t* full_r = empty_b + kSB;
+  uint64_t* empty_r = full_r + kSR;
+  uint64_t* acc_full = empty_r + kSR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  int* tile_meta = reinterpret_cast<int*>(tmem_slot + 4);   // [0] expert, [1] first 64-row tile, [2] valid rows
+  int* arow = tile_meta + 4;                               // [128] gathered source rows (kGather)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int kstages = p.k / kBK;
+
+  // ---- which rows: dense tile, or a 128-row super-tile of one expert made of <= 2 schedule tiles
+  int m0 = blockIdx.y * kBM;
+  int valid_rows = min(kBM, p.rows - m0);
+  const uint8_t* wb = p.w;
+  const uint8_t* w2b = p.w2;
+  if (GROUP != kDense) {
+    if (threadIdx.x == 0) {
+      // super-tile s = blockIdx.y: walk tile_info (experts in order), pairing consecutive tiles of one expert
+      int s = 0, found = -1, first = 0, nrows = 0;
+      for (int t = 0; t < p.max_tiles;) {
+        int e = p.tile_info[2 * t];
+        if (e < 0) break;
+        int rows0 = p.tile_info[2 * t + 1];
+        bool pair = t + 1 < p.max_tiles && p.tile_info[2 * (t + 1)] == e;
+        int rows = rows0 + (pair ? p.tile_info[2 * (t + 1) + 1] : 0);
+        if (s == int(blockIdx.y)) {
+          found = e;
+          first = t;
+          nrows = pair ? 64 + p.tile_info[2 * (t + 1) + 1] : rows0;
+          break;
+        }
+        (void)rows;
+        ++s;
+        t += pair ? 2 : 1;
+      }
+      tile_meta[0] = found;
+      tile_meta[1] = first;
+      tile_meta[2] = nrows;
+    }
+    __syncthreads();
+    if (tile_meta[0] < 0) return;   // no such super-tile: this launch had more CTAs than the schedule needs
+    int e = min(tile_meta[0], p.n_experts - 1);
+    m0 = tile_meta[1] * 64;
+    valid_rows = tile_meta[2];
+    wb = p.w + int64_t(e) * p.expert_stride;
+    if (NW == 2) w2b = p.w2 ? p.w2 + int64_t(e) * p.expert_stride : wb + p.w2_offset;
+    if (GROUP == kGather && threadIdx.x < kBM) {
+      int r = threadIdx.x;
+      int a = r < valid_rows ? p.rowmap[m0 + r] : -1;
+      arow[r] = a >= 0 ? a / p.ku : p.xrows;   // out-of-range row -> TMA fills zeros
+    }
+  }
+  const int nb_rows = min(BN, p.n - n0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSA; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < kSB; ++i) {
+      mbar_init(&full_b[i], kDqWarps);
+      mbar_init(&empty_b[i], 1);
+    }
+    for (int i = 0; i < kSR; ++i) {
+      mbar_init(&full_r[i], 1);
+      mbar_init(&empty_r[i], kDqWarps);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) prefetch_tensormap(&amap);
+    for (int ks = 0; ks < kstages; ++ks) {
+      if ((ks & 3) == 0) {
+        int c = ks >> 2, sr = c % kSR;
+        if (c >= kSR && !mbar_wait(&empty_r[sr], ((c / kSR) - 1) & 1)) atomicOr(&g_status, 1u);
+        if (lane == 0) mbar_expect_tx(&full_r[sr], uint32_t(nb_rows * NW * kChunkBytes));
+        __syncwarp();
+        for (int i = lane; i < kRowsB; i += 32) {
+          int wi = i / BN, r = i % BN;
+          if (r < nb_rows) {
+            const uint8_t* src = (wi ? w2b : wb) + int64_t(n0 + r) * p.row_bytes + int64_t(c) * kChunkBytes;
+            bulk_g2s(sR + sr * kRBytes + i * kChunkBytes, src, kChunkBytes, &full_r[sr]);
+          }
+        }
+      }
+      int sa = ks % kSA;
+      if (ks >= kSA && !mbar_wait(&empty_a[sa], ((ks / kSA) - 1) & 1)) atomicOr(&g_status, 1u);
+      if (GROUP == kGather) {
+        if (lane == 0) mbar_expect_tx(&full_a[sa], kABytes);
+        __syncwarp();
+        // 32 lanes x 4 rows: one gather4 each (row boxes of 64 f16 = 128 bytes)
+        int r = lane * 4;
+        tma_gather4(sA + sa * kABytes + r * 128, &amap, ks * kBK, arow[r], arow[r + 1], arow[r + 2], arow[r + 3],
+                    &full_a[sa]);
+      } else if (lane == 0) {
+        mbar_expect_tx(&full_a[sa], kABytes);
+        tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
+    const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+    for (int ks = 0; ks < kstages; ++ks) {
+      int sa = ks % kSA, sb = ks % kSB;
+      if (!mbar_wait(&full_a[sa], (ks / kSA) & 1)) atomicOr(&g_status, 1u);
+      if (!mbar_wait(&full_b[sb], (ks / kSB) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          uint64_t ad = sdesc_k128(a_base + sa * kABytes + kk * 32);
+#pragma unroll
+          for (int wi = 0; wi < NW; ++wi) {
+            uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
+            umma_f16(tmem + wi * BN, ad, bd, idesc, (ks | kk) != 0);
+          }
+        }
+        umma_commit(&empty_a[sa]);
+        umma_commit(&empty_b[sb]);
+        if (ks == kstages - 1) umma_commit(acc_full);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ dequant warps, then the epilogue
+    const int dt = threadIdx.x - 64;   // 0..255
+    constexpr int kGroupsPerThread = kRowsB * 2 / (kDqWarps * 32);   // 2 (256 rows) or 1 (128 rows)
+    for (int ks = 0; ks < kstages; ++ks) {
+      int c = ks >> 2, sub = ks & 3, sr = c % kSR, sb = ks % kSB;
+      if (sub == 0 && !mbar_wait(&full_r[sr], (c / kSR) & 1)) atomicOr(&g_status, 1u);
+      if (ks >= kSB && !mbar_wait(&empty_b[sb], ((ks / kSB) - 1) & 1)) atomicOr(&g_status, 1u);
+      uint8_t* bt = sB + sb * kBBytes;
+#pragma unroll
+      for (int gi = 0; gi < kGroupsPerThread; ++gi) {
+        int item = dt * kGroupsPerThread + gi;   // (row, half) pairs
+        int r = item >> 1, h = item & 1;
+        dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&full_b[sb]);
+        if (sub == 3) mbar_arrive(&empty_r[sr]);
+      }
+    }
+    // epilogue: warp quadrant q reads TMEM lanes 32q..32q+31 (= tile rows); two warps per quadrant split columns
+    if (!mbar_wait(acc_full, 0)) atomicOr(&g_status, 1u);
+    tc_fence_after();
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = 32 * q + lane;
+    const bool row_ok = row < valid_rows;
+    float inv = 0.f;
+    float* yrow = nullptr;
+    if (row_ok) {
+      int grow = m0 + row;
+      int srow = grow;
+      if (GROUP == kGather) {
+        int a = p.rowmap[grow];
+        srow = a >= 0 ? a / p.ku : -1;
+      }
+      inv = srow >= 0 ? p.scales[2 * int64_t(srow) + 1] : 0.f;
+      yrow = p.y + int64_t(grow) * p.n + n0;
+    }
+    constexpr int kColsPerWarp = BN / 2;
+#pragma unroll 1
+    for (int cb = 0; cb < kColsPerWarp; cb += 32) {
+      int col = half * kColsPerWarp + cb;
+      float v[32];
+      tmem_ld32(tmem + (uint32_t(32 * q) << 16) + col, v);
+      if (NW == 2) {
+        float u[32];
+        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + BN + col, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= inv;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          if (col + i >= nb_rows) break;
+          float4* dst = reinterpret_cast<float4*>(yrow + col + i);
+          float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          if (MODE == LK_ACC) {
+            float4 old = *dst;
+            o.x += old.x;
+            o.y += old.y;
+            o.z += old.z;
+            o.w += old.w;
+          }
+          *dst = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a row-major [rows][cols] matrix of 16-bit or 8-bit elements, box = box_cols x box_rows, 128-byte swizzle
+int make_map_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols, int box_cols,
+                int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LK_ECUDA;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols * elem_bytes)};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LK_OK : LK_EINVAL;
+}
+
+template <int FMT, int BN, int NW, int MODE, int GROUP>
+static int launch_gemm(const CUtensorMap& map, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+  constexpr int kRowsB = BN * NW;
+  constexpr int smem = 1024 + kSA * kBM * kBK * 2 + kSB * kRowsB * kBK * 2 + kSR * kRowsB * kChunkBytes + 256 + 32 +
+                       kBM * 4;
+  auto kern = k_gemm<FMT, BN, NW, MODE, GROUP>;
+  static unsigned configured = 0;
+  if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  kern<<<grid, kGemmThreads, smem, s>>>(map, a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+template <int FMT>
+static int gemm_fmt(int mode, int group, const CUtensorMap& map, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+  if (group == kDense) {
+    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense>(map, a, grid, s);
+    if (mode == LK_ACC) return launch_gemm<FMT, 256, 1, LK_ACC, kDense>(map, a, grid, s);
+    return launch_gemm<FMT, 256, 1, LK_STORE, kDense>(map, a, grid, s);
+  }
+  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather>(map, a, grid, s);
+  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted>(map, a, grid, s);
+}
+
+int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
+         const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
+         int n_experts, int64_t expert_stride, int64_t w2_offset) {
+  GemmArgs a{};
+  a.w = (const uint8_t*)w;
+  a.w2 = (const uint8_t*)w2;
+  a.scales = scales;
+  a.y = y;
+  a.rows = rows;
+  a.k = k;
+  a.n = n;
+  a.row_bytes = lk_row_bytes(fmt, k);
+  int group = kDense;
+  if (tile_info) {
+    group = mode == LK_SWIGLU ? kGather : kSorted;
+    a.tile_info = tile_info;
+    a.rowmap = rowmap;
+    a.max_tiles = rows / 64;
+    a.xrows = xrows;
+    a.ku = ku;
+    a.n_experts = n_experts;
+    a.expert_stride = expert_stride;
+    a.w2_offset = w2_offset;
+  }
+  CUtensorMap map;
+  int rc;
+  if (group == kGather)
+    rc = make_map_2d(&map, x16, 2, xrows, k, kBK, 1);       // one-row boxes for gather4
+  else
+    rc = make_map_2d(&map, x16, 2, group == kSorted ? rows : rows, k, kBK, kBM);
+  if (rc != LK_OK) return rc;
+  int bn = (mode == LK_SWIGLU) ? 128 : 256;
+  // grouped: one CTA per possible 128-row super-tile (at most one per schedule tile)
+  dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + kBM - 1) / kBM : rows / 64);
+  switch (fmt) {
+    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, map, a, grid, s);
+    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, map, a, grid, s);
+    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, map, a, grid, s);
+  }
+  return LK_EUNSUPPORTED;
+}
+
+LK_STATUS_READER(status_gemm)
+
+}  // namespace lk

@@ -1,0 +1,35 @@
+// Internal launchers shared between the kernel files and the C-ABI layer (lk_api.cu). Validation happens in lk_api.cu;
+// these assume their arguments were checked.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lk {
+
+int dequant(int fmt, const void* w, const void* ws, int64_t n_values, void* out, int out_dtype, cudaStream_t s);
+int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
+              cudaStream_t s);
+
+// decode matvec, dense and per-assignment (MoE) forms
+struct MvArgs {
+  const uint8_t* w;      // packed rows of the first weight (expert 0 for MoE)
+  const uint8_t* w2;     // second weight (swiglu) or nullptr
+  const void* x;         // activations [x_rows][k]
+  float* y;              // outputs [y_rows][n]
+  int n, k;
+  int tokens;            // dense: number of token rows
+  int accumulate;
+  int x_dtype;
+  int64_t row_bytes;
+  // MoE per-assignment mode (ids != nullptr): CTA column g = assignment, expert = ids[g],
+  // x row = g / x_div (gu: x_div = ku; dn: 1), y row = g
+  const int32_t* ids;
+  int x_div;
+  int n_experts;
+  int64_t expert_stride;   // bytes between experts of w
+  int64_t w2_offset;       // bytes from w to w2 inside an expert (fused gate/up), used when w2 == nullptr && swiglu
+  int swiglu;
+};
+int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
+
+}  // namespace lk

@@ -1,0 +1,262 @@
+// MoE routing, the GPU-built per-expert tile schedule, and the weighted combines.
+//
+// g_moe_route / g_moe_route_tr  gen_moe.py:116-253, 255-470   router logits, gating, top-k, weights
+// g_moe_bucket                   gen_moe.py:829-955             tile_info / rowmap / pos
+// g_moe_combine_sorted           gen_moe.py:1231-1280           y[t] (+)= sum_k w[t,k] ys[pos[t,k]]
+// g_moe_combine                  gen_moe.py:730-762             y[t] (+)= sum_k w[t,k] ys[t*KU + k]
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+
+constexpr int kTile = 64;   // gen_moe.py:826 TILE
+
+// ---------------------------------------------------------------------------------------------------------------
+// router: one 256-thread block per token; thread e owns expert e
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16W>
+__global__ void __launch_bounds__(256) k_route(int h, int E, int ku, int gating, int norm, float scale,
+                                               const float* __restrict__ x, const void* __restrict__ router_w,
+                                               const float* __restrict__ bias, int32_t* __restrict__ ids,
+                                               float* __restrict__ wts) {
+  __shared__ float logit[256];
+  __shared__ float red_f[8];
+  __shared__ int red_i[8];
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (router_w) {
+    // warp w scores experts w, w+8, ...: lanes stride over h, then a warp sum
+    const float* xr = x + int64_t(t) * h;
+    for (int e = warp; e < E; e += 8) {
+      float acc = 0.f;
+      if (BF16W) {
+        const uint16_t* wr = static_cast<const uint16_t*>(router_w) + int64_t(e) * h;
+        for (int i = lane; i < h; i += 32) acc = fmaf(xr[i], bf2f(wr[i]), acc);
+      } else {
+        const float* wr = static_cast<const float*>(router_w) + int64_t(e) * h;
+        for (int i = lane; i < h; i += 32) acc = fmaf(xr[i], wr[i], acc);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) logit[e] = acc;
+    }
+  } else {
+    for (int e = tid; e < E; e += 256) logit[e] = x[int64_t(t) * E + e];
+  }
+  __syncthreads();
+  const bool in = tid < E;
+  const float lg = in ? logit[tid] : -INFINITY;
+  auto bmax = [&](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) red_f[warp] = v;
+    __syncthreads();
+    float r = red_f[0];
+    for (int i = 1; i < 8; ++i) r = fmaxf(r, red_f[i]);
+    return r;
+  };
+  auto bsum = [&](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red_f[warp] = v;
+    __syncthreads();
+    float r = 0.f;
+    for (int i = 0; i < 8; ++i) r += red_f[i];
+    return r;
+  };
+  auto bmin_i = [&](int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) red_i[warp] = v;
+    __syncthreads();
+    int r = red_i[0];
+    for (int i = 1; i < 8; ++i) r = min(r, red_i[i]);
+    return r;
+  };
+  // probability (the weight's source) and selection score
+  float prob, score;
+  if (gating == 1) {
+    float m = bmax(lg);
+    float ex = in ? expf(lg - m) : 0.f;
+    float den = bsum(ex);
+    prob = ex / den;
+    score = in ? lg : -INFINITY;   // softmax is monotonic in the logit: rank on the exact input
+  } else if (gating == 2) {
+    prob = in ? 1.0f / (1.0f + expf(-lg)) : 0.f;
+    score = in ? prob + (bias ? bias[tid] : 0.f) : -INFINITY;
+  } else {
+    prob = in ? lg + (bias ? bias[tid] : 0.f) : -INFINITY;
+    score = prob;
+  }
+  // ku rounds: the best score, ties to the lowest expert index
+  int my_k = -1;
+  float sc = score, sel_sum = 0.f;
+  for (int r = 0; r < ku; ++r) {
+    float best = bmax(sc);
+    int cand = (in && sc == best) ? tid : 1 << 30;
+    int winner = bmin_i(cand);
+    if (tid == winner) {
+      my_k = r;
+      ids[int64_t(t) * ku + r] = tid;
+      sc = -INFINITY;
+    }
+    sel_sum += bsum(tid == winner ? prob : 0.f);
+  }
+  float wv;
+  if (gating == 3) {
+    float m = bmax(my_k >= 0 ? prob : -INFINITY);
+    float ex = my_k >= 0 ? expf(prob - m) : 0.f;
+    float den = bsum(ex);
+    wv = ex / den;
+  } else {
+    float den = norm ? fmaxf(sel_sum, 6.103515625e-05f) : 1.0f;
+    wv = prob / den;
+  }
+  if (my_k >= 0) wts[int64_t(t) * ku + my_k] = wv * scale;
+}
+
+int moe_route(int tokens, int h, int E, int ku, int gating, int norm, float scale, const float* x,
+              const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s) {
+  if (w_dtype == LK_BF16)
+    k_route<true><<<tokens, 256, 0, s>>>(h, E, ku, gating, norm, scale, x, router_w, bias, ids, wts);
+  else
+    k_route<false><<<tokens, 256, 0, s>>>(h, E, ku, gating, norm, scale, x, router_w, bias, ids, wts);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// bucket: one 1024-thread block. Counting sort by expert, stable in the assignment index, so the schedule is
+// deterministic (the reference's atomics give any order within an expert's rows).
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int max_tiles,
+                                                 const int32_t* __restrict__ info, const int32_t* __restrict__ ids,
+                                                 int32_t* __restrict__ tile_info, int32_t* __restrict__ rowmap,
+                                                 int32_t* __restrict__ pos) {
+  __shared__ int count[256];
+  __shared__ int cursor[256];
+  __shared__ int tbase[257];
+  __shared__ int wcnt[32][256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int A = tokens * ku;
+  for (int i = tid; i < 256; i += 1024) count[i] = 0;
+  for (int i = tid; i < 32 * 256; i += 1024) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  auto expert_of = [&](int a) -> int {
+    int t = a / ku;
+    if (info && info[4 * t + 2] == 0) return -1;
+    return min(max(ids[a], 0), E - 1);
+  };
+  for (int a = tid; a < A; a += 1024) {
+    int e = expert_of(a);
+    if (e >= 0) atomicAdd(&count[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      tbase[e] = acc;
+      acc += (count[e] + kTile - 1) / kTile;
+    }
+    tbase[E] = acc;
+  }
+  __syncthreads();
+  const int total = tbase[E];
+  if (tid < E) {
+    int n = count[tid], tiles = (n + kTile - 1) / kTile;
+    for (int j = 0; j < tiles; ++j) {
+      int tile = tbase[tid] + j;
+      if (tile < max_tiles) {
+        tile_info[2 * tile] = tid;
+        tile_info[2 * tile + 1] = min(kTile, n - j * kTile);
+      }
+    }
+    cursor[tid] = tbase[tid] * kTile;
+  }
+  for (int u = total + tid; u < max_tiles; u += 1024) {
+    tile_info[2 * u] = -1;
+    tile_info[2 * u + 1] = 0;
+  }
+  // padding rows of used tiles and every row of unused tiles
+  for (int e = 0; e < E; ++e) {
+    int first = tbase[e] * kTile + count[e], end = tbase[e + 1] * kTile;
+    for (int r = first + tid; r < end; r += 1024)
+      if (r < max_tiles * kTile) rowmap[r] = -1;
+  }
+  for (int r = total * kTile + tid; r < max_tiles * kTile; r += 1024) rowmap[r] = -1;
+  __syncthreads();
+  // stable placement, 1024 assignments per round
+  for (int base = 0; base < A; base += 1024) {
+    int a = base + tid;
+    int e = a < A ? expert_of(a) : -2;
+    unsigned peers = __match_any_sync(0xffffffffu, e);
+    int rank = __popc(peers & ((1u << lane) - 1));
+    bool leader = rank == 0;
+    if (e >= 0 && leader) wcnt[warp][e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int off = cursor[e] + rank;
+      for (int w = 0; w < warp; ++w) off += wcnt[w][e];
+      if (off < max_tiles * kTile) rowmap[off] = a;
+      pos[a] = off;
+    } else if (e == -1) {
+      pos[a] = -1;
+    }
+    __syncthreads();
+    if (tid < E) {
+      int add = 0;
+      for (int w = 0; w < 32; ++w) add += wcnt[w][tid];
+      cursor[tid] += add;
+    }
+    __syncthreads();
+    if (e >= 0 && leader) wcnt[warp][e] = 0;
+    __syncthreads();
+  }
+}
+
+int moe_bucket(int tokens, int ku, int E, int max_tiles, const int32_t* info, const int32_t* ids, int32_t* tile_info,
+               int32_t* rowmap, int32_t* pos, cudaStream_t s) {
+  k_bucket<<<1, 1024, 0, s>>>(tokens, ku, E, max_tiles, info, ids, tile_info, rowmap, pos);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// combines: one block per token; the fma chain runs over k in order, as the reference's
+// ---------------------------------------------------------------------------------------------------------------
+template <bool SORTED>
+__global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, const float* __restrict__ ys,
+                                                 const int32_t* __restrict__ pos, const float* __restrict__ wts,
+                                                 float* __restrict__ y) {
+  const int t = blockIdx.x;
+  __shared__ float w[8];
+  __shared__ int p[8];
+  if (threadIdx.x < ku) {
+    w[threadIdx.x] = wts[int64_t(t) * ku + threadIdx.x];
+    p[threadIdx.x] = SORTED ? pos[int64_t(t) * ku + threadIdx.x] : t * ku + threadIdx.x;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < h; c += 256) {
+    float acc = accumulate ? y[int64_t(t) * h + c] : 0.f;
+    for (int k = 0; k < ku; ++k) {
+      float v = p[k] >= 0 ? ys[int64_t(p[k]) * h + c] : 0.f;
+      acc = fmaf(w[k], v, acc);
+    }
+    y[int64_t(t) * h + c] = acc;
+  }
+}
+
+int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
+                       const float* wts, float* y, cudaStream_t s) {
+  (void)rows;
+  k_combine<true><<<tokens, 256, 0, s>>>(h, ku, accumulate, ys, pos, wts, y);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
+                cudaStream_t s) {
+  k_combine<false><<<tokens, 256, 0, s>>>(h, ku, accumulate, ys, nullptr, wts, y);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+}  // namespace lk

@@ -1,0 +1,230 @@
+"""Host-side mirror of the reference generators' op interface for the quantized-matmul path, on torch CUDA tensors.
+
+Each function launches liblk kernels on the current CUDA stream through the C ABI (include/lk.h). The operand names,
+order and meaning follow the reference's kernel launch signatures (paths relative to the loom-skills checkout):
+
+  mv                 g_mv_{fmt}_k{K}...           gen_llm.py:1185-1194   (%n, %tokens, %accumulate, %x, %w[, %w2], %y)
+  row_scale_f16      g_row_scale_f16              gen_llm.py:1843-1912   (%rows, %k, %x, %scales, %x16)
+  row_scale_f8       g_row_scale_f16_f8_rdna4     gen_mxfp4s.py:887-938  (..., %x16, %x8, %s8, %w16)
+  gemm               g_gemm_{fmt}_{mode}          gen_gemm.py:549-556    (%rows, %k, %n, %x, %scales, %w[, %w2], %y)
+  gemm_mxfp4s_f8     g_gemm_mxfp4s_*_f8_m256      gen_mxfp4s.py:101      (%rows, %k, %n, %x, %scales, %w, %ws, ..., %y)
+  moe_route          g_moe_route[_tr]             gen_moe.py:116-470     (%tokens, %h, %router_w, %bias, %ids, %wts)
+  moe_bucket         g_moe_bucket                 gen_moe.py:829-955     (%tokens, %max_tiles, %info, %ids, %tile_info,
+                                                                          %rowmap, %pos)
+  moe_grouped_gemm   g_moe_ggu_* / g_moe_gdn_*    gen_moe.py:1126-1228   (%rows, %k, %n, %xrows, %tile_info, %rowmap,
+                                                                          %x, %scales, %w[, %w2], %y)
+  moe_combine_sorted g_moe_combine_sorted         gen_moe.py:1231-1280   (%tokens, %rows, %ys, %pos, %wts, %y)
+  moe_expert_mv      g_moe_gu_* / g_moe_dn_*      gen_moe.py:535-727
+  moe_combine        g_moe_combine                gen_moe.py:730-762
+
+Errors raise LkError (the C ABI's negative return codes). There is no CPU fallback: tensors must be on a CUDA device.
+"""
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}
+
+
+def _fmt(fmt):
+    return L.FMT_IDS[fmt] if isinstance(fmt, str) else int(fmt)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise L.LkError("liblk ops take CUDA tensors (there is no CPU path)")
+
+
+def row_bytes(fmt, k):
+    return int(L.load().lk_row_bytes(_fmt(fmt), k))
+
+
+def device_status(clear=True):
+    """Bit 0 set: a kernel's bounded wait gave up since the last clear (its results are invalid)."""
+    return int(L.load().lk_device_status(1 if clear else 0))
+
+
+def dequant(fmt, w, n_values, out_dtype=torch.float32, w_scales=None):
+    """Packed blocks -> values (f32 exact, or the GEMM's f16 staging)."""
+    _cuda(w, w_scales)
+    out = torch.empty(n_values, dtype=out_dtype, device=w.device)
+    L.check(L.load().lk_dequant(_fmt(fmt), _ptr(w), _ptr(w_scales), n_values, _ptr(out), _DT[out_dtype], _stream()),
+            "lk_dequant")
+    return out
+
+
+def row_scale_f16(x):
+    """x [rows][k] (f32 or bf16) -> (x16 [rows][k] f16, scales [rows][2] f32)."""
+    _cuda(x)
+    x = x.contiguous()
+    rows, k = x.shape
+    x16 = torch.empty(rows, k, dtype=torch.float16, device=x.device)
+    sc = torch.empty(rows, 2, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_row_scale_f16(rows, k, _ptr(x), _DT[x.dtype], _ptr(sc), _ptr(x16), _stream()),
+            "lk_row_scale_f16")
+    return x16, sc
+
+
+def row_scale_f8(x, with_f16=False):
+    """x [rows][k] -> (x8 e4m3 bytes [rows][k] uint8, s8 [rows][2]) (+ (x16, scales) when with_f16)."""
+    _cuda(x)
+    x = x.contiguous()
+    rows, k = x.shape
+    x8 = torch.empty(rows, k, dtype=torch.uint8, device=x.device)
+    s8 = torch.empty(rows, 2, dtype=torch.float32, device=x.device)
+    x16 = torch.empty(rows, k, dtype=torch.float16, device=x.device) if with_f16 else None
+    sc = torch.empty(rows, 2, dtype=torch.float32, device=x.device) if with_f16 else None
+    L.check(L.load().lk_row_scale_f8(rows, k, _ptr(x), _DT[x.dtype], _ptr(sc), _ptr(x16), _ptr(x8), _ptr(s8),
+                                     _stream()), "lk_row_scale_f8")
+    return (x8, s8, x16, sc) if with_f16 else (x8, s8)
+
+
+def mv(fmt, w, x, n, k, w2=None, y=None, accumulate=False):
+    """Decode matvec: y[t][n] (+)= x[t] . W[n] (swiglu with w2). x [tokens][k] f32/f16/bf16."""
+    _cuda(w, x, w2, y)
+    x = x.contiguous()
+    tokens = x.shape[0]
+    if y is None:
+        y = torch.empty(tokens, n, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_mv(_fmt(fmt), n, k, tokens, 1 if accumulate else 0, _ptr(x), _DT[x.dtype], _ptr(w), _ptr(w2),
+                           _ptr(y), _stream()), "lk_mv")
+    return y
+
+
+def gemm(fmt, mode, x16, scales, w, n, w2=None, y=None):
+    """Prefill GEMM: y[rows][n] (+)= (x16 . W16^T) * scales[row][1]; mode 'store' | 'acc' | 'swiglu'."""
+    _cuda(x16, scales, w, w2, y)
+    rows, k = x16.shape
+    if y is None:
+        y = torch.empty(rows, n, dtype=torch.float32, device=x16.device)
+    m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
+    L.check(L.load().lk_gemm(_fmt(fmt), m, rows, k, n, _ptr(x16), _ptr(scales), _ptr(w), _ptr(w2), _ptr(y),
+                             _stream()), "lk_gemm")
+    return y
+
+
+def gemm_mxfp4s_f8(mode, x8, s8, w, ws, n, w2=None, w2s=None, order=L.ORDER_PAIRS, y=None):
+    """MXFP4 split planes x e4m3: y = (x8 . (W * 2^8)^T) * s8[row][1]."""
+    _cuda(x8, s8, w, ws, w2, w2s, y)
+    rows, k = x8.shape
+    if y is None:
+        y = torch.empty(rows, n, dtype=torch.float32, device=x8.device)
+    m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
+    L.check(L.load().lk_gemm_mxfp4s_f8(m, order, rows, k, n, _ptr(x8), _ptr(s8), _ptr(w), _ptr(ws), _ptr(w2),
+                                       _ptr(w2s), _ptr(y), _stream()), "lk_gemm_mxfp4s_f8")
+    return y
+
+
+def moe_route(x, n_experts, ku, router_w=None, gating=1, norm=True, scale=1.0, bias=None):
+    """Router top-k. router_w None: x is the logits [tokens][n_experts] (f32)."""
+    _cuda(x, router_w, bias)
+    x = x.contiguous().float()
+    tokens = x.shape[0]
+    ids = torch.empty(tokens, ku, dtype=torch.int32, device=x.device)
+    wts = torch.empty(tokens, ku, dtype=torch.float32, device=x.device)
+    h = x.shape[1] if router_w is not None else 0
+    wdt = _DT[router_w.dtype] if router_w is not None else L.F32
+    L.check(L.load().lk_moe_route(tokens, h, n_experts, ku, gating, 1 if norm else 0, scale, _ptr(x), _ptr(router_w),
+                                  wdt, _ptr(bias), _ptr(ids), _ptr(wts), _stream()), "lk_moe_route")
+    return ids, wts
+
+
+def moe_max_tiles(tokens, ku, n_experts):
+    """Worst-case schedule size (gen_llm.py:5406-5411)."""
+    a = tokens * ku
+    return (a + 63) // 64 + min(n_experts, a)
+
+
+def moe_bucket(ids, n_experts, max_tiles=None, info=None):
+    """-> (tile_info [max_tiles][2], rowmap [max_tiles*64], pos [tokens*ku]) int32."""
+    _cuda(ids, info)
+    tokens, ku = ids.shape
+    if max_tiles is None:
+        max_tiles = moe_max_tiles(tokens, ku, n_experts)
+    dev = ids.device
+    ti = torch.empty(max_tiles, 2, dtype=torch.int32, device=dev)
+    rm = torch.empty(max_tiles * 64, dtype=torch.int32, device=dev)
+    pos = torch.empty(tokens * ku, dtype=torch.int32, device=dev)
+    L.check(L.load().lk_moe_bucket(tokens, ku, n_experts, max_tiles, _ptr(info), _ptr(ids.contiguous()), _ptr(ti),
+                                   _ptr(rm), _ptr(pos), _stream()), "lk_moe_bucket")
+    return ti, rm, pos
+
+
+def moe_grouped_gemm(fmt, mode, tile_info, rowmap, x16, scales, w, n, ku, n_experts, fused=False, w2=None, y=None):
+    """Grouped expert GEMM over the bucketed 64-row tiles. mode 'swiglu' (gate/up, x16 = token rows) or 'store'
+    (down, x16 = sorted rows). y: [max_tiles*64][n]."""
+    _cuda(tile_info, rowmap, x16, scales, w, w2, y)
+    rows = rowmap.shape[0]
+    xrows, k = x16.shape
+    if y is None:
+        y = torch.empty(rows, n, dtype=torch.float32, device=x16.device)
+    m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
+    L.check(L.load().lk_moe_grouped_gemm(_fmt(fmt), m, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
+                                         _ptr(tile_info), _ptr(rowmap), _ptr(x16), _ptr(scales), _ptr(w), _ptr(w2),
+                                         _ptr(y), _stream()), "lk_moe_grouped_gemm")
+    return y
+
+
+def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False):
+    _cuda(ys, pos, wts, y)
+    tokens, ku = wts.shape
+    rows, h = ys.shape
+    if y is None:
+        y = torch.empty(tokens, h, dtype=torch.float32, device=ys.device)
+    L.check(L.load().lk_moe_combine_sorted(tokens, rows, h, ku, 1 if accumulate else 0, _ptr(ys), _ptr(pos),
+                                           _ptr(wts), _ptr(y), _stream()), "lk_moe_combine_sorted")
+    return y
+
+
+def moe_expert_mv(fmt, mode, ids, x, w, n, k, ku, n_experts, fused=True, w2=None, y=None):
+    """Decode expert matvecs per assignment: mode 'gu' -> silu(Wg x) * (Wu x); 'dn' -> Wd x."""
+    _cuda(ids, x, w, w2, y)
+    a = ids.numel()
+    if y is None:
+        y = torch.empty(a, n, dtype=torch.float32, device=x.device)
+    md = 0 if mode == "gu" else 1
+    L.check(L.load().lk_moe_expert_mv(_fmt(fmt), md, n, k, a, ku, n_experts, 1 if fused else 0, _ptr(ids),
+                                      _ptr(x.contiguous()), _DT[x.dtype], _ptr(w), _ptr(w2), _ptr(y), _stream()),
+            "lk_moe_expert_mv")
+    return y
+
+
+def moe_combine(ys, wts, y=None, accumulate=False):
+    _cuda(ys, wts, y)
+    tokens, ku = wts.shape
+    h = ys.shape[1]
+    if y is None:
+        y = torch.empty(tokens, h, dtype=torch.float32, device=ys.device)
+    L.check(L.load().lk_moe_combine(tokens, h, ku, 1 if accumulate else 0, _ptr(ys), _ptr(wts), _ptr(y), _stream()),
+            "lk_moe_combine")
+    return y
+
+
+def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None):
+    """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route -> bucket -> grouped gate/up
+    (SwiGLU) -> row scale -> grouped down -> weighted combine (prefill), or per-assignment expert matvecs (decode).
+    x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values;
+    w_dn: per expert h rows of f values."""
+    tokens = x.shape[0]
+    ids, wts = moe_route(logits, n_experts, ku, norm=norm)
+    if prefill is None:
+        prefill = tokens >= 64   # gen_llm.py:6107: %gemm = t >= 64
+    if not prefill:
+        act = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=True)
+        ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act, w_dn, h, f, ku, n_experts)
+        return moe_combine(ys, wts)
+    ti, rm, pos = moe_bucket(ids, n_experts)
+    x16, sc = row_scale_f16(x)
+    act = moe_grouped_gemm(fmt, "swiglu", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True)
+    a16, asc = row_scale_f16(act)
+    ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts)
+    return moe_combine_sorted(ys, pos, wts)

@@ -117,7 +117,9 @@ def quantize_iq4_nl(w):
     d = d16.astype(np.float64)
     with np.errstate(divide="ignore", invalid="ignore"):
         v = np.where(d != 0, blocks / d, 0.0)
-    idx = np.abs(v[..., None] - IQ4_KVALUES[None, None, :]).argmin(-1).astype(np.uint8)   # argmin: first minimum
+    # nearest codebook entry; a value exactly between two entries takes the lower index
+    mid = (IQ4_KVALUES[:-1] + IQ4_KVALUES[1:]) / 2.0
+    idx = np.searchsorted(mid, v, side="left").astype(np.uint8)
     packed = idx[:, :16] | (idx[:, 16:] << np.uint8(4))
     out = np.concatenate([d16.view(np.uint8).reshape(-1, 2), packed], axis=-1)
     return out.reshape(*lead, -1)
@@ -126,11 +128,10 @@ def quantize_iq4_nl(w):
 def _e2m1_codes(v):
     """float64 values in [-6, 6] -> nearest e2m1 codes (bit 3 = sign), ties to the even table index."""
     a = np.abs(v)
-    dist = np.abs(a[..., None] - E2M1)
-    best = dist.min(-1, keepdims=True)
-    cand = dist == best
-    even = cand & (np.arange(8) % 2 == 0)
-    mag = np.where(even.any(-1), even.argmax(-1), cand.argmax(-1))
+    mid = (E2M1[:-1] + E2M1[1:]) / 2.0
+    mag = np.searchsorted(mid, a, side="left")            # ties -> the lower magnitude ...
+    tie = (mag < 7) & (a == mid[np.minimum(mag, 6)]) & (mag % 2 == 1)
+    mag = mag + tie                                       # ... unless that index is odd: ties to even
     sign = (v < 0) & (mag > 0)
     return (mag | (sign << 3)).astype(np.uint8)
 
