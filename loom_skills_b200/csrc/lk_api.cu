@@ -70,29 +70,33 @@ int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, v
   return dequant(fmt, w, w_scales, n_values, out, out_dtype, (cudaStream_t)stream);
 }
 
+// Zero-sized calls succeed before the pointer checks: an empty tensor has no storage (a null data pointer).
 int lk_row_scale_f16(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, lk_stream_t stream) {
-  if (rows < 0 || k <= 0 || !x || !scales || !x16) return LK_EINVAL;
+  if (rows < 0 || k <= 0) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
+  if (!x || !scales || !x16) return LK_EINVAL;
   return row_scale(rows, k, x, x_dtype, scales, x16, nullptr, nullptr, (cudaStream_t)stream);
 }
 
 int lk_row_scale_f8(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
                     lk_stream_t stream) {
-  if (rows < 0 || k <= 0 || !x || !x8 || !s8) return LK_EINVAL;
+  if (rows < 0 || k <= 0) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
+  if (!x || !x8 || !s8) return LK_EINVAL;
   return row_scale(rows, k, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
 }
 
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
           float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
-  if (n <= 0 || k <= 0 || tokens < 0 || !x || !w || !y) return LK_EINVAL;
+  if (n <= 0 || k <= 0 || tokens < 0) return LK_EINVAL;
   if (k % 256) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
-  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
   if (tokens == 0) return LK_OK;
+  if (!x || !w || !y) return LK_EINVAL;
+  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
   MvArgs a{};
   a.w = (const uint8_t*)w;
   a.w2 = (const uint8_t*)w2;
@@ -112,13 +116,14 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                      const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
                      lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
-  if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0 || !ids || !x || !w || !y) return LK_EINVAL;
+  if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
   if (mode != 0 && mode != 1) return LK_EINVAL;
   if (k % 256) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (assignments == 0) return LK_OK;
+  if (!ids || !x || !w || !y) return LK_EINVAL;
   if (mode == 0 && !fused && !w2) return LK_EINVAL;
   if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
-  if (assignments == 0) return LK_OK;
   MvArgs a{};
   a.w = (const uint8_t*)w;
   a.w2 = (mode == 0 && !fused) ? (const uint8_t*)w2 : nullptr;
@@ -142,11 +147,12 @@ int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, cons
             const void* w2, float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_ACC && mode != LK_SWIGLU) return LK_EINVAL;
-  if (rows < 0 || k <= 0 || n <= 0 || !x16 || !scales || !w || !y) return LK_EINVAL;
-  if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
+  if (rows < 0 || k <= 0 || n <= 0) return LK_EINVAL;
   if (k % 256 || n % 16) return LK_EINVAL;
-  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
   if (rows == 0) return LK_OK;
+  if (!x16 || !scales || !w || !y) return LK_EINVAL;
+  if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
+  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
   return gemm(fmt, mode, rows, k, n, x16, scales, w, w2, y, (cudaStream_t)stream, nullptr, nullptr, rows, 1, 1, 0, 0);
 }
 
@@ -173,22 +179,24 @@ int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t
                       lk_stream_t stream) {
   if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
-  if (rows < 0 || k <= 0 || n <= 0 || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
-  if (mode == LK_SWIGLU && (!w2 || !w2s)) return LK_EINVAL;
+  if (rows < 0 || k <= 0 || n <= 0) return LK_EINVAL;
   if (k % 128 || n % 16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
+  if (mode == LK_SWIGLU && (!w2 || !w2s)) return LK_EINVAL;
   if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(ws, 16) || !aligned(y, 16)) return LK_EALIGN;
   if (w2 && (!aligned(w2, 16) || !aligned(w2s, 16))) return LK_EALIGN;
-  if (rows == 0) return LK_OK;
   return gemm_mxfp4s(mode, order, rows, k, n, x8, s8, w, ws, w2, w2s, y, (cudaStream_t)stream);
 }
 
 int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
                  const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, lk_stream_t stream) {
   if (tokens < 0 || n_experts <= 0 || n_experts > 256 || ku <= 0 || ku > 8 || ku > n_experts) return LK_EINVAL;
-  if (gating < 1 || gating > 3 || !x || !ids || !wts) return LK_EINVAL;
+  if (gating < 1 || gating > 3) return LK_EINVAL;
   if (router_w && (h <= 0 || (w_dtype != LK_F32 && w_dtype != LK_BF16))) return LK_EINVAL;
   if (gating == 1 && bias) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
+  if (!x || !ids || !wts) return LK_EINVAL;
   return moe_route(tokens, h, n_experts, ku, gating, norm, scale, x, router_w, w_dtype, bias, ids, wts,
                    (cudaStream_t)stream);
 }
@@ -205,15 +213,17 @@ int lk_moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_
 
 int lk_moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
                           const float* wts, float* y, lk_stream_t stream) {
-  if (tokens < 0 || rows <= 0 || h <= 0 || ku <= 0 || ku > 8 || !ys || !pos || !wts || !y) return LK_EINVAL;
+  if (tokens < 0 || rows <= 0 || h <= 0 || ku <= 0 || ku > 8) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
+  if (!ys || !pos || !wts || !y) return LK_EINVAL;
   return moe_combine_sorted(tokens, rows, h, ku, accumulate, ys, pos, wts, y, (cudaStream_t)stream);
 }
 
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream) {
-  if (tokens < 0 || h <= 0 || ku <= 0 || ku > 8 || !ys || !wts || !y) return LK_EINVAL;
+  if (tokens < 0 || h <= 0 || ku <= 0 || ku > 8) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
+  if (!ys || !wts || !y) return LK_EINVAL;
   return moe_combine(tokens, h, ku, accumulate, ys, wts, y, (cudaStream_t)stream);
 }
 
