@@ -5,7 +5,8 @@ Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B
 (K=4096: N=4096 q/o, N=1024 k/v, N=24576 fused gate+up; down K=12288, N=4096), bf16 activations. One STEP is one decode
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
 868 MB at 8 layers, exceed the 126 MB L2). `value` is the decode GEMV weight GB/s; the line also carries the prefill
-TFLOP/s at M=2048 over the same shapes, and a sweep over M in {1, 8, 64, 512, 2048}.
+TFLOP/s at M=2048 over the same shapes (step = row scale + the six tcgen05 GEMMs), and a sweep over M in
+{1, 8, 64, 512, 2048}. Each step is one CUDA-graph replay of the public ops' launches (48 matvecs per decode step).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
@@ -30,6 +31,9 @@ METRIC = "decode GEMV weight GB/s (% HBM peak); prefill TFLOPS (% tensor peak)"
 SHAPES = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096), ("gate_up", 4096, 24576),
           ("down", 12288, 4096)]   # (name, K, N)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures (profiles/), None until captured
+TRAFFIC_DECODE = None
+TRAFFIC_PREFILL = None
 
 
 def peaks():
@@ -49,21 +53,30 @@ def rank_env():
 # clocks during the timed region
 # ------------------------------------------------------------------------------------------------------------------
 class Clocks:
-    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    Q = ("timestamp,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, uuid):
         self.uuid = uuid
         self.proc = None
         self.out = os.path.join("/tmp", f"lk_clocks_{os.getpid()}.csv")
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=open(self.out, "w"), stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=open(self.out, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        time.sleep(0.3)   # the sampler's first query takes a moment
+
+    def mark(self, begin):
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
 
     def stop(self):
         if not self.proc:
@@ -73,17 +86,21 @@ class Clocks:
         rows = []
         for line in open(self.out):
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 10 and (self.uuid is None or f[1] == self.uuid):
-                rows.append(f)
+            if len(f) >= 9 and f[1] == self.uuid:
+                try:
+                    ts = time.mktime(time.strptime(f[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                except ValueError:
+                    ts = None
+                rows.append((ts, f))
         os.unlink(self.out)
-        if not rows:
+        inside = [f for ts, f in rows if ts is not None and self.t0 - 1 <= ts <= self.t1 + 1] or [f for _, f in rows]
+        if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        mx = max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
+        sm = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
+        mx = max(float(r[3]) for r in inside if r[3].replace(".", "").isdigit())
+        reasons = sorted({self.NAMES[i] for r in inside for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(inside), "timed_s": round(self.t1 - self.t0, 3)}
 
 
 # ------------------------------------------------------------------------------------------------------------------
@@ -102,7 +119,7 @@ def cpu_decode_gbs(budget_s=10.0, rows=1024):
         O.mv_ref("q4_k", w, x, rows, k)
         reps += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 10000:
+        if el >= budget_s or reps >= 100000:
             break
     gbs = reps * w.nbytes / el / 1e9
     return gbs, {"kind": "port", "cores": os.cpu_count(),
@@ -114,17 +131,19 @@ def run_reference(args):
     rank, _, world = rank_env()
     if rank != 0:
         return
-    # each step: a bounded sample of the decode workload on the host cores (~2 s)
+    # each step: a bounded sample of the decode workload on the host cores (~0.5 s)
     vals = []
-    for i in range(args.warmup + args.steps):
-        v, desc = cpu_decode_gbs(budget_s=2.0)
+    t_all = time.perf_counter()
+    for i in range(args.warmup + min(args.steps, 20)):
+        v, desc = cpu_decode_gbs(budget_s=0.5)
         if i >= args.warmup:
             vals.append(v)
     v = statistics.median(vals)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2000.0, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "configs[1] Q4_K decode, M=1, gate_up slice (CPU sample)"},
+            "steps": len(vals), "warmup": args.warmup,
+            "ms_per_step": round((time.perf_counter() - t_all) * 1e3 / (len(vals) + args.warmup), 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "configs[1] Qwen3-8B-like Q4_K projections, decode M=1 (CPU: gate_up slice)"},
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", **desc},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -144,10 +163,26 @@ def make_weights(torch, layers, seed=0):
             r1 = min(n, r0 + 2048)
             chunks.append(O.quantize_q4_k((rng.standard_normal((r1 - r0, k)) * 0.02).astype(np.float32)))
         base[name] = torch.from_numpy(np.concatenate(chunks)).cuda()
-    stack = []
-    for li in range(layers):
-        stack.append({name: (t if li == 0 else t.clone()) for name, t in base.items()})
-    return stack
+    return [{name: (t if li == 0 else t.clone()) for name, t in base.items()} for li in range(layers)]
+
+
+class Timed:
+    """A step's launches captured as one CUDA graph (the kernels then run back to back, without host gaps)."""
+
+    def __init__(self, torch, body):
+        body()   # eager first call: per-device kernel set-up happens outside the capture
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                body()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = g
+
+    def replay(self):
+        self.graph.replay()
 
 
 def run_ours(args):
@@ -168,18 +203,13 @@ def run_ours(args):
     ys = [{name: torch.empty(1, n, device=dev) for name, _, n in SHAPES} for _ in range(args.layers)]
     wbytes_layer = sum(t.numel() for t in wstack[0].values())
     act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
-    stream = torch.cuda.current_stream()
+    launches_per_step = args.layers * len(SHAPES)
+    step_bytes = args.layers * wbytes_layer
 
-    def decode_step(ev=None):
+    def decode_body():
         for li in range(args.layers):
             for name, k, n in SHAPES:
-                if ev is not None:
-                    ev[0].append(torch.cuda.Event(enable_timing=True))
-                    ev[0][-1].record(stream)
                 ops.mv("q4_k", wstack[li][name], xs[k], n, k, y=ys[li][name])
-                if ev is not None:
-                    ev[1].append(torch.cuda.Event(enable_timing=True))
-                    ev[1][-1].record(stream)
 
     def barrier():
         if world > 1:
@@ -193,36 +223,40 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- decode: device-resident inputs
+    def time_steps(fn, steps, clk=None):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        if clk:
+            clk.mark(True)
+        t0.record()
+        for _ in range(steps):
+            fn()
+        t1.record()
+        barrier()
+        if clk:
+            clk.mark(False)
+        return max_over_ranks(t0.elapsed_time(t1)) / steps
+
+    # ---- decode: device-resident inputs, one graph replay per step. Every launch of the step is the matvec kernel,
+    # back to back, so its average launch duration is the step time (CUDA events around the timed steps) / launches.
+    dec = Timed(torch, decode_body)
     for _ in range(args.warmup):
-        decode_step()
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    clk = Clocks(uuid)
-    barrier()
+        dec.replay()
+    clk = Clocks("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
     clk.start()
-    kev = ([], [])
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        decode_step(kev)
-    t1.record(stream)
-    barrier()
+    ms = time_steps(dec.replay, args.steps, clk)
     clocks = clk.stop()
-    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
-    launch_ms = [a.elapsed_time(b) for a, b in zip(*kev)]
-    launches_per_step = args.layers * len(SHAPES)
-    step_bytes = args.layers * wbytes_layer
     value = world * step_bytes / (ms * 1e-3) / 1e9
-    # dominant kernel: the Q4_K matvec (every launch of the step); algorithmic bytes = weights + x + y
     alg_per_launch = (step_bytes + args.layers * act_bytes) / launches_per_step
-    kavg = statistics.mean(launch_ms)
+    kavg = ms / launches_per_step
     achieved = alg_per_launch / (kavg * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_source": pk_src,
-            "kernel": "k_mv<Q4_K, bf16> (lk_mv)"}
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": TRAFFIC_DECODE, "peak_source": pk_src,
+            "kernel": "k_mv<Q4_K, bf16, TOK=1> (lk_mv)", "avg_launch_us": round(kavg * 1e3, 2),
+            "alg_bytes_per_launch": int(alg_per_launch)}
 
-    # ---- e2e through the public API: pinned host x in, every projection output back, each step
+    # ---- e2e through the public API: pinned host x in, every projection output back, each step (one graph)
     hx = {k: torch.empty(1, k, dtype=torch.bfloat16).pin_memory() for k in xs}
     for k in hx:
         hx[k].copy_(xs[k].cpu())
@@ -230,90 +264,87 @@ def run_ours(args):
     h2d = sum(t.numel() * 2 for t in hx.values())
     d2h = sum(t.numel() * 4 for d in hy for t in d.values())
 
-    def e2e_step():
+    def e2e_body():
         for k in hx:
             xs[k].copy_(hx[k], non_blocking=True)
-        decode_step()
+        decode_body()
         for li in range(args.layers):
             for name in ys[li]:
                 hy[li][name].copy_(ys[li][name], non_blocking=True)
 
+    e2e_g = Timed(torch, e2e_body)
     for _ in range(args.warmup):
-        e2e_step()
-    barrier()
-    t0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    t1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+        e2e_g.replay()
+    e2e_ms = time_steps(e2e_g.replay, args.steps)
     e2e = {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
 
-    # ---- prefill: M=2048 through the same shapes (row scale to f16 + tcgen05 GEMM), one layer
+    # ---- prefill: M rows through the same shapes (row scale to f16 + tcgen05 GEMM), one layer
     M = args.prefill_rows
     xp = {k: torch.randn(M, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
     yp = {name: torch.empty(M, n, device=dev) for name, _, n in SHAPES}
     flops = sum(2.0 * M * n * k for _, k, n in SHAPES)
 
-    def prefill_step(ev=None):
-        x16 = {k: ops.row_scale_f16(xp[k]) for k in xp}
+    x16p = {}
+
+    def scale_body():
+        for k in xp:
+            x16p[k] = ops.row_scale_f16(xp[k])
+
+    def gemm_body():
         for name, k, n in SHAPES:
-            if ev is not None:
-                ev[0].append(torch.cuda.Event(enable_timing=True))
-                ev[0][-1].record(stream)
-            ops.gemm("q4_k", "store", x16[k][0], x16[k][1], wstack[0][name], n, y=yp[name])
-            if ev is not None:
-                ev[1].append(torch.cuda.Event(enable_timing=True))
-                ev[1][-1].record(stream)
+            ops.gemm("q4_k", "store", x16p[k][0], x16p[k][1], wstack[0][name], n, y=yp[name])
+
+    scale_g = Timed(torch, scale_body)
+    gemm_g = Timed(torch, gemm_body)
+    ge = []
+
+    def prefill_step():
+        # the GEMM graph between CUDA events: the dominant kernel's time, live inside the timed region
+        scale_g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        gemm_g.replay()
+        b.record()
+        ge.append((a, b))
 
     for _ in range(args.warmup):
         prefill_step()
-    barrier()
-    pev = ([], [])
-    t0.record(stream)
-    for _ in range(args.steps):
-        prefill_step(pev)
-    t1.record(stream)
-    barrier()
-    pms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
-    gms = statistics.mean(a.elapsed_time(b) for a, b in zip(*pev)) * len(SHAPES)
+    ge.clear()
+    psteps = max(3, args.steps // 8)
+    pms = time_steps(prefill_step, psteps)
+    gms = statistics.mean(a.elapsed_time(b) for a, b in ge)
     ptflops = flops / (pms * 1e-3) / 1e12
     gemm_tf = flops / (gms * 1e-3) / 1e12
     peak_tf = pk["bf16_tflops_sustained"]
-    prefill = {"rows": M, "tflops": round(world * ptflops, 1), "ms_per_step": round(pms, 4),
+    prefill = {"rows": M, "tflops": round(world * ptflops, 1), "ms_per_step": round(pms, 4), "steps": psteps,
                "roofline": {"bound": "tensor", "achieved": round(gemm_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                            "frac": round(gemm_tf / peak_tf, 4), "traffic": None, "peak_source": pk_src + " sustained",
-                            "kernel": "k_gemm<Q4_K> (tcgen05 kind::f16, lk_gemm)"}}
+                            "frac": round(gemm_tf / peak_tf, 4), "traffic": TRAFFIC_PREFILL,
+                            "peak_source": pk_src + " sustained", "kernel": "k_gemm<Q4_K> (tcgen05 kind::f16, lk_gemm)"}}
 
-    # ---- sweep over the config's token counts (one layer, per-step ms)
+    # ---- sweep over the config's token counts (one layer, per-step ms; row scale included for M >= 64)
     sweep = {}
     if not args.no_sweep:
         for m in (1, 8, 64, 512, 2048):
             xm = {k: torch.randn(m, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
             ym = {name: torch.empty(m, n, device=dev) for name, _, n in SHAPES}
 
-            def step_m():
-                if m < 64:
+            def body_m():
+                if m < 64:   # gen_llm.py:6107: matvecs below 64 tokens, GEMMs from 64
                     for name, k, n in SHAPES:
                         ops.mv("q4_k", wstack[0][name], xm[k], n, k, y=ym[name])
                 else:
                     x16 = {k: ops.row_scale_f16(xm[k]) for k in xm}
                     for name, k, n in SHAPES:
                         ops.gemm("q4_k", "store", x16[k][0], x16[k][1], wstack[0][name], n, y=ym[name])
+            tm = Timed(torch, body_m)
             for _ in range(3):
-                step_m()
-            torch.cuda.synchronize()
-            reps = 10
-            t0.record(stream)
-            for _ in range(reps):
-                step_m()
-            t1.record(stream)
-            torch.cuda.synchronize()
-            mms = t0.elapsed_time(t1) / reps
+                tm.replay()
+            mms = time_steps(tm.replay, 20)
             sweep[str(m)] = {"ms": round(mms, 4), "weight_gbs": round(wbytes_layer / (mms * 1e-3) / 1e9, 1),
                              "tflops": round(sum(2.0 * m * n * k for _, k, n in SHAPES) / (mms * 1e-3) / 1e12, 2)}
 
+    gpu_launches = args.steps * launches_per_step
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
         line = {
@@ -326,12 +357,14 @@ def run_ours(args):
                        "weight_bytes_per_step": step_bytes,
                        "l2": f"inputs larger than L2: {step_bytes / 1e6:.0f} MB of weights rotated over "
                              f"{args.layers} layer copies",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "launch": "one CUDA graph replay per step"},
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
-            "gpu_launches": args.steps * launches_per_step, "clocks": clocks, "prefill": prefill, "sweep": sweep,
+            "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
             "hbm_frac": round(value / world / pk["hbm_gbs"], 4)}
         print(json.dumps(line), flush=True)
     if world > 1:
+        del dec, e2e_g, scale_g, gemm_g
         dist.barrier()
         dist.destroy_process_group()
 
@@ -339,8 +372,8 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--prefill-rows", type=int, default=2048)

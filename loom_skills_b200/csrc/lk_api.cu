@@ -137,8 +137,9 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
   a.ids = ids;
   a.x_div = mode == 0 ? ku : 1;
   a.n_experts = n_experts;
-  a.expert_stride = a.row_bytes * n * ((mode == 0 && fused) ? 2 : 1);
-  a.w2_offset = a.row_bytes * n;
+  a.rows_per_expert = n * ((mode == 0 && fused) ? 2 : 1);
+  a.rows_per_expert2 = (mode == 0 && fused) ? 2 * n : n;   // fused: the up rows live in the same stacked tensor
+  a.w2_row_offset = (mode == 0 && fused) ? n : 0;
   a.swiglu = mode == 0;
   return mv(fmt, a, assignments, (cudaStream_t)stream);
 }

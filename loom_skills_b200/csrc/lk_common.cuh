@@ -51,6 +51,24 @@ LK_DEV uint32_t iq4_lookup4(uint32_t idx) {
 LK_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 LK_DEV float bf2f(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
 
+// Q4_K 6-bit (scale, minimum) of group j from the three little-endian words of the 12-byte scale field
+// (header bytes 4..15), register arithmetic only (gen_llm.py:234-266 @g_k_scale_minimum)
+LK_DEV void q4k_scale_min_w(uint32_t s0, uint32_t s1, uint32_t s2, int j, uint32_t& sc, uint32_t& m) {
+  uint32_t sh = 8u * uint32_t(j & 3);
+  if (j < 4) {
+    sc = (s0 >> sh) & 63u;
+    m = (s1 >> sh) & 63u;
+  } else {
+    uint32_t lo = s2 >> sh;
+    sc = (lo & 15u) | (((s0 >> sh) >> 2) & 48u);
+    m = ((lo >> 4) & 15u) | (((s1 >> sh) >> 2) & 48u);
+  }
+}
+// small integer (0..2047) -> f16 exactly, without a conversion instruction: bits of (1024 + v) minus 1024
+LK_DEV __half small_int_half(uint32_t v) {
+  return __hsub(__ushort_as_half(uint16_t(0x6400u | v)), __ushort_as_half(uint16_t(0x6400u)));
+}
+
 // Q4_K 6-bit (scale, minimum) of group j of a 12-byte scale field (gen_llm.py:234-266)
 LK_DEV void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
   if (j < 4) {

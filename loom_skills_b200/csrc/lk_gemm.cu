@@ -6,7 +6,8 @@
 //
 // One CTA computes a 128-row x BN-column output tile (BN = 256; swiglu: 128 columns of each of gate and up):
 //   warp 0      producer: A tiles of X16 by 2-D TMA (128 rows x 64 k, 128-byte swizzle; MoE gate/up: TMA gather4 of
-//               the routed token rows) and the weights' packed bytes by 1-D bulk copies (144 bytes per row per 256 k)
+//               the routed token rows) and the weights' packed bytes by one 2-D TMA box per 256 k (BN rows x 144
+//               bytes, the packed rows read as u32 columns; experts stacked as rows)
 //   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, M=128, N=256, K=16) from one lane
 //   warps 2-9   dequantise the packed bytes into f16 B tiles in the UMMA K-major 128-byte-swizzle layout -- the
 //               reference's one-rounding staging exactly (f16(d*(q-8)), f16(d*kvalue), fma_f16(q, f16(d*sc),
@@ -28,18 +29,17 @@ constexpr int kGemmThreads = (2 + kDqWarps) * 32;
 enum { kDense = 0, kGather = 1, kSorted = 2 };
 
 struct GemmArgs {
-  const uint8_t* w;     // packed weight rows (expert 0 for MoE)
-  const uint8_t* w2;    // second weight (swiglu, not fused) or nullptr
   const float* scales;  // [rows or xrows][2]
   float* y;             // [rows][n]
   int rows, k, n;
-  int64_t row_bytes;
+  // weights: wmap / w2map cover [rows][row_bytes / 4] u32 of the (expert-stacked) packed weights; an expert's
+  // first row is e * rows_per_expert (w2: e * rows_per_expert2 + w2_row_offset)
+  int rows_per_expert, rows_per_expert2, w2_row_offset;
   // MoE
   const int32_t* tile_info;   // [max_tiles][2]
   const int32_t* rowmap;      // [max_tiles*64]
   int max_tiles;
   int xrows, ku, n_experts;
-  int64_t expert_stride, w2_offset;
 };
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
@@ -77,28 +77,24 @@ LK_DEV void magic8(uint32_t t0, uint32_t t1, uint32_t (&h)[4]) {
 // Dequantise one 32-value group of one weight row into 4 swizzled 16-byte chunks of the B tile.
 //   raw    : the row's 144-byte packed chunk (256 values) in shared memory
 //   j      : group within the chunk (0..7); b_tile: the B stage; r: tile row; c0: first 16-byte chunk (0 or 4)
+// Register arithmetic only: scales are formed in f16 (exact products rounded once), no conversion instructions.
 template <int FMT>
 LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int c0) {
-  uint32_t q[4];   // 16 packed bytes holding the group's 32 codes
-  __half2 scale, offset;
-  bool hi_half_is_next;   // Q4_0 / IQ4: values 16..31 are the high nibbles of the same 16 bytes
   if (FMT == LK_Q4_K) {
     const uint8_t* qs = raw + 16 + 32 * (j >> 1);
     uint4 a = *reinterpret_cast<const uint4*>(qs);
     uint4 b = *reinterpret_cast<const uint4*>(qs + 16);
+    uint4 hd = *reinterpret_cast<const uint4*>(raw);
     uint32_t sh = (j & 1) * 4;
-    // 32 codes: byte l's nibble (low for even groups, high for odd) is value l
     uint32_t c[8] = {(a.x >> sh) & 0x0F0F0F0Fu, (a.y >> sh) & 0x0F0F0F0Fu, (a.z >> sh) & 0x0F0F0F0Fu,
                      (a.w >> sh) & 0x0F0F0F0Fu, (b.x >> sh) & 0x0F0F0F0Fu, (b.y >> sh) & 0x0F0F0F0Fu,
                      (b.z >> sh) & 0x0F0F0F0Fu, (b.w >> sh) & 0x0F0F0F0Fu};
-    uint4 hd = *reinterpret_cast<const uint4*>(raw);
-    const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hd);
-    float d = h2f(uint16_t(hd.x & 0xffff)), dmin = h2f(uint16_t(hd.x >> 16));
-    int sc, m;
-    q4k_scale_min(hb + 4, j, sc, m);
-    __half a16 = __float2half_rn(d * float(sc)), c16 = __float2half_rn(-(dmin * float(m)));
-    scale = __halves2half2(a16, a16);
-    offset = __halves2half2(c16, c16);
+    uint32_t sc, m;
+    q4k_scale_min_w(hd.y, hd.z, hd.w, j, sc, m);
+    // f16(d * sc) and f16(-dmin * m): the f16 product of exact operands rounds once, like the f32 product + fptrunc
+    __half a16 = __hmul(__ushort_as_half(uint16_t(hd.x & 0xffffu)), small_int_half(sc));
+    __half c16 = __hneg(__hmul(__ushort_as_half(uint16_t(hd.x >> 16)), small_int_half(m)));
+    __half2 scale = __halves2half2(a16, a16), offset = __halves2half2(c16, c16);
     const uint32_t k1024 = 0x64006400u;
 #pragma unroll
     for (int cc = 0; cc < 4; ++cc) {
@@ -111,17 +107,15 @@ LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int
       out.w = hfma2u(hsub2u(h[3], k1024), scale, offset);
       *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
     }
-    (void)hi_half_is_next;
     return;
   }
   // Q4_0 / IQ4_NL: 18-byte block j at raw + 18j: f16 d, then 16 code bytes (2-byte aligned)
-  const uint8_t* blk = raw + 18 * j;
-  const uint16_t* p16 = reinterpret_cast<const uint16_t*>(blk);
-  float d = h2f(p16[0]);
+  const uint16_t* p16 = reinterpret_cast<const uint16_t*>(raw + 18 * j);
+  uint32_t q[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) q[i] = uint32_t(p16[1 + 2 * i]) | (uint32_t(p16[2 + 2 * i]) << 16);
-  __half dh = __float2half_rn(d);
-  scale = __halves2half2(dh, dh);
+  __half dh = __ushort_as_half(p16[0]);
+  __half2 scale = __halves2half2(dh, dh);
   const uint32_t koff = FMT == LK_Q4_0 ? 0x64086408u : 0x64806480u;   // f16 1032 (1024 + 8) | 1152 (1024 + 128)
 #pragma unroll
   for (int cc = 0; cc < 4; ++cc) {
@@ -143,13 +137,12 @@ LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int
     out.w = hmul2u(hsub2u(h[3], koff), scale);
     *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
   }
-  (void)offset;
-  (void)hi_half_is_next;
 }
 
 template <int FMT, int BN, int NW, int MODE, int GROUP>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    k_gemm(const __grid_constant__ CUtensorMap amap, const GemmArgs p) {
+    k_gemm(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+           const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
   constexpr int kRowsB = BN * NW;                 // weight rows dequantised per stage (256)
   constexpr int kABytes = kBM * kBK * 2;          // 16 KB
   constexpr int kBBytes = kRowsB * kBK * 2;       // 32 KB
@@ -180,8 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---- which rows: dense tile, or a 128-row super-tile of one expert made of <= 2 schedule tiles
   int m0 = blockIdx.y * kBM;
   int valid_rows = min(kBM, p.rows - m0);
-  const uint8_t* wb = p.w;
-  const uint8_t* w2b = p.w2;
+  int wrow = n0, w2row = n0 + p.w2_row_offset;   // first weight row of this tile in wmap / w2map
   if (GROUP != kDense) {
     if (threadIdx.x == 0) {
       // super-tile s = blockIdx.y: walk tile_info (experts in order), pairing consecutive tiles of one expert
@@ -211,8 +203,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int e = min(tile_meta[0], p.n_experts - 1);
     m0 = tile_meta[1] * 64;
     valid_rows = tile_meta[2];
-    wb = p.w + int64_t(e) * p.expert_stride;
-    if (NW == 2) w2b = p.w2 ? p.w2 + int64_t(e) * p.expert_stride : wb + p.w2_offset;
+    wrow = e * p.rows_per_expert + n0;
+    w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
     if (GROUP == kGather && threadIdx.x < kBM) {
       int r = threadIdx.x;
       int a = r < valid_rows ? p.rowmap[m0 + r] : -1;
@@ -248,20 +240,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    if (lane == 0) prefetch_tensormap(&amap);
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+    }
     for (int ks = 0; ks < kstages; ++ks) {
       if ((ks & 3) == 0) {
+        // the packed bytes of the next 256 k of all BN rows (x NW weights): one TMA box of BN rows x 144 bytes each
         int c = ks >> 2, sr = c % kSR;
         if (c >= kSR && !mbar_wait(&empty_r[sr], ((c / kSR) - 1) & 1)) atomicOr(&g_status, 1u);
-        if (lane == 0) mbar_expect_tx(&full_r[sr], uint32_t(nb_rows * NW * kChunkBytes));
-        __syncwarp();
-        for (int i = lane; i < kRowsB; i += 32) {
-          int wi = i / BN, r = i % BN;
-          if (r < nb_rows) {
-            const uint8_t* src = (wi ? w2b : wb) + int64_t(n0 + r) * p.row_bytes + int64_t(c) * kChunkBytes;
-            bulk_g2s(sR + sr * kRBytes + i * kChunkBytes, src, kChunkBytes, &full_r[sr]);
-          }
+        if (lane == 0) {
+          mbar_expect_tx(&full_r[sr], uint32_t(kRBytes));
+          tma_load_2d(sR + sr * kRBytes, &wmap, c * (kChunkBytes / 4), wrow, &full_r[sr]);
+          if (NW == 2) tma_load_2d(sR + sr * kRBytes + BN * kChunkBytes, &w2map, c * (kChunkBytes / 4), w2row,
+                                   &full_r[sr]);
         }
+        __syncwarp();
       }
       int sa = ks % kSA;
       if (ks >= kSA && !mbar_wait(&empty_a[sa], ((ks / kSA) - 1) & 1)) atomicOr(&g_status, 1u);
@@ -404,57 +399,60 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D map over a row-major [rows][cols] matrix of 16-bit or 8-bit elements, box = box_cols x box_rows, 128-byte swizzle
-int make_map_2d(CUtensorMap* map, const void* base, int elem_bytes, int64_t rows, int64_t cols, int box_cols,
-                int box_rows) {
+// 2-D tensor map over a row-major [rows][cols] matrix; box = box_cols x box_rows elements
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
+             int box_cols, int box_rows, CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return LK_ECUDA;
   cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
   cuuint64_t strides[1] = {cuuint64_t(cols * elem_bytes)};
   cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? LK_OK : LK_EINVAL;
 }
 
+struct GemmMaps {
+  CUtensorMap a, w, w2;
+};
+
 template <int FMT, int BN, int NW, int MODE, int GROUP>
-static int launch_gemm(const CUtensorMap& map, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
   constexpr int smem = 1024 + kSA * kBM * kBK * 2 + kSB * kRowsB * kBK * 2 + kSR * kRowsB * kChunkBytes + 256 + 32 +
                        kBM * 4;
   auto kern = k_gemm<FMT, BN, NW, MODE, GROUP>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<grid, kGemmThreads, smem, s>>>(map, a);
+  kern<<<grid, kGemmThreads, smem, s>>>(m.a, m.w, m.w2, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 template <int FMT>
-static int gemm_fmt(int mode, int group, const CUtensorMap& map, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
   if (group == kDense) {
-    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense>(map, a, grid, s);
-    if (mode == LK_ACC) return launch_gemm<FMT, 256, 1, LK_ACC, kDense>(map, a, grid, s);
-    return launch_gemm<FMT, 256, 1, LK_STORE, kDense>(map, a, grid, s);
+    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense>(m, a, grid, s);
+    if (mode == LK_ACC) return launch_gemm<FMT, 256, 1, LK_ACC, kDense>(m, a, grid, s);
+    return launch_gemm<FMT, 256, 1, LK_STORE, kDense>(m, a, grid, s);
   }
-  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather>(map, a, grid, s);
-  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted>(map, a, grid, s);
+  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather>(m, a, grid, s);
+  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted>(m, a, grid, s);
 }
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
          int n_experts, int64_t expert_stride, int64_t w2_offset) {
   GemmArgs a{};
-  a.w = (const uint8_t*)w;
-  a.w2 = (const uint8_t*)w2;
   a.scales = scales;
   a.y = y;
   a.rows = rows;
   a.k = k;
   a.n = n;
-  a.row_bytes = lk_row_bytes(fmt, k);
+  const int64_t rb = lk_row_bytes(fmt, k);
   int group = kDense;
+  int64_t wrows = n, w2rows = n;
+  a.rows_per_expert = a.rows_per_expert2 = 0;
   if (tile_info) {
     group = mode == LK_SWIGLU ? kGather : kSorted;
     a.tile_info = tile_info;
@@ -463,23 +461,32 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     a.xrows = xrows;
     a.ku = ku;
     a.n_experts = n_experts;
-    a.expert_stride = expert_stride;
-    a.w2_offset = w2_offset;
+    a.rows_per_expert = int(expert_stride / rb);
+    a.rows_per_expert2 = w2 ? n : a.rows_per_expert;
+    wrows = int64_t(n_experts) * a.rows_per_expert;
+    w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
-  CUtensorMap map;
-  int rc;
-  if (group == kGather)
-    rc = make_map_2d(&map, x16, 2, xrows, k, kBK, 1);       // one-row boxes for gather4
-  else
-    rc = make_map_2d(&map, x16, 2, group == kSorted ? rows : rows, k, kBK, kBM);
+  a.w2_row_offset = (mode == LK_SWIGLU && !w2) ? int(w2_offset / rb) : 0;
+  const int bn = (mode == LK_SWIGLU) ? 128 : 256;
+  GemmMaps m;
+  int rc = group == kGather ? make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xrows, k, kBK, 1,
+                                       CU_TENSOR_MAP_SWIZZLE_128B)   // one-row boxes for gather4
+                            : make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, k, kBK, kBM,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == LK_OK)
+    rc = make_map(&m.w, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wrows, rb / 4, kChunkBytes / 4, bn,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == LK_OK)
+    rc = w2 ? make_map(&m.w2, w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w2rows, rb / 4, kChunkBytes / 4, bn,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)
+            : (m.w2 = m.w, LK_OK);
   if (rc != LK_OK) return rc;
-  int bn = (mode == LK_SWIGLU) ? 128 : 256;
   // grouped: one CTA per possible 128-row super-tile (at most one per schedule tile)
   dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + kBM - 1) / kBM : rows / 64);
   switch (fmt) {
-    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, map, a, grid, s);
-    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, map, a, grid, s);
-    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, map, a, grid, s);
+    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, m, a, grid, s);
+    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, m, a, grid, s);
+    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, m, a, grid, s);
   }
   return LK_EUNSUPPORTED;
 }

@@ -26,8 +26,9 @@ struct MvArgs {
   const int32_t* ids;
   int x_div;
   int n_experts;
-  int64_t expert_stride;   // bytes between experts of w
-  int64_t w2_offset;       // bytes from w to w2 inside an expert (fused gate/up), used when w2 == nullptr && swiglu
+  int rows_per_expert;    // weight rows of one expert in w (fused gate/up: 2n)
+  int rows_per_expert2;   // weight rows of one expert in w2
+  int w2_row_offset;      // first row of the second weight inside an expert (fused gate/up: n; else 0)
   int swiglu;
 };
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);

@@ -3,16 +3,17 @@
 // Replaces g_mv_{fmt}_k{K}[_t{TG}][_r{R}] and its swiglu pair (gen_llm.py:1159-1378) and the MoE expert matvecs
 // g_moe_gu_/g_moe_dn_ (gen_moe.py:535-727).
 //
-// Design (HBM-bound): a CTA owns 16 weight rows and up to 8 tokens. A producer warp streams the rows' packed bytes
-// into a shared-memory ring with 1-D bulk copies (TMA), 576 contiguous bytes per row per stage; four consumer warps
-// each take one 256-value chunk of every stage. A consumer unpacks nibbles in registers straight into the A fragments
-// of warp-level f16 MMAs (16 rows x 16 k x 8 tokens): the weights never go back to shared memory, so the only shared
-// memory traffic is the bulk copy in and one read. Codes enter the MMA exactly as (1024 + code) f16 values; the
-// per-32-value group scale is applied in f32 afterwards:
+// Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, one 2-D TMA
+// box of the rows' packed bytes (16 rows x 576 bytes = 1024 k) plus the matching slice of each token's activations
+// (1-D bulk copies) into a 4-stage shared-memory ring. Four consumer warps each take one 256-value chunk of every
+// stage: they convert their activation slice to f16 once (with per-32-value group sums), then unpack nibbles in
+// registers straight into the A fragments of warp-level f16 MMAs (16 rows x 16 k x 8 tokens) -- the weights never
+// go back to shared memory. Codes enter the MMA exactly as (1024 + code) f16 values (high nibbles as 1024 + 16 code);
+// the per-32-value group scale is applied in f32 afterwards:
 //     sum_k (a*q_k - c) x_k = a * D - (1024 a + c) * S,   D = sum (1024 + q_k) x_k,  S = sum x_k
-// with S from a second MMA against a ones operand. Q4_0: a = d, c = 8d; IQ4_NL: codes are the biased codebook bytes
-// (kvalue + 128), a = d, offset 1152 a; Q4_K: a = d*sc, c = dmin*m per group. The f32 accumulation of exact codes
-// is more precise than the reference's f32 per-value dequant-then-dot (gen_llm.py:1281-1357).
+// Q4_0: a = d, c = 8d; IQ4_NL: codes are the biased codebook bytes (kvalue + 128), a = d, offset 1152 a; Q4_K:
+// a = d*sc, c = dmin*m per group. The f32 accumulation of exact codes is at least as precise as the reference's f32
+// dequant-then-dot (gen_llm.py:1281-1357).
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
@@ -21,9 +22,12 @@ namespace lk {
 constexpr int kMvConsumers = 4;
 constexpr int kMvThreads = (kMvConsumers + 1) * 32;
 constexpr int kMvRows = 16;
-constexpr int kMvStageChunks = 4;                   // 256-value chunks per stage (one per consumer warp)
-constexpr int kMvStages = 4;
-constexpr int kMvRowStageBytes = kMvStageChunks * kChunkBytes;   // 576
+constexpr int kMvStageChunks = 4;                               // 256-value chunks per stage, one per consumer
+// ring depth: 4 stages, or 2 when a stage is large (two weights and 8 f32 tokens) so the CTA fits shared memory
+constexpr int mv_stages(int stage_bytes) { return 4 * stage_bytes <= 150 * 1024 ? 4 : 2; }
+constexpr int kMvRowStageBytes = kMvStageChunks * kChunkBytes;  // 576
+constexpr int kMvWBytes = kMvRows * kMvRowStageBytes;           // 9216: one weight's box per stage
+constexpr int kXStride = 272;                                   // f16 row stride of a consumer's x tile
 
 LK_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -32,56 +36,22 @@ LK_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint3
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// D = A * B (zero accumulator input)
+LK_DEV void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
 
 LK_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// B fragment of 4 consecutive activations x[kk .. kk+3] of one token (f16 MMA operand); f32 inputs split hi + lo
-template <int XT>
-struct BFrag {
-  uint32_t b0, b1, l0, l1;
-  LK_DEV void load(const void* xrow, int kk, bool valid) {
-    b0 = b1 = l0 = l1 = 0;
-    if (!valid) return;
-    if (XT == LK_F16) {
-      uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(xrow) + kk));
-      b0 = v.x;
-      b1 = v.y;
-    } else if (XT == LK_BF16) {
-      uint2 v = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(xrow) + kk));
-      b0 = h2u(__floats2half2_rn(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u)));
-      b1 = h2u(__floats2half2_rn(__uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u)));
-    } else {
-      float4 v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(xrow) + kk));
-      __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
-      b0 = h2u(h0);
-      b1 = h2u(h1);
-      float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-      l0 = h2u(__floats2half2_rn(v.x - f0.x, v.y - f0.y));
-      l1 = h2u(__floats2half2_rn(v.z - f1.x, v.w - f1.y));
-    }
-  }
-};
-
-// D += A(code word pair) * B, for both hi and lo parts of an f32 activation
-template <int XT>
-LK_DEV void mma_codes(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, const BFrag<XT>& b) {
-  mma16816(d, a0, a1, a2, a3, b.b0, b.b1);
-  if (XT == LK_F32) mma16816(d, a0, a1, a2, a3, b.l0, b.l1);
-}
-
-constexpr uint32_t kOnes = 0x3C003C00u;   // f16x2 (1, 1)
-
-// nibble codes (bits 0-3 of each byte) -> the A fragment halves (1024 + code) for 4 consecutive k
+// bytes of t (code in the low or high nibble, other nibble zero) -> A fragment halves (1024 + byte) for 4 consecutive k
 LK_DEV void code_frag(uint32_t t, uint32_t& first, uint32_t& second) {
   first = prmt(t, 0x64646464u, 0x4140u);
   second = prmt(t, 0x64646464u, 0x4342u);
-}
-
-template <int FMT>
-LK_DEV uint32_t nib_bytes(uint32_t w, bool hi) {
-  uint32_t t = (hi ? (w >> 4) : w) & 0x0F0F0F0Fu;
-  if (FMT == LK_IQ4_NL) t = iq4_lookup4(t);
-  return t;
 }
 
 LK_DEV uint32_t lds_u16x2(const uint8_t* p) {   // 2-byte aligned 4 bytes
@@ -89,78 +59,138 @@ LK_DEV uint32_t lds_u16x2(const uint8_t* p) {   // 2-byte aligned 4 bytes
   return uint32_t(q[0]) | (uint32_t(q[1]) << 16);
 }
 
-struct Acc {
-  float v[4];
-};
-
-LK_DEV void group_epilogue(Acc& acc, const float (&d)[4], const float (&s)[4], float a_g, float c_g, float a_g8,
+LK_DEV void group_epilogue(float (&acc)[4], const float (&d)[4], float2 s01, float a_g, float c_g, float a_g8,
                            float c_g8) {
-  acc.v[0] = fmaf(a_g, d[0], fmaf(-c_g, s[0], acc.v[0]));
-  acc.v[1] = fmaf(a_g, d[1], fmaf(-c_g, s[1], acc.v[1]));
-  acc.v[2] = fmaf(a_g8, d[2], fmaf(-c_g8, s[2], acc.v[2]));
-  acc.v[3] = fmaf(a_g8, d[3], fmaf(-c_g8, s[3], acc.v[3]));
+  acc[0] = fmaf(a_g, d[0], fmaf(-c_g, s01.x, acc[0]));
+  acc[1] = fmaf(a_g, d[1], fmaf(-c_g, s01.y, acc[1]));
+  acc[2] = fmaf(a_g8, d[2], fmaf(-c_g8, s01.x, acc[2]));
+  acc[3] = fmaf(a_g8, d[3], fmaf(-c_g8, s01.y, acc[3]));
 }
 
-// One 256-value chunk of 16 rows (rows at `rb + r * rstride`) against the B operand at k0.
+// B fragment (token g, 4 consecutive k) from a consumer's f16 x tile; zero for lanes past the token count
+LK_DEV void bfrag(const __half* xt, int g, int kk, bool valid, uint32_t& b0, uint32_t& b1) {
+  if (valid) {
+    uint2 v = *reinterpret_cast<const uint2*>(xt + g * kXStride + kk);
+    b0 = v.x;
+    b1 = v.y;
+  } else {
+    b0 = b1 = 0;
+  }
+}
+
+// Convert this chunk's activations (ntok tokens x 256 values) to the f16 tile(s) and per-group sums S[t][8].
+template <int XT, int TOK>
+LK_DEV void stage_x(const uint8_t* xraw, int xraw_stride, int ntok, int lane, __half* xt, __half* xl, float* S) {
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) {
+    if (t >= ntok) break;
+    float f[8];
+    if (XT == LK_F32) {
+      const float4* p = reinterpret_cast<const float4*>(xraw + t * xraw_stride) + 2 * lane;
+      float4 u = p[0], v = p[1];
+      f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w; f[4] = v.x; f[5] = v.y; f[6] = v.z; f[7] = v.w;
+    } else {
+      uint4 u = reinterpret_cast<const uint4*>(xraw + t * xraw_stride)[lane];
+      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (XT == LK_BF16) {
+          f[2 * i] = __uint_as_float(w[i] << 16);
+          f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        } else {
+          float2 h = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
+          f[2 * i] = h.x;
+          f[2 * i + 1] = h.y;
+        }
+      }
+    }
+    uint32_t hp[4], lp[4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      hp[i] = h2u(h);
+      if (XT == LK_F32) {
+        float2 hf = __half22float2(h);
+        lp[i] = h2u(__floats2half2_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y));
+      }
+      s += f[2 * i] + f[2 * i + 1];
+    }
+    *reinterpret_cast<uint4*>(xt + t * kXStride + 8 * lane) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+    if (XT == LK_F32)
+      *reinterpret_cast<uint4*>(xl + t * kXStride + 8 * lane) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((lane & 3) == 0) S[t * 8 + (lane >> 2)] = s;   // group lane/4 of token t
+  }
+}
+
+// One 256-value chunk of 16 rows (row r at rb + r*576) against the staged x tile.
 template <int FMT, int XT, int NW>
-LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, int rstride, const void* xrow, bool xvalid, int k0,
-                     int g, int tig, int lane, float2* actab, Acc (&acc)[NW]) {
+LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, const __half* xl, const float* S,
+                     bool xvalid, int g, int tig, int lane, float2* actab, float (&acc)[NW][4]) {
+  constexpr int RS = kMvRowStageBytes;
+  // S for tokens 2tig, 2tig+1 of group j
+  auto sums = [&](int j) { return make_float2(S[(2 * tig) * 8 + j], S[(2 * tig + 1) * 8 + j]); };
   if (FMT == LK_Q4_K) {
-    // cooperative header decode: lane -> (row lane/2, groups 4*(lane&1) .. +3); (a, c') per row and group
+    // cooperative header decode: lane -> (row lane/2, groups 4*(lane&1) .. +3); low-nibble groups (even j) hold
+    // (a, 1024 a + c), high-nibble groups (odd j, codes seen as 16 q) hold (a / 16, 64 a + c)
 #pragma unroll
     for (int wi = 0; wi < NW; ++wi) {
       const uint8_t* rb = wi ? rb1 : rb0;
       int r = lane >> 1, j0 = (lane & 1) * 4;
-      uint4 hv = *reinterpret_cast<const uint4*>(rb + r * rstride);
-      const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hv);
+      uint4 hv = *reinterpret_cast<const uint4*>(rb + r * RS);
       float d = h2f(uint16_t(hv.x & 0xffff)), dmin = h2f(uint16_t(hv.x >> 16));
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        int sc, m;
-        q4k_scale_min(hb + 4, j0 + jj, sc, m);
-        float a = d * float(sc);
-        actab[wi * 128 + r * 8 + j0 + jj] = make_float2(a, fmaf(1024.0f, a, dmin * float(m)));
+        uint32_t sc, m;
+        q4k_scale_min_w(hv.y, hv.z, hv.w, j0 + jj, sc, m);
+        float a = d * float(int(sc)), c = dmin * float(int(m));
+        float2 v = (jj & 1) ? make_float2(a * 0.0625f, fmaf(64.0f, a, c)) : make_float2(a, fmaf(1024.0f, a, c));
+        actab[wi * 128 + r * 8 + j0 + jj] = v;
       }
     }
     __syncwarp();
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      float dl[NW][4], dh[NW][4], sl[4], sh[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        sl[i] = sh[i] = 0.f;
-#pragma unroll
-        for (int wi = 0; wi < NW; ++wi) dl[wi][i] = dh[wi][i] = 0.f;
-      }
+      float dl[NW][4], dh[NW][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        BFrag<XT> bl, bh;
-        int kk = k0 + 64 * p + 16 * h + 4 * tig;
-        bl.load(xrow, kk, xvalid);
-        bh.load(xrow, kk + 32, xvalid);
-        mma_codes<XT>(sl, kOnes, kOnes, kOnes, kOnes, bl);
-        mma_codes<XT>(sh, kOnes, kOnes, kOnes, kOnes, bh);
+        uint32_t bl0, bl1, bh0, bh1;
+        int kk = 64 * p + 16 * h + 4 * tig;
+        bfrag(xt, g, kk, xvalid, bl0, bl1);
+        bfrag(xt, g, kk + 32, xvalid, bh0, bh1);
+        uint32_t ll0 = 0, ll1 = 0, lh0 = 0, lh1 = 0;
+        if (XT == LK_F32) {
+          bfrag(xl, g, kk, xvalid, ll0, ll1);
+          bfrag(xl, g, kk + 32, xvalid, lh0, lh1);
+        }
 #pragma unroll
         for (int wi = 0; wi < NW; ++wi) {
           const uint8_t* rb = wi ? rb1 : rb0;
           int off = 16 + 32 * p + 16 * h + 4 * tig;
-          uint32_t w0 = *reinterpret_cast<const uint32_t*>(rb + g * rstride + off);
-          uint32_t w8 = *reinterpret_cast<const uint32_t*>(rb + (g + 8) * rstride + off);
+          uint32_t w0 = *reinterpret_cast<const uint32_t*>(rb + g * RS + off);
+          uint32_t w8 = *reinterpret_cast<const uint32_t*>(rb + (g + 8) * RS + off);
           uint32_t f0, s0, f8, s8;
-          code_frag(nib_bytes<FMT>(w0, false), f0, s0);
-          code_frag(nib_bytes<FMT>(w8, false), f8, s8);
-          mma_codes<XT>(dl[wi], f0, f8, s0, s8, bl);
-          code_frag(nib_bytes<FMT>(w0, true), f0, s0);
-          code_frag(nib_bytes<FMT>(w8, true), f8, s8);
-          mma_codes<XT>(dh[wi], f0, f8, s0, s8, bh);
+          code_frag(w0 & 0x0F0F0F0Fu, f0, s0);
+          code_frag(w8 & 0x0F0F0F0Fu, f8, s8);
+          if (h == 0) mma16816_z(dl[wi], f0, f8, s0, s8, bl0, bl1);
+          else mma16816(dl[wi], f0, f8, s0, s8, bl0, bl1);
+          if (XT == LK_F32) mma16816(dl[wi], f0, f8, s0, s8, ll0, ll1);
+          code_frag(w0 & 0xF0F0F0F0u, f0, s0);
+          code_frag(w8 & 0xF0F0F0F0u, f8, s8);
+          if (h == 0) mma16816_z(dh[wi], f0, f8, s0, s8, bh0, bh1);
+          else mma16816(dh[wi], f0, f8, s0, s8, bh0, bh1);
+          if (XT == LK_F32) mma16816(dh[wi], f0, f8, s0, s8, lh0, lh1);
         }
       }
+      float2 sl = sums(2 * p), sh = sums(2 * p + 1);
 #pragma unroll
       for (int wi = 0; wi < NW; ++wi) {
-        float2 lo0 = actab[wi * 128 + g * 8 + 2 * p], lo8 = actab[wi * 128 + (g + 8) * 8 + 2 * p];
-        float2 hi0 = actab[wi * 128 + g * 8 + 2 * p + 1], hi8 = actab[wi * 128 + (g + 8) * 8 + 2 * p + 1];
-        group_epilogue(acc[wi], dl[wi], sl, lo0.x, lo0.y, lo8.x, lo8.y);
-        group_epilogue(acc[wi], dh[wi], sh, hi0.x, hi0.y, hi8.x, hi8.y);
+        float4 r0 = *reinterpret_cast<const float4*>(&actab[wi * 128 + g * 8 + 2 * p]);
+        float4 r8 = *reinterpret_cast<const float4*>(&actab[wi * 128 + (g + 8) * 8 + 2 * p]);
+        group_epilogue(acc[wi], dl[wi], sl, r0.x, r0.y, r8.x, r8.y);
+        group_epilogue(acc[wi], dh[wi], sh, r0.z, r0.w, r8.z, r8.w);
       }
     }
     __syncwarp();   // the table is rewritten by the next chunk
@@ -168,65 +198,80 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, int rstride, const 
     constexpr float kOff = FMT == LK_Q4_0 ? 1032.0f : 1152.0f;   // magic 1024 + (8 | 128 codebook bias)
 #pragma unroll 2
     for (int j = 0; j < 8; ++j) {
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-      float dd[NW][4];
-      BFrag<XT> b0, b1;
-      int kk = k0 + 32 * j + 4 * tig;
-      b0.load(xrow, kk, xvalid);
-      b1.load(xrow, kk + 16, xvalid);
-      mma_codes<XT>(s, kOnes, kOnes, kOnes, kOnes, b0);
-      mma_codes<XT>(s, kOnes, kOnes, kOnes, kOnes, b1);
+      uint32_t b00, b01, b10, b11, l00 = 0, l01 = 0, l10 = 0, l11 = 0;
+      int kk = 32 * j + 4 * tig;
+      bfrag(xt, g, kk, xvalid, b00, b01);
+      bfrag(xt, g, kk + 16, xvalid, b10, b11);
+      if (XT == LK_F32) {
+        bfrag(xl, g, kk, xvalid, l00, l01);
+        bfrag(xl, g, kk + 16, xvalid, l10, l11);
+      }
+      float2 s = sums(j);
 #pragma unroll
       for (int wi = 0; wi < NW; ++wi) {
-        const uint8_t* rb = (wi ? rb1 : rb0) + 18 * j;
-        const uint8_t* p0 = rb + g * rstride;
-        const uint8_t* p8 = rb + (g + 8) * rstride;
+        const uint8_t* blk = (wi ? rb1 : rb0) + 18 * j;
+        const uint8_t* p0 = blk + g * RS;
+        const uint8_t* p8 = blk + (g + 8) * RS;
         float d0 = h2f(*reinterpret_cast<const uint16_t*>(p0));
         float d8 = h2f(*reinterpret_cast<const uint16_t*>(p8));
         uint32_t w0 = lds_u16x2(p0 + 2 + 4 * tig), w8 = lds_u16x2(p8 + 2 + 4 * tig);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dd[wi][i] = 0.f;
+        uint32_t t0 = w0 & 0x0F0F0F0Fu, t8 = w8 & 0x0F0F0F0Fu;
+        uint32_t u0 = (w0 >> 4) & 0x0F0F0F0Fu, u8 = (w8 >> 4) & 0x0F0F0F0Fu;
+        if (FMT == LK_IQ4_NL) {
+          t0 = iq4_lookup4(t0);
+          t8 = iq4_lookup4(t8);
+          u0 = iq4_lookup4(u0);
+          u8 = iq4_lookup4(u8);
+        }
+        float dd[4];
         uint32_t f0, s0, f8, s8;
-        code_frag(nib_bytes<FMT>(w0, false), f0, s0);
-        code_frag(nib_bytes<FMT>(w8, false), f8, s8);
-        mma_codes<XT>(dd[wi], f0, f8, s0, s8, b0);
-        code_frag(nib_bytes<FMT>(w0, true), f0, s0);
-        code_frag(nib_bytes<FMT>(w8, true), f8, s8);
-        mma_codes<XT>(dd[wi], f0, f8, s0, s8, b1);
-        group_epilogue(acc[wi], dd[wi], s, d0, kOff * d0, d8, kOff * d8);
+        code_frag(t0, f0, s0);
+        code_frag(t8, f8, s8);
+        mma16816_z(dd, f0, f8, s0, s8, b00, b01);
+        if (XT == LK_F32) mma16816(dd, f0, f8, s0, s8, l00, l01);
+        code_frag(u0, f0, s0);
+        code_frag(u8, f8, s8);
+        mma16816(dd, f0, f8, s0, s8, b10, b11);
+        if (XT == LK_F32) mma16816(dd, f0, f8, s0, s8, l10, l11);
+        group_epilogue(acc[wi], dd, s, d0, kOff * d0, d8, kOff * d8);
       }
     }
   }
 }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE>
-__global__ void __launch_bounds__(kMvThreads) k_mv(MvArgs a) {
+template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
+__global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUtensorMap wmap,
+                                                   const __grid_constant__ CUtensorMap w2map, MvArgs a) {
   constexpr int NW = SWIGLU ? 2 : 1;
-  constexpr int kStageBytes = NW * kMvRows * kMvRowStageBytes;
+  constexpr int XE = XT == LK_F32 ? 4 : 2;                          // activation element bytes
+  constexpr int kXStageBytes = TOK * kMvStageChunks * 256 * XE;     // raw activations per stage
+  constexpr int kStageBytes = NW * kMvWBytes + kXStageBytes;
+  constexpr int kMvStages = mv_stages(kStageBytes);
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * TOK * kXStride;      // f16 elements of a consumer's x tile(s)
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kMvStages * kStageBytes);
   uint64_t* empty = full + kMvStages;
-  float2* actab_all = reinterpret_cast<float2*>(empty + kMvStages);   // [consumers][NW][16][8]
-  float* red = reinterpret_cast<float*>(actab_all + kMvConsumers * NW * 128);   // [consumers][NW][32][4]
+  float2* actab_all = reinterpret_cast<float2*>(empty + kMvStages);                 // [consumers][NW][16][8]
+  float* red = reinterpret_cast<float*>(actab_all + kMvConsumers * NW * 128);       // [consumers][NW][32][4]
+  float* S_all = red + kMvConsumers * NW * 32 * 4;                                  // [consumers][TOK][8]
+  __half* xt_all = reinterpret_cast<__half*>(S_all + kMvConsumers * TOK * 8);       // [consumers][kXT]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * kMvRows;
-  const int nrows = min(kMvRows, a.n - r0);
-  const uint8_t* wb = a.w;
-  const uint8_t* w2b = a.w2;
+  int wrow = r0, w2row = r0 + a.w2_row_offset;
   int xrow0, ntok, yrow0;
   if (MOE) {
     int asg = blockIdx.y;
     int e = min(max(a.ids[asg], 0), a.n_experts - 1);
-    wb = a.w + int64_t(e) * a.expert_stride;
-    if (SWIGLU) w2b = a.w2 ? a.w2 + int64_t(e) * a.expert_stride : wb + a.w2_offset;
+    wrow = e * a.rows_per_expert + r0;
+    w2row = e * a.rows_per_expert2 + a.w2_row_offset + r0;
     xrow0 = asg / a.x_div;
     ntok = 1;
     yrow0 = asg;
   } else {
-    xrow0 = blockIdx.y * 8;
-    ntok = min(8, a.tokens - xrow0);
+    xrow0 = blockIdx.y * TOK;
+    ntok = min(TOK, a.tokens - xrow0);
     yrow0 = xrow0;
   }
   const int kchunks = a.k / kChunkValues;
@@ -242,24 +287,23 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(MvArgs a) {
   __syncthreads();
 
   if (warp == kMvConsumers) {
-    // producer: stage st holds chunks [st*4, st*4+4) of every row
-    for (int st = 0; st < nstages; ++st) {
-      int s = st % kMvStages;
-      if (st >= kMvStages) {
-        if (!mbar_wait(&empty[s], ((st / kMvStages) - 1) & 1)) atomicOr(&g_status, 1u);
-      }
-      int c0 = st * kMvStageChunks;
-      int nch = min(kMvStageChunks, kchunks - c0);
-      uint32_t bytes = uint32_t(nch) * kChunkBytes;
-      if (lane == 0) mbar_expect_tx(&full[s], bytes * nrows * NW);
-      __syncwarp();
-      if (lane < NW * kMvRows) {
-        int wi = lane / kMvRows, r = lane % kMvRows;
-        if (r < nrows) {
-          const uint8_t* src = (wi ? w2b : wb) + int64_t(r0 + r) * a.row_bytes + int64_t(c0) * kChunkBytes;
-          uint8_t* dst = ring + s * kStageBytes + wi * kMvRows * kMvRowStageBytes + r * kMvRowStageBytes;
-          bulk_g2s(dst, src, bytes, &full[s]);
-        }
+    // producer: stage st = chunks [4 st, 4 st + 4) of the 16 rows, and the same k range of every token
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+      const uint8_t* xbase = static_cast<const uint8_t*>(a.x) + int64_t(xrow0) * a.k * XE;
+      for (int st = 0; st < nstages; ++st) {
+        int s = st % kMvStages;
+        if (st >= kMvStages && !mbar_wait(&empty[s], ((st / kMvStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        int c0 = st * kMvStageChunks;
+        uint32_t xbytes = uint32_t(min(kMvStageChunks, kchunks - c0)) * 256u * XE;
+        mbar_expect_tx(&full[s], uint32_t(NW * kMvWBytes) + xbytes * ntok);
+        uint8_t* stg = ring + s * kStageBytes;
+        tma_load_2d(stg, &wmap, c0 * (kChunkBytes / 4), wrow, &full[s]);
+        if (NW == 2) tma_load_2d(stg + kMvWBytes, &w2map, c0 * (kChunkBytes / 4), w2row, &full[s]);
+        for (int t = 0; t < ntok; ++t)
+          bulk_g2s(stg + NW * kMvWBytes + t * (kMvStageChunks * 256 * XE), xbase + (int64_t(t) * a.k + c0 * 256) * XE,
+                   xbytes, &full[s]);
       }
     }
     return;
@@ -267,23 +311,26 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(MvArgs a) {
 
   // consumers
   const int g = lane >> 2, tig = lane & 3;
-  Acc acc[NW];
+  float acc[NW][4];
 #pragma unroll
   for (int wi = 0; wi < NW; ++wi)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[wi].v[i] = 0.f;
+    for (int i = 0; i < 4; ++i) acc[wi][i] = 0.f;
   const bool xvalid = g < ntok;
-  const void* xrow = static_cast<const uint8_t*>(a.x) +
-                     (int64_t(xrow0) + (xvalid ? g : 0)) * a.k * (a.x_dtype == LK_F32 ? 4 : 2);
   float2* actab = actab_all + warp * NW * 128;
+  float* S = S_all + warp * TOK * 8;
+  __half* xt = xt_all + warp * kXT;
+  __half* xl = xt + TOK * kXStride;
   for (int st = 0; st < nstages; ++st) {
     int s = st % kMvStages;
     if (!mbar_wait(&full[s], (st / kMvStages) & 1)) atomicOr(&g_status, 1u);
     int c = st * kMvStageChunks + warp;
     if (c < kchunks) {
-      const uint8_t* rb0 = ring + s * kStageBytes + warp * kChunkBytes;
-      const uint8_t* rb1 = rb0 + kMvRows * kMvRowStageBytes;
-      mv_chunk<FMT, XT, NW>(rb0, rb1, kMvRowStageBytes, xrow, xvalid, c * kChunkValues, g, tig, lane, actab, acc);
+      const uint8_t* stg = ring + s * kStageBytes;
+      stage_x<XT, TOK>(stg + NW * kMvWBytes + warp * 256 * XE, kMvStageChunks * 256 * XE, ntok, lane, xt, xl, S);
+      __syncwarp();
+      const uint8_t* rb0 = stg + warp * kChunkBytes;
+      mv_chunk<FMT, XT, NW>(rb0, rb0 + kMvWBytes, xt, xl, S, xvalid, g, tig, lane, actab, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -293,7 +340,7 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(MvArgs a) {
 #pragma unroll
   for (int wi = 0; wi < NW; ++wi)
     *reinterpret_cast<float4*>(red + ((warp * NW + wi) * 32 + lane) * 4) =
-        make_float4(acc[wi].v[0], acc[wi].v[1], acc[wi].v[2], acc[wi].v[3]);
+        make_float4(acc[wi][0], acc[wi][1], acc[wi][2], acc[wi][3]);
   asm volatile("bar.sync 1, %0;" ::"r"(kMvConsumers * 32));
   if (warp != 0) return;
   float out[NW][4];
@@ -317,42 +364,67 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(MvArgs a) {
   }
 }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE>
-static int launch_mv(const MvArgs& a, int groups, cudaStream_t s) {
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
+             int box_cols, int box_rows, CUtensorMapSwizzle swz);
+
+template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
+static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
   constexpr int NW = SWIGLU ? 2 : 1;
-  constexpr int kStageBytes = NW * kMvRows * kMvRowStageBytes;
+  constexpr int XE = XT == LK_F32 ? 4 : 2;
+  constexpr int kStageBytes = NW * kMvWBytes + TOK * kMvStageChunks * 256 * XE;
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * TOK * kXStride;
+  constexpr int kMvStages = mv_stages(kStageBytes);
+  static_assert(kMvStages * kStageBytes + 64 * 1024 <= 227 * 1024, "matvec CTA exceeds shared memory");
   constexpr int smem = kMvStages * kStageBytes + 2 * kMvStages * 8 + kMvConsumers * NW * 128 * 8 +
-                       kMvConsumers * NW * 32 * 4 * 4;
-  auto kern = k_mv<FMT, XT, SWIGLU, MOE>;
-  static unsigned configured = 0;   // one bit per device
+                       kMvConsumers * NW * 32 * 4 * 4 + kMvConsumers * TOK * 8 * 4 + kMvConsumers * kXT * 2;
+  auto kern = k_mv<FMT, XT, SWIGLU, MOE, TOK>;
+  static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((a.n + kMvRows - 1) / kMvRows, groups);
-  kern<<<grid, kMvThreads, smem, s>>>(a);
+  kern<<<grid, kMvThreads, smem, s>>>(wm, w2m, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 template <int FMT, int XT>
-static int mv_x(const MvArgs& a, int groups, cudaStream_t s) {
-  bool moe = a.ids != nullptr;
-  if (a.swiglu) return moe ? launch_mv<FMT, XT, true, true>(a, groups, s) : launch_mv<FMT, XT, true, false>(a, groups, s);
-  return moe ? launch_mv<FMT, XT, false, true>(a, groups, s) : launch_mv<FMT, XT, false, false>(a, groups, s);
+static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
+  if (a.ids) {
+    if (a.swiglu) return launch_mv<FMT, XT, true, true, 1>(wm, w2m, a, groups, s);
+    return launch_mv<FMT, XT, false, true, 1>(wm, w2m, a, groups, s);
+  }
+  if (a.tokens == 1) {
+    if (a.swiglu) return launch_mv<FMT, XT, true, false, 1>(wm, w2m, a, groups, s);
+    return launch_mv<FMT, XT, false, false, 1>(wm, w2m, a, groups, s);
+  }
+  if (a.swiglu) return launch_mv<FMT, XT, true, false, 8>(wm, w2m, a, groups, s);
+  return launch_mv<FMT, XT, false, false, 8>(wm, w2m, a, groups, s);
 }
 
 template <int FMT>
-static int mv_f(const MvArgs& a, int groups, cudaStream_t s) {
+static int mv_f(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
   switch (a.x_dtype) {
-    case LK_F16: return mv_x<FMT, LK_F16>(a, groups, s);
-    case LK_BF16: return mv_x<FMT, LK_BF16>(a, groups, s);
-    case LK_F32: return mv_x<FMT, LK_F32>(a, groups, s);
+    case LK_F16: return mv_x<FMT, LK_F16>(wm, w2m, a, groups, s);
+    case LK_BF16: return mv_x<FMT, LK_BF16>(wm, w2m, a, groups, s);
+    case LK_F32: return mv_x<FMT, LK_F32>(wm, w2m, a, groups, s);
   }
   return LK_EINVAL;
 }
 
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s) {
+  // weight maps: the packed rows as u32 columns, 16 rows x 576 bytes per box; MoE experts stacked as rows
+  int64_t rows = a.ids ? int64_t(a.n_experts) * a.rows_per_expert : a.n;
+  int64_t rows2 = a.ids ? int64_t(a.n_experts) * a.rows_per_expert2 : a.n;
+  CUtensorMap wm, w2m;
+  int rc = make_map(&wm, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows, a.row_bytes / 4, kMvRowStageBytes / 4, kMvRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == LK_OK)
+    rc = a.w2 ? make_map(&w2m, a.w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows2, a.row_bytes / 4, kMvRowStageBytes / 4,
+                         kMvRows, CU_TENSOR_MAP_SWIZZLE_NONE)
+              : (w2m = wm, LK_OK);
+  if (rc != LK_OK) return rc;
   switch (fmt) {
-    case LK_Q4_0: return mv_f<LK_Q4_0>(a, groups, s);
-    case LK_Q4_K: return mv_f<LK_Q4_K>(a, groups, s);
-    case LK_IQ4_NL: return mv_f<LK_IQ4_NL>(a, groups, s);
+    case LK_Q4_0: return mv_f<LK_Q4_0>(wm, w2m, a, groups, s);
+    case LK_Q4_K: return mv_f<LK_Q4_K>(wm, w2m, a, groups, s);
+    case LK_IQ4_NL: return mv_f<LK_IQ4_NL>(wm, w2m, a, groups, s);
   }
   return LK_EUNSUPPORTED;
 }
