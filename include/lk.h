@@ -100,11 +100,21 @@ int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, cons
  * (gen_mxfp4s.py:50-500; signature test tests/test_mxfp4s_f8.py:150-160),
  * launch(%rows, %k, %n, %x, %scales, %w, %ws [, %w2, %w2s], %y): y = (x8 . (W * 2^8)^T) * s8[row][1].
  * x8: [rows][k] e4m3, s8: [rows][2] (lk_row_scale_f8), w: nibble plane [n][k/2], ws: E8M0 plane [n][k/32].
- * k % 128 == 0, n % 16 == 0.
+ * k % 32 == 0 (the reference asks k % 128; gpt-oss's k = 2880 is not), n % 16 == 0. The block scales are applied
+ * by the tensor core (exact for every E8M0 value; the reference's e5m2 decode covers exponents 107..132 only).
  */
 int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8,
                       const uint8_t* w, const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y,
                       lk_stream_t stream);
+/* The MXFP4 x FP8 GEMM grouped over the MoE tile schedule: the grouped-GEMM signature (gen_moe.py:1145-1146,
+ * %xrows, %tile_info, %rowmap before %x) with the fp8 GEMM's operands (gen_mxfp4s.py:101). Rows, tiles, gather,
+ * fused gate/up and skipped tiles as lk_moe_grouped_gemm; x8/s8 as lk_gemm_mxfp4s_f8 (gate/up: [xrows] token rows,
+ * down: [rows] sorted rows); w/ws per expert n rows (fused gate/up: 2n, gate then up) of k/2 nibble bytes and k/32
+ * E8M0 bytes. */
+int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
+                                  int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
+                                  const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
+                                  const uint8_t* w2s, float* y, lk_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * MoE (gen_moe.py). Assignment a = t * ku + slot.

@@ -30,6 +30,8 @@ SIGNATURES = {
     "lk_moe_route": (_I, [_I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _P, _P, _P]),
     "lk_moe_bucket": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "lk_moe_grouped_gemm": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "lk_moe_grouped_gemm_mxfp4s_f8": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                           _P]),
     "lk_moe_combine_sorted": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "lk_moe_expert_mv": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "lk_moe_combine": (_I, [_I, _I, _I, _I, _P, _P, _P, _P]),

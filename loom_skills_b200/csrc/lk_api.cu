@@ -13,6 +13,11 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
          int n_experts, int64_t expert_stride, int64_t w2_offset);
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
+int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+            const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
+            const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
+            int w2_row_offset);
+unsigned int status_mx(bool clear);
 int moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
               const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s);
 int moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_t* info, const int32_t* ids,
@@ -56,7 +61,9 @@ int64_t lk_row_bytes(int fmt, int64_t k) {
 }
 
 // Reads (and optionally clears) the device-side status word: bit 0 = a kernel's bounded wait gave up. Synchronous.
-unsigned int lk_device_status(int clear) { return status_mv(clear != 0) | status_gemm(clear != 0); }
+unsigned int lk_device_status(int clear) {
+  return status_mv(clear != 0) | status_gemm(clear != 0) | status_mx(clear != 0);
+}
 
 int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,
                lk_stream_t stream) {
@@ -181,13 +188,31 @@ int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t
   if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
   if (rows < 0 || k <= 0 || n <= 0) return LK_EINVAL;
-  if (k % 128 || n % 16) return LK_EINVAL;
+  if (k % 32 || n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
   if (!x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
   if (mode == LK_SWIGLU && (!w2 || !w2s)) return LK_EINVAL;
-  if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(ws, 16) || !aligned(y, 16)) return LK_EALIGN;
-  if (w2 && (!aligned(w2, 16) || !aligned(w2s, 16))) return LK_EALIGN;
+  if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(y, 16)) return LK_EALIGN;
+  if (w2 && !aligned(w2, 16)) return LK_EALIGN;
   return gemm_mxfp4s(mode, order, rows, k, n, x8, s8, w, ws, w2, w2s, y, (cudaStream_t)stream);
+}
+
+int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
+                                  int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
+                                  const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
+                                  const uint8_t* w2s, float* y, lk_stream_t stream) {
+  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
+  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (k % 32 || n % 16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!tile_info || !rowmap || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
+  const bool two = mode == LK_SWIGLU && !fused;
+  if (two && (!w2 || !w2s)) return LK_EINVAL;
+  if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(y, 16) || (two && !aligned(w2, 16))) return LK_EALIGN;
+  const int fuse = mode == LK_SWIGLU && fused;
+  return gemm_mx(mode, order, rows, k, n, x8, s8, w, ws, two ? w2 : nullptr, two ? w2s : nullptr, y,
+                 (cudaStream_t)stream, tile_info, rowmap, xrows, ku, n_experts, fuse ? 2 * n : n, fuse ? n : 0);
 }
 
 int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,

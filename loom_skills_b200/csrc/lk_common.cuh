@@ -147,6 +147,17 @@ LK_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// Four rows (row coordinates r0..r3, one-row boxes) gathered by one TMA instruction, completing on `bar`
+LK_DEV void tma_gather4(void* dst, const CUtensorMap* map, int x, int r0, int r1, int r2, int r3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
+// 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile (1024-byte aligned)
+LK_DEV uint32_t sw128(int r, int c) { return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
 LK_DEV void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -184,6 +195,37 @@ LK_DEV void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// kind::mxf8f6f4 with block scale factors (one E8M0 byte per 32 k per row of A and of B) read from TMEM at sfa/sfb
+// (bits 30-31 of each address: the byte of the 32-bit scale column, matching the instruction descriptor's sf ids)
+LK_DEV void umma_mx(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                    uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// 32 rows x 16 bytes of shared memory -> 4 TMEM columns of lanes 0-31, replicated to all four lane quarters
+LK_DEV void tmem_cp_32x128_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Shared-memory descriptor of a dense, unswizzled block of 16-byte rows (8-row core matrices 128 bytes apart)
+LK_DEV uint64_t sdesc_rows16(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFF);
+  d |= uint64_t(128 >> 4) << 16;   // leading byte offset (one 16-byte column: unused)
+  d |= uint64_t(128 >> 4) << 32;   // stride byte offset: next 8-row core matrix
+  d |= uint64_t(1) << 46;          // version (sm_100); layout type 0 = no swizzle
+  return d;
+}
+// Instruction descriptor, kind::mxf8f6f4.block_scale: A format fa, B format fb (0 e4m3, 1 e5m2, 5 e2m1), E8M0
+// scales, K-major operands, sf ids of A and B
+__host__ __device__ constexpr uint32_t idesc_mx(int m, int n, int fa, int fb, int sfa_id, int sfb_id) {
+  return (uint32_t(sfb_id) << 4) | (uint32_t(fa) << 7) | (uint32_t(fb) << 10) | (uint32_t(n >> 3) << 17) |
+         (1u << 23) | (uint32_t(m >> 4) << 24) | (uint32_t(sfa_id) << 29);
+}
+
 // arrive on `bar` when every previously issued tcgen05.mma of this thread has completed
 LK_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

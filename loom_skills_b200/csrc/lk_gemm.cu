@@ -22,7 +22,7 @@
 namespace lk {
 
 constexpr int kBM = 128, kBK = 64;
-constexpr int kSA = 4, kSB = 2, kSR = 2;
+constexpr int kSA = 4, kSR = 2;
 constexpr int kDqWarps = 8;
 constexpr int kGemmThreads = (2 + kDqWarps) * 32;
 
@@ -43,15 +43,6 @@ struct GemmArgs {
 };
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
-LK_DEV uint32_t sw128(int r, int c) { return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
-
-LK_DEV void tma_gather4(void* dst, const CUtensorMap* map, int x, int r0, int r1, int r2, int r3, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
-      : "memory");
-}
 
 LK_DEV uint32_t hsub2u(uint32_t a, uint32_t b) {
   __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
@@ -139,27 +130,38 @@ LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int
   }
 }
 
-template <int FMT, int BN, int NW, int MODE, int GROUP>
+// stage counts for a tile configuration: 4 A stages, 2 packed-byte stages, as many B stages (2..4) as fit
+constexpr int gemm_sb(int a_bytes, int b_bytes, int r_bytes) {
+  return (220 * 1024 - 4 * a_bytes - 2 * r_bytes) / b_bytes >= 4 ? 4
+         : (220 * 1024 - 4 * a_bytes - 2 * r_bytes) / b_bytes >= 3 ? 3 : 2;
+}
+
+// MH: 128-row halves per tile (2 = a 256-row tile: two M=128 accumulators share every dequantised B stage, halving
+// the dequantisation per FLOP)
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
            const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
-  constexpr int kRowsB = BN * NW;                 // weight rows dequantised per stage (256)
-  constexpr int kABytes = kBM * kBK * 2;          // 16 KB
-  constexpr int kBBytes = kRowsB * kBK * 2;       // 32 KB
-  constexpr int kRBytes = kRowsB * kChunkBytes;   // 36 KB
-  constexpr uint32_t kTmemCols = BN * NW;         // 256
+  constexpr int kTM = kBM * MH;                   // tile rows
+  constexpr int kRowsB = BN * NW;                 // weight rows dequantised per stage
+  constexpr int kABytes = kTM * kBK * 2;
+  constexpr int kBBytes = kRowsB * kBK * 2;
+  constexpr int kRBytes = kRowsB * kChunkBytes;
+  constexpr int kSBt = gemm_sb(kABytes, kBBytes, kRBytes);
+  constexpr uint32_t kTmemCols = MH * NW * BN;    // 256
   static_assert(kRowsB == 2 * kDqWarps * 16 || kRowsB == kDqWarps * 16, "one or two rows per dequant thread");
+  static_assert(kTmemCols == 256, "accumulator columns");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + kSA * kABytes;
-  uint8_t* sR = sB + kSB * kBBytes;
+  uint8_t* sR = sB + kSBt * kBBytes;
   uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + kSR * kRBytes);
   uint64_t* empty_a = full_a + kSA;
   uint64_t* full_b = empty_a + kSA;
-  uint64_t* empty_b = full_b + kSB;
-  uint64_t* full_r = empty_b + kSB;
+  uint64_t* empty_b = full_b + kSBt;
+  uint64_t* full_r = empty_b + kSBt;
   uint64_t* empty_r = full_r + kSR;
   uint64_t* acc_full = empty_r + kSR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
@@ -171,8 +173,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int kstages = p.k / kBK;
 
   // ---- which rows: dense tile, or a 128-row super-tile of one expert made of <= 2 schedule tiles
-  int m0 = blockIdx.y * kBM;
-  int valid_rows = min(kBM, p.rows - m0);
+  int m0 = blockIdx.y * kTM;
+  int valid_rows = min(kTM, p.rows - m0);
   int wrow = n0, w2row = n0 + p.w2_row_offset;   // first weight row of this tile in wmap / w2map
   if (GROUP != kDense) {
     if (threadIdx.x == 0) {
@@ -183,14 +185,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (e < 0) break;
         int rows0 = p.tile_info[2 * t + 1];
         bool pair = t + 1 < p.max_tiles && p.tile_info[2 * (t + 1)] == e;
-        int rows = rows0 + (pair ? p.tile_info[2 * (t + 1) + 1] : 0);
         if (s == int(blockIdx.y)) {
           found = e;
           first = t;
           nrows = pair ? 64 + p.tile_info[2 * (t + 1) + 1] : rows0;
           break;
         }
-        (void)rows;
         ++s;
         t += pair ? 2 : 1;
       }
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&full_a[i], 1);
       mbar_init(&empty_a[i], 1);
     }
-    for (int i = 0; i < kSB; ++i) {
+    for (int i = 0; i < kSBt; ++i) {
       mbar_init(&full_b[i], kDqWarps);
       mbar_init(&empty_b[i], 1);
     }
@@ -278,18 +278,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
     const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
     for (int ks = 0; ks < kstages; ++ks) {
-      int sa = ks % kSA, sb = ks % kSB;
+      int sa = ks % kSA, sb = ks % kSBt;
       if (!mbar_wait(&full_a[sa], (ks / kSA) & 1)) atomicOr(&g_status, 1u);
-      if (!mbar_wait(&full_b[sb], (ks / kSB) & 1)) atomicOr(&g_status, 1u);
+      if (!mbar_wait(&full_b[sb], (ks / kSBt) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
-          uint64_t ad = sdesc_k128(a_base + sa * kABytes + kk * 32);
 #pragma unroll
-          for (int wi = 0; wi < NW; ++wi) {
-            uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
-            umma_f16(tmem + wi * BN, ad, bd, idesc, (ks | kk) != 0);
+          for (int mh = 0; mh < MH; ++mh) {
+            uint64_t ad = sdesc_k128(a_base + sa * kABytes + mh * (kBM * 128) + kk * 32);
+#pragma unroll
+            for (int wi = 0; wi < NW; ++wi) {
+              uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
+              umma_f16(tmem + (mh * NW + wi) * BN, ad, bd, idesc, (ks | kk) != 0);
+            }
           }
         }
         umma_commit(&empty_a[sa]);
@@ -303,9 +306,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int dt = threadIdx.x - 64;   // 0..255
     constexpr int kGroupsPerThread = kRowsB * 2 / (kDqWarps * 32);   // 2 (256 rows) or 1 (128 rows)
     for (int ks = 0; ks < kstages; ++ks) {
-      int c = ks >> 2, sub = ks & 3, sr = c % kSR, sb = ks % kSB;
+      int c = ks >> 2, sub = ks & 3, sr = c % kSR, sb = ks % kSBt;
       if (sub == 0 && !mbar_wait(&full_r[sr], (c / kSR) & 1)) atomicOr(&g_status, 1u);
-      if (ks >= kSB && !mbar_wait(&empty_b[sb], ((ks / kSB) - 1) & 1)) atomicOr(&g_status, 1u);
+      if (ks >= kSBt && !mbar_wait(&empty_b[sb], ((ks / kSBt) - 1) & 1)) atomicOr(&g_status, 1u);
       uint8_t* bt = sB + sb * kBBytes;
 #pragma unroll
       for (int gi = 0; gi < kGroupsPerThread; ++gi) {
@@ -320,11 +323,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (sub == 3) mbar_arrive(&empty_r[sr]);
       }
     }
-    // epilogue: warp quadrant q reads TMEM lanes 32q..32q+31 (= tile rows); two warps per quadrant split columns
+    // epilogue: warp quadrant q reads TMEM lanes 32q..32q+31 (rows of a 128-row half). With MH = 2 the two warps of
+    // a quadrant take one half each; with MH = 1 they split the columns.
     if (!mbar_wait(acc_full, 0)) atomicOr(&g_status, 1u);
     tc_fence_after();
-    const int q = warp & 3, half = (warp - 2) >> 2;
-    const int row = 32 * q + lane;
+    const int q = warp & 3, pair = (warp - 2) >> 2;
+    const int mh = MH == 2 ? pair : 0;
+    const int row = mh * kBM + 32 * q + lane;
     const bool row_ok = row < valid_rows;
     float inv = 0.f;
     float* yrow = nullptr;
@@ -338,15 +343,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       inv = srow >= 0 ? p.scales[2 * int64_t(srow) + 1] : 0.f;
       yrow = p.y + int64_t(grow) * p.n + n0;
     }
-    constexpr int kColsPerWarp = BN / 2;
+    constexpr int kColsPerWarp = MH == 2 ? BN : BN / 2;
+    const int col0 = MH == 2 ? 0 : pair * kColsPerWarp;
+    const uint32_t tbase = tmem + (uint32_t(32 * q) << 16) + mh * NW * BN;
 #pragma unroll 1
     for (int cb = 0; cb < kColsPerWarp; cb += 32) {
-      int col = half * kColsPerWarp + cb;
+      int col = col0 + cb;
       float v[32];
-      tmem_ld32(tmem + (uint32_t(32 * q) << 16) + col, v);
+      tmem_ld32(tbase + col, v);
       if (NW == 2) {
         float u[32];
-        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + BN + col, u);
+        tmem_ld32(tbase + BN + col, u);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
       } else {
@@ -417,27 +424,34 @@ struct GemmMaps {
   CUtensorMap a, w, w2;
 };
 
-template <int FMT, int BN, int NW, int MODE, int GROUP>
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH>
 static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
-  constexpr int smem = 1024 + kSA * kBM * kBK * 2 + kSB * kRowsB * kBK * 2 + kSR * kRowsB * kChunkBytes + 256 + 32 +
-                       kBM * 4;
-  auto kern = k_gemm<FMT, BN, NW, MODE, GROUP>;
+  constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2, kRBytes = kRowsB * kChunkBytes;
+  constexpr int smem = 1024 + kSA * kABytes + gemm_sb(kABytes, kBBytes, kRBytes) * kBBytes + kSR * kRBytes + 256 +
+                       32 + kBM * 4;
+  static_assert(smem <= 227 * 1024, "GEMM CTA exceeds shared memory");
+  auto kern = k_gemm<FMT, BN, NW, MODE, GROUP, MH>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   kern<<<grid, kGemmThreads, smem, s>>>(m.a, m.w, m.w2, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
+// tile shape per mode: (BN, NW, MH)
+//   dense store/acc  128 x 1 x 2   a 256 x 128 tile, two M=128 accumulators sharing each dequantised B stage
+//   dense swiglu     128 x 2 x 1   128 rows x 128 columns of gate and of up
+//   grouped gate/up  128 x 2 x 1   (MoE super-tiles hold at most 128 rows of one expert)
+//   grouped down     256 x 1 x 1
 template <int FMT>
 static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
   if (group == kDense) {
-    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense>(m, a, grid, s);
-    if (mode == LK_ACC) return launch_gemm<FMT, 256, 1, LK_ACC, kDense>(m, a, grid, s);
-    return launch_gemm<FMT, 256, 1, LK_STORE, kDense>(m, a, grid, s);
+    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense, 1>(m, a, grid, s);
+    if (mode == LK_ACC) return launch_gemm<FMT, 128, 1, LK_ACC, kDense, 2>(m, a, grid, s);
+    return launch_gemm<FMT, 128, 1, LK_STORE, kDense, 2>(m, a, grid, s);
   }
-  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather>(m, a, grid, s);
-  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted>(m, a, grid, s);
+  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather, 1>(m, a, grid, s);
+  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted, 1>(m, a, grid, s);
 }
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
@@ -467,11 +481,12 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
   a.w2_row_offset = (mode == LK_SWIGLU && !w2) ? int(w2_offset / rb) : 0;
-  const int bn = (mode == LK_SWIGLU) ? 128 : 256;
+  const int bn = (group == kSorted) ? 256 : 128;
+  const int tm = (group == kDense && mode != LK_SWIGLU) ? 2 * kBM : kBM;   // tile rows
   GemmMaps m;
   int rc = group == kGather ? make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xrows, k, kBK, 1,
                                        CU_TENSOR_MAP_SWIZZLE_128B)   // one-row boxes for gather4
-                            : make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, k, kBK, kBM,
+                            : make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, k, kBK, tm,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc == LK_OK)
     rc = make_map(&m.w, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wrows, rb / 4, kChunkBytes / 4, bn,
@@ -482,7 +497,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
             : (m.w2 = m.w, LK_OK);
   if (rc != LK_OK) return rc;
   // grouped: one CTA per possible 128-row super-tile (at most one per schedule tile)
-  dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + kBM - 1) / kBM : rows / 64);
+  dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + tm - 1) / tm : rows / 64);
   switch (fmt) {
     case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, m, a, grid, s);
     case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, m, a, grid, s);

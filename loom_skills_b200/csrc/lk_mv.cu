@@ -3,9 +3,9 @@
 // Replaces g_mv_{fmt}_k{K}[_t{TG}][_r{R}] and its swiglu pair (gen_llm.py:1159-1378) and the MoE expert matvecs
 // g_moe_gu_/g_moe_dn_ (gen_moe.py:535-727).
 //
-// Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, one 2-D TMA
-// box of the rows' packed bytes (16 rows x 576 bytes = 1024 k) plus the matching slice of each token's activations
-// (1-D bulk copies) into a 4-stage shared-memory ring. Four consumer warps each take one 256-value chunk of every
+// Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, four 2-D TMA
+// boxes of the rows' packed bytes (16 rows x 144 bytes = 256 k each, 1024 k per stage) plus the matching slice of
+// each token's activations (1-D bulk copies) into a 4-stage shared-memory ring. Four consumer warps each take one 256-value chunk of every
 // stage: they convert their activation slice to f16 once (with per-32-value group sums), then unpack nibbles in
 // registers straight into the A fragments of warp-level f16 MMAs (16 rows x 16 k x 8 tokens) -- the weights never
 // go back to shared memory. Codes enter the MMA exactly as (1024 + code) f16 values (high nibbles as 1024 + 16 code);
@@ -25,8 +25,9 @@ constexpr int kMvRows = 16;
 constexpr int kMvStageChunks = 4;                               // 256-value chunks per stage, one per consumer
 // ring depth: 4 stages, or 2 when a stage is large (two weights and 8 f32 tokens) so the CTA fits shared memory
 constexpr int mv_stages(int stage_bytes) { return 4 * stage_bytes <= 150 * 1024 ? 4 : 2; }
-constexpr int kMvRowStageBytes = kMvStageChunks * kChunkBytes;  // 576
-constexpr int kMvWBytes = kMvRows * kMvRowStageBytes;           // 9216: one weight's box per stage
+constexpr int kMvChunkTile = kMvRows * kChunkBytes;             // 2304: 16 rows x 144 bytes (one TMA box)
+constexpr int kMvWBytes = kMvStageChunks * kMvChunkTile;        // 9216: one weight's 4 chunk tiles per stage
+constexpr int kAcStride = 10;                                   // float2 stride of a row of the (a, c') table
 constexpr int kXStride = 272;                                   // f16 row stride of a consumer's x tile
 
 LK_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -59,12 +60,22 @@ LK_DEV uint32_t lds_u16x2(const uint8_t* p) {   // 2-byte aligned 4 bytes
   return uint32_t(q[0]) | (uint32_t(q[1]) << 16);
 }
 
+// acc += a * D - c' * S for the lane's D elements: rows g, g+8 x tokens 2tig, 2tig+1. With one token only the
+// token-0 column carries data (elements 0 and 2).
+template <int TOK>
 LK_DEV void group_epilogue(float (&acc)[4], const float (&d)[4], float2 s01, float a_g, float c_g, float a_g8,
                            float c_g8) {
   acc[0] = fmaf(a_g, d[0], fmaf(-c_g, s01.x, acc[0]));
-  acc[1] = fmaf(a_g, d[1], fmaf(-c_g, s01.y, acc[1]));
   acc[2] = fmaf(a_g8, d[2], fmaf(-c_g8, s01.x, acc[2]));
-  acc[3] = fmaf(a_g8, d[3], fmaf(-c_g8, s01.y, acc[3]));
+  if (TOK > 1) {
+    acc[1] = fmaf(a_g, d[1], fmaf(-c_g, s01.y, acc[1]));
+    acc[3] = fmaf(a_g8, d[3], fmaf(-c_g8, s01.y, acc[3]));
+  }
+}
+
+// 4 bytes (values 0..255) of w -> f32, without a conversion instruction
+LK_DEV float byte_f32(uint32_t w, uint32_t sel) {
+  return __uint_as_float(prmt(w, 0x4B000000u, sel)) - 8388608.0f;
 }
 
 // B fragment (token g, 4 consecutive k) from a consumer's f16 x tile; zero for lanes past the token count
@@ -125,30 +136,37 @@ LK_DEV void stage_x(const uint8_t* xraw, int xraw_stride, int ntok, int lane, __
   }
 }
 
-// One 256-value chunk of 16 rows (row r at rb + r*576) against the staged x tile.
-template <int FMT, int XT, int NW>
+// One 256-value chunk of 16 rows (row r at rb + r*144, one TMA box) against the staged x tile.
+template <int FMT, int XT, int NW, int TOK>
 LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, const __half* xl, const float* S,
                      bool xvalid, int g, int tig, int lane, float2* actab, float (&acc)[NW][4]) {
-  constexpr int RS = kMvRowStageBytes;
-  // S for tokens 2tig, 2tig+1 of group j
-  auto sums = [&](int j) { return make_float2(S[(2 * tig) * 8 + j], S[(2 * tig + 1) * 8 + j]); };
+  constexpr int RS = kChunkBytes;
+  // S for tokens 2tig, 2tig+1 of group j (with one token, token 0's for every lane)
+  auto sums = [&](int j) {
+    return TOK == 1 ? make_float2(S[j], 0.f) : make_float2(S[(2 * tig) * 8 + j], S[(2 * tig + 1) * 8 + j]);
+  };
   if (FMT == LK_Q4_K) {
-    // cooperative header decode: lane -> (row lane/2, groups 4*(lane&1) .. +3); low-nibble groups (even j) hold
-    // (a, 1024 a + c), high-nibble groups (odd j, codes seen as 16 q) hold (a / 16, 64 a + c)
+    // cooperative header decode: lane -> (row lane/2, groups 4*(lane&1) .. +3), four groups at a time with byte-wise
+    // bit operations. Low-nibble groups (even j) hold (a, 1024 a + c); high-nibble groups (odd j, whose codes the
+    // MMA sees as 16 q) hold (a / 16, 64 a + c).
 #pragma unroll
     for (int wi = 0; wi < NW; ++wi) {
       const uint8_t* rb = wi ? rb1 : rb0;
-      int r = lane >> 1, j0 = (lane & 1) * 4;
+      const int r = lane >> 1, hh = lane & 1;
       uint4 hv = *reinterpret_cast<const uint4*>(rb + r * RS);
       float d = h2f(uint16_t(hv.x & 0xffff)), dmin = h2f(uint16_t(hv.x >> 16));
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        uint32_t sc, m;
-        q4k_scale_min_w(hv.y, hv.z, hv.w, j0 + jj, sc, m);
-        float a = d * float(int(sc)), c = dmin * float(int(m));
-        float2 v = (jj & 1) ? make_float2(a * 0.0625f, fmaf(64.0f, a, c)) : make_float2(a, fmaf(1024.0f, a, c));
-        actab[wi * 128 + r * 8 + j0 + jj] = v;
-      }
+      uint32_t sc4 = hh ? ((hv.w & 0x0F0F0F0Fu) | ((hv.y >> 2) & 0x30303030u)) : (hv.y & 0x3F3F3F3Fu);
+      uint32_t m4 = hh ? (((hv.w >> 4) & 0x0F0F0F0Fu) | ((hv.z >> 2) & 0x30303030u)) : (hv.z & 0x3F3F3F3Fu);
+      float4 lo, hi;
+      float a0 = d * byte_f32(sc4, 0x7650u), a1 = d * byte_f32(sc4, 0x7651u);
+      float a2 = d * byte_f32(sc4, 0x7652u), a3 = d * byte_f32(sc4, 0x7653u);
+      lo = make_float4(a0, fmaf(1024.0f, a0, dmin * byte_f32(m4, 0x7650u)), a1 * 0.0625f,
+                       fmaf(64.0f, a1, dmin * byte_f32(m4, 0x7651u)));
+      hi = make_float4(a2, fmaf(1024.0f, a2, dmin * byte_f32(m4, 0x7652u)), a3 * 0.0625f,
+                       fmaf(64.0f, a3, dmin * byte_f32(m4, 0x7653u)));
+      float4* dst = reinterpret_cast<float4*>(actab + wi * 16 * kAcStride + r * kAcStride + 4 * hh);
+      dst[0] = lo;
+      dst[1] = hi;
     }
     __syncwarp();
 #pragma unroll
@@ -187,10 +205,10 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
       float2 sl = sums(2 * p), sh = sums(2 * p + 1);
 #pragma unroll
       for (int wi = 0; wi < NW; ++wi) {
-        float4 r0 = *reinterpret_cast<const float4*>(&actab[wi * 128 + g * 8 + 2 * p]);
-        float4 r8 = *reinterpret_cast<const float4*>(&actab[wi * 128 + (g + 8) * 8 + 2 * p]);
-        group_epilogue(acc[wi], dl[wi], sl, r0.x, r0.y, r8.x, r8.y);
-        group_epilogue(acc[wi], dh[wi], sh, r0.z, r0.w, r8.z, r8.w);
+        float4 r0 = *reinterpret_cast<const float4*>(&actab[wi * 16 * kAcStride + g * kAcStride + 2 * p]);
+        float4 r8 = *reinterpret_cast<const float4*>(&actab[wi * 16 * kAcStride + (g + 8) * kAcStride + 2 * p]);
+        group_epilogue<TOK>(acc[wi], dl[wi], sl, r0.x, r0.y, r8.x, r8.y);
+        group_epilogue<TOK>(acc[wi], dh[wi], sh, r0.z, r0.w, r8.z, r8.w);
       }
     }
     __syncwarp();   // the table is rewritten by the next chunk
@@ -233,7 +251,7 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
         code_frag(u8, f8, s8);
         mma16816(dd, f0, f8, s0, s8, b10, b11);
         if (XT == LK_F32) mma16816(dd, f0, f8, s0, s8, l10, l11);
-        group_epilogue(acc[wi], dd, s, d0, kOff * d0, d8, kOff * d8);
+        group_epilogue<TOK>(acc[wi], dd, s, d0, kOff * d0, d8, kOff * d8);
       }
     }
   }
@@ -252,8 +270,8 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kMvStages * kStageBytes);
   uint64_t* empty = full + kMvStages;
-  float2* actab_all = reinterpret_cast<float2*>(empty + kMvStages);                 // [consumers][NW][16][8]
-  float* red = reinterpret_cast<float*>(actab_all + kMvConsumers * NW * 128);       // [consumers][NW][32][4]
+  float2* actab_all = reinterpret_cast<float2*>(empty + kMvStages);    // [consumers][NW][16][kAcStride]
+  float* red = reinterpret_cast<float*>(actab_all + kMvConsumers * NW * 16 * kAcStride);   // [consumers][NW][32][4]
   float* S_all = red + kMvConsumers * NW * 32 * 4;                                  // [consumers][TOK][8]
   __half* xt_all = reinterpret_cast<__half*>(S_all + kMvConsumers * TOK * 8);       // [consumers][kXT]
 
@@ -296,11 +314,16 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
         int s = st % kMvStages;
         if (st >= kMvStages && !mbar_wait(&empty[s], ((st / kMvStages) - 1) & 1)) atomicOr(&g_status, 1u);
         int c0 = st * kMvStageChunks;
-        uint32_t xbytes = uint32_t(min(kMvStageChunks, kchunks - c0)) * 256u * XE;
-        mbar_expect_tx(&full[s], uint32_t(NW * kMvWBytes) + xbytes * ntok);
+        int nch = min(kMvStageChunks, kchunks - c0);
+        uint32_t xbytes = uint32_t(nch) * 256u * XE;
+        mbar_expect_tx(&full[s], uint32_t(NW * nch * kMvChunkTile) + xbytes * ntok);
         uint8_t* stg = ring + s * kStageBytes;
-        tma_load_2d(stg, &wmap, c0 * (kChunkBytes / 4), wrow, &full[s]);
-        if (NW == 2) tma_load_2d(stg + kMvWBytes, &w2map, c0 * (kChunkBytes / 4), w2row, &full[s]);
+        // one box per chunk: a [16 rows][144 bytes] tile, whose 36-word row stride spreads the rows over the banks
+        for (int c = 0; c < nch; ++c) {
+          tma_load_2d(stg + c * kMvChunkTile, &wmap, (c0 + c) * (kChunkBytes / 4), wrow, &full[s]);
+          if (NW == 2)
+            tma_load_2d(stg + kMvWBytes + c * kMvChunkTile, &w2map, (c0 + c) * (kChunkBytes / 4), w2row, &full[s]);
+        }
         for (int t = 0; t < ntok; ++t)
           bulk_g2s(stg + NW * kMvWBytes + t * (kMvStageChunks * 256 * XE), xbase + (int64_t(t) * a.k + c0 * 256) * XE,
                    xbytes, &full[s]);
@@ -317,7 +340,7 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[wi][i] = 0.f;
   const bool xvalid = g < ntok;
-  float2* actab = actab_all + warp * NW * 128;
+  float2* actab = actab_all + warp * NW * 16 * kAcStride;
   float* S = S_all + warp * TOK * 8;
   __half* xt = xt_all + warp * kXT;
   __half* xl = xt + TOK * kXStride;
@@ -329,8 +352,8 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
       const uint8_t* stg = ring + s * kStageBytes;
       stage_x<XT, TOK>(stg + NW * kMvWBytes + warp * 256 * XE, kMvStageChunks * 256 * XE, ntok, lane, xt, xl, S);
       __syncwarp();
-      const uint8_t* rb0 = stg + warp * kChunkBytes;
-      mv_chunk<FMT, XT, NW>(rb0, rb0 + kMvWBytes, xt, xl, S, xvalid, g, tig, lane, actab, acc);
+      const uint8_t* rb0 = stg + warp * kMvChunkTile;
+      mv_chunk<FMT, XT, NW, TOK>(rb0, rb0 + kMvWBytes, xt, xl, S, xvalid, g, tig, lane, actab, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -375,7 +398,7 @@ static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs
   constexpr int kXT = (XT == LK_F32 ? 2 : 1) * TOK * kXStride;
   constexpr int kMvStages = mv_stages(kStageBytes);
   static_assert(kMvStages * kStageBytes + 64 * 1024 <= 227 * 1024, "matvec CTA exceeds shared memory");
-  constexpr int smem = kMvStages * kStageBytes + 2 * kMvStages * 8 + kMvConsumers * NW * 128 * 8 +
+  constexpr int smem = kMvStages * kStageBytes + 2 * kMvStages * 8 + kMvConsumers * NW * 16 * kAcStride * 8 +
                        kMvConsumers * NW * 32 * 4 * 4 + kMvConsumers * TOK * 8 * 4 + kMvConsumers * kXT * 2;
   auto kern = k_mv<FMT, XT, SWIGLU, MOE, TOK>;
   static unsigned configured = 0;
@@ -414,10 +437,10 @@ int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s) {
   int64_t rows = a.ids ? int64_t(a.n_experts) * a.rows_per_expert : a.n;
   int64_t rows2 = a.ids ? int64_t(a.n_experts) * a.rows_per_expert2 : a.n;
   CUtensorMap wm, w2m;
-  int rc = make_map(&wm, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows, a.row_bytes / 4, kMvRowStageBytes / 4, kMvRows,
+  int rc = make_map(&wm, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows, a.row_bytes / 4, kChunkBytes / 4, kMvRows,
                     CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc == LK_OK)
-    rc = a.w2 ? make_map(&w2m, a.w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows2, a.row_bytes / 4, kMvRowStageBytes / 4,
+    rc = a.w2 ? make_map(&w2m, a.w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, rows2, a.row_bytes / 4, kChunkBytes / 4,
                          kMvRows, CU_TENSOR_MAP_SWIZZLE_NONE)
               : (w2m = wm, LK_OK);
   if (rc != LK_OK) return rc;

@@ -1,15 +1,398 @@
-// MXFP4 (split planes) x FP8 prefill GEMM on tcgen05 -- replaces g_gemm_mxfp4s_{store,swiglu}_f8_m256_rdna4
-// (gen_mxfp4s.py:50-500).
+// MXFP4 (split planes) weight x FP8 (e4m3) activation GEMM on the 5th-generation tensor cores with native block
+// scaling: tcgen05.mma kind::mxf8f6f4.block_scale, e4m3 A, e2m1 B, one E8M0 scale per 32 k of every row.
+//
+// Replaces g_gemm_mxfp4s_{store,swiglu}[_pair]_f8_m256_rdna4 (gen_mxfp4s.py:50-500, launch signature gen_mxfp4s.py:101)
+// and, grouped over the MoE tile schedule, the expert GEMMs of an MXFP4 MoE (gen_moe.py:1126-1228 layout).
+//   y = (x8 . (W * 2^8)^T) * s8[row][1]   (the reference holds W at 2^8 times its value; s8[row][1] carries 2^-8)
+// The reference decodes every nibble to an e5m2 byte and is exact only for block exponents 107..132
+// (gen_mxfp4s.py:14-27); here the tensor core applies the block scales itself, exact for every E8M0 value.
+//
+// One CTA computes a 128-row x 256-column tile (swiglu: 128 columns of gate and of up), K in steps of 128:
+//   warp 0      producer: A (x8) tiles by 2-D TMA with 128-byte swizzle (MoE gate/up: TMA gather4 of token rows), the
+//               packed nibble rows (64 bytes per row per step) by 2-D TMA; out-of-range k is zero-filled by TMA
+//   warp 1      allocates TMEM; copies scale factors into TMEM (tcgen05.cp 32x128b.warpx4) and issues the MMAs
+//   warps 2-9   expand each packed row into the operand layout the MMA reads e2m1 from (16 values in the first 8 of
+//               every 16 bytes, 128-byte swizzle; split16 blocks reordered to pairs), stage the row's four E8M0
+//               bytes in the scale-factor atom (row 32j+i at byte 16i+4j), then run the epilogue.
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
 namespace lk {
 
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
+             int box_cols, int box_rows, CUtensorMapSwizzle swz);
+
+namespace {
+
+constexpr int kBM = 128, kBK = 128;               // tile rows, k per stage (bytes of e4m3 A per row)
+constexpr int kSA = 4, kSP = 3, kSB = 2;
+constexpr int kXWarps = 8;
+constexpr int kThreads = (2 + kXWarps) * 32;
+constexpr int kRowsB = 256;                       // weight rows per tile (x NW weights)
+constexpr int kABytes = kBM * kBK;                // 16 KB
+constexpr int kPBytes = kRowsB * (kBK / 2);       // 16 KB of packed nibbles
+constexpr int kBBytes = kRowsB * kBK;             // 32 KB expanded operand
+constexpr int kSFBytes = kRowsB * 4;              // 1 KB: two 512-byte scale-factor atoms
+constexpr uint32_t kColSFA = 256, kColSFB = 264;  // TMEM columns: accumulators 0..255, SFA 4, SFB 8 per stage
+enum { kDense = 0, kGather = 1, kSorted = 2 };
+
+struct MxArgs {
+  const float* s8;              // [rows or xrows][2]
+  float* y;                     // [rows][n]
+  const uint8_t* ws;            // E8M0 plane of w  [rows of wmap][k/32]
+  const uint8_t* ws2;           // E8M0 plane of w2 (or ws when fused)
+  int rows, k, n;
+  int sf_stride;                // bytes per scale row (k/32)
+  int rows_per_expert, rows_per_expert2, w2_row_offset;
+  const int32_t* tile_info;
+  const int32_t* rowmap;
+  int max_tiles, xrows, ku, n_experts;
+};
+
+// split16 block bytes (element i low nibble of byte i, element i+16 high nibble) -> pairs order (element 2j low,
+// 2j+1 high nibble of byte j), for one 32-value block held in 4 words
+LK_DEV void split16_to_pairs(uint32_t (&w)[4]) {
+  uint32_t e0 = prmt(w[0], w[1], 0x6420u), o0 = prmt(w[0], w[1], 0x7531u);   // even / odd bytes 0..7
+  uint32_t e1 = prmt(w[2], w[3], 0x6420u), o1 = prmt(w[2], w[3], 0x7531u);   // even / odd bytes 8..15
+  uint32_t lo0 = (e0 & 0x0F0F0F0Fu) | ((o0 & 0x0F0F0F0Fu) << 4), lo1 = (e1 & 0x0F0F0F0Fu) | ((o1 & 0x0F0F0F0Fu) << 4);
+  uint32_t hi0 = ((e0 >> 4) & 0x0F0F0F0Fu) | (o0 & 0xF0F0F0F0u), hi1 = ((e1 >> 4) & 0x0F0F0F0Fu) | (o1 & 0xF0F0F0F0u);
+  w[0] = lo0;
+  w[1] = lo1;
+  w[2] = hi0;
+  w[3] = hi1;
+}
+
+template <int NW, int GROUP, int ORDER>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_mx(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+              const __grid_constant__ CUtensorMap w2map, const MxArgs p) {
+  constexpr int BN = kRowsB / NW;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kSA * kABytes;
+  uint8_t* sP = sB + kSB * kBBytes;
+  uint8_t* sSF = sP + kSP * kPBytes;          // [kSB][1024]
+  uint8_t* sSFA = sSF + kSB * kSFBytes;       // 512 bytes of 127 (2^0): the activations' block scales
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(sSFA + 512);
+  uint64_t* empty_a = full_a + kSA;
+  uint64_t* full_p = empty_a + kSA;
+  uint64_t* empty_p = full_p + kSP;
+  uint64_t* full_b = empty_p + kSP;
+  uint64_t* empty_b = full_b + kSB;
+  uint64_t* acc_full = empty_b + kSB;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  int* tile_meta = reinterpret_cast<int*>(tmem_slot + 4);
+  int* arow = tile_meta + 4;   // [128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int kstages = (p.k + kBK - 1) / kBK;
+  const int kblocks = p.k / 32;
+  int m0 = blockIdx.y * kBM;
+  int valid_rows = min(kBM, p.rows - m0);
+  int expert = 0;
+  if (GROUP != kDense) {
+    if (threadIdx.x == 0) {
+      int s = 0, found = -1, first = 0, nrows = 0;
+      for (int t = 0; t < p.max_tiles;) {
+        int e = p.tile_info[2 * t];
+        if (e < 0) break;
+        bool pair = t + 1 < p.max_tiles && p.tile_info[2 * (t + 1)] == e;
+        if (s == int(blockIdx.y)) {
+          found = e;
+          first = t;
+          nrows = pair ? 64 + p.tile_info[2 * (t + 1) + 1] : p.tile_info[2 * t + 1];
+          break;
+        }
+        ++s;
+        t += pair ? 2 : 1;
+      }
+      tile_meta[0] = found;
+      tile_meta[1] = first;
+      tile_meta[2] = nrows;
+    }
+    __syncthreads();
+    if (tile_meta[0] < 0) return;
+    expert = min(tile_meta[0], p.n_experts - 1);
+    m0 = tile_meta[1] * 64;
+    valid_rows = tile_meta[2];
+    if (GROUP == kGather && threadIdx.x < kBM) {
+      int r = threadIdx.x;
+      int a = r < valid_rows ? p.rowmap[m0 + r] : -1;
+      arow[r] = a >= 0 ? a / p.ku : p.xrows;
+    }
+  }
+  const int wrow = expert * p.rows_per_expert + n0;
+  const int w2row = expert * p.rows_per_expert2 + p.w2_row_offset + n0;
+  const int nb_rows = min(BN, p.n - n0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSA; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < kSP; ++i) {
+      mbar_init(&full_p[i], 1);
+      mbar_init(&empty_p[i], kXWarps);
+    }
+    for (int i = 0; i < kSB; ++i) {
+      mbar_init(&full_b[i], kXWarps);
+      mbar_init(&empty_b[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + 128) reinterpret_cast<uint32_t*>(sSFA)[threadIdx.x - 64] = 0x7F7F7F7Fu;
+  fence_proxy_async();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+    }
+    for (int ks = 0; ks < kstages; ++ks) {
+      int sp = ks % kSP, sa = ks % kSA;
+      if (ks >= kSP && !mbar_wait(&empty_p[sp], ((ks / kSP) - 1) & 1)) atomicOr(&g_status, 1u);
+      if (lane == 0) {
+        mbar_expect_tx(&full_p[sp], uint32_t(kPBytes));
+        tma_load_2d(sP + sp * kPBytes, &wmap, ks * (kBK / 2), wrow, &full_p[sp]);
+        if (NW == 2) tma_load_2d(sP + sp * kPBytes + BN * (kBK / 2), &w2map, ks * (kBK / 2), w2row, &full_p[sp]);
+      }
+      if (ks >= kSA && !mbar_wait(&empty_a[sa], ((ks / kSA) - 1) & 1)) atomicOr(&g_status, 1u);
+      if (GROUP == kGather) {
+        if (lane == 0) mbar_expect_tx(&full_a[sa], kABytes);
+        __syncwarp();
+        int r = lane * 4;
+        tma_gather4(sA + sa * kABytes + r * 128, &amap, ks * kBK, arow[r], arow[r + 1], arow[r + 2], arow[r + 3],
+                    &full_a[sa]);
+      } else if (lane == 0) {
+        mbar_expect_tx(&full_a[sa], kABytes);
+        tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ scale-factor copies + MMA issue
+    const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+    if (lane == 0) tmem_cp_32x128_x4(tmem + kColSFA, sdesc_rows16(smem_u32(sSFA)));
+    for (int ks = 0; ks < kstages; ++ks) {
+      int sa = ks % kSA, sb = ks % kSB;
+      if (!mbar_wait(&full_a[sa], (ks / kSA) & 1)) atomicOr(&g_status, 1u);
+      if (!mbar_wait(&full_b[sb], (ks / kSB) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t sfb = tmem + kColSFB + 8 * sb;
+        tmem_cp_32x128_x4(sfb, sdesc_rows16(smem_u32(sSF + sb * kSFBytes)));
+        tmem_cp_32x128_x4(sfb + 4, sdesc_rows16(smem_u32(sSF + sb * kSFBytes + 512)));
+#pragma unroll
+        for (int s = 0; s < kBK / 32; ++s) {
+          uint64_t ad = sdesc_k128(a_base + sa * kABytes + s * 32);
+#pragma unroll
+          for (int wi = 0; wi < NW; ++wi) {
+            uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + s * 32);
+            uint32_t idesc = idesc_mx(kBM, BN, 0, 5, s, s);
+            umma_mx(tmem + wi * BN, ad, bd, idesc, (tmem + kColSFA) | (uint32_t(s) << 30),
+                    (sfb + 4 * wi) | (uint32_t(s) << 30), (ks | s) != 0);
+          }
+        }
+        umma_commit(&empty_a[sa]);
+        umma_commit(&empty_b[sb]);
+        if (ks == kstages - 1) umma_commit(acc_full);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ operand expansion + scales, then epilogue
+    const int r = threadIdx.x - 64;   // tile weight row 0..255
+    const int wi = r / BN, rr = r % BN;
+    const bool row_ok = n0 + rr < p.n;
+    const uint8_t* sfrow = (wi ? p.ws2 : p.ws) + int64_t((wi ? w2row : wrow) + rr) * p.sf_stride;
+    // block visiting order: q ^ perm[(r >> 1) & 3] with perm = {0, 2, 3, 1} (x -> alpha.x in GF(4)); both the
+    // 64-byte-strided row reads and the swizzled chunk writes of 8 consecutive rows then hit 8 distinct bank groups
+    const int qperm = (0x1320 >> (4 * ((r >> 1) & 3))) & 3;
+    auto load_sf = [&](int ks) -> uint32_t {
+      uint32_t v = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int b = ks * 4 + i;
+        uint32_t e = (row_ok && b < kblocks) ? uint32_t(__ldg(sfrow + b)) : 0x7Fu;
+        v |= e << (8 * i);
+      }
+      return v;
+    };
+    uint32_t sfv = load_sf(0);
+    for (int ks = 0; ks < kstages; ++ks) {
+      int sp = ks % kSP, sb = ks % kSB;
+      if (!mbar_wait(&full_p[sp], (ks / kSP) & 1)) atomicOr(&g_status, 1u);
+      if (ks >= kSB && !mbar_wait(&empty_b[sb], ((ks / kSB) - 1) & 1)) atomicOr(&g_status, 1u);
+      const uint4* prow = reinterpret_cast<const uint4*>(sP + sp * kPBytes + r * (kBK / 2));
+      uint8_t* bt = sB + sb * kBBytes;
+#pragma unroll
+      for (int qi = 0; qi < 4; ++qi) {   // 16 packed bytes = one 32-value block = two 16-value chunks
+        const int q = qi ^ qperm;
+        uint4 v = prow[q];
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        if (ORDER == LK_ORDER_SPLIT16) split16_to_pairs(w);
+        *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q)) = make_uint4(w[0], w[1], 0u, 0u);
+        *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q + 1)) = make_uint4(w[2], w[3], 0u, 0u);
+      }
+      // scale-factor atom: row 32j + i of a 128-row half at byte 16i + 4j, the four k blocks in its four bytes
+      *reinterpret_cast<uint32_t*>(sSF + sb * kSFBytes + (r >> 7) * 512 + 16 * (r & 31) + 4 * ((r & 127) >> 5)) = sfv;
+      if (ks + 1 < kstages) sfv = load_sf(ks + 1);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&full_b[sb]);
+        mbar_arrive(&empty_p[sp]);
+      }
+    }
+    // epilogue: quadrant q = TMEM lanes 32q..; the two warps of a quadrant split the columns
+    if (!mbar_wait(acc_full, 0)) atomicOr(&g_status, 1u);
+    tc_fence_after();
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = 32 * q + lane;
+    const bool ok = row < valid_rows;
+    float inv = 0.f;
+    float* yrow = nullptr;
+    if (ok) {
+      int grow = m0 + row;
+      int srow = grow;
+      if (GROUP == kGather) {
+        int a = p.rowmap[grow];
+        srow = a >= 0 ? a / p.ku : -1;
+      }
+      inv = srow >= 0 ? p.s8[2 * int64_t(srow) + 1] * 256.0f : 0.f;   // 2^8: the reference's weight pre-scale
+      yrow = p.y + int64_t(grow) * p.n + n0;
+    }
+    constexpr int kCols = BN / 2;
+    const uint32_t tbase = tmem + (uint32_t(32 * q) << 16);
+#pragma unroll 1
+    for (int cb = 0; cb < kCols; cb += 32) {
+      int col = half * kCols + cb;
+      float v[32];
+      tmem_ld32(tbase + col, v);
+      if (NW == 2) {
+        float u[32];
+        tmem_ld32(tbase + BN + col, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= inv;
+      }
+      if (ok) {
+        if ((p.n & 3) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            if (col + i < nb_rows)
+              *reinterpret_cast<float4*>(yrow + col + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col + i < nb_rows) yrow[col + i] = v[i];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int NW, int GROUP, int ORDER>
+int launch(const CUtensorMap& am, const CUtensorMap& wm, const CUtensorMap& w2m, const MxArgs& a, dim3 grid,
+           cudaStream_t s) {
+  constexpr int smem = 1024 + kSA * kABytes + kSB * kBBytes + kSP * kPBytes + kSB * kSFBytes + 512 + 256 + 32 + 512;
+  static_assert(smem <= 227 * 1024, "MXFP4 GEMM CTA exceeds shared memory");
+  auto kern = k_gemm_mx<NW, GROUP, ORDER>;
+  static unsigned configured = 0;
+  if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  kern<<<grid, kThreads, smem, s>>>(am, wm, w2m, a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+template <int NW, int GROUP>
+int launch_o(int order, const CUtensorMap& am, const CUtensorMap& wm, const CUtensorMap& w2m, const MxArgs& a,
+             dim3 grid, cudaStream_t s) {
+  if (order == LK_ORDER_SPLIT16) return launch<NW, GROUP, LK_ORDER_SPLIT16>(am, wm, w2m, a, grid, s);
+  return launch<NW, GROUP, LK_ORDER_PAIRS>(am, wm, w2m, a, grid, s);
+}
+
+}  // namespace
+
+// dense (tile_info == nullptr) or grouped over the MoE schedule
+int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+            const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
+            const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
+            int w2_row_offset) {
+  const int NW = mode == LK_SWIGLU ? 2 : 1;
+  const int bn = kRowsB / NW;
+  MxArgs a{};
+  a.s8 = s8;
+  a.y = y;
+  a.rows = rows;
+  a.k = k;
+  a.n = n;
+  a.sf_stride = k / 32;
+  a.ws = ws;
+  a.ws2 = w2s ? w2s : ws;
+  int group = kDense;
+  int64_t wrows = n, w2rows = n;
+  a.rows_per_expert = a.rows_per_expert2 = 0;
+  a.w2_row_offset = (NW == 2 && !w2) ? w2_row_offset : 0;
+  if (tile_info) {
+    group = mode == LK_SWIGLU ? kGather : kSorted;
+    a.tile_info = tile_info;
+    a.rowmap = rowmap;
+    a.max_tiles = rows / 64;
+    a.xrows = xrows;
+    a.ku = ku;
+    a.n_experts = n_experts;
+    a.rows_per_expert = rows_per_expert;
+    a.rows_per_expert2 = w2 ? n : rows_per_expert;
+    wrows = int64_t(n_experts) * rows_per_expert;
+    w2rows = int64_t(n_experts) * a.rows_per_expert2;
+  }
+  CUtensorMap am, wm, w2m;
+  int rc = group == kGather ? make_map(&am, x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xrows, k, kBK, 1,
+                                       CU_TENSOR_MAP_SWIZZLE_128B)
+                            : make_map(&am, x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, k, kBK, kBM,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == LK_OK)
+    rc = make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, wrows, k / 2, kBK / 2, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == LK_OK)
+    rc = w2 ? make_map(&w2m, w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w2rows, k / 2, kBK / 2, bn,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)
+            : (w2m = wm, LK_OK);
+  if (rc != LK_OK) return rc;
+  dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + kBM - 1) / kBM : rows / 64);
+  if (NW == 2) {
+    if (group == kGather) return launch_o<2, kGather>(order, am, wm, w2m, a, grid, s);
+    return launch_o<2, kDense>(order, am, wm, w2m, a, grid, s);
+  }
+  if (group == kSorted) return launch_o<1, kSorted>(order, am, wm, w2m, a, grid, s);
+  return launch_o<1, kDense>(order, am, wm, w2m, a, grid, s);
+}
+
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s) {
-  (void)mode; (void)order; (void)rows; (void)k; (void)n; (void)x8; (void)s8; (void)w; (void)ws; (void)w2; (void)w2s;
-  (void)y; (void)s;
-  return LK_EUNSUPPORTED;
+  return gemm_mx(mode, order, rows, k, n, x8, s8, w, ws, w2, w2s, y, s, nullptr, nullptr, rows, 1, 1, 0, 0);
 }
+
+LK_STATUS_READER(status_mx)
 
 }  // namespace lk

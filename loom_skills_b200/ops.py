@@ -174,6 +174,23 @@ def moe_grouped_gemm(fmt, mode, tile_info, rowmap, x16, scales, w, n, ku, n_expe
     return y
 
 
+def moe_grouped_gemm_mxfp4s_f8(mode, tile_info, rowmap, x8, s8, w, ws, n, ku, n_experts, fused=False, w2=None,
+                               w2s=None, order=L.ORDER_PAIRS, y=None):
+    """MXFP4 x e4m3 grouped expert GEMM over the bucketed 64-row tiles; operands as gemm_mxfp4s_f8, rows and tiles
+    as moe_grouped_gemm (gate/up: x8/s8 are token rows; down: sorted rows)."""
+    _cuda(tile_info, rowmap, x8, s8, w, ws, w2, w2s, y)
+    rows = rowmap.shape[0]
+    xrows, k = x8.shape
+    if y is None:
+        y = torch.empty(rows, n, dtype=torch.float32, device=x8.device)
+    m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
+    L.check(L.load().lk_moe_grouped_gemm_mxfp4s_f8(m, order, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
+                                                   _ptr(tile_info), _ptr(rowmap), _ptr(x8), _ptr(s8), _ptr(w),
+                                                   _ptr(ws), _ptr(w2), _ptr(w2s), _ptr(y), _stream()),
+            "lk_moe_grouped_gemm_mxfp4s_f8")
+    return y
+
+
 def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False):
     _cuda(ys, pos, wts, y)
     tokens, ku = wts.shape
