@@ -169,7 +169,8 @@ int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, in
                         const void* w, const void* w2, float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
-  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
+    return LK_EINVAL;
   if (!tile_info || !rowmap || !x16 || !scales || !w || !y) return LK_EINVAL;
   if (mode == LK_SWIGLU && !fused && !w2) return LK_EINVAL;
   if (k % 256 || n % 16) return LK_EINVAL;
@@ -203,7 +204,8 @@ int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, i
                                   const uint8_t* w2s, float* y, lk_stream_t stream) {
   if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
-  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
+    return LK_EINVAL;
   if (k % 32 || n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
   if (!tile_info || !rowmap || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;

@@ -281,4 +281,67 @@ inline bool once_per_device(unsigned& mask) {
 
 LK_DEV float silu(float g) { return g / (1.0f + __expf(-g)); }
 
+// ---------------------------------------------------------------------------------------------------------------
+// MoE schedule: 128-row super-tiles over the bucket's 64-row tiles
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kMaxExperts = 256;
+// Super-tile `s` of a tile schedule laid out as the bucket writes it (the tiles of each expert contiguous, experts
+// ascending, unused tiles (-1, 0)): consecutive tiles of one expert are paired from the start of its run, so expert e
+// owns ceil(tiles_e / 2) super-tiles. Called by every thread of the CTA; `scratch` is 3 * kMaxExperts ints of shared
+// memory that nothing else uses yet (the async proxy may write it afterwards). meta[0] = expert (-1: the schedule has
+// fewer super-tiles than s + 1), meta[1] = first tile, meta[2] = valid rows (64 + rows of the second tile if paired).
+LK_DEV void moe_super_tile(const int32_t* tile_info, int max_tiles, int n_experts, int s, int* scratch, int* meta) {
+  int* start = scratch;
+  int* count = scratch + kMaxExperts;
+  int* base = scratch + 2 * kMaxExperts;
+  for (int e = threadIdx.x; e < kMaxExperts; e += blockDim.x) {
+    start[e] = 0x7FFFFFFF;
+    count[e] = 0;
+  }
+  if (threadIdx.x == 0) meta[0] = -1;
+  __syncthreads();
+  for (int t = threadIdx.x; t < max_tiles; t += blockDim.x) {
+    int e = __ldg(tile_info + 2 * t);
+    if (e >= 0 && e < n_experts) {
+      atomicMin(&start[e], t);
+      atomicAdd(&count[e], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {   // exclusive scan of ceil(count / 2), 8 experts per lane
+    const int lane = threadIdx.x;
+    int v[kMaxExperts / 32], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      v[i] = (count[lane * (kMaxExperts / 32) + i] + 1) >> 1;
+      sum += v[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      base[lane * (kMaxExperts / 32) + i] = run;
+      run += v[i];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+    const int ns = (count[e] + 1) >> 1;
+    if (s >= base[e] && s < base[e] + ns) {
+      const int first = start[e] + 2 * (s - base[e]);
+      const bool pair = first + 1 < start[e] + count[e];
+      meta[0] = e;
+      meta[1] = first;
+      meta[2] = pair ? 64 + __ldg(tile_info + 2 * (first + 1) + 1) : __ldg(tile_info + 2 * first + 1);
+    }
+  }
+  fence_proxy_async();
+  __syncthreads();
+}
+
 }  // namespace lk

@@ -177,28 +177,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int valid_rows = min(kTM, p.rows - m0);
   int wrow = n0, w2row = n0 + p.w2_row_offset;   // first weight row of this tile in wmap / w2map
   if (GROUP != kDense) {
-    if (threadIdx.x == 0) {
-      // super-tile s = blockIdx.y: walk tile_info (experts in order), pairing consecutive tiles of one expert
-      int s = 0, found = -1, first = 0, nrows = 0;
-      for (int t = 0; t < p.max_tiles;) {
-        int e = p.tile_info[2 * t];
-        if (e < 0) break;
-        int rows0 = p.tile_info[2 * t + 1];
-        bool pair = t + 1 < p.max_tiles && p.tile_info[2 * (t + 1)] == e;
-        if (s == int(blockIdx.y)) {
-          found = e;
-          first = t;
-          nrows = pair ? 64 + p.tile_info[2 * (t + 1) + 1] : rows0;
-          break;
-        }
-        ++s;
-        t += pair ? 2 : 1;
-      }
-      tile_meta[0] = found;
-      tile_meta[1] = first;
-      tile_meta[2] = nrows;
-    }
-    __syncthreads();
+    // super-tile s = blockIdx.y (the A ring is free scratch until the first TMA load)
+    moe_super_tile(p.tile_info, p.max_tiles, p.n_experts, blockIdx.y, reinterpret_cast<int*>(sA), tile_meta);
     if (tile_meta[0] < 0) return;   // no such super-tile: this launch had more CTAs than the schedule needs
     int e = min(tile_meta[0], p.n_experts - 1);
     m0 = tile_meta[1] * 64;

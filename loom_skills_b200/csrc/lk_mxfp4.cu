@@ -93,26 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int valid_rows = min(kBM, p.rows - m0);
   int expert = 0;
   if (GROUP != kDense) {
-    if (threadIdx.x == 0) {
-      int s = 0, found = -1, first = 0, nrows = 0;
-      for (int t = 0; t < p.max_tiles;) {
-        int e = p.tile_info[2 * t];
-        if (e < 0) break;
-        bool pair = t + 1 < p.max_tiles && p.tile_info[2 * (t + 1)] == e;
-        if (s == int(blockIdx.y)) {
-          found = e;
-          first = t;
-          nrows = pair ? 64 + p.tile_info[2 * (t + 1) + 1] : p.tile_info[2 * t + 1];
-          break;
-        }
-        ++s;
-        t += pair ? 2 : 1;
-      }
-      tile_meta[0] = found;
-      tile_meta[1] = first;
-      tile_meta[2] = nrows;
-    }
-    __syncthreads();
+    // super-tile s = blockIdx.y (the A ring is free scratch until the first TMA load)
+    moe_super_tile(p.tile_info, p.max_tiles, p.n_experts, blockIdx.y, reinterpret_cast<int*>(sA), tile_meta);
     if (tile_meta[0] < 0) return;
     expert = min(tile_meta[0], p.n_experts - 1);
     m0 = tile_meta[1] * 64;
@@ -231,30 +213,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return v;
     };
-    uint32_t sfv = load_sf(0);
-    for (int ks = 0; ks < kstages; ++ks) {
-      int sp = ks % kSP, sb = ks % kSB;
-      if (!mbar_wait(&full_p[sp], (ks / kSP) & 1)) atomicOr(&g_status, 1u);
-      if (ks >= kSB && !mbar_wait(&empty_b[sb], ((ks / kSB) - 1) & 1)) atomicOr(&g_status, 1u);
-      const uint4* prow = reinterpret_cast<const uint4*>(sP + sp * kPBytes + r * (kBK / 2));
-      uint8_t* bt = sB + sb * kBBytes;
+    // the scale bytes of stage ks + kSfAhead are requested while stage ks is expanded (a register ring: the loads'
+    // latency spans kSfAhead stages instead of one)
+    constexpr int kSfAhead = 4;
+    uint32_t sfr[kSfAhead];
 #pragma unroll
-      for (int qi = 0; qi < 4; ++qi) {   // 16 packed bytes = one 32-value block = two 16-value chunks
-        const int q = qi ^ qperm;
-        uint4 v = prow[q];
-        uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        if (ORDER == LK_ORDER_SPLIT16) split16_to_pairs(w);
-        *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q)) = make_uint4(w[0], w[1], 0u, 0u);
-        *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q + 1)) = make_uint4(w[2], w[3], 0u, 0u);
-      }
-      // scale-factor atom: row 32j + i of a 128-row half at byte 16i + 4j, the four k blocks in its four bytes
-      *reinterpret_cast<uint32_t*>(sSF + sb * kSFBytes + (r >> 7) * 512 + 16 * (r & 31) + 4 * ((r & 127) >> 5)) = sfv;
-      if (ks + 1 < kstages) sfv = load_sf(ks + 1);
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&full_b[sb]);
-        mbar_arrive(&empty_p[sp]);
+    for (int j = 0; j < kSfAhead; ++j) sfr[j] = load_sf(j);
+    for (int ks0 = 0; ks0 < kstages; ks0 += kSfAhead) {
+#pragma unroll
+      for (int j = 0; j < kSfAhead; ++j) {
+        const int ks = ks0 + j;
+        if (ks >= kstages) break;
+        int sp = ks % kSP, sb = ks % kSB;
+        if (!mbar_wait(&full_p[sp], (ks / kSP) & 1)) atomicOr(&g_status, 1u);
+        if (ks >= kSB && !mbar_wait(&empty_b[sb], ((ks / kSB) - 1) & 1)) atomicOr(&g_status, 1u);
+        const uint4* prow = reinterpret_cast<const uint4*>(sP + sp * kPBytes + r * (kBK / 2));
+        uint8_t* bt = sB + sb * kBBytes;
+#pragma unroll
+        for (int qi = 0; qi < 4; ++qi) {   // 16 packed bytes = one 32-value block = two 16-value chunks
+          const int q = qi ^ qperm;
+          uint4 v = prow[q];
+          uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          if (ORDER == LK_ORDER_SPLIT16) split16_to_pairs(w);
+          *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q)) = make_uint4(w[0], w[1], 0u, 0u);
+          *reinterpret_cast<uint4*>(bt + sw128(r, 2 * q + 1)) = make_uint4(w[2], w[3], 0u, 0u);
+        }
+        // scale-factor atom: row 32j + i of a 128-row half at byte 16i + 4j, the four k blocks in its four bytes
+        *reinterpret_cast<uint32_t*>(sSF + sb * kSFBytes + (r >> 7) * 512 + 16 * (r & 31) + 4 * ((r & 127) >> 5)) =
+            sfr[j];
+        sfr[j] = load_sf(ks + kSfAhead);   // past the last block: 127 (2^0) without a load
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full_b[sb]);
+          mbar_arrive(&empty_p[sp]);
+        }
       }
     }
     // epilogue: quadrant q = TMEM lanes 32q..; the two warps of a quadrant split the columns

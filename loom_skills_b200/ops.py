@@ -245,3 +245,17 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     a16, asc = row_scale_f16(act)
     ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts)
     return moe_combine_sorted(ys, pos, wts)
+
+
+def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, norm=True, order=L.ORDER_PAIRS):
+    """The routed expert FFN of one MoE layer with MXFP4 experts and e4m3 activations (gpt-oss-like; the fp8 fusion of
+    gen_mxfp4s.py:969-1110 applied to gen_llm.py:5324-5386): route -> bucket -> e4m3 row scale -> grouped gate/up
+    (SwiGLU) -> e4m3 row scale -> grouped down -> weighted combine. w_gu / ws_gu: per expert 2f rows (gate then up)
+    of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per expert h rows of f/2 / f/32 bytes."""
+    ids, wts = moe_route(logits, n_experts, ku, norm=norm)
+    ti, rm, pos = moe_bucket(ids, n_experts)
+    x8, s8 = row_scale_f8(x)
+    act = moe_grouped_gemm_mxfp4s_f8("swiglu", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True, order=order)
+    a8, as8 = row_scale_f8(act)
+    ys = moe_grouped_gemm_mxfp4s_f8("store", ti, rm, a8, as8, w_dn, ws_dn, h, ku, n_experts, order=order)
+    return moe_combine_sorted(ys, pos, wts)

@@ -503,6 +503,27 @@ def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts):
     return y
 
 
+def moe_ffn_mxfp4_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs"):
+    """The routed expert FFN with MXFP4 experts on the fp8 path (gen_llm.py:5324-5386 wiring with the e4m3 producer
+    and fp8 GEMMs of gen_mxfp4s.py:969-1110): x8 = row_scale_f8(x); act = silu(g) * u from the fp8 gate/up GEMM;
+    a8 = row_scale_f8(act) per assignment; ys = fp8 down GEMM; y[t] = sum_k wts[t,k] ys[t,k]. nib_gu/sc_gu: per expert
+    2f rows (gate then up) of h values; nib_dn/sc_dn: per expert h rows of f values."""
+    t, ku = ids.shape
+    x8, s8 = row_scale_f8(x)
+    y = np.zeros((t, h), np.float64)
+    for e in np.unique(ids):
+        sel = np.nonzero(ids == e)
+        tt = sel[0]
+        g0, g1 = 2 * f * e, 2 * f * e + f
+        g = gemm_mxfp4_f8_ref(x8[tt], s8[tt], nib_gu[g0:g1], sc_gu[g0:g1], f, h, order)
+        u = gemm_mxfp4_f8_ref(x8[tt], s8[tt], nib_gu[g1:g1 + f], sc_gu[g1:g1 + f], f, h, order)
+        act = (silu(g) * u).astype(np.float32)
+        a8, as8 = row_scale_f8(act)
+        ys = gemm_mxfp4_f8_ref(a8, as8, nib_dn[h * e:h * (e + 1)], sc_dn[h * e:h * (e + 1)], h, f, order)
+        np.add.at(y, tt, ys * np.asarray(wts, np.float64)[sel][:, None])
+    return y
+
+
 def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

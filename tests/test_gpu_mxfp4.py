@@ -139,3 +139,17 @@ class TestGroupedMxfp4:
             ref = O.gemm_mxfp4_f8_ref(ha8[sel], has8[sel], dn[ex * h:(ex + 1) * h], dns[ex * h:(ex + 1) * h], h, f)
             assert O.rel_l2(hys[sel], ref) < TOL_SAME, (ex, O.rel_l2(hys[sel], ref))
         assert ops.L.load().lk_device_status(1) == 0
+
+    @pytest.mark.parametrize("tokens", [1, 40, 300])
+    def test_moe_ffn_end_to_end(self, ops, tokens):
+        E, ku, h, f = 8, 4, 576, 320
+        rng = np.random.default_rng(41)
+        _, gu, gus = mx_weights(E * 2 * f, h, 42)
+        _, dn, dns = mx_weights(E * h, f, 43)
+        x = rng.standard_normal((tokens, h)).astype(np.float32)
+        logits = rng.standard_normal((tokens, E)).astype(np.float32)
+        y = host(ops.moe_ffn_mxfp4s(dev(x), dev(logits), dev(gu), dev(gus), dev(dn), dev(dns), h, f, E, ku))
+        ids, wts = O.route_ref(logits, ku)
+        ref = O.moe_ffn_mxfp4_ref(x, ids, wts, gu, gus, dn, dns, h, f)
+        assert O.rel_l2(y, ref) < TOL_F8, O.rel_l2(y, ref)
+        assert ops.L.load().lk_device_status(1) == 0
