@@ -154,6 +154,25 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Multi-GPU: N-sharded GEMM with the all-gather fused into the epilogue. No reference counterpart (the reference
+ * runs on one device); the sharding is the one BASELINE.json asks for (output columns across the GPUs of one box).
+ * lk_peer_alloc: a device buffer of `bytes` (cudaMalloc) and its 64-byte interprocess handle; lk_peer_open maps a
+ *   peer rank's handle into this process with peer access enabled; lk_peer_close / lk_peer_free release them.
+ * lk_gemm_allgather: the prefill GEMM of this rank's shard (n_local output columns from its slice of weight rows),
+ *   every output tile stored to all n_dst ranks' y buffers ([rows][n_total] f32, this rank's included) at columns
+ *   col_offset .. col_offset + n_local - 1: P2P stores over NVLink as each tile finishes. y_dst is a HOST array of
+ *   n_dst (<= 8) device pointers. The caller orders it against readers of the y buffers (a barrier of the ranks
+ *   before and after). mode LK_STORE or LK_SWIGLU (w2 = this rank's up shard).
+ */
+int lk_peer_alloc(int64_t bytes, void** ptr, void* handle64);
+int lk_peer_open(const void* handle64, void** ptr);
+int lk_peer_close(void* ptr);
+int lk_peer_free(void* ptr);
+int lk_gemm_allgather(int fmt, int mode, int rows, int k, int n_local, const uint16_t* x16, const float* scales,
+                      const void* w, const void* w2, float* const* y_dst, int n_dst, int n_total, int col_offset,
+                      lk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

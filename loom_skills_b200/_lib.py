@@ -35,6 +35,11 @@ SIGNATURES = {
     "lk_moe_combine_sorted": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "lk_moe_expert_mv": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "lk_moe_combine": (_I, [_I, _I, _I, _I, _P, _P, _P, _P]),
+    "lk_peer_alloc": (_I, [_L, ctypes.POINTER(_P), _P]),
+    "lk_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "lk_peer_close": (_I, [_P]),
+    "lk_peer_free": (_I, [_P]),
+    "lk_gemm_allgather": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, ctypes.POINTER(_P), _I, _I, _I, _P]),
 }
 
 _lib = None

@@ -8,9 +8,6 @@ using namespace lk;
 namespace lk {
 unsigned int status_mv(bool clear);
 unsigned int status_gemm(bool clear);
-int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
-         const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
-         int n_experts, int64_t expert_stride, int64_t w2_offset);
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
 int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
@@ -162,6 +159,31 @@ int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, cons
   if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
   if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
   return gemm(fmt, mode, rows, k, n, x16, scales, w, w2, y, (cudaStream_t)stream, nullptr, nullptr, rows, 1, 1, 0, 0);
+}
+
+int lk_gemm_allgather(int fmt, int mode, int rows, int k, int n_local, const uint16_t* x16, const float* scales,
+                      const void* w, const void* w2, float* const* y_dst, int n_dst, int n_total, int col_offset,
+                      lk_stream_t stream) {
+  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (rows < 0 || k <= 0 || n_local <= 0 || n_dst <= 0 || n_dst > kMaxPeers) return LK_EINVAL;
+  if (k % 256 || n_local % 16 || n_total % 16 || col_offset % 16) return LK_EINVAL;
+  if (col_offset < 0 || col_offset + n_local > n_total) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!x16 || !scales || !w || !y_dst) return LK_EINVAL;
+  if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
+  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16))) return LK_EALIGN;
+  OutSpec out{};
+  for (int d = 0; d < n_dst; ++d) {
+    if (!y_dst[d]) return LK_EINVAL;
+    if (!aligned(y_dst[d], 16)) return LK_EALIGN;
+    out.dst[d] = y_dst[d];
+  }
+  out.ndst = n_dst;
+  out.ld = n_total;
+  out.col_off = col_offset;
+  return gemm(fmt, mode, rows, k, n_local, x16, scales, w, w2, y_dst[0], (cudaStream_t)stream, nullptr, nullptr,
+              rows, 1, 1, 0, 0, &out);
 }
 
 int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,

@@ -285,6 +285,7 @@ LK_DEV float silu(float g) { return g / (1.0f + __expf(-g)); }
 // MoE schedule: 128-row super-tiles over the bucket's 64-row tiles
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kMaxExperts = 256;
+constexpr int kMaxPeers = 8;   // ranks of one NVSwitch domain a GEMM epilogue can store to
 // Super-tile `s` of a tile schedule laid out as the bucket writes it (the tiles of each expert contiguous, experts
 // ascending, unused tiles (-1, 0)): consecutive tiles of one expert are paired from the start of its run, so expert e
 // owns ceil(tiles_e / 2) super-tiles. Called by every thread of the CTA; `scratch` is 3 * kMaxExperts ints of shared

@@ -28,9 +28,16 @@ constexpr int kGemmThreads = (2 + kDqWarps) * 32;
 
 enum { kDense = 0, kGather = 1, kSorted = 2 };
 
+constexpr int kStgStride = 36;   // floats per row of the epilogue's 32 x 32 staging tile (16-byte aligned rows)
+
 struct GemmArgs {
   const float* scales;  // [rows or xrows][2]
-  float* y;             // [rows][n]
+  // outputs: tile (row, col) goes to dst[d][row * ld + col_off + col] for every d < ndst (one destination: y with
+  // ld = n; the all-gather form: every rank's y, ld = the full width, col_off = this rank's first column)
+  float* dst[kMaxPeers];
+  int ndst;
+  int64_t ld;
+  int col_off;
   int rows, k, n;
   // weights: wmap / w2map cover [rows][row_bytes / 4] u32 of the (expert-stacked) packed weights; an expert's
   // first row is e * rows_per_expert (w2: e * rows_per_expert2 + w2_row_offset)
@@ -312,7 +319,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = mh * kBM + 32 * q + lane;
     const bool row_ok = row < valid_rows;
     float inv = 0.f;
-    float* yrow = nullptr;
     if (row_ok) {
       int grow = m0 + row;
       int srow = grow;
@@ -321,11 +327,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         srow = a >= 0 ? a / p.ku : -1;
       }
       inv = srow >= 0 ? p.scales[2 * int64_t(srow) + 1] : 0.f;
-      yrow = p.y + int64_t(grow) * p.n + n0;
     }
     constexpr int kColsPerWarp = MH == 2 ? BN : BN / 2;
     const int col0 = MH == 2 ? 0 : pair * kColsPerWarp;
     const uint32_t tbase = tmem + (uint32_t(32 * q) << 16) + mh * NW * BN;
+    // 32 x 32 blocks go through a per-warp staging tile in the (drained) A ring: written a row per lane, read back
+    // a quarter row per lane, so every store instruction covers four full 128-byte row segments. The block is
+    // stored to each destination (this rank's y, and the peers' for the all-gather form).
+    float* stg = reinterpret_cast<float*>(sA) + (warp - 2) * (32 * kStgStride);
+    const int sr = lane >> 3, sc = 4 * (lane & 7);
 #pragma unroll 1
     for (int cb = 0; cb < kColsPerWarp; cb += 32) {
       int col = col0 + cb;
@@ -340,22 +350,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= inv;
       }
-      if (row_ok) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          if (col + i >= nb_rows) break;
-          float4* dst = reinterpret_cast<float4*>(yrow + col + i);
-          float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(stg + lane * kStgStride + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      __syncwarp();
+      const bool col_ok = col + sc < nb_rows;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int rr = 4 * j + sr;                       // row inside the warp's 32
+        const int trow = mh * kBM + 32 * q + rr;         // row inside the tile
+        float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
+        if (col_ok && trow < valid_rows) {
+          const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
           if (MODE == LK_ACC) {
-            float4 old = *dst;
+            float4 old = *reinterpret_cast<const float4*>(p.dst[0] + off);
             o.x += old.x;
             o.y += old.y;
             o.z += old.z;
             o.w += old.w;
           }
-          *dst = o;
+#pragma unroll
+          for (int d = 0; d < kMaxPeers; ++d)
+            if (d < p.ndst) *reinterpret_cast<float4*>(p.dst[d] + off) = o;
         }
       }
+      __syncwarp();
     }
   }
   tc_fence_before();
@@ -436,10 +455,20 @@ static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, d
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
-         int n_experts, int64_t expert_stride, int64_t w2_offset) {
+         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out) {
   GemmArgs a{};
   a.scales = scales;
-  a.y = y;
+  if (out) {
+    for (int d = 0; d < out->ndst; ++d) a.dst[d] = out->dst[d];
+    a.ndst = out->ndst;
+    a.ld = out->ld;
+    a.col_off = out->col_off;
+  } else {
+    a.dst[0] = y;
+    a.ndst = 1;
+    a.ld = n;
+    a.col_off = 0;
+  }
   a.rows = rows;
   a.k = k;
   a.n = n;

@@ -33,4 +33,15 @@ struct MvArgs {
 };
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
 
+// where a GEMM stores its tile: dst[d][row * ld + col_off + col] for d < ndst (at most 8)
+struct OutSpec {
+  float* dst[8];
+  int ndst;
+  int64_t ld;
+  int col_off;
+};
+int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
+         const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
+         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out = nullptr);
+
 }  // namespace lk
