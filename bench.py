@@ -11,8 +11,9 @@ TFLOP/s at M=2048 over the same shapes (step = row scale + the six tcgen05 GEMMs
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
 --gpus N > 1 runs under torchrun, one rank per GPU, each rank with its own replica of the workload (weak scaling;
-the decode step has no exchange). --impl reference times the reference's CPU path (the numpy dequant + float64
-matvec of make_kernel_tests.py, restated in oracle/) on the same metric.
+the decode step has no exchange); the sharded IQ4_NL GEMMs of configs[4] split their output columns over the ranks
+and all-gather them (strong scaling). --impl reference times the reference's CPU path (gguf's dequantize + a float64
+numpy matvec, as make_kernel_tests.py builds its references) on the same metric.
 """
 import argparse
 import json
@@ -104,26 +105,54 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------------------------
-# CPU baseline / reference arm: the reference's numpy path (restated in oracle/)
+# inputs: Q4_K blocks synthesised from a seed (timing does not depend on the values; parity is tested on quantised
+# weights): f16 d and dmin of the size N(0, 0.02) weights get, uniform 6-bit scale/min fields and nibbles
+# ------------------------------------------------------------------------------------------------------------------
+Q4K_D = np.frombuffer(np.float16(5.2e-5).tobytes() * 2, np.uint8)   # d, dmin
+
+
+def synth_q4k(rng, rows, k):
+    w = rng.integers(0, 256, (rows, k // 256, 144), dtype=np.uint8)
+    w[:, :, 0:4] = Q4K_D
+    return w.reshape(rows, -1)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's own CPU path for the decode matvec -- gguf's dequantize (the
+# reference's pinned third-party dequantiser, gguf 0.19.0) and a float64 numpy matvec, as make_kernel_tests.py:45-47,
+# 231-238 builds its references; the oracle port stands in only if gguf is missing
 # ------------------------------------------------------------------------------------------------------------------
 def cpu_decode_gbs(budget_s=10.0, rows=1024):
     """Dequantise + float64 matvec of a `rows`-row slice of the gate_up projection, repeated for ~budget_s seconds."""
-    from oracle import qmm_oracle as O
     k = 4096
     rng = np.random.default_rng(1)
-    w = O.quantize_q4_k((rng.standard_normal((rows, k)) * 0.02).astype(np.float32))
+    w = synth_q4k(rng, rows, k)
     x = rng.standard_normal((1, k)).astype(np.float32)
+    try:
+        import gguf
+        from gguf import GGMLQuantizationType
+
+        def step():
+            W = gguf.quants.dequantize(w, GGMLQuantizationType.Q4_K).reshape(rows, k)
+            return x.astype(np.float64) @ W.T.astype(np.float64)
+        kind, what = "reference", f"gguf {getattr(gguf, '__version__', '0.19.0')} dequantize + float64 numpy matvec"
+    except ImportError:
+        from oracle import qmm_oracle as O
+
+        def step():
+            return O.mv_ref("q4_k", w, x, rows, k)
+        kind, what = "port", "oracle restatement (numpy dequant + float64 matvec)"
     t0 = time.perf_counter()
     reps = 0
     while True:
-        O.mv_ref("q4_k", w, x, rows, k)
+        step()
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s or reps >= 100000:
             break
     gbs = reps * w.nbytes / el / 1e9
-    return gbs, {"kind": "port", "cores": os.cpu_count(),
-                 "sample": f"Q4_K {rows}x{k} slice of gate_up (numpy dequant + float64 matvec, OpenBLAS threads), "
+    return gbs, {"kind": kind, "cores": os.cpu_count(),
+                 "sample": f"Q4_K {rows}x{k} slice of gate_up: {what} (BLAS threads = all host cores), "
                            f"{reps} reps in {el:.1f} s"}
 
 
@@ -153,16 +182,9 @@ def run_reference(args):
 # our arm
 # ------------------------------------------------------------------------------------------------------------------
 def make_weights(torch, layers, seed=0):
-    """Q4_K weights for one layer (seeded N(0,0.02), quantised on the host), copied to `layers` distinct buffers."""
-    from oracle import qmm_oracle as O
+    """Q4_K weights for one layer, copied to `layers` distinct buffers (rotated so they exceed L2)."""
     rng = np.random.default_rng(seed)
-    base = {}
-    for name, k, n in SHAPES:
-        chunks = []
-        for r0 in range(0, n, 2048):
-            r1 = min(n, r0 + 2048)
-            chunks.append(O.quantize_q4_k((rng.standard_normal((r1 - r0, k)) * 0.02).astype(np.float32)))
-        base[name] = torch.from_numpy(np.concatenate(chunks)).cuda()
+    base = {name: torch.from_numpy(synth_q4k(rng, n, k)).cuda() for name, k, n in SHAPES}
     return [{name: (t if li == 0 else t.clone()) for name, t in base.items()} for li in range(layers)]
 
 
@@ -183,6 +205,135 @@ class Timed:
 
     def replay(self):
         self.graph.replay()
+
+
+F16_SCALE = {"q4_0": 5.6e-3, "iq4_nl": 3.5e-4}   # block scales of quantised N(0, 0.02): amax / 8, amax / 127
+
+
+def synth_blocks(torch, dev, rows, k, fmt, gen):
+    """Packed 18-byte blocks synthesised on the device for timing: uniform 4-bit codes, the f16 scale a block of
+    N(0, 0.02) weights gets (the values do not change the work; parity is tested on quantised weights)."""
+    w = torch.randint(0, 256, (rows, k // 32, 18), dtype=torch.uint8, device=dev, generator=gen)
+    d = np.frombuffer(np.float16(F16_SCALE[fmt]).tobytes(), np.uint8)
+    w[:, :, 0] = int(d[0])
+    w[:, :, 1] = int(d[1])
+    return w.view(rows, -1)
+
+
+def synth_mxfp4(torch, dev, rows, k, gen):
+    """MXFP4 split planes synthesised on the device: uniform nibbles, E8M0 exponents 119..121 (N(0, 0.02) blocks)."""
+    nib = torch.randint(0, 256, (rows, k // 2), dtype=torch.uint8, device=dev, generator=gen)
+    sc = torch.randint(119, 122, (rows, k // 32), dtype=torch.uint8, device=dev, generator=gen)
+    return nib, sc
+
+
+def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
+    """IQ4_NL K=5120 N=27648 and K=27648 N=5120 at M=4096, output columns sharded over the ranks and
+    all-gathered; one step = both GEMMs. Strong scaling (the job is fixed). Exchanges: 'p2p' (tiles stored into
+    every rank's y by the GEMM epilogue) and 'collective' (local GEMM + NCCL all-gather + column interleave)."""
+    from loom_skills_b200 import ops
+    from loom_skills_b200.parallel import ShardedGemm, shard_range
+    M = 4096
+    shapes = [("gate_up", 5120, 27648), ("down", 27648, 5120)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    xgen = torch.Generator(device=dev)
+    xgen.manual_seed(99)   # the same activations on every rank
+    parts = []
+    for name, k, n in shapes:
+        c0, c1 = shard_range(n, world, rank)
+        w = synth_blocks(torch, dev, c1 - c0, k, "iq4_nl", gen)
+        x = torch.randn(M, k, device=dev, generator=xgen).to(torch.bfloat16)
+        x16, sc = ops.row_scale_f16(x)
+        parts.append((name, k, n, w, x16, sc))
+    flops = sum(2.0 * M * k * n for _, k, n, *_ in parts)
+    out = {"workload": "configs[4] Qwen2.5-32B-like IQ4_NL, M=4096: K=5120 N=27648 and K=27648 N=5120",
+           "data": "IQ4_NL blocks synthesised on the device (uniform indices, f16 scale 3.5e-4); bf16 N(0,1) x",
+           "n_gpus": world, "scaling": "strong", "sharding": "output columns (weight rows) per rank, y all-gathered"}
+    steps = max(5, min(20, args.steps // 50))
+    for exchange in ("p2p", "collective"):
+        sgs = [ShardedGemm("iq4_nl", "store", w, n, k, exchange=exchange) for _, k, n, w, _, _ in parts]
+
+        def step():
+            for sg, (_, _, _, _, x16, sc) in zip(sgs, parts):
+                sg(x16, sc)
+        for _ in range(max(3, args.warmup // 3)):
+            step()
+        ms = time_steps(step, steps)
+        out[exchange] = {"ms_per_step": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                         "steps": steps}
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        for sg in sgs:
+            sg.close()
+    # fused compute + collective roofline: the slower of the GEMM at the measured tensor peak and the bytes each rank
+    # must push over NVLink (its f32 shard to world - 1 peers) at the measured 770 GB/s per direction
+    pk, _ = peaks()
+    t_math = flops / world / (pk["bf16_tflops_sustained"] * 1e12)
+    t_link = sum((world - 1) * M * (n / world) * 4 for _, _, n, *_ in parts) / 770e9
+    target = max(t_math, t_link)
+    out["roofline"] = {"target_ms": round(target * 1e3, 4), "t_math_ms": round(t_math * 1e3, 4),
+                       "t_link_ms": round(t_link * 1e3, 4), "frac": round(target * 1e3 / out["p2p"]["ms_per_step"], 4),
+                       "peaks": "measured bf16 sustained; NVLink 770 GB/s per direction (measured peer copy)"}
+    return out
+
+
+def bench_moe(args, torch, dev, time_steps, pk):
+    """configs[2] (Q4_0 MoE, Qwen3-30B-A3B-like) and configs[3] (MXFP4 x e4m3 MoE, gpt-oss-20b-like): one MoE layer
+    (route, schedule, expert GEMMs / matvecs, combine) per step as a CUDA graph; plus the dense MXFP4 x FP8 GEMM."""
+    from loom_skills_b200 import ops
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321)
+    out = {}
+    E, ku, h, f = 128, 8, 2048, 768
+    w_gu = synth_blocks(torch, dev, E * 2 * f, h, "q4_0", gen)
+    w_dn = synth_blocks(torch, dev, E * h, f, "q4_0", gen)
+    q = {}
+    for m in (1, 16, 256, 4096):
+        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
+        lg = torch.randn(m, E, device=dev, generator=gen)
+        g = Timed(torch, lambda: ops.moe_ffn("q4_0", x, lg, w_gu, w_dn, h, f, E, ku))
+        for _ in range(3):
+            g.replay()
+        ms = time_steps(g.replay, 20)
+        q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2)}
+    out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
+                             "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
+    del w_gu, w_dn
+    E, ku, h, f = 32, 4, 2880, 2880
+    gu, gus = synth_mxfp4(torch, dev, E * 2 * f, h, gen)
+    dn, dns = synth_mxfp4(torch, dev, E * h, f, gen)
+    mx = {}
+    for m in (1, 32, 1024, 8192):
+        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
+        lg = torch.randn(m, E, device=dev, generator=gen)
+        g = Timed(torch, lambda: ops.moe_ffn_mxfp4s(x, lg, gu, gus, dn, dns, h, f, E, ku))
+        for _ in range(3):
+            g.replay()
+        ms = time_steps(g.replay, 20)
+        mx[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2)}
+    # the dense kernel alone: fused gate/up shape, M=8192
+    M = 8192
+    x8, s8 = ops.row_scale_f8(torch.randn(M, h, device=dev, generator=gen))
+    yg = torch.empty(M, f, device=dev)
+    g = Timed(torch, lambda: ops.gemm_mxfp4s_f8("swiglu", x8, s8, gu[:f], gus[:f], f, w2=gu[f:2 * f],
+                                                 w2s=gus[f:2 * f], y=yg))
+    for _ in range(3):
+        g.replay()
+    ms = time_steps(g.replay, 50)
+    tf = 2.0 * M * h * 2 * f / (ms * 1e-3) / 1e12
+    f8_peak = 2 * pk["bf16_tflops_sustained"]
+    out["mxfp4_gpt_oss_20b"] = {
+        "experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": mx,
+        "data": "MXFP4 planes synthesised on the device (uniform nibbles, E8M0 119..121); bf16 N(0,1) x",
+        "dense_gemm": {"shape": [M, h, 2 * f], "mode": "swiglu", "ms": round(ms, 4), "tflops": round(tf, 1),
+                       "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": round(f8_peak, 1),
+                                    "unit": "TFLOP/s", "frac": round(tf / f8_peak, 4),
+                                    "peak_source": "2 x measured bf16 sustained: kind::mxf8f6f4 runs at the fp8 rate "
+                                                   "(e4m3 activations keep it off the fp4 rate)",
+                                    "kernel": "k_gemm_mx (tcgen05 kind::mxf8f6f4.block_scale, lk_mxfp4)"}}}
+    return out
 
 
 def run_ours(args):
@@ -344,6 +495,11 @@ def run_ours(args):
             sweep[str(m)] = {"ms": round(mms, 4), "weight_gbs": round(wbytes_layer / (mms * 1e-3) / 1e9, 1),
                              "tflops": round(sum(2.0 * m * n * k for _, k, n in SHAPES) / (mms * 1e-3) / 1e12, 2)}
 
+    # ---- the IQ4_NL GEMMs N-sharded over the ranks, all-gather fused into the epilogue (strong scaling)
+    sharded = bench_sharded(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
+    # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
+    moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
+
     gpu_launches = args.steps * launches_per_step
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
@@ -351,7 +507,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q4_k x bf16 (f16 tensor-core codes, f32 accumulate)",
-            "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K, N(0,1) bf16 activations",
+            "data": "synthetic: seeded Q4_K blocks (f16 d/dmin of N(0,0.02) weights, uniform 6-bit fields and nibbles), N(0,1) bf16 activations",
             "config": {"workload": "configs[1] Qwen3-8B-like Q4_K projections, decode M=1",
                        "shapes_k_n": [[k, n] for _, k, n in SHAPES], "layers": args.layers,
                        "weight_bytes_per_step": step_bytes,
@@ -361,7 +517,7 @@ def run_ours(args):
                        "launch": "one CUDA graph replay per step"},
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
-            "hbm_frac": round(value / world / pk["hbm_gbs"], 4)}
+            "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "sharded_iq4_nl": sharded, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
         del dec, e2e_g, scale_g, gemm_g
@@ -379,6 +535,7 @@ def main():
     ap.add_argument("--prefill-rows", type=int, default=2048)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the sharded-GEMM and MoE sections")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

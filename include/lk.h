@@ -8,7 +8,8 @@
  *
  * Conventions
  *  - All pointers are device pointers (cudaMalloc'd or views of them); the caller owns every buffer, as the
- *    reference's command programs do. Nothing here allocates device memory or synchronises.
+ *    reference's command programs do. Nothing here allocates device memory (lk_peer_alloc, the multi-GPU buffer
+ *    set-up, excepted) or synchronises (lk_device_status excepted).
  *  - Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
  *  - Return 0 (LK_OK) or a negative LK_E* code after host-side validation of formats, shapes and alignment. The
  *    reference has no runtime errors (its contracts are index.assume preconditions); violating one here is an error

@@ -39,6 +39,9 @@ def shard_range(n, world, rank, align=ALIGN):
 
 
 def _world(group):
+    """(world size, rank) of `group`; a process without a process group is a world of one."""
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
     return dist.get_world_size(group), dist.get_rank(group)
 
 
@@ -66,8 +69,10 @@ class PeerBuffers:
         handle = (ctypes.c_uint8 * 64)()
         L.check(self.L.lk_peer_alloc(nbytes, ctypes.byref(own), handle), "lk_peer_alloc")
         self.own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
         self.opened = []
         ptrs = []
         for r in range(self.world):
@@ -112,6 +117,8 @@ class ShardedGemm:
         self._flag = None
 
     def _barrier(self, device):
+        if self.world == 1:
+            return
         if self._flag is None:
             self._flag = torch.zeros(1, device=device)
         dist.all_reduce(self._flag, group=self.group)
@@ -131,6 +138,8 @@ class ShardedGemm:
 
     def _collective(self, x16, scales, rows):
         y_local = self._local(x16, scales).contiguous()
+        if self.world == 1:
+            return y_local
         widths = [shard_range(self.n, self.world, r) for r in range(self.world)]
         if all(c1 - c0 == widths[0][1] - widths[0][0] for c0, c1 in widths):
             buf = torch.empty(self.world * rows, y_local.shape[1], dtype=y_local.dtype, device=y_local.device)
