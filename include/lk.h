@@ -155,6 +155,21 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream);
 
+/* lk_moe_ffn_decode_noalloc: the decode MoE layer in one call that allocates nothing. No counterpart in the
+ * reference. It runs lk_moe_route (gating 1 over the given logits [tokens][n_experts] f32, renormalised when norm),
+ * then lk_moe_expert_mv in both modes (w_gu: per expert f gate rows then f up rows of h values; w_dn: per expert
+ * h rows of f values), then lk_moe_combine into y [tokens][h] f32. Its four intermediates (ids, weights, activations,
+ * expert outputs) live in one fixed device array inside liblk instead of buffers the caller allocates.
+ * It is for callers that cannot call cudaMalloc: an embedding runtime with a fixed device-memory budget, a host
+ * callback, or a process whose device allocator belongs to someone else.
+ * Limits: tokens * ku <= 128, h <= 4096, f <= 4096 (LK_ERANGE beyond); h % 256 == f % 256 == 0.
+ * Every call on a device shares the one array, so calls that overlap on the GPU (other streams, other host threads)
+ * race. Nothing in the array needs to start at zero. The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress); make that call before any stream capture. */
+int lk_moe_ffn_decode_noalloc(int fmt, int tokens, int h, int f, int n_experts, int ku, int norm,
+                              const float* logits, const void* x, int x_dtype, const void* w_gu, const void* w_dn,
+                              float* y, lk_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Multi-GPU: N-sharded GEMM with the all-gather fused into the epilogue. No reference counterpart (the reference
  * runs on one device); the sharding is the one BASELINE.json asks for (output columns across the GPUs of one box).

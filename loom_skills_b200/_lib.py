@@ -40,6 +40,7 @@ SIGNATURES = {
     "lk_peer_close": (_I, [_P]),
     "lk_peer_free": (_I, [_P]),
     "lk_gemm_allgather": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, ctypes.POINTER(_P), _I, _I, _I, _P]),
+    "lk_moe_ffn_decode_noalloc": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -44,4 +44,25 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
          int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out = nullptr);
 
+int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+                const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
+int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+            const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
+            const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
+            int w2_row_offset);
+
+int moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
+              const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s);
+int moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_t* info, const int32_t* ids,
+               int32_t* tile_info, int32_t* rowmap, int32_t* pos, cudaStream_t s);
+int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
+                       const float* wts, float* y, cudaStream_t s);
+int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
+                cudaStream_t s);
+
+// device status words of the kernel files (bit 0: a bounded wait gave up)
+unsigned int status_mv(bool clear);
+unsigned int status_gemm(bool clear);
+unsigned int status_mx(bool clear);
+
 }  // namespace lk

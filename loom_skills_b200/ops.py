@@ -259,3 +259,19 @@ def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, nor
     a8, as8 = row_scale_f8(act)
     ys = moe_grouped_gemm_mxfp4s_f8("store", ti, rm, a8, as8, w_dn, ws_dn, h, ku, n_experts, order=order)
     return moe_combine_sorted(ys, pos, wts)
+
+
+def moe_ffn_decode_noalloc(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, y=None):
+    """The decode MoE layer in one C-ABI call whose intermediates live in liblk's fixed device array (no allocation
+    inside the call; only the output y is allocated here when not given). For callers that cannot allocate device
+    memory. Limits: tokens * ku <= 128, h, f <= 4096; calls that overlap on the GPU race on the shared array."""
+    _cuda(x, logits, w_gu, w_dn, y)
+    x = x.contiguous()
+    logits = logits.contiguous().float()
+    tokens = x.shape[0]
+    if y is None:
+        y = torch.empty(tokens, h, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_moe_ffn_decode_noalloc(_fmt(fmt), tokens, h, f, n_experts, ku, 1 if norm else 0,
+                                               _ptr(logits), _ptr(x), _DT[x.dtype], _ptr(w_gu), _ptr(w_dn), _ptr(y),
+                                               _stream()), "lk_moe_ffn_decode_noalloc")
+    return y
