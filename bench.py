@@ -4,9 +4,12 @@
 Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B-like projection shapes
 (K=4096: N=4096 q/o, N=1024 k/v, N=24576 fused gate+up; down K=12288, N=4096), bf16 activations. One STEP is one decode
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
-868 MB at 8 layers, exceed the 126 MB L2). `value` is the decode GEMV weight GB/s; the line also carries the prefill
-TFLOP/s at M=2048 over the same shapes (step = row scale + the six tcgen05 GEMMs), and a sweep over M in
-{1, 8, 64, 512, 2048}. Each step is one CUDA-graph replay of the public ops' launches (48 matvecs per decode step).
+868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer the activations are
+quantised to int8 (g_quant_q8) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
+weight GB/s; the line also carries the bf16-activation decode, the prefill TFLOP/s at M=2048 over the same shapes
+(step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
+MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 48 matvecs per decode
+step; the kernels chain with programmatic dependent launch).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
@@ -357,7 +360,27 @@ def run_ours(args):
     launches_per_step = args.layers * len(SHAPES)
     step_bytes = args.layers * wbytes_layer
 
-    def decode_body():
+    # int8 activations per layer: the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518)
+    xq = [{k: torch.empty(k + (k // 32) * 8, dtype=torch.uint8, device=dev) for k in xs} for _ in range(args.layers)]
+
+    def quant_layer(li):
+        for k in xs:
+            ops.quant_q8(xs[k], out=xq[li][k])
+
+    def mv_layer(li):
+        for name, k, n in SHAPES:
+            ops.mv_q8("q4_k", wstack[li][name], xq[li][k], n, k, 1, y=ys[li][name])
+
+    def decode_body():   # one decode step: per layer, quantise the activations, then the six projections
+        for li in range(args.layers):
+            quant_layer(li)
+            mv_layer(li)
+
+    def mv_body():       # the matvecs alone (the dominant kernel, for the roofline)
+        for li in range(args.layers):
+            mv_layer(li)
+
+    def decode_bf16_body():   # the f32/bf16-activation path (ACT_Q8=0)
         for li in range(args.layers):
             for name, k, n in SHAPES:
                 ops.mv("q4_k", wstack[li][name], xs[k], n, k, y=ys[li][name])
@@ -389,8 +412,7 @@ def run_ours(args):
             clk.mark(False)
         return max_over_ranks(t0.elapsed_time(t1)) / steps
 
-    # ---- decode: device-resident inputs, one graph replay per step. Every launch of the step is the matvec kernel,
-    # back to back, so its average launch duration is the step time (CUDA events around the timed steps) / launches.
+    # ---- decode: device-resident inputs, one graph replay per step (16 quantisations + 48 matvecs)
     dec = Timed(torch, decode_body)
     for _ in range(args.warmup):
         dec.replay()
@@ -399,13 +421,25 @@ def run_ours(args):
     ms = time_steps(dec.replay, args.steps, clk)
     clocks = clk.stop()
     value = world * step_bytes / (ms * 1e-3) / 1e9
-    alg_per_launch = (step_bytes + args.layers * act_bytes) / launches_per_step
-    kavg = ms / launches_per_step
+    # the matvec kernel alone: the same 48 launches back to back in one graph, CUDA events around the timed replays
+    mvg = Timed(torch, mv_body)
+    for _ in range(args.warmup):
+        mvg.replay()
+    mv_ms = time_steps(mvg.replay, args.steps)
+    act_q8 = sum((k + k // 32 * 8) + n * 4 for _, k, n in SHAPES)   # int8 codes + meta read, f32 y written
+    alg_per_launch = (step_bytes + args.layers * act_q8) / launches_per_step
+    kavg = mv_ms / launches_per_step
     achieved = alg_per_launch / (kavg * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": TRAFFIC_DECODE, "peak_source": pk_src,
-            "kernel": "k_mv<Q4_K, bf16, TOK=1> (lk_mv)", "avg_launch_us": round(kavg * 1e3, 2),
-            "alg_bytes_per_launch": int(alg_per_launch)}
+            "kernel": "k_mv_q8_rows / k_mv_q8 (Q4_K x int8, dp4a; lk_mvq8)", "avg_launch_us": round(kavg * 1e3, 2),
+            "alg_bytes_per_launch": int(alg_per_launch), "mv_ms_per_step": round(mv_ms, 4)}
+    bf = Timed(torch, decode_bf16_body)
+    for _ in range(args.warmup):
+        bf.replay()
+    bf_ms = time_steps(bf.replay, max(3, args.steps // 4))
+    decode_bf16 = {"value": round(world * step_bytes / (bf_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                   "ms_per_step": round(bf_ms, 4), "numerics": "bf16 activations (ACT_Q8=0), k_mv (lk_mv)"}
 
     # ---- e2e through the public API: pinned host x in, every projection output back, each step (one graph)
     hx = {k: torch.empty(1, k, dtype=torch.bfloat16).pin_memory() for k in xs}
@@ -481,9 +515,10 @@ def run_ours(args):
             ym = {name: torch.empty(m, n, device=dev) for name, _, n in SHAPES}
 
             def body_m():
-                if m < 64:   # gen_llm.py:6107: matvecs below 64 tokens, GEMMs from 64
+                if m < 64:   # gen_llm.py:6107: matvecs below 64 tokens (int8 activations), GEMMs from 64
+                    xqm = {k: ops.quant_q8(xm[k]) for k in xm}
                     for name, k, n in SHAPES:
-                        ops.mv("q4_k", wstack[0][name], xm[k], n, k, y=ym[name])
+                        ops.mv_q8("q4_k", wstack[0][name], xqm[k], n, k, m, y=ym[name])
                 else:
                     x16 = {k: ops.row_scale_f16(xm[k]) for k in xm}
                     for name, k, n in SHAPES:
@@ -500,13 +535,13 @@ def run_ours(args):
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
 
-    gpu_launches = args.steps * launches_per_step
+    gpu_launches = args.steps * (launches_per_step + 2 * args.layers)   # 48 matvecs + 16 quantisations per step
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_k x bf16 (f16 tensor-core codes, f32 accumulate)",
+            "vs_baseline": None, "dtype": "q4_k x int8 (Q8_1 activations, integer dot, f32 group scaling)",
             "data": "synthetic: seeded Q4_K blocks (f16 d/dmin of N(0,0.02) weights, uniform 6-bit fields and nibbles), N(0,1) bf16 activations",
             "config": {"workload": "configs[1] Qwen3-8B-like Q4_K projections, decode M=1",
                        "shapes_k_n": [[k, n] for _, k, n in SHAPES], "layers": args.layers,
@@ -517,10 +552,11 @@ def run_ours(args):
                        "launch": "one CUDA graph replay per step"},
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
-            "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "sharded_iq4_nl": sharded, "moe": moe}
+            "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_bf16": decode_bf16,
+            "sharded_iq4_nl": sharded, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
-        del dec, e2e_g, scale_g, gemm_g
+        del dec, mvg, bf, e2e_g, scale_g, gemm_g
         dist.barrier()
         dist.destroy_process_group()
 

@@ -87,6 +87,21 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
           const void* w2, float* y, lk_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
+ * Decode matvec with int8 activations: the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518).
+ * lk_quant_q8: g_quant_q8 (gen_llm.py:683-750), launch(%rows, %width, %x, %xq): per 32-value group d = amax/127,
+ *   q = round(x/d) (halves away from zero; 0 for an all-zero group); xq = codes int8 [rows][k], then at byte rows*k
+ *   the meta [rows][k/32][2] f32 = (d rounded to f16, sum of the group's codes). x_dtype LK_F32 or LK_BF16, k % 32 == 0.
+ *   xq holds rows*k + rows*(k/32)*8 bytes.
+ * lk_mv_q8: g_mv_{fmt}_k{K}[_t{TG}]_q8 (gen_llm.py:1159-1378 with @g_q4_0_icodes / @g_q4_k_icodes, :521-680),
+ *   launch(%n, %tokens, %accumulate, %xq, %w, %y): y[t][n] (+)= sum_k dequant(W)[n][k] * xcode[t][k] * d[t][k/32],
+ *   the weight codes contracted with the activation codes in integer arithmetic per 32-group. xq: lk_quant_q8's
+ *   output for `tokens` rows. Formats Q4_0 and Q4_K (IQ4_NL: LK_EUNSUPPORTED); k % 256 == 0.
+ */
+int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_stream_t stream);
+int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+             lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
  * Prefill GEMM (tcgen05 + TMEM). Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704,
  * 706, 1224), launch(%rows, %k, %n, %x, %scales, %w [, %w2], %y):
  *   Y[rows][n] (+)= (X16 . W16^T) * scales[row][1]; swiglu: silu(G) * U with G, U the two weights' products.

@@ -25,6 +25,8 @@ SIGNATURES = {
     "lk_row_scale_f16": (_I, [_I, _I, _P, _I, _P, _P, _P]),
     "lk_row_scale_f8": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _P]),
     "lk_mv": (_I, [_I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
+    "lk_quant_q8": (_I, [_I, _I, _P, _I, _P, _P]),
+    "lk_mv_q8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "lk_gemm": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "lk_gemm_mxfp4s_f8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lk_moe_route": (_I, [_I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _P, _P, _P]),

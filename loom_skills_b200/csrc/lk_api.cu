@@ -39,7 +39,26 @@ int64_t lk_row_bytes(int fmt, int64_t k) {
 
 // Reads (and optionally clears) the device-side status word: bit 0 = a kernel's bounded wait gave up. Synchronous.
 unsigned int lk_device_status(int clear) {
-  return status_mv(clear != 0) | status_gemm(clear != 0) | status_mx(clear != 0);
+  return status_mv(clear != 0) | status_gemm(clear != 0) | status_mx(clear != 0) | status_q8(clear != 0);
+}
+
+int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_stream_t stream) {
+  if (rows < 0 || k <= 0 || k % 32) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!x || !xq) return LK_EINVAL;
+  if (!aligned(xq, 16)) return LK_EALIGN;
+  return quant_q8(rows, k, x, x_dtype, xq, (cudaStream_t)stream);
+}
+
+int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+             lk_stream_t stream) {
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return q4_family(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (n <= 0 || k <= 0 || tokens < 0 || k % 256) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!xq || !w || !y) return LK_EINVAL;
+  if (!aligned(xq, 16) || !aligned(w, 16)) return LK_EALIGN;
+  return mv_q8(fmt, n, k, tokens, accumulate, xq, w, y, (cudaStream_t)stream);
 }
 
 int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,

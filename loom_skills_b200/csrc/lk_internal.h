@@ -60,7 +60,13 @@ int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, cons
 int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                 cudaStream_t s);
 
+// int8-activation decode path (xq: codes [rows][k] int8, then [rows][k/32][2] f32 meta)
+int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStream_t s);
+int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+          cudaStream_t s);
+
 // device status words of the kernel files (bit 0: a bounded wait gave up)
+unsigned int status_q8(bool clear);
 unsigned int status_mv(bool clear);
 unsigned int status_gemm(bool clear);
 unsigned int status_mx(bool clear);

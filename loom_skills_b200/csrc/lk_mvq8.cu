@@ -1,0 +1,587 @@
+// Decode matvec with int8 activations -- the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518):
+//
+//   g_quant_q8 (gen_llm.py:683-750)   x [rows][k] -> codes int8 [rows][k/32][32], then at byte rows*k the group meta
+//                                     [rows][k/32][2] f32 = (f16-rounded d, sum of codes); d = amax/127, q = round(x/d)
+//   g_mv_{fmt}_q8 (gen_llm.py:1159-1378, @g_<fmt>_icodes :521-680)
+//                                     y[t][n] (+)= sum over 32-groups g of  wscale_g * d_x[g] * dot(wcode_g, xcode_g)
+//                                                                           - wmin_g  * d_x[g] * sum(xcode_g)
+//
+// k_mv_q8 contracts the 4-bit weight codes with the int8 activation codes by dp4a (4 products per instruction, integer
+// exact), so a weight value costs about one instruction: a nibble mask per 4 values and a dp4a per 4 values. The high
+// nibbles are used in place (16 * code, 0..240): their group's integer dot is 16x and the 1/16 goes into that group's
+// f32 scale. Per 32-group the integer dot is scaled once in f32.
+//
+// CTA = 1 producer warp + 8 consumer warps, 64 weight rows, a K-range of 256-value chunks:
+//   producer   TMA: per chunk one box of 64 rows x 144 bytes of packed weights, the chunk's activation codes
+//              [tokens][256] and group meta [tokens][16 f32], into a 4-stage mbarrier ring. It issues the weight boxes
+//              of the first stages before griddepcontrol.wait -- weights never depend on the previous kernel -- so
+//              under programmatic dependent launch the weight stream starts while the previous kernel finishes.
+//   consumers  thread = (64-byte page / block pair p of the chunk, one row); partial sums over the 4 threads of a
+//              row are combined by shuffles at the end. Small stages (37 KB of ring) keep 6 CTAs = 54 warps on an SM:
+//              the per-thread work is a short dependent chain, so latency is hidden by warps, not by ILP alone.
+//   split-K    small N runs S CTAs per row tile as one thread-block cluster; their partial sums meet in CTA 0's
+//              shared memory (distributed shared memory reads, fixed order: deterministic).
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
+             int box_cols, int box_rows, CUtensorMapSwizzle swz);
+
+namespace {
+
+constexpr int kQRows = 64;
+constexpr int kQConsumers = 8;
+constexpr int kQThreads = 32 * (1 + kQConsumers);
+constexpr int kQStages = 4;
+constexpr int kQWBytes = kQRows * kChunkBytes;   // 9216
+constexpr int kQRpt = kQRows * 4 / (32 * kQConsumers);   // rows per consumer thread
+constexpr int kQRowStride = kQRows / kQRpt;
+
+LK_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LK_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+LK_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {   // unsigned bytes of a . signed bytes of b + c
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// exact int -> float for |v| < 2^22 without a conversion instruction
+LK_DEV float i2f_small(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
+LK_DEV float u6_to_f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+LK_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+LK_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+LK_DEV float ld_dsmem_f32(const float* local_addr, uint32_t rank) {
+  uint32_t a = smem_u32(local_addr), r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+  return v;
+}
+
+struct Q8Args {
+  float* y;
+  int n, k, ntok, accumulate;
+  int nchunks, splits, cps;   // chunks of 256, CTAs per row tile (cluster size), chunks per split
+};
+
+template <int TOKB>
+constexpr int q8_stage_bytes() {
+  return (kQWBytes + TOKB * 256 + TOKB * 64 + 127) / 128 * 128;
+}
+
+// The four 16-byte x code words of token t for groups (2p, 2p+1) of the staged chunk, and their meta.
+template <int FMT, int TOKB>
+__global__ void __launch_bounds__(kQThreads)
+    k_mv_q8(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+            const __grid_constant__ CUtensorMap mmap, const Q8Args p) {
+  constexpr int kStage = q8_stage_bytes<TOKB>();
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kQStages * kStage);
+  uint64_t* empty = full + kQStages;
+  float* red = reinterpret_cast<float*>(empty + kQStages);   // [TOKB][kQRows] partial sums (split-K)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.y * kQRows;
+  const int split = blockIdx.x;
+  const int c0 = split * p.cps;
+  const int nst = max(0, min(p.nchunks, c0 + p.cps) - c0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kQStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kQConsumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      griddep_launch();
+      prefetch_tensormap(&wmap);
+      const uint32_t bytes = kQWBytes + TOKB * 256 + TOKB * 64;
+      const int pre = min(kQStages, nst);
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], bytes);
+        tma_load_2d(smem + i * kStage, &wmap, (c0 + i) * (kChunkBytes / 4), row0, &full[i]);
+      }
+      griddep_wait();   // activations come from the previous kernel
+      for (int i = 0; i < pre; ++i) {
+        tma_load_2d(smem + i * kStage + kQWBytes, &xmap, (c0 + i) * 256, 0, &full[i]);
+        tma_load_2d(smem + i * kStage + kQWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[i]);
+      }
+      for (int i = pre; i < nst; ++i) {
+        const int s = i % kQStages;
+        if (!mbar_wait(&empty[s], ((i / kQStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        mbar_expect_tx(&full[s], bytes);
+        uint8_t* st = smem + s * kStage;
+        tma_load_2d(st, &wmap, (c0 + i) * (kChunkBytes / 4), row0, &full[s]);
+        tma_load_2d(st + kQWBytes, &xmap, (c0 + i) * 256, 0, &full[s]);
+        tma_load_2d(st + kQWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[s]);
+      }
+    }
+    __syncwarp();
+  } else {
+    griddep_wait();
+    const int ct = threadIdx.x - 32;
+    const int pg = ct & 3, rs = ct >> 2;
+    const int ntok = min(p.ntok, TOKB);
+    float acc[kQRpt][TOKB];
+#pragma unroll
+    for (int r = 0; r < kQRpt; ++r)
+#pragma unroll
+      for (int t = 0; t < TOKB; ++t) acc[r][t] = 0.f;
+
+    for (int i = 0; i < nst; ++i) {
+      const int s = i % kQStages;
+      if (!mbar_wait(&full[s], (i / kQStages) & 1)) atomicOr(&g_status, 1u);
+      const uint8_t* st = smem + s * kStage;
+      const uint8_t* xs = st + kQWBytes;
+      const float* ms = reinterpret_cast<const float*>(st + kQWBytes + TOKB * 256);
+#pragma unroll
+      for (int rr = 0; rr < kQRpt; ++rr) {
+        const uint8_t* wr = st + (rs + kQRowStride * rr) * kChunkBytes;
+        if (FMT == LK_Q4_K) {
+          // page pg = groups 2pg (low nibbles) and 2pg + 1 (high nibbles) of the super-block
+          const uint4 hd = *reinterpret_cast<const uint4*>(wr);
+          const uint4 q0 = *reinterpret_cast<const uint4*>(wr + 16 + 32 * pg);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(wr + 32 + 32 * pg);
+          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          uint32_t sc0, m0, sc1, m1;
+          q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * pg, sc0, m0);
+          q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * pg + 1, sc1, m1);
+          const float d = h2f(uint16_t(hd.x & 0xffffu)), dmin = h2f(uint16_t(hd.x >> 16));
+          const float ds0 = d * u6_to_f(sc0), ds1 = d * u6_to_f(sc1) * 0.0625f;   // high nibbles: 16 x code
+          const float dm0 = dmin * u6_to_f(m0), dm1 = dmin * u6_to_f(m1);
+#pragma unroll
+          for (int t = 0; t < TOKB; ++t) {
+            if (t >= ntok) break;
+            const uint4* xw = reinterpret_cast<const uint4*>(xs + t * 256 + 64 * pg);
+            const uint4 xa0 = xw[0], xa1 = xw[1], xb0 = xw[2], xb1 = xw[3];
+            const float4 mt = *reinterpret_cast<const float4*>(ms + t * 16 + 4 * pg);   // d0, sum0, d1, sum1
+            const uint32_t xa[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+            const uint32_t xb[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
+            int i0 = 0, i1 = 0, i2 = 0, i3 = 0;   // four independent dp4a chains
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              i0 = dp4a_us(w[j] & 0x0F0F0F0Fu, xa[j], i0);
+              i1 = dp4a_us(w[j] & 0xF0F0F0F0u, xb[j], i1);
+              i2 = dp4a_us(w[j + 1] & 0x0F0F0F0Fu, xa[j + 1], i2);
+              i3 = dp4a_us(w[j + 1] & 0xF0F0F0F0u, xb[j + 1], i3);
+            }
+            acc[rr][t] += mt.x * (ds0 * i2f_small(i0 + i2) - dm0 * mt.y) +
+                          mt.z * (ds1 * i2f_small(i1 + i3) - dm1 * mt.w);
+          }
+        } else {
+          // block pair pg = blocks 2pg (bytes 36pg..+17: d, then codes starting 2 bytes into a word) and 2pg + 1
+          const uint32_t* wv = reinterpret_cast<const uint32_t*>(wr + 36 * pg);
+          uint32_t v[9];
+#pragma unroll
+          for (int j = 0; j < 9; ++j) v[j] = wv[j];
+          uint32_t qa[4], qb[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            qa[j] = __funnelshift_r(v[j], v[j + 1], 16);   // codes of the even block, realigned
+            qb[j] = v[5 + j];
+          }
+          const float da = h2f(uint16_t(v[0] & 0xffffu)), db = h2f(uint16_t(v[4] >> 16));
+#pragma unroll
+          for (int t = 0; t < TOKB; ++t) {
+            if (t >= ntok) break;
+            const uint4* xw = reinterpret_cast<const uint4*>(xs + t * 256 + 64 * pg);
+            const uint4 xa0 = xw[0], xa1 = xw[1], xb0 = xw[2], xb1 = xw[3];
+            const float4 mt = *reinterpret_cast<const float4*>(ms + t * 16 + 4 * pg);
+            // block a: elements 0-15 = low nibbles (x words xa0), 16-31 = high nibbles (xa1)
+            const uint32_t xal[4] = {xa0.x, xa0.y, xa0.z, xa0.w}, xah[4] = {xa1.x, xa1.y, xa1.z, xa1.w};
+            const uint32_t xbl[4] = {xb0.x, xb0.y, xb0.z, xb0.w}, xbh[4] = {xb1.x, xb1.y, xb1.z, xb1.w};
+            int la = 0, ha = 0, lb = 0, hb = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (FMT == LK_Q4_0) {
+                la = dp4a_us(qa[j] & 0x0F0F0F0Fu, xal[j], la);
+                ha = dp4a_us(qa[j] & 0xF0F0F0F0u, xah[j], ha);
+                lb = dp4a_us(qb[j] & 0x0F0F0F0Fu, xbl[j], lb);
+                hb = dp4a_us(qb[j] & 0xF0F0F0F0u, xbh[j], hb);
+              }
+            }
+            // Q4_0 values are code - 8: sum((q - 8) x) = dot - 8 sum(x)
+            const int ca = la + (ha >> 4) - 8 * int(mt.y), cb = lb + (hb >> 4) - 8 * int(mt.w);
+            acc[rr][t] += da * mt.x * i2f_small(ca) + db * mt.z * i2f_small(cb);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // the four threads of a row hold its four page / block-pair partial sums
+#pragma unroll
+    for (int rr = 0; rr < kQRpt; ++rr)
+#pragma unroll
+      for (int t = 0; t < TOKB; ++t) {
+        acc[rr][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[rr][t], 1);
+        acc[rr][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[rr][t], 2);
+      }
+    if (p.splits > 1) {
+      if (pg == 0)
+#pragma unroll
+        for (int rr = 0; rr < kQRpt; ++rr)
+#pragma unroll
+          for (int t = 0; t < TOKB; ++t) red[t * kQRows + rs + kQRowStride * rr] = acc[rr][t];
+    } else if (pg == 0) {
+#pragma unroll
+      for (int rr = 0; rr < kQRpt; ++rr) {
+        const int row = row0 + rs + kQRowStride * rr;
+        if (row >= p.n) continue;
+#pragma unroll
+        for (int t = 0; t < TOKB; ++t) {
+          if (t >= ntok) break;
+          float* dst = p.y + int64_t(t) * p.n + row;
+          *dst = p.accumulate ? *dst + acc[rr][t] : acc[rr][t];
+        }
+      }
+    }
+  }
+  if (p.splits > 1) {
+    // every CTA of the cluster reaches both barriers (no early exit above)
+    cluster_sync();
+    if (cluster_ctarank() == 0) {
+      for (int e = threadIdx.x; e < TOKB * kQRows; e += kQThreads) {
+        const int t = e / kQRows, r = e % kQRows, row = row0 + r;
+        if (t >= p.ntok || row >= p.n) continue;
+        float v = 0.f;
+        for (int c = 0; c < p.splits; ++c) v += ld_dsmem_f32(red + e, uint32_t(c));
+        float* dst = p.y + int64_t(t) * p.n + row;
+        *dst = p.accumulate ? *dst + v : v;
+      }
+    }
+    cluster_sync();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Single-token Q4_K matvec over whole rows (K % 4096 == 0): a persistent grid streams stages of SR consecutive rows
+// (one contiguous bulk copy each) round-robin over the CTAs. WPR warps share a row; lane l of row-warp w owns the two
+// (chunk, page) units w*64 + l and w*64 + l + 32 for every row, so its activation codes and group meta are loaded
+// into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles (and, when WPR > 1,
+// the row's warps meet in shared memory).
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kRStages = 4;
+constexpr int kRowsCtasPerSm = 8;
+
+// the Q4_K (scale, min) pairs of groups (2pg, 2pg + 1) as "2^23 + value" floats: f[0..1] scales, f[2..3] minima.
+// pg is constant per thread: byte half h = pg & 1 of each scale word, the 4-bit-plus-2-bit form for pg >= 2.
+LK_DEV void q4k_pair_magic(uint4 hd, uint32_t hsel, uint32_t big_mask, float (&f)[4]) {
+  const uint32_t a = prmt(hd.y, 0u, hsel), b = prmt(hd.z, 0u, hsel), c = prmt(hd.w, 0u, hsel);
+  const uint32_t sc_lo = a & 0x3F3Fu, m_lo = b & 0x3F3Fu;
+  const uint32_t sc_hi = (c & 0x0F0Fu) | ((a >> 2) & 0x3030u);
+  const uint32_t m_hi = ((c >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u);
+  const uint32_t v = ((sc_hi & big_mask) | (sc_lo & ~big_mask)) | (((m_hi & big_mask) | (m_lo & ~big_mask)) << 16);
+  f[0] = __uint_as_float(prmt(v, 0x4B000000u, 0x7650u));
+  f[1] = __uint_as_float(prmt(v, 0x4B000000u, 0x7651u));
+  f[2] = __uint_as_float(prmt(v, 0x4B000000u, 0x7652u));
+  f[3] = __uint_as_float(prmt(v, 0x4B000000u, 0x7653u));
+}
+
+struct RowArgs {
+  const uint8_t* w;
+  const uint8_t* xq;   // codes [1][k] then meta [1][k/32][2]
+  float* y;
+  int n, k, accumulate;
+  int64_t rb;          // bytes per packed row
+  int sr;              // rows per stage
+  int nstages;         // ceil(n / sr)
+};
+
+template <int WPR>
+__global__ void __launch_bounds__(32 * (1 + 4 * WPR))
+    k_mv_q8_rows(const RowArgs p) {
+  constexpr int kCW = 4 * WPR;                 // consumer warps
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int stage_bytes = int((int64_t(p.sr) * p.rb + 127) / 128 * 128);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRStages * stage_bytes);
+  uint64_t* empty = full + kRStages;
+  float* part = reinterpret_cast<float*>(empty + kRStages);   // [kCW] per-stage warp partials
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kCW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int my_stages = p.nstages > int(blockIdx.x) ? (p.nstages - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      griddep_launch();
+      for (int i = 0; i < my_stages; ++i) {
+        const int s = i % kRStages;
+        if (i >= kRStages && !mbar_wait(&empty[s], ((i / kRStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        const int st = int(blockIdx.x) + i * int(gridDim.x);
+        const int rows = min(p.sr, p.n - st * p.sr);
+        const uint32_t bytes = uint32_t(int64_t(rows) * p.rb);
+        mbar_expect_tx(&full[s], bytes);
+        bulk_g2s(smem + s * stage_bytes, p.w + int64_t(st) * p.sr * p.rb, bytes, &full[s]);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int cw = warp - 1;                   // consumer warp
+    const int rslot = cw / WPR, wpart = cw % WPR;
+    const int cp0 = wpart * 64 + lane;         // this lane's units: cp0 and cp0 + 32
+    griddep_wait();                            // the activations come from the previous kernel
+    uint32_t xa[2][8], xb[2][8];
+    float dx0[2], dx1[2], b0[2], b1[2];
+    const float* meta = reinterpret_cast<const float*>(p.xq + p.k);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int cp = cp0 + 32 * u, c = cp >> 2, pg = cp & 3;
+      const uint4* xw = reinterpret_cast<const uint4*>(p.xq + c * 256 + 64 * pg);
+      const uint4 v0 = __ldg(xw), v1 = __ldg(xw + 1), v2 = __ldg(xw + 2), v3 = __ldg(xw + 3);
+      xa[u][0] = v0.x; xa[u][1] = v0.y; xa[u][2] = v0.z; xa[u][3] = v0.w;
+      xa[u][4] = v1.x; xa[u][5] = v1.y; xa[u][6] = v1.z; xa[u][7] = v1.w;
+      xb[u][0] = v2.x; xb[u][1] = v2.y; xb[u][2] = v2.z; xb[u][3] = v2.w;
+      xb[u][4] = v3.x; xb[u][5] = v3.y; xb[u][6] = v3.z; xb[u][7] = v3.w;
+      const float4 mt = __ldg(reinterpret_cast<const float4*>(meta + c * 16 + 4 * pg));
+      dx0[u] = mt.x;
+      dx1[u] = mt.z * 0.0625f;                 // high nibbles: the dot is 16 x
+      b0[u] = mt.x * mt.y;
+      b1[u] = mt.z * mt.w;
+    }
+    const int pg = lane & 3;                   // both units share the page (cp0 and cp0 + 32 differ by 8 chunks)
+    const uint32_t hsel = (pg & 1) ? 0x4432u : 0x4410u;
+    const uint32_t big = (pg >> 1) ? 0xFFFFFFFFu : 0u;
+    for (int i = 0; i < my_stages; ++i) {
+      const int s = i % kRStages;
+      if (!mbar_wait(&full[s], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
+      const int st = int(blockIdx.x) + i * int(gridDim.x);
+      const int row = st * p.sr + rslot;
+      float acc = 0.f;
+      if (row < p.n) {
+        const uint8_t* wr = smem + s * stage_bytes + int64_t(rslot) * p.rb;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = (cp0 + 32 * u) >> 2;
+          const uint8_t* sb = wr + c * kChunkBytes;
+          const uint4 hd = *reinterpret_cast<const uint4*>(sb);
+          const uint4 q0 = *reinterpret_cast<const uint4*>(sb + 16 + 32 * pg);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(sb + 32 + 32 * pg);
+          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          float f[4];
+          q4k_pair_magic(hd, hsel, big, f);
+          const float d = h2f(uint16_t(hd.x & 0xffffu)), dmin = h2f(uint16_t(hd.x >> 16));
+          const float nd = -8388608.0f * d, ndm = -8388608.0f * dmin;
+          int i0 = 0, i1 = 0, i2 = 0, i3 = 0;
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            i0 = dp4a_us(w[j] & 0x0F0F0F0Fu, xa[u][j], i0);
+            i1 = dp4a_us(w[j] & 0xF0F0F0F0u, xb[u][j], i1);
+            i2 = dp4a_us(w[j + 1] & 0x0F0F0F0Fu, xa[u][j + 1], i2);
+            i3 = dp4a_us(w[j + 1] & 0xF0F0F0F0u, xb[u][j + 1], i3);
+          }
+          // d*sc = fma(d, 2^23 + sc, -d*2^23), exact; the same for the minima
+          acc += fmaf(d, f[0], nd) * (dx0[u] * i2f_small(i0 + i2)) + fmaf(d, f[1], nd) * (dx1[u] * i2f_small(i1 + i3)) -
+                 fmaf(dmin, f[2], ndm) * b0[u] - fmaf(dmin, f[3], ndm) * b1[u];
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (WPR > 1) {
+        if (lane == 0) part[cw] = acc;
+        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
+        if (wpart == 0 && lane == 0 && row < p.n) {
+          float v = 0.f;
+#pragma unroll
+          for (int j = 0; j < WPR; ++j) v += part[rslot * WPR + j];
+          p.y[row] = p.accumulate ? p.y[row] + v : v;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
+      } else if (lane == 0 && row < p.n) {
+        p.y[row] = p.accumulate ? p.y[row] + acc : acc;
+      }
+    }
+  }
+}
+
+template <int WPR>
+int launch_rows(RowArgs a, cudaStream_t s) {
+  const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
+  const int smem = kRStages * stage_bytes + 2 * kRStages * 8 + 4 * WPR * 4;
+  auto kern = k_mv_q8_rows<WPR>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + 4 * WPR), smem) != cudaSuccess ||
+      per_sm < 1)
+    return LK_ECUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaLaunchConfig_t cfg = {};
+  // at most kRowsCtasPerSm CTAs per SM: the rest of the SM stays free for the next kernel's CTAs, which (under
+  // programmatic dependent launch) start streaming their weights while this grid finishes
+  cfg.gridDim = dim3(min(a.nstages, sms * min(per_sm, kRowsCtasPerSm)), 1, 1);
+  cfg.blockDim = dim3(32 * (1 + 4 * WPR), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// g_quant_q8: one warp per 32-value group, 8 groups per CTA
+template <int XT>
+__global__ void __launch_bounds__(256) k_quant_q8(int rows, int k, const void* x, int8_t* codes, float* meta) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = k / 32;
+  const int g = blockIdx.x * 8 + warp, row = blockIdx.y;
+  griddep_launch();   // the next matvec may start streaming its weights now
+  griddep_wait();     // x comes from the previous kernel
+  if (g >= groups) return;
+  const int64_t idx = int64_t(row) * k + g * 32 + lane;
+  const float v = XT == LK_BF16 ? bf2f(static_cast<const uint16_t*>(x)[idx]) : static_cast<const float*>(x)[idx];
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float d = amax / 127.0f;
+  int q = 0;
+  if (amax > 0.0f) q = int(roundf(v / d));   // ordered compare: a NaN maximum gives code 0, like the reference
+  codes[idx] = int8_t(q);
+  int sum = q;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+  if (lane == 0) {
+    float* m = meta + (int64_t(row) * groups + g) * 2;
+    m[0] = __half2float(__float2half_rn(d));
+    m[1] = float(sum);
+  }
+}
+
+template <int FMT, int TOKB>
+int launch_q8(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& mm, const Q8Args& a, int row_tiles,
+              cudaStream_t s) {
+  constexpr int smem = kQStages * q8_stage_bytes<TOKB>() + 2 * kQStages * 8 + TOKB * kQRows * 4;
+  auto kern = k_mv_q8<FMT, TOKB>;
+  static unsigned configured = 0;
+  if (!once_per_device(configured)) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, row_tiles, 1);
+  cfg.blockDim = dim3(kQThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (a.splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = a.splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, wm, xm, mm, a) == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+}  // namespace
+
+int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStream_t s) {
+  int8_t* codes = reinterpret_cast<int8_t*>(xq);
+  float* meta = reinterpret_cast<float*>(xq + int64_t(rows) * k);
+  dim3 grid((k / 32 + 7) / 8, rows);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = x_dtype == LK_BF16 ? cudaLaunchKernelEx(&cfg, k_quant_q8<LK_BF16>, rows, k, x, codes, meta)
+                                     : cudaLaunchKernelEx(&cfg, k_quant_q8<LK_F32>, rows, k, x, codes, meta);
+  return e == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+          cudaStream_t s) {
+  if (fmt != LK_Q4_K && fmt != LK_Q4_0) return LK_EUNSUPPORTED;
+  const int64_t rb = int64_t(k) / 256 * kChunkBytes;
+  if (fmt == LK_Q4_K && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096) {
+    RowArgs ra{};
+    ra.w = static_cast<const uint8_t*>(w);
+    ra.xq = xq;
+    ra.y = y;
+    ra.n = n;
+    ra.k = k;
+    ra.accumulate = accumulate;
+    ra.rb = rb;
+    ra.sr = 4;
+    ra.nstages = (n + 3) / 4;
+    switch (k / 4096) {
+      case 1: return launch_rows<1>(ra, s);
+      case 2: return launch_rows<2>(ra, s);
+      case 3: return launch_rows<3>(ra, s);
+    }
+  }
+  const int tokb = tokens <= 1 ? 1 : 8;
+  CUtensorMap wm;
+  int rc = make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, n, rb / 4, kChunkBytes / 4, kQRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc != LK_OK) return rc;
+  Q8Args a{};
+  a.n = n;
+  a.k = k;
+  a.accumulate = accumulate;
+  a.nchunks = k / 256;
+  const int row_tiles = (n + kQRows - 1) / kQRows;
+  // split K until about one full wave of CTAs (6 per SM on 148 SMs), at most 8 CTAs per cluster
+  int splits = (888 + row_tiles - 1) / row_tiles;
+  splits = max(1, min(splits, min(8, a.nchunks)));
+  a.cps = (a.nchunks + splits - 1) / splits;
+  a.splits = (a.nchunks + a.cps - 1) / a.cps;
+  const float* meta = reinterpret_cast<const float*>(xq + int64_t(tokens) * k);
+  for (int t0 = 0; t0 < tokens; t0 += 8) {   // token tiles of 8 (one when tokens == 1)
+    const int nt = min(8, tokens - t0);
+    CUtensorMap xm, mm;
+    rc = make_map(&xm, xq + int64_t(t0) * k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, nt, k, 256, tokb,
+                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc == LK_OK)
+      rc = make_map(&mm, meta + int64_t(t0) * (k / 16), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, nt, k / 16, 16, tokb,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != LK_OK) return rc;
+    a.y = y + int64_t(t0) * n;
+    a.ntok = nt;
+    if (tokb == 1)
+      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 1>(wm, xm, mm, a, row_tiles, s)
+                          : launch_q8<LK_Q4_0, 1>(wm, xm, mm, a, row_tiles, s);
+    else
+      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 8>(wm, xm, mm, a, row_tiles, s)
+                          : launch_q8<LK_Q4_0, 8>(wm, xm, mm, a, row_tiles, s);
+    if (rc != LK_OK) return rc;
+  }
+  return LK_OK;
+}
+
+LK_STATUS_READER(status_q8)
+
+}  // namespace lk

@@ -275,3 +275,31 @@ def moe_ffn_decode_noalloc(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm
                                                _ptr(logits), _ptr(x), _DT[x.dtype], _ptr(w_gu), _ptr(w_dn), _ptr(y),
                                                _stream()), "lk_moe_ffn_decode_noalloc")
     return y
+
+
+def quant_q8(x, out=None):
+    """g_quant_q8: x [rows][k] (f32 / bf16) -> xq uint8 holding int8 codes [rows][k], then the group meta
+    [rows][k/32][2] f32 (f16-rounded d, sum of codes) -- the reference's single-buffer layout."""
+    _cuda(x, out)
+    x = x.contiguous()
+    rows, k = x.shape
+    xq = out if out is not None else torch.empty(rows * k + rows * (k // 32) * 8, dtype=torch.uint8, device=x.device)
+    L.check(L.load().lk_quant_q8(rows, k, _ptr(x), _DT[x.dtype], _ptr(xq), _stream()), "lk_quant_q8")
+    return xq
+
+
+def q8_views(xq, rows, k):
+    """(codes int8 [rows][k], meta f32 [rows][k/32][2]) views of a quant_q8 buffer."""
+    codes = xq[:rows * k].view(torch.int8).view(rows, k)
+    meta = xq[rows * k:rows * k + rows * (k // 32) * 8].view(torch.float32).view(rows, k // 32, 2)
+    return codes, meta
+
+
+def mv_q8(fmt, w, xq, n, k, tokens, y=None, accumulate=False):
+    """Decode matvec on int8 activations (quant_q8's buffer for `tokens` rows): y[t][n] (+)= x_q8[t] . W[n]."""
+    _cuda(w, xq, y)
+    if y is None:
+        y = torch.empty(tokens, n, dtype=torch.float32, device=xq.device)
+    L.check(L.load().lk_mv_q8(_fmt(fmt), n, k, tokens, 1 if accumulate else 0, _ptr(xq), _ptr(w), _ptr(y),
+                              _stream()), "lk_mv_q8")
+    return y

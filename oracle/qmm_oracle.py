@@ -248,6 +248,31 @@ def _f32_exponent_field(a):
     return (np.asarray(a, np.float32).view(np.uint32) >> 23) & 255
 
 
+def quant_q8(x):
+    """g_quant_q8 (gen_llm.py:683-750; llama.cpp quantize_q8_1): per 32-value group d = amax / 127 (f32 division),
+    q = round(x / d) half away from zero (0 when amax == 0), codes int8 [rows][k]; meta f32 [rows][k/32][2] =
+    (f32(f16(d)), sum of q). make_kernel_tests.py:32-40 (q8_ref) dequantises with the same f16-rounded d."""
+    x = np.asarray(x, np.float32)
+    rows, k = x.shape
+    g = x.reshape(rows, k // 32, 32)
+    amax = np.abs(g).max(-1, keepdims=True)
+    d = (amax / np.float32(127)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        v = (g / d).astype(np.float32)
+    t = np.trunc(v)
+    r = t + np.where(np.abs(v - t) >= np.float32(0.5), np.sign(v), np.float32(0))   # roundf: halves away from zero
+    q = np.where(amax > 0, r, 0).astype(np.int8)
+    meta = np.stack([d[..., 0].astype(np.float16).astype(np.float32), q.astype(np.int32).sum(-1).astype(np.float32)],
+                    -1)
+    return q.reshape(rows, k), meta.astype(np.float32)
+
+
+def dequant_q8(codes, meta):
+    """The activations the _q8 matvecs contract with: code * f16-rounded d per 32-value group."""
+    rows, k = codes.shape
+    return (codes.reshape(rows, k // 32, 32).astype(np.float64) * meta[..., :1].astype(np.float64)).reshape(rows, k)
+
+
 def row_scale_f16(x):
     """g_row_scale_f16 (gen_llm.py:1843-1912): per row e = clamp(exp(max|x|) - 127 - 13, 0, 100), s = 2^-e,
     x16 = f16(x * s), scales[row] = (s, 2^e)."""

@@ -132,6 +132,21 @@ def main(ref):
         out[f"gemm_{fmt}_scales"] = np.stack([s, inv], -1)
         out[f"gemm_{fmt}_y"] = (x16.astype(np.float64) @ W.T) * inv[:, None].astype(np.float64)
 
+    # int8 activations: make_kernel_tests.py:32-40 (q8_ref), taken out of the script by its syntax tree (the module
+    # itself runs a model build at import)
+    import ast
+    src_path = os.path.join(starter, "make_kernel_tests.py")
+    tree = ast.parse(open(src_path).read())
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "q8_ref")
+    ns = {"np": np}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), src_path, "exec"), ns)
+    rng = np.random.default_rng(23)
+    xq = np.concatenate([rng.standard_normal((5, 512)) * rng.choice([1e-3, 1.0, 300.0], (5, 1)),
+                         np.zeros((1, 512))]).astype(np.float32)
+    xq[2, 64:96] = 0.0    # an all-zero group inside a live row
+    out["q8_in"] = xq
+    out["q8_deq"] = ns["q8_ref"](xq).astype(np.float32)
+
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **out)
     print("wrote", os.path.join(HERE, "golden.npz"), sum(a.nbytes for a in out.values()), "bytes uncompressed")
 

@@ -1,0 +1,87 @@
+"""GPU parity of the int8-activation decode path (the reference's default ACT_Q8=1 numerics) through the C ABI:
+g_quant_q8 bit-exact against the oracle (codes and group meta), and the dp4a matvec against the float64 product of
+the dequantised weights with the same int8 activations (relative L2 <= 1e-3; integer dots are exact, so the
+difference is f32 rounding of the per-group scaling, ~1e-7)."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle import qmm_oracle as O  # noqa: E402
+
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from loom_skills_b200 import ops as _ops
+    return _ops
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+QUANT = {"q4_0": O.quantize_q4_0, "q4_k": O.quantize_q4_k}
+
+
+class TestQuantQ8:
+    @pytest.mark.parametrize("dtype", ["f32", "bf16"])
+    def test_bit_exact(self, ops, golden, dtype):
+        rng = np.random.default_rng(3)
+        x = np.concatenate([golden["q8_in"][:, :512],
+                            (rng.standard_normal((7, 512)) * rng.choice([1e-4, 1.0, 5e3], (7, 1)))]).astype(np.float32)
+        x[3, 100:132] = 0.0
+        xt = dev(x)
+        if dtype == "bf16":
+            xt = xt.to(torch.bfloat16)
+            x = xt.float().cpu().numpy()
+        xq = ops.quant_q8(xt)
+        codes, meta = ops.q8_views(xq, x.shape[0], x.shape[1])
+        rc, rm = O.quant_q8(x)
+        assert np.array_equal(host(codes), rc)
+        assert np.array_equal(host(meta).view(np.uint32), rm.view(np.uint32))
+
+
+class TestMvQ8:
+    @pytest.mark.parametrize("fmt", ["q4_0", "q4_k"])
+    @pytest.mark.parametrize("n,k,tokens", [(256, 256, 1), (4096, 4096, 1), (1000, 2048, 3), (64, 12288, 8),
+                                            (300, 1024, 13), (1024, 4096, 1)])
+    def test_vs_oracle(self, ops, fmt, n, k, tokens):
+        rng = np.random.default_rng(n + k + tokens)
+        w = QUANT[fmt]((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        xq = ops.quant_q8(dev(x))
+        codes, meta = ops.q8_views(xq, tokens, k)
+        y = host(ops.mv_q8(fmt, dev(w), xq, n, k, tokens))
+        ref = O.mv_ref(fmt, w, O.dequant_q8(host(codes), host(meta)), n, k)
+        assert O.rel_l2(y, ref) < TOL, O.rel_l2(y, ref)
+        assert ops.device_status() == 0
+
+    @pytest.mark.parametrize("fmt", ["q4_0", "q4_k"])
+    def test_golden_weights_and_accumulate(self, ops, golden, fmt):
+        w, x = golden[f"mv_{fmt}_w"], golden[f"mv_{fmt}_x"]
+        n, k = w.shape[0], x.shape[1]
+        xq = ops.quant_q8(dev(x))
+        codes, meta = ops.q8_views(xq, x.shape[0], k)
+        xd = O.dequant_q8(host(codes), host(meta))
+        y0 = np.random.default_rng(1).standard_normal((x.shape[0], n)).astype(np.float32)
+        y = ops.mv_q8(fmt, dev(w), xq, n, k, x.shape[0], y=dev(y0), accumulate=True)
+        ref = O.mv_ref(fmt, w, xd, n, k, y_old=y0)
+        assert O.rel_l2(host(y), ref) < TOL
+        # the q8 activations stay within the reference's own tolerance of the f32 product (make_kernel_tests q8 path)
+        assert O.rel_l2(host(ops.mv_q8(fmt, dev(w), xq, n, k, x.shape[0])), golden[f"mv_{fmt}_y"]) < 2e-2
+
+    def test_unsupported_and_empty(self, ops):
+        xq = torch.zeros(256 + 8 * 8, dtype=torch.uint8, device="cuda")
+        w = torch.zeros(4, 144, dtype=torch.uint8, device="cuda")
+        with pytest.raises(ops.L.LkError):
+            ops.mv_q8("iq4_nl", w, xq, 4, 256, 1)
+        assert ops.mv_q8("q4_k", w, xq, 4, 256, 0).shape == (0, 4)

@@ -191,3 +191,20 @@ class TestMoE:
         rm2[rows[0]], rm2[-1] = -1, rm2[rows[0]]
         assert O.check_bucket(ids, E, mt, ti, rm2, pos2, live) is not None
         assert e0 >= 0
+
+
+class TestQuantQ8:
+    def test_matches_reference_q8_ref(self, golden):
+        """quant_q8 + dequant_q8 == make_kernel_tests.py q8_ref (numerically; q8_ref's float codes can be -0.0)."""
+        codes, meta = O.quant_q8(golden["q8_in"])
+        got = O.dequant_q8(codes, meta).astype(np.float32)
+        assert np.array_equal(got, golden["q8_deq"])
+
+    def test_rounding_and_zero_groups(self):
+        x = np.zeros((1, 64), np.float32)
+        x[0, 0] = 127.0                       # d = 1: codes are round(x) half away from zero
+        x[0, 1:6] = [0.5, -0.5, 1.5, -2.5, 0.49999997]
+        codes, meta = O.quant_q8(x)
+        assert codes[0, :6].tolist() == [127, 1, -1, 2, -3, 0]
+        assert meta[0, 0, 0] == 1.0 and meta[0, 0, 1] == 127 + 1 - 1 + 2 - 3
+        assert (codes[0, 32:] == 0).all() and meta[0, 1].tolist() == [0.0, 0.0]
