@@ -8,8 +8,8 @@ token (M=1) through the six projections of a stack of `--layers` distinct weight
 quantised to int8 (g_quant_q8) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
 weight GB/s; the line also carries the bf16-activation decode, the prefill TFLOP/s at M=2048 over the same shapes
 (step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
-MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 48 matvecs per decode
-step; the kernels chain with programmatic dependent launch).
+MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 32 matvec launches per
+decode step -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
@@ -357,7 +357,7 @@ def run_ours(args):
     ys = [{name: torch.empty(1, n, device=dev) for name, _, n in SHAPES} for _ in range(args.layers)]
     wbytes_layer = sum(t.numel() for t in wstack[0].values())
     act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
-    launches_per_step = args.layers * len(SHAPES)
+    launches_per_step = args.layers * 4   # matvec launches: q|k|v, o, gate_up, down
     step_bytes = args.layers * wbytes_layer
 
     # int8 activations per layer: the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518)
@@ -368,8 +368,12 @@ def run_ours(args):
             ops.quant_q8(xs[k], out=xq[li][k])
 
     def mv_layer(li):
-        for name, k, n in SHAPES:
-            ops.mv_q8("q4_k", wstack[li][name], xq[li][k], n, k, 1, y=ys[li][name])
+        # q | k | v share the activation: one launch over the three weights (lk_mv_q8_multi)
+        w, y = wstack[li], ys[li]
+        ops.mv_q8_multi("q4_k", [w["q"], w["k"], w["v"]], xq[li][4096], [4096, 1024, 1024], 4096, 1,
+                        ys=[y["q"], y["k"], y["v"]])
+        for name, k, n in SHAPES[3:]:
+            ops.mv_q8("q4_k", w[name], xq[li][k], n, k, 1, y=y[name])
 
     def decode_body():   # one decode step: per layer, quantise the activations, then the six projections
         for li in range(args.layers):
@@ -412,7 +416,7 @@ def run_ours(args):
             clk.mark(False)
         return max_over_ranks(t0.elapsed_time(t1)) / steps
 
-    # ---- decode: device-resident inputs, one graph replay per step (16 quantisations + 48 matvecs)
+    # ---- decode: device-resident inputs, one graph replay per step (16 quantisations + 32 matvec launches)
     dec = Timed(torch, decode_body)
     for _ in range(args.warmup):
         dec.replay()
@@ -421,7 +425,7 @@ def run_ours(args):
     ms = time_steps(dec.replay, args.steps, clk)
     clocks = clk.stop()
     value = world * step_bytes / (ms * 1e-3) / 1e9
-    # the matvec kernel alone: the same 48 launches back to back in one graph, CUDA events around the timed replays
+    # the matvec kernel alone: the same 32 launches back to back in one graph, CUDA events around the timed replays
     mvg = Timed(torch, mv_body)
     for _ in range(args.warmup):
         mvg.replay()
@@ -535,7 +539,7 @@ def run_ours(args):
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
 
-    gpu_launches = args.steps * (launches_per_step + 2 * args.layers)   # 48 matvecs + 16 quantisations per step
+    gpu_launches = args.steps * (launches_per_step + 2 * args.layers)   # 32 matvec + 16 quantisation launches
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
         line = {

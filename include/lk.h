@@ -100,6 +100,12 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
 int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_stream_t stream);
 int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
              lk_stream_t stream);
+/* lk_mv_q8_multi: lk_mv_q8 for up to 4 weights that share one activation (the q | k | v projections of an attention
+ * layer; the reference reaches the same with one fused attn_qkv tensor, gen_llm.py:99-100, 6221): segment g has n[g]
+ * rows in w[g] and writes y[g]. One launch over all segments where the kernel allows, else one per segment.
+ * n, w, y are HOST arrays of nseg entries. */
+int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int tokens,
+                   int accumulate, const uint8_t* xq, lk_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Prefill GEMM (tcgen05 + TMEM). Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704,

@@ -27,6 +27,7 @@ SIGNATURES = {
     "lk_mv": (_I, [_I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
     "lk_quant_q8": (_I, [_I, _I, _P, _I, _P, _P]),
     "lk_mv_q8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "lk_mv_q8_multi": (_I, [_I, _I, _P, _P, _P, _I, _I, _I, _P, _P]),
     "lk_gemm": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "lk_gemm_mxfp4s_f8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lk_moe_route": (_I, [_I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _P, _P, _P]),

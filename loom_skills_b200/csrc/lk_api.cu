@@ -61,6 +61,22 @@ int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* x
   return mv_q8(fmt, n, k, tokens, accumulate, xq, w, y, (cudaStream_t)stream);
 }
 
+int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int tokens,
+                   int accumulate, const uint8_t* xq, lk_stream_t stream) {
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return q4_family(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (nseg <= 0 || nseg > 4 || !n || !w || !y) return LK_EINVAL;
+  if (k <= 0 || tokens < 0 || k % 256) return LK_EINVAL;
+  for (int g = 0; g < nseg; ++g) {
+    if (n[g] <= 0) return LK_EINVAL;
+    if (tokens > 0 && (!w[g] || !y[g])) return LK_EINVAL;
+    if (tokens > 0 && !aligned(w[g], 16)) return LK_EALIGN;
+  }
+  if (tokens == 0) return LK_OK;
+  if (!xq) return LK_EINVAL;
+  if (!aligned(xq, 16)) return LK_EALIGN;
+  return mv_q8_multi(fmt, nseg, n, w, y, k, tokens, accumulate, xq, (cudaStream_t)stream);
+}
+
 int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,
                lk_stream_t stream) {
   if (!w || !out || n_values < 0) return LK_EINVAL;

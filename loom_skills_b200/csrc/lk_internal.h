@@ -64,6 +64,8 @@ int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, cons
 int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStream_t s);
 int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
           cudaStream_t s);
+int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int tokens,
+                int accumulate, const uint8_t* xq, cudaStream_t s);
 
 // device status words of the kernel files (bit 0: a bounded wait gave up)
 unsigned int status_q8(bool clear);

@@ -268,14 +268,13 @@ __global__ void __launch_bounds__(kQThreads)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Single-token Q4_K matvec over whole rows (K % 4096 == 0): a persistent grid streams stages of SR consecutive rows
-// (one contiguous bulk copy each) round-robin over the CTAs. WPR warps share a row; lane l of row-warp w owns the two
-// (chunk, page) units w*64 + l and w*64 + l + 32 for every row, so its activation codes and group meta are loaded
-// into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles (and, when WPR > 1,
-// the row's warps meet in shared memory).
+// Single-token Q4_K matvec over whole rows (K % 4096 == 0): a persistent grid streams stages of 4 consecutive rows
+// (one contiguous bulk copy each) round-robin over the CTAs. Each of the 4 consumer warps owns one row of the stage;
+// lane l owns the K/2048 (chunk, page) units l + 32u of every row, so its activation codes and group meta are loaded
+// into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles and stores y.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRStages = 4;
-constexpr int kRowsCtasPerSm = 8;
+constexpr int kRowWarps = 4;   // consumer warps = rows per stage
 
 // the Q4_K (scale, min) pairs of groups (2pg, 2pg + 1) as "2^23 + value" floats: f[0..1] scales, f[2..3] minima.
 // pg is constant per thread: byte half h = pg & 1 of each scale word, the 4-bit-plus-2-bit form for pg >= 2.
@@ -291,30 +290,42 @@ LK_DEV void q4k_pair_magic(uint4 hd, uint32_t hsel, uint32_t big_mask, float (&f
   f[3] = __uint_as_float(prmt(v, 0x4B000000u, 0x7653u));
 }
 
+constexpr int kMaxSegs = 4;
 struct RowArgs {
-  const uint8_t* w;
+  // up to kMaxSegs weights sharing the activation: segment g has n[g] rows, stages start[g] .. start[g + 1] - 1
+  const uint8_t* w[kMaxSegs];
+  float* y[kMaxSegs];
+  int n[kMaxSegs];
+  int start[kMaxSegs + 1];
+  int nseg;
   const uint8_t* xq;   // codes [1][k] then meta [1][k/32][2]
-  float* y;
-  int n, k, accumulate;
+  int k, accumulate;
   int64_t rb;          // bytes per packed row
   int sr;              // rows per stage
-  int nstages;         // ceil(n / sr)
+  int nstages;         // start[nseg]
 };
+// segment of a global stage, and the stage's first row inside it
+LK_DEV int seg_of(const RowArgs& p, int st, int& row0) {
+  int g = 0;
+#pragma unroll
+  for (int j = 1; j < kMaxSegs; ++j)
+    if (j < p.nseg && st >= p.start[j]) g = j;
+  row0 = (st - p.start[g]) * p.sr;
+  return g;
+}
 
-template <int WPR>
-__global__ void __launch_bounds__(32 * (1 + 4 * WPR))
+template <int UPL>
+__global__ void __launch_bounds__(32 * (1 + kRowWarps))
     k_mv_q8_rows(const RowArgs p) {
-  constexpr int kCW = 4 * WPR;                 // consumer warps
   extern __shared__ __align__(128) uint8_t smem[];
   const int stage_bytes = int((int64_t(p.sr) * p.rb + 127) / 128 * 128);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRStages * stage_bytes);
   uint64_t* empty = full + kRStages;
-  float* part = reinterpret_cast<float*>(empty + kRStages);   // [kCW] per-stage warp partials
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kCW);
+      mbar_init(&empty[i], kRowWarps);
     }
     fence_mbar_init();
   }
@@ -328,24 +339,26 @@ __global__ void __launch_bounds__(32 * (1 + 4 * WPR))
         const int s = i % kRStages;
         if (i >= kRStages && !mbar_wait(&empty[s], ((i / kRStages) - 1) & 1)) atomicOr(&g_status, 1u);
         const int st = int(blockIdx.x) + i * int(gridDim.x);
-        const int rows = min(p.sr, p.n - st * p.sr);
+        int r0;
+        const int g = seg_of(p, st, r0);
+        const int rows = min(p.sr, p.n[g] - r0);
         const uint32_t bytes = uint32_t(int64_t(rows) * p.rb);
         mbar_expect_tx(&full[s], bytes);
-        bulk_g2s(smem + s * stage_bytes, p.w + int64_t(st) * p.sr * p.rb, bytes, &full[s]);
+        bulk_g2s(smem + s * stage_bytes, p.w[g] + int64_t(r0) * p.rb, bytes, &full[s]);
       }
     }
     __syncwarp();
   } else {
-    const int cw = warp - 1;                   // consumer warp
-    const int rslot = cw / WPR, wpart = cw % WPR;
-    const int cp0 = wpart * 64 + lane;         // this lane's units: cp0 and cp0 + 32
+    const int rslot = warp - 1;                // this warp's row of every stage
     griddep_wait();                            // the activations come from the previous kernel
-    uint32_t xa[2][8], xb[2][8];
-    float dx0[2], dx1[2], b0[2], b1[2];
+    // lane l owns the (chunk, page) units l + 32u: chunk l/4 + 8u, page l % 4 -- the same page for every unit
+    const int pg = lane & 3;
+    uint32_t xa[UPL][8], xb[UPL][8];
+    float dx0[UPL], dx1[UPL], b0[UPL], b1[UPL];
     const float* meta = reinterpret_cast<const float*>(p.xq + p.k);
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int cp = cp0 + 32 * u, c = cp >> 2, pg = cp & 3;
+    for (int u = 0; u < UPL; ++u) {
+      const int c = (lane >> 2) + 8 * u;
       const uint4* xw = reinterpret_cast<const uint4*>(p.xq + c * 256 + 64 * pg);
       const uint4 v0 = __ldg(xw), v1 = __ldg(xw + 1), v2 = __ldg(xw + 2), v3 = __ldg(xw + 3);
       xa[u][0] = v0.x; xa[u][1] = v0.y; xa[u][2] = v0.z; xa[u][3] = v0.w;
@@ -358,21 +371,21 @@ __global__ void __launch_bounds__(32 * (1 + 4 * WPR))
       b0[u] = mt.x * mt.y;
       b1[u] = mt.z * mt.w;
     }
-    const int pg = lane & 3;                   // both units share the page (cp0 and cp0 + 32 differ by 8 chunks)
     const uint32_t hsel = (pg & 1) ? 0x4432u : 0x4410u;
     const uint32_t big = (pg >> 1) ? 0xFFFFFFFFu : 0u;
     for (int i = 0; i < my_stages; ++i) {
       const int s = i % kRStages;
       if (!mbar_wait(&full[s], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
       const int st = int(blockIdx.x) + i * int(gridDim.x);
-      const int row = st * p.sr + rslot;
+      int r0;
+      const int g = seg_of(p, st, r0);
+      const int row = r0 + rslot;
       float acc = 0.f;
-      if (row < p.n) {
+      if (row < p.n[g]) {
         const uint8_t* wr = smem + s * stage_bytes + int64_t(rslot) * p.rb;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = (cp0 + 32 * u) >> 2;
-          const uint8_t* sb = wr + c * kChunkBytes;
+        for (int u = 0; u < UPL; ++u) {
+          const uint8_t* sb = wr + ((lane >> 2) + 8 * u) * kChunkBytes;
           const uint4 hd = *reinterpret_cast<const uint4*>(sb);
           const uint4 q0 = *reinterpret_cast<const uint4*>(sb + 16 + 32 * pg);
           const uint4 q1 = *reinterpret_cast<const uint4*>(sb + 32 + 32 * pg);
@@ -397,42 +410,30 @@ __global__ void __launch_bounds__(32 * (1 + 4 * WPR))
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (WPR > 1) {
-        if (lane == 0) part[cw] = acc;
-        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
-        if (wpart == 0 && lane == 0 && row < p.n) {
-          float v = 0.f;
-#pragma unroll
-          for (int j = 0; j < WPR; ++j) v += part[rslot * WPR + j];
-          p.y[row] = p.accumulate ? p.y[row] + v : v;
-        }
-        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
-      } else if (lane == 0 && row < p.n) {
-        p.y[row] = p.accumulate ? p.y[row] + acc : acc;
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        if (row < p.n[g]) p.y[g][row] = p.accumulate ? p.y[g][row] + acc : acc;
       }
     }
   }
 }
 
-template <int WPR>
+template <int UPL>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
-  const int smem = kRStages * stage_bytes + 2 * kRStages * 8 + 4 * WPR * 4;
-  auto kern = k_mv_q8_rows<WPR>;
+  const int smem = kRStages * stage_bytes + 2 * kRStages * 8;
+  auto kern = k_mv_q8_rows<UPL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + 4 * WPR), smem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + kRowWarps), smem) != cudaSuccess ||
       per_sm < 1)
     return LK_ECUDA;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaLaunchConfig_t cfg = {};
-  // at most kRowsCtasPerSm CTAs per SM: the rest of the SM stays free for the next kernel's CTAs, which (under
-  // programmatic dependent launch) start streaming their weights while this grid finishes
-  cfg.gridDim = dim3(min(a.nstages, sms * min(per_sm, kRowsCtasPerSm)), 1, 1);
-  cfg.blockDim = dim3(32 * (1 + 4 * WPR), 1, 1);
+  cfg.gridDim = dim3(min(a.nstages, sms * per_sm), 1, 1);   // persistent: every resident CTA slot, once
+  cfg.blockDim = dim3(32 * (1 + kRowWarps), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -522,26 +523,56 @@ int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStrea
   return e == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
+static bool rows_path(int fmt, int k, int tokens) {
+  return fmt == LK_Q4_K && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096;
+}
+
+static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
+                      const uint8_t* xq, cudaStream_t s) {
+  RowArgs ra{};
+  ra.xq = xq;
+  ra.k = k;
+  ra.accumulate = accumulate;
+  ra.rb = int64_t(k) / 256 * kChunkBytes;
+  ra.sr = kRowWarps;
+  ra.nseg = nseg;
+  ra.start[0] = 0;
+  for (int g = 0; g < nseg; ++g) {
+    ra.w[g] = static_cast<const uint8_t*>(ws[g]);
+    ra.y[g] = ys[g];
+    ra.n[g] = ns[g];
+    ra.start[g + 1] = ra.start[g] + (ns[g] + ra.sr - 1) / ra.sr;
+  }
+  ra.nstages = ra.start[nseg];
+  switch (k / 2048) {   // units (chunk, page) per lane
+    case 2: return launch_rows<2>(ra, s);
+    case 4: return launch_rows<4>(ra, s);
+    case 6: return launch_rows<6>(ra, s);
+  }
+  return LK_EUNSUPPORTED;
+}
+
+// Several weights sharing one activation (q | k | v of an attention layer): one launch over all their rows when the
+// row-streaming kernel applies, else one launch each.
+int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int tokens,
+                int accumulate, const uint8_t* xq, cudaStream_t s) {
+  if (rows_path(fmt, k, tokens) && nseg <= kMaxSegs) return mv_q8_rows(nseg, ns, ws, ys, k, accumulate, xq, s);
+  for (int g = 0; g < nseg; ++g) {
+    int rc = mv_q8(fmt, ns[g], k, tokens, accumulate, xq, ws[g], ys[g], s);
+    if (rc != LK_OK) return rc;
+  }
+  return LK_OK;
+}
+
 int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
           cudaStream_t s) {
   if (fmt != LK_Q4_K && fmt != LK_Q4_0) return LK_EUNSUPPORTED;
   const int64_t rb = int64_t(k) / 256 * kChunkBytes;
-  if (fmt == LK_Q4_K && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096) {
-    RowArgs ra{};
-    ra.w = static_cast<const uint8_t*>(w);
-    ra.xq = xq;
-    ra.y = y;
-    ra.n = n;
-    ra.k = k;
-    ra.accumulate = accumulate;
-    ra.rb = rb;
-    ra.sr = 4;
-    ra.nstages = (n + 3) / 4;
-    switch (k / 4096) {
-      case 1: return launch_rows<1>(ra, s);
-      case 2: return launch_rows<2>(ra, s);
-      case 3: return launch_rows<3>(ra, s);
-    }
+  if (rows_path(fmt, k, tokens)) {
+    const int ns[1] = {n};
+    const void* ws[1] = {w};
+    float* ys[1] = {y};
+    return mv_q8_rows(1, ns, ws, ys, k, accumulate, xq, s);
   }
   const int tokb = tokens <= 1 ? 1 : 8;
   CUtensorMap wm;

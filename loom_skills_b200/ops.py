@@ -303,3 +303,18 @@ def mv_q8(fmt, w, xq, n, k, tokens, y=None, accumulate=False):
     L.check(L.load().lk_mv_q8(_fmt(fmt), n, k, tokens, 1 if accumulate else 0, _ptr(xq), _ptr(w), _ptr(y),
                               _stream()), "lk_mv_q8")
     return y
+
+
+def mv_q8_multi(fmt, ws, xq, ns, k, tokens, ys=None, accumulate=False):
+    """mv_q8 over several weights sharing one activation (q | k | v): one launch where possible. Returns the ys."""
+    import ctypes
+    _cuda(xq, *ws)
+    g = len(ws)
+    if ys is None:
+        ys = [torch.empty(tokens, n, dtype=torch.float32, device=xq.device) for n in ns]
+    n_arr = (ctypes.c_int * g)(*ns)
+    w_arr = (ctypes.c_void_p * g)(*[w.data_ptr() for w in ws])
+    y_arr = (ctypes.c_void_p * g)(*[y.data_ptr() for y in ys])
+    L.check(L.load().lk_mv_q8_multi(_fmt(fmt), g, n_arr, w_arr, y_arr, k, tokens, 1 if accumulate else 0, _ptr(xq),
+                                    _stream()), "lk_mv_q8_multi")
+    return ys

@@ -85,3 +85,21 @@ class TestMvQ8:
         with pytest.raises(ops.L.LkError):
             ops.mv_q8("iq4_nl", w, xq, 4, 256, 1)
         assert ops.mv_q8("q4_k", w, xq, 4, 256, 0).shape == (0, 4)
+
+
+class TestMvQ8Multi:
+    @pytest.mark.parametrize("fmt,k,tokens", [("q4_k", 4096, 1), ("q4_k", 12288, 1), ("q4_0", 4096, 1),
+                                              ("q4_k", 4096, 3)])
+    def test_segments_match_single_launches(self, ops, fmt, k, tokens):
+        rng = np.random.default_rng(k + tokens)
+        ns = [512, 128, 130] if fmt == "q4_k" else [256, 64]
+        ws = [QUANT[fmt]((rng.standard_normal((n, k)) * 0.02).astype(np.float32)) for n in ns]
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        xq = ops.quant_q8(dev(x))
+        codes, meta = ops.q8_views(xq, tokens, k)
+        xd = O.dequant_q8(host(codes), host(meta))
+        ys = ops.mv_q8_multi(fmt, [dev(w) for w in ws], xq, ns, k, tokens)
+        for w, n, y in zip(ws, ns, ys):
+            ref = O.mv_ref(fmt, w, xd, n, k)
+            assert O.rel_l2(host(y), ref) < TOL, O.rel_l2(host(y), ref)
+        assert ops.device_status() == 0
