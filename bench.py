@@ -348,13 +348,18 @@ def run_ours(args):
     rank, local, world = rank_env()
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     pk, pk_src = peaks()
     wstack = make_weights(torch, args.layers, seed=rank)
     torch.manual_seed(rank)
     xs = {k: torch.randn(1, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
-    ys = [{name: torch.empty(1, n, device=dev) for name, _, n in SHAPES} for _ in range(args.layers)]
+    # every projection output of the step is a view of one buffer, so the e2e step reads them back with one copy
+    ncols = sum(n for _, _, n in SHAPES)
+    yall = torch.empty(args.layers, ncols, device=dev)
+    offs = np.cumsum([0] + [n for _, _, n in SHAPES])
+    ys = [{name: yall[li, offs[j]:offs[j + 1]].view(1, n) for j, (name, _, n) in enumerate(SHAPES)}
+          for li in range(args.layers)]
     wbytes_layer = sum(t.numel() for t in wstack[0].values())
     act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
     launches_per_step = args.layers * 4   # matvec launches: q|k|v, o, gate_up, down
@@ -449,17 +454,15 @@ def run_ours(args):
     hx = {k: torch.empty(1, k, dtype=torch.bfloat16).pin_memory() for k in xs}
     for k in hx:
         hx[k].copy_(xs[k].cpu())
-    hy = [{name: torch.empty(1, n).pin_memory() for name, _, n in SHAPES} for _ in range(args.layers)]
+    hy = torch.empty(args.layers, ncols).pin_memory()
     h2d = sum(t.numel() * 2 for t in hx.values())
-    d2h = sum(t.numel() * 4 for d in hy for t in d.values())
+    d2h = hy.numel() * 4
 
     def e2e_body():
         for k in hx:
             xs[k].copy_(hx[k], non_blocking=True)
         decode_body()
-        for li in range(args.layers):
-            for name in ys[li]:
-                hy[li][name].copy_(ys[li][name], non_blocking=True)
+        hy.copy_(yall, non_blocking=True)
 
     e2e_g = Timed(torch, e2e_body)
     for _ in range(args.warmup):
