@@ -386,6 +386,254 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Persistent dense GEMM: one CTA per SM walks the output tiles (tile t = blockIdx.x + i * gridDim.x; m fastest, so
+// the CTAs in flight share weight tiles in L2). The rings run on across tile boundaries, and the two TMEM
+// accumulator buffers (2 x 256 columns) let four dedicated epilogue warps drain tile i while the tensor core already
+// accumulates tile i + 1:
+//   warp 0        producer (A boxes, packed weight boxes)
+//   warp 1        TMEM allocation, MMA issue; waits acc_empty[buf] before reusing an accumulator buffer
+//   warps 2-9     dequantise B stages
+//   warps 10-13   epilogue: acc_full[buf] -> tcgen05.ld -> scale (silu * u) -> shared staging -> coalesced stores
+//                 -> acc_empty[buf]
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kEpWarps = 4;
+constexpr int kGemmPThreads = (2 + kDqWarps + kEpWarps) * 32;
+constexpr int kStgBytes = kEpWarps * 32 * kStgStride * 4;
+
+
+// NBUF accumulator buffers of MH * NW * BN columns each (512 TMEM columns in all); SAP / SBP / SRP stages of the A,
+// B and packed-weight rings
+template <int FMT, int BN, int NW, int MODE, int MH, int NBUF, int SAP, int SBP, int SRP>
+__global__ void __launch_bounds__(kGemmPThreads, 1)
+    k_gemm_p(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+             const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
+  constexpr int kTM = kBM * MH;
+  constexpr int kRowsB = BN * NW;
+  constexpr int kABytes = kTM * kBK * 2;
+  constexpr int kBBytes = kRowsB * kBK * 2;
+  constexpr int kRBytes = kRowsB * kChunkBytes;
+  constexpr int kSAp = SAP;
+  constexpr int kSBp = SBP;
+  constexpr uint32_t kAcc = MH * NW * BN;   // accumulator columns of one tile
+  static_assert(NBUF * kAcc == 512, "the accumulator buffers fill the 512 TMEM columns");
+  static_assert(kRowsB == 2 * kDqWarps * 16 || kRowsB == kDqWarps * 16, "one or two rows per dequant thread");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kSAp * kABytes;
+  uint8_t* sR = sB + kSBp * kBBytes;
+  float* stg_all = reinterpret_cast<float*>(sR + SRP * kRBytes);
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stg_all) + kStgBytes);
+  uint64_t* empty_a = full_a + kSAp;
+  uint64_t* full_b = empty_a + kSAp;
+  uint64_t* empty_b = full_b + kSBp;
+  uint64_t* full_r = empty_b + kSBp;
+  uint64_t* empty_r = full_r + SRP;
+  uint64_t* acc_full = empty_r + SRP;    // [NBUF]
+  uint64_t* acc_empty = acc_full + 2;    // [NBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kstages = p.k / kBK;
+  const int mt = (p.rows + kTM - 1) / kTM, nt = (p.n + BN - 1) / BN;
+  const int ntiles = mt * nt;
+  const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSAp; ++i) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < kSBp; ++i) {
+      mbar_init(&full_b[i], kDqWarps);
+      mbar_init(&empty_b[i], 1);
+    }
+    for (int i = 0; i < SRP; ++i) {
+      mbar_init(&full_r[i], 1);
+      mbar_init(&empty_r[i], kDqWarps);
+    }
+    for (int i = 0; i < NBUF; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, NBUF * kAcc);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+      int ga = 0, gr = 0;
+      for (int li = 0; li < my_tiles; ++li) {
+        const int t = int(blockIdx.x) + li * int(gridDim.x);
+        const int m0 = (t % mt) * kTM, n0 = (t / mt) * BN;
+        const int wrow = n0, w2row = n0 + p.w2_row_offset;
+        for (int ks = 0; ks < kstages; ++ks) {
+          if ((ks & 3) == 0) {
+            const int sr = gr % SRP;
+            if (gr >= SRP && !mbar_wait(&empty_r[sr], ((gr / SRP) - 1) & 1)) atomicOr(&g_status, 1u);
+            mbar_expect_tx(&full_r[sr], uint32_t(kRBytes));
+            tma_load_2d(sR + sr * kRBytes, &wmap, (ks >> 2) * (kChunkBytes / 4), wrow, &full_r[sr]);
+            if (NW == 2)
+              tma_load_2d(sR + sr * kRBytes + BN * kChunkBytes, &w2map, (ks >> 2) * (kChunkBytes / 4), w2row,
+                          &full_r[sr]);
+            ++gr;
+          }
+          const int sa = ga % kSAp;
+          if (ga >= kSAp && !mbar_wait(&empty_a[sa], ((ga / kSAp) - 1) & 1)) atomicOr(&g_status, 1u);
+          mbar_expect_tx(&full_a[sa], kABytes);
+          tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
+          ++ga;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
+    const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+    int ga = 0, gb = 0;
+    for (int li = 0; li < my_tiles; ++li) {
+      const int buf = li % NBUF;
+      if (li >= NBUF && !mbar_wait(&acc_empty[buf], ((li / NBUF) - 1) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+      const uint32_t tacc = tmem + buf * kAcc;
+      for (int ks = 0; ks < kstages; ++ks) {
+        const int sa = ga % kSAp, sb = gb % kSBp;
+        if (!mbar_wait(&full_a[sa], (ga / kSAp) & 1)) atomicOr(&g_status, 1u);
+        if (!mbar_wait(&full_b[sb], (gb / kSBp) & 1)) atomicOr(&g_status, 1u);
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+#pragma unroll
+            for (int mh = 0; mh < MH; ++mh) {
+              uint64_t ad = sdesc_k128(a_base + sa * kABytes + mh * (kBM * 128) + kk * 32);
+#pragma unroll
+              for (int wi = 0; wi < NW; ++wi) {
+                uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
+                umma_f16(tacc + (mh * NW + wi) * BN, ad, bd, idesc, (ks | kk) != 0);
+              }
+            }
+          }
+          umma_commit(&empty_a[sa]);
+          umma_commit(&empty_b[sb]);
+          if (ks == kstages - 1) umma_commit(&acc_full[buf]);
+        }
+        __syncwarp();
+        ++ga;
+        ++gb;
+      }
+    }
+  } else if (warp < 2 + kDqWarps) {
+    // ------------------------------------------------------------------ dequant warps
+    const int dt = threadIdx.x - 64;   // 0..255
+    constexpr int kGroupsPerThread = kRowsB * 2 / (kDqWarps * 32);
+    int gb = 0, gr = 0;
+    for (int li = 0; li < my_tiles; ++li) {
+      for (int ks = 0; ks < kstages; ++ks) {
+        const int sub = ks & 3, sr = gr % SRP, sb = gb % kSBp;
+        if (sub == 0 && !mbar_wait(&full_r[sr], (gr / SRP) & 1)) atomicOr(&g_status, 1u);
+        if (gb >= kSBp && !mbar_wait(&empty_b[sb], ((gb / kSBp) - 1) & 1)) atomicOr(&g_status, 1u);
+        uint8_t* bt = sB + sb * kBBytes;
+#pragma unroll
+        for (int gi = 0; gi < kGroupsPerThread; ++gi) {
+          const int item = dt * kGroupsPerThread + gi;   // (row, half) pairs
+          const int r = item >> 1, h = item & 1;
+          dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full_b[sb]);
+          if (sub == 3) mbar_arrive(&empty_r[sr]);
+        }
+        ++gb;
+        if (sub == 3) ++gr;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;                    // TMEM lane quadrant this warp may read
+    float* stg = stg_all + (warp - 2 - kDqWarps) * (32 * kStgStride);
+    const int sr = lane >> 3, sc = 4 * (lane & 7);
+    for (int li = 0; li < my_tiles; ++li) {
+      const int t = int(blockIdx.x) + li * int(gridDim.x);
+      const int m0 = (t % mt) * kTM, n0 = (t / mt) * BN;
+      const int valid_rows = min(kTM, p.rows - m0), nb_rows = min(BN, p.n - n0);
+      const int buf = li % NBUF;
+      if (!mbar_wait(&acc_full[buf], (li / NBUF) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+#pragma unroll 1
+      for (int mh = 0; mh < MH; ++mh) {
+        const int row = mh * kBM + 32 * q + lane;
+        const float inv = row < valid_rows ? p.scales[2 * int64_t(m0 + row) + 1] : 0.f;
+        const uint32_t tbase = tmem + buf * kAcc + (uint32_t(32 * q) << 16) + mh * NW * BN;
+#pragma unroll 1
+        for (int col = 0; col < BN; col += 32) {
+          float v[32];
+          tmem_ld32(tbase + col, v);
+          if (NW == 2) {
+            float u[32];
+            tmem_ld32(tbase + BN + col, u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= inv;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(stg + lane * kStgStride + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          __syncwarp();
+          const bool col_ok = col + sc < nb_rows;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int rr = 4 * j + sr;
+            const int trow = mh * kBM + 32 * q + rr;
+            float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
+            if (col_ok && trow < valid_rows) {
+              const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
+              if (MODE == LK_ACC) {
+                float4 old = *reinterpret_cast<const float4*>(p.dst[0] + off);
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+              }
+#pragma unroll
+              for (int d = 0; d < kMaxPeers; ++d)
+                if (d < p.ndst) *reinterpret_cast<float4*>(p.dst[d] + off) = o;
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, NBUF * kAcc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -437,6 +685,24 @@ static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStre
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
+template <int FMT, int BN, int NW, int MODE, int MH, int NBUF, int SAP, int SBP, int SRP>
+static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
+  constexpr int kRowsB = BN * NW;
+  constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2, kRBytes = kRowsB * kChunkBytes;
+  constexpr int smem = 1024 + SAP * kABytes + SBP * kBBytes + SRP * kRBytes + kStgBytes +
+                       (2 * (SAP + SBP + SRP) + 4) * 8 + 16;
+  static_assert(smem <= 227 * 1024, "persistent GEMM CTA exceeds shared memory");
+  auto kern = k_gemm_p<FMT, BN, NW, MODE, MH, NBUF, SAP, SBP, SRP>;
+  static unsigned configured = 0;
+  if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ntiles = ((a.rows + kBM * MH - 1) / (kBM * MH)) * ((a.n + BN - 1) / BN);
+  kern<<<min(ntiles, sms), kGemmPThreads, smem, s>>>(m.a, m.w, m.w2, a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
 // tile shape per mode: (BN, NW, MH)
 //   dense store/acc  128 x 1 x 2   a 256 x 128 tile, two M=128 accumulators sharing each dequantised B stage
 //   dense swiglu     128 x 2 x 1   128 rows x 128 columns of gate and of up
@@ -444,10 +710,10 @@ static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStre
 //   grouped down     256 x 1 x 1
 template <int FMT>
 static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
-  if (group == kDense) {
-    if (mode == LK_SWIGLU) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kDense, 1>(m, a, grid, s);
-    if (mode == LK_ACC) return launch_gemm<FMT, 128, 1, LK_ACC, kDense, 2>(m, a, grid, s);
-    return launch_gemm<FMT, 128, 1, LK_STORE, kDense, 2>(m, a, grid, s);
+  if (group == kDense) {   // persistent kernel
+    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, 1, 2, 4, 2, 2>(m, a, s);
+    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, 2, 2, 3, 4, 2>(m, a, s);
+    return launch_gemm_p<FMT, 128, 1, LK_STORE, 2, 2, 3, 4, 2>(m, a, s);
   }
   if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather, 1>(m, a, grid, s);
   return launch_gemm<FMT, 256, 1, LK_STORE, kSorted, 1>(m, a, grid, s);
@@ -490,6 +756,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
   a.w2_row_offset = (mode == LK_SWIGLU && !w2) ? int(w2_offset / rb) : 0;
+  // weight rows per tile: 256 for grouped down, 128 per weight otherwise
   const int bn = (group == kSorted) ? 256 : 128;
   const int tm = (group == kDense && mode != LK_SWIGLU) ? 2 * kBM : kBM;   // tile rows
   GemmMaps m;
