@@ -35,9 +35,12 @@ METRIC = "decode GEMV weight GB/s (% HBM peak); prefill TFLOPS (% tensor peak)"
 SHAPES = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096), ("gate_up", 4096, 24576),
           ("down", 12288, 4096)]   # (name, K, N)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures (profiles/), None until captured
-TRAFFIC_DECODE = None
-TRAFFIC_PREFILL = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu-captured launch (`--profile-case mv_gate_up` /
+# `gemm_gate_up`) divided by its algorithmic bytes: decode 56.666 MB / 56.727 MB; prefill 226.7 MB / 274.7 MB (output
+# lines still in L2 at kernel exit are not counted). The bench scales them to its average launch, since traffic
+# grows in proportion to the bytes a launch streams.
+TRAFFIC_RATIO_DECODE = 56.666 / 56.727
+TRAFFIC_RATIO_PREFILL = 226.7 / 274.7
 
 
 def peaks():
@@ -440,7 +443,7 @@ def run_ours(args):
     kavg = mv_ms / launches_per_step
     achieved = alg_per_launch / (kavg * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": TRAFFIC_DECODE, "peak_source": pk_src,
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": int(TRAFFIC_RATIO_DECODE * alg_per_launch), "peak_source": pk_src,
             "kernel": "k_mv_q8_rows / k_mv_q8 (Q4_K x int8, dp4a; lk_mvq8)", "avg_launch_us": round(kavg * 1e3, 2),
             "alg_bytes_per_launch": int(alg_per_launch), "mv_ms_per_step": round(mv_ms, 4)}
     bf = Timed(torch, decode_bf16_body)
@@ -476,6 +479,7 @@ def run_ours(args):
     xp = {k: torch.randn(M, k, device=dev).to(torch.bfloat16) for k in (4096, 12288)}
     yp = {name: torch.empty(M, n, device=dev) for name, _, n in SHAPES}
     flops = sum(2.0 * M * n * k for _, k, n in SHAPES)
+    prefill_bytes = sum(M * k * 2 + n * k // 256 * 144 + M * n * 4 for _, k, n in SHAPES)   # x16 + weights + y
 
     x16p = {}
 
@@ -511,7 +515,7 @@ def run_ours(args):
     peak_tf = pk["bf16_tflops_sustained"]
     prefill = {"rows": M, "tflops": round(world * ptflops, 1), "ms_per_step": round(pms, 4), "steps": psteps,
                "roofline": {"bound": "tensor", "achieved": round(gemm_tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                            "frac": round(gemm_tf / peak_tf, 4), "traffic": TRAFFIC_PREFILL,
+                            "frac": round(gemm_tf / peak_tf, 4), "traffic": int(TRAFFIC_RATIO_PREFILL * prefill_bytes / len(SHAPES)),
                             "peak_source": pk_src + " sustained", "kernel": "k_gemm<Q4_K> (tcgen05 kind::f16, lk_gemm)"}}
 
     # ---- sweep over the config's token counts (one layer, per-step ms; row scale included for M >= 64)
@@ -568,6 +572,45 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    """A few launches of one hot kernel at one bench shape, for ncu captures (profiles/): warm-up launches, then
+    `--steps` profiled ones. Cases: mv_gate_up (Q4_K q8 matvec, K=4096 N=24576), mv_down (K=12288 N=4096),
+    gemm_gate_up (Q4_K GEMM, M=2048 K=4096 N=24576), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880)."""
+    import torch
+
+    from loom_skills_b200 import ops
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    case = args.profile_case
+    if case.startswith("mv_"):
+        k, n = (4096, 24576) if case == "mv_gate_up" else (12288, 4096)
+        w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+        xq = ops.quant_q8(torch.randn(1, k, device=dev))
+        y = torch.empty(1, n, device=dev)
+        fn = lambda: ops.mv_q8("q4_k", w, xq, n, k, 1, y=y)   # noqa: E731
+    elif case == "gemm_gate_up":
+        m, k, n = 2048, 4096, 24576
+        w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+        x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
+        y = torch.empty(m, n, device=dev)
+        fn = lambda: ops.gemm("q4_k", "store", x16, sc, w, n, y=y)   # noqa: E731
+    elif case == "mx_gate_up":
+        m, k, n = 8192, 2880, 2880
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        g, gs = synth_mxfp4(torch, dev, n, k, gen)
+        u, us = synth_mxfp4(torch, dev, n, k, gen)
+        x8, s8 = ops.row_scale_f8(torch.randn(m, k, device=dev))
+        y = torch.empty(m, n, device=dev)
+        fn = lambda: ops.gemm_mxfp4s_f8("swiglu", x8, s8, g, gs, n, w2=u, w2s=us, y=y)   # noqa: E731
+    else:
+        raise SystemExit(f"unknown --profile-case {case}")
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "launches": args.warmup + args.steps}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -579,10 +622,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the sharded-GEMM and MoE sections")
+    ap.add_argument("--profile-case", default=None, help="run one kernel a few times for an ncu capture")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
