@@ -314,18 +314,25 @@ LK_DEV int seg_of(const RowArgs& p, int st, int& row0) {
   return g;
 }
 
-template <int UPL>
-__global__ void __launch_bounds__(32 * (1 + kRowWarps))
+// UPL units per lane over the whole row; HALVES warps per row (each takes UPL / HALVES of the units; the second
+// hands its partial sum to the first through shared memory and a per-row mbarrier)
+template <int UPL, int HALVES>
+__global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
+  constexpr int kU = UPL / HALVES;             // units this lane computes
+  constexpr int kCW = kRowWarps * HALVES;      // consumer warps
   extern __shared__ __align__(128) uint8_t smem[];
   const int stage_bytes = int((int64_t(p.sr) * p.rb + 127) / 128 * 128);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRStages * stage_bytes);
   uint64_t* empty = full + kRStages;
+  uint64_t* pair = empty + kRStages;                               // [kRStages][kRowWarps]
+  float* part = reinterpret_cast<float*>(pair + kRStages * kRowWarps);   // [kRStages][kRowWarps]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kRStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kRowWarps);
+      mbar_init(&empty[i], kCW);
+      for (int r = 0; r < kRowWarps; ++r) mbar_init(&pair[i * kRowWarps + r], 1);
     }
     fence_mbar_init();
   }
@@ -349,16 +356,17 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps))
     }
     __syncwarp();
   } else {
-    const int rslot = warp - 1;                // this warp's row of every stage
+    const int rslot = (warp - 1) % kRowWarps;  // this warp's row of every stage
+    const int half = (warp - 1) / kRowWarps;   // which share of the row's units
     griddep_wait();                            // the activations come from the previous kernel
     // lane l owns the (chunk, page) units l + 32u: chunk l/4 + 8u, page l % 4 -- the same page for every unit
     const int pg = lane & 3;
-    uint32_t xa[UPL][8], xb[UPL][8];
-    float dx0[UPL], dx1[UPL], b0[UPL], b1[UPL];
+    uint32_t xa[kU][8], xb[kU][8];
+    float dx0[kU], dx1[kU], b0[kU], b1[kU];
     const float* meta = reinterpret_cast<const float*>(p.xq + p.k);
 #pragma unroll
-    for (int u = 0; u < UPL; ++u) {
-      const int c = (lane >> 2) + 8 * u;
+    for (int u = 0; u < kU; ++u) {
+      const int c = (lane >> 2) + 8 * (half * kU + u);
       const uint4* xw = reinterpret_cast<const uint4*>(p.xq + c * 256 + 64 * pg);
       const uint4 v0 = __ldg(xw), v1 = __ldg(xw + 1), v2 = __ldg(xw + 2), v3 = __ldg(xw + 3);
       xa[u][0] = v0.x; xa[u][1] = v0.y; xa[u][2] = v0.z; xa[u][3] = v0.w;
@@ -384,8 +392,8 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps))
       if (row < p.n[g]) {
         const uint8_t* wr = smem + s * stage_bytes + int64_t(rslot) * p.rb;
 #pragma unroll
-        for (int u = 0; u < UPL; ++u) {
-          const uint8_t* sb = wr + ((lane >> 2) + 8 * u) * kChunkBytes;
+        for (int u = 0; u < kU; ++u) {
+          const uint8_t* sb = wr + ((lane >> 2) + 8 * (half * kU + u)) * kChunkBytes;
           const uint4 hd = *reinterpret_cast<const uint4*>(sb);
           const uint4 q0 = *reinterpret_cast<const uint4*>(sb + 16 + 32 * pg);
           const uint4 q1 = *reinterpret_cast<const uint4*>(sb + 32 + 32 * pg);
@@ -410,22 +418,35 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps))
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&empty[s]);
-        if (row < p.n[g]) p.y[g][row] = p.accumulate ? p.y[g][row] + acc : acc;
+      if (HALVES == 2 && half == 1) {
+        if (lane == 0) {
+          part[s * kRowWarps + rslot] = acc;
+          mbar_arrive(&pair[s * kRowWarps + rslot]);   // release: the partial is visible to the row's first warp
+          mbar_arrive(&empty[s]);
+        }
+      } else {
+        if (HALVES == 2) {
+          if (!mbar_wait(&pair[s * kRowWarps + rslot], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
+          acc += part[s * kRowWarps + rslot];
+        }
+        if (lane == 0) {
+          mbar_arrive(&empty[s]);
+          if (row < p.n[g]) p.y[g][row] = p.accumulate ? p.y[g][row] + acc : acc;
+        }
       }
     }
   }
 }
 
-template <int UPL>
+template <int UPL, int HALVES>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
-  const int smem = kRStages * stage_bytes + 2 * kRStages * 8;
-  auto kern = k_mv_q8_rows<UPL>;
+  const int smem = kRStages * stage_bytes + 2 * kRStages * 8 + kRStages * kRowWarps * 12;
+  auto kern = k_mv_q8_rows<UPL, HALVES>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + kRowWarps), smem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + kRowWarps * HALVES), smem) !=
+          cudaSuccess ||
       per_sm < 1)
     return LK_ECUDA;
   int dev = 0, sms = 0;
@@ -433,7 +454,7 @@ int launch_rows(RowArgs a, cudaStream_t s) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(min(a.nstages, sms * per_sm), 1, 1);   // persistent: every resident CTA slot, once
-  cfg.blockDim = dim3(32 * (1 + kRowWarps), 1, 1);
+  cfg.blockDim = dim3(32 * (1 + kRowWarps * HALVES), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -545,9 +566,9 @@ static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* con
   }
   ra.nstages = ra.start[nseg];
   switch (k / 2048) {   // units (chunk, page) per lane
-    case 2: return launch_rows<2>(ra, s);
-    case 4: return launch_rows<4>(ra, s);
-    case 6: return launch_rows<6>(ra, s);
+    case 2: return launch_rows<2, 1>(ra, s);
+    case 4: return launch_rows<4, 2>(ra, s);
+    case 6: return launch_rows<6, 2>(ra, s);
   }
   return LK_EUNSUPPORTED;
 }
