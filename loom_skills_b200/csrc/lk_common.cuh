@@ -291,6 +291,69 @@ constexpr int kMaxPeers = 8;   // ranks of one NVSwitch domain a GEMM epilogue c
 // owns ceil(tiles_e / 2) super-tiles. Called by every thread of the CTA; `scratch` is 3 * kMaxExperts ints of shared
 // memory that nothing else uses yet (the async proxy may write it afterwards). meta[0] = expert (-1: the schedule has
 // fewer super-tiles than s + 1), meta[1] = first tile, meta[2] = valid rows (64 + rows of the second tile if paired).
+// The whole super-tile table of a schedule, for kernels that walk many super-tiles: called by every thread of the
+// CTA; tbl = 3 * kMaxExperts ints of shared memory that stay for the kernel's life: start[e] (first tile), count[e]
+// (tiles), base[e] (first super-tile). Returns the number of super-tiles.
+LK_DEV int moe_super_table(const int32_t* tile_info, int max_tiles, int n_experts, int* tbl) {
+  int* start = tbl;
+  int* count = tbl + kMaxExperts;
+  int* base = tbl + 2 * kMaxExperts;
+  for (int e = threadIdx.x; e < kMaxExperts; e += blockDim.x) {
+    start[e] = 0x7FFFFFFF;
+    count[e] = 0;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < max_tiles; t += blockDim.x) {
+    int e = __ldg(tile_info + 2 * t);
+    if (e >= 0 && e < n_experts) {
+      atomicMin(&start[e], t);
+      atomicAdd(&count[e], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int v[kMaxExperts / 32], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      v[i] = (count[lane * (kMaxExperts / 32) + i] + 1) >> 1;
+      sum += v[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      base[lane * (kMaxExperts / 32) + i] = run;
+      run += v[i];
+    }
+  }
+  __syncthreads();
+  return base[kMaxExperts - 1] + ((count[kMaxExperts - 1] + 1) >> 1);
+}
+// Super-tile s of a table built by moe_super_table (s below the returned count): expert, first 64-row tile, valid
+// rows.
+LK_DEV void moe_super_lookup(const int32_t* tile_info, const int* tbl, int s, int& expert, int& first, int& rows) {
+  const int* start = tbl;
+  const int* count = tbl + kMaxExperts;
+  const int* base = tbl + 2 * kMaxExperts;
+  int lo = 0, hi = kMaxExperts;   // first e with base[e] > s
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (base[mid] <= s) lo = mid + 1;
+    else hi = mid;
+  }
+  const int e = lo - 1;
+  expert = e;
+  first = start[e] + 2 * (s - base[e]);
+  const bool pair = first + 1 < start[e] + count[e];
+  rows = pair ? 64 + __ldg(tile_info + 2 * (first + 1) + 1) : __ldg(tile_info + 2 * first + 1);
+}
+
 LK_DEV void moe_super_tile(const int32_t* tile_info, int max_tiles, int n_experts, int s, int* scratch, int* meta) {
   int* start = scratch;
   int* count = scratch + kMaxExperts;

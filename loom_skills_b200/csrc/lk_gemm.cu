@@ -47,6 +47,7 @@ struct GemmArgs {
   const int32_t* rowmap;      // [max_tiles*64]
   int max_tiles;
   int xrows, ku, n_experts;
+  int n_fast;                 // persistent dense kernel: walk the n tiles of an m tile first (large A, small W)
 };
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
@@ -403,7 +404,7 @@ constexpr int kStgBytes = kEpWarps * 32 * kStgStride * 4;
 
 // NBUF accumulator buffers of MH * NW * BN columns each (512 TMEM columns in all); SAP / SBP / SRP stages of the A,
 // B and packed-weight rings
-template <int FMT, int BN, int NW, int MODE, int MH, int NBUF, int SAP, int SBP, int SRP>
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP>
 __global__ void __launch_bounds__(kGemmPThreads, 1)
     k_gemm_p(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
              const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
@@ -433,12 +434,31 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
   uint64_t* acc_full = empty_r + SRP;    // [NBUF]
   uint64_t* acc_empty = acc_full + 2;    // [NBUF]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* stbl = reinterpret_cast<int*>(tmem_slot + 4);   // MoE super-tile table [3][kMaxExperts]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kstages = p.k / kBK;
   const int mt = (p.rows + kTM - 1) / kTM, nt = (p.n + BN - 1) / BN;
-  const int ntiles = mt * nt;
+  // tiles: dense m x n; grouped (super-tile, n) with the n tiles of a super-tile consecutive
+  const int ntiles = GROUP == kDense ? mt * nt : moe_super_table(p.tile_info, p.max_tiles, p.n_experts, stbl) * nt;
   const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  // tile t -> first output row, first weight row of the tile inside the expert block, expert, valid rows
+  auto tile_of = [&](int t, int& m0, int& n0, int& e, int& valid) {
+    if (GROUP == kDense) {
+      const int mi = p.n_fast ? t / nt : t % mt, ni = p.n_fast ? t % nt : t / mt;
+      m0 = mi * kTM;
+      n0 = ni * BN;
+      e = 0;
+      valid = min(kTM, p.rows - m0);
+    } else {
+      int first, rows;
+      moe_super_lookup(p.tile_info, stbl, t / nt, e, first, rows);
+      e = min(e, p.n_experts - 1);
+      m0 = first * 64;
+      n0 = (t % nt) * BN;
+      valid = rows;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSAp; ++i) {
@@ -474,31 +494,48 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
       prefetch_tensormap(&amap);
       prefetch_tensormap(&wmap);
       if (NW == 2) prefetch_tensormap(&w2map);
-      int ga = 0, gr = 0;
-      for (int li = 0; li < my_tiles; ++li) {
-        const int t = int(blockIdx.x) + li * int(gridDim.x);
-        const int m0 = (t % mt) * kTM, n0 = (t / mt) * BN;
-        const int wrow = n0, w2row = n0 + p.w2_row_offset;
-        for (int ks = 0; ks < kstages; ++ks) {
-          if ((ks & 3) == 0) {
-            const int sr = gr % SRP;
-            if (gr >= SRP && !mbar_wait(&empty_r[sr], ((gr / SRP) - 1) & 1)) atomicOr(&g_status, 1u);
+    }
+    int ga = 0, gr = 0;
+    for (int li = 0; li < my_tiles; ++li) {
+      int m0, n0, e, valid;
+      tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid);
+      const int wrow = e * p.rows_per_expert + n0, w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
+      int arow[4] = {0, 0, 0, 0};
+      if (GROUP == kGather) {   // the routed token rows of this tile: 4 per lane, out-of-range -> zero rows
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = lane * 4 + j;
+          const int a = r < valid ? p.rowmap[m0 + r] : -1;
+          arow[j] = a >= 0 ? a / p.ku : p.xrows;
+        }
+      }
+      for (int ks = 0; ks < kstages; ++ks) {
+        if ((ks & 3) == 0) {
+          const int sr = gr % SRP;
+          if (gr >= SRP && !mbar_wait(&empty_r[sr], ((gr / SRP) - 1) & 1)) atomicOr(&g_status, 1u);
+          if (lane == 0) {
             mbar_expect_tx(&full_r[sr], uint32_t(kRBytes));
             tma_load_2d(sR + sr * kRBytes, &wmap, (ks >> 2) * (kChunkBytes / 4), wrow, &full_r[sr]);
             if (NW == 2)
               tma_load_2d(sR + sr * kRBytes + BN * kChunkBytes, &w2map, (ks >> 2) * (kChunkBytes / 4), w2row,
                           &full_r[sr]);
-            ++gr;
           }
-          const int sa = ga % kSAp;
-          if (ga >= kSAp && !mbar_wait(&empty_a[sa], ((ga / kSAp) - 1) & 1)) atomicOr(&g_status, 1u);
-          mbar_expect_tx(&full_a[sa], kABytes);
-          tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
-          ++ga;
+          ++gr;
         }
+        const int sa = ga % kSAp;
+        if (ga >= kSAp && !mbar_wait(&empty_a[sa], ((ga / kSAp) - 1) & 1)) atomicOr(&g_status, 1u);
+        if (lane == 0) mbar_expect_tx(&full_a[sa], kABytes);
+        __syncwarp();
+        if (GROUP == kGather) {
+          tma_gather4(sA + sa * kABytes + lane * 4 * 128, &amap, ks * kBK, arow[0], arow[1], arow[2], arow[3],
+                      &full_a[sa]);
+        } else if (lane == 0) {
+          tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
+        }
+        __syncwarp();
+        ++ga;
       }
     }
-    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
@@ -569,16 +606,21 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
     float* stg = stg_all + (warp - 2 - kDqWarps) * (32 * kStgStride);
     const int sr = lane >> 3, sc = 4 * (lane & 7);
     for (int li = 0; li < my_tiles; ++li) {
-      const int t = int(blockIdx.x) + li * int(gridDim.x);
-      const int m0 = (t % mt) * kTM, n0 = (t / mt) * BN;
-      const int valid_rows = min(kTM, p.rows - m0), nb_rows = min(BN, p.n - n0);
+      int m0, n0, e, valid_rows;
+      tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid_rows);
+      const int nb_rows = min(BN, p.n - n0);
       const int buf = li % NBUF;
       if (!mbar_wait(&acc_full[buf], (li / NBUF) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
 #pragma unroll 1
       for (int mh = 0; mh < MH; ++mh) {
         const int row = mh * kBM + 32 * q + lane;
-        const float inv = row < valid_rows ? p.scales[2 * int64_t(m0 + row) + 1] : 0.f;
+        int srow = row < valid_rows ? m0 + row : -1;
+        if (GROUP == kGather && srow >= 0) {
+          const int a = p.rowmap[srow];
+          srow = a >= 0 ? a / p.ku : -1;
+        }
+        const float inv = srow >= 0 ? p.scales[2 * int64_t(srow) + 1] : 0.f;
         const uint32_t tbase = tmem + buf * kAcc + (uint32_t(32 * q) << 16) + mh * NW * BN;
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
@@ -685,20 +727,21 @@ static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStre
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
-template <int FMT, int BN, int NW, int MODE, int MH, int NBUF, int SAP, int SBP, int SRP>
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP>
 static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
   constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2, kRBytes = kRowsB * kChunkBytes;
   constexpr int smem = 1024 + SAP * kABytes + SBP * kBBytes + SRP * kRBytes + kStgBytes +
-                       (2 * (SAP + SBP + SRP) + 4) * 8 + 16;
+                       (2 * (SAP + SBP + SRP) + 4) * 8 + 16 + 3 * kMaxExperts * 4;
   static_assert(smem <= 227 * 1024, "persistent GEMM CTA exceeds shared memory");
-  auto kern = k_gemm_p<FMT, BN, NW, MODE, MH, NBUF, SAP, SBP, SRP>;
+  auto kern = k_gemm_p<FMT, BN, NW, MODE, GROUP, MH, NBUF, SAP, SBP, SRP>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int ntiles = ((a.rows + kBM * MH - 1) / (kBM * MH)) * ((a.n + BN - 1) / BN);
+  // dense: the exact tile count; grouped: a bound (at most one super-tile per schedule tile)
+  const int ntiles = (GROUP == kDense ? (a.rows + kBM * MH - 1) / (kBM * MH) : a.rows / 64) * ((a.n + BN - 1) / BN);
   kern<<<min(ntiles, sms), kGemmPThreads, smem, s>>>(m.a, m.w, m.w2, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
@@ -711,12 +754,12 @@ static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
 template <int FMT>
 static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
   if (group == kDense) {   // persistent kernel
-    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, 1, 2, 4, 2, 2>(m, a, s);
-    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, 2, 2, 3, 4, 2>(m, a, s);
-    return launch_gemm_p<FMT, 128, 1, LK_STORE, 2, 2, 3, 4, 2>(m, a, s);
+    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kDense, 1, 2, 4, 2, 2>(m, a, s);
+    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 2, 2, 3, 4, 2>(m, a, s);
+    return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 3, 4, 2>(m, a, s);
   }
-  if (group == kGather) return launch_gemm<FMT, 128, 2, LK_SWIGLU, kGather, 1>(m, a, grid, s);
-  return launch_gemm<FMT, 256, 1, LK_STORE, kSorted, 1>(m, a, grid, s);
+  if (group == kGather) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kGather, 1, 2, 4, 2, 2>(m, a, s);
+  return launch_gemm_p<FMT, 256, 1, LK_STORE, kSorted, 1, 2, 4, 2, 2>(m, a, s);
 }
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
@@ -739,6 +782,9 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   a.k = k;
   a.n = n;
   const int64_t rb = lk_row_bytes(fmt, k);
+  // rasterise so the larger operand is read once: n tiles of an m tile first when the activations outweigh the
+  // weights (each A tile is then reused from L2 across the n tiles)
+  a.n_fast = int64_t(rows) * k * 2 > int64_t(n) * rb * (mode == LK_SWIGLU ? 2 : 1);
   int group = kDense;
   int64_t wrows = n, w2rows = n;
   a.rows_per_expert = a.rows_per_expert2 = 0;
