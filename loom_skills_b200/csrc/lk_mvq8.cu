@@ -13,9 +13,12 @@
 //
 // CTA = 1 producer warp + 8 consumer warps, 64 weight rows, a K-range of 256-value chunks:
 //   producer   TMA: per chunk one box of 64 rows x 144 bytes of packed weights, the chunk's activation codes
-//              [tokens][256] and group meta [tokens][16 f32], into a 4-stage mbarrier ring. It issues the weight boxes
-//              of the first stages before griddepcontrol.wait -- weights never depend on the previous kernel -- so
+//              [tokens][256] and group meta [tokens][16 f32], into a 4-stage mbarrier ring. It issues the weight box
+//              of the first stage before griddepcontrol.wait -- weights never depend on the previous kernel -- so
 //              under programmatic dependent launch the weight stream starts while the previous kernel finishes.
+//              Only one stage goes out early: loads still in flight on the SMs were measured to hold back the
+//              previous grid's completion (the release of griddepcontrol.wait) by up to 2 us when every CTA
+//              requested its whole ring up front; one stage per CTA keeps the overlap without the delay.
 //   consumers  thread = (64-byte page / block pair p of the chunk, one row); partial sums over the 4 threads of a
 //              row are combined by shuffles at the end. Small stages (37 KB of ring) keep 6 CTAs = 54 warps on an SM:
 //              the per-thread work is a short dependent chain, so latency is hidden by warps, not by ILP alone.
@@ -38,6 +41,7 @@ constexpr int kQStages = 4;
 constexpr int kQWBytes = kQRows * kChunkBytes;   // 9216
 constexpr int kQRpt = kQRows * 4 / (32 * kQConsumers);   // rows per consumer thread
 constexpr int kQRowStride = kQRows / kQRpt;
+constexpr int kPreWaitStages = 1;   // weight stages a CTA requests before griddepcontrol.wait (see above)
 
 LK_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LK_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -109,7 +113,7 @@ __global__ void __launch_bounds__(kQThreads)
       griddep_launch();
       prefetch_tensormap(&wmap);
       const uint32_t bytes = kQWBytes + TOKB * 256 + TOKB * 64;
-      const int pre = min(kQStages, nst);
+      const int pre = min(kPreWaitStages, nst);
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], bytes);
         tma_load_2d(smem + i * kStage, &wmap, (c0 + i) * (kChunkBytes / 4), row0, &full[i]);
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kQThreads)
       }
       for (int i = pre; i < nst; ++i) {
         const int s = i % kQStages;
-        if (!mbar_wait(&empty[s], ((i / kQStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        if (i >= kQStages && !mbar_wait(&empty[s], ((i / kQStages) - 1) & 1)) atomicOr(&g_status, 1u);
         mbar_expect_tx(&full[s], bytes);
         uint8_t* st = smem + s * kStage;
         tma_load_2d(st, &wmap, (c0 + i) * (kChunkBytes / 4), row0, &full[s]);
@@ -344,6 +348,7 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
       griddep_launch();
       for (int i = 0; i < my_stages; ++i) {
         const int s = i % kRStages;
+        if (i == kPreWaitStages) griddep_wait();   // the first stage only goes out before the previous grid ends
         if (i >= kRStages && !mbar_wait(&empty[s], ((i / kRStages) - 1) & 1)) atomicOr(&g_status, 1u);
         const int st = int(blockIdx.x) + i * int(gridDim.x);
         int r0;
