@@ -709,6 +709,17 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int ele
   return r == CUDA_SUCCESS ? LK_OK : LK_EINVAL;
 }
 
+// any tiled tensor map (dims, strides in bytes, box and element strides given in full), zero out-of-range fill
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return LK_ECUDA;
+  CUresult r = fn(map, dt, cuuint32_t(rank), const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LK_OK : LK_EINVAL;
+}
+
 struct GemmMaps {
   CUtensorMap a, w, w2;
 };

@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kQThreads)
 // lane l owns the K/2048 (chunk, page) units l + 32u of every row, so its activation codes and group meta are loaded
 // into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles and stores y.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kRStages = 4;
+constexpr int kRStages = 3;
 constexpr int kRowWarps = 4;   // consumer warps = rows per stage
 
 // the Q4_K (scale, min) pairs of groups (2pg, 2pg + 1) as "2^23 + value" floats: f[0..1] scales, f[2..3] minima.

@@ -21,6 +21,8 @@ namespace lk {
 
 int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
              int box_cols, int box_rows, CUtensorMapSwizzle swz);
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* estr, CUtensorMapSwizzle swz);
 
 namespace {
 
@@ -325,6 +327,321 @@ int launch_o(int order, const CUtensorMap& am, const CUtensorMap& wm, const CUte
   return launch<NW, GROUP, LK_ORDER_PAIRS>(am, wm, w2m, a, grid, s);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Persistent dense MXFP4 x e4m3 GEMM for pairs-order nibbles: the tensor map unpacks the e2m1 operand itself.
+//
+// A TMA load of data type 16U4_ALIGN16B writes every 16 packed nibbles into the first 8 bytes of a 16-byte slot and
+// leaves the other 8 alone: the layout kind::mxf8f6f4 reads e2m1 from. With the 128-byte swizzle the packed weight
+// rows land in the MMA's K-major operand layout directly, so no warps rewrite them (the transaction count is the
+// packed size). The map's K extent must be a multiple of 128 values: k = 128 q + 64 runs q stages over the first
+// 128 q values and one tail stage over the LAST 128 values (a second map based (k - 128) / 2 bytes into each row),
+// whose first 64 values, already counted, are skipped by starting that stage's MMAs at sub-step 2.
+//
+// One CTA per SM walks output tiles of 128 rows x 192 weight rows (swiglu: 96 gate + 96 up rows, one N = 192 MMA per
+// 32 k) into two TMEM accumulators, so the epilogue of a tile overlaps the accumulation of the next:
+//   warp 0     TMA producer: A box 128 x 128 bytes (e4m3, 128-byte swizzle) and the weight boxes, unpacked
+//   warp 1     TMEM owner; per stage copies the weights' scale-factor atoms into TMEM and issues the MMAs
+//   warps 2-3  stage the E8M0 bytes of every weight row in the scale-factor atom (row 32j + i at byte 16i + 4j),
+//              their loads issued kMxpSfAhead stages ahead of use
+//   warps 4-7  epilogue: TMEM lane quarter w % 4, row scale, silu(g) * u or the plain product, f32 stores
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kMxpNT = 192;                  // weight rows per tile = accumulator columns
+constexpr int kMxpS = 5;                     // stages
+constexpr int kMxpA = kBM * kBK;             // 16 KB of e4m3
+constexpr int kMxpB = kMxpNT * kBK;          // 24 KB of unpacked e2m1
+constexpr int kMxpBtx = kMxpNT * kBK / 2;    // 12 KB of packed nibbles: the weight boxes' transaction bytes
+constexpr int kMxpSF = 1024;                 // two scale-factor atoms: weight rows 0..127 and 128..255
+constexpr int kMxpThreads = 256;
+constexpr int kMxpSfAhead = 4;
+constexpr uint32_t kMxpAcc1 = 256, kMxpColSFA = 192, kMxpColSFB = 200;   // TMEM: acc 0..191 / 256..447, scales
+constexpr int kMxpSmem = 1024 + kMxpS * (kMxpA + kMxpB + kMxpSF) + 512 + 8 * (3 * kMxpS + 4) + 16;
+static_assert(kMxpSmem <= 227 * 1024, "persistent MXFP4 GEMM CTA exceeds shared memory");
+static_assert(kMxpColSFB + 8 * kMxpS <= kMxpAcc1, "scale-factor columns overlap the second accumulator");
+
+struct MxpArgs {
+  const float* s8;        // [rows][2]
+  float* y;               // [rows][n]
+  const uint8_t* ws;      // E8M0 plane of w  [n][k/32]
+  const uint8_t* ws2;     // E8M0 plane of w2
+  int rows, k, n;
+  int sf_stride;          // k / 32
+  int kmain;              // stages over the first 128 * kmain values
+  int tail_sub;           // first MMA sub-step of the tail stage; 4 = no tail stage
+  int m_tiles, n_tiles;
+};
+
+template <int NW>
+__global__ void __launch_bounds__(kMxpThreads, 1)
+    k_gemm_mxp(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+               const __grid_constant__ CUtensorMap w2map, const __grid_constant__ CUtensorMap wtmap,
+               const __grid_constant__ CUtensorMap w2tmap, const MxpArgs p) {
+  constexpr int BNW = kMxpNT / NW;   // columns of each weight per tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kMxpS * kMxpA;
+  uint8_t* sSF = sB + kMxpS * kMxpB;       // [kMxpS][1024]
+  uint8_t* sSFA = sSF + kMxpS * kMxpSF;    // 512 bytes of 127 (2^0): the activations' block scales
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFA + 512);
+  uint64_t* sfull = full + kMxpS;
+  uint64_t* empty = sfull + kMxpS;
+  uint64_t* accf = empty + kMxpS;          // [2]
+  uint64_t* acce = accf + 2;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nks = p.kmain + (p.tail_sub < 4 ? 1 : 0);
+  const int ntiles = p.m_tiles * p.n_tiles;
+  const int my_tiles = int(blockIdx.x) < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMxpS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&sfull[i], 2);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 4);
+    }
+    fence_mbar_init();
+  }
+  // the TMA never writes the 8-byte gaps of the unpacked weight tiles: zero them once; unused scale rows = 2^0
+  for (int i = threadIdx.x; i < kMxpS * kMxpB / 16; i += kMxpThreads)
+    reinterpret_cast<uint4*>(sB)[i] = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = threadIdx.x; i < (kMxpS * kMxpSF + 512) / 4; i += kMxpThreads)
+    reinterpret_cast<uint32_t*>(sSF)[i] = 0x7F7F7F7Fu;
+  fence_proxy_async();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&amap);
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&wtmap);
+      if (NW == 2) {
+        prefetch_tensormap(&w2map);
+        prefetch_tensormap(&w2tmap);
+      }
+      uint32_t g = 0;
+      for (int ti = 0; ti < my_tiles; ++ti) {
+        const int t = int(blockIdx.x) + ti * int(gridDim.x);
+        const int m0 = (t / p.n_tiles) * kBM, n0 = (t % p.n_tiles) * BNW;
+        for (int ks = 0; ks < nks; ++ks, ++g) {
+          const int s = int(g % kMxpS);
+          if (g >= uint32_t(kMxpS) && !mbar_wait(&empty[s], ((g / kMxpS) - 1) & 1)) atomicOr(&g_status, 1u);
+          const bool tail = ks == p.kmain;
+          mbar_expect_tx(&full[s], uint32_t(kMxpA + kMxpBtx));
+          tma_load_2d(sA + s * kMxpA, &amap, tail ? p.k - kBK : ks * kBK, m0, &full[s]);
+          uint8_t* b = sB + s * kMxpB;
+          tma_load_2d(b, tail ? &wtmap : &wmap, tail ? 0 : ks * kBK, n0, &full[s]);
+          if (NW == 2) tma_load_2d(b + BNW * kBK, tail ? &w2tmap : &w2map, tail ? 0 : ks * kBK, n0, &full[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ scale-factor copies + MMA issue
+    if (lane == 0) tmem_cp_32x128_x4(tmem + kMxpColSFA, sdesc_rows16(smem_u32(sSFA)));
+    uint32_t g = 0;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const int b = ti & 1;
+      if (ti >= 2 && !mbar_wait(&acce[b], ((ti >> 1) - 1) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+      const uint32_t acc = tmem + uint32_t(b) * kMxpAcc1;
+      for (int ks = 0; ks < nks; ++ks, ++g) {
+        const int s = int(g % kMxpS);
+        const uint32_t ph = (g / kMxpS) & 1;
+        if (!mbar_wait(&full[s], ph)) atomicOr(&g_status, 1u);
+        if (!mbar_wait(&sfull[s], ph)) atomicOr(&g_status, 1u);
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sfb = tmem + kMxpColSFB + 8 * s;
+          tmem_cp_32x128_x4(sfb, sdesc_rows16(smem_u32(sSF + s * kMxpSF)));
+          tmem_cp_32x128_x4(sfb + 4, sdesc_rows16(smem_u32(sSF + s * kMxpSF + 512)));
+          const int s0 = ks == p.kmain ? p.tail_sub : 0;
+          const uint32_t a_base = smem_u32(sA + s * kMxpA), b_base = smem_u32(sB + s * kMxpB);
+#pragma unroll
+          for (int j = 0; j < kBK / 32; ++j) {
+            if (j < s0) continue;
+            umma_mx(acc, sdesc_k128(a_base + j * 32), sdesc_k128(b_base + j * 32), idesc_mx(kBM, kMxpNT, 0, 5, j, j),
+                    (tmem + kMxpColSFA) | (uint32_t(j) << 30), sfb | (uint32_t(j) << 30), (ks | (j - s0)) != 0);
+          }
+          umma_commit(&empty[s]);
+          if (ks == nks - 1) umma_commit(&accf[b]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ E8M0 scale staging
+    const int jt = threadIdx.x - 64;   // tile weight rows jt, jt + 64, jt + 128
+    const int total = my_tiles * nks;
+    // two 16-bit loads per row per stage (row stride k/32 and block offsets are even); beyond the CTA's last stage
+    // or past n: 2^0 without a load
+    auto issue = [&](int q, uint32_t (&v)[3][2]) {
+      const int ti = q / nks, ks = q - ti * nks;
+      const int t = int(blockIdx.x) + ti * int(gridDim.x);
+      const int n0 = (t % p.n_tiles) * BNW;
+      const int b0 = ks < p.kmain ? 4 * ks : (p.k - kBK) / 32;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        const int r = jt + 64 * i;
+        const int wi = r / BNW, rr = r - wi * BNW;
+        const bool ok = q < total && n0 + rr < p.n;
+        const uint16_t* src =
+            reinterpret_cast<const uint16_t*>((wi ? p.ws2 : p.ws) + int64_t(n0 + rr) * p.sf_stride + b0);
+        v[i][0] = ok ? uint32_t(__ldg(src)) : 0x7F7Fu;
+        v[i][1] = ok ? uint32_t(__ldg(src + 1)) : 0x7F7Fu;
+      }
+    };
+    uint32_t ring[kMxpSfAhead][3][2];
+#pragma unroll
+    for (int a = 0; a < kMxpSfAhead; ++a) issue(a, ring[a]);
+    for (int q0 = 0; q0 < total; q0 += kMxpSfAhead) {
+#pragma unroll
+      for (int a = 0; a < kMxpSfAhead; ++a) {
+        const int q = q0 + a;
+        if (q < total) {
+          const int s = q % kMxpS;
+          if (q >= kMxpS && !mbar_wait(&empty[s], ((q / kMxpS) - 1) & 1)) atomicOr(&g_status, 1u);
+          uint8_t* atom = sSF + s * kMxpSF;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) {
+            const int r = jt + 64 * i;
+            *reinterpret_cast<uint32_t*>(atom + (r >> 7) * 512 + 16 * (r & 31) + 4 * ((r & 127) >> 5)) =
+                ring[a][i][0] | (ring[a][i][1] << 16);
+          }
+          issue(q + kMxpSfAhead, ring[a]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sfull[s]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (TMEM lanes 32 (w % 4) ..)
+    const int qd = warp & 3;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const int t = int(blockIdx.x) + ti * int(gridDim.x);
+      const int b = ti & 1;
+      const int m0 = (t / p.n_tiles) * kBM, n0 = (t % p.n_tiles) * BNW;
+      if (!mbar_wait(&accf[b], (ti >> 1) & 1)) atomicOr(&g_status, 1u);
+      tc_fence_after();
+      const int row = m0 + 32 * qd + lane;
+      const bool ok = row < p.rows;
+      const float inv = ok ? __ldg(p.s8 + 2 * int64_t(row) + 1) * 256.0f : 0.f;   // 2^8: the weight pre-scale
+      float* yrow = p.y + int64_t(ok ? row : 0) * p.n + n0;
+      const uint32_t tb = tmem + uint32_t(b) * kMxpAcc1 + (uint32_t(32 * qd) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BNW; c += 32) {
+        float v[32];
+        tmem_ld32(tb + c, v);
+        if (NW == 2) {
+          float u[32];
+          tmem_ld32(tb + BNW + c, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= inv;
+        }
+        if (c + 32 >= BNW) {   // the tile's last TMEM read is done: hand the accumulator back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce[b]);
+        }
+        if (ok) {
+          if ((p.n & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              if (n0 + c + i < p.n)
+                *reinterpret_cast<float4*>(yrow + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n0 + c + i < p.n) yrow[c + i] = v[i];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// 2-D map over MXFP4 nibble rows that unpacks 16 values per 16-byte slot: `vals` values per row from `base`, rows
+// `row_bytes` apart, boxes of 128 values x box_rows rows, 128-byte swizzle
+int make_map_u4(CUtensorMap* map, const void* base, int64_t rows, int64_t vals, int64_t row_bytes, int box_rows) {
+  cuuint64_t dims[2] = {cuuint64_t(vals), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+  cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// the persistent kernel's conditions: dense, pairs order, k a multiple of 64 (at least 128), 32-byte aligned planes
+bool mxp_applies(int order, int k, const uint8_t* w, const uint8_t* w2) {
+  auto a32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31) == 0; };
+  return order == LK_ORDER_PAIRS && k >= kBK && k % 64 == 0 && a32(w) && (!w2 || a32(w2));
+}
+
+int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
+             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s) {
+  const int NW = mode == LK_SWIGLU ? 2 : 1;
+  const int bnw = kMxpNT / NW;
+  MxpArgs a{};
+  a.s8 = s8;
+  a.y = y;
+  a.ws = ws;
+  a.ws2 = w2s ? w2s : ws;
+  a.rows = rows;
+  a.k = k;
+  a.n = n;
+  a.sf_stride = k / 32;
+  a.kmain = k / kBK;
+  a.tail_sub = k % kBK ? (kBK - k % kBK) / 32 : 4;
+  a.m_tiles = (rows + kBM - 1) / kBM;
+  a.n_tiles = (n + bnw - 1) / bnw;
+  const uint8_t* w2p = w2 ? w2 : w;
+  CUtensorMap am, wm, w2m, wtm, w2tm;
+  int rc = make_map(&am, x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == LK_OK) rc = make_map_u4(&wm, w, n, int64_t(a.kmain) * kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&wtm, w + (k - kBK) / 2, n, kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&w2m, w2p, n, int64_t(a.kmain) * kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&w2tm, w2p + (k - kBK) / 2, n, kBK, k / 2, bnw);
+  if (rc != LK_OK) return rc;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = min(sms, a.m_tiles * a.n_tiles);
+  if (NW == 2) {
+    static unsigned configured = 0;
+    if (!once_per_device(configured))
+      cudaFuncSetAttribute(k_gemm_mxp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
+    k_gemm_mxp<2><<<grid, kMxpThreads, kMxpSmem, s>>>(am, wm, w2m, wtm, w2tm, a);
+  } else {
+    static unsigned configured = 0;
+    if (!once_per_device(configured))
+      cudaFuncSetAttribute(k_gemm_mxp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
+    k_gemm_mxp<1><<<grid, kMxpThreads, kMxpSmem, s>>>(am, wm, w2m, wtm, w2tm, a);
+  }
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
 }  // namespace
 
 // dense (tile_info == nullptr) or grouped over the MoE schedule
@@ -332,6 +649,8 @@ int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, cons
             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
             int w2_row_offset) {
+  if (!tile_info && mxp_applies(order, k, w, w2))
+    return gemm_mxp(mode, rows, k, n, x8, s8, w, ws, w2, w2s, y, s);
   const int NW = mode == LK_SWIGLU ? 2 : 1;
   const int bn = kRowsB / NW;
   MxArgs a{};
