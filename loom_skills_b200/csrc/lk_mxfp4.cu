@@ -17,6 +17,8 @@
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
+#include <algorithm>
+
 namespace lk {
 
 int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
@@ -338,7 +340,9 @@ int launch_o(int order, const CUtensorMap& am, const CUtensorMap& wm, const CUte
 // whose first 64 values, already counted, are skipped by starting that stage's MMAs at sub-step 2.
 //
 // One CTA per SM walks output tiles of 128 rows x 192 weight rows (swiglu: 96 gate + 96 up rows, one N = 192 MMA per
-// 32 k) into two TMEM accumulators, so the epilogue of a tile overlaps the accumulation of the next:
+// 32 k) into two TMEM accumulators, so the epilogue of a tile overlaps the accumulation of the next. Grouped over the
+// MoE schedule a tile's rows are one 128-row super-tile of an expert (its table built in shared memory at start):
+// gate/up gathers the token rows of x8 by TMA gather4, down reads the sorted rows.
 //   warp 0     TMA producer: A box 128 x 128 bytes (e4m3, 128-byte swizzle) and the weight boxes, unpacked
 //   warp 1     TMEM owner; per stage copies the weights' scale-factor atoms into TMEM and issues the MMAs
 //   warps 2-3  stage the E8M0 bytes of every weight row in the scale-factor atom (row 32j + i at byte 16i + 4j),
@@ -354,7 +358,7 @@ constexpr int kMxpSF = 1024;                 // two scale-factor atoms: weight r
 constexpr int kMxpThreads = 256;
 constexpr int kMxpSfAhead = 4;
 constexpr uint32_t kMxpAcc1 = 256, kMxpColSFA = 192, kMxpColSFB = 200;   // TMEM: acc 0..191 / 256..447, scales
-constexpr int kMxpSmem = 1024 + kMxpS * (kMxpA + kMxpB + kMxpSF) + 512 + 8 * (3 * kMxpS + 4) + 16;
+constexpr int kMxpSmem = 1024 + kMxpS * (kMxpA + kMxpB + kMxpSF) + 512 + 8 * (3 * kMxpS + 4) + 16 + 3 * kMaxExperts * 4;
 static_assert(kMxpSmem <= 227 * 1024, "persistent MXFP4 GEMM CTA exceeds shared memory");
 static_assert(kMxpColSFB + 8 * kMxpS <= kMxpAcc1, "scale-factor columns overlap the second accumulator");
 
@@ -367,10 +371,15 @@ struct MxpArgs {
   int sf_stride;          // k / 32
   int kmain;              // stages over the first 128 * kmain values
   int tail_sub;           // first MMA sub-step of the tail stage; 4 = no tail stage
-  int m_tiles, n_tiles;
+  int m_tiles, n_tiles;   // dense: row tiles; grouped: m_tiles unused (super-tiles counted on the device)
+  // grouped over the MoE schedule
+  const int32_t* tile_info;
+  const int32_t* rowmap;
+  int max_tiles, xrows, ku, n_experts;
+  int rows_per_expert, rows_per_expert2, w2_row_offset;
 };
 
-template <int NW>
+template <int NW, int GROUP>
 __global__ void __launch_bounds__(kMxpThreads, 1)
     k_gemm_mxp(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
                const __grid_constant__ CUtensorMap w2map, const __grid_constant__ CUtensorMap wtmap,
@@ -388,11 +397,28 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
   uint64_t* accf = empty + kMxpS;          // [2]
   uint64_t* acce = accf + 2;               // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  int* stbl = reinterpret_cast<int*>(tmem_slot + 4);   // [3][kMaxExperts]: the MoE super-tile table
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nks = p.kmain + (p.tail_sub < 4 ? 1 : 0);
-  const int ntiles = p.m_tiles * p.n_tiles;
+  const int msup = GROUP == kDense ? p.m_tiles : moe_super_table(p.tile_info, p.max_tiles, p.n_experts, stbl);
+  const int ntiles = msup * p.n_tiles;
   const int my_tiles = int(blockIdx.x) < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  // tile t: rows m0 .. m0 + vrows - 1 (dense: of x8 / y; grouped: sorted positions of expert `e`), columns n0 ..
+  auto tile_of = [&](int t, int& m0, int& vrows, int& e, int& n0) {
+    const int mt = t / p.n_tiles;
+    n0 = (t - mt * p.n_tiles) * BNW;
+    if (GROUP == kDense) {
+      m0 = mt * kBM;
+      vrows = min(kBM, p.rows - m0);
+      e = 0;
+    } else {
+      int first;
+      moe_super_lookup(p.tile_info, stbl, mt, e, first, vrows);
+      e = min(max(e, 0), p.n_experts - 1);
+      m0 = first * 64;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMxpS; ++i) {
@@ -422,7 +448,7 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+    // ------------------------------------------------------------------ producer (gather: every lane, 4 rows each)
     if (lane == 0) {
       prefetch_tensormap(&amap);
       prefetch_tensormap(&wmap);
@@ -431,20 +457,38 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
         prefetch_tensormap(&w2map);
         prefetch_tensormap(&w2tmap);
       }
-      uint32_t g = 0;
-      for (int ti = 0; ti < my_tiles; ++ti) {
-        const int t = int(blockIdx.x) + ti * int(gridDim.x);
-        const int m0 = (t / p.n_tiles) * kBM, n0 = (t % p.n_tiles) * BNW;
-        for (int ks = 0; ks < nks; ++ks, ++g) {
-          const int s = int(g % kMxpS);
-          if (g >= uint32_t(kMxpS) && !mbar_wait(&empty[s], ((g / kMxpS) - 1) & 1)) atomicOr(&g_status, 1u);
-          const bool tail = ks == p.kmain;
-          mbar_expect_tx(&full[s], uint32_t(kMxpA + kMxpBtx));
-          tma_load_2d(sA + s * kMxpA, &amap, tail ? p.k - kBK : ks * kBK, m0, &full[s]);
-          uint8_t* b = sB + s * kMxpB;
-          tma_load_2d(b, tail ? &wtmap : &wmap, tail ? 0 : ks * kBK, n0, &full[s]);
-          if (NW == 2) tma_load_2d(b + BNW * kBK, tail ? &w2tmap : &w2map, tail ? 0 : ks * kBK, n0, &full[s]);
+    }
+    uint32_t g = 0;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const int t = int(blockIdx.x) + ti * int(gridDim.x);
+      int m0, vrows, e, n0;
+      tile_of(t, m0, vrows, e, n0);
+      const int wrow = e * p.rows_per_expert + n0;
+      const int w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
+      int arow[4];   // gather: the token rows of tile rows 4 lane .. 4 lane + 3 (xrows: past the end, zero-filled)
+      if (GROUP == kGather) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = 4 * lane + i;
+          const int a = r < vrows ? __ldg(p.rowmap + m0 + r) : -1;
+          arow[i] = a >= 0 ? a / p.ku : p.xrows;
         }
+      }
+      for (int ks = 0; ks < nks; ++ks, ++g) {
+        const int s = int(g % kMxpS);
+        if (g >= uint32_t(kMxpS) && !mbar_wait(&empty[s], ((g / kMxpS) - 1) & 1)) atomicOr(&g_status, 1u);
+        const bool tail = ks == p.kmain;
+        const int ka = tail ? p.k - kBK : ks * kBK;
+        if (lane == 0) {
+          mbar_expect_tx(&full[s], uint32_t(kMxpA + kMxpBtx));
+          if (GROUP != kGather) tma_load_2d(sA + s * kMxpA, &amap, ka, m0, &full[s]);
+          uint8_t* b = sB + s * kMxpB;
+          tma_load_2d(b, tail ? &wtmap : &wmap, tail ? 0 : ks * kBK, wrow, &full[s]);
+          if (NW == 2) tma_load_2d(b + BNW * kBK, tail ? &w2tmap : &w2map, tail ? 0 : ks * kBK, w2row, &full[s]);
+        }
+        __syncwarp();
+        if (GROUP == kGather)
+          tma_gather4(sA + s * kMxpA + 4 * lane * kBK, &amap, ka, arow[0], arow[1], arow[2], arow[3], &full[s]);
       }
     }
     __syncwarp();
@@ -487,18 +531,25 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
     const int total = my_tiles * nks;
     // two 16-bit loads per row per stage (row stride k/32 and block offsets are even); beyond the CTA's last stage
     // or past n: 2^0 without a load
+    int cur_t = -1, wrow = 0, w2row = 0, n0 = 0;   // the tile whose weight rows are cached
     auto issue = [&](int q, uint32_t (&v)[3][2]) {
       const int ti = q / nks, ks = q - ti * nks;
       const int t = int(blockIdx.x) + ti * int(gridDim.x);
-      const int n0 = (t % p.n_tiles) * BNW;
+      if (q < total && t != cur_t) {
+        int m0, vrows, e;
+        tile_of(t, m0, vrows, e, n0);
+        wrow = e * p.rows_per_expert + n0;
+        w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
+        cur_t = t;
+      }
       const int b0 = ks < p.kmain ? 4 * ks : (p.k - kBK) / 32;
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         const int r = jt + 64 * i;
         const int wi = r / BNW, rr = r - wi * BNW;
         const bool ok = q < total && n0 + rr < p.n;
-        const uint16_t* src =
-            reinterpret_cast<const uint16_t*>((wi ? p.ws2 : p.ws) + int64_t(n0 + rr) * p.sf_stride + b0);
+        const uint16_t* src = reinterpret_cast<const uint16_t*>((wi ? p.ws2 : p.ws) +
+                                                                int64_t((wi ? w2row : wrow) + rr) * p.sf_stride + b0);
         v[i][0] = ok ? uint32_t(__ldg(src)) : 0x7F7Fu;
         v[i][1] = ok ? uint32_t(__ldg(src + 1)) : 0x7F7Fu;
       }
@@ -533,12 +584,19 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
     for (int ti = 0; ti < my_tiles; ++ti) {
       const int t = int(blockIdx.x) + ti * int(gridDim.x);
       const int b = ti & 1;
-      const int m0 = (t / p.n_tiles) * kBM, n0 = (t % p.n_tiles) * BNW;
+      int m0, vrows, e, n0;
+      tile_of(t, m0, vrows, e, n0);
+      const int r = 32 * qd + lane;
+      const bool ok = r < vrows;
+      const int row = m0 + r;   // output row (grouped: sorted position)
+      int srow = row;           // its activation scale row (gather: the token)
+      if (GROUP == kGather && ok) {
+        const int a = __ldg(p.rowmap + row);
+        srow = a >= 0 ? a / p.ku : -1;
+      }
+      const float inv = ok && srow >= 0 ? __ldg(p.s8 + 2 * int64_t(srow) + 1) * 256.0f : 0.f;   // 2^8: weight pre-scale
       if (!mbar_wait(&accf[b], (ti >> 1) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
-      const int row = m0 + 32 * qd + lane;
-      const bool ok = row < p.rows;
-      const float inv = ok ? __ldg(p.s8 + 2 * int64_t(row) + 1) * 256.0f : 0.f;   // 2^8: the weight pre-scale
       float* yrow = p.y + int64_t(ok ? row : 0) * p.n + n0;
       const uint32_t tb = tmem + uint32_t(b) * kMxpAcc1 + (uint32_t(32 * qd) << 16);
 #pragma unroll 1
@@ -594,15 +652,31 @@ int make_map_u4(CUtensorMap* map, const void* base, int64_t rows, int64_t vals, 
 }
 
 // the persistent kernel's conditions: dense, pairs order, k a multiple of 64 (at least 128), 32-byte aligned planes
-bool mxp_applies(int order, int k, const uint8_t* w, const uint8_t* w2) {
-  auto a32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31) == 0; };
-  return order == LK_ORDER_PAIRS && k >= kBK && k % 64 == 0 && a32(w) && (!w2 || a32(w2));
+// the persistent kernel's conditions: pairs order, k a multiple of 64 (at least 128), 32-byte aligned nibble planes,
+// 2-byte aligned scale planes
+bool mxp_applies(int order, int k, const uint8_t* w, const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s) {
+  auto al = [](const void* q, uintptr_t b) { return (reinterpret_cast<uintptr_t>(q) & (b - 1)) == 0; };
+  return order == LK_ORDER_PAIRS && k >= kBK && k % 64 == 0 && al(w, 32) && al(ws, 2) && (!w2 || al(w2, 32)) &&
+         (!w2s || al(w2s, 2));
 }
 
+template <int NW, int GROUP>
+int launch_mxp(const CUtensorMap* m, const MxpArgs& a, int grid, cudaStream_t s) {
+  auto kern = k_gemm_mxp<NW, GROUP>;
+  static unsigned configured = 0;
+  if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
+  kern<<<grid, kMxpThreads, kMxpSmem, s>>>(m[0], m[1], m[2], m[3], m[4], a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// dense (tile_info == nullptr) or grouped over the MoE schedule, arguments as gemm_mx
 int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
-             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s) {
+             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
+             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
+             int w2_row_offset) {
   const int NW = mode == LK_SWIGLU ? 2 : 1;
   const int bnw = kMxpNT / NW;
+  const int group = tile_info ? (NW == 2 ? kGather : kSorted) : kDense;
   MxpArgs a{};
   a.s8 = s8;
   a.y = y;
@@ -616,30 +690,39 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
   a.tail_sub = k % kBK ? (kBK - k % kBK) / 32 : 4;
   a.m_tiles = (rows + kBM - 1) / kBM;
   a.n_tiles = (n + bnw - 1) / bnw;
+  int64_t wrows = n, w2rows = n;
+  a.w2_row_offset = (NW == 2 && !w2) ? w2_row_offset : 0;
+  if (tile_info) {
+    a.tile_info = tile_info;
+    a.rowmap = rowmap;
+    a.max_tiles = rows / 64;
+    a.xrows = xrows;
+    a.ku = ku;
+    a.n_experts = n_experts;
+    a.rows_per_expert = rows_per_expert;
+    a.rows_per_expert2 = w2 ? n : rows_per_expert;
+    wrows = int64_t(n_experts) * rows_per_expert;
+    w2rows = int64_t(n_experts) * a.rows_per_expert2;
+  }
   const uint8_t* w2p = w2 ? w2 : w;
-  CUtensorMap am, wm, w2m, wtm, w2tm;
-  int rc = make_map(&am, x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc == LK_OK) rc = make_map_u4(&wm, w, n, int64_t(a.kmain) * kBK, k / 2, bnw);
-  if (rc == LK_OK) rc = make_map_u4(&wtm, w + (k - kBK) / 2, n, kBK, k / 2, bnw);
-  if (rc == LK_OK) rc = make_map_u4(&w2m, w2p, n, int64_t(a.kmain) * kBK, k / 2, bnw);
-  if (rc == LK_OK) rc = make_map_u4(&w2tm, w2p + (k - kBK) / 2, n, kBK, k / 2, bnw);
+  CUtensorMap m[5];   // A, w, w2, w tail, w2 tail
+  int rc = group == kGather
+               ? make_map(&m[0], x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xrows, k, kBK, 1, CU_TENSOR_MAP_SWIZZLE_128B)
+               : make_map(&m[0], x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == LK_OK) rc = make_map_u4(&m[1], w, wrows, int64_t(a.kmain) * kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&m[2], w2p, w2rows, int64_t(a.kmain) * kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&m[3], w + (k - kBK) / 2, wrows, kBK, k / 2, bnw);
+  if (rc == LK_OK) rc = make_map_u4(&m[4], w2p + (k - kBK) / 2, w2rows, kBK, k / 2, bnw);
   if (rc != LK_OK) return rc;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = min(sms, a.m_tiles * a.n_tiles);
-  if (NW == 2) {
-    static unsigned configured = 0;
-    if (!once_per_device(configured))
-      cudaFuncSetAttribute(k_gemm_mxp<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
-    k_gemm_mxp<2><<<grid, kMxpThreads, kMxpSmem, s>>>(am, wm, w2m, wtm, w2tm, a);
-  } else {
-    static unsigned configured = 0;
-    if (!once_per_device(configured))
-      cudaFuncSetAttribute(k_gemm_mxp<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
-    k_gemm_mxp<1><<<grid, kMxpThreads, kMxpSmem, s>>>(am, wm, w2m, wtm, w2tm, a);
-  }
-  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+  // grouped: at most rows / 128 + n_experts super-tiles (the count itself is known on the device only)
+  const int64_t max_m = tile_info ? int64_t(rows) / kBM + n_experts : a.m_tiles;
+  const int grid = int(std::min(int64_t(sms), max_m * a.n_tiles));
+  if (group == kGather) return launch_mxp<2, kGather>(m, a, grid, s);
+  if (group == kSorted) return launch_mxp<1, kSorted>(m, a, grid, s);
+  return NW == 2 ? launch_mxp<2, kDense>(m, a, grid, s) : launch_mxp<1, kDense>(m, a, grid, s);
 }
 
 }  // namespace
@@ -649,8 +732,9 @@ int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, cons
             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
             int w2_row_offset) {
-  if (!tile_info && mxp_applies(order, k, w, w2))
-    return gemm_mxp(mode, rows, k, n, x8, s8, w, ws, w2, w2s, y, s);
+  if (mxp_applies(order, k, w, ws, w2, w2s))
+    return gemm_mxp(mode, rows, k, n, x8, s8, w, ws, w2, w2s, y, s, tile_info, rowmap, xrows, ku, n_experts,
+                    rows_per_expert, w2_row_offset);
   const int NW = mode == LK_SWIGLU ? 2 : 1;
   const int bn = kRowsB / NW;
   MxArgs a{};
