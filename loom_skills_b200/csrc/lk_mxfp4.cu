@@ -347,10 +347,12 @@ int launch_o(int order, const CUtensorMap& am, const CUtensorMap& wm, const CUte
 //   warp 1     TMEM owner; per stage copies the weights' scale-factor atoms into TMEM and issues the MMAs
 //   warps 2-3  stage the E8M0 bytes of every weight row in the scale-factor atom (row 32j + i at byte 16i + 4j),
 //              their loads issued kMxpSfAhead stages ahead of use
-//   warps 4-7  epilogue: TMEM lane quarter w % 4, row scale, silu(g) * u or the plain product, f32 stores
+//   warps 4-7  epilogue: TMEM lane quarter w % 4, row scale, silu(g) * u or the plain product; each warp's 32 x 32
+//              f32 blocks go through a 128-byte-swizzled shared tile and one TMA store (rows the tile does not
+//              own, in a partly filled MoE super-tile, are stored by the threads instead)
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kMxpNT = 192;                  // weight rows per tile = accumulator columns
-constexpr int kMxpS = 5;                     // stages
+constexpr int kMxpS = 4;                     // stages (5 measured the same)
 constexpr int kMxpA = kBM * kBK;             // 16 KB of e4m3
 constexpr int kMxpB = kMxpNT * kBK;          // 24 KB of unpacked e2m1
 constexpr int kMxpBtx = kMxpNT * kBK / 2;    // 12 KB of packed nibbles: the weight boxes' transaction bytes
@@ -358,7 +360,9 @@ constexpr int kMxpSF = 1024;                 // two scale-factor atoms: weight r
 constexpr int kMxpThreads = 256;
 constexpr int kMxpSfAhead = 4;
 constexpr uint32_t kMxpAcc1 = 256, kMxpColSFA = 192, kMxpColSFB = 200;   // TMEM: acc 0..191 / 256..447, scales
-constexpr int kMxpSmem = 1024 + kMxpS * (kMxpA + kMxpB + kMxpSF) + 512 + 8 * (3 * kMxpS + 4) + 16 + 3 * kMaxExperts * 4;
+constexpr int kMxpStg = 4 * 32 * 32 * 4;     // epilogue staging: a 32 x 32 f32 block per epilogue warp
+constexpr int kMxpSmem =
+    1024 + kMxpS * (kMxpA + kMxpB + kMxpSF) + kMxpStg + 512 + 8 * (3 * kMxpS + 4) + 16 + 3 * kMaxExperts * 4;
 static_assert(kMxpSmem <= 227 * 1024, "persistent MXFP4 GEMM CTA exceeds shared memory");
 static_assert(kMxpColSFB + 8 * kMxpS <= kMxpAcc1, "scale-factor columns overlap the second accumulator");
 
@@ -383,14 +387,15 @@ template <int NW, int GROUP>
 __global__ void __launch_bounds__(kMxpThreads, 1)
     k_gemm_mxp(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
                const __grid_constant__ CUtensorMap w2map, const __grid_constant__ CUtensorMap wtmap,
-               const __grid_constant__ CUtensorMap w2tmap, const MxpArgs p) {
+               const __grid_constant__ CUtensorMap w2tmap, const __grid_constant__ CUtensorMap ymap, const MxpArgs p) {
   constexpr int BNW = kMxpNT / NW;   // columns of each weight per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + kMxpS * kMxpA;
   uint8_t* sSF = sB + kMxpS * kMxpB;       // [kMxpS][1024]
-  uint8_t* sSFA = sSF + kMxpS * kMxpSF;    // 512 bytes of 127 (2^0): the activations' block scales
+  float* sStg = reinterpret_cast<float*>(sSF + kMxpS * kMxpSF);   // [4][32][32] f32, 1024-byte aligned
+  uint8_t* sSFA = sSF + kMxpS * kMxpSF + kMxpStg;   // 512 bytes of 127 (2^0): the activations' block scales
   uint64_t* full = reinterpret_cast<uint64_t*>(sSFA + 512);
   uint64_t* sfull = full + kMxpS;
   uint64_t* empty = sfull + kMxpS;
@@ -435,8 +440,8 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
   // the TMA never writes the 8-byte gaps of the unpacked weight tiles: zero them once; unused scale rows = 2^0
   for (int i = threadIdx.x; i < kMxpS * kMxpB / 16; i += kMxpThreads)
     reinterpret_cast<uint4*>(sB)[i] = make_uint4(0u, 0u, 0u, 0u);
-  for (int i = threadIdx.x; i < (kMxpS * kMxpSF + 512) / 4; i += kMxpThreads)
-    reinterpret_cast<uint32_t*>(sSF)[i] = 0x7F7F7F7Fu;
+  for (int i = threadIdx.x; i < kMxpS * kMxpSF / 4; i += kMxpThreads) reinterpret_cast<uint32_t*>(sSF)[i] = 0x7F7F7F7Fu;
+  if (threadIdx.x < 128) reinterpret_cast<uint32_t*>(sSFA)[threadIdx.x] = 0x7F7F7F7Fu;
   fence_proxy_async();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -581,6 +586,8 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (TMEM lanes 32 (w % 4) ..)
     const int qd = warp & 3;
+    float* stg = sStg + qd * 1024;
+    if (lane == 0) prefetch_tensormap(&ymap);
     for (int ti = 0; ti < my_tiles; ++ti) {
       const int t = int(blockIdx.x) + ti * int(gridDim.x);
       const int b = ti & 1;
@@ -617,7 +624,23 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acce[b]);
         }
-        if (ok) {
+        // the TMA store clips rows past p.rows and columns past n; a grouped tile's rows past vrows belong to the
+        // next super-tile, so a warp with any of those stores its own rows
+        if (GROUP == kDense || 32 * qd + 31 < vrows) {
+          if (m0 + 32 * qd >= p.rows || n0 + c >= p.n) continue;   // nothing of this block is in the output
+          if (lane == 0) bulk_wait_group_read0();   // this warp's previous block has left the staging tile
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)   // 16-byte chunk i of row `lane` at chunk i ^ (lane % 8): the 128-byte swizzle
+            *reinterpret_cast<float4*>(stg + lane * 32 + ((i ^ (lane & 7)) << 2)) =
+                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&ymap, stg, n0 + c, m0 + 32 * qd);
+            bulk_commit_group();
+          }
+        } else if (ok) {
           if ((p.n & 3) == 0) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
@@ -631,6 +654,7 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_group0();   // every TMA store of this warp has completed
   }
   tc_fence_before();
   __syncthreads();
@@ -665,7 +689,7 @@ int launch_mxp(const CUtensorMap* m, const MxpArgs& a, int grid, cudaStream_t s)
   auto kern = k_gemm_mxp<NW, GROUP>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxpSmem);
-  kern<<<grid, kMxpThreads, kMxpSmem, s>>>(m[0], m[1], m[2], m[3], m[4], a);
+  kern<<<grid, kMxpThreads, kMxpSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
@@ -705,7 +729,7 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
   const uint8_t* w2p = w2 ? w2 : w;
-  CUtensorMap m[5];   // A, w, w2, w tail, w2 tail
+  CUtensorMap m[6];   // A, w, w2, w tail, w2 tail, y
   int rc = group == kGather
                ? make_map(&m[0], x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xrows, k, kBK, 1, CU_TENSOR_MAP_SWIZZLE_128B)
                : make_map(&m[0], x8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -713,6 +737,8 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
   if (rc == LK_OK) rc = make_map_u4(&m[2], w2p, w2rows, int64_t(a.kmain) * kBK, k / 2, bnw);
   if (rc == LK_OK) rc = make_map_u4(&m[3], w + (k - kBK) / 2, wrows, kBK, k / 2, bnw);
   if (rc == LK_OK) rc = make_map_u4(&m[4], w2p + (k - kBK) / 2, w2rows, kBK, k / 2, bnw);
+  if (rc == LK_OK)
+    rc = make_map(&m[5], y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != LK_OK) return rc;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
