@@ -32,8 +32,10 @@ typedef struct CUstream_st* lk_stream_t;   /* == cudaStream_t */
 enum { LK_Q4_0 = 2, LK_Q4_K = 12, LK_IQ4_NL = 20, LK_MXFP4 = 39, LK_MXFP4S = 1039 };
 /* element types (ggml ids where ggml has one) */
 enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 30, LK_E4M3 = 1000 };
-/* GEMM epilogues (gen_gemm.py:535 `mode`): y = acc, y += acc, y = silu(acc_w) * acc_w2 */
-enum { LK_STORE = 0, LK_ACC = 1, LK_SWIGLU = 2 };
+/* GEMM epilogues (gen_gemm.py:535 `mode`): y = acc, y += acc, y = silu(acc_w) * acc_w2. LK_SWIGLU_SORTED (grouped
+ * GEMMs only; no counterpart in the reference, whose gate/up gathers token rows inside the GEMM): the swiglu gate/up
+ * on activation rows already in bucket order (lk_moe_row_scale_gather's output), read as plain tiles. */
+enum { LK_STORE = 0, LK_ACC = 1, LK_SWIGLU = 2, LK_SWIGLU_SORTED = 3 };
 /* MXFP4 nibble order inside a 32-value block (gen_mxfp4s.py:1-7): OCP pairs, or ggml split16 */
 enum { LK_ORDER_PAIRS = 0, LK_ORDER_SPLIT16 = 1 };
 
@@ -131,7 +133,7 @@ int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t
 /* The MXFP4 x FP8 GEMM grouped over the MoE tile schedule: the grouped-GEMM signature (gen_moe.py:1145-1146,
  * %xrows, %tile_info, %rowmap before %x) with the fp8 GEMM's operands (gen_mxfp4s.py:101). Rows, tiles, gather,
  * fused gate/up and skipped tiles as lk_moe_grouped_gemm; x8/s8 as lk_gemm_mxfp4s_f8 (gate/up: [xrows] token rows,
- * down: [rows] sorted rows); w/ws per expert n rows (fused gate/up: 2n, gate then up) of k/2 nibble bytes and k/32
+ * LK_SWIGLU_SORTED gate/up and down: [rows] sorted rows); w/ws per expert n rows (fused gate/up: 2n, gate then up) of k/2 nibble bytes and k/32
  * E8M0 bytes. */
 int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
                                   int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
@@ -153,8 +155,10 @@ int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, i
  * lk_moe_grouped_gemm: g_moe_ggu_{fmt}[_fused]_k{H} / g_moe_gdn_{fmt}_k{F} (gen_moe.py:1126-1228), launch(%rows,
  *   %k, %n, %xrows, %tile_info, %rowmap, %x, %scales, %w [, %w2], %y). mode LK_SWIGLU (gate/up): A rows gathered
  *   from x16[rowmap[r] / ku] (rowmap < 0 -> zero row), y[r] = silu(g) * u with g, u scaled by scales[token][1];
- *   fused: w holds per expert n gate rows then n up rows. mode LK_STORE (down): A = sorted rows x16[r],
- *   y[r] = acc * scales[r][1]. Tiles with expert < 0 are skipped (their y rows are not written).
+ *   fused: w holds per expert n gate rows then n up rows. mode LK_SWIGLU_SORTED: the same gate/up with A = sorted
+ *   rows x16[r] and scales[r] (x16 [rows][k] from lk_moe_row_scale_gather; xrows is then not read). mode LK_STORE
+ *   (down): A = sorted rows x16[r], y[r] = acc * scales[r][1]. Tiles with expert < 0 are skipped (their y rows are
+ *   not written).
  * lk_moe_combine_sorted: g_moe_combine_sorted (gen_moe.py:1231-1280), launch(%tokens, %rows, %ys, %pos, %wts, %y):
  *   y[t] (+)= sum_k wts[t][k] * ys[pos[t][k]] (pos < 0 -> 0).
  * lk_moe_expert_mv: decode expert matvecs g_moe_gu_{fmt} / g_moe_dn_{fmt} (gen_moe.py:535-727): mode 0 (gu):
@@ -168,6 +172,14 @@ int lk_moe_bucket(int tokens, int ku, int n_experts, int max_tiles, const int32_
 int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
                         const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
                         const void* w, const void* w2, float* y, lk_stream_t stream);
+/* lk_moe_row_scale_gather: the gate/up activations of a bucketed MoE in bucket order. No single counterpart in the
+ * reference: it is the gather g_moe_ggu_* does on its A loads (gen_moe.py:1126-1228) moved into the row-scale
+ * producer (g_row_scale_f16 / its fp8 twin, gen_llm.py:1843-1912, gen_mxfp4s.py:887-938). Row r of the outputs is
+ * lk_row_scale_f16 / lk_row_scale_f8 of x[rowmap[r] / ku] (a zero row where rowmap[r] < 0), bit for bit; x16/scales
+ * and x8/s8 are written when non-NULL. rows = the schedule's rows (max_tiles * 64); k % 8 == 0; x, x16 16-byte and
+ * x8 8-byte aligned. Feed the outputs to the grouped GEMMs with LK_SWIGLU_SORTED. */
+int lk_moe_row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, const void* x, int x_dtype,
+                            float* scales, uint16_t* x16, uint8_t* x8, float* s8, lk_stream_t stream);
 int lk_moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
                           const float* wts, float* y, lk_stream_t stream);
 int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,

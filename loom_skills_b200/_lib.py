@@ -8,10 +8,10 @@ LIB_PATH = os.path.join(HERE, "liblk.so")
 # formats / dtypes / modes (include/lk.h)
 Q4_0, Q4_K, IQ4_NL, MXFP4, MXFP4S = 2, 12, 20, 39, 1039
 F32, F16, BF16, E4M3 = 0, 1, 30, 1000
-STORE, ACC, SWIGLU = 0, 1, 2
+STORE, ACC, SWIGLU, SWIGLU_SORTED = 0, 1, 2, 3
 ORDER_PAIRS, ORDER_SPLIT16 = 0, 1
 FMT_IDS = {"q4_0": Q4_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "mxfp4": MXFP4, "mxfp4s": MXFP4S}
-MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU}
+MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU, "swiglu_sorted": SWIGLU_SORTED}
 
 _P, _I, _L, _F, _U = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint
 
@@ -43,6 +43,7 @@ SIGNATURES = {
     "lk_peer_close": (_I, [_P]),
     "lk_peer_free": (_I, [_P]),
     "lk_gemm_allgather": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, ctypes.POINTER(_P), _I, _I, _I, _P]),
+    "lk_moe_row_scale_gather": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "lk_moe_ffn_decode_noalloc": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
 }
 

@@ -107,6 +107,16 @@ int lk_row_scale_f8(int rows, int k, const void* x, int x_dtype, float* scales, 
   return row_scale(rows, k, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
 }
 
+int lk_moe_row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, const void* x, int x_dtype,
+                            float* scales, uint16_t* x16, uint8_t* x8, float* s8, lk_stream_t stream) {
+  if (rows < 0 || k <= 0 || k % 8 || ku <= 0) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!rowmap || !x || (!x16 && !x8) || (x16 && !scales) || (x8 && !s8)) return LK_EINVAL;
+  if (!aligned(x, 16) || !aligned(x16, 16) || !aligned(x8, 8)) return LK_EALIGN;
+  return row_scale_gather(rows, k, ku, rowmap, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
+}
+
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
           float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
@@ -205,19 +215,20 @@ int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, in
                         const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
                         const void* w, const void* w2, float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
-  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
   if (!tile_info || !rowmap || !x16 || !scales || !w || !y) return LK_EINVAL;
-  if (mode == LK_SWIGLU && !fused && !w2) return LK_EINVAL;
+  const bool gu = mode != LK_STORE;   // gate/up: gathered or already sorted activation rows
+  if (gu && !fused && !w2) return LK_EINVAL;
   if (k % 256 || n % 16) return LK_EINVAL;
   if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
   if (rows == 0) return LK_OK;
   int64_t rb = lk_row_bytes(fmt, k);
-  int64_t stride = rb * n * ((mode == LK_SWIGLU && fused) ? 2 : 1);
-  const void* w2e = (mode == LK_SWIGLU) ? (fused ? nullptr : w2) : nullptr;
+  int64_t stride = rb * n * ((gu && fused) ? 2 : 1);
+  const void* w2e = gu ? (fused ? nullptr : w2) : nullptr;
   return gemm(fmt, mode, rows, k, n, x16, scales, w, w2e, y, (cudaStream_t)stream, tile_info, rowmap, xrows, ku,
-              n_experts, stride, (mode == LK_SWIGLU && fused) ? rb * n : 0);
+              n_experts, stride, (gu && fused) ? rb * n : 0);
 }
 
 int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8,
@@ -239,17 +250,18 @@ int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, i
                                   int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
                                   const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
                                   const uint8_t* w2s, float* y, lk_stream_t stream) {
-  if (mode != LK_STORE && mode != LK_SWIGLU) return LK_EINVAL;
+  if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
   if (k % 32 || n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
   if (!tile_info || !rowmap || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
-  const bool two = mode == LK_SWIGLU && !fused;
+  const bool gu = mode != LK_STORE;
+  const bool two = gu && !fused;
   if (two && (!w2 || !w2s)) return LK_EINVAL;
   if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(y, 16) || (two && !aligned(w2, 16))) return LK_EALIGN;
-  const int fuse = mode == LK_SWIGLU && fused;
+  const int fuse = gu && fused;
   return gemm_mx(mode, order, rows, k, n, x8, s8, w, ws, two ? w2 : nullptr, two ? w2s : nullptr, y,
                  (cudaStream_t)stream, tile_info, rowmap, xrows, ku, n_experts, fuse ? 2 * n : n, fuse ? n : 0);
 }

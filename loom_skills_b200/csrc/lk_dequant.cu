@@ -177,10 +177,115 @@ __global__ void __launch_bounds__(256) k_row_scale(int k, const void* __restrict
   }
 }
 
+// 8 consecutive values of row `src` from column 8 * v (16 or 32 bytes, one or two vector loads)
+template <bool BF16>
+LK_DEV void load8(const void* x, int64_t off, float (&v)[8]) {
+  if (BF16) {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// The same row scale with one warp per output row (8 rows per CTA) and 16-byte vector accesses; k % 8 == 0. GATHER:
+// output row r is the row scale of x[rowmap[r] / ku] (a zero row where rowmap[r] < 0) -- the MoE gate/up activations
+// in bucket order, so the grouped GEMM reads plain tiles instead of gathering rows.
+template <bool BF16, bool F8, bool GATHER>
+__global__ void __launch_bounds__(256) k_row_scale_w(int rows, int k, const void* __restrict__ x,
+                                                     const int32_t* __restrict__ rowmap, int ku,
+                                                     float* __restrict__ scales, __half* __restrict__ x16,
+                                                     uint8_t* __restrict__ x8, float* __restrict__ s8) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  int64_t src = row;
+  if (GATHER) {
+    const int a = __ldg(rowmap + row);
+    src = a >= 0 ? a / ku : -1;
+  }
+  const int nv = k / 8;
+  float m = 0.0f;
+  if (src >= 0)
+    for (int i = lane; i < nv; i += 32) {
+      float v[8];
+      load8<BF16>(x, src * k + 8 * i, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int biased = int((__float_as_uint(m) >> 23) & 255);
+  const int e = min(max(biased - 127 - 13, 0), 100);
+  const float s = __uint_as_float(uint32_t(127 - e) << 23), inv = __uint_as_float(uint32_t(127 + e) << 23);
+  float fs = 0.0f, finv = 0.0f;
+  if (F8) {
+    fs = __uint_as_float(uint32_t(min(max(261 - biased, 1), 254)) << 23);
+    finv = __uint_as_float(uint32_t(min(max(biased - 15, 1), 254)) << 23);
+  }
+  const int64_t base = row * k;
+  for (int i = lane; i < nv; i += 32) {
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (src >= 0) load8<BF16>(x, src * k + 8 * i, v);
+    if (x16) {
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        h[j] = uint32_t(__half_as_ushort(__float2half_rn(v[2 * j] * s))) |
+               (uint32_t(__half_as_ushort(__float2half_rn(v[2 * j + 1] * s))) << 16);
+      *reinterpret_cast<uint4*>(x16 + base + 8 * i) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    if (F8) {
+      uint32_t q[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        q[j >> 2] |= uint32_t(__nv_cvt_float_to_fp8(v[j] * fs, __NV_SATFINITE, __NV_E4M3)) << (8 * (j & 3));
+      *reinterpret_cast<uint2*>(x8 + base + 8 * i) = make_uint2(q[0], q[1]);
+    }
+  }
+  if (lane == 0) {
+    if (scales) {
+      scales[2 * row] = s;
+      scales[2 * row + 1] = inv;
+    }
+    if (F8) {
+      s8[2 * row] = fs;
+      s8[2 * row + 1] = finv;
+    }
+  }
+}
+
+template <bool GATHER>
+static cudaError_t launch_row_scale_w(int rows, int k, const void* x, bool bf, const int32_t* rowmap, int ku,
+                                      float* scales, __half* h, uint8_t* x8, float* s8, cudaStream_t s) {
+  const dim3 grid((rows + 7) / 8);
+  if (x8) {
+    if (bf) k_row_scale_w<true, true, GATHER><<<grid, 256, 0, s>>>(rows, k, x, rowmap, ku, scales, h, x8, s8);
+    else k_row_scale_w<false, true, GATHER><<<grid, 256, 0, s>>>(rows, k, x, rowmap, ku, scales, h, x8, s8);
+  } else {
+    if (bf) k_row_scale_w<true, false, GATHER><<<grid, 256, 0, s>>>(rows, k, x, rowmap, ku, scales, h, nullptr, nullptr);
+    else k_row_scale_w<false, false, GATHER><<<grid, 256, 0, s>>>(rows, k, x, rowmap, ku, scales, h, nullptr, nullptr);
+  }
+  return cudaGetLastError();
+}
+
+static bool al(const void* p, uintptr_t b) { return (reinterpret_cast<uintptr_t>(p) & (b - 1)) == 0; }
+
 int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
               cudaStream_t s) {
   bool bf = x_dtype == LK_BF16;
   __half* h = reinterpret_cast<__half*>(x16);
+  if (k % 8 == 0 && al(x, 16) && al(x16, 16) && al(x8, 8))   // vector form (null outputs are aligned)
+    return launch_row_scale_w<false>(rows, k, x, bf, nullptr, 1, scales, h, x8, s8, s) == cudaSuccess ? LK_OK
+                                                                                                      : LK_ECUDA;
   if (x8) {
     if (bf) k_row_scale<true, true><<<rows, 256, 0, s>>>(k, x, scales, h, x8, s8);
     else k_row_scale<false, true><<<rows, 256, 0, s>>>(k, x, scales, h, x8, s8);
@@ -189,6 +294,15 @@ int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16
     else k_row_scale<false, false><<<rows, 256, 0, s>>>(k, x, scales, h, nullptr, nullptr);
   }
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// the gate/up activations of the MoE in bucket order (k % 8 == 0 and aligned operands, checked by the caller)
+int row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, const void* x, int x_dtype, float* scales,
+                     uint16_t* x16, uint8_t* x8, float* s8, cudaStream_t s) {
+  return launch_row_scale_w<true>(rows, k, x, x_dtype == LK_BF16, rowmap, ku, scales, reinterpret_cast<__half*>(x16),
+                                  x8, s8, s) == cudaSuccess
+             ? LK_OK
+             : LK_ECUDA;
 }
 
 }  // namespace lk

@@ -760,7 +760,7 @@ static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
 // tile shape per mode: (BN, NW, MH)
 //   dense store/acc  128 x 1 x 2   a 256 x 128 tile, two M=128 accumulators sharing each dequantised B stage
 //   dense swiglu     128 x 2 x 1   128 rows x 128 columns of gate and of up
-//   grouped gate/up  128 x 2 x 1   (MoE super-tiles hold at most 128 rows of one expert)
+//   grouped gate/up  128 x 2 x 1   (MoE super-tiles hold at most 128 rows of one expert; gathered or sorted rows)
 //   grouped down     256 x 1 x 1
 template <int FMT>
 static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
@@ -770,6 +770,7 @@ static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, d
     return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 3, 4, 2>(m, a, s);
   }
   if (group == kGather) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kGather, 1, 2, 4, 2, 2>(m, a, s);
+  if (mode == LK_SWIGLU_SORTED) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kSorted, 1, 2, 4, 2, 2>(m, a, s);
   return launch_gemm_p<FMT, 256, 1, LK_STORE, kSorted, 1, 2, 4, 2, 2>(m, a, s);
 }
 
@@ -812,9 +813,9 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     wrows = int64_t(n_experts) * a.rows_per_expert;
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
-  a.w2_row_offset = (mode == LK_SWIGLU && !w2) ? int(w2_offset / rb) : 0;
+  a.w2_row_offset = (mode != LK_STORE && mode != LK_ACC && !w2) ? int(w2_offset / rb) : 0;
   // weight rows per tile: 256 for grouped down, 128 per weight otherwise
-  const int bn = (group == kSorted) ? 256 : 128;
+  const int bn = (group == kSorted && mode == LK_STORE) ? 256 : 128;
   const int tm = (group == kDense && mode != LK_SWIGLU) ? 2 * kBM : kBM;   // tile rows
   GemmMaps m;
   int rc = group == kGather ? make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xrows, k, kBK, 1,

@@ -9,6 +9,8 @@ namespace lk {
 int dequant(int fmt, const void* w, const void* ws, int64_t n_values, void* out, int out_dtype, cudaStream_t s);
 int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
               cudaStream_t s);
+int row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, const void* x, int x_dtype, float* scales,
+                     uint16_t* x16, uint8_t* x8, float* s8, cudaStream_t s);
 
 // decode matvec, dense and per-assignment (MoE) forms
 struct MvArgs {

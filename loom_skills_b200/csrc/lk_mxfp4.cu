@@ -698,9 +698,9 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
              const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
              const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
              int w2_row_offset) {
-  const int NW = mode == LK_SWIGLU ? 2 : 1;
+  const int NW = mode == LK_STORE ? 1 : 2;   // swiglu: gathered or sorted gate/up rows
   const int bnw = kMxpNT / NW;
-  const int group = tile_info ? (NW == 2 ? kGather : kSorted) : kDense;
+  const int group = tile_info ? (mode == LK_SWIGLU ? kGather : kSorted) : kDense;
   MxpArgs a{};
   a.s8 = s8;
   a.y = y;
@@ -747,7 +747,7 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
   const int64_t max_m = tile_info ? int64_t(rows) / kBM + n_experts : a.m_tiles;
   const int grid = int(std::min(int64_t(sms), max_m * a.n_tiles));
   if (group == kGather) return launch_mxp<2, kGather>(m, a, grid, s);
-  if (group == kSorted) return launch_mxp<1, kSorted>(m, a, grid, s);
+  if (group == kSorted) return NW == 2 ? launch_mxp<2, kSorted>(m, a, grid, s) : launch_mxp<1, kSorted>(m, a, grid, s);
   return NW == 2 ? launch_mxp<2, kDense>(m, a, grid, s) : launch_mxp<1, kDense>(m, a, grid, s);
 }
 
@@ -761,7 +761,7 @@ int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, cons
   if (mxp_applies(order, k, w, ws, w2, w2s))
     return gemm_mxp(mode, rows, k, n, x8, s8, w, ws, w2, w2s, y, s, tile_info, rowmap, xrows, ku, n_experts,
                     rows_per_expert, w2_row_offset);
-  const int NW = mode == LK_SWIGLU ? 2 : 1;
+  const int NW = mode == LK_STORE ? 1 : 2;
   const int bn = kRowsB / NW;
   MxArgs a{};
   a.s8 = s8;
@@ -804,6 +804,7 @@ int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, cons
   dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + kBM - 1) / kBM : rows / 64);
   if (NW == 2) {
     if (group == kGather) return launch_o<2, kGather>(order, am, wm, w2m, a, grid, s);
+    if (group == kSorted) return launch_o<2, kSorted>(order, am, wm, w2m, a, grid, s);
     return launch_o<2, kDense>(order, am, wm, w2m, a, grid, s);
   }
   if (group == kSorted) return launch_o<1, kSorted>(order, am, wm, w2m, a, grid, s);

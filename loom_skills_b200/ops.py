@@ -88,6 +88,28 @@ def row_scale_f8(x, with_f16=False):
     return (x8, s8, x16, sc) if with_f16 else (x8, s8)
 
 
+def moe_row_scale_gather(x, rowmap, ku, f8=False):
+    """The MoE gate/up activations in bucket order: row r = the row scale of x[rowmap[r] // ku] (zero row where
+    rowmap[r] < 0). f8=False: (x16 [rows][k] f16, scales [rows][2]); f8=True: (x8 [rows][k] e4m3 bytes, s8 [rows][2])
+    -- the operands of the grouped GEMMs' 'swiglu_sorted' mode."""
+    _cuda(x, rowmap)
+    x = x.contiguous()
+    rows = rowmap.shape[0]
+    k = x.shape[1]
+    dev = x.device
+    if f8:
+        x8 = torch.empty(rows, k, dtype=torch.uint8, device=dev)
+        s8 = torch.empty(rows, 2, dtype=torch.float32, device=dev)
+        L.check(L.load().lk_moe_row_scale_gather(rows, k, ku, _ptr(rowmap), _ptr(x), _DT[x.dtype], None, None,
+                                                 _ptr(x8), _ptr(s8), _stream()), "lk_moe_row_scale_gather")
+        return x8, s8
+    x16 = torch.empty(rows, k, dtype=torch.float16, device=dev)
+    sc = torch.empty(rows, 2, dtype=torch.float32, device=dev)
+    L.check(L.load().lk_moe_row_scale_gather(rows, k, ku, _ptr(rowmap), _ptr(x), _DT[x.dtype], _ptr(sc), _ptr(x16),
+                                             None, None, _stream()), "lk_moe_row_scale_gather")
+    return x16, sc
+
+
 def mv(fmt, w, x, n, k, w2=None, y=None, accumulate=False):
     """Decode matvec: y[t][n] (+)= x[t] . W[n] (swiglu with w2). x [tokens][k] f32/f16/bf16."""
     _cuda(w, x, w2, y)
@@ -160,8 +182,9 @@ def moe_bucket(ids, n_experts, max_tiles=None, info=None):
 
 
 def moe_grouped_gemm(fmt, mode, tile_info, rowmap, x16, scales, w, n, ku, n_experts, fused=False, w2=None, y=None):
-    """Grouped expert GEMM over the bucketed 64-row tiles. mode 'swiglu' (gate/up, x16 = token rows) or 'store'
-    (down, x16 = sorted rows). y: [max_tiles*64][n]."""
+    """Grouped expert GEMM over the bucketed 64-row tiles. mode 'swiglu' (gate/up, x16 = token rows, gathered),
+    'swiglu_sorted' (gate/up, x16 = sorted rows from moe_row_scale_gather) or 'store' (down, x16 = sorted rows).
+    y: [max_tiles*64][n]."""
     _cuda(tile_info, rowmap, x16, scales, w, w2, y)
     rows = rowmap.shape[0]
     xrows, k = x16.shape
@@ -240,8 +263,9 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
         ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act, w_dn, h, f, ku, n_experts)
         return moe_combine(ys, wts)
     ti, rm, pos = moe_bucket(ids, n_experts)
-    x16, sc = row_scale_f16(x)
-    act = moe_grouped_gemm(fmt, "swiglu", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True)
+    # the token rows row-scaled straight into bucket order: gate/up then reads plain tiles (no row gather)
+    x16, sc = moe_row_scale_gather(x, rm, ku)
+    act = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True)
     a16, asc = row_scale_f16(act)
     ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts)
     return moe_combine_sorted(ys, pos, wts)
@@ -254,8 +278,9 @@ def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, nor
     of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per expert h rows of f/2 / f/32 bytes."""
     ids, wts = moe_route(logits, n_experts, ku, norm=norm)
     ti, rm, pos = moe_bucket(ids, n_experts)
-    x8, s8 = row_scale_f8(x)
-    act = moe_grouped_gemm_mxfp4s_f8("swiglu", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True, order=order)
+    x8, s8 = moe_row_scale_gather(x, rm, ku, f8=True)
+    act = moe_grouped_gemm_mxfp4s_f8("swiglu_sorted", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True,
+                                     order=order)
     a8, as8 = row_scale_f8(act)
     ys = moe_grouped_gemm_mxfp4s_f8("store", ti, rm, a8, as8, w_dn, ws_dn, h, ku, n_experts, order=order)
     return moe_combine_sorted(ys, pos, wts)
