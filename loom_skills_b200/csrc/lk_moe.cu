@@ -117,8 +117,116 @@ __global__ void __launch_bounds__(256) k_route(int h, int E, int ku, int gating,
   if (my_k >= 0) wts[int64_t(t) * ku + my_k] = wv * scale;
 }
 
+// router on given logits: one warp per token (8 per CTA), lane l holds experts l, l + 32, ... (E <= 256): the same
+// gating, top-k (ties to the lowest index) and weight rules as k_route, every reduction a warp shuffle
+__global__ void __launch_bounds__(256) k_route_w(int tokens, int E, int ku, int gating, int norm, float scale,
+                                                 const float* __restrict__ logits, const float* __restrict__ bias,
+                                                 int32_t* __restrict__ ids, float* __restrict__ wts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  auto wmax = [](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  };
+  auto wsum = [](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+  };
+  float lg[8], prob[8], sc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = lane + 32 * j;
+    lg[j] = e < E ? __ldg(logits + t * E + e) : -INFINITY;
+  }
+  if (gating == 1) {
+    float m = lg[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) m = fmaxf(m, lg[j]);
+    m = wmax(m);
+    float den = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      prob[j] = lane + 32 * j < E ? expf(lg[j] - m) : 0.f;
+      den += prob[j];
+    }
+    den = wsum(den);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      prob[j] = prob[j] / den;
+      sc[j] = lg[j];   // softmax is monotonic in the logit: rank on the exact input
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = lane + 32 * j;
+      const bool in = e < E;
+      const float b = (bias && in) ? __ldg(bias + e) : 0.f;
+      if (gating == 2) {
+        prob[j] = in ? 1.0f / (1.0f + expf(-lg[j])) : 0.f;
+        sc[j] = in ? prob[j] + b : -INFINITY;
+      } else {
+        prob[j] = in ? lg[j] + b : -INFINITY;
+        sc[j] = prob[j];
+      }
+    }
+  }
+  int my[8];   // round each held expert was picked in, or -1
+#pragma unroll
+  for (int j = 0; j < 8; ++j) my[j] = -1;
+  float sel_sum = 0.f;
+  for (int r = 0; r < ku; ++r) {
+    float best = sc[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) best = fmaxf(best, sc[j]);
+    best = wmax(best);
+    int cand = 1 << 30;
+#pragma unroll
+    for (int j = 7; j >= 0; --j)
+      if (lane + 32 * j < E && sc[j] == best) cand = lane + 32 * j;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
+    float pw = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (lane + 32 * j == cand) {
+        my[j] = r;
+        sc[j] = -INFINITY;
+        pw = prob[j];
+      }
+    if (lane == (cand & 31)) ids[t * ku + r] = cand;
+    sel_sum += wsum(pw);
+  }
+  float m3 = 0.f, den3 = 1.f;
+  if (gating == 3) {   // softmax over the picked
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (my[j] >= 0) m = fmaxf(m, prob[j]);
+    m3 = wmax(m);
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (my[j] >= 0) d += expf(prob[j] - m3);
+    den3 = wsum(d);
+  }
+  const float den = norm ? fmaxf(sel_sum, 6.103515625e-05f) : 1.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (my[j] >= 0) {
+      const float wv = gating == 3 ? expf(prob[j] - m3) / den3 : prob[j] / den;
+      wts[t * ku + my[j]] = wv * scale;
+    }
+}
+
 int moe_route(int tokens, int h, int E, int ku, int gating, int norm, float scale, const float* x,
               const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s) {
+  if (!router_w) {
+    k_route_w<<<(tokens + 7) / 8, 256, 0, s>>>(tokens, E, ku, gating, norm, scale, x, bias, ids, wts);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+  }
   if (w_dtype == LK_BF16)
     k_route<true><<<tokens, 256, 0, s>>>(h, E, ku, gating, norm, scale, x, router_w, bias, ids, wts);
   else
@@ -128,7 +236,9 @@ int moe_route(int tokens, int h, int E, int ku, int gating, int norm, float scal
 
 // ---------------------------------------------------------------------------------------------------------------
 // bucket: one 1024-thread block. Counting sort by expert, stable in the assignment index, so the schedule is
-// deterministic (the reference's atomics give any order within an expert's rows).
+// deterministic (the reference's atomics give any order within an expert's rows). Warp w owns the contiguous
+// assignments [w * chunk, (w + 1) * chunk): per-warp expert counts, one scan over the warps per expert, then each warp
+// places its own assignments in rounds of 32 with no block-wide barrier (rank inside a round by __match_any_sync).
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int max_tiles,
                                                  const int32_t* __restrict__ info, const int32_t* __restrict__ ids,
@@ -137,10 +247,11 @@ __global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int 
   __shared__ int count[256];
   __shared__ int cursor[256];
   __shared__ int tbase[257];
-  __shared__ int wcnt[32][256];
+  __shared__ int wcnt[32][256];   // per warp and expert: count, then the count in the warps before, then a cursor
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int A = tokens * ku;
-  for (int i = tid; i < 256; i += 1024) count[i] = 0;
+  const int chunk = (A + 31) / 32;
+  const int a0 = min(A, warp * chunk), a1 = min(A, a0 + chunk);
   for (int i = tid; i < 32 * 256; i += 1024) (&wcnt[0][0])[i] = 0;
   __syncthreads();
   auto expert_of = [&](int a) -> int {
@@ -148,9 +259,19 @@ __global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int 
     if (info && info[4 * t + 2] == 0) return -1;
     return min(max(ids[a], 0), E - 1);
   };
-  for (int a = tid; a < A; a += 1024) {
+  for (int a = a0 + lane; a < a1; a += 32) {
     int e = expert_of(a);
-    if (e >= 0) atomicAdd(&count[e], 1);
+    if (e >= 0) atomicAdd(&wcnt[warp][e], 1);
+  }
+  __syncthreads();
+  if (tid < E) {   // exclusive scan over the warps: assignments of expert tid in the ranges before warp w
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wcnt[w][tid];
+      wcnt[w][tid] = run;
+      run += c;
+    }
+    count[tid] = run;
   }
   __syncthreads();
   if (tid == 0) {
@@ -186,32 +307,22 @@ __global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int 
   }
   for (int r = total * kTile + tid; r < max_tiles * kTile; r += 1024) rowmap[r] = -1;
   __syncthreads();
-  // stable placement, 1024 assignments per round
-  for (int base = 0; base < A; base += 1024) {
-    int a = base + tid;
-    int e = a < A ? expert_of(a) : -2;
-    unsigned peers = __match_any_sync(0xffffffffu, e);
-    int rank = __popc(peers & ((1u << lane) - 1));
-    bool leader = rank == 0;
-    if (e >= 0 && leader) wcnt[warp][e] = __popc(peers);
-    __syncthreads();
+  // stable placement: warp-local rounds over the warp's own assignments, in ascending order
+  for (int base = a0; base < a1; base += 32) {
+    const int a = base + lane;
+    const int e = a < a1 ? expert_of(a) : -2;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1));
     if (e >= 0) {
-      int off = cursor[e] + rank;
-      for (int w = 0; w < warp; ++w) off += wcnt[w][e];
+      const int off = cursor[e] + wcnt[warp][e] + rank;
       if (off < max_tiles * kTile) rowmap[off] = a;
       pos[a] = off;
     } else if (e == -1) {
       pos[a] = -1;
     }
-    __syncthreads();
-    if (tid < E) {
-      int add = 0;
-      for (int w = 0; w < 32; ++w) add += wcnt[w][tid];
-      cursor[tid] += add;
-    }
-    __syncthreads();
-    if (e >= 0 && leader) wcnt[warp][e] = 0;
-    __syncthreads();
+    __syncwarp();
+    if (e >= 0 && rank == 0) wcnt[warp][e] += __popc(peers);
+    __syncwarp();
   }
 }
 
