@@ -195,8 +195,8 @@ class GpuMoEBackend:
             act = ops.moe_expert_mv(self.fmt, "gu", eids, x, w_gu, f, h, 1, n_local, fused=True)
             return ops.moe_expert_mv(self.fmt, "dn", eids, act, w_dn, h, f, 1, n_local)
         ti, rm, pos = ops.moe_bucket(eids.view(r, 1), n_local)
-        x16, sc = ops.row_scale_f16(x)
-        act = ops.moe_grouped_gemm(self.fmt, "swiglu", ti, rm, x16, sc, w_gu, f, 1, n_local, fused=True)
+        x16, sc = ops.moe_row_scale_gather(x, rm, 1)   # the rows in bucket order: gate/up reads plain tiles
+        act = ops.moe_grouped_gemm(self.fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, 1, n_local, fused=True)
         a16, asc = ops.row_scale_f16(act)
         ys = ops.moe_grouped_gemm(self.fmt, "store", ti, rm, a16, asc, w_dn, h, 1, n_local)
         ones = torch.ones(r, 1, dtype=torch.float32, device=x.device)
