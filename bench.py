@@ -188,10 +188,18 @@ def run_reference(args):
 # our arm
 # ------------------------------------------------------------------------------------------------------------------
 def make_weights(torch, layers, seed=0):
-    """Q4_K weights for one layer, copied to `layers` distinct buffers (rotated so they exceed L2)."""
+    """Q4_K weights for one layer, copied to `layers` distinct buffers (rotated so they exceed L2). q, k and v are
+    row slices of one contiguous "qkv" tensor, the fused attn_qkv layout the reference also loads (gen_llm.py:99-100):
+    the decode reads them as three weights of one launch, the prefill as one N = 6144 GEMM."""
     rng = np.random.default_rng(seed)
-    base = {name: torch.from_numpy(synth_q4k(rng, n, k)).cuda() for name, k, n in SHAPES}
-    return [{name: (t if li == 0 else t.clone()) for name, t in base.items()} for li in range(layers)]
+    base = {name: torch.from_numpy(synth_q4k(rng, n, k)).cuda() for name, k, n in SHAPES if name not in ("q", "k", "v")}
+    base["qkv"] = torch.from_numpy(synth_q4k(rng, 6144, 4096)).cuda()
+    out = []
+    for li in range(layers):
+        w = {name: (t if li == 0 else t.clone()) for name, t in base.items()}
+        w["q"], w["k"], w["v"] = w["qkv"][:4096], w["qkv"][4096:5120], w["qkv"][5120:]
+        out.append(w)
+    return out
 
 
 class Timed:
@@ -363,7 +371,7 @@ def run_ours(args):
     offs = np.cumsum([0] + [n for _, _, n in SHAPES])
     ys = [{name: yall[li, offs[j]:offs[j + 1]].view(1, n) for j, (name, _, n) in enumerate(SHAPES)}
           for li in range(args.layers)]
-    wbytes_layer = sum(t.numel() for t in wstack[0].values())
+    wbytes_layer = sum(wstack[0][name].numel() for name, _, _ in SHAPES)
     act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
     launches_per_step = args.layers * 4   # matvec launches: q|k|v, o, gate_up, down
     step_bytes = args.layers * wbytes_layer
@@ -487,8 +495,11 @@ def run_ours(args):
         for k in xp:
             x16p[k] = ops.row_scale_f16(xp[k])
 
-    def gemm_body():
-        for name, k, n in SHAPES:
+    yqkv = torch.empty(M, 6144, device=dev)
+
+    def gemm_body():   # q | k | v as one GEMM over the fused qkv rows, then o, gate_up, down
+        ops.gemm("q4_k", "store", x16p[4096][0], x16p[4096][1], wstack[0]["qkv"], 6144, y=yqkv)
+        for name, k, n in SHAPES[3:]:
             ops.gemm("q4_k", "store", x16p[k][0], x16p[k][1], wstack[0][name], n, y=yp[name])
 
     scale_g = Timed(torch, scale_body)

@@ -267,9 +267,99 @@ __global__ void __launch_bounds__(256) k_row_scale_w(int rows, int k, const void
   }
 }
 
+// The same row scale for long rows (2048 < k <= 8192, k % 8 == 0): one 128-thread CTA per output row, each thread's
+// up to NV vectors of 8 values held in registers between the max and the conversion, so the row is read once.
+template <bool BF16, bool F8, bool GATHER, int NV>
+__global__ void __launch_bounds__(128) k_row_scale_b(int k, const void* __restrict__ x, const int32_t* __restrict__ rowmap,
+                                                     int ku, float* __restrict__ scales, __half* __restrict__ x16,
+                                                     uint8_t* __restrict__ x8, float* __restrict__ s8) {
+  __shared__ float red[4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  int64_t src = row;
+  if (GATHER) {
+    const int a = __ldg(rowmap + row);
+    src = a >= 0 ? a / ku : -1;
+  }
+  const int nv = k / 8;
+  float v[NV][8];
+  float m = 0.0f;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int i = threadIdx.x + 128 * u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[u][j] = 0.0f;
+    if (src >= 0 && i < nv) load8<BF16>(x, src * k + 8 * i, v[u]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[u][j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const int biased = int((__float_as_uint(m) >> 23) & 255);
+  const int e = min(max(biased - 127 - 13, 0), 100);
+  const float s = __uint_as_float(uint32_t(127 - e) << 23), inv = __uint_as_float(uint32_t(127 + e) << 23);
+  float fs = 0.0f, finv = 0.0f;
+  if (F8) {
+    fs = __uint_as_float(uint32_t(min(max(261 - biased, 1), 254)) << 23);
+    finv = __uint_as_float(uint32_t(min(max(biased - 15, 1), 254)) << 23);
+  }
+  const int64_t base = row * k;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int i = threadIdx.x + 128 * u;
+    if (i >= nv) break;
+    if (x16) {
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        h[j] = uint32_t(__half_as_ushort(__float2half_rn(v[u][2 * j] * s))) |
+               (uint32_t(__half_as_ushort(__float2half_rn(v[u][2 * j + 1] * s))) << 16);
+      *reinterpret_cast<uint4*>(x16 + base + 8 * i) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    if (F8) {
+      uint32_t q[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; j += 2)
+        q[j >> 2] |= uint32_t(__nv_cvt_float2_to_fp8x2(make_float2(v[u][j] * fs, v[u][j + 1] * fs), __NV_SATFINITE,
+                                                       __NV_E4M3))
+                     << (8 * (j & 3));
+      *reinterpret_cast<uint2*>(x8 + base + 8 * i) = make_uint2(q[0], q[1]);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (scales) {
+      scales[2 * row] = s;
+      scales[2 * row + 1] = inv;
+    }
+    if (F8) {
+      s8[2 * row] = fs;
+      s8[2 * row + 1] = finv;
+    }
+  }
+}
+
+template <bool GATHER, int NV>
+static cudaError_t launch_row_scale_b(int rows, int k, const void* x, bool bf, const int32_t* rowmap, int ku,
+                                      float* scales, __half* h, uint8_t* x8, float* s8, cudaStream_t s) {
+  if (x8) {
+    if (bf) k_row_scale_b<true, true, GATHER, NV><<<rows, 128, 0, s>>>(k, x, rowmap, ku, scales, h, x8, s8);
+    else k_row_scale_b<false, true, GATHER, NV><<<rows, 128, 0, s>>>(k, x, rowmap, ku, scales, h, x8, s8);
+  } else {
+    if (bf) k_row_scale_b<true, false, GATHER, NV><<<rows, 128, 0, s>>>(k, x, rowmap, ku, scales, h, nullptr, nullptr);
+    else k_row_scale_b<false, false, GATHER, NV><<<rows, 128, 0, s>>>(k, x, rowmap, ku, scales, h, nullptr, nullptr);
+  }
+  return cudaGetLastError();
+}
+
 template <bool GATHER>
 static cudaError_t launch_row_scale_w(int rows, int k, const void* x, bool bf, const int32_t* rowmap, int ku,
                                       float* scales, __half* h, uint8_t* x8, float* s8, cudaStream_t s) {
+  // one pass for long rows (measured: 2880-wide e4m3 rows 129 -> 74 us; 2048-wide rows are faster on the warp form)
+  if (k > 2048 && k <= 4096) return launch_row_scale_b<GATHER, 4>(rows, k, x, bf, rowmap, ku, scales, h, x8, s8, s);
+  if (k > 4096 && k <= 8192) return launch_row_scale_b<GATHER, 8>(rows, k, x, bf, rowmap, ku, scales, h, x8, s8, s);
   const dim3 grid((rows + 7) / 8);
   if (x8) {
     if (bf) k_row_scale_w<true, true, GATHER><<<grid, 256, 0, s>>>(rows, k, x, rowmap, ku, scales, h, x8, s8);

@@ -83,9 +83,10 @@ class TestDequant:
 # ---------------------------------------------------------------------------------------------------------- producers
 class TestRowScale:
     @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-    def test_row_scale_f16_bit_exact(self, ops, dtype):
+    @pytest.mark.parametrize("k", [768, 2880, 5120, 12288, 1000])   # warp form, one-pass CTA forms, scalar form
+    def test_row_scale_f16_bit_exact(self, ops, dtype, k):
         rng = np.random.default_rng(3)
-        x = (rng.standard_normal((37, 768)) * rng.choice([1e-3, 1.0, 3e4, 3e6], (37, 1))).astype(np.float32)
+        x = (rng.standard_normal((37, k)) * rng.choice([1e-3, 1.0, 3e4, 3e6], (37, 1))).astype(np.float32)
         xt = dev(x)
         if dtype == "bf16":
             xt = xt.to(torch.bfloat16)
@@ -95,9 +96,10 @@ class TestRowScale:
         assert np.array_equal(host(x16).view(np.uint16), rx16.view(np.uint16))
         assert np.array_equal(bits32(host(sc)), bits32(rsc))
 
-    def test_row_scale_f8_bit_exact(self, ops):
+    @pytest.mark.parametrize("k", [2880, 768, 6144])
+    def test_row_scale_f8_bit_exact(self, ops, k):
         rng = np.random.default_rng(4)
-        x = (rng.standard_normal((19, 2880)) * rng.choice([1e-2, 1.0, 50.0], (19, 1))).astype(np.float32)
+        x = (rng.standard_normal((19, k)) * rng.choice([1e-2, 1.0, 50.0], (19, 1))).astype(np.float32)
         x8, s8 = ops.row_scale_f8(dev(x))
         rx8, rs8 = O.row_scale_f8(x)
         assert np.array_equal(host(x8), rx8)
