@@ -24,6 +24,8 @@
 //              the per-thread work is a short dependent chain, so latency is hidden by warps, not by ILP alone.
 //   split-K    small N runs S CTAs per row tile as one thread-block cluster; their partial sums meet in CTA 0's
 //              shared memory (distributed shared memory reads, fixed order: deterministic).
+#include <mutex>
+
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
@@ -279,6 +281,9 @@ __global__ void __launch_bounds__(kQThreads)
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRStages = 3;
 constexpr int kRowWarps = 4;   // consumer warps = rows per stage
+// rings per CTA for K = 4096 rows and for longer rows (measured on the 8-layer decode mix: 2 rings of the short
+// form 4263 GB/s against 4207 with one; 3 or more rings, or 2 of the long form, were slower)
+constexpr int kRingsShort = 2, kRingsLong = 1;
 
 // the Q4_K (scale, min) pairs of groups (2pg, 2pg + 1) as "2^23 + value" floats: f[0..1] scales, f[2..3] minima.
 // pg is constant per thread: byte half h = pg & 1 of each scale word, the 4-bit-plus-2-bit form for pg >= 2.
@@ -318,21 +323,30 @@ LK_DEV int seg_of(const RowArgs& p, int st, int& row0) {
   return g;
 }
 
+// bytes of one ring's shared memory: its stages, then full / empty barriers, per-row pair barriers and partial sums
+__host__ __device__ inline int ring_bytes(int stage_bytes) {
+  return (kRStages * stage_bytes + 2 * kRStages * 8 + kRStages * kRowWarps * 12 + 127) / 128 * 128;
+}
+
 // UPL units per lane over the whole row; HALVES warps per row (each takes UPL / HALVES of the units; the second
-// hands its partial sum to the first through shared memory and a per-row mbarrier)
-template <int UPL, int HALVES>
-__global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
+// hands its partial sum to the first through shared memory and a per-row mbarrier). A CTA runs RINGS independent
+// rings (a producer warp, its consumer warps, its own stages and barriers); stages go round-robin over the
+// gridDim.x * RINGS rings. Fewer, larger CTAs make the grid cheaper to launch, retire and hand over to the next grid.
+template <int UPL, int HALVES, int RINGS>
+__global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
   constexpr int kU = UPL / HALVES;             // units this lane computes
-  constexpr int kCW = kRowWarps * HALVES;      // consumer warps
-  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kCW = kRowWarps * HALVES;      // consumer warps per ring
+  extern __shared__ __align__(128) uint8_t smem_all[];
   const int stage_bytes = int((int64_t(p.sr) * p.rb + 127) / 128 * 128);
+  const int ring = (threadIdx.x >> 5) / (1 + kCW);
+  uint8_t* smem = smem_all + ring * ring_bytes(stage_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRStages * stage_bytes);
   uint64_t* empty = full + kRStages;
   uint64_t* pair = empty + kRStages;                               // [kRStages][kRowWarps]
   float* part = reinterpret_cast<float*>(pair + kRStages * kRowWarps);   // [kRStages][kRowWarps]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
+  const int warp = (threadIdx.x >> 5) % (1 + kCW), lane = threadIdx.x & 31;   // warp within the ring
+  if (warp == 0 && lane == 0) {
     for (int i = 0; i < kRStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCW);
@@ -341,7 +355,8 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
     fence_mbar_init();
   }
   __syncthreads();
-  const int my_stages = p.nstages > int(blockIdx.x) ? (p.nstages - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  const int vb = int(blockIdx.x) * RINGS + ring, vg = int(gridDim.x) * RINGS;   // this ring, all rings
+  const int my_stages = p.nstages > vb ? (p.nstages - 1 - vb) / vg + 1 : 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -350,7 +365,7 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
         const int s = i % kRStages;
         if (i == kPreWaitStages) griddep_wait();   // the first stage only goes out before the previous grid ends
         if (i >= kRStages && !mbar_wait(&empty[s], ((i / kRStages) - 1) & 1)) atomicOr(&g_status, 1u);
-        const int st = int(blockIdx.x) + i * int(gridDim.x);
+        const int st = vb + i * vg;
         int r0;
         const int g = seg_of(p, st, r0);
         const int rows = min(p.sr, p.n[g] - r0);
@@ -389,7 +404,7 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
     for (int i = 0; i < my_stages; ++i) {
       const int s = i % kRStages;
       if (!mbar_wait(&full[s], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
-      const int st = int(blockIdx.x) + i * int(gridDim.x);
+      const int st = vb + i * vg;
       int r0;
       const int g = seg_of(p, st, r0);
       const int row = r0 + rslot;
@@ -443,23 +458,41 @@ __global__ void __launch_bounds__(32 * (1 + kRowWarps * HALVES))
   }
 }
 
-template <int UPL, int HALVES>
+template <int UPL, int HALVES, int RINGS>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
-  const int smem = kRStages * stage_bytes + 2 * kRStages * 8 + kRStages * kRowWarps * 12;
-  auto kern = k_mv_q8_rows<UPL, HALVES>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (1 + kRowWarps * HALVES), smem) !=
-          cudaSuccess ||
-      per_sm < 1)
-    return LK_ECUDA;
-  int dev = 0, sms = 0;
+  const int smem = RINGS * ring_bytes(stage_bytes);
+  constexpr int threads = 32 * RINGS * (1 + kRowWarps * HALVES);
+  auto kern = k_mv_q8_rows<UPL, HALVES, RINGS>;
+  // the attribute and the occupancy query once per (device, shared-memory size): they cost host time on every call
+  struct Entry {
+    int dev, smem, per_sm, sms;
+  };
+  static Entry cache[16];
+  static int ncache = 0;
+  static std::mutex mu;
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int per_sm = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < ncache; ++i)
+      if (cache[i].dev == dev && cache[i].smem == smem) {
+        per_sm = cache[i].per_sm;
+        sms = cache[i].sms;
+      }
+    if (per_sm == 0) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+        return LK_ECUDA;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (ncache < 16) cache[ncache++] = Entry{dev, smem, per_sm, sms};
+    }
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(min(a.nstages, sms * per_sm), 1, 1);   // persistent: every resident CTA slot, once
-  cfg.blockDim = dim3(32 * (1 + kRowWarps * HALVES), 1, 1);
+  // persistent: every resident CTA slot, once (no more CTAs than rings have stages)
+  cfg.gridDim = dim3(min((a.nstages + RINGS - 1) / RINGS, sms * per_sm), 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -571,9 +604,9 @@ static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* con
   }
   ra.nstages = ra.start[nseg];
   switch (k / 2048) {   // units (chunk, page) per lane
-    case 2: return launch_rows<2, 1>(ra, s);
-    case 4: return launch_rows<4, 2>(ra, s);
-    case 6: return launch_rows<6, 2>(ra, s);
+    case 2: return launch_rows<2, 1, kRingsShort>(ra, s);
+    case 4: return launch_rows<4, 2, kRingsLong>(ra, s);
+    case 6: return launch_rows<6, 2, kRingsLong>(ra, s);
   }
   return LK_EUNSUPPORTED;
 }
