@@ -6,7 +6,8 @@ Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
 868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer the activations are
 quantised to int8 (g_quant_q8) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
-weight GB/s; the line also carries the bf16-activation decode, the prefill TFLOP/s at M=2048 over the same shapes
+weight GB/s; the line also carries each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up, down, each
+streamed from HBM), the bf16-activation decode, the prefill TFLOP/s at M=2048 over the same shapes
 (step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
 MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 32 matvec launches per
 decode step -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
@@ -199,6 +200,42 @@ def make_weights(torch, layers, seed=0):
         w = {name: (t if li == 0 else t.clone()) for name, t in base.items()}
         w["q"], w["k"], w["v"] = w["qkv"][:4096], w["qkv"][4096:5120], w["qkv"][5120:]
         out.append(w)
+    return out
+
+
+def bench_gemv_forms(args, torch, wstack, xq, pk, time_steps):
+    """Each decode launch form alone: 32 back-to-back launches per graph replay, rotated over enough copies of its
+    weights to exceed twice the L2, so every launch streams its weights from HBM. Per launch: device time, weight
+    GB/s and the fraction of the measured HBM copy."""
+    from loom_skills_b200 import ops
+    forms = [("q|k|v", "qkv", 4096, [4096, 1024, 1024]), ("o", "o", 4096, [4096]),
+             ("gate_up", "gate_up", 4096, [24576]), ("down", "down", 12288, [4096])]
+    chain = 32
+    out = {}
+    for label, name, k, ns in forms:
+        base = wstack[0][name]
+        nbytes = base.numel()
+        copies = max(2, -(-256_000_000 // nbytes))
+        ws = [base] + [base.clone() for _ in range(copies - 1)]
+        ys = [torch.empty(1, n, device=base.device) for n in ns]
+        r0 = np.cumsum([0] + ns)
+        x = xq[0][k]
+
+        def body():
+            for i in range(chain):
+                w = ws[i % copies]
+                if len(ns) > 1:
+                    ops.mv_q8_multi("q4_k", [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, 1, ys=ys)
+                else:
+                    ops.mv_q8("q4_k", w, x, ns[0], k, 1, y=ys[0])
+        g = Timed(torch, body)
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        us = time_steps(g.replay, max(5, args.steps)) * 1e3 / chain
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[label] = {"us_per_launch": round(us, 2), "weight_mb": round(nbytes / 1e6, 1), "weight_gbs": round(gbs, 1),
+                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies}
+        del g, ws
     return out
 
 
@@ -564,6 +601,8 @@ def run_ours(args):
             sweep[str(m)] = {"ms": round(mms, 4), "weight_gbs": round(wbytes_layer / (mms * 1e-3) / 1e9, 1),
                              "tflops": round(sum(2.0 * m * n * k for _, k, n in SHAPES) / (mms * 1e-3) / 1e12, 2)}
 
+    # ---- each decode launch form alone (its weights rotated past L2): the GEMV's own fraction of HBM per shape
+    gemv = bench_gemv_forms(args, torch, wstack, xq, pk, time_steps) if not args.no_extra else None
     # ---- the IQ4_NL GEMMs N-sharded over the ranks, all-gather fused into the epilogue (strong scaling)
     sharded = bench_sharded(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
@@ -586,7 +625,7 @@ def run_ours(args):
                        "launch": "one CUDA graph replay per step"},
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
-            "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_bf16": decode_bf16,
+            "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_gemv": gemv, "decode_bf16": decode_bf16,
             "sharded_iq4_nl": sharded, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
