@@ -6,8 +6,9 @@ Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
 868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer the activations are
 quantised to int8 (g_quant_q8) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
-weight GB/s; the line also carries each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up, down, each
-streamed from HBM), the bf16-activation decode, the prefill TFLOP/s at M=2048 over the same shapes
+weight GB/s; the line also carries each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up, down and
+configs[0]'s Q4_0 4096 x 4096 GEMV, each streamed from HBM), the bf16-activation decode, the prefill TFLOP/s at M=2048
+over the same shapes
 (step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
 MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 32 matvec launches per
 decode step -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
@@ -206,14 +207,19 @@ def make_weights(torch, layers, seed=0):
 def bench_gemv_forms(args, torch, wstack, xq, pk, time_steps):
     """Each decode launch form alone: 32 back-to-back launches per graph replay, rotated over enough copies of its
     weights to exceed twice the L2, so every launch streams its weights from HBM. Per launch: device time, weight
-    GB/s and the fraction of the measured HBM copy."""
+    GB/s and the fraction of the measured HBM copy. The four Q4_K forms of the step, and configs[0]'s Q4_0 4096 x 4096
+    GEMV (the reference's CPU-runnable case) on the same int8 activations."""
     from loom_skills_b200 import ops
-    forms = [("q|k|v", "qkv", 4096, [4096, 1024, 1024]), ("o", "o", 4096, [4096]),
-             ("gate_up", "gate_up", 4096, [24576]), ("down", "down", 12288, [4096])]
+    gen = torch.Generator(device=wstack[0]["o"].device)
+    gen.manual_seed(7)
+    q40 = synth_blocks(torch, wstack[0]["o"].device, 4096, 4096, "q4_0", gen)
+    forms = [("q|k|v", wstack[0]["qkv"], "q4_k", 4096, [4096, 1024, 1024]), ("o", wstack[0]["o"], "q4_k", 4096, [4096]),
+             ("gate_up", wstack[0]["gate_up"], "q4_k", 4096, [24576]),
+             ("down", wstack[0]["down"], "q4_k", 12288, [4096]),
+             ("q4_0 4096x4096 (configs[0])", q40, "q4_0", 4096, [4096])]
     chain = 32
     out = {}
-    for label, name, k, ns in forms:
-        base = wstack[0][name]
+    for label, base, fmt, k, ns in forms:
         nbytes = base.numel()
         copies = max(2, -(-256_000_000 // nbytes))
         ws = [base] + [base.clone() for _ in range(copies - 1)]
@@ -225,15 +231,16 @@ def bench_gemv_forms(args, torch, wstack, xq, pk, time_steps):
             for i in range(chain):
                 w = ws[i % copies]
                 if len(ns) > 1:
-                    ops.mv_q8_multi("q4_k", [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, 1, ys=ys)
+                    ops.mv_q8_multi(fmt, [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, 1, ys=ys)
                 else:
-                    ops.mv_q8("q4_k", w, x, ns[0], k, 1, y=ys[0])
+                    ops.mv_q8(fmt, w, x, ns[0], k, 1, y=ys[0])
         g = Timed(torch, body)
         for _ in range(max(3, args.warmup)):
             g.replay()
         us = time_steps(g.replay, max(5, args.steps)) * 1e3 / chain
         gbs = nbytes / (us * 1e-6) / 1e9
-        out[label] = {"us_per_launch": round(us, 2), "weight_mb": round(nbytes / 1e6, 1), "weight_gbs": round(gbs, 1),
+        out[label] = {"format": fmt, "us_per_launch": round(us, 2), "weight_mb": round(nbytes / 1e6, 1),
+                      "weight_gbs": round(gbs, 1),
                       "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies}
         del g, ws
     return out

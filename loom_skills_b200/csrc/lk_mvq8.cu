@@ -274,10 +274,13 @@ __global__ void __launch_bounds__(kQThreads)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Single-token Q4_K matvec over whole rows (K % 4096 == 0): a persistent grid streams stages of 4 consecutive rows
-// (one contiguous bulk copy each) round-robin over the CTAs. Each of the 4 consumer warps owns one row of the stage;
-// lane l owns the K/2048 (chunk, page) units l + 32u of every row, so its activation codes and group meta are loaded
-// into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles and stores y.
+// Single-token Q4_K / Q4_0 matvec over whole rows (K % 4096 == 0): a persistent grid streams stages of 4 consecutive
+// rows (one contiguous bulk copy each) round-robin over the CTAs. Each of the 4 consumer warps owns one row of the
+// stage; lane l owns the K/2048 (chunk, page) units l + 32u of every row, so its activation codes and group meta are
+// loaded into registers once per launch. Per stage a warp reduces its row's partial sums with shuffles and stores y.
+// Both formats spend 144 bytes per 256 values, so a unit of 64 values is one 32-byte nibble page of a Q4_K
+// super-block (with the super-block's 16-byte header) or two consecutive 18-byte Q4_0 blocks, 36 bytes at a 4-byte
+// aligned offset: nine word loads, the first block's nibbles realigned by funnel shifts.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRStages = 3;
 constexpr int kRowWarps = 4;   // consumer warps = rows per stage
@@ -332,7 +335,7 @@ __host__ __device__ inline int ring_bytes(int stage_bytes) {
 // hands its partial sum to the first through shared memory and a per-row mbarrier). A CTA runs RINGS independent
 // rings (a producer warp, its consumer warps, its own stages and barriers); stages go round-robin over the
 // gridDim.x * RINGS rings. Fewer, larger CTAs make the grid cheaper to launch, retire and hand over to the next grid.
-template <int UPL, int HALVES, int RINGS>
+template <int FMT, int UPL, int HALVES, int RINGS>
 __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
   constexpr int kU = UPL / HALVES;             // units this lane computes
@@ -382,7 +385,8 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     // lane l owns the (chunk, page) units l + 32u: chunk l/4 + 8u, page l % 4 -- the same page for every unit
     const int pg = lane & 3;
     uint32_t xa[kU][8], xb[kU][8];
-    float dx0[kU], dx1[kU], b0[kU], b1[kU];
+    float dx0[kU], dx1[kU], b0[kU], b1[kU];   // Q4_0: b0, b1 unused
+    int s0x8[kU], s1x8[kU];                   // Q4_0: 8 x the groups' code sums (codes are q - 8)
     const float* meta = reinterpret_cast<const float*>(p.xq + p.k);
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -395,9 +399,17 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
       xb[u][4] = v3.x; xb[u][5] = v3.y; xb[u][6] = v3.z; xb[u][7] = v3.w;
       const float4 mt = __ldg(reinterpret_cast<const float4*>(meta + c * 16 + 4 * pg));
       dx0[u] = mt.x;
-      dx1[u] = mt.z * 0.0625f;                 // high nibbles: the dot is 16 x
-      b0[u] = mt.x * mt.y;
-      b1[u] = mt.z * mt.w;
+      if (FMT == LK_Q4_0) {
+        dx1[u] = mt.z;
+        b0[u] = b1[u] = 0.f;
+        s0x8[u] = 8 * int(mt.y);
+        s1x8[u] = 8 * int(mt.w);
+      } else {
+        dx1[u] = mt.z * 0.0625f;               // high nibbles: the dot is 16 x
+        b0[u] = mt.x * mt.y;
+        b1[u] = mt.z * mt.w;
+        s0x8[u] = s1x8[u] = 0;
+      }
     }
     const uint32_t hsel = (pg & 1) ? 0x4432u : 0x4410u;
     const uint32_t big = (pg >> 1) ? 0xFFFFFFFFu : 0u;
@@ -414,6 +426,26 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
           const uint8_t* sb = wr + ((lane >> 2) + 8 * (half * kU + u)) * kChunkBytes;
+          if (FMT == LK_Q4_0) {
+            // blocks 2 pg, 2 pg + 1 of the chunk: [d_a | 16 nibble bytes | d_b | 16 nibble bytes] from byte 36 pg
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(sb + 36 * pg);
+            uint32_t v[9];
+#pragma unroll
+            for (int j = 0; j < 9; ++j) v[j] = bw[j];
+            const float da = h2f(uint16_t(v[0] & 0xffffu)), db = h2f(uint16_t(v[4] >> 16));
+            int la = 0, ha = 0, lb = 0, hb = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {   // byte i of a block: element i (low nibble), element 16 + i (high)
+              const uint32_t qa = __funnelshift_r(v[j], v[j + 1], 16), qb = v[5 + j];
+              la = dp4a_us(qa & 0x0F0F0F0Fu, xa[u][j], la);
+              ha = dp4a_us(qa & 0xF0F0F0F0u, xa[u][4 + j], ha);
+              lb = dp4a_us(qb & 0x0F0F0F0Fu, xb[u][j], lb);
+              hb = dp4a_us(qb & 0xF0F0F0F0u, xb[u][4 + j], hb);
+            }
+            // sum((q - 8) x) = dot - 8 sum(x); the high nibbles' dot is 16 x, exactly
+            acc += da * dx0[u] * i2f_small(la + (ha >> 4) - s0x8[u]) + db * dx1[u] * i2f_small(lb + (hb >> 4) - s1x8[u]);
+            continue;
+          }
           const uint4 hd = *reinterpret_cast<const uint4*>(sb);
           const uint4 q0 = *reinterpret_cast<const uint4*>(sb + 16 + 32 * pg);
           const uint4 q1 = *reinterpret_cast<const uint4*>(sb + 32 + 32 * pg);
@@ -458,12 +490,12 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
   }
 }
 
-template <int UPL, int HALVES, int RINGS>
+template <int FMT, int UPL, int HALVES, int RINGS>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
   const int smem = RINGS * ring_bytes(stage_bytes);
   constexpr int threads = 32 * RINGS * (1 + kRowWarps * HALVES);
-  auto kern = k_mv_q8_rows<UPL, HALVES, RINGS>;
+  auto kern = k_mv_q8_rows<FMT, UPL, HALVES, RINGS>;
   // the attribute and the occupancy query once per (device, shared-memory size): they cost host time on every call
   struct Entry {
     int dev, smem, per_sm, sms;
@@ -583,16 +615,16 @@ int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStrea
 }
 
 static bool rows_path(int fmt, int k, int tokens) {
-  return fmt == LK_Q4_K && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096;
+  return (fmt == LK_Q4_K || fmt == LK_Q4_0) && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096;
 }
 
-static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
+static int mv_q8_rows(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
                       const uint8_t* xq, cudaStream_t s) {
   RowArgs ra{};
   ra.xq = xq;
   ra.k = k;
   ra.accumulate = accumulate;
-  ra.rb = int64_t(k) / 256 * kChunkBytes;
+  ra.rb = int64_t(k) / 256 * kChunkBytes;   // Q4_K: k / 256 super-blocks; Q4_0: k / 32 blocks of 18 bytes, the same
   ra.sr = kRowWarps;
   ra.nseg = nseg;
   ra.start[0] = 0;
@@ -603,10 +635,11 @@ static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* con
     ra.start[g + 1] = ra.start[g] + (ns[g] + ra.sr - 1) / ra.sr;
   }
   ra.nstages = ra.start[nseg];
+  const bool q40 = fmt == LK_Q4_0;
   switch (k / 2048) {   // units (chunk, page) per lane
-    case 2: return launch_rows<2, 1, kRingsShort>(ra, s);
-    case 4: return launch_rows<4, 2, kRingsLong>(ra, s);
-    case 6: return launch_rows<6, 2, kRingsLong>(ra, s);
+    case 2: return q40 ? launch_rows<LK_Q4_0, 2, 1, kRingsShort>(ra, s) : launch_rows<LK_Q4_K, 2, 1, kRingsShort>(ra, s);
+    case 4: return q40 ? launch_rows<LK_Q4_0, 4, 2, kRingsLong>(ra, s) : launch_rows<LK_Q4_K, 4, 2, kRingsLong>(ra, s);
+    case 6: return q40 ? launch_rows<LK_Q4_0, 6, 2, kRingsLong>(ra, s) : launch_rows<LK_Q4_K, 6, 2, kRingsLong>(ra, s);
   }
   return LK_EUNSUPPORTED;
 }
@@ -615,7 +648,7 @@ static int mv_q8_rows(int nseg, const int* ns, const void* const* ws, float* con
 // row-streaming kernel applies, else one launch each.
 int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int tokens,
                 int accumulate, const uint8_t* xq, cudaStream_t s) {
-  if (rows_path(fmt, k, tokens) && nseg <= kMaxSegs) return mv_q8_rows(nseg, ns, ws, ys, k, accumulate, xq, s);
+  if (rows_path(fmt, k, tokens) && nseg <= kMaxSegs) return mv_q8_rows(fmt, nseg, ns, ws, ys, k, accumulate, xq, s);
   for (int g = 0; g < nseg; ++g) {
     int rc = mv_q8(fmt, ns[g], k, tokens, accumulate, xq, ws[g], ys[g], s);
     if (rc != LK_OK) return rc;
@@ -631,7 +664,7 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
     const int ns[1] = {n};
     const void* ws[1] = {w};
     float* ys[1] = {y};
-    return mv_q8_rows(1, ns, ws, ys, k, accumulate, xq, s);
+    return mv_q8_rows(fmt, 1, ns, ws, ys, k, accumulate, xq, s);
   }
   const int tokb = tokens <= 1 ? 1 : 8;
   CUtensorMap wm;

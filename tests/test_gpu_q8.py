@@ -53,7 +53,8 @@ class TestQuantQ8:
 class TestMvQ8:
     @pytest.mark.parametrize("fmt", ["q4_0", "q4_k"])
     @pytest.mark.parametrize("n,k,tokens", [(256, 256, 1), (4096, 4096, 1), (1000, 2048, 3), (64, 12288, 8),
-                                            (300, 1024, 13), (1024, 4096, 1)])
+                                            (300, 1024, 13), (1024, 4096, 1), (130, 8192, 1), (96, 12288, 1),
+                                            (4099, 4096, 1)])
     def test_vs_oracle(self, ops, fmt, n, k, tokens):
         rng = np.random.default_rng(n + k + tokens)
         w = QUANT[fmt]((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
@@ -89,7 +90,7 @@ class TestMvQ8:
 
 class TestMvQ8Multi:
     @pytest.mark.parametrize("fmt,k,tokens", [("q4_k", 4096, 1), ("q4_k", 12288, 1), ("q4_0", 4096, 1),
-                                              ("q4_k", 4096, 3)])
+                                              ("q4_0", 12288, 1), ("q4_k", 4096, 3)])
     def test_segments_match_single_launches(self, ops, fmt, k, tokens):
         rng = np.random.default_rng(k + tokens)
         ns = [512, 128, 130] if fmt == "q4_k" else [256, 64]
