@@ -644,21 +644,23 @@ def run_ours(args):
 def run_profile_case(args):
     """A few launches of one hot kernel at one bench shape, for ncu captures (profiles/): warm-up launches, then
     `--steps` profiled ones. Cases: mv_gate_up (Q4_K q8 matvec, K=4096 N=24576), mv_down (K=12288 N=4096),
-    gemm_gate_up (Q4_K GEMM, M=2048 K=4096 N=24576), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880)."""
+    mv8_gate_up (the gate_up matvec on 8 tokens), gemm_gate_up (Q4_K GEMM, M=2048 K=4096 N=24576), gemm64_down
+    (Q4_K GEMM, M=64 K=12288 N=4096), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880)."""
     import torch
 
     from loom_skills_b200 import ops
     dev = torch.device("cuda", 0)
     rng = np.random.default_rng(0)
     case = args.profile_case
-    if case.startswith("mv_"):
-        k, n = (4096, 24576) if case == "mv_gate_up" else (12288, 4096)
+    if case.startswith("mv"):
+        k, n = (12288, 4096) if case == "mv_down" else (4096, 24576)
+        t = 8 if case == "mv8_gate_up" else 1
         w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
-        xq = ops.quant_q8(torch.randn(1, k, device=dev))
-        y = torch.empty(1, n, device=dev)
-        fn = lambda: ops.mv_q8("q4_k", w, xq, n, k, 1, y=y)   # noqa: E731
-    elif case == "gemm_gate_up":
-        m, k, n = 2048, 4096, 24576
+        xq = ops.quant_q8(torch.randn(t, k, device=dev))
+        y = torch.empty(t, n, device=dev)
+        fn = lambda: ops.mv_q8("q4_k", w, xq, n, k, t, y=y)   # noqa: E731
+    elif case.startswith("gemm"):
+        m, k, n = (64, 12288, 4096) if case == "gemm64_down" else (2048, 4096, 24576)
         w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
         x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
         y = torch.empty(m, n, device=dev)

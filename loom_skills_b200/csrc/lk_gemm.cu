@@ -48,6 +48,9 @@ struct GemmArgs {
   int max_tiles;
   int xrows, ku, n_experts;
   int n_fast;                 // persistent dense kernel: walk the n tiles of an m tile first (large A, small W)
+  // persistent dense store / acc: K split into ksplit ranges of kps packed stages (256 values) each; every range is
+  // a tile of its own whose row-scaled partial product is added into y (zeroed first for store)
+  int ksplit, kps;
 };
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
@@ -440,16 +443,22 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
   const int kstages = p.k / kBK;
   const int mt = (p.rows + kTM - 1) / kTM, nt = (p.n + BN - 1) / BN;
   // tiles: dense m x n; grouped (super-tile, n) with the n tiles of a super-tile consecutive
-  const int ntiles = GROUP == kDense ? mt * nt : moe_super_table(p.tile_info, p.max_tiles, p.n_experts, stbl) * nt;
+  const int ntiles =
+      GROUP == kDense ? mt * nt * p.ksplit : moe_super_table(p.tile_info, p.max_tiles, p.n_experts, stbl) * nt;
   const int my_tiles = ntiles > int(blockIdx.x) ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
-  // tile t -> first output row, first weight row of the tile inside the expert block, expert, valid rows
+  // tile t -> first output row, first weight row of the tile inside the expert block, expert, valid rows, and the
+  // k stages [ks0, ks1) it accumulates (dense: split ranges start on packed-stage boundaries)
+  int ks0 = 0, ks1 = kstages;
   auto tile_of = [&](int t, int& m0, int& n0, int& e, int& valid) {
     if (GROUP == kDense) {
-      const int mi = p.n_fast ? t / nt : t % mt, ni = p.n_fast ? t % nt : t / mt;
+      const int tt = t % (mt * nt), si = t / (mt * nt);
+      const int mi = p.n_fast ? tt / nt : tt % mt, ni = p.n_fast ? tt % nt : tt / mt;
       m0 = mi * kTM;
       n0 = ni * BN;
       e = 0;
       valid = min(kTM, p.rows - m0);
+      ks0 = si * p.kps * 4;
+      ks1 = min(kstages, ks0 + p.kps * 4);
     } else {
       int first, rows;
       moe_super_lookup(p.tile_info, stbl, t / nt, e, first, rows);
@@ -509,7 +518,7 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
           arow[j] = a >= 0 ? a / p.ku : p.xrows;
         }
       }
-      for (int ks = 0; ks < kstages; ++ks) {
+      for (int ks = ks0; ks < ks1; ++ks) {
         if ((ks & 3) == 0) {
           const int sr = gr % SRP;
           if (gr >= SRP && !mbar_wait(&empty_r[sr], ((gr / SRP) - 1) & 1)) atomicOr(&g_status, 1u);
@@ -542,11 +551,13 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
     const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
     int ga = 0, gb = 0;
     for (int li = 0; li < my_tiles; ++li) {
+      int m0, n0, e, valid;
+      tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid);
       const int buf = li % NBUF;
       if (li >= NBUF && !mbar_wait(&acc_empty[buf], ((li / NBUF) - 1) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
       const uint32_t tacc = tmem + buf * kAcc;
-      for (int ks = 0; ks < kstages; ++ks) {
+      for (int ks = ks0; ks < ks1; ++ks) {
         const int sa = ga % kSAp, sb = gb % kSBp;
         if (!mbar_wait(&full_a[sa], (ga / kSAp) & 1)) atomicOr(&g_status, 1u);
         if (!mbar_wait(&full_b[sb], (gb / kSBp) & 1)) atomicOr(&g_status, 1u);
@@ -560,13 +571,13 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
 #pragma unroll
               for (int wi = 0; wi < NW; ++wi) {
                 uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
-                umma_f16(tacc + (mh * NW + wi) * BN, ad, bd, idesc, (ks | kk) != 0);
+                umma_f16(tacc + (mh * NW + wi) * BN, ad, bd, idesc, ks != ks0 || kk != 0);
               }
             }
           }
           umma_commit(&empty_a[sa]);
           umma_commit(&empty_b[sb]);
-          if (ks == kstages - 1) umma_commit(&acc_full[buf]);
+          if (ks == ks1 - 1) umma_commit(&acc_full[buf]);
         }
         __syncwarp();
         ++ga;
@@ -579,7 +590,9 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
     constexpr int kGroupsPerThread = kRowsB * 2 / (kDqWarps * 32);
     int gb = 0, gr = 0;
     for (int li = 0; li < my_tiles; ++li) {
-      for (int ks = 0; ks < kstages; ++ks) {
+      int m0, n0, e, valid;
+      tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid);
+      for (int ks = ks0; ks < ks1; ++ks) {
         const int sub = ks & 3, sr = gr % SRP, sb = gb % kSBp;
         if (sub == 0 && !mbar_wait(&full_r[sr], (gr / SRP) & 1)) atomicOr(&g_status, 1u);
         if (gb >= kSBp && !mbar_wait(&empty_b[sb], ((gb / kSBp) - 1) & 1)) atomicOr(&g_status, 1u);
@@ -647,6 +660,10 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
             if (col_ok && trow < valid_rows) {
               const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
+              if (GROUP == kDense && p.ksplit > 1) {   // one K range of several: add the partial
+                atomicAdd(reinterpret_cast<float4*>(p.dst[0] + off), o);
+                continue;
+              }
               if (MODE == LK_ACC) {
                 float4 old = *reinterpret_cast<const float4*>(p.dst[0] + off);
                 o.x += old.x;
@@ -751,27 +768,52 @@ static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // dense: the exact tile count; grouped: a bound (at most one super-tile per schedule tile)
-  const int ntiles = (GROUP == kDense ? (a.rows + kBM * MH - 1) / (kBM * MH) : a.rows / 64) * ((a.n + BN - 1) / BN);
+  // dense: the exact tile count (with the K ranges); grouped: a bound (at most one super-tile per schedule tile)
+  const int ntiles = (GROUP == kDense ? (a.rows + kBM * MH - 1) / (kBM * MH) * a.ksplit : a.rows / 64) *
+                     ((a.n + BN - 1) / BN);
   kern<<<min(ntiles, sms), kGemmPThreads, smem, s>>>(m.a, m.w, m.w2, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 // tile shape per mode: (BN, NW, MH)
 //   dense store/acc  128 x 1 x 2   a 256 x 128 tile, two M=128 accumulators sharing each dequantised B stage
+//   ... at most 128 rows  256 x 1 x 1   a 128 x 256 tile: no padded M half, twice the weight rows per stage
 //   dense swiglu     128 x 2 x 1   128 rows x 128 columns of gate and of up
 //   grouped gate/up  128 x 2 x 1   (MoE super-tiles hold at most 128 rows of one expert; gathered or sorted rows)
 //   grouped down     256 x 1 x 1
 template <int FMT>
-static int gemm_fmt(int mode, int group, const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+static int gemm_fmt(int mode, int group, bool short_m, const GemmMaps& m, const GemmArgs& a, dim3 grid,
+                    cudaStream_t s) {
   if (group == kDense) {   // persistent kernel
     if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kDense, 1, 2, 4, 2, 2>(m, a, s);
+    if (short_m)
+      return mode == LK_ACC ? launch_gemm_p<FMT, 256, 1, LK_ACC, kDense, 1, 2, 4, 2, 2>(m, a, s)
+                            : launch_gemm_p<FMT, 256, 1, LK_STORE, kDense, 1, 2, 4, 2, 2>(m, a, s);
     if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 2, 2, 3, 4, 2>(m, a, s);
     return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 3, 4, 2>(m, a, s);
   }
   if (group == kGather) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kGather, 1, 2, 4, 2, 2>(m, a, s);
   if (mode == LK_SWIGLU_SORTED) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kSorted, 1, 2, 4, 2, 2>(m, a, s);
   return launch_gemm_p<FMT, 256, 1, LK_STORE, kSorted, 1, 2, 4, 2, 2>(m, a, s);
+}
+
+// K ranges for a dense store / acc GEMM of `tiles` output tiles and kp packed stages on `sms` persistent CTAs: the
+// count whose rounds x (stages per range + 1) is least -- the + 1 stands for a tile's fill and epilogue -- with no
+// empty range; the smallest such count on ties
+static int choose_ksplit(int tiles, int kp, int sms) {
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int sp = 1; sp <= std::min(kp, 32); ++sp) {
+    const int per = (kp + sp - 1) / sp;
+    if ((kp + per - 1) / per != sp) continue;
+    const int64_t rounds = (int64_t(tiles) * sp + sms - 1) / sms;
+    const int64_t cost = rounds * (per + 1);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
 }
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
@@ -814,9 +856,23 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
   a.w2_row_offset = (mode != LK_STORE && mode != LK_ACC && !w2) ? int(w2_offset / rb) : 0;
-  // weight rows per tile: 256 for grouped down, 128 per weight otherwise
-  const int bn = (group == kSorted && mode == LK_STORE) ? 256 : 128;
-  const int tm = (group == kDense && mode != LK_SWIGLU) ? 2 * kBM : kBM;   // tile rows
+  // at most 128 rows (dense store / acc): 128-row tiles of 256 weight rows
+  const bool short_m = group == kDense && mode != LK_SWIGLU && rows <= kBM;
+  // weight rows per tile: 256 for grouped down and short dense, 128 per weight otherwise
+  const int bn = ((group == kSorted && mode == LK_STORE) || short_m) ? 256 : 128;
+  const int tm = (group == kDense && mode != LK_SWIGLU && !short_m) ? 2 * kBM : kBM;   // tile rows
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int kp = k / 256;
+  a.ksplit = 1;
+  a.kps = kp;
+  // fewer output tiles than SMs, one destination: the K ranges may add into y
+  const int dense_tiles = ((rows + tm - 1) / tm) * ((n + bn - 1) / bn);
+  if (group == kDense && mode != LK_SWIGLU && !out && rows > 0 && dense_tiles < sms) {
+    a.ksplit = choose_ksplit(dense_tiles, kp, sms);
+    a.kps = (kp + a.ksplit - 1) / a.ksplit;
+  }
   GemmMaps m;
   int rc = group == kGather ? make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xrows, k, kBK, 1,
                                        CU_TENSOR_MAP_SWIZZLE_128B)   // one-row boxes for gather4
@@ -832,10 +888,12 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   if (rc != LK_OK) return rc;
   // grouped: one CTA per possible 128-row super-tile (at most one per schedule tile)
   dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + tm - 1) / tm : rows / 64);
+  if (a.ksplit > 1 && mode == LK_STORE && cudaMemsetAsync(y, 0, size_t(rows) * n * 4, s) != cudaSuccess)
+    return LK_ECUDA;   // the K ranges add into a zeroed y
   switch (fmt) {
-    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, m, a, grid, s);
-    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, m, a, grid, s);
-    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, m, a, grid, s);
+    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, short_m, m, a, grid, s);
+    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, short_m, m, a, grid, s);
+    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, short_m, m, a, grid, s);
   }
   return LK_EUNSUPPORTED;
 }

@@ -192,6 +192,23 @@ class TestGemm:
         ys = host(ops.gemm(fmt, "swiglu", dev(x16), dev(sc), dev(w), n, w2=dev(w2)))
         assert O.rel_l2(ys, O.gemm_ref(fmt, w, x16, sc, n, k, mode="swiglu", w2=w2)) < TOL
 
+    @pytest.mark.parametrize("fmt", ["q4_k", "q4_0", "iq4_nl"])
+    @pytest.mark.parametrize("rows,n,k", [(64, 1024, 4096), (37, 512, 12288), (128, 272, 1024), (129, 256, 2048)])
+    def test_short_rows_split_k(self, ops, fmt, rows, n, k):
+        # at most 128 rows: 128 x 256 tiles; few tiles: K split into ranges whose partials add into y (store zeroes
+        # y first, acc adds onto it)
+        w = weights(fmt, n, k, 71)
+        _, x16, sc = row_scaled(rows, k, 72, big=True)
+        y = host(ops.gemm(fmt, "store", dev(x16), dev(sc), dev(w), n, y=dev(np.full((rows, n), 7.0, np.float32))))
+        ref = O.gemm_ref(fmt, w, x16, sc, n, k)
+        assert O.rel_l2(y, ref) < TOL, O.rel_l2(y, ref)
+        y0 = np.random.default_rng(73).standard_normal((rows, n)).astype(np.float32)
+        ya = dev(y0)
+        ops.gemm(fmt, "acc", dev(x16), dev(sc), dev(w), n, y=ya)
+        ref_acc = O.gemm_ref(fmt, w, x16, sc, n, k, mode="acc", y_old=y0)
+        assert O.rel_l2(host(ya), ref_acc) < TOL, O.rel_l2(host(ya), ref_acc)
+        assert ops.device_status() == 0
+
     def test_empty_rows(self, ops):
         w = weights("q4_k", 256, 256, 1)
         y = ops.gemm("q4_k", "store", torch.empty(0, 256, dtype=torch.float16, device="cuda"),
