@@ -115,6 +115,9 @@ int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float*
  *   Y[rows][n] (+)= (X16 . W16^T) * scales[row][1]; swiglu: silu(G) * U with G, U the two weights' products.
  * x16: [rows][k] f16 (lk_row_scale_f16's output), scales: [rows][2] f32, y: [rows][n] f32.
  * Formats Q4_0, Q4_K, IQ4_NL. k % 256 == 0, n % 16 == 0; x16, w 16-byte aligned. Any rows >= 1.
+ * When store / acc has fewer output tiles than the device has SMs (few rows and narrow n), K is split into ranges
+ * whose partial products are added into y atomically (store first zeroes y on the stream): the f32 sums then run
+ * in a varying order, so such results agree between runs to rounding, not bit for bit.
  */
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
             const void* w2, float* y, lk_stream_t stream);

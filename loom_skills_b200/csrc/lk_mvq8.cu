@@ -36,13 +36,12 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int ele
 
 namespace {
 
-constexpr int kQRows = 64;
 constexpr int kQConsumers = 8;
 constexpr int kQThreads = 32 * (1 + kQConsumers);
-constexpr int kQStages = 4;
-constexpr int kQWBytes = kQRows * kChunkBytes;   // 9216
-constexpr int kQRpt = kQRows * 4 / (32 * kQConsumers);   // rows per consumer thread
-constexpr int kQRowStride = kQRows / kQRpt;
+// chunked matvec tiles: one token -- 64 rows, 4 stages; token tiles of 8 -- 128 rows (2 per thread, so each x load
+// serves two rows), 3 stages, 96 registers: two CTAs per SM. Measured on the eight-token Qwen3-8B projections:
+// 256 rows (151 registers, one CTA per SM) and forced two-CTA 256-row builds (spills) were slower.
+constexpr int kQRows1 = 64, kQStages1 = 4, kQRows8 = 128, kQStages8 = 3;
 constexpr int kPreWaitStages = 1;   // weight stages a CTA requests before griddepcontrol.wait (see above)
 
 LK_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -79,30 +78,45 @@ struct Q8Args {
   int nchunks, splits, cps;   // chunks of 256, CTAs per row tile (cluster size), chunks per split
 };
 
-template <int TOKB>
+// stage of the chunked kernel: QR weight rows of one 256-value chunk, then the chunk's x codes and meta of TOKB tokens
+template <int TOKB, int QR>
 constexpr int q8_stage_bytes() {
-  return (kQWBytes + TOKB * 256 + TOKB * 64 + 127) / 128 * 128;
+  return (QR * kChunkBytes + TOKB * 256 + TOKB * 64 + 127) / 128 * 128;
+}
+template <int TOKB, int QR, int QS>
+constexpr int q8_smem_bytes() {
+  return QS * q8_stage_bytes<TOKB, QR>() + 2 * QS * 8 + TOKB * QR * 4;
 }
 
-// The four 16-byte x code words of token t for groups (2p, 2p+1) of the staged chunk, and their meta.
-template <int FMT, int TOKB>
+// Matvec over chunks of 256 values, for several tokens (tiles of TOKB) or for one token outside the row kernel's
+// shapes. CTA (split, row tile) streams QR rows over its range of chunks through a QS-stage ring; a stage is one 2-D
+// TMA box of the rows' 144-byte chunks plus the chunk's x codes and meta for the TOKB tokens. Consumer thread (rs, pg)
+// owns page pg (64 values) of rows rs + 64 r, r < QR / 64: per stage it decodes those rows' weight words and scales
+// into registers once, then for every token loads the page's x once and runs it against all its rows. Every one of
+// the TOKB token rows is computed: rows past the tile's tokens are zero-filled by the TMA and never stored, and the
+// unconditional loop lets the loads of later tokens go out ahead of the arithmetic of earlier ones. The split CTAs
+// of a row tile form a cluster and reduce their partial sums through distributed shared memory.
+template <int FMT, int TOKB, int QR, int QS>
 __global__ void __launch_bounds__(kQThreads)
     k_mv_q8(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
             const __grid_constant__ CUtensorMap mmap, const Q8Args p) {
-  constexpr int kStage = q8_stage_bytes<TOKB>();
+  constexpr int kStage = q8_stage_bytes<TOKB, QR>();
+  constexpr int kWBytes = QR * kChunkBytes;
+  constexpr int kRpt = QR / 64;   // rows per consumer thread
+  static_assert(QR % 64 == 0 && QR <= 256, "64 to 256 rows per tile (one TMA box)");
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kQStages * kStage);
-  uint64_t* empty = full + kQStages;
-  float* red = reinterpret_cast<float*>(empty + kQStages);   // [TOKB][kQRows] partial sums (split-K)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + QS * kStage);
+  uint64_t* empty = full + QS;
+  float* red = reinterpret_cast<float*>(empty + QS);   // [TOKB][QR] partial sums (split-K)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.y * kQRows;
+  const int row0 = blockIdx.y * QR;
   const int split = blockIdx.x;
   const int c0 = split * p.cps;
   const int nst = max(0, min(p.nchunks, c0 + p.cps) - c0);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kQStages; ++i) {
+    for (int i = 0; i < QS; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kQConsumers);
     }
@@ -114,7 +128,7 @@ __global__ void __launch_bounds__(kQThreads)
     if (lane == 0) {
       griddep_launch();
       prefetch_tensormap(&wmap);
-      const uint32_t bytes = kQWBytes + TOKB * 256 + TOKB * 64;
+      const uint32_t bytes = kWBytes + TOKB * 256 + TOKB * 64;
       const int pre = min(kPreWaitStages, nst);
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], bytes);
@@ -122,17 +136,17 @@ __global__ void __launch_bounds__(kQThreads)
       }
       griddep_wait();   // activations come from the previous kernel
       for (int i = 0; i < pre; ++i) {
-        tma_load_2d(smem + i * kStage + kQWBytes, &xmap, (c0 + i) * 256, 0, &full[i]);
-        tma_load_2d(smem + i * kStage + kQWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[i]);
+        tma_load_2d(smem + i * kStage + kWBytes, &xmap, (c0 + i) * 256, 0, &full[i]);
+        tma_load_2d(smem + i * kStage + kWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[i]);
       }
       for (int i = pre; i < nst; ++i) {
-        const int s = i % kQStages;
-        if (i >= kQStages && !mbar_wait(&empty[s], ((i / kQStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        const int s = i % QS;
+        if (i >= QS && !mbar_wait(&empty[s], ((i / QS) - 1) & 1)) atomicOr(&g_status, 1u);
         mbar_expect_tx(&full[s], bytes);
         uint8_t* st = smem + s * kStage;
         tma_load_2d(st, &wmap, (c0 + i) * (kChunkBytes / 4), row0, &full[s]);
-        tma_load_2d(st + kQWBytes, &xmap, (c0 + i) * 256, 0, &full[s]);
-        tma_load_2d(st + kQWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[s]);
+        tma_load_2d(st + kWBytes, &xmap, (c0 + i) * 256, 0, &full[s]);
+        tma_load_2d(st + kWBytes + TOKB * 256, &mmap, (c0 + i) * 16, 0, &full[s]);
       }
     }
     __syncwarp();
@@ -141,87 +155,96 @@ __global__ void __launch_bounds__(kQThreads)
     const int ct = threadIdx.x - 32;
     const int pg = ct & 3, rs = ct >> 2;
     const int ntok = min(p.ntok, TOKB);
-    float acc[kQRpt][TOKB];
+    float acc[kRpt][TOKB];
 #pragma unroll
-    for (int r = 0; r < kQRpt; ++r)
+    for (int r = 0; r < kRpt; ++r)
 #pragma unroll
       for (int t = 0; t < TOKB; ++t) acc[r][t] = 0.f;
 
     for (int i = 0; i < nst; ++i) {
-      const int s = i % kQStages;
-      if (!mbar_wait(&full[s], (i / kQStages) & 1)) atomicOr(&g_status, 1u);
+      const int s = i % QS;
+      if (!mbar_wait(&full[s], (i / QS) & 1)) atomicOr(&g_status, 1u);
       const uint8_t* st = smem + s * kStage;
-      const uint8_t* xs = st + kQWBytes;
-      const float* ms = reinterpret_cast<const float*>(st + kQWBytes + TOKB * 256);
+      const uint8_t* xs = st + kWBytes;
+      const float* ms = reinterpret_cast<const float*>(st + kWBytes + TOKB * 256);
+      // this thread's rows, page pg: eight nibble words each and their scales. Q4_K: words = the page's 32 bytes
+      // (low nibbles group 2pg, high nibbles group 2pg + 1), sa / sb = d * sc of the two groups (sb / 16: the high
+      // nibbles' dot is 16 x), ma / mb = dmin * m. Q4_0: words 0-3 = block 2pg's codes (realigned), 4-7 = block
+      // 2pg + 1's, sa / sb = their d.
+      uint32_t w[kRpt][8];
+      float sa[kRpt], sb[kRpt], ma[kRpt], mb[kRpt];
 #pragma unroll
-      for (int rr = 0; rr < kQRpt; ++rr) {
-        const uint8_t* wr = st + (rs + kQRowStride * rr) * kChunkBytes;
+      for (int r = 0; r < kRpt; ++r) {
+        const uint8_t* wr = st + (rs + 64 * r) * kChunkBytes;
         if (FMT == LK_Q4_K) {
-          // page pg = groups 2pg (low nibbles) and 2pg + 1 (high nibbles) of the super-block
           const uint4 hd = *reinterpret_cast<const uint4*>(wr);
           const uint4 q0 = *reinterpret_cast<const uint4*>(wr + 16 + 32 * pg);
           const uint4 q1 = *reinterpret_cast<const uint4*>(wr + 32 + 32 * pg);
-          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          w[r][0] = q0.x;
+          w[r][1] = q0.y;
+          w[r][2] = q0.z;
+          w[r][3] = q0.w;
+          w[r][4] = q1.x;
+          w[r][5] = q1.y;
+          w[r][6] = q1.z;
+          w[r][7] = q1.w;
           uint32_t sc0, m0, sc1, m1;
           q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * pg, sc0, m0);
           q4k_scale_min_w(hd.y, hd.z, hd.w, 2 * pg + 1, sc1, m1);
           const float d = h2f(uint16_t(hd.x & 0xffffu)), dmin = h2f(uint16_t(hd.x >> 16));
-          const float ds0 = d * u6_to_f(sc0), ds1 = d * u6_to_f(sc1) * 0.0625f;   // high nibbles: 16 x code
-          const float dm0 = dmin * u6_to_f(m0), dm1 = dmin * u6_to_f(m1);
-#pragma unroll
-          for (int t = 0; t < TOKB; ++t) {
-            if (t >= ntok) break;
-            const uint4* xw = reinterpret_cast<const uint4*>(xs + t * 256 + 64 * pg);
-            const uint4 xa0 = xw[0], xa1 = xw[1], xb0 = xw[2], xb1 = xw[3];
-            const float4 mt = *reinterpret_cast<const float4*>(ms + t * 16 + 4 * pg);   // d0, sum0, d1, sum1
-            const uint32_t xa[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
-            const uint32_t xb[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
-            int i0 = 0, i1 = 0, i2 = 0, i3 = 0;   // four independent dp4a chains
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              i0 = dp4a_us(w[j] & 0x0F0F0F0Fu, xa[j], i0);
-              i1 = dp4a_us(w[j] & 0xF0F0F0F0u, xb[j], i1);
-              i2 = dp4a_us(w[j + 1] & 0x0F0F0F0Fu, xa[j + 1], i2);
-              i3 = dp4a_us(w[j + 1] & 0xF0F0F0F0u, xb[j + 1], i3);
-            }
-            acc[rr][t] += mt.x * (ds0 * i2f_small(i0 + i2) - dm0 * mt.y) +
-                          mt.z * (ds1 * i2f_small(i1 + i3) - dm1 * mt.w);
-          }
+          sa[r] = d * u6_to_f(sc0);
+          sb[r] = d * u6_to_f(sc1) * 0.0625f;
+          ma[r] = dmin * u6_to_f(m0);
+          mb[r] = dmin * u6_to_f(m1);
         } else {
           // block pair pg = blocks 2pg (bytes 36pg..+17: d, then codes starting 2 bytes into a word) and 2pg + 1
           const uint32_t* wv = reinterpret_cast<const uint32_t*>(wr + 36 * pg);
           uint32_t v[9];
 #pragma unroll
           for (int j = 0; j < 9; ++j) v[j] = wv[j];
-          uint32_t qa[4], qb[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            qa[j] = __funnelshift_r(v[j], v[j + 1], 16);   // codes of the even block, realigned
-            qb[j] = v[5 + j];
+            w[r][j] = __funnelshift_r(v[j], v[j + 1], 16);   // codes of the even block, realigned
+            w[r][4 + j] = v[5 + j];
           }
-          const float da = h2f(uint16_t(v[0] & 0xffffu)), db = h2f(uint16_t(v[4] >> 16));
+          sa[r] = h2f(uint16_t(v[0] & 0xffffu));
+          sb[r] = h2f(uint16_t(v[4] >> 16));
+          ma[r] = mb[r] = 0.f;
+        }
+      }
 #pragma unroll
-          for (int t = 0; t < TOKB; ++t) {
-            if (t >= ntok) break;
-            const uint4* xw = reinterpret_cast<const uint4*>(xs + t * 256 + 64 * pg);
-            const uint4 xa0 = xw[0], xa1 = xw[1], xb0 = xw[2], xb1 = xw[3];
-            const float4 mt = *reinterpret_cast<const float4*>(ms + t * 16 + 4 * pg);
-            // block a: elements 0-15 = low nibbles (x words xa0), 16-31 = high nibbles (xa1)
-            const uint32_t xal[4] = {xa0.x, xa0.y, xa0.z, xa0.w}, xah[4] = {xa1.x, xa1.y, xa1.z, xa1.w};
-            const uint32_t xbl[4] = {xb0.x, xb0.y, xb0.z, xb0.w}, xbh[4] = {xb1.x, xb1.y, xb1.z, xb1.w};
+      for (int t = 0; t < TOKB; ++t) {
+        const uint4* xw = reinterpret_cast<const uint4*>(xs + t * 256 + 64 * pg);
+        const uint4 xa0 = xw[0], xa1 = xw[1], xb0 = xw[2], xb1 = xw[3];
+        const float4 mt = *reinterpret_cast<const float4*>(ms + t * 16 + 4 * pg);   // d0, sum0, d1, sum1
+        const uint32_t xa[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+        const uint32_t xb[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
+#pragma unroll
+        for (int r = 0; r < kRpt; ++r) {
+          if (FMT == LK_Q4_K) {
+            int i0 = 0, i1 = 0, i2 = 0, i3 = 0;   // four independent dp4a chains
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              i0 = dp4a_us(w[r][j] & 0x0F0F0F0Fu, xa[j], i0);
+              i1 = dp4a_us(w[r][j] & 0xF0F0F0F0u, xb[j], i1);
+              i2 = dp4a_us(w[r][j + 1] & 0x0F0F0F0Fu, xa[j + 1], i2);
+              i3 = dp4a_us(w[r][j + 1] & 0xF0F0F0F0u, xb[j + 1], i3);
+            }
+            acc[r][t] += mt.x * (sa[r] * i2f_small(i0 + i2) - ma[r] * mt.y) +
+                         mt.z * (sb[r] * i2f_small(i1 + i3) - mb[r] * mt.w);
+          } else {
+            // block a: elements 0-15 = low nibbles (x words 0-3), 16-31 = high nibbles (x words 4-7); block b alike
             int la = 0, ha = 0, lb = 0, hb = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              if (FMT == LK_Q4_0) {
-                la = dp4a_us(qa[j] & 0x0F0F0F0Fu, xal[j], la);
-                ha = dp4a_us(qa[j] & 0xF0F0F0F0u, xah[j], ha);
-                lb = dp4a_us(qb[j] & 0x0F0F0F0Fu, xbl[j], lb);
-                hb = dp4a_us(qb[j] & 0xF0F0F0F0u, xbh[j], hb);
-              }
+              la = dp4a_us(w[r][j] & 0x0F0F0F0Fu, xa[j], la);
+              ha = dp4a_us(w[r][j] & 0xF0F0F0F0u, xa[4 + j], ha);
+              lb = dp4a_us(w[r][4 + j] & 0x0F0F0F0Fu, xb[j], lb);
+              hb = dp4a_us(w[r][4 + j] & 0xF0F0F0F0u, xb[4 + j], hb);
             }
             // Q4_0 values are code - 8: sum((q - 8) x) = dot - 8 sum(x)
             const int ca = la + (ha >> 4) - 8 * int(mt.y), cb = lb + (hb >> 4) - 8 * int(mt.w);
-            acc[rr][t] += da * mt.x * i2f_small(ca) + db * mt.z * i2f_small(cb);
+            acc[r][t] += sa[r] * mt.x * i2f_small(ca) + sb[r] * mt.z * i2f_small(cb);
           }
         }
       }
@@ -230,28 +253,28 @@ __global__ void __launch_bounds__(kQThreads)
     }
     // the four threads of a row hold its four page / block-pair partial sums
 #pragma unroll
-    for (int rr = 0; rr < kQRpt; ++rr)
+    for (int r = 0; r < kRpt; ++r)
 #pragma unroll
       for (int t = 0; t < TOKB; ++t) {
-        acc[rr][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[rr][t], 1);
-        acc[rr][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[rr][t], 2);
+        acc[r][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][t], 1);
+        acc[r][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[r][t], 2);
       }
     if (p.splits > 1) {
       if (pg == 0)
 #pragma unroll
-        for (int rr = 0; rr < kQRpt; ++rr)
+        for (int r = 0; r < kRpt; ++r)
 #pragma unroll
-          for (int t = 0; t < TOKB; ++t) red[t * kQRows + rs + kQRowStride * rr] = acc[rr][t];
+          for (int t = 0; t < TOKB; ++t) red[t * QR + rs + 64 * r] = acc[r][t];
     } else if (pg == 0) {
 #pragma unroll
-      for (int rr = 0; rr < kQRpt; ++rr) {
-        const int row = row0 + rs + kQRowStride * rr;
+      for (int r = 0; r < kRpt; ++r) {
+        const int row = row0 + rs + 64 * r;
         if (row >= p.n) continue;
 #pragma unroll
         for (int t = 0; t < TOKB; ++t) {
           if (t >= ntok) break;
           float* dst = p.y + int64_t(t) * p.n + row;
-          *dst = p.accumulate ? *dst + acc[rr][t] : acc[rr][t];
+          *dst = p.accumulate ? *dst + acc[r][t] : acc[r][t];
         }
       }
     }
@@ -260,8 +283,8 @@ __global__ void __launch_bounds__(kQThreads)
     // every CTA of the cluster reaches both barriers (no early exit above)
     cluster_sync();
     if (cluster_ctarank() == 0) {
-      for (int e = threadIdx.x; e < TOKB * kQRows; e += kQThreads) {
-        const int t = e / kQRows, r = e % kQRows, row = row0 + r;
+      for (int e = threadIdx.x; e < TOKB * QR; e += kQThreads) {
+        const int t = e / QR, r = e % QR, row = row0 + r;
         if (t >= p.ntok || row >= p.n) continue;
         float v = 0.f;
         for (int c = 0; c < p.splits; ++c) v += ld_dsmem_f32(red + e, uint32_t(c));
@@ -563,11 +586,12 @@ __global__ void __launch_bounds__(256) k_quant_q8(int rows, int k, const void* x
   }
 }
 
-template <int FMT, int TOKB>
+template <int FMT, int TOKB, int QR, int QS>
 int launch_q8(const CUtensorMap& wm, const CUtensorMap& xm, const CUtensorMap& mm, const Q8Args& a, int row_tiles,
               cudaStream_t s) {
-  constexpr int smem = kQStages * q8_stage_bytes<TOKB>() + 2 * kQStages * 8 + TOKB * kQRows * 4;
-  auto kern = k_mv_q8<FMT, TOKB>;
+  constexpr int smem = q8_smem_bytes<TOKB, QR, QS>();
+  static_assert(smem <= 227 * 1024, "chunked matvec CTA exceeds shared memory");
+  auto kern = k_mv_q8<FMT, TOKB, QR, QS>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -668,7 +692,8 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
   }
   const int tokb = tokens <= 1 ? 1 : 8;
   CUtensorMap wm;
-  int rc = make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, n, rb / 4, kChunkBytes / 4, kQRows,
+  const int qr = tokb == 1 ? kQRows1 : kQRows8;   // rows per tile (the weight box's height)
+  int rc = make_map(&wm, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, n, rb / 4, kChunkBytes / 4, qr,
                     CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != LK_OK) return rc;
   Q8Args a{};
@@ -676,9 +701,11 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
   a.k = k;
   a.accumulate = accumulate;
   a.nchunks = k / 256;
-  const int row_tiles = (n + kQRows - 1) / kQRows;
-  // split K until about one full wave of CTAs (6 per SM on 148 SMs), at most 8 CTAs per cluster
-  int splits = (888 + row_tiles - 1) / row_tiles;
+  const int row_tiles = (n + qr - 1) / qr;
+  // split K until about one full wave of CTAs (one token: 6 per SM on 148 SMs; 8 tokens: 2 per SM), at most 8 CTAs
+  // per cluster
+  const int wave = tokb == 1 ? 888 : 296;
+  int splits = (wave + row_tiles - 1) / row_tiles;
   splits = max(1, min(splits, min(8, a.nchunks)));
   a.cps = (a.nchunks + splits - 1) / splits;
   a.splits = (a.nchunks + a.cps - 1) / a.cps;
@@ -695,11 +722,11 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
     a.y = y + int64_t(t0) * n;
     a.ntok = nt;
     if (tokb == 1)
-      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 1>(wm, xm, mm, a, row_tiles, s)
-                          : launch_q8<LK_Q4_0, 1>(wm, xm, mm, a, row_tiles, s);
+      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 1, kQRows1, kQStages1>(wm, xm, mm, a, row_tiles, s)
+                          : launch_q8<LK_Q4_0, 1, kQRows1, kQStages1>(wm, xm, mm, a, row_tiles, s);
     else
-      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 8>(wm, xm, mm, a, row_tiles, s)
-                          : launch_q8<LK_Q4_0, 8>(wm, xm, mm, a, row_tiles, s);
+      rc = fmt == LK_Q4_K ? launch_q8<LK_Q4_K, 8, kQRows8, kQStages8>(wm, xm, mm, a, row_tiles, s)
+                          : launch_q8<LK_Q4_0, 8, kQRows8, kQStages8>(wm, xm, mm, a, row_tiles, s);
     if (rc != LK_OK) return rc;
   }
   return LK_OK;

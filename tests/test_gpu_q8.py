@@ -54,7 +54,7 @@ class TestMvQ8:
     @pytest.mark.parametrize("fmt", ["q4_0", "q4_k"])
     @pytest.mark.parametrize("n,k,tokens", [(256, 256, 1), (4096, 4096, 1), (1000, 2048, 3), (64, 12288, 8),
                                             (300, 1024, 13), (1024, 4096, 1), (130, 8192, 1), (96, 12288, 1),
-                                            (4099, 4096, 1)])
+                                            (4099, 4096, 1), (200, 4096, 40), (129, 2048, 16)])
     def test_vs_oracle(self, ops, fmt, n, k, tokens):
         rng = np.random.default_rng(n + k + tokens)
         w = QUANT[fmt]((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
