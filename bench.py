@@ -337,6 +337,17 @@ def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
     return out
 
 
+def moe_path(ops, torch, lg, E, ku, m, expert_bytes, ms, matvec_below=64):
+    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 64 tokens, gen_llm.py:6107; MXFP4: matvecs for at
+    most 8 assignments), and for the matvecs the weight GB/s over the experts the routing touches."""
+    if m >= matvec_below:
+        return {"path": "grouped GEMMs"}
+    ids, _ = ops.moe_route(lg, E, ku)
+    eu = int(torch.unique(ids).numel())
+    return {"path": "expert matvecs", "touched_experts": eu,
+            "weight_gbs": round(eu * expert_bytes / (ms * 1e-3) / 1e9, 1)}
+
+
 def bench_moe(args, torch, dev, time_steps, pk):
     """configs[2] (Q4_0 MoE, Qwen3-30B-A3B-like) and configs[3] (MXFP4 x e4m3 MoE, gpt-oss-20b-like): one MoE layer
     (route, schedule, expert GEMMs / matvecs, combine) per step as a CUDA graph; plus the dense MXFP4 x FP8 GEMM."""
@@ -355,7 +366,8 @@ def bench_moe(args, torch, dev, time_steps, pk):
         for _ in range(3):
             g.replay()
         ms = time_steps(g.replay, 20)
-        q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2)}
+        q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
+                     **moe_path(ops, torch, lg, E, ku, m, 3 * h * f * 18 // 32, ms)}
     out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
                              "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
     del w_gu, w_dn
@@ -370,7 +382,8 @@ def bench_moe(args, torch, dev, time_steps, pk):
         for _ in range(3):
             g.replay()
         ms = time_steps(g.replay, 20)
-        mx[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2)}
+        mx[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
+                      **moe_path(ops, torch, lg, E, ku, m, 3 * h * f // 2 + 3 * h * f // 32, ms, 8 // ku + 1)}
     # the dense kernel alone: fused gate/up shape, M=8192
     M = 8192
     x8, s8 = ops.row_scale_f8(torch.randn(M, h, device=dev, generator=gen))

@@ -190,6 +190,16 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                      lk_stream_t stream);
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream);
+/* lk_moe_expert_mv_mxfp4s: lk_moe_expert_mv over MXFP4S experts (the reference's expert_mv, gen_moe.py:535-727, with
+ * the split-plane MXFP4S format of gen_llm.py:844-895; the MoE counterpart of lk_moe_grouped_gemm_mxfp4s_f8 at decode
+ * sizes). w / ws: nibble plane [rows][k/2] and E8M0 plane [rows][k/32] of the stacked experts -- mode 0 (gu): per
+ * expert n gate rows then n up rows of k values, y[a] = silu(Wg x[a/ku]) * (Wu x[a/ku]); mode 1 (dn): per expert n
+ * rows, y[a] = Wd x[a]. order: LK_ORDER_PAIRS or LK_ORDER_SPLIT16. The activations (f32, f16 or bf16) are multiplied
+ * in f32 with the exact MXFP4 values, f32 accumulation. k % 32 == 0 and k <= 4096 (LK_EUNSUPPORTED beyond);
+ * assignments <= 65535 (LK_ERANGE beyond); x, w 16-byte aligned. */
+int lk_moe_expert_mv_mxfp4s(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
+                            const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
+                            float* y, lk_stream_t stream);
 
 /* lk_moe_ffn_decode_noalloc: the decode MoE layer in one call that allocates nothing. No counterpart in the
  * reference. It runs lk_moe_route (gating 1 over the given logits [tokens][n_experts] f32, renormalised when norm),

@@ -37,6 +37,7 @@ SIGNATURES = {
                                            _P]),
     "lk_moe_combine_sorted": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "lk_moe_expert_mv": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
+    "lk_moe_expert_mv_mxfp4s": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "lk_moe_combine": (_I, [_I, _I, _I, _I, _P, _P, _P, _P]),
     "lk_peer_alloc": (_I, [_L, ctypes.POINTER(_P), _P]),
     "lk_peer_open": (_I, [_P, ctypes.POINTER(_P)]),

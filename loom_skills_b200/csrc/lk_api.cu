@@ -141,6 +141,22 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
   return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
 }
 
+int lk_moe_expert_mv_mxfp4s(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
+                            const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
+                            float* y, lk_stream_t stream) {
+  if (mode != 0 && mode != 1) return LK_EINVAL;
+  if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
+  if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0 || k % 32) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (k > 4096) return LK_EUNSUPPORTED;
+  if (assignments > 65535) return LK_ERANGE;   // one grid row per assignment
+  if (assignments == 0) return LK_OK;
+  if (!ids || !x || !w || !ws || !y) return LK_EINVAL;
+  if (!aligned(w, 16) || !aligned(x, 16)) return LK_EALIGN;
+  return moe_expert_mv_mx(mode, order, n, k, assignments, ku, n_experts, ids, x, x_dtype, w, ws, y,
+                          (cudaStream_t)stream);
+}
+
 int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
                      const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
                      lk_stream_t stream) {

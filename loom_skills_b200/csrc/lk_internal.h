@@ -48,6 +48,9 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
 
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
+// decode expert matvecs over MXFP4S experts (lk_mvmx.cu)
+int moe_expert_mv_mx(int mode, int order, int n, int k, int assignments, int ku, int n_experts, const int32_t* ids,
+                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s);
 int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,

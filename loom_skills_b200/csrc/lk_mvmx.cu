@@ -1,0 +1,211 @@
+// Decode expert matvecs for MXFP4S experts: the reference's expert_mv (gen_moe.py:535-727) over the MXFP4S weight
+// format (split planes, gen_llm.py:844-895), f32 accumulation of f32 activations as its decode path does.
+//   mode 0 (gate/up; expert e holds f gate rows, then f up rows): act[a][j] = silu(g) * u,
+//          g = Wg[e][j] . x[a / ku], u = Wu[e][j] . x[a / ku]
+//   mode 1 (down; expert e holds h rows):                        y[a][j] = Wd[e][j] . x[a]
+// with e = ids[a] and W the exact MXFP4 values: e2m1 code * 2^(s - 127), s the row's E8M0 byte of the 32-value block.
+//
+// Design (HBM-bound at decode sizes). One CTA per (64 output rows, assignment); a warp computes 8 of the rows (a
+// gate/up pair counts as one). Lane l owns the 32-value blocks l + 32 i of every row (i < BPL = ceil(k / 1024)) and
+// holds those blocks' activations in registers as f32 for all its rows. Per block a lane loads the block's 16 nibble
+// bytes (consecutive lanes read consecutive 16-byte segments of the row) and its E8M0 byte, loads for two (gate/up)
+// or four (down) rows going out before any of their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign,
+// exponent and mantissa bits placed in the f16 sign, low exponent and top mantissa bits give value * 2^-14, e = 0
+// landing on the f16 subnormal 0.5 * 2^-14 -- then an f32 for an f32 FMA against the activation. The block's sum
+// takes its scale, and the row's warp-reduced total is multiplied by 2^14.
+#include "lk_common.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+namespace {
+
+constexpr int kMxMvWarps = 8;
+constexpr int kMxMvRowsPerWarp = 8;
+constexpr int kMxMvRowsPerCta = kMxMvWarps * kMxMvRowsPerWarp;
+
+struct MxMvArgs {
+  const uint8_t* w;     // nibble plane [n_experts * rows_per_expert][k / 2]
+  const uint8_t* ws;    // E8M0 plane [n_experts * rows_per_expert][k / 32]
+  const void* x;        // activations [tokens][k]
+  float* y;             // [assignments][n]
+  const int32_t* ids;   // expert of each assignment
+  int n, k, x_div, n_experts, rows_per_expert, x_dtype;
+};
+
+// f16 bit patterns of the 2 nibbles held in the low 4 bits of each 16-bit half of r: value * 2^-14, sign included
+LK_DEV uint32_t e2m1x2_f16(uint32_t r) { return ((r << 9) & 0x0E000E00u) | ((r << 12) & 0x80008000u); }
+
+LK_DEV float2 h2f2(uint32_t h) { return __half22float2(*reinterpret_cast<const __half2*>(&h)); }
+
+// E8M0 byte -> 2^(e - 127) (e = 0: 2^-127, a subnormal)
+LK_DEV float e8m0_scale(uint32_t e) { return e >= 1 ? __uint_as_float(e << 23) : __uint_as_float(0x00400000u); }
+
+// sum of the 32 products of one block (16 nibble bytes q against activations xb), times 2^-14
+template <int ORDER>
+LK_DEV float block_dot(const uint4 q, const float (&xb)[32]) {
+  const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {   // bytes 4i .. 4i + 3
+    const uint32_t lo4 = wv[i] & 0x0F0F0F0Fu, hi4 = (wv[i] >> 4) & 0x0F0F0F0Fu;
+    const float2 l01 = h2f2(e2m1x2_f16(prmt(lo4, 0u, 0x4140u))), l23 = h2f2(e2m1x2_f16(prmt(lo4, 0u, 0x4342u)));
+    const float2 h01 = h2f2(e2m1x2_f16(prmt(hi4, 0u, 0x4140u))), h23 = h2f2(e2m1x2_f16(prmt(hi4, 0u, 0x4342u)));
+    if (ORDER == LK_ORDER_PAIRS) {   // byte b: element 2b (low nibble), 2b + 1 (high)
+      const int v = 8 * i;
+      s0 = fmaf(l01.x, xb[v], s0);
+      s1 = fmaf(h01.x, xb[v + 1], s1);
+      s0 = fmaf(l01.y, xb[v + 2], s0);
+      s1 = fmaf(h01.y, xb[v + 3], s1);
+      s0 = fmaf(l23.x, xb[v + 4], s0);
+      s1 = fmaf(h23.x, xb[v + 5], s1);
+      s0 = fmaf(l23.y, xb[v + 6], s0);
+      s1 = fmaf(h23.y, xb[v + 7], s1);
+    } else {   // split16 (ggml): byte b: element b (low nibble), b + 16 (high)
+      const int v = 4 * i;
+      s0 = fmaf(l01.x, xb[v], s0);
+      s0 = fmaf(l01.y, xb[v + 1], s0);
+      s0 = fmaf(l23.x, xb[v + 2], s0);
+      s0 = fmaf(l23.y, xb[v + 3], s0);
+      s1 = fmaf(h01.x, xb[v + 16], s1);
+      s1 = fmaf(h01.y, xb[v + 17], s1);
+      s1 = fmaf(h23.x, xb[v + 18], s1);
+      s1 = fmaf(h23.y, xb[v + 19], s1);
+    }
+  }
+  return s0 + s1;
+}
+
+LK_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// RB output rows per load batch: the rows' blocks are all requested before any is used
+template <int MODE, int ORDER, int BPL>
+__global__ void __launch_bounds__(kMxMvWarps * 32) k_moe_mv_mx(const MxMvArgs p) {
+  constexpr int RB = MODE == 0 ? 2 : 4;   // output rows per batch (gate/up: two weight rows each)
+  constexpr int NW = MODE == 0 ? 2 : 1;   // weight rows per output row
+  const int a = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.k / 32;
+  const int e = min(max(p.ids[a], 0), p.n_experts - 1);
+  const int tok = a / p.x_div;
+
+  // this lane's blocks of the activation row, f32 (blocks past the row: zero, never used)
+  float xr[BPL][32];
+#pragma unroll
+  for (int i = 0; i < BPL; ++i) {
+    const int b = lane + 32 * i;
+#pragma unroll
+    for (int v = 0; v < 32; ++v) xr[i][v] = 0.f;
+    if (b >= nb) continue;
+    const int64_t off = int64_t(tok) * p.k + int64_t(b) * 32;
+    if (p.x_dtype == LK_F32) {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + off);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float4 f = __ldg(src + c);
+        xr[i][4 * c] = f.x;
+        xr[i][4 * c + 1] = f.y;
+        xr[i][4 * c + 2] = f.z;
+        xr[i][4 * c + 3] = f.w;
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + off);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 u = __ldg(src + c);
+        const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int hh = 0; hh < 4; ++hh) {
+          if (p.x_dtype == LK_BF16) {
+            xr[i][8 * c + 2 * hh] = __uint_as_float(wv[hh] << 16);
+            xr[i][8 * c + 2 * hh + 1] = __uint_as_float(wv[hh] & 0xffff0000u);
+          } else {
+            const float2 f = h2f2(wv[hh]);
+            xr[i][8 * c + 2 * hh] = f.x;
+            xr[i][8 * c + 2 * hh + 1] = f.y;
+          }
+        }
+      }
+    }
+  }
+
+  const int64_t rb = p.k / 2;   // nibble bytes per row
+  const int j0 = blockIdx.x * kMxMvRowsPerCta + warp * kMxMvRowsPerWarp;
+#pragma unroll 1
+  for (int r0 = 0; r0 < kMxMvRowsPerWarp; r0 += RB) {
+    uint4 q[RB][NW][BPL];
+    uint32_t sc[RB][NW][BPL];
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+      for (int wi = 0; wi < NW; ++wi)
+#pragma unroll
+        for (int i = 0; i < BPL; ++i) {
+          const int j = j0 + r0 + r, b = lane + 32 * i;
+          q[r][wi][i] = make_uint4(0u, 0u, 0u, 0u);
+          sc[r][wi][i] = 127u;
+          if (j < p.n && b < nb) {
+            const int64_t row = int64_t(e) * p.rows_per_expert + j + (wi ? p.n : 0);
+            q[r][wi][i] = __ldg(reinterpret_cast<const uint4*>(p.w + row * rb) + b);
+            sc[r][wi][i] = __ldg(p.ws + row * nb + b);
+          }
+        }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      float acc[NW];
+#pragma unroll
+      for (int wi = 0; wi < NW; ++wi) {
+        acc[wi] = 0.f;
+#pragma unroll
+        for (int i = 0; i < BPL; ++i)
+          if (lane + 32 * i < nb)
+            acc[wi] = fmaf(block_dot<ORDER>(q[r][wi][i], xr[i]), e8m0_scale(sc[r][wi][i]), acc[wi]);
+        acc[wi] = warp_sum(acc[wi]) * 16384.0f;
+      }
+      const int j = j0 + r0 + r;
+      if (lane == 0 && j < p.n) p.y[int64_t(a) * p.n + j] = MODE == 0 ? silu(acc[0]) * acc[NW - 1] : acc[0];
+    }
+  }
+}
+
+template <int MODE, int ORDER>
+int launch_mx_mv(const MxMvArgs& a, int assignments, cudaStream_t s) {
+  const dim3 grid((a.n + kMxMvRowsPerCta - 1) / kMxMvRowsPerCta, assignments);
+  const int bpl = (a.k / 32 + 31) / 32;
+  switch (bpl) {
+    case 1: k_moe_mv_mx<MODE, ORDER, 1><<<grid, kMxMvWarps * 32, 0, s>>>(a); break;
+    case 2: k_moe_mv_mx<MODE, ORDER, 2><<<grid, kMxMvWarps * 32, 0, s>>>(a); break;
+    case 3: k_moe_mv_mx<MODE, ORDER, 3><<<grid, kMxMvWarps * 32, 0, s>>>(a); break;
+    case 4: k_moe_mv_mx<MODE, ORDER, 4><<<grid, kMxMvWarps * 32, 0, s>>>(a); break;
+    default: return LK_EUNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+}  // namespace
+
+int moe_expert_mv_mx(int mode, int order, int n, int k, int assignments, int ku, int n_experts, const int32_t* ids,
+                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s) {
+  MxMvArgs a{};
+  a.w = w;
+  a.ws = ws;
+  a.x = x;
+  a.y = y;
+  a.ids = ids;
+  a.n = n;
+  a.k = k;
+  a.x_div = mode == 0 ? ku : 1;
+  a.n_experts = n_experts;
+  a.rows_per_expert = mode == 0 ? 2 * n : n;
+  a.x_dtype = x_dtype;
+  if (mode == 0)
+    return order == LK_ORDER_PAIRS ? launch_mx_mv<0, LK_ORDER_PAIRS>(a, assignments, s)
+                                   : launch_mx_mv<0, LK_ORDER_SPLIT16>(a, assignments, s);
+  return order == LK_ORDER_PAIRS ? launch_mx_mv<1, LK_ORDER_PAIRS>(a, assignments, s)
+                                 : launch_mx_mv<1, LK_ORDER_SPLIT16>(a, assignments, s);
+}
+
+}  // namespace lk

@@ -238,6 +238,20 @@ def moe_expert_mv(fmt, mode, ids, x, w, n, k, ku, n_experts, fused=True, w2=None
     return y
 
 
+def moe_expert_mv_mxfp4s(mode, ids, x, w, ws, n, k, ku, n_experts, order=L.ORDER_PAIRS, y=None):
+    """Decode expert matvecs over MXFP4S experts per assignment: mode 'gu' (per expert n gate rows then n up rows)
+    -> silu(Wg x) * (Wu x); 'dn' -> Wd x. w / ws: the stacked nibble and E8M0 planes."""
+    _cuda(ids, x, w, ws, y)
+    a = ids.numel()
+    if y is None:
+        y = torch.empty(a, n, dtype=torch.float32, device=x.device)
+    md = 0 if mode == "gu" else 1
+    L.check(L.load().lk_moe_expert_mv_mxfp4s(md, int(order), n, k, a, ku, n_experts, _ptr(ids), _ptr(x.contiguous()),
+                                             _DT[x.dtype], _ptr(w), _ptr(ws), _ptr(y), _stream()),
+            "lk_moe_expert_mv_mxfp4s")
+    return y
+
+
 def moe_combine(ys, wts, y=None, accumulate=False):
     _cuda(ys, wts, y)
     tokens, ku = wts.shape
@@ -271,12 +285,24 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     return moe_combine_sorted(ys, pos, wts)
 
 
-def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, norm=True, order=L.ORDER_PAIRS):
-    """The routed expert FFN of one MoE layer with MXFP4 experts and e4m3 activations (gpt-oss-like; the fp8 fusion of
-    gen_mxfp4s.py:969-1110 applied to gen_llm.py:5324-5386): route -> bucket -> e4m3 row scale -> grouped gate/up
-    (SwiGLU) -> e4m3 row scale -> grouped down -> weighted combine. w_gu / ws_gu: per expert 2f rows (gate then up)
-    of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per expert h rows of f/2 / f/32 bytes."""
+def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, norm=True, order=L.ORDER_PAIRS,
+                   prefill=None):
+    """The routed expert FFN of one MoE layer with MXFP4 experts (gpt-oss-like; gen_llm.py:5324-5386 wiring): the fp8
+    fusion of gen_mxfp4s.py:969-1110 -- route -> bucket -> e4m3 row scale -> grouped gate/up (SwiGLU) -> e4m3 row
+    scale -> grouped down -> weighted combine -- or, for at most 8 assignments, per-assignment expert matvecs on the
+    unquantised activations (gen_moe.py:535-727). The reference switches at 64 tokens (gen_llm.py:6107); here the
+    matvecs stream each assignment's expert on its own, which measured faster only for a handful of assignments
+    (gpt-oss shapes: 4 assignments 72 against 83 us, 128 assignments 1155 against 265 us). `prefill` forces either
+    path. w_gu / ws_gu: per expert 2f rows (gate then up) of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per
+    expert h rows of f/2 / f/32 bytes."""
+    tokens = x.shape[0]
     ids, wts = moe_route(logits, n_experts, ku, norm=norm)
+    if prefill is None:
+        prefill = tokens * ku > 8
+    if not prefill:
+        act = moe_expert_mv_mxfp4s("gu", ids.reshape(-1), x, w_gu, ws_gu, f, h, ku, n_experts, order=order)
+        ys = moe_expert_mv_mxfp4s("dn", ids.reshape(-1), act, w_dn, ws_dn, h, f, ku, n_experts, order=order)
+        return moe_combine(ys, wts)
     ti, rm, pos = moe_bucket(ids, n_experts)
     x8, s8 = moe_row_scale_gather(x, rm, ku, f8=True)
     act = moe_grouped_gemm_mxfp4s_f8("swiglu_sorted", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True,

@@ -528,6 +528,24 @@ def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts):
     return y
 
 
+def moe_ffn_mxfp4_decode_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs"):
+    """The routed expert FFN with MXFP4 experts at decode sizes (gen_llm.py:5324-5386 wiring below the GEMM threshold
+    of gen_llm.py:6107, the expert matvecs of gen_moe.py:535-727): per assignment act = silu(Wg x) * (Wu x) and
+    ys = Wd act with the exact MXFP4 weights and unquantised activations, y[t] = sum_k wts[t,k] ys[t,k]."""
+    t, ku = ids.shape
+    E = nib_dn.shape[0] // h
+    Wgu = dequant_mxfp4_planar(nib_gu, sc_gu, nib_gu.shape[0], h, order).reshape(E, 2 * f, h)
+    Wdn = dequant_mxfp4_planar(nib_dn, sc_dn, nib_dn.shape[0], f, order).reshape(E, h, f)
+    y = np.zeros((t, h), np.float64)
+    for i in range(t):
+        for j in range(ku):
+            e = ids[i, j]
+            v = Wgu[e] @ np.asarray(x[i], np.float64)
+            act = silu(v[:f]) * v[f:]
+            y[i] += float(wts[i, j]) * (Wdn[e] @ act)
+    return y
+
+
 def moe_ffn_mxfp4_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs"):
     """The routed expert FFN with MXFP4 experts on the fp8 path (gen_llm.py:5324-5386 wiring with the e4m3 producer
     and fp8 GEMMs of gen_mxfp4s.py:969-1110): x8 = row_scale_f8(x); act = silu(g) * u from the fp8 gate/up GEMM;

@@ -140,7 +140,7 @@ class TestGroupedMxfp4:
             assert O.rel_l2(hys[sel], ref) < TOL_SAME, (ex, O.rel_l2(hys[sel], ref))
         assert ops.L.load().lk_device_status(1) == 0
 
-    @pytest.mark.parametrize("tokens", [1, 40, 300])
+    @pytest.mark.parametrize("tokens", [1, 2, 40, 300])
     def test_moe_ffn_end_to_end(self, ops, tokens):
         E, ku, h, f = 8, 4, 576, 320
         rng = np.random.default_rng(41)
@@ -150,6 +150,74 @@ class TestGroupedMxfp4:
         logits = rng.standard_normal((tokens, E)).astype(np.float32)
         y = host(ops.moe_ffn_mxfp4s(dev(x), dev(logits), dev(gu), dev(gus), dev(dn), dev(dns), h, f, E, ku))
         ids, wts = O.route_ref(logits, ku)
+        if tokens * ku > 8:   # the fp8 GEMM path
+            ref = O.moe_ffn_mxfp4_ref(x, ids, wts, gu, gus, dn, dns, h, f)
+            assert O.rel_l2(y, ref) < TOL_F8, O.rel_l2(y, ref)
+        else:              # expert matvecs on the unquantised activations, f32 accumulation
+            ref = O.moe_ffn_mxfp4_decode_ref(x, ids, wts, gu, gus, dn, dns, h, f)
+            assert O.rel_l2(y, ref) < 1e-3, O.rel_l2(y, ref)
+        assert ops.L.load().lk_device_status(1) == 0
+
+    def test_moe_ffn_prefill_path_at_decode_sizes(self, ops):
+        # the fp8 GEMM pipeline stays selectable for a few assignments (prefill=True)
+        E, ku, h, f, tokens = 8, 4, 576, 320, 2
+        rng = np.random.default_rng(44)
+        _, gu, gus = mx_weights(E * 2 * f, h, 45)
+        _, dn, dns = mx_weights(E * h, f, 46)
+        x = rng.standard_normal((tokens, h)).astype(np.float32)
+        logits = rng.standard_normal((tokens, E)).astype(np.float32)
+        y = host(ops.moe_ffn_mxfp4s(dev(x), dev(logits), dev(gu), dev(gus), dev(dn), dev(dns), h, f, E, ku,
+                                    prefill=True))
+        ids, wts = O.route_ref(logits, ku)
         ref = O.moe_ffn_mxfp4_ref(x, ids, wts, gu, gus, dn, dns, h, f)
         assert O.rel_l2(y, ref) < TOL_F8, O.rel_l2(y, ref)
-        assert ops.L.load().lk_device_status(1) == 0
+
+
+class TestExpertMvMxfp4:
+    """Decode expert matvecs over MXFP4S experts (gen_moe.py:535-727 expert_mv with the MXFP4S format): f32
+    accumulation of the activations against the exact MXFP4 values, so against the float64 product the bar is the
+    f32 one (relative L2 <= 1e-4 here; the path's tolerance is 1e-3)."""
+
+    @pytest.mark.parametrize("k", [2880, 64, 1024, 4096, 2080])
+    @pytest.mark.parametrize("order", ["pairs", "split16"])
+    @pytest.mark.parametrize("xdt", ["f32", "bf16"])
+    def test_gate_up_and_down(self, ops, k, order, xdt):
+        rng = np.random.default_rng(k + (order == "pairs") + 3 * (xdt == "bf16"))
+        E, ku, tokens, f = 5, 2, 3, 200
+        a = tokens * ku
+        _, nib, sc = mx_weights(E * 2 * f, k, 81)
+        ids = rng.integers(0, E, a).astype(np.int32)
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        xt = dev(x) if xdt == "f32" else dev(x).to(torch.bfloat16)
+        xs = host(xt.float())
+        od = ops.L.ORDER_PAIRS if order == "pairs" else ops.L.ORDER_SPLIT16
+        nb = nib if order == "pairs" else to_split16(nib)
+        act = host(ops.moe_expert_mv_mxfp4s("gu", dev(ids), xt, dev(nb), dev(sc), f, k, ku, E, order=od))
+        W = O.dequant_mxfp4_planar(nib, sc, E * 2 * f, k).reshape(E, 2 * f, k)
+        ref = np.empty((a, f))
+        for i in range(a):
+            v = W[ids[i]] @ xs[i // ku].astype(np.float64)
+            g, u = v[:f], v[f:]
+            ref[i] = g / (1.0 + np.exp(-g)) * u
+        assert O.rel_l2(act, ref) < 1e-4, O.rel_l2(act, ref)
+        # down: one activation row per assignment against per-expert h x 256 weights
+        h, kd = 72, 256
+        _, nd, sd = mx_weights(E * h, kd, 83)
+        xd = rng.standard_normal((a, kd)).astype(np.float32)
+        nbd = nd if order == "pairs" else to_split16(nd)
+        y = host(ops.moe_expert_mv_mxfp4s("dn", dev(ids), dev(xd), dev(nbd), dev(sd), h, kd, ku, E, order=od))
+        Wd = O.dequant_mxfp4_planar(nd, sd, E * h, kd).reshape(E, h, kd)
+        refd = np.stack([Wd[ids[i]] @ xd[i].astype(np.float64) for i in range(a)])
+        assert O.rel_l2(y, refd) < 1e-4, O.rel_l2(y, refd)
+        assert ops.device_status() == 0
+
+    def test_contract(self, ops):
+        ids = torch.zeros(2, dtype=torch.int32, device="cuda")
+        x = torch.zeros(1, 4128, device="cuda")
+        w = torch.zeros(4, 4128 // 2, dtype=torch.uint8, device="cuda")
+        ws = torch.zeros(4, 4128 // 32, dtype=torch.uint8, device="cuda")
+        with pytest.raises(ops.L.LkError):   # k > 4096
+            ops.moe_expert_mv_mxfp4s("gu", ids, x, w, ws, 2, 4128, 2, 1)
+        with pytest.raises(ops.L.LkError):   # k % 32
+            ops.moe_expert_mv_mxfp4s("dn", ids, x[:, :48], w, ws, 2, 48, 1, 1)
+        assert ops.moe_expert_mv_mxfp4s("dn", ids[:0], x, w, ws, 4, 64, 1, 1).shape == (0, 4)
