@@ -6,8 +6,10 @@
 // with e = ids[a] and W the exact MXFP4 values: e2m1 code * 2^(s - 127), s the row's E8M0 byte of the 32-value block.
 //
 // Design (HBM-bound at decode sizes). One CTA per (64 output rows, assignment); a warp computes 8 of the rows (a
-// gate/up pair counts as one). Lane l owns the 32-value blocks l + 32 i of every row (i < BPL = ceil(k / 1024)) and
-// holds those blocks' activations in registers as f32 for all its rows. Per block a lane loads the block's 16 nibble
+// gate/up pair counts as one). The CTA stages the assignment's activation row in shared memory as f32 once, each
+// 128-byte block in 16-byte granules swizzled by the block index (granule q of block b at q ^ (b % 8)), so the lanes
+// of a warp, which read the same granule of 32 consecutive blocks, spread over eight bank groups. Lane l owns the
+// 32-value blocks l + 32 i of every row (i < BPL = ceil(k / 1024)). Per block a lane loads the block's 16 nibble
 // bytes (consecutive lanes read consecutive 16-byte segments of the row) and its E8M0 byte, loads for two (gate/up)
 // or four (down) rows going out before any of their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign,
 // exponent and mantissa bits placed in the f16 sign, low exponent and top mantissa bits give value * 2^-14, e = 0
@@ -40,9 +42,12 @@ LK_DEV float2 h2f2(uint32_t h) { return __half22float2(*reinterpret_cast<const _
 // E8M0 byte -> 2^(e - 127) (e = 0: 2^-127, a subnormal)
 LK_DEV float e8m0_scale(uint32_t e) { return e >= 1 ? __uint_as_float(e << 23) : __uint_as_float(0x00400000u); }
 
-// sum of the 32 products of one block (16 nibble bytes q against activations xb), times 2^-14
+// granule g (values 4g .. 4g + 3) of the staged activation block whose 16-byte granules start at xb, key = b % 8
+LK_DEV float4 xgran(const float4* xb, int key, int g) { return xb[g ^ key]; }
+
+// sum of the 32 products of one block (16 nibble bytes q against the staged activations), times 2^-14
 template <int ORDER>
-LK_DEV float block_dot(const uint4 q, const float (&xb)[32]) {
+LK_DEV float block_dot(const uint4 q, const float4* xb, int key) {
   const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -50,26 +55,26 @@ LK_DEV float block_dot(const uint4 q, const float (&xb)[32]) {
     const uint32_t lo4 = wv[i] & 0x0F0F0F0Fu, hi4 = (wv[i] >> 4) & 0x0F0F0F0Fu;
     const float2 l01 = h2f2(e2m1x2_f16(prmt(lo4, 0u, 0x4140u))), l23 = h2f2(e2m1x2_f16(prmt(lo4, 0u, 0x4342u)));
     const float2 h01 = h2f2(e2m1x2_f16(prmt(hi4, 0u, 0x4140u))), h23 = h2f2(e2m1x2_f16(prmt(hi4, 0u, 0x4342u)));
-    if (ORDER == LK_ORDER_PAIRS) {   // byte b: element 2b (low nibble), 2b + 1 (high)
-      const int v = 8 * i;
-      s0 = fmaf(l01.x, xb[v], s0);
-      s1 = fmaf(h01.x, xb[v + 1], s1);
-      s0 = fmaf(l01.y, xb[v + 2], s0);
-      s1 = fmaf(h01.y, xb[v + 3], s1);
-      s0 = fmaf(l23.x, xb[v + 4], s0);
-      s1 = fmaf(h23.x, xb[v + 5], s1);
-      s0 = fmaf(l23.y, xb[v + 6], s0);
-      s1 = fmaf(h23.y, xb[v + 7], s1);
-    } else {   // split16 (ggml): byte b: element b (low nibble), b + 16 (high)
-      const int v = 4 * i;
-      s0 = fmaf(l01.x, xb[v], s0);
-      s0 = fmaf(l01.y, xb[v + 1], s0);
-      s0 = fmaf(l23.x, xb[v + 2], s0);
-      s0 = fmaf(l23.y, xb[v + 3], s0);
-      s1 = fmaf(h01.x, xb[v + 16], s1);
-      s1 = fmaf(h01.y, xb[v + 17], s1);
-      s1 = fmaf(h23.x, xb[v + 18], s1);
-      s1 = fmaf(h23.y, xb[v + 19], s1);
+    if (ORDER == LK_ORDER_PAIRS) {   // byte b: element 2b (low nibble), 2b + 1 (high): values 8i .. 8i + 7
+      const float4 xa = xgran(xb, key, 2 * i), xc = xgran(xb, key, 2 * i + 1);
+      s0 = fmaf(l01.x, xa.x, s0);
+      s1 = fmaf(h01.x, xa.y, s1);
+      s0 = fmaf(l01.y, xa.z, s0);
+      s1 = fmaf(h01.y, xa.w, s1);
+      s0 = fmaf(l23.x, xc.x, s0);
+      s1 = fmaf(h23.x, xc.y, s1);
+      s0 = fmaf(l23.y, xc.z, s0);
+      s1 = fmaf(h23.y, xc.w, s1);
+    } else {   // split16 (ggml): byte b: element b (low nibble), b + 16 (high): values 4i .. 4i + 3, 16 + 4i ..
+      const float4 xa = xgran(xb, key, i), xc = xgran(xb, key, 4 + i);
+      s0 = fmaf(l01.x, xa.x, s0);
+      s0 = fmaf(l01.y, xa.y, s0);
+      s0 = fmaf(l23.x, xa.z, s0);
+      s0 = fmaf(l23.y, xa.w, s0);
+      s1 = fmaf(h01.x, xc.x, s1);
+      s1 = fmaf(h01.y, xc.y, s1);
+      s1 = fmaf(h23.x, xc.z, s1);
+      s1 = fmaf(h23.y, xc.w, s1);
     }
   }
   return s0 + s1;
@@ -83,7 +88,7 @@ LK_DEV float warp_sum(float v) {
 
 // RB output rows per load batch: the rows' blocks are all requested before any is used
 template <int MODE, int ORDER, int BPL>
-__global__ void __launch_bounds__(kMxMvWarps * 32) k_moe_mv_mx(const MxMvArgs p) {
+__global__ void __launch_bounds__(kMxMvWarps * 32, 2) k_moe_mv_mx(const MxMvArgs p) {
   constexpr int RB = MODE == 0 ? 2 : 4;   // output rows per batch (gate/up: two weight rows each)
   constexpr int NW = MODE == 0 ? 2 : 1;   // weight rows per output row
   const int a = blockIdx.y;
@@ -92,45 +97,27 @@ __global__ void __launch_bounds__(kMxMvWarps * 32) k_moe_mv_mx(const MxMvArgs p)
   const int e = min(max(p.ids[a], 0), p.n_experts - 1);
   const int tok = a / p.x_div;
 
-  // this lane's blocks of the activation row, f32 (blocks past the row: zero, never used)
-  float xr[BPL][32];
-#pragma unroll
-  for (int i = 0; i < BPL; ++i) {
-    const int b = lane + 32 * i;
-#pragma unroll
-    for (int v = 0; v < 32; ++v) xr[i][v] = 0.f;
-    if (b >= nb) continue;
-    const int64_t off = int64_t(tok) * p.k + int64_t(b) * 32;
+  // the activation row as f32 in shared memory: granule g of block b (values 32b + 4g ..) at 16 (8b + (g ^ b % 8))
+  __shared__ float4 xs[4096 / 4];
+  for (int gi = threadIdx.x; gi < nb * 8; gi += kMxMvWarps * 32) {
+    const int b = gi >> 3, g = gi & 7;
+    const int64_t off = int64_t(tok) * p.k + 4 * int64_t(gi);
+    float4 f;
     if (p.x_dtype == LK_F32) {
-      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + off);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const float4 f = __ldg(src + c);
-        xr[i][4 * c] = f.x;
-        xr[i][4 * c + 1] = f.y;
-        xr[i][4 * c + 2] = f.z;
-        xr[i][4 * c + 3] = f.w;
-      }
+      f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + off));
     } else {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + off);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 u = __ldg(src + c);
-        const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int hh = 0; hh < 4; ++hh) {
-          if (p.x_dtype == LK_BF16) {
-            xr[i][8 * c + 2 * hh] = __uint_as_float(wv[hh] << 16);
-            xr[i][8 * c + 2 * hh + 1] = __uint_as_float(wv[hh] & 0xffff0000u);
-          } else {
-            const float2 f = h2f2(wv[hh]);
-            xr[i][8 * c + 2 * hh] = f.x;
-            xr[i][8 * c + 2 * hh + 1] = f.y;
-          }
-        }
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.x) + off));
+      if (p.x_dtype == LK_BF16) {
+        f = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                        __uint_as_float(u.y & 0xffff0000u));
+      } else {
+        const float2 f0 = h2f2(u.x), f1 = h2f2(u.y);
+        f = make_float4(f0.x, f0.y, f1.x, f1.y);
       }
     }
+    xs[8 * b + (g ^ (b & 7))] = f;
   }
+  __syncthreads();
 
   const int64_t rb = p.k / 2;   // nibble bytes per row
   const int j0 = blockIdx.x * kMxMvRowsPerCta + warp * kMxMvRowsPerWarp;
@@ -161,8 +148,10 @@ __global__ void __launch_bounds__(kMxMvWarps * 32) k_moe_mv_mx(const MxMvArgs p)
         acc[wi] = 0.f;
 #pragma unroll
         for (int i = 0; i < BPL; ++i)
-          if (lane + 32 * i < nb)
-            acc[wi] = fmaf(block_dot<ORDER>(q[r][wi][i], xr[i]), e8m0_scale(sc[r][wi][i]), acc[wi]);
+          if (lane + 32 * i < nb) {
+            const int b = lane + 32 * i;
+            acc[wi] = fmaf(block_dot<ORDER>(q[r][wi][i], xs + 8 * b, b & 7), e8m0_scale(sc[r][wi][i]), acc[wi]);
+          }
         acc[wi] = warp_sum(acc[wi]) * 16384.0f;
       }
       const int j = j0 + r0 + r;
