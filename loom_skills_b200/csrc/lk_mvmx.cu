@@ -5,13 +5,14 @@
 //   mode 1 (down; expert e holds h rows):                        y[a][j] = Wd[e][j] . x[a]
 // with e = ids[a] and W the exact MXFP4 values: e2m1 code * 2^(s - 127), s the row's E8M0 byte of the 32-value block.
 //
-// Design (HBM-bound at decode sizes). One CTA per (64 output rows, assignment); a warp computes 8 of the rows (a
-// gate/up pair counts as one). The CTA stages the assignment's activation row in shared memory as f32 once, each
+// Design (HBM-bound at decode sizes). One CTA per (16 output rows, assignment); a warp computes 2 of the rows (a
+// gate/up pair counts as one) -- measured at one token of gpt-oss shapes: 8 rows per warp 56 us per MoE layer, 4 rows
+// 50 us, 2 rows 45 us (more CTAs in flight; the activation staging is cheap). The CTA stages the assignment's activation row in shared memory as f32 once, each
 // 128-byte block in 16-byte granules swizzled by the block index (granule q of block b at q ^ (b % 8)), so the lanes
 // of a warp, which read the same granule of 32 consecutive blocks, spread over eight bank groups. Lane l owns the
 // 32-value blocks l + 32 i of every row (i < BPL = ceil(k / 1024)). Per block a lane loads the block's 16 nibble
-// bytes (consecutive lanes read consecutive 16-byte segments of the row) and its E8M0 byte, loads for two (gate/up)
-// or four (down) rows going out before any of their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign,
+// bytes (consecutive lanes read consecutive 16-byte segments of the row) and its E8M0 byte, the loads of the warp's
+// rows going out before any of their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign,
 // exponent and mantissa bits placed in the f16 sign, low exponent and top mantissa bits give value * 2^-14, e = 0
 // landing on the f16 subnormal 0.5 * 2^-14 -- then an f32 for an f32 FMA against the activation. The block's sum
 // takes its scale, and the row's warp-reduced total is multiplied by 2^14.
@@ -22,7 +23,7 @@ namespace lk {
 namespace {
 
 constexpr int kMxMvWarps = 8;
-constexpr int kMxMvRowsPerWarp = 8;
+constexpr int kMxMvRowsPerWarp = 2;
 constexpr int kMxMvRowsPerCta = kMxMvWarps * kMxMvRowsPerWarp;
 
 struct MxMvArgs {
@@ -89,7 +90,7 @@ LK_DEV float warp_sum(float v) {
 // RB output rows per load batch: the rows' blocks are all requested before any is used
 template <int MODE, int ORDER, int BPL>
 __global__ void __launch_bounds__(kMxMvWarps * 32, 2) k_moe_mv_mx(const MxMvArgs p) {
-  constexpr int RB = MODE == 0 ? 2 : 4;   // output rows per batch (gate/up: two weight rows each)
+  constexpr int RB = MODE == 0 ? 2 : (kMxMvRowsPerWarp < 4 ? kMxMvRowsPerWarp : 4);   // output rows per batch
   constexpr int NW = MODE == 0 ? 2 : 1;   // weight rows per output row
   const int a = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

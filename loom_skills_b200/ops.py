@@ -292,8 +292,8 @@ def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, nor
     scale -> grouped down -> weighted combine -- or, for at most 8 assignments, per-assignment expert matvecs on the
     unquantised activations (gen_moe.py:535-727). The reference switches at 64 tokens (gen_llm.py:6107); here the
     matvecs stream each assignment's expert on its own, which measured faster only for a handful of assignments
-    (gpt-oss shapes: 4 assignments 56 against 83 us, 128 assignments 1155 against 265 us, before the activations
-    moved to shared memory). `prefill` forces either
+    (gpt-oss shapes: 4 assignments 45 against 83 us; 128 assignments took 1155 against 265 us in the kernel's
+    first form). `prefill` forces either
     path. w_gu / ws_gu: per expert 2f rows (gate then up) of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per
     expert h rows of f/2 / f/32 bytes."""
     tokens = x.shape[0]
