@@ -658,7 +658,8 @@ def run_profile_case(args):
     """A few launches of one hot kernel at one bench shape, for ncu captures (profiles/): warm-up launches, then
     `--steps` profiled ones. Cases: mv_gate_up (Q4_K q8 matvec, K=4096 N=24576), mv_down (K=12288 N=4096),
     mv8_gate_up (the gate_up matvec on 8 tokens), gemm_gate_up (Q4_K GEMM, M=2048 K=4096 N=24576), gemm64_down
-    (Q4_K GEMM, M=64 K=12288 N=4096), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880)."""
+    (Q4_K GEMM, M=64 K=12288 N=4096), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880), mxmv_gate_up (the
+    MXFP4S expert matvecs of one gpt-oss token: 4 assignments of 32 experts, h = f = 2880, bf16 x)."""
     import torch
 
     from loom_skills_b200 import ops
@@ -687,6 +688,15 @@ def run_profile_case(args):
         x8, s8 = ops.row_scale_f8(torch.randn(m, k, device=dev))
         y = torch.empty(m, n, device=dev)
         fn = lambda: ops.gemm_mxfp4s_f8("swiglu", x8, s8, g, gs, n, w2=u, w2s=us, y=y)   # noqa: E731
+    elif case == "mxmv_gate_up":
+        E, ku, h, f = 32, 4, 2880, 2880
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        gu, gus = synth_mxfp4(torch, dev, E * 2 * f, h, gen)
+        x = torch.randn(1, h, device=dev).to(torch.bfloat16)
+        ids = torch.tensor([3, 11, 17, 29], dtype=torch.int32, device=dev)
+        y = torch.empty(ku, f, device=dev)
+        fn = lambda: ops.moe_expert_mv_mxfp4s("gu", ids, x, gu, gus, f, h, ku, E, y=y)   # noqa: E731
     else:
         raise SystemExit(f"unknown --profile-case {case}")
     for _ in range(args.warmup + args.steps):
