@@ -338,8 +338,8 @@ def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
 
 
 def moe_path(ops, torch, lg, E, ku, m, expert_bytes, ms, matvec_below=64):
-    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 64 tokens, gen_llm.py:6107; MXFP4: matvecs for at
-    most 8 assignments), and for the matvecs the weight GB/s over the experts the routing touches."""
+    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 192 assignments; MXFP4: matvecs for at most 8
+    assignments), and for the matvecs the weight GB/s over the experts the routing touches."""
     if m >= matvec_below:
         return {"path": "grouped GEMMs"}
     ids, _ = ops.moe_route(lg, E, ku)
@@ -367,7 +367,7 @@ def bench_moe(args, torch, dev, time_steps, pk):
             g.replay()
         ms = time_steps(g.replay, 20)
         q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
-                     **moe_path(ops, torch, lg, E, ku, m, 3 * h * f * 18 // 32, ms)}
+                     **moe_path(ops, torch, lg, E, ku, m, 3 * h * f * 18 // 32, ms, 192 // ku)}
     out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
                              "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
     del w_gu, w_dn

@@ -267,11 +267,13 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route -> bucket -> grouped gate/up
     (SwiGLU) -> row scale -> grouped down -> weighted combine (prefill), or per-assignment expert matvecs (decode).
     x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values;
-    w_dn: per expert h rows of f values."""
+    w_dn: per expert h rows of f values. The reference switches to the GEMMs at 64 tokens (gen_llm.py:6107); here
+    from 192 assignments (tokens * ku), where they measured faster on configs[2] shapes (top-8 of 128 experts:
+    matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 / 312 us). `prefill` forces either path."""
     tokens = x.shape[0]
     ids, wts = moe_route(logits, n_experts, ku, norm=norm)
     if prefill is None:
-        prefill = tokens >= 64   # gen_llm.py:6107: %gemm = t >= 64
+        prefill = tokens * ku >= 192
     if not prefill:
         act = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=True)
         ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act, w_dn, h, f, ku, n_experts)

@@ -191,7 +191,7 @@ class GpuMoEBackend:
         r = x.shape[0]
         if r == 0:
             return torch.zeros(0, h, dtype=torch.float32, device=x.device)
-        if r < 64:   # decode-sized: per-row expert matvecs (gen_llm.py:6107 threshold)
+        if r < 192:   # decode-sized: per-row expert matvecs (the crossover ops.moe_ffn measured)
             act = ops.moe_expert_mv(self.fmt, "gu", eids, x, w_gu, f, h, 1, n_local, fused=True)
             return ops.moe_expert_mv(self.fmt, "dn", eids, act, w_dn, h, f, 1, n_local)
         ti, rm, pos = ops.moe_bucket(eids.view(r, 1), n_local)

@@ -289,7 +289,7 @@ class TestMoE:
                 ref_y[t] += wts[t, kk] * ys_h[rpos[t * ku + kk]]
         assert O.rel_l2(y, ref_y) < 1e-6
 
-    @pytest.mark.parametrize("tokens", [1, 16, 256])
+    @pytest.mark.parametrize("tokens", [1, 16, 24, 40, 256])
     def test_moe_ffn_end_to_end(self, ops, tokens):
         E, ku, H, F, fmt = 32, 8, 1024, 256, "q4_0"
         rng = np.random.default_rng(90 + tokens)
