@@ -338,7 +338,7 @@ def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
 
 
 def moe_path(ops, torch, lg, E, ku, m, expert_bytes, ms, matvec_below=64):
-    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 192 assignments; MXFP4: matvecs for at most 8
+    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 192 assignments; MXFP4: matvecs for at most 16
     assignments), and for the matvecs the weight GB/s over the experts the routing touches."""
     if m >= matvec_below:
         return {"path": "grouped GEMMs"}
@@ -383,7 +383,7 @@ def bench_moe(args, torch, dev, time_steps, pk):
             g.replay()
         ms = time_steps(g.replay, 20)
         mx[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
-                      **moe_path(ops, torch, lg, E, ku, m, 3 * h * f // 2 + 3 * h * f // 32, ms, 8 // ku + 1)}
+                      **moe_path(ops, torch, lg, E, ku, m, 3 * h * f // 2 + 3 * h * f // 32, ms, 16 // ku + 1)}
     # the dense kernel alone: fused gate/up shape, M=8192
     M = 8192
     x8, s8 = ops.row_scale_f8(torch.randn(M, h, device=dev, generator=gen))

@@ -291,17 +291,17 @@ def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, nor
                    prefill=None):
     """The routed expert FFN of one MoE layer with MXFP4 experts (gpt-oss-like; gen_llm.py:5324-5386 wiring): the fp8
     fusion of gen_mxfp4s.py:969-1110 -- route -> bucket -> e4m3 row scale -> grouped gate/up (SwiGLU) -> e4m3 row
-    scale -> grouped down -> weighted combine -- or, for at most 8 assignments, per-assignment expert matvecs on the
+    scale -> grouped down -> weighted combine -- or, for at most 16 assignments, per-assignment expert matvecs on the
     unquantised activations (gen_moe.py:535-727). The reference switches at 64 tokens (gen_llm.py:6107); here the
-    matvecs stream each assignment's expert on its own, which measured faster only for a handful of assignments
-    (gpt-oss shapes: 4 assignments 45 against 83 us; 128 assignments took 1155 against 265 us in the kernel's
-    first form). `prefill` forces either
+    matvecs stream each assignment's expert on its own, which measured faster only up to about 20 assignments
+    (gpt-oss shapes, matvecs / GEMMs: 4 assignments 45 / 83 us, 16: 139 / 165 us, 24: 196 / 170 us). `prefill`
+    forces either
     path. w_gu / ws_gu: per expert 2f rows (gate then up) of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per
     expert h rows of f/2 / f/32 bytes."""
     tokens = x.shape[0]
     ids, wts = moe_route(logits, n_experts, ku, norm=norm)
     if prefill is None:
-        prefill = tokens * ku > 8
+        prefill = tokens * ku > 16
     if not prefill:
         act = moe_expert_mv_mxfp4s("gu", ids.reshape(-1), x, w_gu, ws_gu, f, h, ku, n_experts, order=order)
         ys = moe_expert_mv_mxfp4s("dn", ids.reshape(-1), act, w_dn, ws_dn, h, f, ku, n_experts, order=order)
