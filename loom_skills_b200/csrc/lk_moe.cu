@@ -333,7 +333,9 @@ int moe_bucket(int tokens, int ku, int E, int max_tiles, const int32_t* info, co
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// combines: one block per token; the fma chain runs over k in order, as the reference's
+// combines: block (t, c) covers columns 256 c .. 256 c + 255 of token t, one per thread (a token's columns spread over
+// h / 256 CTAs, so a decode token's combine is not one CTA walking h); the fma chain runs over k in order, as the
+// reference's
 // ---------------------------------------------------------------------------------------------------------------
 template <bool SORTED>
 __global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, const float* __restrict__ ys,
@@ -347,26 +349,26 @@ __global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, 
     p[threadIdx.x] = SORTED ? pos[int64_t(t) * ku + threadIdx.x] : t * ku + threadIdx.x;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < h; c += 256) {
-    float acc = accumulate ? y[int64_t(t) * h + c] : 0.f;
-    for (int k = 0; k < ku; ++k) {
-      float v = p[k] >= 0 ? ys[int64_t(p[k]) * h + c] : 0.f;
-      acc = fmaf(w[k], v, acc);
-    }
-    y[int64_t(t) * h + c] = acc;
+  const int c = blockIdx.y * 256 + threadIdx.x;
+  if (c >= h) return;
+  float acc = accumulate ? y[int64_t(t) * h + c] : 0.f;
+  for (int k = 0; k < ku; ++k) {
+    float v = p[k] >= 0 ? ys[int64_t(p[k]) * h + c] : 0.f;
+    acc = fmaf(w[k], v, acc);
   }
+  y[int64_t(t) * h + c] = acc;
 }
 
 int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
                        const float* wts, float* y, cudaStream_t s) {
   (void)rows;
-  k_combine<true><<<tokens, 256, 0, s>>>(h, ku, accumulate, ys, pos, wts, y);
+  k_combine<true><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, pos, wts, y);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                 cudaStream_t s) {
-  k_combine<false><<<tokens, 256, 0, s>>>(h, ku, accumulate, ys, nullptr, wts, y);
+  k_combine<false><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, nullptr, wts, y);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
