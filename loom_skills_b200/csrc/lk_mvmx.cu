@@ -5,17 +5,19 @@
 //   mode 1 (down; expert e holds h rows):                        y[a][j] = Wd[e][j] . x[a]
 // with e = ids[a] and W the exact MXFP4 values: e2m1 code * 2^(s - 127), s the row's E8M0 byte of the 32-value block.
 //
-// Design (HBM-bound at decode sizes). One CTA per (16 output rows, assignment); a warp computes 2 of the rows (a
-// gate/up pair counts as one) -- measured at one token of gpt-oss shapes: 8 rows per warp 56 us per MoE layer, 4 rows
-// 50 us, 2 rows 45 us (more CTAs in flight; the activation staging is cheap). The CTA stages the assignment's activation row in shared memory as f32 once, each
-// 128-byte block in 16-byte granules swizzled by the block index (granule q of block b at q ^ (b % 8)), so the lanes
-// of a warp, which read the same granule of 32 consecutive blocks, spread over eight bank groups. Lane l owns the
-// 32-value blocks l + 32 i of every row (i < BPL = ceil(k / 1024)). Per block a lane loads the block's 16 nibble
-// bytes (consecutive lanes read consecutive 16-byte segments of the row) and its E8M0 byte, the loads of the warp's
-// rows going out before any of their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign,
-// exponent and mantissa bits placed in the f16 sign, low exponent and top mantissa bits give value * 2^-14, e = 0
-// landing on the f16 subnormal 0.5 * 2^-14 -- then an f32 for an f32 FMA against the activation. The block's sum
-// takes its scale, and the row's warp-reduced total is multiplied by 2^14.
+// Design. One CTA per (16 output rows, assignment); a warp computes 2 of the rows (a gate/up pair counts as one). The
+// CTA first stages the assignment's activation row in shared memory as f32, each 128-byte block in 16-byte granules
+// swizzled by the block index (granule q of block b at q ^ (b % 8)), so the lanes of a warp, which read the same
+// granule of 32 consecutive blocks, spread over eight bank groups. Lane l owns the 32-value blocks l + 32 i of every
+// row (i < BPL = ceil(k / 1024)). Per block a lane loads the block's 16 nibble bytes (consecutive lanes read
+// consecutive 16-byte segments of the row) and its E8M0 byte, the loads of the warp's rows going out before any of
+// their arithmetic. Each nibble becomes an exact f16 -- the e2m1 sign, exponent and mantissa bits placed in the f16
+// sign, low exponent and top mantissa bits give value * 2^-14, e = 0 landing on the f16 subnormal 0.5 * 2^-14 --
+// then an f32 for an f32 FMA against the activation. The block's sum takes its scale, and the row's warp-reduced
+// total is multiplied by 2^14.
+// Measured at one token of gpt-oss shapes (a MoE layer, CUDA events): 8 rows per warp 56 us, 4 rows 50 us, 2 rows
+// 42-45 us; with the activations in registers instead of shared memory (one CTA per SM) 72 us. ncu counts it
+// instruction-bound (issue 64 % of cycles, DRAM 16 %): about 4.4 instructions per weight value.
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
