@@ -180,15 +180,15 @@ class TestExpertMvMxfp4:
 
     @pytest.mark.parametrize("k", [2880, 64, 1024, 4096, 2080])
     @pytest.mark.parametrize("order", ["pairs", "split16"])
-    @pytest.mark.parametrize("xdt", ["f32", "bf16"])
+    @pytest.mark.parametrize("xdt", ["f32", "bf16", "f16"])
     def test_gate_up_and_down(self, ops, k, order, xdt):
-        rng = np.random.default_rng(k + (order == "pairs") + 3 * (xdt == "bf16"))
+        rng = np.random.default_rng(k + (order == "pairs") + 3 * (xdt == "bf16") + 5 * (xdt == "f16"))
         E, ku, tokens, f = 5, 2, 3, 200
         a = tokens * ku
         _, nib, sc = mx_weights(E * 2 * f, k, 81)
         ids = rng.integers(0, E, a).astype(np.int32)
         x = rng.standard_normal((tokens, k)).astype(np.float32)
-        xt = dev(x) if xdt == "f32" else dev(x).to(torch.bfloat16)
+        xt = dev(x).to({"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[xdt])
         xs = host(xt.float())
         od = ops.L.ORDER_PAIRS if order == "pairs" else ops.L.ORDER_SPLIT16
         nb = nib if order == "pairs" else to_split16(nib)
