@@ -20,7 +20,9 @@ It restates, in numpy, the numerics of loom-fun/loom-skills for this path (paths
   e4m3 rounding ``make_kernel_tests.py:2006-2019``; MXFP4 -> e5m2 decode ``gen_mxfp4s.py:14-48``
 * products: ``make_kernel_tests.py:45-47, 231-238`` (matvec), ``:1860-1876`` (GEMM: (x16 . W^T) * inv)
 * MoE: router ``gen_moe.py:116-253``, bucket ``gen_moe.py:829-955``, grouped GEMM ``gen_moe.py:1126-1228``,
-  combine ``gen_moe.py:730-762, 1231-1280``, reference F64 pipeline ``.github/devlab/kbench/moe_q4_0/gen_bench.py:185-248``.
+  combine ``gen_moe.py:730-762, 1231-1280``, reference F64 pipeline ``.github/devlab/kbench/moe_q4_0/gen_bench.py:185-248``;
+  the decode-size layer (expert matvecs ``gen_moe.py:535-727`` below the GEMM threshold of ``gen_llm.py:6107``), also
+  over MXFP4 experts.
 
 The quantisers below are test-input generators (seeded synthetic weights), not part of the reference path:
 Q4_0 restates gguf's quantiser; Q4_K, IQ4_NL and MXFP4 are this repository's own (gguf 0.19.0 cannot quantise Q4_K
