@@ -414,10 +414,11 @@ def dequant_mxfp4_planar(nib, sc, n, k, order="pairs"):
 # ------------------------------------------------------------------------------------------------------------------
 # MoE
 # ------------------------------------------------------------------------------------------------------------------
-def route_ref(logits, ku, gating=1, norm=True, bias=None):
+def route_ref(logits, ku, gating=1, norm=True, bias=None, scale=1.0):
     """Router top-k (gen_moe.py:116-253): gating 1 softmax over all experts then top-k, gating 2 sigmoid (+bias for
     the pick), gating 3 top-k of the (biased) logits weighted by a softmax over the picked. Ties: lowest index.
-    norm: w / max(sum, 6.103515625e-05)."""
+    norm: w / max(sum, 6.103515625e-05) (gating 1 and 2); the final weights times `scale` (expert_weights_scale,
+    gen_moe.py:111-113; make_kernel_tests.py:3166-3186 applies it for every gating). f32 arithmetic as the kernels'."""
     lg = np.asarray(logits, np.float32)
     t, E = lg.shape
     if gating == 1:
@@ -444,7 +445,62 @@ def route_ref(logits, ku, gating=1, norm=True, bias=None):
             wts[i] = p / max(p.sum(), 6.103515625e-05)
         else:
             wts[i] = p
-    return ids, wts
+    return ids, (wts * np.float32(scale)).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# expert activations, biases, per-expert down scale, shared-expert gate
+# ------------------------------------------------------------------------------------------------------------------
+ACT_SILU, ACT_GELU, ACT_SWIGLU_OAI = 0, 1, 2   # include/lk.h LK_ACT_*
+
+
+def gelu_tanh(x):
+    """GEGLU's gate activation (make_kernel_tests.py:78-80 ffn_act "gelu"; kbench moe_q4_0/gen_bench.py:38-39)."""
+    x = np.asarray(x, np.float64)
+    return 0.5 * x * (1 + np.tanh(np.sqrt(2 / np.pi) * (x + 0.044715 * x ** 3)))
+
+
+def act_ref(g, u, act=ACT_SILU, alpha=1.702, limit=7.0):
+    """The expert gate/up activation (gen_moe.py:27-64 act_scalar / act_vector): silu(g) * u; gelu_tanh(g) * u;
+    swiglu_oai: x = min(g, limit), y = clamp(u, -limit, limit), x * sigmoid(alpha x) * (y + 1)
+    (make_kernel_tests.py:3208-3210)."""
+    g = np.asarray(g, np.float64)
+    u = np.asarray(u, np.float64)
+    if act == ACT_SILU:
+        return silu(g) * u
+    if act == ACT_GELU:
+        return gelu_tanh(g) * u
+    xg = np.minimum(g, limit)
+    return xg / (1 + np.exp(-alpha * xg)) * (np.clip(u, -limit, limit) + 1)
+
+
+def wscale_ref(ids, wts, scale):
+    """g_moe_wscale (gen_moe.py:1010-1045): wts[t, k] * scale[ids[t, k]] (ids clamped to the expert range), f32."""
+    ids = np.clip(np.asarray(ids, np.int64), 0, len(scale) - 1)
+    return (np.asarray(wts, np.float32) * np.asarray(scale, np.float32)[ids]).astype(np.float32)
+
+
+def shared_gate_ref(x, w):
+    """g_moe_shared_gate (gen_moe.py:780-823): sg[t] = sigmoid(x[t] . w), float64."""
+    d = np.asarray(x, np.float64) @ np.asarray(w, np.float64).reshape(-1)
+    return 1.0 / (1.0 + np.exp(-d))
+
+
+def combine_ref(ys, wts, pos=None, y0=None, sg=None):
+    """g_moe_combine / _sorted (gen_moe.py:730-762, 1231-1280), optionally shared_gated (gen_moe.py:765-777):
+    y[t] = sg[t] * y0[t] + sum_k wts[t, k] * ys[row(t, k)], row = pos[t*ku + k] (sorted; < 0 -> 0) or t*ku + k."""
+    wts = np.asarray(wts, np.float64)
+    t, ku = wts.shape
+    ys = np.asarray(ys, np.float64)
+    h = ys.shape[1]
+    y = np.zeros((t, h)) if y0 is None else np.asarray(y0, np.float64) * (1.0 if sg is None else
+                                                                          np.asarray(sg, np.float64)[:, None])
+    for i in range(t):
+        for k in range(ku):
+            r = i * ku + k if pos is None else int(pos[i * ku + k])
+            if r >= 0:
+                y[i] += wts[i, k] * ys[r]
+    return y
 
 
 def moe_max_tiles(tokens, ku, n_experts, tile=64):
@@ -490,13 +546,20 @@ def check_bucket(ids, n_experts, max_tiles, tile_info, rowmap, pos, live=None, t
     pos = np.asarray(pos)
     if not np.array_equal(rm < 0, rowmap < 0):
         return "padding rows differ"
-    for e_tile in range(max_tiles):
-        e = ti[e_tile, 0]
-        if e < 0:
-            continue
-        seg = slice(e_tile * tile, (e_tile + 1) * tile)
-    # same set of assignments per expert, and pos is the inverse of rowmap
+    # per tile: the live rows are its first tile_info rows, each holding an assignment routed to the tile's expert
     idsf = np.asarray(ids).reshape(-1)
+    for e_tile in range(max_tiles):
+        e, nrows = int(ti[e_tile, 0]), int(ti[e_tile, 1])
+        seg = rowmap[e_tile * tile:(e_tile + 1) * tile]
+        if e < 0:
+            if (seg >= 0).any():
+                return f"unused tile {e_tile} holds rows"
+            continue
+        if not ((seg[:nrows] >= 0).all() and (seg[nrows:] < 0).all()):
+            return f"tile {e_tile}: live rows are not its first {nrows}"
+        if (np.clip(idsf[seg[:nrows]], 0, n_experts - 1) != e).any():
+            return f"tile {e_tile} holds an assignment of another expert"
+    # same set of assignments per expert, and pos is the inverse of rowmap
     for r in np.nonzero(rowmap >= 0)[0]:
         a = rowmap[r]
         if pos[a] != r:
@@ -508,25 +571,34 @@ def check_bucket(ids, n_experts, max_tiles, tile_info, rowmap, pos, live=None, t
     return None
 
 
-def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts):
-    """The routed expert FFN in float64 (kbench moe_q4_0/gen_bench.py:185-248 with SiLU):
-    y[t] = sum_k wts[t,k] * Wd[e] (silu(Wg[e] x[t]) * (Wu[e] x[t])), e = ids[t,k]; w_gu[e] = gate rows then up rows."""
+def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts, act=ACT_SILU, alpha=1.702, limit=7.0, b_gate=None,
+                b_up=None, b_down=None, dsc=None, y0=None, sg=None):
+    """The routed expert FFN in float64 (kbench moe_q4_0/gen_bench.py:185-248; make_kernel_tests.py:3196-3215
+    experts_ref and :3268-3271 chain): y[t] = sg[t] y0[t] + sum_k wts[t,k] dsc[e] (Wd[e] act(Wg[e] x[t] + bg[e],
+    Wu[e] x[t] + bu[e]) + bd[e]), e = ids[t,k]; w_gu[e] = gate rows then up rows (packed blocks of `fmt`, or float
+    weights when fmt is None); biases [E][f] / [E][h] f32."""
     x = np.asarray(x, np.float64)
     t, ku = ids.shape
     y = np.zeros((t, h), np.float64)
-    cache = {}
+    if y0 is not None:
+        y += np.asarray(y0, np.float64) * (1.0 if sg is None else np.asarray(sg, np.float64)[:, None])
+    w_eff = np.asarray(wts, np.float64) if dsc is None else wscale_ref(ids, wts, dsc).astype(np.float64)
     for e in np.unique(ids):
-        gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
-        dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
-        cache[int(e)] = (gu, dn)
-    for e in np.unique(ids):
-        gu, dn = cache[int(e)]
+        if fmt is None:   # float weights [E][2f][h] / [E][h][f] (e.g. dequant_mxfp4_planar's output)
+            gu, dn = np.asarray(w_gu[e], np.float64), np.asarray(w_dn[e], np.float64)
+        else:
+            gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
+            dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
         sel = np.nonzero(ids == e)
-        xs = x[sel[0]]
-        pair = xs @ gu.T
-        act = silu(pair[:, :f]) * pair[:, f:]
-        ys = act @ dn.T
-        np.add.at(y, sel[0], ys * np.asarray(wts, np.float64)[sel][:, None])
+        pair = x[sel[0]] @ gu.T
+        g, u = pair[:, :f], pair[:, f:]
+        if b_gate is not None:
+            g = g + np.asarray(b_gate, np.float64)[e]
+            u = u + np.asarray(b_up, np.float64)[e]
+        ys = act_ref(g, u, act, alpha, limit) @ dn.T
+        if b_down is not None:
+            ys = ys + np.asarray(b_down, np.float64)[e]
+        np.add.at(y, sel[0], ys * w_eff[sel][:, None])
     return y
 
 
@@ -573,3 +645,88 @@ def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# the reference's hand-built MoE kernel cases (kbench moe_q4_0): inputs regenerated from their seed
+# ------------------------------------------------------------------------------------------------------------------
+KB_H, KB_F, KB_E, KB_U = 2816, 704, 8, 8          # .github/devlab/kbench/moe_q4_0/gen_bench.py:142 (Gemma dimensions)
+KB_COUNTS = (64, 17, 1, 0)                          # gen_bench.py:206: one full tile, 17- and 1-row tails, a dead tile
+KB_TILE_INFO = ((7, 64), (0, 17), (3, 1), (-1, 0))  # gen_bench.py:207
+KB_SENTINEL = 42.0                                  # gen_bench.py:175: outputs start filled with 42
+
+
+def kbench_q4_0_weights(rng, shape):
+    """gen_bench.py:27-35 weights(): Q4_0 blocks with f16 scales uniform in +-[0.0005, 0.003] (both signs) and
+    uniform code bytes -> (raw uint8 [blocks*18], float64 values of `shape`)."""
+    blocks = int(np.prod(shape)) // 32
+    raw = np.empty((blocks, 18), np.uint8)
+    scale = (rng.uniform(.0005, .003, blocks) * rng.choice([-1, 1], blocks)).astype('<f2')
+    raw[:, :2] = scale.view(np.uint8).reshape(-1, 2)
+    raw[:, 2:] = rng.integers(0, 256, (blocks, 16), dtype=np.uint8)
+    vals = dequant("q4_0", raw, 32).astype(np.float64).reshape(shape)
+    return raw.reshape(-1), vals
+
+
+def kbench_moe_inputs(seed=490):
+    """The inputs of the kbench moe_q4_0 cases (gen_bench.py:142-248) drawn in the generator's order from
+    default_rng(seed): stacked Q4_0 expert weights (gate/up fused [E][2F][H], down [E][H][F]), the decode cases
+    (t = 1, 4: a permutation of the experts per token), the grouped cases (t = 63, 65: the hand-built tile_info with
+    random row maps, f16 activations and row scales in {0.5, 1, 2}) and the down-scale + combine case (t = 4)."""
+    H, F, E, U = KB_H, KB_F, KB_E, KB_U
+    rng = np.random.default_rng(seed)
+    out = {}
+    out["wg"], out["gu"] = kbench_q4_0_weights(rng, (E, 2 * F, H))
+    out["wd"], out["down"] = kbench_q4_0_weights(rng, (E, H, F))
+    for t in (1, 4):
+        out[f"decode_t{t}_ids"] = np.stack([rng.permutation(E) for _ in range(t)]).astype(np.int32)
+        out[f"decode_t{t}_x"] = rng.standard_normal((t, H)).astype(np.float32)
+        out[f"decode_t{t}_xdn"] = (rng.standard_normal((t * U, F)) * .1).astype(np.float32)
+    for t in (63, 65):
+        rm = np.full(256, -1, np.int32)
+        for j, n in enumerate(KB_COUNTS):
+            rm[j * 64:j * 64 + n] = rng.choice(t * U, n, replace=False)
+        out[f"grouped_t{t}_rm"] = rm
+        out[f"grouped_t{t}_x"] = rng.standard_normal((t, H)).astype(np.float16)
+        s = np.ones((t, 2), np.float32)
+        s[:, 1] = rng.choice([.5, 1, 2], t)
+        out[f"grouped_t{t}_s"] = s
+        xd = (rng.standard_normal((256, F)) * .1).astype(np.float16)
+        sd = np.ones((256, 2), np.float32)
+        sd[:, 1] = rng.choice([.5, 1, 2], 256)
+        for j, n in enumerate(KB_COUNTS[:-1]):
+            xd[j * 64 + n:(j + 1) * 64] = 0
+        out[f"grouped_t{t}_xd"] = xd
+        out[f"grouped_t{t}_sd"] = sd
+    t = 4
+    out["dsc_ids"] = np.stack([rng.permutation(E) for _ in range(t)]).astype(np.int32)
+    out["dsc_scales"] = np.linspace(.25, 1.5, E, dtype=np.float32)
+    out["dsc_wts"] = rng.uniform(.01, .2, (t, U)).astype(np.float32)
+    out["dsc_ys"] = rng.standard_normal((t * U, H)).astype(np.float32) * .1
+    return out
+
+
+def ffn_golden_inputs(seed=8102, E=8, H=512, F=256, KU=4, t=6):
+    """Seeded inputs of the expert-FFN golden chains (tests/golden/make_golden.py main_moe): Q4_0 and MXFP4 (split
+    planes, pairs order) experts of N(0, 0.02) weights, activations, routing, per-expert biases, down scales, the
+    shared-expert gate vector and the shared output y0."""
+    rng = np.random.default_rng(seed)
+    q = lambda n, k: quantize_q4_0((rng.standard_normal((n, k)) * 0.02).astype(np.float32))   # noqa: E731
+    out = {"w_gu": np.stack([q(2 * F, H) for _ in range(E)]), "w_dn": np.stack([q(H, F) for _ in range(E)])}
+    mx_gu = [quantize_mxfp4((rng.standard_normal((2 * F, H)) * 0.02).astype(np.float32)) for _ in range(E)]
+    mx_dn = [quantize_mxfp4((rng.standard_normal((H, F)) * 0.02).astype(np.float32)) for _ in range(E)]
+    out["mx_gu_nib"] = np.concatenate([a for a, _ in mx_gu])
+    out["mx_gu_sc"] = np.concatenate([b for _, b in mx_gu])
+    out["mx_dn_nib"] = np.concatenate([a for a, _ in mx_dn])
+    out["mx_dn_sc"] = np.concatenate([b for _, b in mx_dn])
+    out["x"] = rng.standard_normal((t, H)).astype(np.float32)
+    lg = rng.standard_normal((t, E)).astype(np.float32)
+    out["ids"] = np.argsort(-lg, -1, kind="stable")[:, :KU].astype(np.int32)
+    out["wts"] = rng.uniform(0.05, 0.4, (t, KU)).astype(np.float32)
+    out["bg"] = (rng.standard_normal((E, F)) * 0.05).astype(np.float32)
+    out["bu"] = (rng.standard_normal((E, F)) * 0.05).astype(np.float32)
+    out["bd"] = (rng.standard_normal((E, H)) * 0.05).astype(np.float32)
+    out["dsc"] = np.linspace(0.5, 1.5, E).astype(np.float32)
+    out["wsg"] = (rng.standard_normal(H) * 0.05).astype(np.float32)
+    out["y0"] = (rng.standard_normal((t, H)) * 0.1).astype(np.float32)
+    return out

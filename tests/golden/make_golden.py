@@ -151,5 +151,153 @@ def main(ref):
     print("wrote", os.path.join(HERE, "golden.npz"), sum(a.nbytes for a in out.values()), "bytes uncompressed")
 
 
+def _reference_functions(ref, names, scope):
+    """Functions of make_kernel_tests.py taken out by its syntax tree (the module runs a model build at import; some
+    of these are nested in its MoE section), executed in `scope` for their free variables."""
+    import ast
+    src_path = os.path.join(ref, "skills/loom-port-llm/starter/make_kernel_tests.py")
+    tree = ast.parse(open(src_path).read())
+    found = {n.name: n for n in ast.walk(tree) if isinstance(n, ast.FunctionDef) and n.name in names}
+    missing = set(names) - set(found)
+    assert not missing, missing
+    exec(compile(ast.Module(body=[found[n] for n in names], type_ignores=[]), src_path, "exec"), scope)
+    return scope
+
+
+def main_moe(ref):
+    """golden_moe.npz: the router, expert-FFN and hand-built MoE schedule vectors, all computed by the reference's
+    own code:
+
+    * router: make_kernel_tests.py:3166-3186 route_ref (gating 1 softmax / 2 sigmoid + selection bias / 3 softmax of
+      the picked biased logits, norm_weights, expert_weights_scale), with Wr = I so the logits are the inputs; rows
+      whose k-th and (k+1)-th scores are within 0.2 % are dropped, as its clear_tokens does (:3187-3194);
+    * expert FFN: make_kernel_tests.py:3196-3215 experts_ref (SiLU, GEGLU gelu-tanh via ffn_act :78-80, gpt-oss
+      swiglu_oai with per-expert biases; the prefill variant f16=True), and the chain of :3268-3271 (per-expert down
+      scale folded into the weights, the Qwen shared-expert gate scaling the shared output y0);
+    * the kbench moe_q4_0 cases (.github/devlab/kbench/moe_q4_0/gen_bench.py:185-248): weights from its own
+      generator, the decode and grouped expert products with its F64 formulas and its gelu, sentinel 42 where a
+      kernel must not write, and the down-scale + combine case. Inputs are regenerated by the oracle
+      (kbench_moe_inputs, same seed and draw order); their SHA-256 digests are stored to pin that."""
+    import hashlib
+    sys.path.insert(0, os.path.dirname(HERE))
+    sys.path.insert(0, os.path.join(os.path.dirname(HERE), ".."))
+    from oracle import qmm_oracle as O
+    from gguf import GGMLQuantizationType as T
+    from gguf.quants import dequantize
+    st = _load(os.path.join(ref, "skills/loom-port-llm/starter/st_tensors.py"), "st_tensors")
+    out = {}
+
+    # ---- router
+    M = {}
+    scope = _reference_functions(ref, ["route_ref"], {"np": np, "M": M})
+    cases = [("r1", 1, True, False, 1.0, 128, 8), ("r2", 1, False, False, 2.5, 64, 6), ("r3", 2, True, True, 1.0, 64, 6),
+             ("r4", 2, False, True, 2.5, 32, 4), ("r5", 3, False, True, 1.0, 32, 4), ("r6", 3, True, False, 1.0, 128, 8)]
+    rng = np.random.default_rng(8101)
+    for name, gating, norm, has_bias, scale, E, KU in cases:
+        M.clear()
+        M.update(gating=gating, norm_weights=norm, scale=scale)
+        scope["KU"] = KU
+        lg = (rng.standard_normal((400, E)) * 2.0).astype(np.float32)
+        bias = (rng.standard_normal(E) * 0.5).astype(np.float32) if has_bias else np.zeros(E, np.float32)
+        ids, wts, rel = scope["route_ref"](lg, np.eye(E, dtype=np.float32), bias)
+        keep = np.flatnonzero(rel > 2e-3)[:96]
+        out[f"route_{name}_logits"] = lg[keep]
+        out[f"route_{name}_bias"] = bias
+        out[f"route_{name}_ids"] = ids[keep].astype(np.int32)
+        out[f"route_{name}_wts"] = wts[keep].astype(np.float32)
+        out[f"route_{name}_cfg"] = np.array([gating, int(norm), int(has_bias), E, KU], np.int64)
+        out[f"route_{name}_scale"] = np.array([scale], np.float64)
+
+    # ---- expert FFN chains (decode precision and the prefill f16 variant); inputs from the oracle's seeded
+    # generator, stored as digests; the float weights the reference multiplies come from gguf / st_tensors
+    E, H, F, KU, t = 8, 512, 256, 4, 6
+    fi = O.ffn_golden_inputs(8102, E, H, F, KU, t)
+    out["ffn_digests"] = np.stack([np.frombuffer(hashlib.sha256(np.ascontiguousarray(fi[k]).tobytes()).digest(), np.uint8)
+                                   for k in sorted(fi)])
+    out["ffn_digest_names"] = np.array(sorted(fi))
+    deq = lambda b, n, k: dequantize(b.reshape(-1), T.Q4_0).reshape(n, k).astype(np.float64)   # noqa: E731
+    gu_f = [deq(b, 2 * F, H) for b in fi["w_gu"]]
+    Wg = np.stack([w[:F] for w in gu_f])
+    Wu = np.stack([w[F:] for w in gu_f])
+    Wd = np.stack([deq(b, H, F) for b in fi["w_dn"]])
+    MGu = st.dequant_mxfp4(fi["mx_gu_nib"], fi["mx_gu_sc"]).astype(np.float64).reshape(E, 2 * F, H)
+    MWd = st.dequant_mxfp4(fi["mx_dn_nib"], fi["mx_dn_sc"]).astype(np.float64).reshape(E, H, F)
+    x, ids, wts, bg, bu, bd = fi["x"], fi["ids"], fi["wts"], fi["bg"], fi["bu"], fi["bd"]
+    dsc, wsg, y0 = fi["dsc"], fi["wsg"], fi["y0"]
+    q8_scope = _reference_functions(ref, ["q8_ref"], {"np": np})
+    for name, act, eb, oai, mx in [("silu", None, False, False, False), ("gelu", "gelu", False, False, False),
+                                   ("oai", None, True, True, False), ("oai_mx", None, True, True, True)]:
+        cfg = {"ffn_act": act} if act else {}
+        scope = _reference_functions(ref, ["ffn_act", "experts_ref"],
+                                     {"np": np, "cfg": cfg, "H": H, "KU": KU, "EB": eb, "OAI": oai,
+                                      "M": {"swiglu_limit": 7.0, "swiglu_alpha": 1.702}, "q8_ref": q8_scope["q8_ref"]})
+        scope.update(_reference_functions(ref, ["f16_rows"], {"np": np}))
+        g_, u_, d_ = (MGu[:, :F], MGu[:, F:], MWd) if mx else (Wg, Wu, Wd)
+        for f16 in (False, True):
+            y = scope["experts_ref"](x, ids, wts, g_, u_, d_, bg, bu, bd, f16=f16)
+            out[f"ffn_{name}_{'p' if f16 else 'd'}_y"] = y.astype(np.float32)
+    # the chain with the per-expert down scale and the shared-expert gate (make_kernel_tests.py:3268-3271)
+    scope = _reference_functions(ref, ["ffn_act", "experts_ref"],
+                                 {"np": np, "cfg": {}, "H": H, "KU": KU, "EB": False, "OAI": False, "M": {},
+                                  "q8_ref": q8_scope["q8_ref"]})
+    sgv = 1 / (1 + np.exp(-(x.astype(np.float64) @ wsg.astype(np.float64))))
+    wts_s = wts * dsc[ids]
+    out["ffn_chain_sg"] = sgv.astype(np.float32)
+    out["ffn_chain_wts_s"] = wts_s.astype(np.float32)
+    out["ffn_chain_y"] = (sgv[:, None] * y0 + scope["experts_ref"](x, ids, wts_s, Wg, Wu, Wd)).astype(np.float32)
+
+    # ---- kbench moe_q4_0 (gen_bench.py:142-248)
+    kb = _load(os.path.join(ref, ".github/devlab/kbench/moe_q4_0/gen_bench.py"), "q40_bench_moe")
+    H, F, E, U = 2816, 704, 8, 8
+    rng = np.random.default_rng(490)
+    wg, gu = kb.weights(rng, (E, 2 * F, H))
+    wd, down = kb.weights(rng, (E, H, F))
+    inp = O.kbench_moe_inputs(490)
+    assert np.array_equal(np.asarray(wg).view(np.uint8), inp["wg"]) and np.array_equal(np.asarray(wd).view(np.uint8), inp["wd"])
+    out["kb_digests"] = np.stack([np.frombuffer(hashlib.sha256(np.ascontiguousarray(inp[k]).tobytes()).digest(), np.uint8)
+                                  for k in sorted(inp)])
+    out["kb_digest_names"] = np.array(sorted(inp))
+    cols_f = np.sort(np.random.default_rng(7).choice(F, 96, replace=False))
+    cols_h = np.sort(np.random.default_rng(8).choice(H, 128, replace=False))
+    out["kb_cols_f"], out["kb_cols_h"] = cols_f, cols_h
+    for t in (1, 4):
+        ids = inp[f"decode_t{t}_ids"]
+        x = inp[f"decode_t{t}_x"]
+        act = np.empty((t * U, F), np.float64)
+        for a, e in enumerate(ids.flat):
+            pair = gu[e] @ x[a // U].astype(np.float64)
+            act[a] = kb.gelu(pair[:F]) * pair[F:]
+        out[f"kb_decode_gu_t{t}"] = act.astype(np.float32)
+        xdn = inp[f"decode_t{t}_xdn"]
+        out[f"kb_decode_dn_t{t}"] = np.stack([down[e] @ xdn[a].astype(np.float64) for a, e in enumerate(ids.flat)])[:, cols_h].astype(np.float32)
+    ti = np.array(O.KB_TILE_INFO, np.int32)
+    for t in (63, 65):
+        rm, x, s = inp[f"grouped_t{t}_rm"], inp[f"grouped_t{t}_x"], inp[f"grouped_t{t}_s"]
+        ref_ = np.full((256, F), 42, np.float64)
+        for j, n in enumerate(O.KB_COUNTS[:-1]):
+            ref_[j * 64:(j + 1) * 64] = 0
+            eid = ti[j, 0]
+            for q in range(n):
+                src = rm[j * 64 + q] // U
+                pair = gu[eid].astype(np.float16).astype(np.float64) @ x[src].astype(np.float64) * s[src, 1]
+                ref_[j * 64 + q] = kb.gelu(pair[:F]) * pair[F:]
+        out[f"kb_grouped_gu_t{t}"] = ref_[:, cols_f].astype(np.float32)
+        xd, sd = inp[f"grouped_t{t}_xd"], inp[f"grouped_t{t}_sd"]
+        refdn = np.full((256, H), 42, np.float64)
+        for j, n in enumerate(O.KB_COUNTS[:-1]):
+            refdn[j * 64:(j + 1) * 64] = (xd[j * 64:(j + 1) * 64].astype(np.float64) @
+                                          down[ti[j, 0]].astype(np.float16).astype(np.float64).T * sd[j * 64:(j + 1) * 64, 1:])
+        out[f"kb_grouped_dn_t{t}"] = refdn[:, cols_h].astype(np.float32)
+    ids, scales, wts, ys = inp["dsc_ids"], inp["dsc_scales"], inp["dsc_wts"], inp["dsc_ys"]
+    out["kb_dsc_y"] = np.sum(ys.reshape(4, U, H).astype(np.float64) * (wts * scales[ids])[:, :, None], axis=1).astype(np.float32)
+    out["kb_dsc_wts_s"] = (wts * scales[ids]).astype(np.float32)
+
+    np.savez_compressed(os.path.join(HERE, "golden_moe.npz"), **out)
+    print("wrote", os.path.join(HERE, "golden_moe.npz"), sum(a.nbytes for a in out.values()), "bytes uncompressed")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py LOOM_SKILLS_CHECKOUT")
+    main(sys.argv[1])
+    main_moe(sys.argv[1])

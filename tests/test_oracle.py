@@ -5,6 +5,7 @@ Everything here runs on the CPU. The golden fixtures come from the reference's o
 integer/byte/exact-float work.
 """
 import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -208,3 +209,95 @@ class TestQuantQ8:
         assert codes[0, :6].tolist() == [127, 1, -1, 2, -3, 0]
         assert meta[0, 0, 0] == 1.0 and meta[0, 0, 1] == 127 + 1 - 1 + 2 - 3
         assert (codes[0, 32:] == 0).all() and meta[0, 1].tolist() == [0.0, 0.0]
+
+
+# ---------------------------------------------------------------------------------------------------------- MoE pins
+@pytest.fixture(scope="module")
+def gmoe():
+    with np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_moe.npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+def _digests_match(inputs, names, digests):
+    import hashlib
+    for name, d in zip(names, digests):
+        got = hashlib.sha256(np.ascontiguousarray(inputs[str(name)]).tobytes()).digest()
+        assert got == d.tobytes(), name
+
+
+@pytest.mark.parametrize("case", ["r1", "r2", "r3", "r4", "r5", "r6"])
+def test_route_ref_matches_reference_router(gmoe, case):
+    # make_kernel_tests.py:3166-3186 route_ref, every gating / norm / bias / scale combination of the golden set
+    gating, norm, has_bias, E, KU = (int(v) for v in gmoe[f"route_{case}_cfg"])
+    ids, wts = O.route_ref(gmoe[f"route_{case}_logits"], KU, gating=gating, norm=bool(norm),
+                           bias=gmoe[f"route_{case}_bias"] if has_bias else None,
+                           scale=float(gmoe[f"route_{case}_scale"][0]))
+    assert np.array_equal(ids, gmoe[f"route_{case}_ids"])
+    np.testing.assert_allclose(wts, gmoe[f"route_{case}_wts"], rtol=2e-6, atol=1e-8)
+
+
+def test_ffn_inputs_regenerate(gmoe):
+    _digests_match(O.ffn_golden_inputs(), gmoe["ffn_digest_names"], gmoe["ffn_digests"])
+
+
+@pytest.mark.parametrize("name,act,mx", [("silu", O.ACT_SILU, False), ("gelu", O.ACT_GELU, False),
+                                         ("oai", O.ACT_SWIGLU_OAI, False), ("oai_mx", O.ACT_SWIGLU_OAI, True)])
+def test_moe_ffn_ref_matches_reference_experts(gmoe, name, act, mx):
+    # make_kernel_tests.py:3196-3215 experts_ref (decode precision); oai cases carry the per-expert biases
+    fi = O.ffn_golden_inputs()
+    E, H, F = 8, 512, 256
+    kw = dict(b_gate=fi["bg"], b_up=fi["bu"], b_down=fi["bd"]) if name.startswith("oai") else {}
+    if mx:
+        wgu = O.dequant_mxfp4_planar(fi["mx_gu_nib"], fi["mx_gu_sc"], E * 2 * F, H).reshape(E, 2 * F, H)
+        wdn = O.dequant_mxfp4_planar(fi["mx_dn_nib"], fi["mx_dn_sc"], E * H, F).reshape(E, H, F)
+        y = O.moe_ffn_ref(fi["x"], fi["ids"], fi["wts"], wgu, wdn, None, H, F, E, act=act, **kw)
+    else:
+        y = O.moe_ffn_ref(fi["x"], fi["ids"], fi["wts"], fi["w_gu"], fi["w_dn"], "q4_0", H, F, E, act=act, **kw)
+    assert O.rel_l2(y, gmoe[f"ffn_{name}_d_y"]) < 1e-6
+
+
+def test_moe_chain_down_scale_and_shared_gate(gmoe):
+    # make_kernel_tests.py:3268-3271: weights scaled per expert (g_moe_wscale), shared output gated (shared_gated)
+    fi = O.ffn_golden_inputs()
+    sg = O.shared_gate_ref(fi["x"], fi["wsg"])
+    np.testing.assert_allclose(sg, gmoe["ffn_chain_sg"], rtol=1e-6)
+    np.testing.assert_array_equal(O.wscale_ref(fi["ids"], fi["wts"], fi["dsc"]), gmoe["ffn_chain_wts_s"])
+    y = O.moe_ffn_ref(fi["x"], fi["ids"], fi["wts"], fi["w_gu"], fi["w_dn"], "q4_0", 512, 256, 8, dsc=fi["dsc"],
+                      y0=fi["y0"], sg=sg)
+    assert O.rel_l2(y, gmoe["ffn_chain_y"]) < 1e-6
+
+
+@pytest.fixture(scope="module")
+def kbench():
+    return O.kbench_moe_inputs(490)
+
+
+def test_kbench_inputs_regenerate(gmoe, kbench):
+    # the oracle draws the kbench moe_q4_0 inputs in the generator's own order (gen_bench.py:142-248)
+    _digests_match(kbench, gmoe["kb_digest_names"], gmoe["kb_digests"])
+
+
+def test_kbench_cases_from_oracle(gmoe, kbench):
+    # the oracle's act / combine restatements reproduce the reference's F64 expectations of every kbench case
+    H, F, U = O.KB_H, O.KB_F, O.KB_U
+    gu, down = kbench["gu"], kbench["down"]
+    for t in (1, 4):
+        ids, x = kbench[f"decode_t{t}_ids"], kbench[f"decode_t{t}_x"]
+        pair = np.stack([gu[e] @ x[a // U].astype(np.float64) for a, e in enumerate(ids.flat)])
+        act = O.act_ref(pair[:, :F], pair[:, F:], O.ACT_GELU)
+        assert O.rel_l2(act, gmoe[f"kb_decode_gu_t{t}"]) < 1e-6
+    ti = np.array(O.KB_TILE_INFO)
+    for t in (63, 65):
+        rm, x, s = kbench[f"grouped_t{t}_rm"], kbench[f"grouped_t{t}_x"], kbench[f"grouped_t{t}_s"]
+        ref = gmoe[f"kb_grouped_gu_t{t}"]
+        assert (ref[192:] == O.KB_SENTINEL).all()          # the dead tile is never written
+        e = ti[1, 0]
+        W16 = gu[e].astype(np.float16).astype(np.float64)
+        for q in range(17):
+            src = rm[64 + q] // U
+            pair = W16 @ x[src].astype(np.float64) * s[src, 1]
+            np.testing.assert_allclose(O.act_ref(pair[:F], pair[F:], O.ACT_GELU)[gmoe["kb_cols_f"]], ref[64 + q],
+                                       rtol=1e-6, atol=1e-9)
+        assert (ref[64 + 17:128] == 0).all()               # padding rows of a live tile hold zeros
+    y = O.combine_ref(kbench["dsc_ys"], O.wscale_ref(kbench["dsc_ids"], kbench["dsc_wts"], kbench["dsc_scales"]))
+    assert O.rel_l2(y, gmoe["kb_dsc_y"]) < 1e-6
