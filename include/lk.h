@@ -38,6 +38,10 @@ enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 30, LK_E4M3 = 1000 };
 enum { LK_STORE = 0, LK_ACC = 1, LK_SWIGLU = 2, LK_SWIGLU_SORTED = 3 };
 /* MXFP4 nibble order inside a 32-value block (gen_mxfp4s.py:1-7): OCP pairs, or ggml split16 */
 enum { LK_ORDER_PAIRS = 0, LK_ORDER_SPLIT16 = 1 };
+/* expert gate/up activations (gen_moe.py:27-64 act_scalar; cfg moe.act): silu(g) * u; GEGLU gelu_tanh(g) * u (the
+ * gemma4 kit's ffn_act "gelu", make_kernel_tests.py:78-80); gpt-oss swiglu_oai: x = min(g, limit),
+ * y = clamp(u, -limit, limit), x * sigmoid(alpha * x) * (y + 1) (llama.cpp ggml_swiglu_oai; alpha 1.702, limit 7) */
+enum { LK_ACT_SILU = 0, LK_ACT_GELU = 1, LK_ACT_SWIGLU_OAI = 2 };
 
 #define LK_OK 0
 #define LK_EINVAL (-1)       /* unknown format / mode / dtype, bad shape, null pointer */
@@ -200,6 +204,49 @@ int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, c
 int lk_moe_expert_mv_mxfp4s(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
                             const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
                             float* y, lk_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * MoE epilogue variants: the same kernels with the reference's expert activation choice and per-expert output biases
+ * (gen_moe.py:958-1007 _gemm_bias_act; expert_mv(bias=True, act=...), gen_moe.py:535-727). The biases are f32
+ * [n_experts][n]: gate/up modes add bias (gate) and bias2 (up) to the two products before the activation, as
+ * g_moe_ggu_* / g_moe_gu_* launch(..., %w, %w2, %bg, %bu, %y); down / store modes add bias (bias2 unused), as
+ * launch(..., %w, %bd, %y). NULL biases: none. act: LK_ACT_* (gate/up modes; ignored otherwise); alpha, limit: the
+ * swiglu_oai constants. The plain entry points above are these with LK_ACT_SILU and no biases.
+ * A grouped GEMM writes every row of each live 64-row tile (rows past the tile's count hold the activation of zero
+ * products plus the biases, zeros without biases, as the reference's tiles do) and no row of a dead tile.
+ */
+int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
+                           const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
+                           const void* w, const void* w2, const float* bias, const float* bias2, int act, float alpha,
+                           float limit, float* y, lk_stream_t stream);
+int lk_moe_grouped_gemm_mxfp4s_f8_ex(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
+                                     int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
+                                     const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
+                                     const uint8_t* w2s, const float* bias, const float* bias2, int act, float alpha,
+                                     float limit, float* y, lk_stream_t stream);
+int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                        const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2,
+                        const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
+                        lk_stream_t stream);
+int lk_moe_expert_mv_mxfp4s_ex(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
+                               const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
+                               const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
+                               lk_stream_t stream);
+/* lk_moe_wscale: g_moe_wscale (gen_moe.py:1010-1045), launch(%tokens, %ids, %wts, %scale): in place,
+ *   wts[t][k] *= scale[clamp(ids[t][k], 0, n_experts - 1)] -- a per-expert down scale (ffn_down_exps.scale) folded
+ *   into the combine weights before the experts run.
+ * lk_moe_shared_gate: g_moe_shared_gate (gen_moe.py:780-823), launch(%tokens, %x, %w, %sg): sg[t] = sigmoid(x[t] . w)
+ *   (the Qwen shared-expert gate ffn_gate_inp_shexp), x [tokens][h] f32, w [h] of w_dtype (LK_F32 / LK_BF16), f32
+ *   accumulation; h % 32 == 0.
+ * lk_moe_combine_gated / lk_moe_combine_sorted_gated: the combines made shared_gated (gen_moe.py:765-777):
+ *   y[t] = sg[t] * y[t] + sum_k wts[t][k] * ys[...] -- y holds the shared experts' output on entry. */
+int lk_moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale,
+                  lk_stream_t stream);
+int lk_moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, lk_stream_t stream);
+int lk_moe_combine_gated(int tokens, int h, int ku, const float* ys, const float* wts, const float* sg, float* y,
+                         lk_stream_t stream);
+int lk_moe_combine_sorted_gated(int tokens, int rows, int h, int ku, const float* ys, const int32_t* pos,
+                                const float* wts, const float* sg, float* y, lk_stream_t stream);
 
 /* lk_moe_ffn_decode_noalloc: the decode MoE layer in one call that allocates nothing. No counterpart in the
  * reference. It runs lk_moe_route (gating 1 over the given logits [tokens][n_experts] f32, renormalised when norm),

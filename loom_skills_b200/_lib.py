@@ -10,6 +10,8 @@ Q4_0, Q4_K, IQ4_NL, MXFP4, MXFP4S = 2, 12, 20, 39, 1039
 F32, F16, BF16, E4M3 = 0, 1, 30, 1000
 STORE, ACC, SWIGLU, SWIGLU_SORTED = 0, 1, 2, 3
 ORDER_PAIRS, ORDER_SPLIT16 = 0, 1
+ACT_SILU, ACT_GELU, ACT_SWIGLU_OAI = 0, 1, 2
+ACT_IDS = {"silu": ACT_SILU, "gelu": ACT_GELU, "swiglu_oai": ACT_SWIGLU_OAI}
 FMT_IDS = {"q4_0": Q4_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "mxfp4": MXFP4, "mxfp4s": MXFP4S}
 MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU, "swiglu_sorted": SWIGLU_SORTED}
 
@@ -46,6 +48,16 @@ SIGNATURES = {
     "lk_gemm_allgather": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, ctypes.POINTER(_P), _I, _I, _I, _P]),
     "lk_moe_row_scale_gather": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "lk_moe_ffn_decode_noalloc": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
+    "lk_moe_grouped_gemm_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _F, _F,
+                                    _P, _P]),
+    "lk_moe_grouped_gemm_mxfp4s_f8_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                              _P, _I, _F, _F, _P, _P]),
+    "lk_moe_expert_mv_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _F, _F, _P, _P]),
+    "lk_moe_expert_mv_mxfp4s_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _F, _F, _P, _P]),
+    "lk_moe_wscale": (_I, [_I, _I, _I, _P, _P, _P, _P]),
+    "lk_moe_shared_gate": (_I, [_I, _I, _P, _P, _I, _P, _P]),
+    "lk_moe_combine_gated": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
+    "lk_moe_combine_sorted_gated": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -7,6 +7,7 @@ using namespace lk;
 
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 static bool q4_family(int fmt) { return fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL; }
+static bool act_ok(int act) { return act == LK_ACT_SILU || act == LK_ACT_GELU || act == LK_ACT_SWIGLU_OAI; }
 
 extern "C" {
 
@@ -141,30 +142,44 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
   return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
 }
 
-int lk_moe_expert_mv_mxfp4s(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
-                            const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
-                            float* y, lk_stream_t stream) {
+int lk_moe_expert_mv_mxfp4s_ex(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
+                               const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
+                               const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
+                               lk_stream_t stream) {
   if (mode != 0 && mode != 1) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
   if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0 || k % 32) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (!act_ok(act)) return LK_EINVAL;
+  if (mode == 0 && (!bias) != (!bias2)) return LK_EINVAL;
   if (k > 4096) return LK_EUNSUPPORTED;
   if (assignments > 65535) return LK_ERANGE;   // one grid row per assignment
   if (assignments == 0) return LK_OK;
   if (!ids || !x || !w || !ws || !y) return LK_EINVAL;
   if (!aligned(w, 16) || !aligned(x, 16)) return LK_EALIGN;
+  ExpertEpi epi{bias, mode == 0 ? bias2 : nullptr, mode == 0 ? act : LK_ACT_SILU, alpha, limit};
   return moe_expert_mv_mx(mode, order, n, k, assignments, ku, n_experts, ids, x, x_dtype, w, ws, y,
-                          (cudaStream_t)stream);
+                          (cudaStream_t)stream, &epi);
 }
 
-int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
-                     const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
-                     lk_stream_t stream) {
+int lk_moe_expert_mv_mxfp4s(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
+                            const int32_t* ids, const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws,
+                            float* y, lk_stream_t stream) {
+  return lk_moe_expert_mv_mxfp4s_ex(mode, order, n, k, assignments, ku, n_experts, ids, x, x_dtype, w, ws, nullptr,
+                                    nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
+}
+
+int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                        const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2,
+                        const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
+                        lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
   if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
   if (mode != 0 && mode != 1) return LK_EINVAL;
   if (k % 256) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (!act_ok(act)) return LK_EINVAL;
+  if (mode == 0 && (!bias) != (!bias2)) return LK_EINVAL;
   if (assignments == 0) return LK_OK;
   if (!ids || !x || !w || !y) return LK_EINVAL;
   if (mode == 0 && !fused && !w2) return LK_EINVAL;
@@ -186,7 +201,15 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
   a.rows_per_expert2 = (mode == 0 && fused) ? 2 * n : n;   // fused: the up rows live in the same stacked tensor
   a.w2_row_offset = (mode == 0 && fused) ? n : 0;
   a.swiglu = mode == 0;
+  a.epi = ExpertEpi{bias, mode == 0 ? bias2 : nullptr, mode == 0 ? act : LK_ACT_SILU, alpha, limit};
   return mv(fmt, a, assignments, (cudaStream_t)stream);
+}
+
+int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                     const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
+                     lk_stream_t stream) {
+  return lk_moe_expert_mv_ex(fmt, mode, n, k, assignments, ku, n_experts, fused, ids, x, x_dtype, w, w2, nullptr,
+                             nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
 }
 
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
@@ -227,24 +250,35 @@ int lk_gemm_allgather(int fmt, int mode, int rows, int k, int n_local, const uin
               rows, 1, 1, 0, 0, &out);
 }
 
-int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
-                        const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
-                        const void* w, const void* w2, float* y, lk_stream_t stream) {
+int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
+                           const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
+                           const void* w, const void* w2, const float* bias, const float* bias2, int act, float alpha,
+                           float limit, float* y, lk_stream_t stream) {
   if (!q4_family(fmt)) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
+  if (!act_ok(act)) return LK_EINVAL;
   if (!tile_info || !rowmap || !x16 || !scales || !w || !y) return LK_EINVAL;
   const bool gu = mode != LK_STORE;   // gate/up: gathered or already sorted activation rows
   if (gu && !fused && !w2) return LK_EINVAL;
+  if (gu && (!bias) != (!bias2)) return LK_EINVAL;   // gate and up biases come together
   if (k % 256 || n % 16) return LK_EINVAL;
   if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
   if (rows == 0) return LK_OK;
   int64_t rb = lk_row_bytes(fmt, k);
   int64_t stride = rb * n * ((gu && fused) ? 2 : 1);
   const void* w2e = gu ? (fused ? nullptr : w2) : nullptr;
+  ExpertEpi epi{bias, gu ? bias2 : nullptr, gu ? act : LK_ACT_SILU, alpha, limit};
   return gemm(fmt, mode, rows, k, n, x16, scales, w, w2e, y, (cudaStream_t)stream, tile_info, rowmap, xrows, ku,
-              n_experts, stride, (gu && fused) ? rb * n : 0);
+              n_experts, stride, (gu && fused) ? rb * n : 0, nullptr, &epi);
+}
+
+int lk_moe_grouped_gemm(int fmt, int mode, int rows, int k, int n, int xrows, int ku, int n_experts, int fused,
+                        const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
+                        const void* w, const void* w2, float* y, lk_stream_t stream) {
+  return lk_moe_grouped_gemm_ex(fmt, mode, rows, k, n, xrows, ku, n_experts, fused, tile_info, rowmap, x16, scales, w,
+                                w2, nullptr, nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
 }
 
 int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8,
@@ -262,24 +296,36 @@ int lk_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, const uint8_t
   return gemm_mxfp4s(mode, order, rows, k, n, x8, s8, w, ws, w2, w2s, y, (cudaStream_t)stream);
 }
 
-int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
-                                  int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
-                                  const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
-                                  const uint8_t* w2s, float* y, lk_stream_t stream) {
+int lk_moe_grouped_gemm_mxfp4s_f8_ex(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
+                                     int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
+                                     const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
+                                     const uint8_t* w2s, const float* bias, const float* bias2, int act, float alpha,
+                                     float limit, float* y, lk_stream_t stream) {
   if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   if (order != LK_ORDER_PAIRS && order != LK_ORDER_SPLIT16) return LK_EINVAL;
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
+  if (!act_ok(act)) return LK_EINVAL;
   if (k % 32 || n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
   if (!tile_info || !rowmap || !x8 || !s8 || !w || !ws || !y) return LK_EINVAL;
   const bool gu = mode != LK_STORE;
   const bool two = gu && !fused;
   if (two && (!w2 || !w2s)) return LK_EINVAL;
+  if (gu && (!bias) != (!bias2)) return LK_EINVAL;
   if (!aligned(x8, 16) || !aligned(w, 16) || !aligned(y, 16) || (two && !aligned(w2, 16))) return LK_EALIGN;
   const int fuse = gu && fused;
+  ExpertEpi epi{bias, gu ? bias2 : nullptr, gu ? act : LK_ACT_SILU, alpha, limit};
   return gemm_mx(mode, order, rows, k, n, x8, s8, w, ws, two ? w2 : nullptr, two ? w2s : nullptr, y,
-                 (cudaStream_t)stream, tile_info, rowmap, xrows, ku, n_experts, fuse ? 2 * n : n, fuse ? n : 0);
+                 (cudaStream_t)stream, tile_info, rowmap, xrows, ku, n_experts, fuse ? 2 * n : n, fuse ? n : 0, &epi);
+}
+
+int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, int xrows, int ku, int n_experts,
+                                  int fused, const int32_t* tile_info, const int32_t* rowmap, const uint8_t* x8,
+                                  const float* s8, const uint8_t* w, const uint8_t* ws, const uint8_t* w2,
+                                  const uint8_t* w2s, float* y, lk_stream_t stream) {
+  return lk_moe_grouped_gemm_mxfp4s_f8_ex(mode, order, rows, k, n, xrows, ku, n_experts, fused, tile_info, rowmap, x8,
+                                          s8, w, ws, w2, w2s, nullptr, nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
 }
 
 int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
@@ -318,6 +364,39 @@ int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, c
   if (tokens == 0) return LK_OK;
   if (!ys || !wts || !y) return LK_EINVAL;
   return moe_combine(tokens, h, ku, accumulate, ys, wts, y, (cudaStream_t)stream);
+}
+
+int lk_moe_combine_gated(int tokens, int h, int ku, const float* ys, const float* wts, const float* sg, float* y,
+                         lk_stream_t stream) {
+  if (tokens < 0 || h <= 0 || ku <= 0 || ku > 8) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!ys || !wts || !sg || !y) return LK_EINVAL;
+  return moe_combine_g(tokens, h, ku, ys, nullptr, wts, sg, y, (cudaStream_t)stream);
+}
+
+int lk_moe_combine_sorted_gated(int tokens, int rows, int h, int ku, const float* ys, const int32_t* pos,
+                                const float* wts, const float* sg, float* y, lk_stream_t stream) {
+  if (tokens < 0 || rows <= 0 || h <= 0 || ku <= 0 || ku > 8) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!ys || !pos || !wts || !sg || !y) return LK_EINVAL;
+  return moe_combine_g(tokens, h, ku, ys, pos, wts, sg, y, (cudaStream_t)stream);
+}
+
+int lk_moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale,
+                  lk_stream_t stream) {
+  if (tokens < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!ids || !wts || !scale) return LK_EINVAL;
+  return moe_wscale(tokens, ku, n_experts, ids, wts, scale, (cudaStream_t)stream);
+}
+
+int lk_moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, lk_stream_t stream) {
+  if (tokens < 0 || h <= 0 || h % 32) return LK_EINVAL;
+  if (w_dtype != LK_F32 && w_dtype != LK_BF16) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!x || !w || !sg) return LK_EINVAL;
+  if (!aligned(x, 16) || !aligned(w, 8)) return LK_EALIGN;
+  return moe_shared_gate(tokens, h, x, w, w_dtype, sg, (cudaStream_t)stream);
 }
 
 }  // extern "C"

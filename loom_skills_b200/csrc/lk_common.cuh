@@ -294,6 +294,19 @@ inline bool once_per_device(unsigned& mask) {
 
 LK_DEV float silu(float g) { return g / (1.0f + __expf(-g)); }
 
+// The expert gate/up activation (gen_moe.py:27-64 act_scalar / act_vector; include/lk.h LK_ACT_*):
+//   LK_ACT_SILU        silu(g) * u
+//   LK_ACT_GELU        gelu_tanh(g) * u: 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))), GEGLU (make_kernel_tests.py:78-80)
+//   LK_ACT_SWIGLU_OAI  x = min(g, limit), y = clamp(u, -limit, limit): x sigmoid(alpha x) (y + 1)   (gpt-oss)
+LK_DEV float act_apply(int act, float g, float u, float alpha, float limit) {
+  if (act == LK_ACT_GELU) return 0.5f * g * (1.0f + tanhf(0.7978845608028654f * fmaf(0.044715f * g, g * g, g))) * u;
+  if (act == LK_ACT_SWIGLU_OAI) {
+    const float x = fminf(g, limit), y = fmaxf(fminf(u, limit), -limit);
+    return x / (1.0f + __expf(-alpha * x)) * (y + 1.0f);
+  }
+  return silu(g) * u;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // MoE schedule: 128-row super-tiles over the bucket's 64-row tiles
 // ---------------------------------------------------------------------------------------------------------------

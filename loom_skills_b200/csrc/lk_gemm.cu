@@ -2,18 +2,14 @@
 //
 // Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704, 706, 1224; dispatch gen_llm.py:4568-4622)
 // and the grouped expert GEMMs g_moe_ggu_{fmt}[_fused]_k{H} / g_moe_gdn_{fmt}_k{F} (gen_moe.py:1126-1228,
-// moe_q4_0.py:126-146):  Y = (X16 . W16^T) * inv[row]  (+ y | silu(G) * U).
+// moe_q4_0.py:126-146) with their bias / activation epilogue (gen_moe.py:958-1007):
+//   Y = (X16 . W16^T) * inv[row]  (+ y | act(G + bg, U + bu) | + bd).
 //
-// One CTA computes a 128-row x BN-column output tile (BN = 256; swiglu: 128 columns of each of gate and up):
-//   warp 0      producer: A tiles of X16 by 2-D TMA (128 rows x 64 k, 128-byte swizzle; MoE gate/up: TMA gather4 of
-//               the routed token rows) and the weights' packed bytes by one 2-D TMA box per 256 k (BN rows x 144
-//               bytes, the packed rows read as u32 columns; experts stacked as rows)
-//   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, M=128, N=256, K=16) from one lane
-//   warps 2-9   dequantise the packed bytes into f16 B tiles in the UMMA K-major 128-byte-swizzle layout -- the
-//               reference's one-rounding staging exactly (f16(d*(q-8)), f16(d*kvalue), fma_f16(q, f16(d*sc),
-//               f16(-dmin*m))) -- then run the epilogue: tcgen05.ld of the f32 accumulators, * inv[row], store.
-// Pipelines: A ring (4 x 16 KB), B ring (2 x 32 KB), packed-bytes ring (2 x 36 KB), each with full/empty mbarriers;
-// the tensor core reads shared memory the dequant warps wrote after a fence.proxy.async.
+// One persistent kernel (k_gemm_p, below) walks output tiles with warp-specialised roles: a TMA producer (A tiles of
+// X16, 128-byte swizzle -- MoE gate/up: TMA gather4 of the routed token rows -- and the weights' packed bytes, one
+// 2-D box of BN rows x 144 bytes per 256 k), an MMA issuer (tcgen05.mma kind::f16 from one lane, accumulators in
+// TMEM), dequantisation warps that write the reference's one-rounding f16 staging (f16(d*(q-8)), f16(d*kvalue),
+// fma_f16(q, f16(d*sc), f16(-dmin*m))) into the UMMA K-major 128-byte-swizzle B layout, and epilogue warps.
 #include <mutex>
 
 #include "lk_common.cuh"
@@ -22,9 +18,7 @@
 namespace lk {
 
 constexpr int kBM = 128, kBK = 64;
-constexpr int kSA = 4, kSR = 2;
 constexpr int kDqWarps = 8;
-constexpr int kGemmThreads = (2 + kDqWarps) * 32;
 
 enum { kDense = 0, kGather = 1, kSorted = 2 };
 
@@ -51,6 +45,7 @@ struct GemmArgs {
   // persistent dense store / acc: K split into ksplit ranges of kps packed stages (256 values) each; every range is
   // a tile of its own whose row-scaled partial product is added into y (zeroed first for store)
   int ksplit, kps;
+  ExpertEpi epi;              // gate/up activation and per-expert biases (bias index: expert * n + column)
 };
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
@@ -138,254 +133,6 @@ LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int
     out.z = hmul2u(hsub2u(h[2], koff), scale);
     out.w = hmul2u(hsub2u(h[3], koff), scale);
     *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
-  }
-}
-
-// stage counts for a tile configuration: 4 A stages, 2 packed-byte stages, as many B stages (2..4) as fit
-constexpr int gemm_sb(int a_bytes, int b_bytes, int r_bytes) {
-  return (220 * 1024 - 4 * a_bytes - 2 * r_bytes) / b_bytes >= 4 ? 4
-         : (220 * 1024 - 4 * a_bytes - 2 * r_bytes) / b_bytes >= 3 ? 3 : 2;
-}
-
-// MH: 128-row halves per tile (2 = a 256-row tile: two M=128 accumulators share every dequantised B stage, halving
-// the dequantisation per FLOP)
-template <int FMT, int BN, int NW, int MODE, int GROUP, int MH>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    k_gemm(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
-           const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
-  constexpr int kTM = kBM * MH;                   // tile rows
-  constexpr int kRowsB = BN * NW;                 // weight rows dequantised per stage
-  constexpr int kABytes = kTM * kBK * 2;
-  constexpr int kBBytes = kRowsB * kBK * 2;
-  constexpr int kRBytes = kRowsB * kChunkBytes;
-  constexpr int kSBt = gemm_sb(kABytes, kBBytes, kRBytes);
-  constexpr uint32_t kTmemCols = MH * NW * BN;    // 256
-  static_assert(kRowsB == 2 * kDqWarps * 16 || kRowsB == kDqWarps * 16, "one or two rows per dequant thread");
-  static_assert(kTmemCols == 256, "accumulator columns");
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = sA + kSA * kABytes;
-  uint8_t* sR = sB + kSBt * kBBytes;
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(sR + kSR * kRBytes);
-  uint64_t* empty_a = full_a + kSA;
-  uint64_t* full_b = empty_a + kSA;
-  uint64_t* empty_b = full_b + kSBt;
-  uint64_t* full_r = empty_b + kSBt;
-  uint64_t* empty_r = full_r + kSR;
-  uint64_t* acc_full = empty_r + kSR;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  int* tile_meta = reinterpret_cast<int*>(tmem_slot + 4);   // [0] expert, [1] first 64-row tile, [2] valid rows
-  int* arow = tile_meta + 4;                               // [128] gathered source rows (kGather)
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int kstages = p.k / kBK;
-
-  // ---- which rows: dense tile, or a 128-row super-tile of one expert made of <= 2 schedule tiles
-  int m0 = blockIdx.y * kTM;
-  int valid_rows = min(kTM, p.rows - m0);
-  int wrow = n0, w2row = n0 + p.w2_row_offset;   // first weight row of this tile in wmap / w2map
-  if (GROUP != kDense) {
-    // super-tile s = blockIdx.y (the A ring is free scratch until the first TMA load)
-    moe_super_tile(p.tile_info, p.max_tiles, p.n_experts, blockIdx.y, reinterpret_cast<int*>(sA), tile_meta);
-    if (tile_meta[0] < 0) return;   // no such super-tile: this launch had more CTAs than the schedule needs
-    int e = min(tile_meta[0], p.n_experts - 1);
-    m0 = tile_meta[1] * 64;
-    valid_rows = tile_meta[2];
-    wrow = e * p.rows_per_expert + n0;
-    w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
-    if (GROUP == kGather && threadIdx.x < kBM) {
-      int r = threadIdx.x;
-      int a = r < valid_rows ? p.rowmap[m0 + r] : -1;
-      arow[r] = a >= 0 ? a / p.ku : p.xrows;   // out-of-range row -> TMA fills zeros
-    }
-  }
-  const int nb_rows = min(BN, p.n - n0);
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSA; ++i) {
-      mbar_init(&full_a[i], 1);
-      mbar_init(&empty_a[i], 1);
-    }
-    for (int i = 0; i < kSBt; ++i) {
-      mbar_init(&full_b[i], kDqWarps);
-      mbar_init(&empty_b[i], 1);
-    }
-    for (int i = 0; i < kSR; ++i) {
-      mbar_init(&full_r[i], 1);
-      mbar_init(&empty_r[i], kDqWarps);
-    }
-    mbar_init(acc_full, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tensormap(&amap);
-      prefetch_tensormap(&wmap);
-      if (NW == 2) prefetch_tensormap(&w2map);
-    }
-    for (int ks = 0; ks < kstages; ++ks) {
-      if ((ks & 3) == 0) {
-        // the packed bytes of the next 256 k of all BN rows (x NW weights): one TMA box of BN rows x 144 bytes each
-        int c = ks >> 2, sr = c % kSR;
-        if (c >= kSR && !mbar_wait(&empty_r[sr], ((c / kSR) - 1) & 1)) atomicOr(&g_status, 1u);
-        if (lane == 0) {
-          mbar_expect_tx(&full_r[sr], uint32_t(kRBytes));
-          tma_load_2d(sR + sr * kRBytes, &wmap, c * (kChunkBytes / 4), wrow, &full_r[sr]);
-          if (NW == 2) tma_load_2d(sR + sr * kRBytes + BN * kChunkBytes, &w2map, c * (kChunkBytes / 4), w2row,
-                                   &full_r[sr]);
-        }
-        __syncwarp();
-      }
-      int sa = ks % kSA;
-      if (ks >= kSA && !mbar_wait(&empty_a[sa], ((ks / kSA) - 1) & 1)) atomicOr(&g_status, 1u);
-      if (GROUP == kGather) {
-        if (lane == 0) mbar_expect_tx(&full_a[sa], kABytes);
-        __syncwarp();
-        // 32 lanes x 4 rows: one gather4 each (row boxes of 64 f16 = 128 bytes)
-        int r = lane * 4;
-        tma_gather4(sA + sa * kABytes + r * 128, &amap, ks * kBK, arow[r], arow[r + 1], arow[r + 2], arow[r + 3],
-                    &full_a[sa]);
-      } else if (lane == 0) {
-        mbar_expect_tx(&full_a[sa], kABytes);
-        tma_load_2d(sA + sa * kABytes, &amap, ks * kBK, m0, &full_a[sa]);
-      }
-      __syncwarp();
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_f16(kBM, BN, 0);
-    const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
-    for (int ks = 0; ks < kstages; ++ks) {
-      int sa = ks % kSA, sb = ks % kSBt;
-      if (!mbar_wait(&full_a[sa], (ks / kSA) & 1)) atomicOr(&g_status, 1u);
-      if (!mbar_wait(&full_b[sb], (ks / kSBt) & 1)) atomicOr(&g_status, 1u);
-      tc_fence_after();
-      if (lane == 0) {
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-#pragma unroll
-          for (int mh = 0; mh < MH; ++mh) {
-            uint64_t ad = sdesc_k128(a_base + sa * kABytes + mh * (kBM * 128) + kk * 32);
-#pragma unroll
-            for (int wi = 0; wi < NW; ++wi) {
-              uint64_t bd = sdesc_k128(b_base + sb * kBBytes + wi * BN * 128 + kk * 32);
-              umma_f16(tmem + (mh * NW + wi) * BN, ad, bd, idesc, (ks | kk) != 0);
-            }
-          }
-        }
-        umma_commit(&empty_a[sa]);
-        umma_commit(&empty_b[sb]);
-        if (ks == kstages - 1) umma_commit(acc_full);
-      }
-      __syncwarp();
-    }
-  } else {
-    // ------------------------------------------------------------------ dequant warps, then the epilogue
-    const int dt = threadIdx.x - 64;   // 0..255
-    constexpr int kGroupsPerThread = kRowsB * 2 / (kDqWarps * 32);   // 2 (256 rows) or 1 (128 rows)
-    for (int ks = 0; ks < kstages; ++ks) {
-      int c = ks >> 2, sub = ks & 3, sr = c % kSR, sb = ks % kSBt;
-      if (sub == 0 && !mbar_wait(&full_r[sr], (c / kSR) & 1)) atomicOr(&g_status, 1u);
-      if (ks >= kSBt && !mbar_wait(&empty_b[sb], ((ks / kSBt) - 1) & 1)) atomicOr(&g_status, 1u);
-      uint8_t* bt = sB + sb * kBBytes;
-#pragma unroll
-      for (int gi = 0; gi < kGroupsPerThread; ++gi) {
-        int item = dt * kGroupsPerThread + gi;   // (row, half) pairs
-        int r = item >> 1, h = item & 1;
-        dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&full_b[sb]);
-        if (sub == 3) mbar_arrive(&empty_r[sr]);
-      }
-    }
-    // epilogue: warp quadrant q reads TMEM lanes 32q..32q+31 (rows of a 128-row half). With MH = 2 the two warps of
-    // a quadrant take one half each; with MH = 1 they split the columns.
-    if (!mbar_wait(acc_full, 0)) atomicOr(&g_status, 1u);
-    tc_fence_after();
-    const int q = warp & 3, pair = (warp - 2) >> 2;
-    const int mh = MH == 2 ? pair : 0;
-    const int row = mh * kBM + 32 * q + lane;
-    const bool row_ok = row < valid_rows;
-    float inv = 0.f;
-    if (row_ok) {
-      int grow = m0 + row;
-      int srow = grow;
-      if (GROUP == kGather) {
-        int a = p.rowmap[grow];
-        srow = a >= 0 ? a / p.ku : -1;
-      }
-      inv = srow >= 0 ? p.scales[2 * int64_t(srow) + 1] : 0.f;
-    }
-    constexpr int kColsPerWarp = MH == 2 ? BN : BN / 2;
-    const int col0 = MH == 2 ? 0 : pair * kColsPerWarp;
-    const uint32_t tbase = tmem + (uint32_t(32 * q) << 16) + mh * NW * BN;
-    // 32 x 32 blocks go through a per-warp staging tile in the (drained) A ring: written a row per lane, read back
-    // a quarter row per lane, so every store instruction covers four full 128-byte row segments. The block is
-    // stored to each destination (this rank's y, and the peers' for the all-gather form).
-    float* stg = reinterpret_cast<float*>(sA) + (warp - 2) * (32 * kStgStride);
-    const int sr = lane >> 3, sc = 4 * (lane & 7);
-#pragma unroll 1
-    for (int cb = 0; cb < kColsPerWarp; cb += 32) {
-      int col = col0 + cb;
-      float v[32];
-      tmem_ld32(tbase + col, v);
-      if (NW == 2) {
-        float u[32];
-        tmem_ld32(tbase + BN + col, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= inv;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(stg + lane * kStgStride + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-      __syncwarp();
-      const bool col_ok = col + sc < nb_rows;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int rr = 4 * j + sr;                       // row inside the warp's 32
-        const int trow = mh * kBM + 32 * q + rr;         // row inside the tile
-        float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
-        if (col_ok && trow < valid_rows) {
-          const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
-          if (MODE == LK_ACC) {
-            float4 old = *reinterpret_cast<const float4*>(p.dst[0] + off);
-            o.x += old.x;
-            o.y += old.y;
-            o.z += old.z;
-            o.w += old.w;
-          }
-#pragma unroll
-          for (int d = 0; d < kMaxPeers; ++d)
-            if (d < p.ndst) *reinterpret_cast<float4*>(p.dst[d] + off) = o;
-        }
-      }
-      __syncwarp();
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -622,6 +369,11 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
       int m0, n0, e, valid_rows;
       tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid_rows);
       const int nb_rows = min(BN, p.n - n0);
+      // rows stored: a dense tile's valid rows; a MoE super-tile's whole 64-row tiles (one, or two when paired),
+      // padding rows included -- their zero products give act(biases) -- as the reference's grouped tiles write
+      const int store_rows = GROUP == kDense ? valid_rows : (valid_rows > 64 ? 128 : 64);
+      const float* bcol = p.epi.bias ? p.epi.bias + int64_t(e) * p.n + n0 : nullptr;
+      const float* b2col = p.epi.bias2 ? p.epi.bias2 + int64_t(e) * p.n + n0 : nullptr;
       const int buf = li % NBUF;
       if (!mbar_wait(&acc_full[buf], (li / NBUF) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
@@ -642,8 +394,25 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
           if (NW == 2) {
             float u[32];
             tmem_ld32(tbase + BN + col, u);
+            if (bcol) {   // per-expert biases (columns past n read nothing: they are never stored)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+              for (int i = 0; i < 32; ++i) {
+                const bool in = col + i < nb_rows;
+                v[i] = fmaf(v[i], inv, in ? __ldg(bcol + col + i) : 0.f);
+                u[i] = fmaf(u[i], inv, in ? __ldg(b2col + col + i) : 0.f);
+              }
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = act_apply(p.epi.act, v[i], u[i], p.epi.alpha, p.epi.limit);
+            } else if (p.epi.act != LK_ACT_SILU) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = act_apply(p.epi.act, v[i] * inv, u[i] * inv, p.epi.alpha, p.epi.limit);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+            }
+          } else if (bcol) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = fmaf(v[i], inv, col + i < nb_rows ? __ldg(bcol + col + i) : 0.f);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= inv;
@@ -658,7 +427,7 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             const int rr = 4 * j + sr;
             const int trow = mh * kBM + 32 * q + rr;
             float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
-            if (col_ok && trow < valid_rows) {
+            if (col_ok && trow < store_rows) {
               const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
               if (GROUP == kDense && p.ksplit > 1) {   // one K range of several: add the partial
                 atomicAdd(reinterpret_cast<float4*>(p.dst[0] + off), o);
@@ -741,20 +510,6 @@ struct GemmMaps {
   CUtensorMap a, w, w2;
 };
 
-template <int FMT, int BN, int NW, int MODE, int GROUP, int MH>
-static int launch_gemm(const GemmMaps& m, const GemmArgs& a, dim3 grid, cudaStream_t s) {
-  constexpr int kRowsB = BN * NW;
-  constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2, kRBytes = kRowsB * kChunkBytes;
-  constexpr int smem = 1024 + kSA * kABytes + gemm_sb(kABytes, kBBytes, kRBytes) * kBBytes + kSR * kRBytes + 256 +
-                       32 + kBM * 4;
-  static_assert(smem <= 227 * 1024, "GEMM CTA exceeds shared memory");
-  auto kern = k_gemm<FMT, BN, NW, MODE, GROUP, MH>;
-  static unsigned configured = 0;
-  if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<grid, kGemmThreads, smem, s>>>(m.a, m.w, m.w2, a);
-  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
-}
-
 template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP>
 static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
@@ -818,9 +573,10 @@ static int choose_ksplit(int tiles, int kp, int sms) {
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
-         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out) {
+         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out, const ExpertEpi* epi) {
   GemmArgs a{};
   a.scales = scales;
+  if (epi) a.epi = *epi;
   if (out) {
     for (int d = 0; d < out->ndst; ++d) a.dst[d] = out->dst[d];
     a.ndst = out->ndst;

@@ -6,6 +6,17 @@
 
 namespace lk {
 
+// What a MoE expert kernel applies after its products: the activation of a gate/up pair (LK_ACT_*) and per-expert
+// output biases ([n_experts][n] f32; bias: the gate's (gate/up) or the down projection's, bias2: the up projection's),
+// as the reference's bias epilogues (gen_moe.py:958-1007 _gemm_bias_act; expert_mv(bias=...), gen_moe.py:535).
+// Zero-initialised: SiLU, no biases.
+struct ExpertEpi {
+  const float* bias;
+  const float* bias2;
+  int act;
+  float alpha, limit;
+};
+
 int dequant(int fmt, const void* w, const void* ws, int64_t n_values, void* out, int out_dtype, cudaStream_t s);
 int row_scale(int rows, int k, const void* x, int x_dtype, float* scales, uint16_t* x16, uint8_t* x8, float* s8,
               cudaStream_t s);
@@ -32,6 +43,7 @@ struct MvArgs {
   int rows_per_expert2;   // weight rows of one expert in w2
   int w2_row_offset;      // first row of the second weight inside an expert (fused gate/up: n; else 0)
   int swiglu;
+  ExpertEpi epi;          // MoE mode: activation and per-expert biases (dense: SiLU, no biases)
 };
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
 
@@ -44,17 +56,19 @@ struct OutSpec {
 };
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
-         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out = nullptr);
+         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out = nullptr,
+         const ExpertEpi* epi = nullptr);
 
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
 // decode expert matvecs over MXFP4S experts (lk_mvmx.cu)
 int moe_expert_mv_mx(int mode, int order, int n, int k, int assignments, int ku, int n_experts, const int32_t* ids,
-                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s);
+                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s,
+                     const ExpertEpi* epi = nullptr);
 int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
-            int w2_row_offset);
+            int w2_row_offset, const ExpertEpi* epi = nullptr);
 
 int moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,
               const void* router_w, int w_dtype, const float* bias, int32_t* ids, float* wts, cudaStream_t s);
@@ -64,6 +78,11 @@ int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, cons
                        const float* wts, float* y, cudaStream_t s);
 int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                 cudaStream_t s);
+// shared_gated combines (sg != nullptr: y = sg * y + sum), the down-scale fold and the shared-expert gate
+int moe_combine_g(int tokens, int h, int ku, const float* ys, const int32_t* pos, const float* wts, const float* sg,
+                  float* y, cudaStream_t s);
+int moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale, cudaStream_t s);
+int moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, cudaStream_t s);
 
 // int8-activation decode path (xq: codes [rows][k] int8, then [rows][k/32][2] f32 meta)
 int quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, cudaStream_t s);

@@ -4,6 +4,9 @@
 // g_moe_bucket                   gen_moe.py:829-955             tile_info / rowmap / pos
 // g_moe_combine_sorted           gen_moe.py:1231-1280           y[t] (+)= sum_k w[t,k] ys[pos[t,k]]
 // g_moe_combine                  gen_moe.py:730-762             y[t] (+)= sum_k w[t,k] ys[t*KU + k]
+// shared_gated                   gen_moe.py:765-777             y[t] = sg[t] y[t] + sum_k ...
+// g_moe_wscale                   gen_moe.py:1010-1045           w[t,k] *= scale[ids[t,k]]
+// g_moe_shared_gate              gen_moe.py:780-823             sg[t] = sigmoid(x[t] . w)
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
@@ -337,10 +340,11 @@ int moe_bucket(int tokens, int ku, int E, int max_tiles, const int32_t* info, co
 // h / 256 CTAs, so a decode token's combine is not one CTA walking h); the fma chain runs over k in order, as the
 // reference's
 // ---------------------------------------------------------------------------------------------------------------
+// sg != nullptr (shared_gated, gen_moe.py:765-777): the shared experts' output in y is scaled by the token's gate first
 template <bool SORTED>
 __global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, const float* __restrict__ ys,
                                                  const int32_t* __restrict__ pos, const float* __restrict__ wts,
-                                                 float* __restrict__ y) {
+                                                 const float* __restrict__ sg, float* __restrict__ y) {
   const int t = blockIdx.x;
   __shared__ float w[8];
   __shared__ int p[8];
@@ -352,6 +356,7 @@ __global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, 
   const int c = blockIdx.y * 256 + threadIdx.x;
   if (c >= h) return;
   float acc = accumulate ? y[int64_t(t) * h + c] : 0.f;
+  if (sg) acc *= sg[t];
   for (int k = 0; k < ku; ++k) {
     float v = p[k] >= 0 ? ys[int64_t(p[k]) * h + c] : 0.f;
     acc = fmaf(w[k], v, acc);
@@ -362,13 +367,73 @@ __global__ void __launch_bounds__(256) k_combine(int h, int ku, int accumulate, 
 int moe_combine_sorted(int tokens, int rows, int h, int ku, int accumulate, const float* ys, const int32_t* pos,
                        const float* wts, float* y, cudaStream_t s) {
   (void)rows;
-  k_combine<true><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, pos, wts, y);
+  k_combine<true><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, pos, wts, nullptr, y);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                 cudaStream_t s) {
-  k_combine<false><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, nullptr, wts, y);
+  k_combine<false><<<dim3(tokens, (h + 255) / 256), 256, 0, s>>>(h, ku, accumulate, ys, nullptr, wts, nullptr, y);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+int moe_combine_g(int tokens, int h, int ku, const float* ys, const int32_t* pos, const float* wts, const float* sg,
+                  float* y, cudaStream_t s) {
+  const dim3 grid(tokens, (h + 255) / 256);
+  if (pos) k_combine<true><<<grid, 256, 0, s>>>(h, ku, 1, ys, pos, wts, sg, y);
+  else k_combine<false><<<grid, 256, 0, s>>>(h, ku, 1, ys, nullptr, wts, sg, y);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// g_moe_wscale (gen_moe.py:1010-1045): wts[t][k] *= scale[ids[t][k]], one thread per assignment
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_wscale(int assignments, int E, const int32_t* __restrict__ ids,
+                                                float* __restrict__ wts, const float* __restrict__ scale) {
+  const int a = blockIdx.x * 256 + threadIdx.x;
+  if (a >= assignments) return;
+  const int e = min(max(ids[a], 0), E - 1);
+  wts[a] *= scale[e];
+}
+
+int moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale, cudaStream_t s) {
+  const int a = tokens * ku;
+  k_wscale<<<(a + 255) / 256, 256, 0, s>>>(a, n_experts, ids, wts, scale);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// g_moe_shared_gate (gen_moe.py:780-823): sg[t] = sigmoid(x[t] . w), one warp per token (8 per CTA), each lane over
+// 4-value slices of h, f32 accumulation
+// ---------------------------------------------------------------------------------------------------------------
+template <bool BF16W>
+__global__ void __launch_bounds__(256) k_shared_gate(int tokens, int h, const float* __restrict__ x,
+                                                     const void* __restrict__ w, float* __restrict__ sg) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const float* xr = x + t * h;
+  float acc = 0.f;
+  for (int i = lane * 4; i < h; i += 128) {
+    const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + i));
+    float4 wv;
+    if (BF16W) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(w) + i));
+      wv = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xffff0000u));
+    } else {
+      wv = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(w) + i));
+    }
+    acc = fmaf(xv.x, wv.x, fmaf(xv.y, wv.y, fmaf(xv.z, wv.z, fmaf(xv.w, wv.w, acc))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) sg[t] = 1.0f / (1.0f + expf(-acc));
+}
+
+int moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, cudaStream_t s) {
+  if (w_dtype == LK_BF16) k_shared_gate<true><<<(tokens + 7) / 8, 256, 0, s>>>(tokens, h, x, w, sg);
+  else k_shared_gate<false><<<(tokens + 7) / 8, 256, 0, s>>>(tokens, h, x, w, sg);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 

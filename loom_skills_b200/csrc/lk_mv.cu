@@ -278,10 +278,10 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * kMvRows;
   int wrow = r0, w2row = r0 + a.w2_row_offset;
-  int xrow0, ntok, yrow0;
+  int xrow0, ntok, yrow0, e = 0;
   if (MOE) {
     int asg = blockIdx.y;
-    int e = min(max(a.ids[asg], 0), a.n_experts - 1);
+    e = min(max(a.ids[asg], 0), a.n_experts - 1);
     wrow = e * a.rows_per_expert + r0;
     w2row = e * a.rows_per_expert2 + a.w2_row_offset + r0;
     xrow0 = asg / a.x_div;
@@ -381,7 +381,12 @@ __global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUten
     int row = r0 + g + (i >= 2 ? 8 : 0);
     int tok = 2 * tig + (i & 1);
     if (row >= a.n || tok >= ntok) continue;
-    float v = SWIGLU ? silu(out[0][i]) * out[NW - 1][i] : out[0][i];
+    float g = out[0][i], u = out[NW - 1][i];
+    if (MOE && a.epi.bias) {   // per-expert output biases (gen_moe.py:535 expert_mv bias=True)
+      g += __ldg(a.epi.bias + int64_t(e) * a.n + row);
+      if (SWIGLU) u += __ldg(a.epi.bias2 + int64_t(e) * a.n + row);
+    }
+    float v = SWIGLU ? act_apply(a.epi.act, g, u, a.epi.alpha, a.epi.limit) : g;
     float* yp = a.y + int64_t(yrow0 + tok) * a.n + row;
     *yp = a.accumulate ? *yp + v : v;
   }

@@ -1,8 +1,8 @@
 // Decode expert matvecs for MXFP4S experts: the reference's expert_mv (gen_moe.py:535-727) over the MXFP4S weight
 // format (split planes, gen_llm.py:844-895), f32 accumulation of f32 activations as its decode path does.
-//   mode 0 (gate/up; expert e holds f gate rows, then f up rows): act[a][j] = silu(g) * u,
+//   mode 0 (gate/up; expert e holds f gate rows, then f up rows): act[a][j] = act(g + bg, u + bu) (SiLU default),
 //          g = Wg[e][j] . x[a / ku], u = Wu[e][j] . x[a / ku]
-//   mode 1 (down; expert e holds h rows):                        y[a][j] = Wd[e][j] . x[a]
+//   mode 1 (down; expert e holds h rows):                        y[a][j] = Wd[e][j] . x[a] (+ bd)
 // with e = ids[a] and W the exact MXFP4 values: e2m1 code * 2^(s - 127), s the row's E8M0 byte of the 32-value block.
 //
 // Design. One CTA per (16 output rows, assignment); a warp computes 2 of the rows (a gate/up pair counts as one). The
@@ -35,6 +35,7 @@ struct MxMvArgs {
   float* y;             // [assignments][n]
   const int32_t* ids;   // expert of each assignment
   int n, k, x_div, n_experts, rows_per_expert, x_dtype;
+  ExpertEpi epi;        // gate/up activation, per-expert biases [n_experts][n]
 };
 
 // f16 bit patterns of the 2 nibbles held in the low 4 bits of each 16-bit half of r: value * 2^-14, sign included
@@ -158,7 +159,14 @@ __global__ void __launch_bounds__(kMxMvWarps * 32, 2) k_moe_mv_mx(const MxMvArgs
         acc[wi] = warp_sum(acc[wi]) * 16384.0f;
       }
       const int j = j0 + r0 + r;
-      if (lane == 0 && j < p.n) p.y[int64_t(a) * p.n + j] = MODE == 0 ? silu(acc[0]) * acc[NW - 1] : acc[0];
+      if (lane == 0 && j < p.n) {
+        float g = acc[0], u = acc[NW - 1];
+        if (p.epi.bias) {   // per-expert output biases (gpt-oss ffn_{gate,up,down}_exps.bias)
+          g += __ldg(p.epi.bias + int64_t(e) * p.n + j);
+          if (MODE == 0) u += __ldg(p.epi.bias2 + int64_t(e) * p.n + j);
+        }
+        p.y[int64_t(a) * p.n + j] = MODE == 0 ? act_apply(p.epi.act, g, u, p.epi.alpha, p.epi.limit) : g;
+      }
     }
   }
 }
@@ -180,8 +188,10 @@ int launch_mx_mv(const MxMvArgs& a, int assignments, cudaStream_t s) {
 }  // namespace
 
 int moe_expert_mv_mx(int mode, int order, int n, int k, int assignments, int ku, int n_experts, const int32_t* ids,
-                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s) {
+                     const void* x, int x_dtype, const uint8_t* w, const uint8_t* ws, float* y, cudaStream_t s,
+                     const ExpertEpi* epi) {
   MxMvArgs a{};
+  if (epi) a.epi = *epi;
   a.w = w;
   a.ws = ws;
   a.x = x;

@@ -51,7 +51,37 @@ struct MxArgs {
   const int32_t* tile_info;
   const int32_t* rowmap;
   int max_tiles, xrows, ku, n_experts;
+  ExpertEpi epi;                // gate/up activation and per-expert biases (bias index: expert * n + column)
 };
+
+// The epilogue of 32 columns of one row: row scale, then act(g + bg, u + bu) (gate/up) or + bd (single weight), the
+// biases of columns c0 .. c0 + 31 read where c0 + i < ncols (bias rows: the expert's, already offset)
+template <int NW>
+LK_DEV void mx_epilogue32(float (&v)[32], const float (&u)[32], float inv, const ExpertEpi& epi, const float* bcol,
+                          const float* b2col, int c0, int ncols) {
+  if (NW == 2) {
+    if (bcol) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const bool in = c0 + i < ncols;
+        v[i] = act_apply(epi.act, fmaf(v[i], inv, in ? __ldg(bcol + c0 + i) : 0.f),
+                         fmaf(u[i], inv, in ? __ldg(b2col + c0 + i) : 0.f), epi.alpha, epi.limit);
+      }
+    } else if (epi.act != LK_ACT_SILU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = act_apply(epi.act, v[i] * inv, u[i] * inv, epi.alpha, epi.limit);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
+    }
+  } else if (bcol) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = fmaf(v[i], inv, c0 + i < ncols ? __ldg(bcol + c0 + i) : 0.f);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= inv;
+  }
+}
 
 // split16 block bytes (element i low nibble of byte i, element i+16 high nibble) -> pairs order (element 2j low,
 // 2j+1 high nibble of byte j), for one 32-value block held in 4 words
@@ -260,8 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3, half = (warp - 2) >> 2;
     const int row = 32 * q + lane;
     const bool ok = row < valid_rows;
+    // rows stored: a MoE super-tile's whole 64-row tiles, padding rows included (act of the biases, zero without)
+    const bool store = GROUP == kDense ? ok : row < (valid_rows > 64 ? 128 : 64);
     float inv = 0.f;
-    float* yrow = nullptr;
+    float* yrow = store ? p.y + int64_t(m0 + row) * p.n + n0 : nullptr;
     if (ok) {
       int grow = m0 + row;
       int srow = grow;
@@ -270,25 +302,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         srow = a >= 0 ? a / p.ku : -1;
       }
       inv = srow >= 0 ? p.s8[2 * int64_t(srow) + 1] * 256.0f : 0.f;   // 2^8: the reference's weight pre-scale
-      yrow = p.y + int64_t(grow) * p.n + n0;
     }
+    const float* bcol = p.epi.bias ? p.epi.bias + int64_t(expert) * p.n + n0 : nullptr;
+    const float* b2col = p.epi.bias2 ? p.epi.bias2 + int64_t(expert) * p.n + n0 : nullptr;
     constexpr int kCols = BN / 2;
     const uint32_t tbase = tmem + (uint32_t(32 * q) << 16);
 #pragma unroll 1
     for (int cb = 0; cb < kCols; cb += 32) {
       int col = half * kCols + cb;
-      float v[32];
+      float v[32], u[32];
       tmem_ld32(tbase + col, v);
-      if (NW == 2) {
-        float u[32];
-        tmem_ld32(tbase + BN + col, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= inv;
-      }
-      if (ok) {
+      if (NW == 2) tmem_ld32(tbase + BN + col, u);
+      mx_epilogue32<NW>(v, u, inv, p.epi, bcol, b2col, col, nb_rows);
+      if (store) {
         if ((p.n & 3) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
@@ -381,6 +407,7 @@ struct MxpArgs {
   const int32_t* rowmap;
   int max_tiles, xrows, ku, n_experts;
   int rows_per_expert, rows_per_expert2, w2_row_offset;
+  ExpertEpi epi;          // gate/up activation and per-expert biases (bias index: expert * n + column)
 };
 
 template <int NW, int GROUP>
@@ -595,6 +622,10 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
       tile_of(t, m0, vrows, e, n0);
       const int r = 32 * qd + lane;
       const bool ok = r < vrows;
+      // rows stored: a MoE super-tile's whole 64-row tiles (padding rows give act of the biases, zero without)
+      const int srows = GROUP == kDense ? vrows : (vrows > 64 ? 128 : 64);
+      const float* bcol = p.epi.bias ? p.epi.bias + int64_t(e) * p.n + n0 : nullptr;
+      const float* b2col = p.epi.bias2 ? p.epi.bias2 + int64_t(e) * p.n + n0 : nullptr;
       const int row = m0 + r;   // output row (grouped: sorted position)
       int srow = row;           // its activation scale row (gather: the token)
       if (GROUP == kGather && ok) {
@@ -608,25 +639,20 @@ __global__ void __launch_bounds__(kMxpThreads, 1)
       const uint32_t tb = tmem + uint32_t(b) * kMxpAcc1 + (uint32_t(32 * qd) << 16);
 #pragma unroll 1
       for (int c = 0; c < BNW; c += 32) {
-        float v[32];
+        float v[32], u[32];
         tmem_ld32(tb + c, v);
-        if (NW == 2) {
-          float u[32];
-          tmem_ld32(tb + BNW + c, u);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = silu(v[i] * inv) * (u[i] * inv);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= inv;
-        }
+        if (NW == 2) tmem_ld32(tb + BNW + c, u);
+        mx_epilogue32<NW>(v, u, inv, p.epi, bcol, b2col, c, p.n - n0);
         if (c + 32 >= BNW) {   // the tile's last TMEM read is done: hand the accumulator back to the MMA warp
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acce[b]);
         }
-        // the TMA store clips rows past p.rows and columns past n; a grouped tile's rows past vrows belong to the
-        // next super-tile, so a warp with any of those stores its own rows
-        if (GROUP == kDense || 32 * qd + 31 < vrows) {
+        // the TMA store clips rows past p.rows and columns past n; a grouped super-tile owns its whole 64-row tiles
+        // (srows, a multiple of 32), the rows past them belong to the next super-tile: its warps past srows store
+        // nothing
+        if (GROUP != kDense && 32 * qd >= srows) continue;
+        if (GROUP == kDense || 32 * qd + 31 < srows) {
           if (m0 + 32 * qd >= p.rows || n0 + c >= p.n) continue;   // nothing of this block is in the output
           if (lane == 0) bulk_wait_group_read0();   // this warp's previous block has left the staging tile
           __syncwarp();
@@ -697,11 +723,12 @@ int launch_mxp(const CUtensorMap* m, const MxpArgs& a, int grid, cudaStream_t s)
 int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
              const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
              const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
-             int w2_row_offset) {
+             int w2_row_offset, const ExpertEpi* epi) {
   const int NW = mode == LK_STORE ? 1 : 2;   // swiglu: gathered or sorted gate/up rows
   const int bnw = kMxpNT / NW;
   const int group = tile_info ? (mode == LK_SWIGLU ? kGather : kSorted) : kDense;
   MxpArgs a{};
+  if (epi) a.epi = *epi;
   a.s8 = s8;
   a.y = y;
   a.ws = ws;
@@ -757,13 +784,14 @@ int gemm_mxp(int mode, int rows, int k, int n, const uint8_t* x8, const float* s
 int gemm_mx(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
             const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s,
             const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku, int n_experts, int rows_per_expert,
-            int w2_row_offset) {
+            int w2_row_offset, const ExpertEpi* epi) {
   if (mxp_applies(order, k, w, ws, w2, w2s))
     return gemm_mxp(mode, rows, k, n, x8, s8, w, ws, w2, w2s, y, s, tile_info, rowmap, xrows, ku, n_experts,
-                    rows_per_expert, w2_row_offset);
+                    rows_per_expert, w2_row_offset, epi);
   const int NW = mode == LK_STORE ? 1 : 2;
   const int bn = kRowsB / NW;
   MxArgs a{};
+  if (epi) a.epi = *epi;
   a.s8 = s8;
   a.y = y;
   a.rows = rows;

@@ -27,18 +27,40 @@ constexpr size_t kNaBytes = kNaActBytes + kNaYsBytes + kNaIdsBytes + kNaWtsBytes
 // weight, the matvecs store (not accumulate) every activation and expert output before the combine reads them.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
 
+// The driver's current context, through the runtime's driver entry point (liblk links only the runtime)
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 // Address of the array on the current device, looked up once per device (cudaGetSymbolAddress, with that device
-// current). The first call on a device must come before any stream capture.
+// current) and again whenever the device's context is no longer the one it was looked up in (after a
+// cudaDeviceReset the runtime makes a new primary context, where the array has a new address). The first call on a
+// device, and the first after a reset, must come before any stream capture.
 int scratch_on_current_device(unsigned char** out) {
   static std::mutex mu;
   static unsigned char* ptrs[64] = {};
+  static CUcontext ctxs[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LK_ECUDA;
+  const CUcontext ctx = current_context();   // null before the runtime has made the device's context current
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || !ctx || ctxs[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return LK_ECUDA;
     ptrs[dev] = static_cast<unsigned char*>(p);
+    ctxs[dev] = current_context();   // the context the lookup ran in (made current by it if none was)
   }
   *out = ptrs[dev];
   return LK_OK;

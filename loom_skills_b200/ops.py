@@ -15,7 +15,12 @@ order and meaning follow the reference's kernel launch signatures (paths relativ
                                                                           %x, %scales, %w[, %w2], %y)
   moe_combine_sorted g_moe_combine_sorted         gen_moe.py:1231-1280   (%tokens, %rows, %ys, %pos, %wts, %y)
   moe_expert_mv      g_moe_gu_* / g_moe_dn_*      gen_moe.py:535-727
-  moe_combine        g_moe_combine                gen_moe.py:730-762
+  moe_combine        g_moe_combine                gen_moe.py:730-762     (+ shared_gated, gen_moe.py:765-777)
+  moe_wscale         g_moe_wscale                 gen_moe.py:1010-1045   (%tokens, %ids, %wts, %scale)
+  moe_shared_gate    g_moe_shared_gate            gen_moe.py:780-823     (%tokens, %x, %w, %sg)
+
+The MoE expert kernels take the reference's activation choice (act: "silu", "gelu" -- GEGLU --, "swiglu_oai") and
+per-expert output biases (gen_moe.py:958-1007, expert_mv bias=True).
 
 Errors raise LkError (the C ABI's negative return codes). There is no CPU fallback: tensors must be on a CUDA device.
 """
@@ -36,6 +41,14 @@ def _ptr(t):
 
 def _stream():
     return torch.cuda.current_stream().cuda_stream
+
+
+def _act(act):
+    return L.ACT_IDS[act] if isinstance(act, str) else int(act)
+
+
+def _f32c(t):
+    return None if t is None else t.contiguous().float()
 
 
 def _cuda(*ts):
@@ -181,43 +194,56 @@ def moe_bucket(ids, n_experts, max_tiles=None, info=None):
     return ti, rm, pos
 
 
-def moe_grouped_gemm(fmt, mode, tile_info, rowmap, x16, scales, w, n, ku, n_experts, fused=False, w2=None, y=None):
+def moe_grouped_gemm(fmt, mode, tile_info, rowmap, x16, scales, w, n, ku, n_experts, fused=False, w2=None, y=None,
+                     act="silu", bias=None, bias2=None, alpha=1.702, limit=7.0):
     """Grouped expert GEMM over the bucketed 64-row tiles. mode 'swiglu' (gate/up, x16 = token rows, gathered),
     'swiglu_sorted' (gate/up, x16 = sorted rows from moe_row_scale_gather) or 'store' (down, x16 = sorted rows).
-    y: [max_tiles*64][n]."""
-    _cuda(tile_info, rowmap, x16, scales, w, w2, y)
+    act / bias (gate, or down) / bias2 (up): the expert activation and per-expert biases [n_experts][n].
+    y: [max_tiles*64][n]; every row of a live 64-row tile is written, no row of a dead tile."""
+    _cuda(tile_info, rowmap, x16, scales, w, w2, y, bias, bias2)
     rows = rowmap.shape[0]
     xrows, k = x16.shape
     if y is None:
         y = torch.empty(rows, n, dtype=torch.float32, device=x16.device)
     m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
-    L.check(L.load().lk_moe_grouped_gemm(_fmt(fmt), m, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
-                                         _ptr(tile_info), _ptr(rowmap), _ptr(x16), _ptr(scales), _ptr(w), _ptr(w2),
-                                         _ptr(y), _stream()), "lk_moe_grouped_gemm")
+    bias, bias2 = _f32c(bias), _f32c(bias2)
+    L.check(L.load().lk_moe_grouped_gemm_ex(_fmt(fmt), m, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
+                                            _ptr(tile_info), _ptr(rowmap), _ptr(x16), _ptr(scales), _ptr(w), _ptr(w2),
+                                            _ptr(bias), _ptr(bias2), _act(act), alpha, limit, _ptr(y), _stream()),
+            "lk_moe_grouped_gemm_ex")
     return y
 
 
 def moe_grouped_gemm_mxfp4s_f8(mode, tile_info, rowmap, x8, s8, w, ws, n, ku, n_experts, fused=False, w2=None,
-                               w2s=None, order=L.ORDER_PAIRS, y=None):
-    """MXFP4 x e4m3 grouped expert GEMM over the bucketed 64-row tiles; operands as gemm_mxfp4s_f8, rows and tiles
-    as moe_grouped_gemm (gate/up: x8/s8 are token rows; down: sorted rows)."""
-    _cuda(tile_info, rowmap, x8, s8, w, ws, w2, w2s, y)
+                               w2s=None, order=L.ORDER_PAIRS, y=None, act="silu", bias=None, bias2=None, alpha=1.702,
+                               limit=7.0):
+    """MXFP4 x e4m3 grouped expert GEMM over the bucketed 64-row tiles; operands as gemm_mxfp4s_f8, rows, tiles,
+    activation and biases as moe_grouped_gemm (gate/up: x8/s8 are token rows; down: sorted rows)."""
+    _cuda(tile_info, rowmap, x8, s8, w, ws, w2, w2s, y, bias, bias2)
     rows = rowmap.shape[0]
     xrows, k = x8.shape
     if y is None:
         y = torch.empty(rows, n, dtype=torch.float32, device=x8.device)
     m = L.MODE_IDS[mode] if isinstance(mode, str) else int(mode)
-    L.check(L.load().lk_moe_grouped_gemm_mxfp4s_f8(m, order, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
-                                                   _ptr(tile_info), _ptr(rowmap), _ptr(x8), _ptr(s8), _ptr(w),
-                                                   _ptr(ws), _ptr(w2), _ptr(w2s), _ptr(y), _stream()),
-            "lk_moe_grouped_gemm_mxfp4s_f8")
+    bias, bias2 = _f32c(bias), _f32c(bias2)
+    L.check(L.load().lk_moe_grouped_gemm_mxfp4s_f8_ex(m, order, rows, k, n, xrows, ku, n_experts, 1 if fused else 0,
+                                                      _ptr(tile_info), _ptr(rowmap), _ptr(x8), _ptr(s8), _ptr(w),
+                                                      _ptr(ws), _ptr(w2), _ptr(w2s), _ptr(bias), _ptr(bias2),
+                                                      _act(act), alpha, limit, _ptr(y), _stream()),
+            "lk_moe_grouped_gemm_mxfp4s_f8_ex")
     return y
 
 
-def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False):
-    _cuda(ys, pos, wts, y)
+def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False, sg=None):
+    """y[t] (+)= sum_k wts[t,k] ys[pos[t,k]]; sg (shared_gated): y[t] = sg[t] y[t] + ... (y holds the shared output)."""
+    _cuda(ys, pos, wts, y, sg)
     tokens, ku = wts.shape
     rows, h = ys.shape
+    if sg is not None:
+        L.check(L.load().lk_moe_combine_sorted_gated(tokens, rows, h, ku, _ptr(ys), _ptr(pos), _ptr(wts),
+                                                     _ptr(sg.contiguous().float()), _ptr(y), _stream()),
+                "lk_moe_combine_sorted_gated")
+        return y
     if y is None:
         y = torch.empty(tokens, h, dtype=torch.float32, device=ys.device)
     L.check(L.load().lk_moe_combine_sorted(tokens, rows, h, ku, 1 if accumulate else 0, _ptr(ys), _ptr(pos),
@@ -225,37 +251,48 @@ def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False):
     return y
 
 
-def moe_expert_mv(fmt, mode, ids, x, w, n, k, ku, n_experts, fused=True, w2=None, y=None):
-    """Decode expert matvecs per assignment: mode 'gu' -> silu(Wg x) * (Wu x); 'dn' -> Wd x."""
-    _cuda(ids, x, w, w2, y)
+def moe_expert_mv(fmt, mode, ids, x, w, n, k, ku, n_experts, fused=True, w2=None, y=None, act="silu", bias=None,
+                  bias2=None, alpha=1.702, limit=7.0):
+    """Decode expert matvecs per assignment: mode 'gu' -> act(Wg x + bg, Wu x + bu); 'dn' -> Wd x (+ bd)."""
+    _cuda(ids, x, w, w2, y, bias, bias2)
     a = ids.numel()
     if y is None:
         y = torch.empty(a, n, dtype=torch.float32, device=x.device)
     md = 0 if mode == "gu" else 1
-    L.check(L.load().lk_moe_expert_mv(_fmt(fmt), md, n, k, a, ku, n_experts, 1 if fused else 0, _ptr(ids),
-                                      _ptr(x.contiguous()), _DT[x.dtype], _ptr(w), _ptr(w2), _ptr(y), _stream()),
-            "lk_moe_expert_mv")
+    bias, bias2 = _f32c(bias), _f32c(bias2)
+    L.check(L.load().lk_moe_expert_mv_ex(_fmt(fmt), md, n, k, a, ku, n_experts, 1 if fused else 0, _ptr(ids),
+                                         _ptr(x.contiguous()), _DT[x.dtype], _ptr(w), _ptr(w2), _ptr(bias),
+                                         _ptr(bias2), _act(act), alpha, limit, _ptr(y), _stream()),
+            "lk_moe_expert_mv_ex")
     return y
 
 
-def moe_expert_mv_mxfp4s(mode, ids, x, w, ws, n, k, ku, n_experts, order=L.ORDER_PAIRS, y=None):
+def moe_expert_mv_mxfp4s(mode, ids, x, w, ws, n, k, ku, n_experts, order=L.ORDER_PAIRS, y=None, act="silu",
+                         bias=None, bias2=None, alpha=1.702, limit=7.0):
     """Decode expert matvecs over MXFP4S experts per assignment: mode 'gu' (per expert n gate rows then n up rows)
-    -> silu(Wg x) * (Wu x); 'dn' -> Wd x. w / ws: the stacked nibble and E8M0 planes."""
-    _cuda(ids, x, w, ws, y)
+    -> act(Wg x + bg, Wu x + bu); 'dn' -> Wd x (+ bd). w / ws: the stacked nibble and E8M0 planes."""
+    _cuda(ids, x, w, ws, y, bias, bias2)
     a = ids.numel()
     if y is None:
         y = torch.empty(a, n, dtype=torch.float32, device=x.device)
     md = 0 if mode == "gu" else 1
-    L.check(L.load().lk_moe_expert_mv_mxfp4s(md, int(order), n, k, a, ku, n_experts, _ptr(ids), _ptr(x.contiguous()),
-                                             _DT[x.dtype], _ptr(w), _ptr(ws), _ptr(y), _stream()),
-            "lk_moe_expert_mv_mxfp4s")
+    bias, bias2 = _f32c(bias), _f32c(bias2)
+    L.check(L.load().lk_moe_expert_mv_mxfp4s_ex(md, int(order), n, k, a, ku, n_experts, _ptr(ids),
+                                                _ptr(x.contiguous()), _DT[x.dtype], _ptr(w), _ptr(ws), _ptr(bias),
+                                                _ptr(bias2), _act(act), alpha, limit, _ptr(y), _stream()),
+            "lk_moe_expert_mv_mxfp4s_ex")
     return y
 
 
-def moe_combine(ys, wts, y=None, accumulate=False):
-    _cuda(ys, wts, y)
+def moe_combine(ys, wts, y=None, accumulate=False, sg=None):
+    """y[t] (+)= sum_k wts[t,k] ys[t*ku + k]; sg (shared_gated): y[t] = sg[t] y[t] + ... (y holds the shared output)."""
+    _cuda(ys, wts, y, sg)
     tokens, ku = wts.shape
     h = ys.shape[1]
+    if sg is not None:
+        L.check(L.load().lk_moe_combine_gated(tokens, h, ku, _ptr(ys), _ptr(wts), _ptr(sg.contiguous().float()),
+                                              _ptr(y), _stream()), "lk_moe_combine_gated")
+        return y
     if y is None:
         y = torch.empty(tokens, h, dtype=torch.float32, device=ys.device)
     L.check(L.load().lk_moe_combine(tokens, h, ku, 1 if accumulate else 0, _ptr(ys), _ptr(wts), _ptr(y), _stream()),
@@ -263,56 +300,110 @@ def moe_combine(ys, wts, y=None, accumulate=False):
     return y
 
 
-def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None):
-    """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route -> bucket -> grouped gate/up
-    (SwiGLU) -> row scale -> grouped down -> weighted combine (prefill), or per-assignment expert matvecs (decode).
+def moe_wscale(ids, wts, scale):
+    """g_moe_wscale: wts[t,k] *= scale[ids[t,k]] in place (a per-expert down scale folded into the combine weights)."""
+    _cuda(ids, wts, scale)
+    tokens, ku = wts.shape
+    L.check(L.load().lk_moe_wscale(tokens, ku, scale.numel(), _ptr(ids), _ptr(wts), _ptr(scale.contiguous().float()),
+                                   _stream()), "lk_moe_wscale")
+    return wts
+
+
+def moe_shared_gate(x, w):
+    """g_moe_shared_gate: sg[t] = sigmoid(x[t] . w) (x f32 [tokens][h], w f32/bf16 [h])."""
+    _cuda(x, w)
+    x = x.contiguous().float()
+    tokens, h = x.shape
+    sg = torch.empty(tokens, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_moe_shared_gate(tokens, h, _ptr(x), _ptr(w.contiguous()), _DT[w.dtype], _ptr(sg), _stream()),
+            "lk_moe_shared_gate")
+    return sg
+
+
+def _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale, shared_gate_w):
+    ids, wts = moe_route(logits, n_experts, ku, gating=gating, norm=norm, scale=scale, bias=router_bias)
+    if down_scale is not None:
+        moe_wscale(ids, wts, down_scale)
+    sg = moe_shared_gate(x.float(), shared_gate_w) if shared_gate_w is not None else None
+    return ids, wts, sg
+
+
+def _combine_out(tokens, h, x, y_shared):
+    """The combine's target: the shared experts' output (accumulated into, in place) or a new output."""
+    if y_shared is not None:
+        _cuda(y_shared)
+        return y_shared, True
+    return torch.empty(tokens, h, dtype=torch.float32, device=x.device), False
+
+
+def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None, gating=1, router_bias=None,
+            scale=1.0, act="silu", b_gate=None, b_up=None, b_down=None, down_scale=None, y_shared=None,
+            shared_gate_w=None, alpha=1.702, limit=7.0):
+    """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route (gating 1/2/3, router bias,
+    expert_weights_scale) -> per-expert down scale folded into the weights (g_moe_wscale) -> bucket -> grouped gate/up
+    (act + biases) -> row scale -> grouped down (+ bias) -> weighted combine (prefill), or per-assignment expert
+    matvecs (decode). The combine adds into y_shared (the shared experts' output) when given -- scaled first by the
+    shared-expert gate sigmoid(x . shared_gate_w) when that is given -- else into a new tensor.
     x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values;
-    w_dn: per expert h rows of f values. The reference switches to the GEMMs at 64 tokens (gen_llm.py:6107); here
-    from 192 assignments (tokens * ku), where they measured faster on configs[2] shapes (top-8 of 128 experts:
-    matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 / 312 us). `prefill` forces either path."""
+    w_dn: per expert h rows of f values; biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
+    switches to the GEMMs at 64 tokens (gen_llm.py:6107); here from 192 assignments (tokens * ku), where they
+    measured faster on configs[2] shapes (top-8 of 128 experts: matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 /
+    312 us). `prefill` forces either path."""
     tokens = x.shape[0]
-    ids, wts = moe_route(logits, n_experts, ku, norm=norm)
+    ids, wts, sg = _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale,
+                                    shared_gate_w)
+    y, acc = _combine_out(tokens, h, x, y_shared)
+    ep = dict(act=act, alpha=alpha, limit=limit)
     if prefill is None:
         prefill = tokens * ku >= 192
     if not prefill:
-        act = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=True)
-        ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act, w_dn, h, f, ku, n_experts)
-        return moe_combine(ys, wts)
+        act_ = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=True, bias=b_gate,
+                             bias2=b_up, **ep)
+        ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts, bias=b_down)
+        return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
     ti, rm, pos = moe_bucket(ids, n_experts)
     # the token rows row-scaled straight into bucket order: gate/up then reads plain tiles (no row gather)
     x16, sc = moe_row_scale_gather(x, rm, ku)
-    act = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True)
-    a16, asc = row_scale_f16(act)
-    ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts)
-    return moe_combine_sorted(ys, pos, wts)
+    act_ = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True, bias=b_gate,
+                            bias2=b_up, **ep)
+    a16, asc = row_scale_f16(act_)
+    ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts, bias=b_down)
+    return moe_combine_sorted(ys, pos, wts, y=y, accumulate=acc, sg=sg)
 
 
 def moe_ffn_mxfp4s(x, logits, w_gu, ws_gu, w_dn, ws_dn, h, f, n_experts, ku, norm=True, order=L.ORDER_PAIRS,
-                   prefill=None):
-    """The routed expert FFN of one MoE layer with MXFP4 experts (gpt-oss-like; gen_llm.py:5324-5386 wiring): the fp8
-    fusion of gen_mxfp4s.py:969-1110 -- route -> bucket -> e4m3 row scale -> grouped gate/up (SwiGLU) -> e4m3 row
-    scale -> grouped down -> weighted combine -- or, for at most 16 assignments, per-assignment expert matvecs on the
-    unquantised activations (gen_moe.py:535-727). The reference switches at 64 tokens (gen_llm.py:6107); here the
-    matvecs stream each assignment's expert on its own, which measured faster only up to about 20 assignments
-    (gpt-oss shapes, matvecs / GEMMs: 4 assignments 45 / 83 us, 16: 139 / 165 us, 24: 196 / 170 us). `prefill`
-    forces either
-    path. w_gu / ws_gu: per expert 2f rows (gate then up) of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per
-    expert h rows of f/2 / f/32 bytes."""
+                   prefill=None, gating=1, router_bias=None, scale=1.0, act="silu", b_gate=None, b_up=None,
+                   b_down=None, down_scale=None, y_shared=None, shared_gate_w=None, alpha=1.702, limit=7.0):
+    """The routed expert FFN of one MoE layer with MXFP4 experts (gpt-oss-like: gating=3 with the router bias,
+    act='swiglu_oai' and the expert biases; gen_llm.py:5324-5386 wiring): the fp8 fusion of gen_mxfp4s.py:969-1110 --
+    route -> bucket -> e4m3 row scale -> grouped gate/up (act + biases) -> e4m3 row scale -> grouped down (+ bias) ->
+    weighted combine -- or, for at most 16 assignments, per-assignment expert matvecs on the unquantised activations
+    (gen_moe.py:535-727). The reference switches at 64 tokens (gen_llm.py:6107); here the matvecs stream each
+    assignment's expert on its own, which measured faster only up to about 20 assignments (gpt-oss shapes, matvecs /
+    GEMMs: 4 assignments 45 / 83 us, 16: 139 / 165 us, 24: 196 / 170 us). `prefill` forces either path.
+    w_gu / ws_gu: per expert 2f rows (gate then up) of h/2 nibble bytes / h/32 E8M0 bytes; w_dn / ws_dn: per
+    expert h rows of f/2 / f/32 bytes. Routing options, down scale and shared output as moe_ffn."""
     tokens = x.shape[0]
-    ids, wts = moe_route(logits, n_experts, ku, norm=norm)
+    ids, wts, sg = _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale,
+                                    shared_gate_w)
+    y, acc = _combine_out(tokens, h, x, y_shared)
+    ep = dict(act=act, alpha=alpha, limit=limit)
     if prefill is None:
         prefill = tokens * ku > 16
     if not prefill:
-        act = moe_expert_mv_mxfp4s("gu", ids.reshape(-1), x, w_gu, ws_gu, f, h, ku, n_experts, order=order)
-        ys = moe_expert_mv_mxfp4s("dn", ids.reshape(-1), act, w_dn, ws_dn, h, f, ku, n_experts, order=order)
-        return moe_combine(ys, wts)
+        act_ = moe_expert_mv_mxfp4s("gu", ids.reshape(-1), x, w_gu, ws_gu, f, h, ku, n_experts, order=order,
+                                    bias=b_gate, bias2=b_up, **ep)
+        ys = moe_expert_mv_mxfp4s("dn", ids.reshape(-1), act_, w_dn, ws_dn, h, f, ku, n_experts, order=order,
+                                  bias=b_down)
+        return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
     ti, rm, pos = moe_bucket(ids, n_experts)
     x8, s8 = moe_row_scale_gather(x, rm, ku, f8=True)
-    act = moe_grouped_gemm_mxfp4s_f8("swiglu_sorted", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True,
-                                     order=order)
-    a8, as8 = row_scale_f8(act)
-    ys = moe_grouped_gemm_mxfp4s_f8("store", ti, rm, a8, as8, w_dn, ws_dn, h, ku, n_experts, order=order)
-    return moe_combine_sorted(ys, pos, wts)
+    act_ = moe_grouped_gemm_mxfp4s_f8("swiglu_sorted", ti, rm, x8, s8, w_gu, ws_gu, f, ku, n_experts, fused=True,
+                                      order=order, bias=b_gate, bias2=b_up, **ep)
+    a8, as8 = row_scale_f8(act_)
+    ys = moe_grouped_gemm_mxfp4s_f8("store", ti, rm, a8, as8, w_dn, ws_dn, h, ku, n_experts, order=order,
+                                    bias=b_down)
+    return moe_combine_sorted(ys, pos, wts, y=y, accumulate=acc, sg=sg)
 
 
 def moe_ffn_decode_noalloc(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, y=None):
