@@ -607,24 +607,24 @@ def moe_ffn_mxfp4_decode_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, or
     of gen_llm.py:6107, the expert matvecs of gen_moe.py:535-727): per assignment act = silu(Wg x) * (Wu x) and
     ys = Wd act with the exact MXFP4 weights and unquantised activations, y[t] = sum_k wts[t,k] ys[t,k]."""
     t, ku = ids.shape
-    E = nib_dn.shape[0] // h
-    Wgu = dequant_mxfp4_planar(nib_gu, sc_gu, nib_gu.shape[0], h, order).reshape(E, 2 * f, h)
-    Wdn = dequant_mxfp4_planar(nib_dn, sc_dn, nib_dn.shape[0], f, order).reshape(E, h, f)
     y = np.zeros((t, h), np.float64)
-    for i in range(t):
-        for j in range(ku):
-            e = ids[i, j]
-            v = Wgu[e] @ np.asarray(x[i], np.float64)
+    for e in np.unique(ids):   # one expert's weights at a time (an expert of gpt-oss size is 25 M values)
+        g0, d0 = 2 * f * e, h * e
+        Wgu = dequant_mxfp4_planar(nib_gu[g0:g0 + 2 * f], sc_gu[g0:g0 + 2 * f], 2 * f, h, order)
+        Wdn = dequant_mxfp4_planar(nib_dn[d0:d0 + h], sc_dn[d0:d0 + h], h, f, order)
+        for i, j in zip(*np.nonzero(ids == e)):
+            v = Wgu @ np.asarray(x[i], np.float64)
             act = silu(v[:f]) * v[f:]
-            y[i] += float(wts[i, j]) * (Wdn[e] @ act)
+            y[i] += float(wts[i, j]) * (Wdn @ act)
     return y
 
 
-def moe_ffn_mxfp4_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs"):
+def moe_ffn_mxfp4_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs", act=0, alpha=1.702, limit=7.0,
+                      b_gate=None, b_up=None, b_down=None):
     """The routed expert FFN with MXFP4 experts on the fp8 path (gen_llm.py:5324-5386 wiring with the e4m3 producer
     and fp8 GEMMs of gen_mxfp4s.py:969-1110): x8 = row_scale_f8(x); act = silu(g) * u from the fp8 gate/up GEMM;
     a8 = row_scale_f8(act) per assignment; ys = fp8 down GEMM; y[t] = sum_k wts[t,k] ys[t,k]. nib_gu/sc_gu: per expert
-    2f rows (gate then up) of h values; nib_dn/sc_dn: per expert h rows of f values."""
+    2f rows (gate then up) of h values; nib_dn/sc_dn: per expert h rows of f values. act / biases as moe_ffn_ref."""
     t, ku = ids.shape
     x8, s8 = row_scale_f8(x)
     y = np.zeros((t, h), np.float64)
@@ -634,9 +634,14 @@ def moe_ffn_mxfp4_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pa
         g0, g1 = 2 * f * e, 2 * f * e + f
         g = gemm_mxfp4_f8_ref(x8[tt], s8[tt], nib_gu[g0:g1], sc_gu[g0:g1], f, h, order)
         u = gemm_mxfp4_f8_ref(x8[tt], s8[tt], nib_gu[g1:g1 + f], sc_gu[g1:g1 + f], f, h, order)
-        act = (silu(g) * u).astype(np.float32)
-        a8, as8 = row_scale_f8(act)
+        if b_gate is not None:   # per-expert biases before the activation (gen_moe.py:958-1007)
+            g = g + np.asarray(b_gate, np.float64)[e]
+            u = u + np.asarray(b_up, np.float64)[e]
+        a = act_ref(g, u, act, alpha, limit).astype(np.float32)
+        a8, as8 = row_scale_f8(a)
         ys = gemm_mxfp4_f8_ref(a8, as8, nib_dn[h * e:h * (e + 1)], sc_dn[h * e:h * (e + 1)], h, f, order)
+        if b_down is not None:
+            ys = ys + np.asarray(b_down, np.float64)[e]
         np.add.at(y, tt, ys * np.asarray(wts, np.float64)[sel][:, None])
     return y
 
