@@ -5,13 +5,13 @@ Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B
 (K=4096: N=4096 q/o, N=1024 k/v, N=24576 fused gate+up; down K=12288, N=4096), bf16 activations. One STEP is one decode
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
 868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer the activations are
-quantised to int8 (g_quant_q8) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
+quantised to int8 (g_quant_q8, inside each matvec's prologue) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
 weight GB/s; the line also carries each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up, down and
 configs[0]'s Q4_0 4096 x 4096 GEMV, each streamed from HBM), the bf16-activation decode, the prefill TFLOP/s at M=2048
 over the same shapes
 (step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
-MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations + 32 matvec launches per
-decode step -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
+MoE layers. Each step is one CUDA-graph replay of the public ops' launches (32 matvec launches per decode step, each
+quantising its own activation row -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
@@ -204,44 +204,52 @@ def make_weights(torch, layers, seed=0):
     return out
 
 
-def bench_gemv_forms(args, torch, wstack, xq, pk, time_steps):
+def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
     """Each decode launch form alone: 32 back-to-back launches per graph replay, rotated over enough copies of its
     weights to exceed twice the L2, so every launch streams its weights from HBM. Per launch: device time, weight
-    GB/s and the fraction of the measured HBM copy. The four Q4_K forms of the step, and configs[0]'s Q4_0 4096 x 4096
-    GEMV (the reference's CPU-runnable case) on the same int8 activations."""
+    GB/s and the fraction of the measured HBM copy. The four Q4_K forms of the step (int8 numerics, quantised in the
+    matvec), and configs[0]'s Q4_0 4096 x 4096 GEMV (the reference's CPU-runnable case) both at its stated precision
+    -- fp16 activations through lk_mv, the reference's default f32-dot numerics for Q4_0 (formats.py:24-27) -- and on
+    int8 activations."""
     from loom_skills_b200 import ops
     gen = torch.Generator(device=wstack[0]["o"].device)
     gen.manual_seed(7)
     q40 = synth_blocks(torch, wstack[0]["o"].device, 4096, 4096, "q4_0", gen)
-    forms = [("q|k|v", wstack[0]["qkv"], "q4_k", 4096, [4096, 1024, 1024]), ("o", wstack[0]["o"], "q4_k", 4096, [4096]),
-             ("gate_up", wstack[0]["gate_up"], "q4_k", 4096, [24576]),
-             ("down", wstack[0]["down"], "q4_k", 12288, [4096]),
-             ("q4_0 4096x4096 (configs[0])", q40, "q4_0", 4096, [4096])]
+    x16 = xs[4096].to(torch.float16)
+    forms = [("q|k|v", wstack[0]["qkv"], "q4_k", 4096, [4096, 1024, 1024], "int8"),
+             ("o", wstack[0]["o"], "q4_k", 4096, [4096], "int8"),
+             ("gate_up", wstack[0]["gate_up"], "q4_k", 4096, [24576], "int8"),
+             ("down", wstack[0]["down"], "q4_k", 12288, [4096], "int8"),
+             ("q4_0 4096x4096 fp16 (configs[0])", q40, "q4_0", 4096, [4096], "fp16"),
+             ("q4_0 4096x4096 int8 (configs[0])", q40, "q4_0", 4096, [4096], "int8")]
     chain = 32
     out = {}
-    for label, base, fmt, k, ns in forms:
+    for label, base, fmt, k, ns, acts in forms:
         nbytes = base.numel()
         copies = max(2, -(-256_000_000 // nbytes))
         ws = [base] + [base.clone() for _ in range(copies - 1)]
         ys = [torch.empty(1, n, device=base.device) for n in ns]
         r0 = np.cumsum([0] + ns)
-        x = xq[0][k]
+        x = xs[k]
 
         def body():
             for i in range(chain):
                 w = ws[i % copies]
-                if len(ns) > 1:
-                    ops.mv_q8_multi(fmt, [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, 1, ys=ys)
+                if acts == "fp16":
+                    ops.mv(fmt, w, x16, ns[0], k, y=ys[0])
+                elif len(ns) > 1:
+                    ops.mv_q8_fused_multi(fmt, [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, ys=ys)
                 else:
-                    ops.mv_q8(fmt, w, x, ns[0], k, 1, y=ys[0])
+                    ops.mv_q8_fused(fmt, w, x, ns[0], k, y=ys[0])
         g = Timed(torch, body)
         for _ in range(max(3, args.warmup)):
             g.replay()
         us = time_steps(g.replay, max(5, args.steps)) * 1e3 / chain
         gbs = nbytes / (us * 1e-6) / 1e9
-        out[label] = {"format": fmt, "us_per_launch": round(us, 2), "weight_mb": round(nbytes / 1e6, 1),
-                      "weight_gbs": round(gbs, 1),
-                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies}
+        out[label] = {"format": fmt, "activations": acts, "us_per_launch": round(us, 2),
+                      "weight_mb": round(nbytes / 1e6, 1), "weight_gbs": round(gbs, 1),
+                      "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies,
+                      "kernel": "k_mv (lk_mv.cu)" if acts == "fp16" else "k_mv_q8_rows, in-kernel quantisation"}
         del g, ws
     return out
 
@@ -374,11 +382,16 @@ def bench_moe(args, torch, dev, time_steps, pk):
     E, ku, h, f = 32, 4, 2880, 2880
     gu, gus = synth_mxfp4(torch, dev, E * 2 * f, h, gen)
     dn, dns = synth_mxfp4(torch, dev, E * h, f, gen)
+    # gpt-oss numerics: softmax of the picked biased logits (gating 3), swiglu_oai, per-expert biases
+    rbias = torch.randn(E, device=dev, generator=gen) * 0.1
+    bg, bu = (torch.randn(E, f, device=dev, generator=gen) * 0.05 for _ in range(2))
+    bd = torch.randn(E, h, device=dev, generator=gen) * 0.05
+    oai = dict(gating=3, router_bias=rbias, norm=False, act="swiglu_oai", b_gate=bg, b_up=bu, b_down=bd)
     mx = {}
     for m in (1, 32, 1024, 8192):
         x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
         lg = torch.randn(m, E, device=dev, generator=gen)
-        g = Timed(torch, lambda: ops.moe_ffn_mxfp4s(x, lg, gu, gus, dn, dns, h, f, E, ku))
+        g = Timed(torch, lambda: ops.moe_ffn_mxfp4s(x, lg, gu, gus, dn, dns, h, f, E, ku, **oai))
         for _ in range(3):
             g.replay()
         ms = time_steps(g.replay, 20)
@@ -397,10 +410,12 @@ def bench_moe(args, torch, dev, time_steps, pk):
     f8_peak = 2 * pk["bf16_tflops_sustained"]
     out["mxfp4_gpt_oss_20b"] = {
         "experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": mx,
+        "numerics": "gating 3 with router bias, swiglu_oai (alpha 1.702, limit 7), per-expert gate/up/down biases",
         "data": "MXFP4 planes synthesised on the device (uniform nibbles, E8M0 119..121); bf16 N(0,1) x",
         "dense_gemm": {"shape": [M, h, 2 * f], "mode": "swiglu", "ms": round(ms, 4), "tflops": round(tf, 1),
                        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": round(f8_peak, 1),
                                     "unit": "TFLOP/s", "frac": round(tf / f8_peak, 4),
+                                    "frac_of_fp4_dense_peak": round(tf / (4 * pk["bf16_tflops_sustained"]), 4),
                                     "peak_source": "2 x measured bf16 sustained: kind::mxf8f6f4 runs at the fp8 rate "
                                                    "(e4m3 activations keep it off the fp4 rate)",
                                     "kernel": "k_gemm_mx (tcgen05 kind::mxf8f6f4.block_scale, lk_mxfp4)"}}}
@@ -450,13 +465,21 @@ def run_ours(args):
         for name, k, n in SHAPES[3:]:
             ops.mv_q8("q4_k", w[name], xq[li][k], n, k, 1, y=y[name])
 
-    def decode_body():   # one decode step: per layer, quantise the activations, then the six projections
+    def fused_layer(li):
+        # the activation quantised inside each matvec (lk_mv_q8_fused): four launches per layer, q | k | v in one
+        w, y = wstack[li], ys[li]
+        ops.mv_q8_fused_multi("q4_k", [w["q"], w["k"], w["v"]], xs[4096], [4096, 1024, 1024], 4096,
+                              ys=[y["q"], y["k"], y["v"]])
+        for name, k, n in SHAPES[3:]:
+            ops.mv_q8_fused("q4_k", w[name], xs[k], n, k, y=y[name])
+
+    def decode_body():   # one decode step: the six projections of every layer, int8 numerics, quantised in-kernel
+        for li in range(args.layers):
+            fused_layer(li)
+
+    def unfused_body():  # the same step with the quantisation as its own launches (16 + 32 launches)
         for li in range(args.layers):
             quant_layer(li)
-            mv_layer(li)
-
-    def mv_body():       # the matvecs alone (the dominant kernel, for the roofline)
-        for li in range(args.layers):
             mv_layer(li)
 
     def decode_bf16_body():   # the f32/bf16-activation path (ACT_Q8=0)
@@ -500,19 +523,25 @@ def run_ours(args):
     ms = time_steps(dec.replay, args.steps, clk)
     clocks = clk.stop()
     value = world * step_bytes / (ms * 1e-3) / 1e9
-    # the matvec kernel alone: the same 32 launches back to back in one graph, CUDA events around the timed replays
-    mvg = Timed(torch, mv_body)
-    for _ in range(args.warmup):
-        mvg.replay()
-    mv_ms = time_steps(mvg.replay, args.steps)
-    act_q8 = sum((k + k // 32 * 8) + n * 4 for _, k, n in SHAPES)   # int8 codes + meta read, f32 y written
-    alg_per_launch = (step_bytes + args.layers * act_q8) / launches_per_step
+    # the matvec kernel: the step is nothing but its 32 launches, so its average launch is the step over the launches
+    # (CUDA events around the timed replays of the one graph)
+    mv_ms = ms
+    act_bytes_l = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read (quantised in-kernel) + f32 y written
+    alg_per_launch = (step_bytes + args.layers * act_bytes_l) / launches_per_step
     kavg = mv_ms / launches_per_step
     achieved = alg_per_launch / (kavg * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": int(TRAFFIC_RATIO_DECODE * alg_per_launch), "peak_source": pk_src,
-            "kernel": "k_mv_q8_rows / k_mv_q8 (Q4_K x int8, dp4a; lk_mvq8)", "avg_launch_us": round(kavg * 1e3, 2),
-            "alg_bytes_per_launch": int(alg_per_launch), "mv_ms_per_step": round(mv_ms, 4)}
+            "kernel": "k_mv_q8_rows<.., LK_BF16> (Q4_K x int8 quantised in the prologue, dp4a; lk_mvq8)",
+            "avg_launch_us": round(kavg * 1e3, 2), "alg_bytes_per_launch": int(alg_per_launch),
+            "mv_ms_per_step": round(mv_ms, 4)}
+    # the unfused form (lk_quant_q8 launches + the matvecs on their codes), for comparison
+    ug = Timed(torch, unfused_body)
+    for _ in range(args.warmup):
+        ug.replay()
+    un_ms = time_steps(ug.replay, max(3, args.steps // 4))
+    decode_unfused = {"value": round(world * step_bytes / (un_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                      "ms_per_step": round(un_ms, 4), "launches_per_step": launches_per_step + 2 * args.layers}
     bf = Timed(torch, decode_bf16_body)
     for _ in range(args.warmup):
         bf.replay()
@@ -535,8 +564,7 @@ def run_ours(args):
         xbuf.copy_(hx, non_blocking=True)
         main = torch.cuda.current_stream()
         for li in range(args.layers):
-            quant_layer(li)
-            mv_layer(li)
+            fused_layer(li)
             done = torch.cuda.Event()
             done.record(main)
             side.wait_event(done)
@@ -622,13 +650,13 @@ def run_ours(args):
                              "tflops": round(sum(2.0 * m * n * k for _, k, n in SHAPES) / (mms * 1e-3) / 1e12, 2)}
 
     # ---- each decode launch form alone (its weights rotated past L2): the GEMV's own fraction of HBM per shape
-    gemv = bench_gemv_forms(args, torch, wstack, xq, pk, time_steps) if not args.no_extra else None
+    gemv = bench_gemv_forms(args, torch, wstack, xs, pk, time_steps) if not args.no_extra else None
     # ---- the IQ4_NL GEMMs N-sharded over the ranks, all-gather fused into the epilogue (strong scaling)
     sharded = bench_sharded(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
 
-    gpu_launches = args.steps * (launches_per_step + 2 * args.layers)   # 32 matvec + 16 quantisation launches
+    gpu_launches = args.steps * launches_per_step   # 32 matvec launches (quantisation inside them)
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
         line = {
@@ -646,10 +674,11 @@ def run_ours(args):
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
             "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_gemv": gemv, "decode_bf16": decode_bf16,
+            "decode_unfused": decode_unfused,
             "sharded_iq4_nl": sharded, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
-        del dec, mvg, bf, e2e_g, scale_g, gemm_g
+        del dec, ug, bf, e2e_g, scale_g, gemm_g
         dist.barrier()
         dist.destroy_process_group()
 

@@ -112,6 +112,16 @@ int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* x
  * n, w, y are HOST arrays of nseg entries. */
 int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int tokens,
                    int accumulate, const uint8_t* xq, lk_stream_t stream);
+/* lk_mv_q8_fused / lk_mv_q8_fused_multi: g_quant_q8 (gen_llm.py:683-750) and g_mv_{fmt}_q8 (gen_llm.py:1159-1378) of
+ * one token in one launch, launch(%n, %accumulate, %x, %w, %y): the activation row x [1][k] (LK_F32 or LK_BF16) is
+ * quantised to Q8_1 codes inside the matvec -- each CTA quantises the row into its shared memory, the codes and group
+ * meta bit for bit lk_quant_q8's -- and contracted with the weight codes as lk_mv_q8 does; no xq buffer exists.
+ * Formats Q4_0 and Q4_K, k a multiple of 4096 up to 12288 (LK_EUNSUPPORTED otherwise: lk_quant_q8 + lk_mv_q8 cover
+ * every other shape). The _multi form takes up to 4 weights that share x, as lk_mv_q8_multi. */
+int lk_mv_q8_fused(int fmt, int n, int k, int accumulate, const void* x, int x_dtype, const void* w, float* y,
+                   lk_stream_t stream);
+int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int accumulate,
+                         const void* x, int x_dtype, lk_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Prefill GEMM (tcgen05 + TMEM). Replaces g_gemm_{fmt}_{store,acc,swiglu}[_m128|_m256] (gen_gemm.py:535-704,

@@ -54,6 +54,8 @@ SIGNATURES = {
                                               _P, _I, _F, _F, _P, _P]),
     "lk_moe_expert_mv_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _F, _F, _P, _P]),
     "lk_moe_expert_mv_mxfp4s_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _I, _F, _F, _P, _P]),
+    "lk_mv_q8_fused": (_I, [_I, _I, _I, _I, _P, _I, _P, _P, _P]),
+    "lk_mv_q8_fused_multi": (_I, [_I, _I, _P, _P, _P, _I, _I, _P, _I, _P]),
     "lk_moe_wscale": (_I, [_I, _I, _I, _P, _P, _P, _P]),
     "lk_moe_shared_gate": (_I, [_I, _I, _P, _P, _I, _P, _P]),
     "lk_moe_combine_gated": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),

@@ -78,6 +78,27 @@ int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float*
   return mv_q8_multi(fmt, nseg, n, w, y, k, tokens, accumulate, xq, (cudaStream_t)stream);
 }
 
+int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int accumulate,
+                         const void* x, int x_dtype, lk_stream_t stream) {
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return q4_family(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (nseg <= 0 || nseg > 4 || !n || !w || !y) return LK_EINVAL;
+  if (k <= 0 || k % 256) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  for (int g = 0; g < nseg; ++g) {
+    if (n[g] <= 0 || !w[g] || !y[g]) return LK_EINVAL;
+    if (!aligned(w[g], 16)) return LK_EALIGN;
+  }
+  if (!x) return LK_EINVAL;
+  if (!aligned(x, x_dtype == LK_BF16 ? 2 : 4)) return LK_EALIGN;
+  if (k % 4096 || k > 3 * 4096) return LK_EUNSUPPORTED;
+  return mv_q8_fused(fmt, nseg, n, w, y, k, accumulate, x, x_dtype, (cudaStream_t)stream);
+}
+
+int lk_mv_q8_fused(int fmt, int n, int k, int accumulate, const void* x, int x_dtype, const void* w, float* y,
+                   lk_stream_t stream) {
+  return lk_mv_q8_fused_multi(fmt, 1, &n, &w, &y, k, accumulate, x, x_dtype, stream);
+}
+
 int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, void* out, int out_dtype,
                lk_stream_t stream) {
   if (!w || !out || n_values < 0) return LK_EINVAL;

@@ -90,6 +90,10 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
           cudaStream_t s);
 int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int tokens,
                 int accumulate, const uint8_t* xq, cudaStream_t s);
+// one token: the activation row quantised inside the row-streaming matvec (no xq buffer); LK_EUNSUPPORTED off its
+// shapes (Q4_0 / Q4_K, k % 4096 == 0, k <= 12288)
+int mv_q8_fused(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
+                const void* x, int x_dtype, cudaStream_t s);
 
 // device status words of the kernel files (bit 0: a bounded wait gave up)
 unsigned int status_q8(bool clear);

@@ -8,12 +8,12 @@
 // each token's activations (1-D bulk copies) into a 4-stage shared-memory ring. Four consumer warps each take one 256-value chunk of every
 // stage: they convert their activation slice to f16 once (with per-32-value group sums), then unpack nibbles in
 // registers straight into the A fragments of warp-level f16 MMAs (16 rows x 16 k x 8 tokens) -- the weights never
-// go back to shared memory. Codes enter the MMA exactly as (1024 + code) f16 values (high nibbles as 1024 + 16 code);
-// the per-32-value group scale is applied in f32 afterwards:
-//     sum_k (a*q_k - c) x_k = a * D - (1024 a + c) * S,   D = sum (1024 + q_k) x_k,  S = sum x_k
-// Q4_0: a = d, c = 8d; IQ4_NL: codes are the biased codebook bytes (kvalue + 128), a = d, offset 1152 a; Q4_K:
-// a = d*sc, c = dmin*m per group. The f32 accumulation of exact codes is at least as precise as the reference's f32
-// dequant-then-dot (gen_llm.py:1281-1357).
+// go back to shared memory. Codes enter the MMA as exact small-integer f16 values, made from a (1024 + code) bit
+// pattern minus its offset: q - 8 (Q4_0), the kvalue (IQ4_NL, from the codebook byte kvalue + 128), q or 16 q (Q4_K
+// low / high nibbles). The per-32-value group scale is applied in f32 afterwards:
+//     Q4_0 / IQ4_NL: sum_k d v_k x_k = d * D;   Q4_K: sum_k (a q_k - c) x_k = a * D - c * S,   S = sum x_k
+// with a = d*sc, c = dmin*m per group. Centred codes keep D free of the cancellation a (1024 + q) offset would cause:
+// the f32 accumulation of exact codes is as precise as the reference's f32 dequant-then-dot (gen_llm.py:1281-1357).
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
@@ -49,11 +49,17 @@ LK_DEV void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uin
 
 LK_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// bytes of t (code in the low or high nibble, other nibble zero) -> A fragment halves (1024 + byte) for 4 consecutive k
-LK_DEV void code_frag(uint32_t t, uint32_t& first, uint32_t& second) {
-  first = prmt(t, 0x64646464u, 0x4140u);
-  second = prmt(t, 0x64646464u, 0x4342u);
+LK_DEV uint32_t hsub2u(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
+// bytes of t (code in the low or high nibble, other nibble zero) -> A fragment halves (byte - off) for 4 consecutive k:
+// the f16 bit pattern of 1024 + byte, minus the f16 pair koff2 = (1024 + off) -- exact for every byte
+LK_DEV void code_frag(uint32_t t, uint32_t koff2, uint32_t& first, uint32_t& second) {
+  first = hsub2u(prmt(t, 0x64646464u, 0x4140u), koff2);
+  second = hsub2u(prmt(t, 0x64646464u, 0x4342u), koff2);
+}
+constexpr uint32_t kMagic1024 = 0x64006400u;   // f16 pair (1024, 1024)
 
 LK_DEV uint32_t lds_u16x2(const uint8_t* p) {   // 2-byte aligned 4 bytes
   const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
@@ -62,6 +68,15 @@ LK_DEV uint32_t lds_u16x2(const uint8_t* p) {   // 2-byte aligned 4 bytes
 
 // acc += a * D - c' * S for the lane's D elements: rows g, g+8 x tokens 2tig, 2tig+1. With one token only the
 // token-0 column carries data (elements 0 and 2).
+template <int TOK>
+LK_DEV void group_epilogue_d(float (&acc)[4], const float (&d)[4], float a_g, float a_g8) {   // no offset term
+  acc[0] = fmaf(a_g, d[0], acc[0]);
+  acc[2] = fmaf(a_g8, d[2], acc[2]);
+  if (TOK > 1) {
+    acc[1] = fmaf(a_g, d[1], acc[1]);
+    acc[3] = fmaf(a_g8, d[3], acc[3]);
+  }
+}
 template <int TOK>
 LK_DEV void group_epilogue(float (&acc)[4], const float (&d)[4], float2 s01, float a_g, float c_g, float a_g8,
                            float c_g8) {
@@ -147,8 +162,8 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
   };
   if (FMT == LK_Q4_K) {
     // cooperative header decode: lane -> (row lane/2, groups 4*(lane&1) .. +3), four groups at a time with byte-wise
-    // bit operations. Low-nibble groups (even j) hold (a, 1024 a + c); high-nibble groups (odd j, whose codes the
-    // MMA sees as 16 q) hold (a / 16, 64 a + c).
+    // bit operations. Low-nibble groups (even j) hold (a, c); high-nibble groups (odd j, whose codes the MMA sees as
+    // 16 q) hold (a / 16, c).
 #pragma unroll
     for (int wi = 0; wi < NW; ++wi) {
       const uint8_t* rb = wi ? rb1 : rb0;
@@ -160,10 +175,8 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
       float4 lo, hi;
       float a0 = d * byte_f32(sc4, 0x7650u), a1 = d * byte_f32(sc4, 0x7651u);
       float a2 = d * byte_f32(sc4, 0x7652u), a3 = d * byte_f32(sc4, 0x7653u);
-      lo = make_float4(a0, fmaf(1024.0f, a0, dmin * byte_f32(m4, 0x7650u)), a1 * 0.0625f,
-                       fmaf(64.0f, a1, dmin * byte_f32(m4, 0x7651u)));
-      hi = make_float4(a2, fmaf(1024.0f, a2, dmin * byte_f32(m4, 0x7652u)), a3 * 0.0625f,
-                       fmaf(64.0f, a3, dmin * byte_f32(m4, 0x7653u)));
+      lo = make_float4(a0, dmin * byte_f32(m4, 0x7650u), a1 * 0.0625f, dmin * byte_f32(m4, 0x7651u));
+      hi = make_float4(a2, dmin * byte_f32(m4, 0x7652u), a3 * 0.0625f, dmin * byte_f32(m4, 0x7653u));
       float4* dst = reinterpret_cast<float4*>(actab + wi * 16 * kAcStride + r * kAcStride + 4 * hh);
       dst[0] = lo;
       dst[1] = hi;
@@ -190,13 +203,13 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
           uint32_t w0 = *reinterpret_cast<const uint32_t*>(rb + g * RS + off);
           uint32_t w8 = *reinterpret_cast<const uint32_t*>(rb + (g + 8) * RS + off);
           uint32_t f0, s0, f8, s8;
-          code_frag(w0 & 0x0F0F0F0Fu, f0, s0);
-          code_frag(w8 & 0x0F0F0F0Fu, f8, s8);
+          code_frag(w0 & 0x0F0F0F0Fu, kMagic1024, f0, s0);
+          code_frag(w8 & 0x0F0F0F0Fu, kMagic1024, f8, s8);
           if (h == 0) mma16816_z(dl[wi], f0, f8, s0, s8, bl0, bl1);
           else mma16816(dl[wi], f0, f8, s0, s8, bl0, bl1);
           if (XT == LK_F32) mma16816(dl[wi], f0, f8, s0, s8, ll0, ll1);
-          code_frag(w0 & 0xF0F0F0F0u, f0, s0);
-          code_frag(w8 & 0xF0F0F0F0u, f8, s8);
+          code_frag(w0 & 0xF0F0F0F0u, kMagic1024, f0, s0);
+          code_frag(w8 & 0xF0F0F0F0u, kMagic1024, f8, s8);
           if (h == 0) mma16816_z(dh[wi], f0, f8, s0, s8, bh0, bh1);
           else mma16816(dh[wi], f0, f8, s0, s8, bh0, bh1);
           if (XT == LK_F32) mma16816(dh[wi], f0, f8, s0, s8, lh0, lh1);
@@ -213,7 +226,7 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
     }
     __syncwarp();   // the table is rewritten by the next chunk
   } else {
-    constexpr float kOff = FMT == LK_Q4_0 ? 1032.0f : 1152.0f;   // magic 1024 + (8 | 128 codebook bias)
+    constexpr uint32_t kOff2 = FMT == LK_Q4_0 ? 0x64086408u : 0x64806480u;   // f16 pairs 1024 + (8 | 128 bias)
 #pragma unroll 2
     for (int j = 0; j < 8; ++j) {
       uint32_t b00, b01, b10, b11, l00 = 0, l01 = 0, l10 = 0, l11 = 0;
@@ -224,7 +237,6 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
         bfrag(xl, g, kk, xvalid, l00, l01);
         bfrag(xl, g, kk + 16, xvalid, l10, l11);
       }
-      float2 s = sums(j);
 #pragma unroll
       for (int wi = 0; wi < NW; ++wi) {
         const uint8_t* blk = (wi ? rb1 : rb0) + 18 * j;
@@ -243,15 +255,15 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
         }
         float dd[4];
         uint32_t f0, s0, f8, s8;
-        code_frag(t0, f0, s0);
-        code_frag(t8, f8, s8);
+        code_frag(t0, kOff2, f0, s0);
+        code_frag(t8, kOff2, f8, s8);
         mma16816_z(dd, f0, f8, s0, s8, b00, b01);
         if (XT == LK_F32) mma16816(dd, f0, f8, s0, s8, l00, l01);
-        code_frag(u0, f0, s0);
-        code_frag(u8, f8, s8);
+        code_frag(u0, kOff2, f0, s0);
+        code_frag(u8, kOff2, f8, s8);
         mma16816(dd, f0, f8, s0, s8, b10, b11);
         if (XT == LK_F32) mma16816(dd, f0, f8, s0, s8, l10, l11);
-        group_epilogue<TOK>(acc[wi], dd, s, d0, kOff * d0, d8, kOff * d8);
+        group_epilogue_d<TOK>(acc[wi], dd, d0, d8);
       }
     }
   }

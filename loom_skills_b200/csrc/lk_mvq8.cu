@@ -333,7 +333,8 @@ struct RowArgs {
   int n[kMaxSegs];
   int start[kMaxSegs + 1];
   int nseg;
-  const uint8_t* xq;   // codes [1][k] then meta [1][k/32][2]
+  const uint8_t* xq;   // codes [1][k] then meta [1][k/32][2] (XIN == kXinCodes)
+  const void* x;       // the activation row [1][k] of f32 / bf16, quantised by the kernel itself (other XIN)
   int k, accumulate;
   int64_t rb;          // bytes per packed row
   int sr;              // rows per stage
@@ -354,11 +355,45 @@ __host__ __device__ inline int ring_bytes(int stage_bytes) {
   return (kRStages * stage_bytes + 2 * kRStages * 8 + kRStages * kRowWarps * 12 + 127) / 128 * 128;
 }
 
+// where the row kernel's activation codes come from: lk_quant_q8's buffer, or x of this type quantised in the kernel
+// (distinct from the LK_* dtype ids, among which LK_F32 is 0)
+enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
+
+// bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
+__host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
+
+// One 32-value group of g_quant_q8 (gen_llm.py:683-750) by one warp, lane = value: d = amax / 127, q = round(x / d)
+// (halves away from zero; 0 for an all-zero group), codes[g*32 + lane] = q, meta[g] = (f16-rounded d, sum of q). The
+// same arithmetic as k_quant_q8, so the codes and meta are the same bit for bit.
+template <int XIN>
+LK_DEV void quant_group(const void* x, int g, int lane, int8_t* codes, float* meta) {
+  static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
+  const int idx = g * 32 + lane;
+  const float v = XIN == kXinBF16 ? bf2f(static_cast<const uint16_t*>(x)[idx]) : static_cast<const float*>(x)[idx];
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const float d = amax / 127.0f;
+  int q = 0;
+  if (amax > 0.0f) q = int(roundf(v / d));   // ordered compare: a NaN maximum gives code 0, like the reference
+  codes[idx] = int8_t(q);
+  int sum = q;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+  if (lane == 0) {
+    meta[2 * g] = __half2float(__float2half_rn(d));
+    meta[2 * g + 1] = float(sum);
+  }
+}
+
 // UPL units per lane over the whole row; HALVES warps per row (each takes UPL / HALVES of the units; the second
 // hands its partial sum to the first through shared memory and a per-row mbarrier). A CTA runs RINGS independent
 // rings (a producer warp, its consumer warps, its own stages and barriers); stages go round-robin over the
 // gridDim.x * RINGS rings. Fewer, larger CTAs make the grid cheaper to launch, retire and hand over to the next grid.
-template <int FMT, int UPL, int HALVES, int RINGS>
+// XIN == kXinCodes: the activation codes come from lk_quant_q8's buffer (p.xq). kXinF32 / kXinBF16: the consumer warps
+// of the CTA first quantise the row p.x into shared memory together (the g_quant_q8 launch folded into the
+// matvec's prologue; it overlaps the first weight stage's flight), then read their codes from there.
+template <int FMT, int UPL, int HALVES, int RINGS, int XIN>
 __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
   constexpr int kU = UPL / HALVES;             // units this lane computes
@@ -405,22 +440,38 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     const int rslot = (warp - 1) % kRowWarps;  // this warp's row of every stage
     const int half = (warp - 1) / kRowWarps;   // which share of the row's units
     griddep_wait();                            // the activations come from the previous kernel
+    const uint8_t* xq = p.xq;
+    if constexpr (XIN != kXinCodes) {
+      // every consumer warp of the CTA takes groups cw, cw + ncw, ... of the row; then all of them read the codes
+      uint8_t* xs = smem_all + RINGS * ring_bytes(stage_bytes);
+      const int cw = ring * kCW + (warp - 1), ncw = RINGS * kCW;
+      for (int g = cw; g < p.k / 32; g += ncw)
+        quant_group<XIN>(p.x, g, lane, reinterpret_cast<int8_t*>(xs), reinterpret_cast<float*>(xs + p.k));
+      asm volatile("bar.sync 1, %0;" ::"r"(ncw * 32) : "memory");   // consumer warps only
+      xq = xs;
+    }
+    // 16-byte loads of the codes and meta: read-only global loads, or shared memory when quantised here
+    auto ld16 = [](const void* q) {
+      return XIN != kXinCodes ? *reinterpret_cast<const uint4*>(q) : __ldg(reinterpret_cast<const uint4*>(q));
+    };
     // lane l owns the (chunk, page) units l + 32u: chunk l/4 + 8u, page l % 4 -- the same page for every unit
     const int pg = lane & 3;
     uint32_t xa[kU][8], xb[kU][8];
     float dx0[kU], dx1[kU], b0[kU], b1[kU];   // Q4_0: b0, b1 unused
     int s0x8[kU], s1x8[kU];                   // Q4_0: 8 x the groups' code sums (codes are q - 8)
-    const float* meta = reinterpret_cast<const float*>(p.xq + p.k);
+    const float* meta = reinterpret_cast<const float*>(xq + p.k);
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int c = (lane >> 2) + 8 * (half * kU + u);
-      const uint4* xw = reinterpret_cast<const uint4*>(p.xq + c * 256 + 64 * pg);
-      const uint4 v0 = __ldg(xw), v1 = __ldg(xw + 1), v2 = __ldg(xw + 2), v3 = __ldg(xw + 3);
+      const uint8_t* xw = xq + c * 256 + 64 * pg;
+      const uint4 v0 = ld16(xw), v1 = ld16(xw + 16), v2 = ld16(xw + 32), v3 = ld16(xw + 48);
       xa[u][0] = v0.x; xa[u][1] = v0.y; xa[u][2] = v0.z; xa[u][3] = v0.w;
       xa[u][4] = v1.x; xa[u][5] = v1.y; xa[u][6] = v1.z; xa[u][7] = v1.w;
       xb[u][0] = v2.x; xb[u][1] = v2.y; xb[u][2] = v2.z; xb[u][3] = v2.w;
       xb[u][4] = v3.x; xb[u][5] = v3.y; xb[u][6] = v3.z; xb[u][7] = v3.w;
-      const float4 mt = __ldg(reinterpret_cast<const float4*>(meta + c * 16 + 4 * pg));
+      const uint4 mu = ld16(meta + c * 16 + 4 * pg);
+      const float4 mt = make_float4(__uint_as_float(mu.x), __uint_as_float(mu.y), __uint_as_float(mu.z),
+                                    __uint_as_float(mu.w));
       dx0[u] = mt.x;
       if (FMT == LK_Q4_0) {
         dx1[u] = mt.z;
@@ -513,12 +564,12 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
   }
 }
 
-template <int FMT, int UPL, int HALVES, int RINGS>
+template <int FMT, int UPL, int HALVES, int RINGS, int XIN>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
-  const int smem = RINGS * ring_bytes(stage_bytes);
+  const int smem = RINGS * ring_bytes(stage_bytes) + (XIN != kXinCodes ? xq_smem_bytes(a.k) : 0);
   constexpr int threads = 32 * RINGS * (1 + kRowWarps * HALVES);
-  auto kern = k_mv_q8_rows<FMT, UPL, HALVES, RINGS>;
+  auto kern = k_mv_q8_rows<FMT, UPL, HALVES, RINGS, XIN>;
   // the attribute and the occupancy query once per (device, shared-memory size): they cost host time on every call
   struct Entry {
     int dev, smem, per_sm, sms;
@@ -642,10 +693,26 @@ static bool rows_path(int fmt, int k, int tokens) {
   return (fmt == LK_Q4_K || fmt == LK_Q4_0) && tokens == 1 && k % 4096 == 0 && k <= 3 * 4096;
 }
 
+template <int XIN>
+static int rows_dispatch(int fmt, int k, const RowArgs& ra, cudaStream_t s) {
+  const bool q40 = fmt == LK_Q4_0;
+  switch (k / 2048) {   // units (chunk, page) per lane
+    case 2:
+      return q40 ? launch_rows<LK_Q4_0, 2, 1, kRingsShort, XIN>(ra, s) : launch_rows<LK_Q4_K, 2, 1, kRingsShort, XIN>(ra, s);
+    case 4:
+      return q40 ? launch_rows<LK_Q4_0, 4, 2, kRingsLong, XIN>(ra, s) : launch_rows<LK_Q4_K, 4, 2, kRingsLong, XIN>(ra, s);
+    case 6:
+      return q40 ? launch_rows<LK_Q4_0, 6, 2, kRingsLong, XIN>(ra, s) : launch_rows<LK_Q4_K, 6, 2, kRingsLong, XIN>(ra, s);
+  }
+  return LK_EUNSUPPORTED;
+}
+
+// xq: lk_quant_q8's buffer; or (xq == nullptr) x of x_dtype, quantised inside the matvec
 static int mv_q8_rows(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
-                      const uint8_t* xq, cudaStream_t s) {
+                      const uint8_t* xq, cudaStream_t s, const void* x = nullptr, int x_dtype = LK_F32) {
   RowArgs ra{};
   ra.xq = xq;
+  ra.x = x;
   ra.k = k;
   ra.accumulate = accumulate;
   ra.rb = int64_t(k) / 256 * kChunkBytes;   // Q4_K: k / 256 super-blocks; Q4_0: k / 32 blocks of 18 bytes, the same
@@ -659,13 +726,15 @@ static int mv_q8_rows(int fmt, int nseg, const int* ns, const void* const* ws, f
     ra.start[g + 1] = ra.start[g] + (ns[g] + ra.sr - 1) / ra.sr;
   }
   ra.nstages = ra.start[nseg];
-  const bool q40 = fmt == LK_Q4_0;
-  switch (k / 2048) {   // units (chunk, page) per lane
-    case 2: return q40 ? launch_rows<LK_Q4_0, 2, 1, kRingsShort>(ra, s) : launch_rows<LK_Q4_K, 2, 1, kRingsShort>(ra, s);
-    case 4: return q40 ? launch_rows<LK_Q4_0, 4, 2, kRingsLong>(ra, s) : launch_rows<LK_Q4_K, 4, 2, kRingsLong>(ra, s);
-    case 6: return q40 ? launch_rows<LK_Q4_0, 6, 2, kRingsLong>(ra, s) : launch_rows<LK_Q4_K, 6, 2, kRingsLong>(ra, s);
-  }
-  return LK_EUNSUPPORTED;
+  if (xq) return rows_dispatch<kXinCodes>(fmt, k, ra, s);
+  return x_dtype == LK_BF16 ? rows_dispatch<kXinBF16>(fmt, k, ra, s) : rows_dispatch<kXinF32>(fmt, k, ra, s);
+}
+
+// g_quant_q8 + g_mv_{fmt}_q8 of one token in one launch (the row-streaming kernel quantises x in its prologue)
+int mv_q8_fused(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
+                const void* x, int x_dtype, cudaStream_t s) {
+  if (!rows_path(fmt, k, 1) || nseg > kMaxSegs) return LK_EUNSUPPORTED;
+  return mv_q8_rows(fmt, nseg, ns, ws, ys, k, accumulate, nullptr, s, x, x_dtype);
 }
 
 // Several weights sharing one activation (q | k | v of an attention layer): one launch over all their rows when the

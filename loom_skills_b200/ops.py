@@ -463,3 +463,31 @@ def mv_q8_multi(fmt, ws, xq, ns, k, tokens, ys=None, accumulate=False):
     L.check(L.load().lk_mv_q8_multi(_fmt(fmt), g, n_arr, w_arr, y_arr, k, tokens, 1 if accumulate else 0, _ptr(xq),
                                     _stream()), "lk_mv_q8_multi")
     return ys
+
+
+def mv_q8_fused(fmt, w, x, n, k, y=None, accumulate=False):
+    """One token's decode matvec on int8 activations, quantised inside the matvec (g_quant_q8 folded into the
+    kernel's prologue): the numerics of quant_q8 + mv_q8 in one launch. x [1][k] f32 / bf16."""
+    _cuda(w, x, y)
+    x = x.contiguous()
+    if y is None:
+        y = torch.empty(1, n, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_mv_q8_fused(_fmt(fmt), n, k, 1 if accumulate else 0, _ptr(x), _DT[x.dtype], _ptr(w), _ptr(y),
+                                    _stream()), "lk_mv_q8_fused")
+    return y
+
+
+def mv_q8_fused_multi(fmt, ws, x, ns, k, ys=None, accumulate=False):
+    """mv_q8_fused over up to 4 weights sharing x (q | k | v) in one launch. Returns the ys."""
+    import ctypes
+    _cuda(x, *ws)
+    x = x.contiguous()
+    g = len(ws)
+    if ys is None:
+        ys = [torch.empty(1, n, dtype=torch.float32, device=x.device) for n in ns]
+    n_arr = (ctypes.c_int * g)(*ns)
+    w_arr = (ctypes.c_void_p * g)(*[w.data_ptr() for w in ws])
+    y_arr = (ctypes.c_void_p * g)(*[y.data_ptr() for y in ys])
+    L.check(L.load().lk_mv_q8_fused_multi(_fmt(fmt), g, n_arr, w_arr, y_arr, k, 1 if accumulate else 0, _ptr(x),
+                                          _DT[x.dtype], _stream()), "lk_mv_q8_fused_multi")
+    return ys

@@ -32,6 +32,10 @@ def host(t):
 QUANT = {"q4_0": O.quantize_q4_0, "q4_k": O.quantize_q4_k}
 
 
+def weights(fmt, n, k, seed):
+    return QUANT[fmt]((np.random.default_rng(seed).standard_normal((n, k)) * 0.02).astype(np.float32))
+
+
 class TestQuantQ8:
     @pytest.mark.parametrize("dtype", ["f32", "bf16"])
     def test_bit_exact(self, ops, golden, dtype):
@@ -104,3 +108,46 @@ class TestMvQ8Multi:
             ref = O.mv_ref(fmt, w, xd, n, k)
             assert O.rel_l2(host(y), ref) < TOL, O.rel_l2(host(y), ref)
         assert ops.device_status() == 0
+
+
+# ---------------------------------------------------------------------------------------------------------- fused
+@pytest.mark.parametrize("fmt", ["q4_k", "q4_0"])
+@pytest.mark.parametrize("k,n", [(4096, 1000), (8192, 512), (12288, 2048)])
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+def test_fused_quantisation_equals_two_launches(ops, fmt, k, n, xdt):
+    # the matvec that quantises x in its own prologue gives lk_quant_q8 + lk_mv_q8's result bit for bit
+    rng = np.random.default_rng(k + n)
+    w = dev(weights(fmt, n, k, 5))
+    x = dev(rng.standard_normal((1, k)).astype(np.float32))
+    if xdt == "bf16":
+        x = x.to(torch.bfloat16)
+    y2 = ops.mv_q8(fmt, w, ops.quant_q8(x), n, k, 1)
+    y1 = ops.mv_q8_fused(fmt, w, x, n, k)
+    assert torch.equal(y1, y2)
+    codes, meta = O.quant_q8(x.float().cpu().numpy())
+    ref = O.mv_ref(fmt, host(w), O.dequant_q8(codes, meta), n, k)
+    assert O.rel_l2(host(y1), ref) < TOL
+    assert ops.device_status() == 0
+
+
+def test_fused_multi_and_accumulate(ops):
+    k = 4096
+    ns = [4096, 1024, 1024]
+    rng = np.random.default_rng(9)
+    ws = [dev(weights("q4_k", n, k, 20 + i)) for i, n in enumerate(ns)]
+    x = dev(rng.standard_normal((1, k)).astype(np.float32)).to(torch.bfloat16)
+    y0 = [dev(rng.standard_normal((1, n)).astype(np.float32)) for n in ns]
+    ys = [t.clone() for t in y0]
+    ops.mv_q8_fused_multi("q4_k", ws, x, ns, k, ys=ys, accumulate=True)
+    ref = [t.clone() for t in y0]
+    ops.mv_q8_multi("q4_k", ws, ops.quant_q8(x), ns, k, 1, ys=ref, accumulate=True)
+    for a, b in zip(ys, ref):
+        assert torch.equal(a, b)
+
+
+def test_fused_shapes_outside_the_row_kernel_are_refused(ops):
+    from loom_skills_b200 import _lib as L
+    w = dev(weights("q4_k", 64, 1024, 3))
+    x = torch.zeros(1, 1024, device="cuda")
+    with pytest.raises(L.LkError, match="no kernel"):
+        ops.mv_q8_fused("q4_k", w, x, 64, 1024)
