@@ -28,8 +28,14 @@ extern "C" {
 
 typedef struct CUstream_st* lk_stream_t;   /* == cudaStream_t */
 
-/* weight formats (ggml type ids); LK_MXFP4S = split planes (nibble plane + E8M0 scale plane), formats.py:11-14 */
-enum { LK_Q4_0 = 2, LK_Q4_K = 12, LK_IQ4_NL = 20, LK_MXFP4 = 39, LK_MXFP4S = 1039 };
+/* weight formats (ggml type ids); LK_MXFP4S = split planes (nibble plane + E8M0 scale plane), formats.py:11-14.
+ * The Q4 family (Q4_0, Q4_K, IQ4_NL) and MXFP4S run on every kernel; Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS and the
+ * ggml 17-byte MXFP4 blocks (the reference's remaining formats, formats.py:5-17) on lk_dequant, the decode matvecs
+ * (lk_mv, lk_moe_expert_mv) and the prefill GEMMs (lk_gemm, lk_moe_grouped_gemm). */
+enum {
+  LK_Q4_0 = 2, LK_Q5_0 = 6, LK_Q8_0 = 8, LK_Q3_K = 11, LK_Q4_K = 12, LK_Q5_K = 13, LK_Q6_K = 14, LK_IQ4_NL = 20,
+  LK_IQ4_XS = 23, LK_MXFP4 = 39, LK_MXFP4S = 1039
+};
 /* element types (ggml ids where ggml has one) */
 enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 30, LK_E4M3 = 1000 };
 /* GEMM epilogues (gen_gemm.py:535 `mode`): y = acc, y += acc, y = silu(acc_w) * acc_w2. LK_SWIGLU_SORTED (grouped

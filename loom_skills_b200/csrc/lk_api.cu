@@ -1,6 +1,7 @@
 // The C ABI of liblk: host-side validation, then the kernel launchers. See include/lk.h for the contract of each
 // entry point and the reference interface it replaces.
 #include "lk_common.cuh"
+#include "lk_formats.cuh"
 #include "lk_internal.h"
 
 using namespace lk;
@@ -26,15 +27,8 @@ const char* lk_strerror(int code) {
 int lk_version(void) { return 1; }
 
 int64_t lk_row_bytes(int fmt, int64_t k) {
-  int qk = 0, bb = 0;
-  switch (fmt) {
-    case LK_Q4_0: case LK_IQ4_NL: qk = 32; bb = 18; break;
-    case LK_Q4_K: qk = 256; bb = 144; break;
-    case LK_MXFP4: qk = 32; bb = 17; break;
-    case LK_MXFP4S: qk = 32; bb = 16; break;
-    default: return -1;
-  }
-  if (k <= 0 || k % qk) return -1;
+  const int qk = fmt == LK_MXFP4S ? 32 : fmt_qk(fmt), bb = fmt == LK_MXFP4S ? 16 : fmt_block_bytes(fmt);
+  if (bb == 0 || k <= 0 || k % qk) return -1;
   return k / qk * bb;
 }
 
@@ -103,7 +97,7 @@ int lk_dequant(int fmt, const void* w, const void* w_scales, int64_t n_values, v
                lk_stream_t stream) {
   if (!w || !out || n_values < 0) return LK_EINVAL;
   if (lk_row_bytes(fmt, 256) < 0) return LK_EINVAL;
-  if (n_values % (fmt == LK_Q4_K ? 256 : 32)) return LK_EINVAL;
+  if (n_values % (fmt == LK_MXFP4S ? 32 : fmt_qk(fmt))) return LK_EINVAL;
   if (out_dtype != LK_F32 && out_dtype != LK_F16) return LK_EINVAL;
   if (fmt == LK_MXFP4S && !w_scales) return LK_EINVAL;
   if (!aligned(out, 16)) return LK_EALIGN;
@@ -139,15 +133,25 @@ int lk_moe_row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, cons
   return row_scale_gather(rows, k, ku, rowmap, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
 }
 
+// formats the decode matvecs and GEMMs take: the Q4 family on the tuned kernels, the rest on the generic ones
+static bool mv_format(int fmt) {
+  return q4_family(fmt) || fmt == LK_Q5_0 || fmt == LK_Q8_0 || fmt == LK_Q3_K || fmt == LK_Q5_K || fmt == LK_Q6_K ||
+         fmt == LK_IQ4_XS || fmt == LK_MXFP4;
+}
+// the tuned Q4 kernels stream whole 256-value chunks by TMA: k % 256, 16-byte aligned rows
+static bool tuned_q4(int fmt, int k, const void* w, const void* w2) {
+  return q4_family(fmt) && k % 256 == 0 && aligned(w, 16) && (!w2 || aligned(w2, 16));
+}
+
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
           float* y, lk_stream_t stream) {
-  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
   if (n <= 0 || k <= 0 || tokens < 0) return LK_EINVAL;
-  if (k % 256) return LK_EINVAL;
+  if (k % fmt_qk(fmt)) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
   if (!x || !w || !y) return LK_EINVAL;
-  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
+  if (!aligned(x, 16)) return LK_EALIGN;
   MvArgs a{};
   a.w = (const uint8_t*)w;
   a.w2 = (const uint8_t*)w2;
@@ -160,7 +164,8 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
   a.x_dtype = x_dtype;
   a.row_bytes = lk_row_bytes(fmt, k);
   a.swiglu = w2 != nullptr;
-  return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
+  if (tuned_q4(fmt, k, w, w2)) return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
+  return mv_generic(fmt, a, (cudaStream_t)stream);
 }
 
 int lk_moe_expert_mv_mxfp4s_ex(int mode, int order, int n, int k, int assignments, int ku, int n_experts,
@@ -194,17 +199,17 @@ int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku
                         const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2,
                         const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
                         lk_stream_t stream) {
-  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
   if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
   if (mode != 0 && mode != 1) return LK_EINVAL;
-  if (k % 256) return LK_EINVAL;
+  if (k % fmt_qk(fmt)) return LK_EINVAL;
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
   if (!act_ok(act)) return LK_EINVAL;
   if (mode == 0 && (!bias) != (!bias2)) return LK_EINVAL;
   if (assignments == 0) return LK_OK;
   if (!ids || !x || !w || !y) return LK_EINVAL;
   if (mode == 0 && !fused && !w2) return LK_EINVAL;
-  if (!aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(x, 16)) return LK_EALIGN;
+  if (!aligned(x, 16)) return LK_EALIGN;
   MvArgs a{};
   a.w = (const uint8_t*)w;
   a.w2 = (mode == 0 && !fused) ? (const uint8_t*)w2 : nullptr;
@@ -223,7 +228,8 @@ int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku
   a.w2_row_offset = (mode == 0 && fused) ? n : 0;
   a.swiglu = mode == 0;
   a.epi = ExpertEpi{bias, mode == 0 ? bias2 : nullptr, mode == 0 ? act : LK_ACT_SILU, alpha, limit};
-  return mv(fmt, a, assignments, (cudaStream_t)stream);
+  if (tuned_q4(fmt, k, w, a.w2)) return mv(fmt, a, assignments, (cudaStream_t)stream);
+  return mv_generic(fmt, a, (cudaStream_t)stream);
 }
 
 int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,

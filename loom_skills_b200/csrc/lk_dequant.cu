@@ -4,14 +4,14 @@
 //              786-895) and the GEMM's f16 staging dequant16 (gen_gemm.py:281-532, moe_q4_0.py:11-38).
 // row scales   g_row_scale_f16 (gen_llm.py:1843-1912) and its fp8 twin (gen_mxfp4s.py:852-870, 887-938).
 #include "lk_common.cuh"
+#include "lk_formats.cuh"
 #include "lk_internal.h"
 
 namespace lk {
 
 __constant__ float kE2M1[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
-__constant__ int kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
-// one thread = one 32-value group; writes 32 outputs
+// one thread = one 32-value group; writes 32 outputs (exact f32 values, or the GEMM's f16 staging)
 template <int FMT, bool F16OUT>
 __global__ void k_dequant(const uint8_t* __restrict__ w, const uint8_t* __restrict__ ws, int64_t groups,
                           void* __restrict__ out) {
@@ -19,56 +19,7 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, const uint8_t* __restri
   if (gid >= groups) return;
   float v[32];
   __half h[32];
-  if (FMT == LK_Q4_0 || FMT == LK_IQ4_NL) {
-    const uint8_t* b = w + gid * 18;
-    float d = h2f(uint16_t(b[0] | (b[1] << 8)));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      int lo = b[2 + i] & 15, hi = b[2 + i] >> 4;
-      float cl = FMT == LK_Q4_0 ? float(lo - 8) : float(kIq4Values[lo]);
-      float ch = FMT == LK_Q4_0 ? float(hi - 8) : float(kIq4Values[hi]);
-      v[i] = d * cl;        // exact in f32 (f16 scale x small integer)
-      v[i + 16] = d * ch;
-    }
-    if (F16OUT)
-#pragma unroll
-      for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);   // one rounding of the exact value
-  } else if (FMT == LK_Q4_K) {
-    int64_t sb = gid >> 3;
-    int j = int(gid & 7);
-    const uint8_t* b = w + sb * 144;
-    float d = h2f(uint16_t(b[0] | (b[1] << 8)));
-    float dmin = h2f(uint16_t(b[2] | (b[3] << 8)));
-    int sc, m;
-    q4k_scale_min(b + 4, j, sc, m);
-    float a = d * float(sc), c = dmin * float(m);
-    const uint8_t* qs = b + 16 + (j >> 1) * 32;
-    int shift = (j & 1) * 4;
-    __half a16 = __float2half_rn(a), c16 = __float2half_rn(-c);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      int q = (qs[i] >> shift) & 15;
-      v[i] = __fsub_rn(__fmul_rn(a, float(q)), c);   // gguf: d*sc*q - dmin*m, the product exact
-      if (F16OUT) h[i] = __hfma(__int2half_rn(q), a16, c16);   // gen_gemm.py:526-532: one f16 fma
-    }
-  } else if (FMT == LK_MXFP4) {
-    // ggml 17-byte block: E8M0 byte, element i low nibble / i+16 high nibble; value = kv2[q] * 2^(e-128)
-    const uint8_t* b = w + gid * 17;
-    int e = b[0];
-    uint32_t bits = e < 2 ? (0x00200000u << e) : (uint32_t(e - 1) << 23);
-    float half_scale = __uint_as_float(bits);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      int lo = b[1 + i] & 15, hi = b[1 + i] >> 4;
-      float kl = 2.0f * kE2M1[lo & 7], kh = 2.0f * kE2M1[hi & 7];
-      // ggml's table holds integers: code 8 is +0, not -0
-      v[i] = half_scale * ((lo & 8) ? -kl : kl) + 0.0f;
-      v[i + 16] = half_scale * ((hi & 8) ? -kh : kh) + 0.0f;
-    }
-    if (F16OUT)
-#pragma unroll
-      for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);
-  } else {  // LK_MXFP4S: nibble plane (pairs order: element 2i low nibble, 2i+1 high) + scale plane
+  if (FMT == LK_MXFP4S) {   // nibble plane (pairs order: element 2i low nibble, 2i+1 high) + scale plane
     const uint8_t* b = w + gid * 16;
     int e = ws[gid];
     float s = e >= 1 ? __uint_as_float(uint32_t(e) << 23) : __uint_as_float(0x00400000u);
@@ -81,6 +32,12 @@ __global__ void k_dequant(const uint8_t* __restrict__ w, const uint8_t* __restri
     if (F16OUT)
 #pragma unroll
       for (int i = 0; i < 32; ++i) h[i] = __float2half_rn(v[i]);
+  } else {
+    constexpr int gpb = fmt_qk(FMT) / 32;   // groups per block
+    const uint8_t* b = w + (gid / gpb) * fmt_block_bytes(FMT);
+    const int j = int(gid % gpb);
+    if (F16OUT) group_f16<FMT>(b, j, h);
+    else group_values<FMT>(b, j, v);
   }
   if (F16OUT) {
     uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + gid * 32);
@@ -113,6 +70,12 @@ int dequant(int fmt, const void* w, const void* ws, int64_t n, void* out, int ou
     case LK_Q4_K: return launch_dequant<LK_Q4_K>(w, ws, groups, out, f16, s);
     case LK_MXFP4: return launch_dequant<LK_MXFP4>(w, ws, groups, out, f16, s);
     case LK_MXFP4S: return launch_dequant<LK_MXFP4S>(w, ws, groups, out, f16, s);
+    case LK_Q5_0: return launch_dequant<LK_Q5_0>(w, ws, groups, out, f16, s);
+    case LK_Q8_0: return launch_dequant<LK_Q8_0>(w, ws, groups, out, f16, s);
+    case LK_Q5_K: return launch_dequant<LK_Q5_K>(w, ws, groups, out, f16, s);
+    case LK_Q6_K: return launch_dequant<LK_Q6_K>(w, ws, groups, out, f16, s);
+    case LK_IQ4_XS: return launch_dequant<LK_IQ4_XS>(w, ws, groups, out, f16, s);
+    case LK_Q3_K: return launch_dequant<LK_Q3_K>(w, ws, groups, out, f16, s);
   }
   return LK_EINVAL;
 }

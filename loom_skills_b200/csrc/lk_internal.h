@@ -46,6 +46,8 @@ struct MvArgs {
   ExpertEpi epi;          // MoE mode: activation and per-expert biases (dense: SiLU, no biases)
 };
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
+// every decodable format and any k of whole blocks (lk_mvg.cu): exact f32 values x f32 activations
+int mv_generic(int fmt, const MvArgs& a, cudaStream_t s);
 
 // where a GEMM stores its tile: dst[d][row * ld + col_off + col] for d < ndst (at most 8)
 struct OutSpec {

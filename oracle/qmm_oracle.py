@@ -32,9 +32,13 @@ from __future__ import annotations
 
 import numpy as np
 
-QK = {"q4_0": 32, "q4_k": 256, "iq4_nl": 32, "mxfp4": 32}          # values per block (formats.py:16-17)
-BLOCK_BYTES = {"q4_0": 18, "q4_k": 144, "iq4_nl": 18, "mxfp4": 17}  # bytes per block (formats.py:5-10)
-GGML_TYPE = {"q4_0": 2, "q4_k": 12, "iq4_nl": 20, "mxfp4": 39}      # gguf.GGMLQuantizationType ids
+# values per block / bytes per block (formats.py:5-17) and gguf.GGMLQuantizationType ids
+QK = {"q4_0": 32, "q4_k": 256, "iq4_nl": 32, "mxfp4": 32, "q8_0": 32, "q5_0": 32, "q5_k": 256, "q6_k": 256,
+      "iq4_xs": 256, "q3_k": 256}
+BLOCK_BYTES = {"q4_0": 18, "q4_k": 144, "iq4_nl": 18, "mxfp4": 17, "q8_0": 34, "q5_0": 22, "q5_k": 176, "q6_k": 210,
+               "iq4_xs": 136, "q3_k": 110}
+GGML_TYPE = {"q4_0": 2, "q4_k": 12, "iq4_nl": 20, "mxfp4": 39, "q8_0": 8, "q5_0": 6, "q5_k": 13, "q6_k": 14,
+             "iq4_xs": 23, "q3_k": 11}
 IQ4_KVALUES = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int64)
 E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float64)
 MXFP4_F8_SHIFT = 8                      # gen_mxfp4s.py:29
@@ -180,6 +184,22 @@ def _codes4(qs):
     return np.concatenate([qs & 15, qs >> 4], axis=-1).astype(np.int64)
 
 
+def _q5k_codes(b):
+    """Q5_K 5-bit codes [B, 8 groups, 32]: nibble of page g/2 (low for even g) | bit g of qh[l] << 4 (gguf Q5_K)."""
+    qh = b[:, 16:48].astype(np.int64)
+    hb = (qh[:, None, :] >> np.arange(8).reshape(1, 8, 1)) & 1
+    qs = b[:, 48:].reshape(-1, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
+    return (qs & 15).reshape(-1, 8, 32).astype(np.int64) | (hb << 4)
+
+
+def _q6k_codes(b):
+    """Q6_K 6-bit codes 0..63 [B, 16 sub-blocks, 16] (gguf Q6_K: ql nibbles, qh 2-bit fields)."""
+    ql, qh = b[:, :128], b[:, 128:192]
+    lo = (ql.reshape(-1, 2, 1, 64) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)) & 15
+    hi = (qh.reshape(-1, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)) & 3
+    return (lo.reshape(-1, 8, 32).astype(np.int64) | (hi.reshape(-1, 8, 32).astype(np.int64) << 4)).reshape(-1, 16, 16)
+
+
 def dequant(fmt, raw, k):
     """Packed rows [..., row_bytes] (or (nibbles, scales) for planar MXFP4) -> float32 [..., k], the exact values
     the reference's numpy path uses (gguf.quants.dequantize; quant_values.loom / gen_llm.py helpers)."""
@@ -210,6 +230,47 @@ def dequant(fmt, raw, k):
         qs = b[:, 16:].reshape(-1, 4, 1, 32) >> np.array([0, 4], np.uint8).reshape(1, 1, 2, 1)
         q = (qs & 15).reshape(-1, 8, 32).astype(np.float32)
         v = (a[:, :, None] * q - c[:, :, None]).reshape(-1, 256)
+    elif fmt == "q8_0":      # gguf Q8_0.dequantize_blocks: d * int8 code
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        v = d[:, None] * b[:, 2:].view(np.int8).astype(np.float32)
+    elif fmt == "q5_0":      # gguf Q5_0: q = nibble | bit j of the u32 qh << 4; d * (q - 16)
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        qh = np.ascontiguousarray(b[:, 2:6]).view("<u4").reshape(-1, 1).astype(np.int64)
+        hb = (qh >> np.arange(32)) & 1
+        q = _codes4(b[:, 6:]) | (hb << 4)
+        v = d[:, None] * (q - 16).astype(np.float32)
+    elif fmt == "q5_k":      # gguf Q5_K: Q4_K's header and nibble pages, qh bit g of byte l = 5th bit of value l of group g
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        dmin = _f16(b[:, 2:4]).astype(np.float32)
+        sc, mn = q4_k_scale_min(b[:, 4:16])
+        a = d[:, None] * sc.astype(np.float32)
+        c = dmin[:, None] * mn.astype(np.float32)
+        v = (a[:, :, None] * _q5k_codes(b).astype(np.float32) - c[:, :, None]).reshape(-1, 256)
+    elif fmt == "q6_k":      # gguf Q6_K: ql[128] qh[64] int8 scales[16] f16 d; (d * sc[v/16]) * (q - 32)
+        sc = b[:, 192:208].view(np.int8).astype(np.float32)
+        d = _f16(b[:, 208:210]).astype(np.float32)
+        dl = (d[:, None] * sc).reshape(-1, 16, 1)
+        v = (dl * (_q6k_codes(b) - 32).astype(np.float32)).reshape(-1, 256)
+    elif fmt == "iq4_xs":    # gguf IQ4_XS: 6-bit sub-block scales (4 low bits in scales_l, 2 high in scales_h) - 32
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        sh = np.ascontiguousarray(b[:, 2:4]).view("<u2").reshape(-1, 1).astype(np.int64)
+        sl = b[:, 4:8].astype(np.int64)
+        lo = (sl.reshape(-1, 4, 1) >> np.array([0, 4]).reshape(1, 1, 2)).reshape(-1, 8) & 15
+        hi = (sh >> (2 * np.arange(8)).reshape(1, 8)) & 3
+        dl = d[:, None] * ((lo | (hi << 4)) - 32).astype(np.float32)   # [B, 8]
+        q = _codes4(b[:, 8:].reshape(-1, 16)).reshape(-1, 8, 32)
+        v = (dl[:, :, None] * IQ4_KVALUES[q].astype(np.float32)).reshape(-1, 256)
+    elif fmt == "q3_k":      # gguf Q3_K: hmask[32] qs[64] 12 bytes of 6-bit scales, f16 d; q = 2 bits - 4 * !hbit
+        hmask, qs, scb = b[:, :32], b[:, 32:96], b[:, 96:108]
+        d = _f16(b[:, 108:110]).astype(np.float32)
+        ls = (scb[:, :8].reshape(-1, 1, 8) >> np.array([0, 4], np.uint8).reshape(1, 2, 1)).reshape(-1, 16) & 15
+        hs = (scb[:, 8:].reshape(-1, 1, 4) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 4, 1)).reshape(-1, 16) & 3
+        scl = ((ls | (hs << 4)).astype(np.int64) - 32).astype(np.float32)
+        dl = (d[:, None] * scl).reshape(-1, 16, 1)
+        ql = (qs.reshape(-1, 2, 1, 32) >> np.array([0, 2, 4, 6], np.uint8).reshape(1, 1, 4, 1)).reshape(-1, 16, 16) & 3
+        hb = (hmask.reshape(-1, 1, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 1, 8, 1)).reshape(-1, 16, 16) & 1
+        q = ql.astype(np.int64) - ((hb ^ 1).astype(np.int64) << 2)
+        v = (dl * q.astype(np.float32)).reshape(-1, 256)
     elif fmt == "mxfp4":
         e = b[:, 0].astype(np.int64)
         # ggml_e8m0_to_fp32_half: 2^(e-128) (e >= 2), subnormal encodings for e < 2; doubled e2m1 table
@@ -225,8 +286,11 @@ def dequant_f16(fmt, raw, k):
     """The f16 weights the prefill GEMM stages (one rounding of the exact value):
     Q4_0 f16(d*(q-8)) (moe_q4_0.py:36-38); IQ4_NL f16(d*kvalue) (gen_gemm.py:228-231);
     Q4_K fma_f16(q, f16(d*sc), f16(-dmin*m)) (gen_gemm.py:526-532)."""
-    if fmt in ("q4_0", "iq4_nl", "mxfp4", "mxfp4_planar"):
+    if fmt in ("q4_0", "iq4_nl", "mxfp4", "mxfp4_planar", "q8_0", "q5_0", "iq4_xs", "q3_k"):
+        # one rounding of the exact value (gen_gemm.py:352-367 for Q8_0; the @g_<fmt>_values helpers + fptrunc)
         return dequant(fmt, raw, k).astype(np.float64).astype(np.float16)
+    if fmt in ("q5_k", "q6_k"):
+        return _dequant_f16_fma(fmt, raw, k)
     assert fmt == "q4_k"
     raw = np.asarray(raw, np.uint8)
     lead = raw.shape[:-1]
@@ -241,6 +305,30 @@ def dequant_f16(fmt, raw, k):
     v = q * a16[:, :, None] + c16[:, :, None]          # exact in f64; one rounding to f16 = the f16 fma
     with np.errstate(over="ignore"):
         return v.reshape(-1, 256).astype(np.float16).reshape(*lead, k)
+
+
+def _dequant_f16_fma(fmt, raw, k):
+    """The GEMM staging of Q5_K / Q6_K (gen_gemm.py:369-444, 445-498): fma_f16(q, f16(scale), f16(offset)) with
+    Q5_K: q = 5-bit code, scale = d*sc, offset = -dmin*m (as Q4_K); Q6_K: q = 6-bit code (0..63), scale = d*sc,
+    offset = -32*d*sc (both f32 products, exact). q * scale16 + offset16 is exact in f64, so its one rounding to f16
+    is the f16 fma."""
+    raw = np.asarray(raw, np.uint8)
+    lead = raw.shape[:-1]
+    b = raw.reshape(-1, BLOCK_BYTES[fmt])
+    if fmt == "q5_k":
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        dmin = _f16(b[:, 2:4]).astype(np.float32)
+        sc, mn = q4_k_scale_min(b[:, 4:16])
+        a16 = (d[:, None] * sc.astype(np.float32)).astype(np.float16).astype(np.float64)[:, :, None]
+        c16 = (-(dmin[:, None] * mn.astype(np.float32))).astype(np.float16).astype(np.float64)[:, :, None]
+        q = _q5k_codes(b).astype(np.float64)                                     # [B, 8, 32]
+    else:
+        s32 = _f16(b[:, 208:210]).astype(np.float32)[:, None] * b[:, 192:208].view(np.int8).astype(np.float32)
+        a16 = s32.astype(np.float16).astype(np.float64)[:, :, None]              # [B, 16, 1]
+        c16 = (s32 * np.float32(-32)).astype(np.float16).astype(np.float64)[:, :, None]
+        q = _q6k_codes(b).astype(np.float64)                                     # [B, 16, 16]
+    with np.errstate(over="ignore", invalid="ignore"):
+        return (q * a16 + c16).reshape(-1, 256).astype(np.float16).reshape(*lead, k)
 
 
 # ------------------------------------------------------------------------------------------------------------------

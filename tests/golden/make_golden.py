@@ -296,8 +296,42 @@ def main_moe(ref):
     print("wrote", os.path.join(HERE, "golden_moe.npz"), sum(a.nbytes for a in out.values()), "bytes uncompressed")
 
 
+def main_formats(ref):
+    """golden_formats.npz: the reference's remaining GGUF formats (formats.py:5-17: Q5_0, Q8_0, Q3_K, Q5_K, Q6_K,
+    IQ4_XS) dequantised by gguf 0.19.0 (the reference's numpy path, make_kernel_tests.py:45-47) on seeded random
+    blocks with finite f16 scales, and small float64 products of those values (make_kernel_tests.py:231-238)."""
+    from gguf import GGMLQuantizationType as T
+    from gguf.quants import dequantize
+    out = {}
+    rng = np.random.default_rng(77)
+    spec = {"q5_0": (22, 32, [0]), "q8_0": (34, 32, [0]), "q3_k": (110, 256, [108]), "q5_k": (176, 256, [0, 2]),
+            "q6_k": (210, 256, [208]), "iq4_xs": (136, 256, [0])}
+    for name, (bb, qk, offs) in spec.items():
+        nb = 64 if qk == 256 else 512
+        b = rng.integers(0, 256, (nb, bb), dtype=np.uint8)
+        for o in offs:
+            b[:, o:o + 2] = (rng.uniform(1e-4, 4e-2, nb) * rng.choice([-1, 1], nb)).astype(np.float16).view(
+                np.uint8).reshape(-1, 2)
+        out[f"{name}_raw"] = b
+        out[f"{name}_f32"] = dequantize(b.reshape(-1), T[name.upper()]).reshape(nb, -1).astype(np.float32)
+        # a matvec: 48 rows of 512 values, 3 tokens
+        n, k, t = 48, 512, 3
+        rows = rng.integers(0, 256, (n * k // qk, bb), dtype=np.uint8)
+        for o in offs:
+            rows[:, o:o + 2] = (rng.uniform(1e-3, 2e-2, len(rows)) * rng.choice([-1, 1], len(rows))).astype(
+                np.float16).view(np.uint8).reshape(-1, 2)
+        W = dequantize(rows.reshape(-1), T[name.upper()]).reshape(n, k).astype(np.float64)
+        x = rng.standard_normal((t, k)).astype(np.float32)
+        out[f"mv_{name}_w"] = rows.reshape(n, -1)
+        out[f"mv_{name}_x"] = x
+        out[f"mv_{name}_y"] = x.astype(np.float64) @ W.T
+    np.savez_compressed(os.path.join(HERE, "golden_formats.npz"), **out)
+    print("wrote", os.path.join(HERE, "golden_formats.npz"), sum(a.nbytes for a in out.values()), "bytes uncompressed")
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: make_golden.py LOOM_SKILLS_CHECKOUT")
     main(sys.argv[1])
     main_moe(sys.argv[1])
+    main_formats(sys.argv[1])

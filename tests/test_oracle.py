@@ -301,3 +301,34 @@ def test_kbench_cases_from_oracle(gmoe, kbench):
         assert (ref[64 + 17:128] == 0).all()               # padding rows of a live tile hold zeros
     y = O.combine_ref(kbench["dsc_ys"], O.wscale_ref(kbench["dsc_ids"], kbench["dsc_wts"], kbench["dsc_scales"]))
     assert O.rel_l2(y, gmoe["kb_dsc_y"]) < 1e-6
+
+
+# ---------------------------------------------------------------------------------------------------------- formats
+@pytest.fixture(scope="module")
+def gfmt():
+    with np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_formats.npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.mark.parametrize("fmt", ["q5_0", "q8_0", "q3_k", "q5_k", "q6_k", "iq4_xs"])
+def test_remaining_formats_match_gguf(gfmt, fmt):
+    # the oracle's restatement of gguf 0.19.0's dequantize_blocks, bit for bit on the golden blocks
+    raw = gfmt[f"{fmt}_raw"]
+    got = O.dequant(fmt, raw.reshape(-1), gfmt[f"{fmt}_f32"].size)
+    assert _bits_equal(got, gfmt[f"{fmt}_f32"].reshape(-1))
+    w, x = gfmt[f"mv_{fmt}_w"], gfmt[f"mv_{fmt}_x"]
+    assert O.rel_l2(O.mv_ref(fmt, w, x, w.shape[0], 512), gfmt[f"mv_{fmt}_y"]) < 1e-12
+
+
+@pytest.mark.parametrize("fmt", ["q5_k", "q6_k", "q8_0"])
+def test_f16_staging_is_one_rounding_or_the_fma(gfmt, fmt):
+    # Q8_0: one rounding of the exact value (gen_gemm.py:352-367); Q5_K / Q6_K: the f16 fma of gen_gemm.py:369-498,
+    # whose f16 scale and offset each round once: within a few f16 steps of the group's largest value
+    raw = gfmt[f"{fmt}_raw"]
+    exact = O.dequant(fmt, raw.reshape(-1), gfmt[f"{fmt}_f32"].size).astype(np.float64)
+    st = O.dequant_f16(fmt, raw.reshape(-1), exact.size).astype(np.float64)
+    if fmt == "q8_0":
+        assert np.array_equal(st, exact.astype(np.float16).astype(np.float64))
+    else:
+        gmax = np.abs(exact).reshape(-1, 16).max(-1, keepdims=True)
+        assert np.all(np.abs(st - exact).reshape(-1, 16) <= gmax * 2.0 ** -8 + 2.0 ** -24)
