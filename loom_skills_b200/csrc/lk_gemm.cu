@@ -13,6 +13,7 @@
 #include <mutex>
 
 #include "lk_common.cuh"
+#include "lk_formats.cuh"
 #include "lk_internal.h"
 
 namespace lk {
@@ -46,7 +47,29 @@ struct GemmArgs {
   // a tile of its own whose row-scaled partial product is added into y (zeroed first for store)
   int ksplit, kps;
   ExpertEpi epi;              // gate/up activation and per-expert biases (bias index: expert * n + column)
+  // window producer (formats whose packed rows are not 16-byte aligned 144-byte chunks): the weights' base
+  // pointers and packed row stride
+  const uint8_t* wp;
+  const uint8_t* w2p;
+  int64_t rb;
 };
+
+// packed bytes of one 256-value chunk of a row, and the bytes a window of it takes in shared memory: the chunk
+// copied from its 16-byte aligned start, so up to 15 bytes before and after it
+__host__ __device__ constexpr int chunk_bytes(int fmt) { return 256 / fmt_qk(fmt) * fmt_block_bytes(fmt); }
+__host__ __device__ constexpr int window_bytes(int fmt) { return (chunk_bytes(fmt) + 15 + 15) / 16 * 16; }
+
+// One 32-value group (j of the 256-value chunk) of any format into 4 swizzled 16-byte chunks of the B tile, with the
+// reference's staging (group_f16: one rounding, or the K-quants' f16 fma)
+template <int FMT>
+LK_DEV void dequant_group_any(const uint8_t* chunk, int j, uint8_t* b_tile, int r, int c0) {
+  __half h[32];
+  if (fmt_qk(FMT) == 32) group_f16<FMT>(chunk + j * fmt_block_bytes(FMT), 0, h);
+  else group_f16<FMT>(chunk, j, h);
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc)
+    *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = reinterpret_cast<const uint4*>(h)[cc];
+}
 
 // 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
 
@@ -154,7 +177,9 @@ constexpr int kStgBytes = kEpWarps * 32 * kStgStride * 4;
 
 // NBUF accumulator buffers of MH * NW * BN columns each (512 TMEM columns in all); SAP / SBP / SRP stages of the A,
 // B and packed-weight rings
-template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP>
+// WIN: the packed chunks come by per-row bulk copies of 16-byte aligned windows (any format, any row stride, a last
+// chunk of fewer than 256 values) instead of one 2-D TMA box of 144-byte chunks per stage.
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP, bool WIN>
 __global__ void __launch_bounds__(kGemmPThreads, 1)
     k_gemm_p(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
              const __grid_constant__ CUtensorMap w2map, const GemmArgs p) {
@@ -162,7 +187,10 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
   constexpr int kRowsB = BN * NW;
   constexpr int kABytes = kTM * kBK * 2;
   constexpr int kBBytes = kRowsB * kBK * 2;
-  constexpr int kRBytes = kRowsB * kChunkBytes;
+  constexpr int kCB = WIN ? chunk_bytes(FMT) : kChunkBytes;    // packed bytes of a 256-value chunk
+  constexpr int kRW = WIN ? window_bytes(FMT) : kChunkBytes;   // shared-memory bytes of one row's chunk
+  constexpr int kRBytes = kRowsB * kRW;
+  static_assert(WIN || chunk_bytes(FMT) == kChunkBytes, "the TMA box form streams 144-byte chunks");
   constexpr int kSAp = SAP;
   constexpr int kSBp = SBP;
   constexpr uint32_t kAcc = MH * NW * BN;   // accumulator columns of one tile
@@ -182,8 +210,8 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
   uint64_t* full_r = empty_b + kSBp;
   uint64_t* empty_r = full_r + SRP;
   uint64_t* acc_full = empty_r + SRP;    // [NBUF]
-  uint64_t* acc_empty = acc_full + 2;    // [NBUF]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* acc_empty = acc_full + NBUF;   // [NBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NBUF);
   int* stbl = reinterpret_cast<int*>(tmem_slot + 4);   // MoE super-tile table [3][kMaxExperts]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -269,13 +297,43 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
         if ((ks & 3) == 0) {
           const int sr = gr % SRP;
           if (gr >= SRP && !mbar_wait(&empty_r[sr], ((gr / SRP) - 1) & 1)) atomicOr(&g_status, 1u);
-          if (lane == 0) {
+          if (WIN) {
+            // every lane copies the chunk of rows lane, lane + 32, ... (those inside n): the 16-byte aligned window
+            // around the row's chunk bytes. Lane 0 announces the stage's total bytes before any copy is issued.
+            const int64_t c0b = int64_t(ks >> 2) * kCB;
+            const uint32_t clen = uint32_t(min(int64_t(kCB), p.rb - c0b));
+            uint32_t mine = 0;
+#pragma unroll
+            for (int i = 0; i < kRowsB / 32; ++i) {
+              const int r = lane + 32 * i, rl = r % BN;
+              if (n0 + rl >= p.n) continue;
+              const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
+                                    uintptr_t((int64_t(r < BN ? wrow : w2row) + rl) * p.rb + c0b);
+              mine += uint32_t(((src + clen + 15) & ~uintptr_t(15)) - (src & ~uintptr_t(15)));
+            }
+            uint32_t total = mine;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xFFFFFFFFu, total, o);
+            if (lane == 0) mbar_expect_tx(&full_r[sr], total);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < kRowsB / 32; ++i) {
+              const int r = lane + 32 * i, rl = r % BN;
+              if (n0 + rl >= p.n) continue;
+              const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
+                                    uintptr_t((int64_t(r < BN ? wrow : w2row) + rl) * p.rb + c0b);
+              const uintptr_t a0 = src & ~uintptr_t(15);
+              bulk_g2s(sR + sr * kRBytes + r * kRW, reinterpret_cast<const void*>(a0),
+                       uint32_t(((src + clen + 15) & ~uintptr_t(15)) - a0), &full_r[sr]);
+            }
+          } else if (lane == 0) {
             mbar_expect_tx(&full_r[sr], uint32_t(kRBytes));
             tma_load_2d(sR + sr * kRBytes, &wmap, (ks >> 2) * (kChunkBytes / 4), wrow, &full_r[sr]);
             if (NW == 2)
               tma_load_2d(sR + sr * kRBytes + BN * kChunkBytes, &w2map, (ks >> 2) * (kChunkBytes / 4), w2row,
                           &full_r[sr]);
           }
+          __syncwarp();
           ++gr;
         }
         const int sa = ga % kSAp;
@@ -339,8 +397,11 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
     for (int li = 0; li < my_tiles; ++li) {
       int m0, n0, e, valid;
       tile_of(int(blockIdx.x) + li * int(gridDim.x), m0, n0, e, valid);
+      const int wrow = e * p.rows_per_expert + n0, w2row = e * p.rows_per_expert2 + p.w2_row_offset + n0;
       for (int ks = ks0; ks < ks1; ++ks) {
         const int sub = ks & 3, sr = gr % SRP, sb = gb % kSBp;
+        // a chunk's last stage: its fourth, or the tile's last (a row whose last chunk holds fewer than 256 values)
+        const bool chunk_end = sub == 3 || ks == ks1 - 1;
         if (sub == 0 && !mbar_wait(&full_r[sr], (gr / SRP) & 1)) atomicOr(&g_status, 1u);
         if (gb >= kSBp && !mbar_wait(&empty_b[sb], ((gb / kSBp) - 1) & 1)) atomicOr(&g_status, 1u);
         uint8_t* bt = sB + sb * kBBytes;
@@ -348,16 +409,26 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
         for (int gi = 0; gi < kGroupsPerThread; ++gi) {
           const int item = dt * kGroupsPerThread + gi;   // (row, half) pairs
           const int r = item >> 1, h = item & 1;
-          dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
+          if (WIN) {
+            // the row's chunk starts (src mod 16) bytes into its window; rows past n hold stale bytes whose
+            // columns are never stored
+            const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
+                                  uintptr_t((int64_t(r < BN ? wrow : w2row) + r % BN) * p.rb + int64_t(ks >> 2) * kCB);
+            const uint8_t* chunk = sR + sr * kRBytes + r * kRW + (src & 15);
+            if (FMT == LK_Q4_0 || FMT == LK_IQ4_NL) dequant_group<FMT>(chunk, 2 * sub + h, bt, r, 4 * h);
+            else dequant_group_any<FMT>(chunk, 2 * sub + h, bt, r, 4 * h);
+          } else {
+            dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
+          }
         }
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&full_b[sb]);
-          if (sub == 3) mbar_arrive(&empty_r[sr]);
+          if (chunk_end) mbar_arrive(&empty_r[sr]);
         }
         ++gb;
-        if (sub == 3) ++gr;
+        if (chunk_end) ++gr;
       }
     }
   } else {
@@ -510,14 +581,15 @@ struct GemmMaps {
   CUtensorMap a, w, w2;
 };
 
-template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP>
+template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP, bool WIN>
 static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
-  constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2, kRBytes = kRowsB * kChunkBytes;
+  constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2;
+  constexpr int kRBytes = kRowsB * (WIN ? window_bytes(FMT) : kChunkBytes);
   constexpr int smem = 1024 + SAP * kABytes + SBP * kBBytes + SRP * kRBytes + kStgBytes +
-                       (2 * (SAP + SBP + SRP) + 4) * 8 + 16 + 3 * kMaxExperts * 4;
+                       (2 * (SAP + SBP + SRP) + 2 * NBUF) * 8 + 16 + 3 * kMaxExperts * 4;
   static_assert(smem <= 227 * 1024, "persistent GEMM CTA exceeds shared memory");
-  auto kern = k_gemm_p<FMT, BN, NW, MODE, GROUP, MH, NBUF, SAP, SBP, SRP>;
+  auto kern = k_gemm_p<FMT, BN, NW, MODE, GROUP, MH, NBUF, SAP, SBP, SRP, WIN>;
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   int dev = 0, sms = 0;
@@ -537,19 +609,37 @@ static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
 //   grouped gate/up  128 x 2 x 1   (MoE super-tiles hold at most 128 rows of one expert; gathered or sorted rows)
 //   grouped down     256 x 1 x 1
 template <int FMT>
-static int gemm_fmt(int mode, int group, bool short_m, const GemmMaps& m, const GemmArgs& a, dim3 grid,
-                    cudaStream_t s) {
+static int gemm_fmt(int mode, int group, bool short_m, const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   if (group == kDense) {   // persistent kernel
-    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kDense, 1, 2, 4, 2, 2>(m, a, s);
+    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kDense, 1, 2, 4, 2, 2, false>(m, a, s);
     if (short_m)
-      return mode == LK_ACC ? launch_gemm_p<FMT, 256, 1, LK_ACC, kDense, 1, 2, 4, 2, 2>(m, a, s)
-                            : launch_gemm_p<FMT, 256, 1, LK_STORE, kDense, 1, 2, 4, 2, 2>(m, a, s);
-    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 2, 2, 3, 4, 2>(m, a, s);
-    return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 3, 4, 2>(m, a, s);
+      return mode == LK_ACC ? launch_gemm_p<FMT, 256, 1, LK_ACC, kDense, 1, 2, 4, 2, 2, false>(m, a, s)
+                            : launch_gemm_p<FMT, 256, 1, LK_STORE, kDense, 1, 2, 4, 2, 2, false>(m, a, s);
+    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 2, 2, 3, 4, 2, false>(m, a, s);
+    return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 3, 4, 2, false>(m, a, s);
   }
-  if (group == kGather) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kGather, 1, 2, 4, 2, 2>(m, a, s);
-  if (mode == LK_SWIGLU_SORTED) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kSorted, 1, 2, 4, 2, 2>(m, a, s);
-  return launch_gemm_p<FMT, 256, 1, LK_STORE, kSorted, 1, 2, 4, 2, 2>(m, a, s);
+  if (group == kGather) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kGather, 1, 2, 4, 2, 2, false>(m, a, s);
+  if (mode == LK_SWIGLU_SORTED) return launch_gemm_p<FMT, 128, 2, LK_SWIGLU, kSorted, 1, 2, 4, 2, 2, false>(m, a, s);
+  return launch_gemm_p<FMT, 256, 1, LK_STORE, kSorted, 1, 2, 4, 2, 2, false>(m, a, s);
+}
+
+// the window form: 128 weight rows per stage in every mode (a window of a large chunk -- Q8_0's 272 bytes, Q6_K's
+// 210 -- takes up to 288 bytes a row), so the rings fit shared memory:
+//   dense swiglu 64 x 2 x 1; dense store/acc 128 x 1 x 2 (at most 128 rows: 128 x 1 x 1); grouped gate/up 64 x 2 x 1;
+//   grouped down 128 x 1 x 1
+template <int FMT>
+static int gemm_fmt_win(int mode, int group, bool short_m, const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
+  if (group == kDense) {
+    if (mode == LK_SWIGLU) return launch_gemm_p<FMT, 64, 2, LK_SWIGLU, kDense, 1, 4, 4, 4, 2, true>(m, a, s);
+    if (short_m)
+      return mode == LK_ACC ? launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 1, 4, 4, 4, 2, true>(m, a, s)
+                            : launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 1, 4, 4, 4, 2, true>(m, a, s);
+    if (mode == LK_ACC) return launch_gemm_p<FMT, 128, 1, LK_ACC, kDense, 2, 2, 2, 4, 2, true>(m, a, s);
+    return launch_gemm_p<FMT, 128, 1, LK_STORE, kDense, 2, 2, 2, 4, 2, true>(m, a, s);
+  }
+  if (group == kGather) return launch_gemm_p<FMT, 64, 2, LK_SWIGLU, kGather, 1, 4, 4, 4, 2, true>(m, a, s);
+  if (mode == LK_SWIGLU_SORTED) return launch_gemm_p<FMT, 64, 2, LK_SWIGLU, kSorted, 1, 4, 4, 4, 2, true>(m, a, s);
+  return launch_gemm_p<FMT, 128, 1, LK_STORE, kSorted, 1, 4, 4, 4, 2, true>(m, a, s);
 }
 
 // K ranges for a dense store / acc GEMM of `tiles` output tiles and kp packed stages on `sms` persistent CTAs: the
@@ -612,15 +702,23 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     w2rows = int64_t(n_experts) * a.rows_per_expert2;
   }
   a.w2_row_offset = (mode != LK_STORE && mode != LK_ACC && !w2) ? int(w2_offset / rb) : 0;
-  // at most 128 rows (dense store / acc): 128-row tiles of 256 weight rows
+  // the window producer: every format but the Q4 family's 144-byte chunks in 16-byte aligned rows
+  const bool win = !((fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL) && k % 256 == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(w2) & 15) == 0);
+  a.wp = static_cast<const uint8_t*>(w);
+  a.w2p = static_cast<const uint8_t*>(w2 ? w2 : w);
+  a.rb = rb;
+  // at most 128 rows (dense store / acc): 128-row tiles of 256 weight rows (window form: 128)
   const bool short_m = group == kDense && mode != LK_SWIGLU && rows <= kBM;
-  // weight rows per tile: 256 for grouped down and short dense, 128 per weight otherwise
-  const int bn = ((group == kSorted && mode == LK_STORE) || short_m) ? 256 : 128;
+  // weight rows per tile (per weight): the TMA form 256 for grouped down and short dense, 128 otherwise; the window
+  // form 128, 64 per weight for gate/up
+  const bool gu = mode == LK_SWIGLU || mode == LK_SWIGLU_SORTED;
+  const int bn = win ? (gu ? 64 : 128) : (((group == kSorted && mode == LK_STORE) || short_m) ? 256 : 128);
   const int tm = (group == kDense && mode != LK_SWIGLU && !short_m) ? 2 * kBM : kBM;   // tile rows
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int kp = k / 256;
+  const int kp = (k + 255) / 256;   // packed chunks of 256 values (the last one may be shorter)
   a.ksplit = 1;
   a.kps = kp;
   // fewer output tiles than SMs, one destination: the K ranges may add into y
@@ -634,22 +732,35 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
                                        CU_TENSOR_MAP_SWIZZLE_128B)   // one-row boxes for gather4
                             : make_map(&m.a, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, k, kBK, tm,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc == LK_OK)
+  if (rc == LK_OK && !win)
     rc = make_map(&m.w, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, wrows, rb / 4, kChunkBytes / 4, bn,
                   CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc == LK_OK)
+  if (rc == LK_OK && !win)
     rc = w2 ? make_map(&m.w2, w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w2rows, rb / 4, kChunkBytes / 4, bn,
                        CU_TENSOR_MAP_SWIZZLE_NONE)
             : (m.w2 = m.w, LK_OK);
   if (rc != LK_OK) return rc;
-  // grouped: one CTA per possible 128-row super-tile (at most one per schedule tile)
-  dim3 grid((n + bn - 1) / bn, group == kDense ? (rows + tm - 1) / tm : rows / 64);
+  if (win) m.w = m.w2 = m.a;   // unused by the window form
   if (a.ksplit > 1 && mode == LK_STORE && cudaMemsetAsync(y, 0, size_t(rows) * n * 4, s) != cudaSuccess)
     return LK_ECUDA;   // the K ranges add into a zeroed y
+  if (!win) {
+    switch (fmt) {
+      case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, short_m, m, a, s);
+      case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, short_m, m, a, s);
+      case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, short_m, m, a, s);
+    }
+    return LK_EUNSUPPORTED;
+  }
   switch (fmt) {
-    case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, short_m, m, a, grid, s);
-    case LK_Q4_K: return gemm_fmt<LK_Q4_K>(mode, group, short_m, m, a, grid, s);
-    case LK_IQ4_NL: return gemm_fmt<LK_IQ4_NL>(mode, group, short_m, m, a, grid, s);
+    case LK_Q4_0: return gemm_fmt_win<LK_Q4_0>(mode, group, short_m, m, a, s);
+    case LK_IQ4_NL: return gemm_fmt_win<LK_IQ4_NL>(mode, group, short_m, m, a, s);
+    case LK_Q5_0: return gemm_fmt_win<LK_Q5_0>(mode, group, short_m, m, a, s);
+    case LK_Q8_0: return gemm_fmt_win<LK_Q8_0>(mode, group, short_m, m, a, s);
+    case LK_Q5_K: return gemm_fmt_win<LK_Q5_K>(mode, group, short_m, m, a, s);
+    case LK_Q6_K: return gemm_fmt_win<LK_Q6_K>(mode, group, short_m, m, a, s);
+    case LK_IQ4_XS: return gemm_fmt_win<LK_IQ4_XS>(mode, group, short_m, m, a, s);
+    case LK_Q3_K: return gemm_fmt_win<LK_Q3_K>(mode, group, short_m, m, a, s);
+    case LK_MXFP4: return gemm_fmt_win<LK_MXFP4>(mode, group, short_m, m, a, s);
   }
   return LK_EUNSUPPORTED;
 }

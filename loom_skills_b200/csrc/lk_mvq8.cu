@@ -362,27 +362,44 @@ enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
 // bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
 __host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
 
-// One 32-value group of g_quant_q8 (gen_llm.py:683-750) by one warp, lane = value: d = amax / 127, q = round(x / d)
-// (halves away from zero; 0 for an all-zero group), codes[g*32 + lane] = q, meta[g] = (f16-rounded d, sum of q). The
-// same arithmetic as k_quant_q8, so the codes and meta are the same bit for bit.
+// g_quant_q8 (gen_llm.py:683-750) of the row's groups cw, cw + ncw, ... by one warp, lane = value of a group:
+// d = amax / 127, q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + lane] = q,
+// meta[g] = (f16-rounded d, sum of q). The same arithmetic as k_quant_q8, so the codes and meta are the same bit for
+// bit. All of the warp's activation loads go out before any group is quantised (one memory latency, not one per
+// group); kMaxQG bounds the groups per warp (k <= 12288 over 8 consumer warps).
+constexpr int kMaxQG = 48;
 template <int XIN>
-LK_DEV void quant_group(const void* x, int g, int lane, int8_t* codes, float* meta) {
+LK_DEV void quant_groups(const void* x, int k, int cw, int ncw, int lane, int8_t* codes, float* meta) {
   static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
-  const int idx = g * 32 + lane;
-  const float v = XIN == kXinBF16 ? bf2f(static_cast<const uint16_t*>(x)[idx]) : static_cast<const float*>(x)[idx];
-  float amax = fabsf(v);
+  const int ng = (k / 32 - cw + ncw - 1) / ncw;
+  float xv[kMaxQG];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-  const float d = amax / 127.0f;
-  int q = 0;
-  if (amax > 0.0f) q = int(roundf(v / d));   // ordered compare: a NaN maximum gives code 0, like the reference
-  codes[idx] = int8_t(q);
-  int sum = q;
+  for (int i = 0; i < kMaxQG; ++i) {
+    const int idx = (cw + i * ncw) * 32 + lane;
+    xv[i] = 0.f;
+    if (i < ng)
+      xv[i] = XIN == kXinBF16 ? bf2f(__ldg(static_cast<const uint16_t*>(x) + idx))
+                              : __ldg(static_cast<const float*>(x) + idx);
+  }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-  if (lane == 0) {
-    meta[2 * g] = __half2float(__float2half_rn(d));
-    meta[2 * g + 1] = float(sum);
+  for (int i = 0; i < kMaxQG; ++i) {
+    if (i >= ng) break;
+    const int g = cw + i * ncw;
+    const float v = xv[i];
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    const float d = amax / 127.0f;
+    int q = 0;
+    if (amax > 0.0f) q = int(roundf(v / d));   // ordered compare: a NaN maximum gives code 0, like the reference
+    codes[g * 32 + lane] = int8_t(q);
+    int sum = q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if (lane == 0) {
+      meta[2 * g] = __half2float(__float2half_rn(d));
+      meta[2 * g + 1] = float(sum);
+    }
   }
 }
 
@@ -445,8 +462,7 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
       // every consumer warp of the CTA takes groups cw, cw + ncw, ... of the row; then all of them read the codes
       uint8_t* xs = smem_all + RINGS * ring_bytes(stage_bytes);
       const int cw = ring * kCW + (warp - 1), ncw = RINGS * kCW;
-      for (int g = cw; g < p.k / 32; g += ncw)
-        quant_group<XIN>(p.x, g, lane, reinterpret_cast<int8_t*>(xs), reinterpret_cast<float*>(xs + p.k));
+      quant_groups<XIN>(p.x, p.k, cw, ncw, lane, reinterpret_cast<int8_t*>(xs), reinterpret_cast<float*>(xs + p.k));
       asm volatile("bar.sync 1, %0;" ::"r"(ncw * 32) : "memory");   // consumer warps only
       xq = xs;
     }
