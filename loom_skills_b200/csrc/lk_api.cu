@@ -9,6 +9,16 @@ using namespace lk;
 static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 static bool q4_family(int fmt) { return fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL; }
 static bool act_ok(int act) { return act == LK_ACT_SILU || act == LK_ACT_GELU || act == LK_ACT_SWIGLU_OAI; }
+// formats the decode matvecs and GEMMs take: the Q4 family on the tuned kernels, the rest on the generic ones
+static bool mv_format(int fmt) {
+  return q4_family(fmt) || fmt == LK_Q5_0 || fmt == LK_Q8_0 || fmt == LK_Q3_K || fmt == LK_Q5_K || fmt == LK_Q6_K ||
+         fmt == LK_IQ4_XS || fmt == LK_MXFP4;
+}
+// the tuned Q4 kernels stream whole 256-value chunks by TMA: k % 256, 16-byte aligned rows
+static bool tuned_q4(int fmt, int k, const void* w, const void* w2) {
+  return q4_family(fmt) && k % 256 == 0 && aligned(w, 16) && (!w2 || aligned(w2, 16));
+}
+
 
 extern "C" {
 
@@ -133,16 +143,6 @@ int lk_moe_row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, cons
   return row_scale_gather(rows, k, ku, rowmap, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
 }
 
-// formats the decode matvecs and GEMMs take: the Q4 family on the tuned kernels, the rest on the generic ones
-static bool mv_format(int fmt) {
-  return q4_family(fmt) || fmt == LK_Q5_0 || fmt == LK_Q8_0 || fmt == LK_Q3_K || fmt == LK_Q5_K || fmt == LK_Q6_K ||
-         fmt == LK_IQ4_XS || fmt == LK_MXFP4;
-}
-// the tuned Q4 kernels stream whole 256-value chunks by TMA: k % 256, 16-byte aligned rows
-static bool tuned_q4(int fmt, int k, const void* w, const void* w2) {
-  return q4_family(fmt) && k % 256 == 0 && aligned(w, 16) && (!w2 || aligned(w2, 16));
-}
-
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
           float* y, lk_stream_t stream) {
   if (!mv_format(fmt)) return LK_EUNSUPPORTED;
@@ -239,16 +239,27 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                              nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
 }
 
+// the prefill GEMMs' weight contract: a whole number of 64-value stages and of the format's blocks; Q4_K keeps its
+// 16-byte aligned rows (it always takes the TMA box form), the others need 2-byte aligned blocks (MXFP4: any)
+static int gemm_weight_check(int fmt, int k, const void* w, const void* w2) {
+  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
+  if (k % 64 || k % fmt_qk(fmt)) return LK_EINVAL;
+  const uintptr_t al = fmt == LK_Q4_K ? 16 : fmt == LK_MXFP4 ? 1 : 2;
+  if (!aligned(w, al) || (w2 && !aligned(w2, al))) return LK_EALIGN;
+  return LK_OK;
+}
+
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
             const void* w2, float* y, lk_stream_t stream) {
-  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_ACC && mode != LK_SWIGLU) return LK_EINVAL;
   if (rows < 0 || k <= 0 || n <= 0) return LK_EINVAL;
-  if (k % 256 || n % 16) return LK_EINVAL;
+  if (n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
   if (!x16 || !scales || !w || !y) return LK_EINVAL;
   if (mode == LK_SWIGLU && !w2) return LK_EINVAL;
-  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
+  if (int rc = gemm_weight_check(fmt, k, w, w2)) return rc;
+  if (!aligned(x16, 16) || !aligned(y, 16)) return LK_EALIGN;
   return gemm(fmt, mode, rows, k, n, x16, scales, w, w2, y, (cudaStream_t)stream, nullptr, nullptr, rows, 1, 1, 0, 0);
 }
 
@@ -281,7 +292,7 @@ int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows,
                            const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
                            const void* w, const void* w2, const float* bias, const float* bias2, int act, float alpha,
                            float limit, float* y, lk_stream_t stream) {
-  if (!q4_family(fmt)) return LK_EUNSUPPORTED;
+  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
@@ -290,8 +301,9 @@ int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows,
   const bool gu = mode != LK_STORE;   // gate/up: gathered or already sorted activation rows
   if (gu && !fused && !w2) return LK_EINVAL;
   if (gu && (!bias) != (!bias2)) return LK_EINVAL;   // gate and up biases come together
-  if (k % 256 || n % 16) return LK_EINVAL;
-  if (!aligned(x16, 16) || !aligned(w, 16) || (w2 && !aligned(w2, 16)) || !aligned(y, 16)) return LK_EALIGN;
+  if (n % 16) return LK_EINVAL;
+  if (int rc = gemm_weight_check(fmt, k, w, w2)) return rc;
+  if (!aligned(x16, 16) || !aligned(y, 16)) return LK_EALIGN;
   if (rows == 0) return LK_OK;
   int64_t rb = lk_row_bytes(fmt, k);
   int64_t stride = rb * n * ((gu && fused) ? 2 : 1);

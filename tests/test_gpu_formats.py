@@ -141,3 +141,70 @@ def test_kbench_decode_down(ops, gmoe, t):
     ys = ops.moe_expert_mv("q4_0", "dn", dev(kb[f"decode_t{t}_ids"].reshape(-1)), dev(kb[f"decode_t{t}_xdn"]),
                            dev(kb["wd"]), H, F, U, E)
     np.testing.assert_allclose(host(ys)[:, gmoe["kb_cols_h"]], gmoe[f"kb_decode_dn_t{t}"], atol=2e-5, rtol=2e-4)
+
+
+# ---------------------------------------------------------------------------------------------------------- GEMM
+def row_scaled(rows, k, seed):
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((rows, k)) * rng.choice([1.0, 3e4], (rows, 1))).astype(np.float32)
+    return O.row_scale_f16(x)
+
+
+@pytest.mark.parametrize("fmt", FORMATS + ["mxfp4", "q4_0", "iq4_nl"])
+@pytest.mark.parametrize("rows,n,k", [(200, 272, 1024), (64, 512, 2048), (300, 192, 1536)])
+def test_gemm_store(ops, fmt, rows, n, k):
+    # the window form of the tcgen05 GEMM (Q4_0 / IQ4_NL take it when k is not a multiple of 256: 1536 is)
+    if fmt == "mxfp4":
+        w = O.quantize_mxfp4((np.random.default_rng(41).standard_normal((n, k)) * 0.02).astype(np.float32), "ggml")
+    else:
+        w = blocks(fmt, n, k, 41)
+    x16, sc = row_scaled(rows, k, 42)
+    y = host(ops.gemm(fmt, "store", dev(x16), dev(sc), dev(w), n))
+    W16 = O.dequant_f16(fmt, w, k).astype(np.float64).reshape(n, k)
+    ref16 = (x16.astype(np.float64) @ W16.T) * sc[:, 1:2]
+    assert O.rel_l2(y, ref16) < 1e-5, O.rel_l2(y, ref16)          # the reference's staged weights, f32 sums
+    assert O.rel_l2(y, O.gemm_ref(fmt, w, x16, sc, n, k)) < TOL
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("fmt", ["q6_k", "q8_0", "q3_k"])
+def test_gemm_swiglu_acc(ops, fmt):
+    rows, n, k = 256, 320, 1024
+    w, w2 = blocks(fmt, n, k, 51), blocks(fmt, n, k, 52)
+    x16, sc = row_scaled(rows, k, 53)
+    ys = host(ops.gemm(fmt, "swiglu", dev(x16), dev(sc), dev(w), n, w2=dev(w2)))
+    assert O.rel_l2(ys, O.gemm_ref(fmt, w, x16, sc, n, k, mode="swiglu", w2=w2)) < TOL
+    y0 = np.random.default_rng(54).standard_normal((rows, n)).astype(np.float32)
+    ya = dev(y0)
+    ops.gemm(fmt, "acc", dev(x16), dev(sc), dev(w), n, y=ya)
+    assert O.rel_l2(host(ya), O.gemm_ref(fmt, w, x16, sc, n, k, mode="acc", y_old=y0)) < TOL
+
+
+@pytest.mark.parametrize("fmt", ["q6_k", "q5_k"])
+def test_grouped_gemms(ops, fmt):
+    E, ku, H, F, tokens = 8, 4, 512, 256, 70
+    rng = np.random.default_rng(60)
+    w_gu = np.stack([blocks(fmt, 2 * F, H, 600 + e) for e in range(E)])
+    w_dn = np.stack([blocks(fmt, H, F, 700 + e) for e in range(E)])
+    x = rng.standard_normal((tokens, H)).astype(np.float32)
+    lg = rng.standard_normal((tokens, E)).astype(np.float32)
+    y = host(ops.moe_ffn(fmt, dev(x), dev(lg), dev(w_gu), dev(w_dn), H, F, E, ku, prefill=True))
+    ids, wts = O.route_ref(lg, ku)
+    ref = O.moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, H, F, E)
+    assert O.rel_l2(y, ref) < TOL, O.rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("t", [63, 65])
+def test_kbench_grouped_down(ops, gmoe, t):
+    # gen_bench.py:227-236: the grouped down GEMM over F = 704 (22 Q4_0 blocks a row), tile_info [[7,64],[0,17],
+    # [3,1],[-1,0]], sorted rows (padding rows zero), row scales in {0.5, 1, 2}, sentinel 42
+    kb = O.kbench_moe_inputs(490)
+    H, F, E, U = O.KB_H, O.KB_F, O.KB_E, O.KB_U
+    ti = dev(np.array(O.KB_TILE_INFO, np.int32))
+    rm = dev(kb[f"grouped_t{t}_rm"])
+    y = torch.full((256, H), O.KB_SENTINEL, dtype=torch.float32, device="cuda")
+    ops.moe_grouped_gemm("q4_0", "store", ti, rm, dev(kb[f"grouped_t{t}_xd"]), dev(kb[f"grouped_t{t}_sd"]),
+                         dev(kb["wd"]), H, U, E, y=y)
+    yh = host(y)
+    assert (yh[192:] == O.KB_SENTINEL).all()
+    np.testing.assert_allclose(yh[:, gmoe["kb_cols_h"]], gmoe[f"kb_grouped_dn_t{t}"], atol=2e-5, rtol=2e-4)
