@@ -93,7 +93,7 @@ int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, 
     if (!aligned(w[g], 16)) return LK_EALIGN;
   }
   if (!x) return LK_EINVAL;
-  if (!aligned(x, x_dtype == LK_BF16 ? 2 : 4)) return LK_EALIGN;
+  if (!aligned(x, 16)) return LK_EALIGN;
   if (k % 4096 || k > 3 * 4096) return LK_EUNSUPPORTED;
   return mv_q8_fused(fmt, nseg, n, w, y, k, accumulate, x, x_dtype, (cudaStream_t)stream);
 }

@@ -362,44 +362,59 @@ enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
 // bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
 __host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
 
-// g_quant_q8 (gen_llm.py:683-750) of the row's groups cw, cw + ncw, ... by one warp, lane = value of a group:
-// d = amax / 127, q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + lane] = q,
-// meta[g] = (f16-rounded d, sum of q). The same arithmetic as k_quant_q8, so the codes and meta are the same bit for
-// bit. All of the warp's activation loads go out before any group is quantised (one memory latency, not one per
-// group); kMaxQG bounds the groups per warp (k <= 12288 over 8 consumer warps).
-constexpr int kMaxQG = 48;
+// g_quant_q8 (gen_llm.py:683-750) of the row's 32-value groups t, t + nt, ... by thread t of the nt quantising threads,
+// one whole group per thread (no cross-lane reductions: every group is an independent chain): d = amax / 127,
+// q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + i] = q_i, meta[g] = (f16-rounded d,
+// sum of q). The same arithmetic as k_quant_q8, so the codes and meta are the same bit for bit. The group's 32 values
+// come in as two or four 16-byte loads (x 16-byte aligned).
 template <int XIN>
-LK_DEV void quant_groups(const void* x, int k, int cw, int ncw, int lane, int8_t* codes, float* meta) {
+LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, float* meta) {
   static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
-  const int ng = (k / 32 - cw + ncw - 1) / ncw;
-  float xv[kMaxQG];
+  for (int g = t; g < k / 32; g += nt) {
+    float v[32];
+    if (XIN == kXinBF16) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + g * 32);
 #pragma unroll
-  for (int i = 0; i < kMaxQG; ++i) {
-    const int idx = (cw + i * ncw) * 32 + lane;
-    xv[i] = 0.f;
-    if (i < ng)
-      xv[i] = XIN == kXinBF16 ? bf2f(__ldg(static_cast<const uint16_t*>(x) + idx))
-                              : __ldg(static_cast<const float*>(x) + idx);
-  }
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = __ldg(p + i);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int i = 0; i < kMaxQG; ++i) {
-    if (i >= ng) break;
-    const int g = cw + i * ncw;
-    const float v = xv[i];
-    float amax = fabsf(v);
+        for (int j = 0; j < 4; ++j) {
+          v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+          v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+        }
+      }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + g * 32);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-    const float d = amax / 127.0f;
-    int q = 0;
-    if (amax > 0.0f) q = int(roundf(v / d));   // ordered compare: a NaN maximum gives code 0, like the reference
-    codes[g * 32 + lane] = int8_t(q);
-    int sum = q;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-    if (lane == 0) {
-      meta[2 * g] = __half2float(__float2half_rn(d));
-      meta[2 * g + 1] = float(sum);
+      for (int i = 0; i < 8; ++i) {
+        const float4 f = __ldg(p + i);
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
+      }
     }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = amax / 127.0f;
+    int sum = 0;
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = 0u;
+    if (amax > 0.0f) {   // ordered compare: a NaN maximum gives codes 0, like the reference
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int q = int(roundf(v[i] / d));
+        sum += q;
+        w[i >> 2] |= (uint32_t(q) & 0xffu) << (8 * (i & 3));
+      }
+    }
+    uint4* c = reinterpret_cast<uint4*>(codes + g * 32);
+    c[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    c[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    reinterpret_cast<float2*>(meta)[g] = make_float2(__half2float(__float2half_rn(d)), float(sum));
   }
 }
 
@@ -410,6 +425,7 @@ LK_DEV void quant_groups(const void* x, int k, int cw, int ncw, int lane, int8_t
 // XIN == kXinCodes: the activation codes come from lk_quant_q8's buffer (p.xq). kXinF32 / kXinBF16: the consumer warps
 // of the CTA first quantise the row p.x into shared memory together (the g_quant_q8 launch folded into the
 // matvec's prologue; it overlaps the first weight stage's flight), then read their codes from there.
+// k_quant_q8 reduces a group across a warp; here a group is one thread's, so the CTA's groups run side by side.
 template <int FMT, int UPL, int HALVES, int RINGS, int XIN>
 __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
@@ -462,7 +478,8 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
       // every consumer warp of the CTA takes groups cw, cw + ncw, ... of the row; then all of them read the codes
       uint8_t* xs = smem_all + RINGS * ring_bytes(stage_bytes);
       const int cw = ring * kCW + (warp - 1), ncw = RINGS * kCW;
-      quant_groups<XIN>(p.x, p.k, cw, ncw, lane, reinterpret_cast<int8_t*>(xs), reinterpret_cast<float*>(xs + p.k));
+      quant_groups<XIN>(p.x, p.k, cw * 32 + lane, ncw * 32, reinterpret_cast<int8_t*>(xs),
+                        reinterpret_cast<float*>(xs + p.k));
       asm volatile("bar.sync 1, %0;" ::"r"(ncw * 32) : "memory");   // consumer warps only
       xq = xs;
     }
