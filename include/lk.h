@@ -123,7 +123,7 @@ int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float*
  * quantised to Q8_1 codes inside the matvec -- each CTA quantises the row into its shared memory, the codes and group
  * meta bit for bit lk_quant_q8's -- and contracted with the weight codes as lk_mv_q8 does; no xq buffer exists.
  * Formats Q4_0 and Q4_K, k a multiple of 4096 up to 12288 (LK_EUNSUPPORTED otherwise: lk_quant_q8 + lk_mv_q8 cover
- * every other shape). The _multi form takes up to 4 weights that share x, as lk_mv_q8_multi. */
+ * every other shape); x 16-byte aligned. The _multi form takes up to 4 weights that share x, as lk_mv_q8_multi. */
 int lk_mv_q8_fused(int fmt, int n, int k, int accumulate, const void* x, int x_dtype, const void* w, float* y,
                    lk_stream_t stream);
 int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int accumulate,
