@@ -338,14 +338,16 @@ def _combine_out(tokens, h, x, y_shared):
 
 def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None, gating=1, router_bias=None,
             scale=1.0, act="silu", b_gate=None, b_up=None, b_down=None, down_scale=None, y_shared=None,
-            shared_gate_w=None, alpha=1.702, limit=7.0):
+            shared_gate_w=None, alpha=1.702, limit=7.0, w_up=None, fmt_down=None):
     """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route (gating 1/2/3, router bias,
     expert_weights_scale) -> per-expert down scale folded into the weights (g_moe_wscale) -> bucket -> grouped gate/up
     (act + biases) -> row scale -> grouped down (+ bias) -> weighted combine (prefill), or per-assignment expert
     matvecs (decode). The combine adds into y_shared (the shared experts' output) when given -- scaled first by the
     shared-expert gate sigmoid(x . shared_gate_w) when that is given -- else into a new tensor.
-    x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values;
-    w_dn: per expert h rows of f values; biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
+    x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values --
+    or, with w_up given (GGUF's separate ffn_gate_exps / ffn_up_exps), per expert f gate rows, and w_up its f up rows;
+    w_dn: per expert h rows of f values, in fmt_down when it differs from fmt (GGUF quants often keep ffn_down_exps in
+    a wider format); biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
     switches to the GEMMs at 64 tokens (gen_llm.py:6107); here from 192 assignments (tokens * ku), where they
     measured faster on configs[2] shapes (top-8 of 128 experts: matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 /
     312 us). `prefill` forces either path."""
@@ -356,18 +358,19 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     ep = dict(act=act, alpha=alpha, limit=limit)
     if prefill is None:
         prefill = tokens * ku >= 192
+    fused = w_up is None
     if not prefill:
-        act_ = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=True, bias=b_gate,
-                             bias2=b_up, **ep)
-        ys = moe_expert_mv(fmt, "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts, bias=b_down)
+        act_ = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=fused, w2=w_up,
+                             bias=b_gate, bias2=b_up, **ep)
+        ys = moe_expert_mv(fmt_down or fmt, "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts, bias=b_down)
         return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
     ti, rm, pos = moe_bucket(ids, n_experts)
     # the token rows row-scaled straight into bucket order: gate/up then reads plain tiles (no row gather)
     x16, sc = moe_row_scale_gather(x, rm, ku)
-    act_ = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=True, bias=b_gate,
-                            bias2=b_up, **ep)
+    act_ = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=fused, w2=w_up,
+                            bias=b_gate, bias2=b_up, **ep)
     a16, asc = row_scale_f16(act_)
-    ys = moe_grouped_gemm(fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts, bias=b_down)
+    ys = moe_grouped_gemm(fmt_down or fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts, bias=b_down)
     return moe_combine_sorted(ys, pos, wts, y=y, accumulate=acc, sg=sg)
 
 
