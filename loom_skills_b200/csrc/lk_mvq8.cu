@@ -362,20 +362,21 @@ enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
 // bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
 __host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
 
-// g_quant_q8 (gen_llm.py:683-750) of the row's 32-value groups t, t + nt, ... by thread t of the nt quantising threads,
-// one whole group per thread (no cross-lane reductions: every group is an independent chain): d = amax / 127,
-// q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + i] = q_i, meta[g] = (f16-rounded d,
-// sum of q). The same arithmetic as k_quant_q8, so the codes and meta are the same bit for bit. The group's 32 values
-// come in as two or four 16-byte loads (x 16-byte aligned).
+// g_quant_q8 (gen_llm.py:683-750) of the row by the nt quantising threads: thread t takes the 16-value half-groups
+// t, t + nt, ... (nt even, so the two halves of a group sit in lanes 2j, 2j + 1 and meet by one shuffle):
+// d = amax / 127, q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + i] = q_i,
+// meta[g] = (f16-rounded d, sum of q). The codes and meta are k_quant_q8's bit for bit: x / d is taken as x * (1/d),
+// which is within 2 units in the last place of the correctly rounded quotient, and only where that product lies
+// within 2^-14 of a rounding boundary k + 1/2 (so the two could round apart) is the exact quotient x / d computed.
 template <int XIN>
 LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, float* meta) {
   static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
-  for (int g = t; g < k / 32; g += nt) {
-    float v[32];
+  for (int hg = t; hg < k / 16; hg += nt) {
+    float v[16];
     if (XIN == kXinBF16) {
-      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + g * 32);
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + hg * 16);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 2; ++i) {
         const uint4 u = __ldg(p + i);
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -385,9 +386,9 @@ LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, flo
         }
       }
     } else {
-      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + g * 32);
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + hg * 16);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         const float4 f = __ldg(p + i);
         v[4 * i] = f.x;
         v[4 * i + 1] = f.y;
@@ -397,24 +398,27 @@ LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, flo
     }
     float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
     const float d = amax / 127.0f;
     int sum = 0;
-    uint32_t w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) w[i] = 0u;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (amax > 0.0f) {   // ordered compare: a NaN maximum gives codes 0, like the reference
+      const float r = __frcp_rn(d);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int q = int(roundf(v[i] / d));
+      for (int i = 0; i < 16; ++i) {
+        float y = __fmul_rn(v[i], r);
+        const float a = fabsf(y);
+        if (!(fabsf(a - floorf(a) - 0.5f) > 6.103515625e-05f)) y = v[i] / d;   // near k + 1/2 (or NaN): exact
+        const int q = int(roundf(y));
         sum += q;
         w[i >> 2] |= (uint32_t(q) & 0xffu) << (8 * (i & 3));
       }
     }
-    uint4* c = reinterpret_cast<uint4*>(codes + g * 32);
-    c[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    c[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    reinterpret_cast<float2*>(meta)[g] = make_float2(__half2float(__float2half_rn(d)), float(sum));
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    reinterpret_cast<uint4*>(codes)[hg] = make_uint4(w[0], w[1], w[2], w[3]);
+    if ((hg & 1) == 0) reinterpret_cast<float2*>(meta)[hg >> 1] = make_float2(__half2float(__float2half_rn(d)),
+                                                                               float(sum));
   }
 }
 

@@ -151,3 +151,23 @@ def test_fused_shapes_outside_the_row_kernel_are_refused(ops):
     x = torch.zeros(1, 1024, device="cuda")
     with pytest.raises(L.LkError, match="no kernel"):
         ops.mv_q8_fused("q4_k", w, x, 64, 1024)
+
+
+def test_fused_quantisation_rounding_boundaries(ops):
+    # activations whose x / d lie on or next to k + 1/2 (exact ties with d = 1; near ties with d = 100/127): the
+    # in-kernel quantisation must round them as lk_quant_q8 does (codes compared through the matvec, bit for bit)
+    k, n = 4096, 512
+    rng = np.random.default_rng(17)
+    x = np.empty((1, k), np.float32)
+    g = x.reshape(-1, 32)
+    half = rng.integers(-126, 126, g.shape).astype(np.float32) + 0.5
+    g[0::2] = half[0::2]
+    g[0::2, 0] = 127.0                                            # d = 127 / 127 = 1: x / d = x, exact ties
+    d = np.float32(100.0) / np.float32(127.0)
+    g[1::2] = (half[1::2] * d).astype(np.float32)                 # x / d within a few ulps of k + 1/2
+    g[1::2] = np.nextafter(g[1::2], rng.choice([-np.inf, np.inf], g[1::2].shape)).astype(np.float32)
+    g[1::2, 0] = 100.0
+    w = dev(weights("q4_k", n, k, 9))
+    for xt in (dev(x), dev(x).to(torch.bfloat16)):
+        ref = ops.mv_q8("q4_k", w, ops.quant_q8(xt), n, k, 1)
+        assert torch.equal(ops.mv_q8_fused("q4_k", w, xt, n, k), ref)
