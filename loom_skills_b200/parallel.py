@@ -103,7 +103,12 @@ class ShardedGemm:
     """y [rows][n] = GEMM(x16, scales, W) with W's rows (output columns) sharded over the ranks of `group`.
 
     w_local: this rank's packed weight rows [c1 - c0][row_bytes] (shard_range(n, world, rank)); w2_local: its up
-    rows for mode 'swiglu'. Every rank passes the same x16/scales (replicated activations)."""
+    rows for mode 'swiglu'. Every rank passes the same x16/scales (replicated activations).
+
+    Lifetime of the result: the 'collective' exchange returns a new tensor. The 'p2p' exchange returns a view of one
+    of two peer buffers that the ranks write in turn: it stays valid until this rank's next call on this object
+    (after that call the peers may already be writing the buffer for the call after). Pass `out` to have the
+    gathered result copied into a tensor of your own instead (on the current stream, before the call returns)."""
 
     def __init__(self, fmt, mode, w_local, n, k, group=None, exchange="p2p", w2_local=None, gemm_fn=None):
         self.fmt, self.mode, self.n, self.k, self.group = fmt, mode, n, k, group
@@ -123,11 +128,13 @@ class ShardedGemm:
             self._flag = torch.zeros(1, device=device)
         dist.all_reduce(self._flag, group=self.group)
 
-    def __call__(self, x16, scales):
+    def __call__(self, x16, scales, out=None):
         rows = x16.shape[0]
-        if self.exchange == "p2p":
-            return self._p2p(x16, scales, rows)
-        return self._collective(x16, scales, rows)
+        y = self._p2p(x16, scales, rows) if self.exchange == "p2p" else self._collective(x16, scales, rows)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     def _local(self, x16, scales):
         fn = self.gemm_fn

@@ -3,7 +3,9 @@
 Checks, on every rank:
   * ShardedGemm ('p2p': all-gather fused into the GEMM epilogue over NVLink; 'collective': NCCL all-gather) equals
     the single-GPU GEMM of the full weight (the same tiles' arithmetic: relative L2 <= 1e-6), in store and swiglu
-    modes, on two calls in a row (the two peer buffers);
+    modes, on four calls in a row with different activations (the two peer buffers each used twice); every result is
+    kept -- as the copy `out=` makes for 'p2p', whose own result lives until the next call -- and all are compared
+    after the last call;
   * ExpertParallelMoE (experts sharded, tokens exchanged by NCCL all_to_all) against the oracle's float64 expert FFN
     within 1e-3, for a prefill-sized and a decode-sized token count.
 Exits non-zero on a mismatch."""
@@ -37,17 +39,23 @@ def main():
     x16, sc = ops.row_scale_f16(x)
     wd, w2d = torch.from_numpy(w).cuda(), torch.from_numpy(w2).cuda()
     c0, c1 = shard_range(n, world, rank)
+    xs = [ops.row_scale_f16((x.float() * (1.0 + 0.5 * c)).to(torch.bfloat16)) for c in range(4)]
     for mode in ("store", "swiglu"):
-        full = ops.gemm("iq4_nl", mode, x16, sc, wd, n, w2=w2d if mode == "swiglu" else None)
+        fulls = [ops.gemm("iq4_nl", mode, a16, asc, wd, n, w2=w2d if mode == "swiglu" else None) for a16, asc in xs]
         for exchange in ("p2p", "collective"):
             sg = ShardedGemm("iq4_nl", mode, wd[c0:c1].contiguous(), n, k, exchange=exchange,
                              w2_local=w2d[c0:c1].contiguous() if mode == "swiglu" else None)
-            for call in range(2):
-                y = sg(x16, sc)
+            kept = []
+            for a16, asc in xs:
+                if exchange == "p2p":
+                    kept.append(sg(a16, asc, out=torch.empty(rows, n, device="cuda")))
+                else:
+                    kept.append(sg(a16, asc))
+            torch.cuda.synchronize()
+            for call, (y, full) in enumerate(zip(kept, fulls)):
                 err = float((y - full).norm() / full.norm())
                 if not err <= 1e-6:
                     failures.append(f"sharded {mode} {exchange} call {call}: rel {err}")
-            torch.cuda.synchronize()
             dist.barrier()
             sg.close()
     # ---------------------------------------------------------------- expert-parallel MoE
