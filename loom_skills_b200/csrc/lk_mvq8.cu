@@ -28,6 +28,7 @@
 
 #include "lk_common.cuh"
 #include "lk_internal.h"
+#include "lk_q8.cuh"
 
 namespace lk {
 
@@ -47,13 +48,12 @@ constexpr int kPreWaitStages = 1;   // weight stages a CTA requests before gridd
 LK_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LK_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-LK_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {   // unsigned bytes of a . signed bytes of b + c
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-// exact int -> float for |v| < 2^22 without a conversion instruction
-LK_DEV float i2f_small(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
+using q8::dp4a_us;
+using q8::i2f_small;
+using q8::kXinBF16;
+using q8::kXinCodes;
+using q8::kXinF32;
+using q8::xq_smem_bytes;
 LK_DEV float u6_to_f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
 
 LK_DEV uint32_t cluster_ctarank() {
@@ -305,25 +305,15 @@ __global__ void __launch_bounds__(kQThreads)
 // super-block (with the super-block's 16-byte header) or two consecutive 18-byte Q4_0 blocks, 36 bytes at a 4-byte
 // aligned offset: nine word loads, the first block's nibbles realigned by funnel shifts.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kRStages = 3;
 constexpr int kRowWarps = 4;   // consumer warps = rows per stage
 // rings per CTA for K = 4096 rows and for longer rows (measured on the 8-layer decode mix: 2 rings of the short
 // form 4263 GB/s against 4207 with one; 3 or more rings, or 2 of the long form, were slower)
 constexpr int kRingsShort = 2, kRingsLong = 1;
-
-// the Q4_K (scale, min) pairs of groups (2pg, 2pg + 1) as "2^23 + value" floats: f[0..1] scales, f[2..3] minima.
-// pg is constant per thread: byte half h = pg & 1 of each scale word, the 4-bit-plus-2-bit form for pg >= 2.
-LK_DEV void q4k_pair_magic(uint4 hd, uint32_t hsel, uint32_t big_mask, float (&f)[4]) {
-  const uint32_t a = prmt(hd.y, 0u, hsel), b = prmt(hd.z, 0u, hsel), c = prmt(hd.w, 0u, hsel);
-  const uint32_t sc_lo = a & 0x3F3Fu, m_lo = b & 0x3F3Fu;
-  const uint32_t sc_hi = (c & 0x0F0Fu) | ((a >> 2) & 0x3030u);
-  const uint32_t m_hi = ((c >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u);
-  const uint32_t v = ((sc_hi & big_mask) | (sc_lo & ~big_mask)) | (((m_hi & big_mask) | (m_lo & ~big_mask)) << 16);
-  f[0] = __uint_as_float(prmt(v, 0x4B000000u, 0x7650u));
-  f[1] = __uint_as_float(prmt(v, 0x4B000000u, 0x7651u));
-  f[2] = __uint_as_float(prmt(v, 0x4B000000u, 0x7652u));
-  f[3] = __uint_as_float(prmt(v, 0x4B000000u, 0x7653u));
-}
+// stages per ring, weight stages a ring requests before griddepcontrol.wait, and the CTAs per SM the grid is sized
+// for (capped by the occupancy)
+constexpr int kStagesShort = 3, kStagesLong = 3;
+constexpr int kRowPreWait = 1;
+constexpr int kRowCtasPerSm = 2;
 
 constexpr int kMaxSegs = 4;
 struct RowArgs {
@@ -339,6 +329,7 @@ struct RowArgs {
   int64_t rb;          // bytes per packed row
   int sr;              // rows per stage
   int nstages;         // start[nseg]
+  int prewait;         // weight stages a ring requests before griddepcontrol.wait
 };
 // segment of a global stage, and the stage's first row inside it
 LK_DEV int seg_of(const RowArgs& p, int st, int& row0) {
@@ -351,75 +342,8 @@ LK_DEV int seg_of(const RowArgs& p, int st, int& row0) {
 }
 
 // bytes of one ring's shared memory: its stages, then full / empty barriers, per-row pair barriers and partial sums
-__host__ __device__ inline int ring_bytes(int stage_bytes) {
-  return (kRStages * stage_bytes + 2 * kRStages * 8 + kRStages * kRowWarps * 12 + 127) / 128 * 128;
-}
-
-// where the row kernel's activation codes come from: lk_quant_q8's buffer, or x of this type quantised in the kernel
-// (distinct from the LK_* dtype ids, among which LK_F32 is 0)
-enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
-
-// bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
-__host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
-
-// g_quant_q8 (gen_llm.py:683-750) of the row by the nt quantising threads: thread t takes the 16-value half-groups
-// t, t + nt, ... (nt even, so the two halves of a group sit in lanes 2j, 2j + 1 and meet by one shuffle):
-// d = amax / 127, q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + i] = q_i,
-// meta[g] = (f16-rounded d, sum of q). The codes and meta are k_quant_q8's bit for bit: x / d is taken as x * (1/d),
-// which is within 2 units in the last place of the correctly rounded quotient, and only where that product lies
-// within 2^-14 of a rounding boundary k + 1/2 (so the two could round apart) is the exact quotient x / d computed.
-template <int XIN>
-LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, float* meta) {
-  static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
-  for (int hg = t; hg < k / 16; hg += nt) {
-    float v[16];
-    if (XIN == kXinBF16) {
-      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + hg * 16);
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const uint4 u = __ldg(p + i);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
-          v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-        }
-      }
-    } else {
-      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + hg * 16);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 f = __ldg(p + i);
-        v[4 * i] = f.x;
-        v[4 * i + 1] = f.y;
-        v[4 * i + 2] = f.z;
-        v[4 * i + 3] = f.w;
-      }
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    const float d = amax / 127.0f;
-    int sum = 0;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (amax > 0.0f) {   // ordered compare: a NaN maximum gives codes 0, like the reference
-      const float r = __frcp_rn(d);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float y = __fmul_rn(v[i], r);
-        const float a = fabsf(y);
-        if (!(fabsf(a - floorf(a) - 0.5f) > 6.103515625e-05f)) y = v[i] / d;   // near k + 1/2 (or NaN): exact
-        const int q = int(roundf(y));
-        sum += q;
-        w[i >> 2] |= (uint32_t(q) & 0xffu) << (8 * (i & 3));
-      }
-    }
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-    reinterpret_cast<uint4*>(codes)[hg] = make_uint4(w[0], w[1], w[2], w[3]);
-    if ((hg & 1) == 0) reinterpret_cast<float2*>(meta)[hg >> 1] = make_float2(__half2float(__float2half_rn(d)),
-                                                                               float(sum));
-  }
+__host__ __device__ inline int ring_bytes(int stage_bytes, int nst) {
+  return (nst * stage_bytes + 2 * nst * 8 + nst * kRowWarps * 12 + 127) / 128 * 128;
 }
 
 // UPL units per lane over the whole row; HALVES warps per row (each takes UPL / HALVES of the units; the second
@@ -430,7 +354,7 @@ LK_DEV void quant_groups(const void* x, int k, int t, int nt, int8_t* codes, flo
 // of the CTA first quantise the row p.x into shared memory together (the g_quant_q8 launch folded into the
 // matvec's prologue; it overlaps the first weight stage's flight), then read their codes from there.
 // k_quant_q8 reduces a group across a warp; here a group is one thread's, so the CTA's groups run side by side.
-template <int FMT, int UPL, int HALVES, int RINGS, int XIN>
+template <int FMT, int UPL, int HALVES, int RINGS, int XIN, int NST>
 __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     k_mv_q8_rows(const RowArgs p) {
   constexpr int kU = UPL / HALVES;             // units this lane computes
@@ -438,14 +362,14 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
   extern __shared__ __align__(128) uint8_t smem_all[];
   const int stage_bytes = int((int64_t(p.sr) * p.rb + 127) / 128 * 128);
   const int ring = (threadIdx.x >> 5) / (1 + kCW);
-  uint8_t* smem = smem_all + ring * ring_bytes(stage_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRStages * stage_bytes);
-  uint64_t* empty = full + kRStages;
-  uint64_t* pair = empty + kRStages;                               // [kRStages][kRowWarps]
-  float* part = reinterpret_cast<float*>(pair + kRStages * kRowWarps);   // [kRStages][kRowWarps]
+  uint8_t* smem = smem_all + ring * ring_bytes(stage_bytes, NST);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * stage_bytes);
+  uint64_t* empty = full + NST;
+  uint64_t* pair = empty + NST;                                    // [NST][kRowWarps]
+  float* part = reinterpret_cast<float*>(pair + NST * kRowWarps);  // [NST][kRowWarps]
   const int warp = (threadIdx.x >> 5) % (1 + kCW), lane = threadIdx.x & 31;   // warp within the ring
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < kRStages; ++i) {
+    for (int i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kCW);
       for (int r = 0; r < kRowWarps; ++r) mbar_init(&pair[i * kRowWarps + r], 1);
@@ -460,9 +384,9 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     if (lane == 0) {
       griddep_launch();
       for (int i = 0; i < my_stages; ++i) {
-        const int s = i % kRStages;
-        if (i == kPreWaitStages) griddep_wait();   // the first stage only goes out before the previous grid ends
-        if (i >= kRStages && !mbar_wait(&empty[s], ((i / kRStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        const int s = i % NST;
+        if (i == p.prewait) griddep_wait();   // the first stages go out before the previous grid ends
+        if (i >= NST && !mbar_wait(&empty[s], ((i / NST) - 1) & 1)) atomicOr(&g_status, 1u);
         const int st = vb + i * vg;
         int r0;
         const int g = seg_of(p, st, r0);
@@ -480,53 +404,23 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     const uint8_t* xq = p.xq;
     if constexpr (XIN != kXinCodes) {
       // every consumer warp of the CTA takes groups cw, cw + ncw, ... of the row; then all of them read the codes
-      uint8_t* xs = smem_all + RINGS * ring_bytes(stage_bytes);
+      uint8_t* xs = smem_all + RINGS * ring_bytes(stage_bytes, NST);
       const int cw = ring * kCW + (warp - 1), ncw = RINGS * kCW;
-      quant_groups<XIN>(p.x, p.k, cw * 32 + lane, ncw * 32, reinterpret_cast<int8_t*>(xs),
-                        reinterpret_cast<float*>(xs + p.k));
+      static_assert(RINGS * kCW == 8, "256 quantising threads");
+      q8::quant_groups<XIN, UPL / 2>(p.x, cw * 32 + lane, reinterpret_cast<int8_t*>(xs), reinterpret_cast<float*>(xs + p.k));
       asm volatile("bar.sync 1, %0;" ::"r"(ncw * 32) : "memory");   // consumer warps only
       xq = xs;
     }
-    // 16-byte loads of the codes and meta: read-only global loads, or shared memory when quantised here
-    auto ld16 = [](const void* q) {
-      return XIN != kXinCodes ? *reinterpret_cast<const uint4*>(q) : __ldg(reinterpret_cast<const uint4*>(q));
-    };
     // lane l owns the (chunk, page) units l + 32u: chunk l/4 + 8u, page l % 4 -- the same page for every unit
     const int pg = lane & 3;
-    uint32_t xa[kU][8], xb[kU][8];
-    float dx0[kU], dx1[kU], b0[kU], b1[kU];   // Q4_0: b0, b1 unused
-    int s0x8[kU], s1x8[kU];                   // Q4_0: 8 x the groups' code sums (codes are q - 8)
-    const float* meta = reinterpret_cast<const float*>(xq + p.k);
+    q8::XUnit xu[kU];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int c = (lane >> 2) + 8 * (half * kU + u);
-      const uint8_t* xw = xq + c * 256 + 64 * pg;
-      const uint4 v0 = ld16(xw), v1 = ld16(xw + 16), v2 = ld16(xw + 32), v3 = ld16(xw + 48);
-      xa[u][0] = v0.x; xa[u][1] = v0.y; xa[u][2] = v0.z; xa[u][3] = v0.w;
-      xa[u][4] = v1.x; xa[u][5] = v1.y; xa[u][6] = v1.z; xa[u][7] = v1.w;
-      xb[u][0] = v2.x; xb[u][1] = v2.y; xb[u][2] = v2.z; xb[u][3] = v2.w;
-      xb[u][4] = v3.x; xb[u][5] = v3.y; xb[u][6] = v3.z; xb[u][7] = v3.w;
-      const uint4 mu = ld16(meta + c * 16 + 4 * pg);
-      const float4 mt = make_float4(__uint_as_float(mu.x), __uint_as_float(mu.y), __uint_as_float(mu.z),
-                                    __uint_as_float(mu.w));
-      dx0[u] = mt.x;
-      if (FMT == LK_Q4_0) {
-        dx1[u] = mt.z;
-        b0[u] = b1[u] = 0.f;
-        s0x8[u] = 8 * int(mt.y);
-        s1x8[u] = 8 * int(mt.w);
-      } else {
-        dx1[u] = mt.z * 0.0625f;               // high nibbles: the dot is 16 x
-        b0[u] = mt.x * mt.y;
-        b1[u] = mt.z * mt.w;
-        s0x8[u] = s1x8[u] = 0;
-      }
-    }
-    const uint32_t hsel = (pg & 1) ? 0x4432u : 0x4410u;
-    const uint32_t big = (pg >> 1) ? 0xFFFFFFFFu : 0u;
+    for (int u = 0; u < kU; ++u)
+      q8::load_xunit<FMT, XIN != kXinCodes>(xq, p.k, (lane >> 2) + 8 * (half * kU + u), pg, xu[u]);
+    const uint32_t hsel = q8::q4k_hsel(pg), big = q8::q4k_big(pg);
     for (int i = 0; i < my_stages; ++i) {
-      const int s = i % kRStages;
-      if (!mbar_wait(&full[s], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
+      const int s = i % NST;
+      if (!mbar_wait(&full[s], (i / NST) & 1)) atomicOr(&g_status, 1u);
       const int st = vb + i * vg;
       int r0;
       const int g = seg_of(p, st, r0);
@@ -535,48 +429,8 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
       if (row < p.n[g]) {
         const uint8_t* wr = smem + s * stage_bytes + int64_t(rslot) * p.rb;
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const uint8_t* sb = wr + ((lane >> 2) + 8 * (half * kU + u)) * kChunkBytes;
-          if (FMT == LK_Q4_0) {
-            // blocks 2 pg, 2 pg + 1 of the chunk: [d_a | 16 nibble bytes | d_b | 16 nibble bytes] from byte 36 pg
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(sb + 36 * pg);
-            uint32_t v[9];
-#pragma unroll
-            for (int j = 0; j < 9; ++j) v[j] = bw[j];
-            const float da = h2f(uint16_t(v[0] & 0xffffu)), db = h2f(uint16_t(v[4] >> 16));
-            int la = 0, ha = 0, lb = 0, hb = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {   // byte i of a block: element i (low nibble), element 16 + i (high)
-              const uint32_t qa = __funnelshift_r(v[j], v[j + 1], 16), qb = v[5 + j];
-              la = dp4a_us(qa & 0x0F0F0F0Fu, xa[u][j], la);
-              ha = dp4a_us(qa & 0xF0F0F0F0u, xa[u][4 + j], ha);
-              lb = dp4a_us(qb & 0x0F0F0F0Fu, xb[u][j], lb);
-              hb = dp4a_us(qb & 0xF0F0F0F0u, xb[u][4 + j], hb);
-            }
-            // sum((q - 8) x) = dot - 8 sum(x); the high nibbles' dot is 16 x, exactly
-            acc += da * dx0[u] * i2f_small(la + (ha >> 4) - s0x8[u]) + db * dx1[u] * i2f_small(lb + (hb >> 4) - s1x8[u]);
-            continue;
-          }
-          const uint4 hd = *reinterpret_cast<const uint4*>(sb);
-          const uint4 q0 = *reinterpret_cast<const uint4*>(sb + 16 + 32 * pg);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(sb + 32 + 32 * pg);
-          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-          float f[4];
-          q4k_pair_magic(hd, hsel, big, f);
-          const float d = h2f(uint16_t(hd.x & 0xffffu)), dmin = h2f(uint16_t(hd.x >> 16));
-          const float nd = -8388608.0f * d, ndm = -8388608.0f * dmin;
-          int i0 = 0, i1 = 0, i2 = 0, i3 = 0;
-#pragma unroll
-          for (int j = 0; j < 8; j += 2) {
-            i0 = dp4a_us(w[j] & 0x0F0F0F0Fu, xa[u][j], i0);
-            i1 = dp4a_us(w[j] & 0xF0F0F0F0u, xb[u][j], i1);
-            i2 = dp4a_us(w[j + 1] & 0x0F0F0F0Fu, xa[u][j + 1], i2);
-            i3 = dp4a_us(w[j + 1] & 0xF0F0F0F0u, xb[u][j + 1], i3);
-          }
-          // d*sc = fma(d, 2^23 + sc, -d*2^23), exact; the same for the minima
-          acc += fmaf(d, f[0], nd) * (dx0[u] * i2f_small(i0 + i2)) + fmaf(d, f[1], nd) * (dx1[u] * i2f_small(i1 + i3)) -
-                 fmaf(dmin, f[2], ndm) * b0[u] - fmaf(dmin, f[3], ndm) * b1[u];
-        }
+        for (int u = 0; u < kU; ++u)
+          acc += q8::unit_dot<FMT>(wr + ((lane >> 2) + 8 * (half * kU + u)) * kChunkBytes, xu[u], pg, hsel, big);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
@@ -589,7 +443,7 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
         }
       } else {
         if (HALVES == 2) {
-          if (!mbar_wait(&pair[s * kRowWarps + rslot], (i / kRStages) & 1)) atomicOr(&g_status, 1u);
+          if (!mbar_wait(&pair[s * kRowWarps + rslot], (i / NST) & 1)) atomicOr(&g_status, 1u);
           acc += part[s * kRowWarps + rslot];
         }
         if (lane == 0) {
@@ -601,12 +455,12 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
   }
 }
 
-template <int FMT, int UPL, int HALVES, int RINGS, int XIN>
+template <int FMT, int UPL, int HALVES, int RINGS, int XIN, int NST>
 int launch_rows(RowArgs a, cudaStream_t s) {
   const int stage_bytes = int((int64_t(a.sr) * a.rb + 127) / 128 * 128);
-  const int smem = RINGS * ring_bytes(stage_bytes) + (XIN != kXinCodes ? xq_smem_bytes(a.k) : 0);
+  const int smem = RINGS * ring_bytes(stage_bytes, NST) + (XIN != kXinCodes ? xq_smem_bytes(a.k) : 0);
   constexpr int threads = 32 * RINGS * (1 + kRowWarps * HALVES);
-  auto kern = k_mv_q8_rows<FMT, UPL, HALVES, RINGS, XIN>;
+  auto kern = k_mv_q8_rows<FMT, UPL, HALVES, RINGS, XIN, NST>;
   // the attribute and the occupancy query once per (device, shared-memory size): they cost host time on every call
   struct Entry {
     int dev, smem, per_sm, sms;
@@ -634,7 +488,8 @@ int launch_rows(RowArgs a, cudaStream_t s) {
   }
   cudaLaunchConfig_t cfg = {};
   // persistent: every resident CTA slot, once (no more CTAs than rings have stages)
-  cfg.gridDim = dim3(min((a.nstages + RINGS - 1) / RINGS, sms * per_sm), 1, 1);
+  cfg.gridDim = dim3(min((a.nstages + RINGS - 1) / RINGS, sms * min(per_sm, kRowCtasPerSm)), 1, 1);
+  a.prewait = kRowPreWait;
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -735,11 +590,14 @@ static int rows_dispatch(int fmt, int k, const RowArgs& ra, cudaStream_t s) {
   const bool q40 = fmt == LK_Q4_0;
   switch (k / 2048) {   // units (chunk, page) per lane
     case 2:
-      return q40 ? launch_rows<LK_Q4_0, 2, 1, kRingsShort, XIN>(ra, s) : launch_rows<LK_Q4_K, 2, 1, kRingsShort, XIN>(ra, s);
+      return q40 ? launch_rows<LK_Q4_0, 2, 1, kRingsShort, XIN, kStagesShort>(ra, s)
+                 : launch_rows<LK_Q4_K, 2, 1, kRingsShort, XIN, kStagesShort>(ra, s);
     case 4:
-      return q40 ? launch_rows<LK_Q4_0, 4, 2, kRingsLong, XIN>(ra, s) : launch_rows<LK_Q4_K, 4, 2, kRingsLong, XIN>(ra, s);
+      return q40 ? launch_rows<LK_Q4_0, 4, 2, kRingsLong, XIN, kStagesLong>(ra, s)
+                 : launch_rows<LK_Q4_K, 4, 2, kRingsLong, XIN, kStagesLong>(ra, s);
     case 6:
-      return q40 ? launch_rows<LK_Q4_0, 6, 2, kRingsLong, XIN>(ra, s) : launch_rows<LK_Q4_K, 6, 2, kRingsLong, XIN>(ra, s);
+      return q40 ? launch_rows<LK_Q4_0, 6, 2, kRingsLong, XIN, kStagesLong>(ra, s)
+                 : launch_rows<LK_Q4_K, 6, 2, kRingsLong, XIN, kStagesLong>(ra, s);
   }
   return LK_EUNSUPPORTED;
 }

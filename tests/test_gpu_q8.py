@@ -171,3 +171,27 @@ def test_fused_quantisation_rounding_boundaries(ops):
     for xt in (dev(x), dev(x).to(torch.bfloat16)):
         ref = ops.mv_q8("q4_k", w, ops.quant_q8(xt), n, k, 1)
         assert torch.equal(ops.mv_q8_fused("q4_k", w, xt, n, k), ref)
+
+
+@pytest.mark.parametrize("k", [4096, 12288])
+def test_fused_quantisation_special_values(ops, k):
+    # all-zero groups, a NaN or an infinity inside a group, subnormal and huge magnitudes: the in-kernel quantisation
+    # gives lk_quant_q8's codes (compared through the matvec; NaN outputs must sit in the same places)
+    n = 256
+    rng = np.random.default_rng(k)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    g = x.reshape(-1, 32)
+    g[0] = 0.0
+    g[1, 5] = np.nan
+    g[2, 7] = np.inf
+    g[3, 9] = -np.inf
+    g[4] = rng.standard_normal(32).astype(np.float32) * np.float32(1e-40)   # subnormal values, d underflows
+    g[5] = rng.standard_normal(32).astype(np.float32) * np.float32(3e38)
+    g[6, :] = np.float32(1e-45)
+    g[7, 3] = -np.float32(1e-45)
+    w = dev(weights("q4_k", n, k, 13))
+    for xt in (dev(x), dev(x).to(torch.bfloat16)):
+        ref = ops.mv_q8("q4_k", w, ops.quant_q8(xt), n, k, 1)
+        got = ops.mv_q8_fused("q4_k", w, xt, n, k)
+        torch.testing.assert_close(got, ref, rtol=0, atol=0, equal_nan=True)
+    assert ops.device_status() == 0
