@@ -4,14 +4,16 @@
 Default workload (N=1): BASELINE.json configs[1] -- Q4_K weights in the Qwen3-8B-like projection shapes
 (K=4096: N=4096 q/o, N=1024 k/v, N=24576 fused gate+up; down K=12288, N=4096), bf16 activations. One STEP is one decode
 token (M=1) through the six projections of a stack of `--layers` distinct weight copies (rotated so the weights,
-868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer the activations are
-quantised to int8 (g_quant_q8, inside each matvec's prologue) and the six matvecs contract them with the weight codes. `value` is the decode GEMV
-weight GB/s; the line also carries each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up, down and
+868 MB at 8 layers, exceed the 126 MB L2), on the reference's default decode numerics: per layer each of the two
+activation rows is quantised to int8 once (g_quant_q8, lk_quant_q8) and the six matvecs contract those codes with the
+weight codes. `value` is the decode GEMV weight GB/s; the line also carries the same step with the quantisation folded
+into every matvec's prologue (`decode_fused`), each decode launch form timed alone (`decode_gemv`: q|k|v, o, gate_up,
+down and
 configs[0]'s Q4_0 4096 x 4096 GEMV, each streamed from HBM), the bf16-activation decode, the prefill TFLOP/s at M=2048
 over the same shapes
 (step = row scale + the six tcgen05 GEMMs), a sweep over M in {1, 8, 64, 512, 2048}, the sharded IQ4_NL GEMMs and the
-MoE layers. Each step is one CUDA-graph replay of the public ops' launches (32 matvec launches per decode step, each
-quantising its own activation row -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
+MoE layers. Each step is one CUDA-graph replay of the public ops' launches (16 quantisations and 32 matvec launches
+per decode step -- q | k | v share one launch; the kernels chain with programmatic dependent launch).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layers L]
 
@@ -207,8 +209,9 @@ def make_weights(torch, layers, seed=0):
 def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
     """Each decode launch form alone: 32 back-to-back launches per graph replay, rotated over enough copies of its
     weights to exceed twice the L2, so every launch streams its weights from HBM. Per launch: device time, weight
-    GB/s and the fraction of the measured HBM copy. The four Q4_K forms of the step (int8 numerics, quantised in the
-    matvec), and configs[0]'s Q4_0 4096 x 4096 GEMV (the reference's CPU-runnable case) both at its stated precision
+    GB/s and the fraction of the measured HBM copy. The four Q4_K forms of the step on int8 codes (and, beside them,
+    the form that quantises its activation row in its own prologue), and configs[0]'s Q4_0 4096 x 4096 GEMV (the
+    reference's CPU-runnable case) both at its stated precision
     -- fp16 activations through lk_mv, the reference's default f32-dot numerics for Q4_0 (formats.py:24-27) -- and on
     int8 activations."""
     from loom_skills_b200 import ops
@@ -224,6 +227,7 @@ def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
              ("q4_0 4096x4096 int8 (configs[0])", q40, "q4_0", 4096, [4096], "int8")]
     chain = 32
     out = {}
+    xq = {k: ops.quant_q8(xs[k]) for k in xs}
     for label, base, fmt, k, ns, acts in forms:
         nbytes = base.numel()
         copies = max(2, -(-256_000_000 // nbytes))
@@ -232,25 +236,31 @@ def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
         r0 = np.cumsum([0] + ns)
         x = xs[k]
 
-        def body():
+        def body(fused=False):
             for i in range(chain):
                 w = ws[i % copies]
+                parts = [w[r0[j]:r0[j + 1]] for j in range(len(ns))]
                 if acts == "fp16":
                     ops.mv(fmt, w, x16, ns[0], k, y=ys[0])
-                elif len(ns) > 1:
-                    ops.mv_q8_fused_multi(fmt, [w[r0[j]:r0[j + 1]] for j in range(len(ns))], x, ns, k, ys=ys)
+                elif fused:
+                    ops.mv_q8_fused_multi(fmt, parts, x, ns, k, ys=ys)
                 else:
-                    ops.mv_q8_fused(fmt, w, x, ns[0], k, y=ys[0])
-        g = Timed(torch, body)
-        for _ in range(max(3, args.warmup)):
-            g.replay()
-        us = time_steps(g.replay, max(5, args.steps)) * 1e3 / chain
+                    ops.mv_q8_multi(fmt, parts, xq[k], ns, k, 1, ys=ys)
+
+        def timed(fused):
+            g = Timed(torch, lambda: body(fused))
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            return time_steps(g.replay, max(5, args.steps)) * 1e3 / chain
+        us = timed(False)
         gbs = nbytes / (us * 1e-6) / 1e9
         out[label] = {"format": fmt, "activations": acts, "us_per_launch": round(us, 2),
                       "weight_mb": round(nbytes / 1e6, 1), "weight_gbs": round(gbs, 1),
                       "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies,
-                      "kernel": "k_mv (lk_mv.cu)" if acts == "fp16" else "k_mv_q8_rows, in-kernel quantisation"}
-        del g, ws
+                      "kernel": "k_mv (lk_mv.cu)" if acts == "fp16" else "k_mv_q8_rows on lk_quant_q8 codes"}
+        if acts == "int8":
+            out[label]["fused_us_per_launch"] = round(timed(True), 2)   # the row quantised in the prologue
+        del ws
     return out
 
 
@@ -447,7 +457,8 @@ def run_ours(args):
           for li in range(args.layers)]
     wbytes_layer = sum(wstack[0][name].numel() for name, _, _ in SHAPES)
     act_bytes = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read + f32 y written, per layer
-    launches_per_step = args.layers * 4   # matvec launches: q|k|v, o, gate_up, down
+    mv_per_step = args.layers * 4          # matvec launches: q|k|v, o, gate_up, down
+    launches_per_step = mv_per_step + args.layers * 2   # + one quantisation per distinct activation row
     step_bytes = args.layers * wbytes_layer
 
     # int8 activations per layer: the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518)
@@ -473,14 +484,18 @@ def run_ours(args):
         for name, k, n in SHAPES[3:]:
             ops.mv_q8_fused("q4_k", w[name], xs[k], n, k, y=y[name])
 
-    def decode_body():   # one decode step: the six projections of every layer, int8 numerics, quantised in-kernel
-        for li in range(args.layers):
-            fused_layer(li)
-
-    def unfused_body():  # the same step with the quantisation as its own launches (16 + 32 launches)
+    def decode_body():   # one decode step: the six projections of every layer, int8 numerics (16 + 32 launches)
         for li in range(args.layers):
             quant_layer(li)
             mv_layer(li)
+
+    def mv_body():       # the step's 32 matvec launches alone (the codes of every layer already in place)
+        for li in range(args.layers):
+            mv_layer(li)
+
+    def fused_body():    # every matvec quantising its own activation row in its prologue (32 launches)
+        for li in range(args.layers):
+            fused_layer(li)
 
     def decode_bf16_body():   # the f32/bf16-activation path (ACT_Q8=0)
         for li in range(args.layers):
@@ -523,25 +538,31 @@ def run_ours(args):
     ms = time_steps(dec.replay, args.steps, clk)
     clocks = clk.stop()
     value = world * step_bytes / (ms * 1e-3) / 1e9
-    # the matvec kernel: the step is nothing but its 32 launches, so its average launch is the step over the launches
-    # (CUDA events around the timed replays of the one graph)
-    mv_ms = ms
-    act_bytes_l = sum(k * 2 + n * 4 for _, k, n in SHAPES)   # bf16 x read (quantised in-kernel) + f32 y written
-    alg_per_launch = (step_bytes + args.layers * act_bytes_l) / launches_per_step
-    kavg = mv_ms / launches_per_step
+    # the matvec kernel: a graph of the step's 32 matvec launches alone, between CUDA events, so its average launch is
+    # that graph's time over the launches
+    mg = Timed(torch, mv_body)
+    for _ in range(args.warmup):
+        mg.replay()
+    mv_ms = time_steps(mg.replay, args.steps)
+    code_bytes = {k: k + k // 32 * 8 for k in xs}             # int8 codes + (d, sum) per group, read by every CTA once
+    act_bytes_l = sum(code_bytes[k] + n * 4 for _, k, n in SHAPES[2:])   # q|k|v read one row: counted once
+    alg_per_launch = (step_bytes + args.layers * act_bytes_l) / mv_per_step
+    kavg = mv_ms / mv_per_step
     achieved = alg_per_launch / (kavg * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": int(TRAFFIC_RATIO_DECODE * alg_per_launch), "peak_source": pk_src,
-            "kernel": "k_mv_q8_rows<.., LK_BF16> (Q4_K x int8 quantised in the prologue, dp4a; lk_mvq8)",
+            "kernel": "k_mv_q8_rows (Q4_K x int8 codes, dp4a; lk_mvq8)",
             "avg_launch_us": round(kavg * 1e3, 2), "alg_bytes_per_launch": int(alg_per_launch),
             "mv_ms_per_step": round(mv_ms, 4)}
-    # the unfused form (lk_quant_q8 launches + the matvecs on their codes), for comparison
-    ug = Timed(torch, unfused_body)
+    # the same step with the quantisation folded into each matvec's prologue (lk_mv_q8_fused), for comparison: every
+    # launch quantises its own row, so the step quantises 32 rows where the graph above quantises 16
+    fg = Timed(torch, fused_body)
     for _ in range(args.warmup):
-        ug.replay()
-    un_ms = time_steps(ug.replay, max(3, args.steps // 4))
-    decode_unfused = {"value": round(world * step_bytes / (un_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                      "ms_per_step": round(un_ms, 4), "launches_per_step": launches_per_step + 2 * args.layers}
+        fg.replay()
+    fu_ms = time_steps(fg.replay, max(3, args.steps // 4))
+    decode_fused = {"value": round(world * step_bytes / (fu_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(fu_ms, 4), "launches_per_step": mv_per_step,
+                    "kernel": "k_mv_q8_rows<.., LK_BF16> (activation row quantised in the prologue)"}
     bf = Timed(torch, decode_bf16_body)
     for _ in range(args.warmup):
         bf.replay()
@@ -564,7 +585,8 @@ def run_ours(args):
         xbuf.copy_(hx, non_blocking=True)
         main = torch.cuda.current_stream()
         for li in range(args.layers):
-            fused_layer(li)
+            quant_layer(li)
+            mv_layer(li)
             done = torch.cuda.Event()
             done.record(main)
             side.wait_event(done)
@@ -656,7 +678,7 @@ def run_ours(args):
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
 
-    gpu_launches = args.steps * launches_per_step   # 32 matvec launches (quantisation inside them)
+    gpu_launches = args.steps * launches_per_step   # 16 quantisations + 32 matvec launches per step
     if rank == 0:
         cpu_v, cpu_desc = cpu_decode_gbs(budget_s=args.cpu_seconds)
         line = {
@@ -674,11 +696,11 @@ def run_ours(args):
             "roofline": roof, "cpu_baseline": {"value": round(cpu_v, 4), "unit": "GB/s", **cpu_desc}, "e2e": e2e,
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
             "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_gemv": gemv, "decode_bf16": decode_bf16,
-            "decode_unfused": decode_unfused,
+            "decode_fused": decode_fused,
             "sharded_iq4_nl": sharded, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
-        del dec, ug, bf, e2e_g, scale_g, gemm_g
+        del dec, mg, fg, bf, e2e_g, scale_g, gemm_g
         dist.barrier()
         dist.destroy_process_group()
 

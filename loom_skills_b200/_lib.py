@@ -19,7 +19,6 @@ MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU, "swiglu_sorted": SWIGL
 
 _P, _I, _L, _F, _U = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint
 
-
 # name -> (restype, argtypes); every symbol include/lk.h declares
 SIGNATURES = {
     "lk_strerror": (ctypes.c_char_p, [_I]),

@@ -49,4 +49,3 @@ def test_host_only_entry_points():
 ])
 def test_validation_rejects_before_any_launch(call):
     assert call(L.load()) < 0
-
