@@ -258,6 +258,22 @@ int lk_moe_expert_mv_mxfp4s_ex(int mode, int order, int n, int k, int assignment
  *   y[t] = sg[t] * y[t] + sum_k wts[t][k] * ys[...] -- y holds the shared experts' output on entry. */
 int lk_moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale,
                   lk_stream_t stream);
+/* lk_moe_ffn_decode_q8: the decode MoE layer on int8 activations -- MOE_Q8=1, the reference's default with ACT_Q8
+ * (gen_llm.py:5290-5302) -- in two launches: routing of every token from `logits` (lk_moe_route's rules: gating,
+ * norm, scale, router_bias), g_quant_q8 of x (gen_llm.py:683-750) and the int8 gate/up expert matvecs with
+ * act(g + b_gate, u + b_up) into act_buf [tokens * ku][f] (gen_moe.py:535-727); then g_quant_q8 of act_buf, the
+ * int8 down expert matvecs (+ b_down) and the weighted combine in assignment order (gen_moe.py:730-777, 1010-1045):
+ *   y[t] = (accumulate ? (sg ? sg[t] : 1) y[t] : 0) + sum_k wts[t,k] dsc[e] (Wd[e] act_k + bd[e]),  e = ids[t,k]
+ * the same fma chain as lk_moe_combine. Weights: w_gate / w_up [E][f] rows of k = h (w_up null: w_gate holds each
+ * expert's f gate rows then f up rows), w_down [E][h] rows of k = f; Q4_0 or Q4_K. ids / wts (both or neither):
+ * the routing, combine weights after down_scale. Limits: h a multiple of 2048 up to 4096, f % 256 == 0 and
+ * f <= 4096 (LK_EUNSUPPORTED / LK_ERANGE beyond), tokens <= 4, ku <= 8, n_experts <= 256, tokens * ku * f <= 65536;
+ * x, act_buf and the weights 16-byte aligned. */
+int lk_moe_ffn_decode_q8(int fmt, int tokens, int h, int f, int n_experts, int ku, int gating, int norm, float scale,
+                         const float* logits, const float* router_bias, const float* down_scale, const void* x,
+                         int x_dtype, const void* w_gate, const void* w_up, const void* w_down, const float* b_gate,
+                         const float* b_up, const float* b_down, int act, float alpha, float limit, float* act_buf,
+                         int32_t* ids, float* wts, const float* sg, int accumulate, float* y, lk_stream_t stream);
 int lk_moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, lk_stream_t stream);
 int lk_moe_combine_gated(int tokens, int h, int ku, const float* ys, const float* wts, const float* sg, float* y,
                          lk_stream_t stream);

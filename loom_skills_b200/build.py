@@ -7,7 +7,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "liblk.so")
 SOURCES = ["lk_api.cu", "lk_dequant.cu", "lk_mv.cu", "lk_mvq8.cu","lk_gemm.cu", "lk_mxfp4.cu", "lk_moe.cu", "lk_peer.cu",
-           "lk_noalloc.cu", "lk_mvmx.cu", "lk_mvg.cu"]
+           "lk_noalloc.cu", "lk_mvmx.cu", "lk_mvg.cu", "lk_moeq8.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler", "-fPIC",
          "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]

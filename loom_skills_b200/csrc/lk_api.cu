@@ -44,7 +44,8 @@ int64_t lk_row_bytes(int fmt, int64_t k) {
 
 // Reads (and optionally clears) the device-side status word: bit 0 = a kernel's bounded wait gave up. Synchronous.
 unsigned int lk_device_status(int clear) {
-  return status_mv(clear != 0) | status_gemm(clear != 0) | status_mx(clear != 0) | status_q8(clear != 0);
+  return status_mv(clear != 0) | status_gemm(clear != 0) | status_mx(clear != 0) | status_q8(clear != 0) |
+         status_moeq8(clear != 0);
 }
 
 int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_stream_t stream) {
@@ -436,6 +437,29 @@ int lk_moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_d
   if (!x || !w || !sg) return LK_EINVAL;
   if (!aligned(x, 16) || !aligned(w, 8)) return LK_EALIGN;
   return moe_shared_gate(tokens, h, x, w, w_dtype, sg, (cudaStream_t)stream);
+}
+
+int lk_moe_ffn_decode_q8(int fmt, int tokens, int h, int f, int n_experts, int ku, int gating, int norm, float scale,
+                         const float* logits, const float* router_bias, const float* down_scale, const void* x,
+                         int x_dtype, const void* w_gate, const void* w_up, const void* w_down, const float* b_gate,
+                         const float* b_up, const float* b_down, int act, float alpha, float limit, float* act_buf,
+                         int32_t* ids, float* wts, const float* sg, int accumulate, float* y, lk_stream_t stream) {
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return (q4_family(fmt) || fmt_qk(fmt) > 0) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (tokens < 0 || h <= 0 || f <= 0 || n_experts <= 0 || ku <= 0 || ku > n_experts) return LK_EINVAL;
+  if (gating < 1 || gating > 3 || !act_ok(act) || (gating == 1 && router_bias)) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (h % 2048 || f % 256) return LK_EUNSUPPORTED;
+  if (tokens > 4 || ku > 8 || n_experts > 256 || h > 4096 || f > 4096 || tokens * ku * f > 65536) return LK_ERANGE;
+  if (tokens == 0) return LK_OK;
+  if (!logits || !x || !w_gate || !w_down || !act_buf || !y) return LK_EINVAL;
+  if ((b_gate == nullptr) != (b_up == nullptr) || (ids == nullptr) != (wts == nullptr)) return LK_EINVAL;
+  if (!aligned(x, 16) || !aligned(act_buf, 16) || !aligned(w_gate, 16) || !aligned(w_down, 16) ||
+      (w_up && !aligned(w_up, 16)))
+    return LK_EALIGN;
+  MoeFfnQ8 p{tokens, h, f, n_experts, ku, gating, norm ? 1 : 0, scale, logits, router_bias, down_scale, x, x_dtype,
+             w_gate, w_up, w_down, b_gate, b_up, b_down, act, alpha, limit, act_buf, ids, wts, sg,
+             accumulate ? 1 : 0, y};
+  return moe_ffn_decode_q8(fmt, p, (cudaStream_t)stream);
 }
 
 }  // extern "C"

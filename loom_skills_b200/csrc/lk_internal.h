@@ -97,10 +97,37 @@ int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* 
 int mv_q8_fused(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,
                 const void* x, int x_dtype, cudaStream_t s);
 
+// the decode MoE layer on int8 activations in two launches (lk_moeq8.cu); arguments of lk_moe_ffn_decode_q8
+struct MoeFfnQ8 {
+  int tokens, h, f, n_experts, ku, gating, norm;
+  float scale;
+  const float* logits;
+  const float* router_bias;
+  const float* down_scale;
+  const void* x;
+  int x_dtype;
+  const void* w_gate;
+  const void* w_up;
+  const void* w_down;
+  const float* b_gate;
+  const float* b_up;
+  const float* b_down;
+  int act;
+  float alpha, limit;
+  float* act_buf;
+  int32_t* ids;
+  float* wts;
+  const float* sg;
+  int accumulate;
+  float* y;
+};
+int moe_ffn_decode_q8(int fmt, const MoeFfnQ8& p, cudaStream_t s);
+
 // device status words of the kernel files (bit 0: a bounded wait gave up)
 unsigned int status_q8(bool clear);
 unsigned int status_mv(bool clear);
 unsigned int status_gemm(bool clear);
 unsigned int status_mx(bool clear);
+unsigned int status_moeq8(bool clear);
 
 }  // namespace lk

@@ -9,6 +9,7 @@
 // g_moe_shared_gate              gen_moe.py:780-823             sg[t] = sigmoid(x[t] . w)
 #include "lk_common.cuh"
 #include "lk_internal.h"
+#include "lk_route.cuh"
 
 namespace lk {
 
@@ -120,108 +121,14 @@ __global__ void __launch_bounds__(256) k_route(int h, int E, int ku, int gating,
   if (my_k >= 0) wts[int64_t(t) * ku + my_k] = wv * scale;
 }
 
-// router on given logits: one warp per token (8 per CTA), lane l holds experts l, l + 32, ... (E <= 256): the same
-// gating, top-k (ties to the lowest index) and weight rules as k_route, every reduction a warp shuffle
+// router on given logits: one warp per token (8 per CTA); the per-token rules are route_token (lk_route.cuh)
 __global__ void __launch_bounds__(256) k_route_w(int tokens, int E, int ku, int gating, int norm, float scale,
                                                  const float* __restrict__ logits, const float* __restrict__ bias,
                                                  int32_t* __restrict__ ids, float* __restrict__ wts) {
   const int lane = threadIdx.x & 31;
   const int64_t t = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (t >= tokens) return;
-  auto wmax = [](float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-  };
-  auto wsum = [](float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-  };
-  float lg[8], prob[8], sc[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int e = lane + 32 * j;
-    lg[j] = e < E ? __ldg(logits + t * E + e) : -INFINITY;
-  }
-  if (gating == 1) {
-    float m = lg[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) m = fmaxf(m, lg[j]);
-    m = wmax(m);
-    float den = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      prob[j] = lane + 32 * j < E ? expf(lg[j] - m) : 0.f;
-      den += prob[j];
-    }
-    den = wsum(den);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      prob[j] = prob[j] / den;
-      sc[j] = lg[j];   // softmax is monotonic in the logit: rank on the exact input
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int e = lane + 32 * j;
-      const bool in = e < E;
-      const float b = (bias && in) ? __ldg(bias + e) : 0.f;
-      if (gating == 2) {
-        prob[j] = in ? 1.0f / (1.0f + expf(-lg[j])) : 0.f;
-        sc[j] = in ? prob[j] + b : -INFINITY;
-      } else {
-        prob[j] = in ? lg[j] + b : -INFINITY;
-        sc[j] = prob[j];
-      }
-    }
-  }
-  int my[8];   // round each held expert was picked in, or -1
-#pragma unroll
-  for (int j = 0; j < 8; ++j) my[j] = -1;
-  float sel_sum = 0.f;
-  for (int r = 0; r < ku; ++r) {
-    float best = sc[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) best = fmaxf(best, sc[j]);
-    best = wmax(best);
-    int cand = 1 << 30;
-#pragma unroll
-    for (int j = 7; j >= 0; --j)
-      if (lane + 32 * j < E && sc[j] == best) cand = lane + 32 * j;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
-    float pw = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (lane + 32 * j == cand) {
-        my[j] = r;
-        sc[j] = -INFINITY;
-        pw = prob[j];
-      }
-    if (lane == (cand & 31)) ids[t * ku + r] = cand;
-    sel_sum += wsum(pw);
-  }
-  float m3 = 0.f, den3 = 1.f;
-  if (gating == 3) {   // softmax over the picked
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (my[j] >= 0) m = fmaxf(m, prob[j]);
-    m3 = wmax(m);
-    float d = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (my[j] >= 0) d += expf(prob[j] - m3);
-    den3 = wsum(d);
-  }
-  const float den = norm ? fmaxf(sel_sum, 6.103515625e-05f) : 1.0f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (my[j] >= 0) {
-      const float wv = gating == 3 ? expf(prob[j] - m3) / den3 : prob[j] / den;
-      wts[t * ku + my[j]] = wv * scale;
-    }
+  route_token(lane, E, ku, gating, norm, scale, logits + t * E, bias, ids + t * ku, wts + t * ku);
 }
 
 int moe_route(int tokens, int h, int E, int ku, int gating, int norm, float scale, const float* x,

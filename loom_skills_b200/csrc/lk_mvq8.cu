@@ -416,7 +416,8 @@ __global__ void __launch_bounds__(32 * RINGS * (1 + kRowWarps * HALVES))
     q8::XUnit xu[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u)
-      q8::load_xunit<FMT, XIN != kXinCodes>(xq, p.k, (lane >> 2) + 8 * (half * kU + u), pg, xu[u]);
+      q8::load_xunit<FMT, XIN != kXinCodes>(xq, reinterpret_cast<const float*>(xq + p.k), (lane >> 2) + 8 * (half * kU + u),
+                                            pg, xu[u]);
     const uint32_t hsel = q8::q4k_hsel(pg), big = q8::q4k_big(pg);
     for (int i = 0; i < my_stages; ++i) {
       const int s = i % NST;

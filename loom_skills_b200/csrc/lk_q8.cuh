@@ -1,5 +1,6 @@
-// Device pieces of the int8-activation decode matvecs (lk_mvq8.cu):
-//   quant_groups   g_quant_q8 (gen_llm.py:683-750) of one activation row into shared memory
+// Device pieces of the int8-activation decode matvecs (lk_mvq8.cu: dense; lk_moeq8.cu: the MoE expert matvecs):
+//   quant_half / quant_groups / quant_flat
+//                  g_quant_q8 (gen_llm.py:683-750) of activation rows into shared memory
 //   XUnit / load_xunit / unit_dot
 //                  one lane's (chunk, page) unit of 64 values: its activation codes and group meta held in registers,
 //                  and its dot with one packed weight row's unit (@g_<fmt>_icodes, gen_llm.py:521-680)
@@ -40,77 +41,123 @@ enum { kXinCodes = 0, kXinF32 = 1, kXinBF16 = 2 };
 // bytes of the shared copy of the quantised activation row (codes, then the group meta), 128-byte rounded
 __host__ __device__ inline int xq_smem_bytes(int k) { return (k + k / 4 + 127) / 128 * 128; }
 
-// g_quant_q8 of the row by 256 quantising threads: thread t takes the 16-value half-groups t + 256 j, j < NIT
-// (k = 4096 NIT; the two halves of a group sit in lanes 2i, 2i + 1 and meet by one shuffle): d = amax / 127,
-// q = round(x / d) (halves away from zero; 0 for an all-zero group), codes[g*32 + i] = q_i,
-// meta[g] = (f16-rounded d, sum of q). The codes and meta are k_quant_q8's bit for bit:
+// g_quant_q8 of one 16-value half-group (the other half of its 32-value group in lane t ^ 1, which must run the same
+// call): d = amax / 127, q = round(x / d) (halves away from zero; 0 for an all-zero group), the 16 codes stored at
+// codes[hg * 16 ..], and for even hg the group meta (f16-rounded d, sum of q) at meta[hg / 2]. The codes and meta are
+// k_quant_q8's bit for bit:
 //  - y = x * (1/d) (both correctly rounded) is within 2 units in the last place of the quotient x / d, |y| <= 127;
 //  - adding 1.5 * 2^23 rounds y to the nearest integer m (ties to even) in the low mantissa bits, whose low byte is
 //    then the two's-complement code; f = y - m is exact (Sterbenz), |f| <= 1/2;
 //  - where |f| lies within 2^-14 of 1/2 (y near a rounding boundary, where y and x / d could round apart or the tie
 //    rules differ) or is NaN, the half-group is recomputed with the exact quotient and roundf.
-// All of a thread's loads are issued before any arithmetic (x comes from an earlier kernel: read-only loads). Codes
-// are packed by byte permutes; their sum is a dp4a.
+// Codes are packed by byte permutes; their sum is a dp4a. `store` false: the shuffles only (a lane past the end).
+LK_DEV void quant_half(const float (&v)[16], int hg, bool store, int8_t* codes, float* meta) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+  const float d = amax / 127.0f;
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  if (amax > 0.0f) {   // ordered compare: a NaN maximum gives codes 0, like the reference
+    const float r = __frcp_rn(d);
+    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+    bool exact = false;
+    uint32_t tb[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float y = __fmul_rn(v[i], r);
+      const float tm = __fadd_rn(y, kMagic);
+      const float f = __fsub_rn(y, __fsub_rn(tm, kMagic));
+      exact |= !(fabsf(f) < 0.49993896484375f);   // within 2^-14 of a half, or NaN
+      tb[i] = __float_as_uint(tm);
+    }
+    if (exact) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tb[i] = uint32_t(int(roundf(v[i] / d)));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = __byte_perm(__byte_perm(tb[4 * i], tb[4 * i + 1], 0x0040), __byte_perm(tb[4 * i + 2], tb[4 * i + 3], 0x0040),
+                         0x5410);
+  }
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sum = __dp4a(int(w[i]), 0x01010101, sum);
+  sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+  if (!store) return;
+  reinterpret_cast<uint4*>(codes)[hg] = make_uint4(w[0], w[1], w[2], w[3]);
+  if ((hg & 1) == 0) reinterpret_cast<float2*>(meta)[hg >> 1] = make_float2(__half2float(__float2half_rn(d)), float(sum));
+}
+
+// the 16 values of half-group hg of x (f32 or bf16), read-only loads
+template <int XIN>
+LK_DEV void load_half(const void* x, int hg, uint32_t (&raw)[XIN == kXinBF16 ? 8 : 16]) {
+  constexpr int kWords = XIN == kXinBF16 ? 8 : 16;
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + int64_t(hg) * 4 * kWords);
+#pragma unroll
+  for (int i = 0; i < kWords / 4; ++i) {
+    const uint4 u = __ldg(p + i);
+    raw[4 * i] = u.x;
+    raw[4 * i + 1] = u.y;
+    raw[4 * i + 2] = u.z;
+    raw[4 * i + 3] = u.w;
+  }
+}
+template <int XIN>
+LK_DEV void unpack_half(const uint32_t (&raw)[XIN == kXinBF16 ? 8 : 16], float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    v[i] = XIN == kXinBF16 ? __uint_as_float((i & 1) ? (raw[i >> 1] & 0xffff0000u) : (raw[i >> 1] << 16))
+                           : __uint_as_float(raw[i]);
+}
+
+// g_quant_q8 of a row of k = 4096 NIT values by 256 threads: thread t takes the half-groups t + 256 j, j < NIT, with
+// all of its loads issued before any arithmetic (x comes from an earlier kernel: read-only loads). Codes [k] and meta
+// [k/32][2] as k_quant_q8 writes them.
 template <int XIN, int NIT>
 LK_DEV void quant_groups(const void* x, int t, int8_t* codes, float* meta) {
   static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
-  constexpr int kWords = XIN == kXinBF16 ? 8 : 16;   // 32-bit words of a half-group
-  uint32_t raw[NIT][kWords];
+  uint32_t raw[NIT][XIN == kXinBF16 ? 8 : 16];
+#pragma unroll
+  for (int j = 0; j < NIT; ++j) load_half<XIN>(x, t + 256 * j, raw[j]);
 #pragma unroll
   for (int j = 0; j < NIT; ++j) {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + int64_t(t + 256 * j) * 4 * kWords);
-#pragma unroll
-    for (int i = 0; i < kWords / 4; ++i) {
-      const uint4 u = __ldg(p + i);
-      raw[j][4 * i] = u.x;
-      raw[j][4 * i + 1] = u.y;
-      raw[j][4 * i + 2] = u.z;
-      raw[j][4 * i + 3] = u.w;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < NIT; ++j) {
-    const int hg = t + 256 * j;
     float v[16];
+    unpack_half<XIN>(raw[j], v);
+    quant_half(v, t + 256 * j, true, codes, meta);
+  }
+}
+
+// g_quant_q8 of `rows` consecutive rows of k values (k % 32 == 0) as one flat vector, by 256 threads: the same codes
+// and meta layout as k_quant_q8 on [rows][k] (codes [rows][k], then meta [rows][k/32][2]). Rounds of 256 half-groups
+// go in batches (4 for bf16, 2 for f32) whose loads are all issued before their arithmetic; every thread runs the same
+// rounds (lanes past the end take part in the pair shuffles only).
+template <int XIN>
+LK_DEV void quant_flat(const void* x, int nvals, int t, int8_t* codes, float* meta) {
+  static_assert(XIN == kXinF32 || XIN == kXinBF16, "an activation type to quantise");
+  constexpr int kW = XIN == kXinBF16 ? 8 : 16;
+  constexpr int kB = XIN == kXinBF16 ? 4 : 2;
+  const int nhg = nvals / 16;
+  for (int base = 0; base < nhg; base += kB * 256) {
+    uint32_t raw[kB][kW];
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      v[i] = XIN == kXinBF16 ? __uint_as_float((i & 1) ? (raw[j][i >> 1] & 0xffff0000u) : (raw[j][i >> 1] << 16))
-                             : __uint_as_float(raw[j][i]);
-    float amax = 0.f;
+    for (int b = 0; b < kB; ++b) {
+      const int hg = base + b * 256 + t;
+      if (hg < nhg) {
+        load_half<XIN>(x, hg, raw[b]);
+      } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    const float d = amax / 127.0f;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (amax > 0.0f) {   // ordered compare: a NaN maximum gives codes 0, like the reference
-      const float r = __frcp_rn(d);
-      constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-      bool exact = false;
-      uint32_t tb[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float y = __fmul_rn(v[i], r);
-        const float tm = __fadd_rn(y, kMagic);
-        const float f = __fsub_rn(y, __fsub_rn(tm, kMagic));
-        exact |= !(fabsf(f) < 0.49993896484375f);   // within 2^-14 of a half, or NaN
-        tb[i] = __float_as_uint(tm);
+        for (int i = 0; i < kW; ++i) raw[b][i] = 0u;
       }
-      if (exact) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) tb[i] = uint32_t(int(roundf(v[i] / d)));
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        w[i] = __byte_perm(__byte_perm(tb[4 * i], tb[4 * i + 1], 0x0040), __byte_perm(tb[4 * i + 2], tb[4 * i + 3], 0x0040),
-                           0x5410);
     }
-    int sum = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sum = __dp4a(int(w[i]), 0x01010101, sum);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-    reinterpret_cast<uint4*>(codes)[hg] = make_uint4(w[0], w[1], w[2], w[3]);
-    if ((hg & 1) == 0) reinterpret_cast<float2*>(meta)[hg >> 1] = make_float2(__half2float(__float2half_rn(d)),
-                                                                               float(sum));
+    for (int b = 0; b < kB; ++b) {
+      if (base + b * 256 >= nhg) break;   // the same for every thread
+      const int hg = base + b * 256 + t;
+      float v[16];
+      unpack_half<XIN>(raw[b], v);
+      quant_half(v, hg, hg < nhg, codes, meta);
+    }
   }
 }
 
@@ -122,14 +169,14 @@ struct XUnit {
   int s0x8, s1x8;           // Q4_0: 8 x the groups' code sums (codes are q - 8)
 };
 
-// SMEM: the codes are in shared memory (quantised by this CTA); else read-only global loads of lk_quant_q8's buffer
+// codes / meta: one activation row's codes [k] and group meta [k/32][2]. SMEM: in shared memory (quantised by this
+// CTA); else read-only global loads of lk_quant_q8's buffer
 template <int FMT, bool SMEM>
-LK_DEV void load_xunit(const uint8_t* xq, int k, int c, int pg, XUnit& u) {
+LK_DEV void load_xunit(const uint8_t* codes, const float* meta, int c, int pg, XUnit& u) {
   auto ld16 = [](const void* q) {
     return SMEM ? *reinterpret_cast<const uint4*>(q) : __ldg(reinterpret_cast<const uint4*>(q));
   };
-  const float* meta = reinterpret_cast<const float*>(xq + k);
-  const uint8_t* xw = xq + c * 256 + 64 * pg;
+  const uint8_t* xw = codes + c * 256 + 64 * pg;
   const uint4 v0 = ld16(xw), v1 = ld16(xw + 16), v2 = ld16(xw + 32), v3 = ld16(xw + 48);
   u.xa[0] = v0.x; u.xa[1] = v0.y; u.xa[2] = v0.z; u.xa[3] = v0.w;
   u.xa[4] = v1.x; u.xa[5] = v1.y; u.xa[6] = v1.z; u.xa[7] = v1.w;

@@ -480,6 +480,38 @@ def mv_q8_fused(fmt, w, x, n, k, y=None, accumulate=False):
     return y
 
 
+def moe_ffn_decode_q8(fmt, x, logits, w_gate, w_down, h, f, n_experts, ku, w_up=None, gating=1, norm=True,
+                      scale=1.0, router_bias=None, down_scale=None, act="silu", alpha=1.702, limit=7.0, b_gate=None,
+                      b_up=None, b_down=None, y=None, accumulate=False, sg=None, act_buf=None, routing=False):
+    """lk_moe_ffn_decode_q8: the decode MoE layer on int8 activations (MOE_Q8=1, the reference's default decode
+    numerics) in two launches -- routing from the logits, quantisation of x and the gate/up expert matvecs; then
+    quantisation of act, the down expert matvecs and the weighted combine. w_up None: w_gate holds each expert's
+    f gate rows then f up rows. Returns y [tokens][h] (and (ids, wts) with routing=True)."""
+    _cuda(x, logits, w_gate, w_down)
+    x = x.contiguous()
+    tokens = x.shape[0]
+    dev = x.device
+    if y is None:
+        if accumulate:
+            raise ValueError("accumulate needs y")
+        y = torch.empty(tokens, h, dtype=torch.float32, device=dev)
+    if act_buf is None:
+        act_buf = torch.empty(tokens * ku, f, dtype=torch.float32, device=dev)
+    ids = wts = None
+    if routing:
+        ids = torch.empty(tokens, ku, dtype=torch.int32, device=dev)
+        wts = torch.empty(tokens, ku, dtype=torch.float32, device=dev)
+    lg = _f32c(logits)
+    rb, ds = _f32c(router_bias), _f32c(down_scale)
+    bg, bu, bd, sgc = _f32c(b_gate), _f32c(b_up), _f32c(b_down), _f32c(sg)
+    L.check(L.load().lk_moe_ffn_decode_q8(
+        _fmt(fmt), tokens, h, f, n_experts, ku, gating, 1 if norm else 0, float(scale), _ptr(lg), _ptr(rb), _ptr(ds),
+        _ptr(x), _DT[x.dtype], _ptr(w_gate), _ptr(w_up), _ptr(w_down), _ptr(bg), _ptr(bu), _ptr(bd), _act(act),
+        float(alpha), float(limit), _ptr(act_buf), _ptr(ids), _ptr(wts), _ptr(sgc), 1 if accumulate else 0, _ptr(y),
+        _stream()), "lk_moe_ffn_decode_q8")
+    return (y, ids, wts) if routing else y
+
+
 def mv_q8_fused_multi(fmt, ws, x, ns, k, ys=None, accumulate=False):
     """mv_q8_fused over up to 4 weights sharing x (q | k | v) in one launch. Returns the ys."""
     import ctypes

@@ -690,6 +690,37 @@ def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts, act=ACT_SILU, alp
     return y
 
 
+def moe_ffn_q8_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, act=ACT_SILU, alpha=1.702, limit=7.0, b_gate=None,
+                   b_up=None, b_down=None, dsc=None, y0=None, sg=None):
+    """The decode expert FFN on int8 activations, MOE_Q8=1 (gen_llm.py:5290-5302): x is quantised by g_quant_q8
+    (quant_q8 above, gen_llm.py:683-750), the gate/up products of those codes with the dequantised weights are taken
+    in float64, act = act(g + bg, u + bu) is rounded to f32 and quantised again per assignment row (the g_quant_q8
+    launch on the gate/up output), the down products likewise (+ bd), then the weighted combine
+    y[t] = sg[t] y0[t] + sum_k wts[t,k] dsc[e] ys. w_gu[e] = the expert's gate rows then up rows (packed blocks)."""
+    xq = dequant_q8(*quant_q8(np.asarray(x, np.float32))).astype(np.float64)
+    t, ku = ids.shape
+    y = np.zeros((t, h), np.float64)
+    if y0 is not None:
+        y += np.asarray(y0, np.float64) * (1.0 if sg is None else np.asarray(sg, np.float64)[:, None])
+    w_eff = np.asarray(wts, np.float64) if dsc is None else wscale_ref(ids, wts, dsc).astype(np.float64)
+    for e in np.unique(ids):
+        gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
+        dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
+        for i, j in zip(*np.nonzero(ids == e)):
+            pair = gu @ xq[i]
+            g, u = pair[:f], pair[f:]
+            if b_gate is not None:
+                g = g + np.asarray(b_gate, np.float64)[e]
+                u = u + np.asarray(b_up, np.float64)[e]
+            a32 = act_ref(g, u, act, alpha, limit).astype(np.float32)[None, :]
+            aq = dequant_q8(*quant_q8(a32)).astype(np.float64)[0]
+            ys = dn @ aq
+            if b_down is not None:
+                ys = ys + np.asarray(b_down, np.float64)[e]
+            y[i] += w_eff[i, j] * ys
+    return y
+
+
 def moe_ffn_mxfp4_decode_ref(x, ids, wts, nib_gu, sc_gu, nib_dn, sc_dn, h, f, order="pairs"):
     """The routed expert FFN with MXFP4 experts at decode sizes (gen_llm.py:5324-5386 wiring below the GEMM threshold
     of gen_llm.py:6107, the expert matvecs of gen_moe.py:535-727): per assignment act = silu(Wg x) * (Wu x) and
