@@ -710,14 +710,49 @@ def run_profile_case(args):
     `--steps` profiled ones. Cases: mv_gate_up (Q4_K q8 matvec, K=4096 N=24576), mv_down (K=12288 N=4096),
     mv8_gate_up (the gate_up matvec on 8 tokens), gemm_gate_up (Q4_K GEMM, M=2048 K=4096 N=24576), gemm64_down
     (Q4_K GEMM, M=64 K=12288 N=4096), mx_gate_up (MXFP4 x e4m3 swiglu, M=8192 K=2880 N=2880), mxmv_gate_up (the
-    MXFP4S expert matvecs of one gpt-oss token: 4 assignments of 32 experts, h = f = 2880, bf16 x)."""
+    MXFP4S expert matvecs of one gpt-oss token: 4 assignments of 32 experts, h = f = 2880, bf16 x), mvf_gate_up (the
+    gate_up matvec quantising its bf16 row in the prologue), mvg_q6k (the generic-format matvec, Q6_K K=4096
+    N=4096, f32 x), gemm_q6k (the window-producer GEMM, Q6_K M=2048 K=4096 N=4096), moeq8 (the int8 decode MoE layer
+    of configs[2] at one token: E=128 top-8, H=2048, F=768, Q4_0)."""
     import torch
 
     from loom_skills_b200 import ops
     dev = torch.device("cuda", 0)
     rng = np.random.default_rng(0)
     case = args.profile_case
-    if case.startswith("mv"):
+    if case == "mvf_gate_up":
+        k, n = 4096, 24576
+        w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+        x = torch.randn(1, k, device=dev).to(torch.bfloat16)
+        y = torch.empty(1, n, device=dev)
+        fn = lambda: ops.mv_q8_fused("q4_k", w, x, n, k, y=y)   # noqa: E731
+    elif case in ("mvg_q6k", "gemm_q6k"):
+        k, n = 4096, 4096
+        # Q6_K blocks (210 bytes per 256 values): uniform 6-bit codes and int8 sub-block scales, f16 d at byte 208
+        b = rng.integers(0, 256, (n * k // 256, 210), dtype=np.uint8)
+        b[:, 208:210] = np.frombuffer(np.float16(2e-4).tobytes(), np.uint8)
+        w = torch.from_numpy(b.reshape(n, -1)).to(dev)
+        if case == "mvg_q6k":
+            x = torch.randn(1, k, device=dev)
+            y = torch.empty(1, n, device=dev)
+            fn = lambda: ops.mv("q6_k", w, x, n, k, y=y)   # noqa: E731
+        else:
+            m = 2048
+            x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
+            y = torch.empty(m, n, device=dev)
+            fn = lambda: ops.gemm("q6_k", "store", x16, sc, w, n, y=y)   # noqa: E731
+    elif case == "moeq8":
+        E, ku, h, f = 128, 8, 2048, 768
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        wgu = synth_blocks(torch, dev, E * 2 * f, h, "q4_0", gen)
+        wdn = synth_blocks(torch, dev, E * h, f, "q4_0", gen)
+        x = torch.randn(1, h, device=dev, generator=gen).to(torch.bfloat16)
+        lg = torch.randn(1, E, device=dev, generator=gen)
+        y = torch.empty(1, h, device=dev)
+        act = torch.empty(ku, f, device=dev)
+        fn = lambda: ops.moe_ffn_decode_q8("q4_0", x, lg, wgu, wdn, h, f, E, ku, y=y, act_buf=act)   # noqa: E731
+    elif case.startswith("mv"):
         k, n = (12288, 4096) if case == "mv_down" else (4096, 24576)
         t = 8 if case == "mv8_gate_up" else 1
         w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
