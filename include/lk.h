@@ -134,10 +134,12 @@ int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, 
  * 706, 1224), launch(%rows, %k, %n, %x, %scales, %w [, %w2], %y):
  *   Y[rows][n] (+)= (X16 . W16^T) * scales[row][1]; swiglu: silu(G) * U with G, U the two weights' products.
  * x16: [rows][k] f16 (lk_row_scale_f16's output), scales: [rows][2] f32, y: [rows][n] f32.
- * Formats Q4_0, Q4_K, IQ4_NL. k % 256 == 0, n % 16 == 0; x16, w 16-byte aligned. Any rows >= 1.
+ * Formats: every one lk_dequant decodes (MXFP4S planes: lk_gemm_mxfp4s_f8). k % 64 == 0 and a whole number of the
+ * format's blocks, n % 16 == 0; x16 16-byte aligned, w 16-byte aligned for the Q4 family (2-byte otherwise, ggml
+ * MXFP4 any). Any rows >= 1.
  * When store / acc has fewer output tiles than the device has SMs (few rows and narrow n), K is split into ranges
- * whose partial products are added into y atomically (store first zeroes y on the stream): the f32 sums then run
- * in a varying order, so such results agree between runs to rounding, not bit for bit.
+ * that meet in y in a fixed order: range 0 stores (acc: adds onto y), range s adds its partial once ranges 0..s-1
+ * have, through a per-tile flag in liblk's device memory. The results are the same from run to run, bit for bit.
  */
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
             const void* w2, float* y, lk_stream_t stream);

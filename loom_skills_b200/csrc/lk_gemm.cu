@@ -12,6 +12,8 @@
 // fma_f16(q, f16(d*sc), f16(-dmin*m))) into the UMMA K-major 128-byte-swizzle B layout, and epilogue warps.
 #include <mutex>
 
+#include <atomic>
+
 #include "lk_common.cuh"
 #include "lk_formats.cuh"
 #include "lk_internal.h"
@@ -44,8 +46,11 @@ struct GemmArgs {
   int xrows, ku, n_experts;
   int n_fast;                 // persistent dense kernel: walk the n tiles of an m tile first (large A, small W)
   // persistent dense store / acc: K split into ksplit ranges of kps packed stages (256 values) each; every range is
-  // a tile of its own whose row-scaled partial product is added into y (zeroed first for store)
+  // a work item of its own. The ranges of an output tile meet in y in a fixed order: range 0 stores (acc: adds to y),
+  // range s adds its partial after range s - 1 has (turnstile: kflags[tile] = kepoch * 64 + ranges done).
   int ksplit, kps;
+  unsigned long long* kflags;
+  unsigned long long kepoch;
   ExpertEpi epi;              // gate/up activation and per-expert biases (bias index: expert * n + column)
   // window producer (formats whose packed rows are not 16-byte aligned 144-byte chunks): the weights' base
   // pointers and packed row stride
@@ -179,6 +184,27 @@ constexpr int kStgBytes = kEpWarps * 32 * kStgStride * 4;
 // B and packed-weight rings
 // WIN: the packed chunks come by per-row bulk copies of 16-byte aligned windows (any format, any row stride, a last
 // chunk of fewer than 256 values) instead of one 2-D TMA box of 144-byte chunks per stage.
+// Split-K turnstiles: one 64-bit flag per output tile of a launch, taken from a ring of slots, so that launches in
+// flight on other streams use other flags. A flag holds epoch * 64 + (K ranges already added); every launch has its
+// own epoch, and one launch's flags end at epoch * 64 + ksplit, a value no range of a later replay waits for.
+constexpr int kKFlags = 4096;
+__device__ unsigned long long g_kflags[kKFlags];
+
+// Waits until *flag == want (acquire); false when it gave up after about 2 s (the caller records the error and carries
+// on, so a missing predecessor cannot hang the GPU).
+LK_DEV bool turnstile_wait(const unsigned long long* flag, unsigned long long want) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    if (v == want) return true;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 2000000000ull) return false;
+    __nanosleep(64);
+  }
+}
+
 template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SAP, int SBP, int SRP, bool WIN>
 __global__ void __launch_bounds__(kGemmPThreads, 1)
     k_gemm_p(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
@@ -448,6 +474,16 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
       const int buf = li % NBUF;
       if (!mbar_wait(&acc_full[buf], (li / NBUF) & 1)) atomicOr(&g_status, 1u);
       tc_fence_after();
+      // split K: this item's K range and output tile; range s > 0 waits until ranges 0 .. s - 1 have added theirs
+      const bool ksp = GROUP == kDense && p.ksplit > 1;
+      const int item = int(blockIdx.x) + li * int(gridDim.x);
+      const int kt = ksp ? item % (mt * nt) : 0, ksi = ksp ? item / (mt * nt) : 0;
+      if (ksp && ksi > 0) {
+        if (warp == 2 + kDqWarps && lane == 0 &&
+            !turnstile_wait(p.kflags + kt, (p.kepoch << 6) | uint64_t(ksi)))
+          atomicOr(&g_status, 4u);
+        asm volatile("bar.sync 3, 128;" ::: "memory");   // the four epilogue warps
+      }
 #pragma unroll 1
       for (int mh = 0; mh < MH; ++mh) {
         const int row = mh * kBM + 32 * q + lane;
@@ -500,8 +536,13 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
             if (col_ok && trow < store_rows) {
               const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
-              if (GROUP == kDense && p.ksplit > 1) {   // one K range of several: add the partial
-                atomicAdd(reinterpret_cast<float4*>(p.dst[0] + off), o);
+              if (ksp && (ksi > 0 || MODE == LK_ACC)) {   // a later K range (or acc): add onto y, in range order
+                const float4 old = __ldcg(reinterpret_cast<const float4*>(p.dst[0] + off));
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+                *reinterpret_cast<float4*>(p.dst[0] + off) = o;
                 continue;
               }
               if (MODE == LK_ACC) {
@@ -517,6 +558,14 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             }
           }
           __syncwarp();
+        }
+      }
+      if (ksp) {   // every epilogue warp's stores of the range are issued: pass the turnstile on
+        asm volatile("bar.sync 3, 128;" ::: "memory");
+        if (warp == 2 + kDqWarps && lane == 0) {
+          __threadfence();
+          asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p.kflags + kt), "l"((p.kepoch << 6) | uint64_t(ksi + 1))
+                       : "memory");
         }
       }
       tc_fence_before();
@@ -741,8 +790,18 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
             : (m.w2 = m.w, LK_OK);
   if (rc != LK_OK) return rc;
   if (win) m.w = m.w2 = m.a;   // unused by the window form
-  if (a.ksplit > 1 && mode == LK_STORE && cudaMemsetAsync(y, 0, size_t(rows) * n * 4, s) != cudaSuccess)
-    return LK_ECUDA;   // the K ranges add into a zeroed y
+  if (a.ksplit > 1) {   // turnstile flags for the dense tiles of this launch (range 0 stores, the others add in order)
+    static unsigned long long* base[32] = {};
+    static std::atomic<unsigned long long> epoch{0};
+    static std::atomic<unsigned> slot{0};
+    if (dev >= 32) return LK_EUNSUPPORTED;
+    if (!base[dev] && cudaGetSymbolAddress(reinterpret_cast<void**>(&base[dev]), g_kflags) != cudaSuccess)
+      return LK_ECUDA;
+    unsigned s0 = slot.fetch_add(unsigned(dense_tiles)) % kKFlags;
+    if (s0 + unsigned(dense_tiles) > unsigned(kKFlags)) s0 = 0;
+    a.kflags = base[dev] + s0;
+    a.kepoch = ++epoch;
+  }
   if (!win) {
     switch (fmt) {
       case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, short_m, m, a, s);

@@ -208,3 +208,20 @@ def test_kbench_grouped_down(ops, gmoe, t):
     yh = host(y)
     assert (yh[192:] == O.KB_SENTINEL).all()
     np.testing.assert_allclose(yh[:, gmoe["kb_cols_h"]], gmoe[f"kb_grouped_dn_t{t}"], atol=2e-5, rtol=2e-4)
+
+
+@pytest.mark.parametrize("fmt", ["q6_k", "q5_0"])
+def test_gemm_split_k_window_deterministic(ops, fmt):
+    # few rows and narrow n on the window producer: K split into ranges that meet in y in a fixed order; against the
+    # f64 product and bit for bit from run to run
+    rows, n, k = 48, 512, 4096
+    w = blocks(fmt, n, k, 91)
+    x16, sc = row_scaled(rows, k, 92)
+    wd, xd, sd = dev(w), dev(x16), dev(sc)
+    y = ops.gemm(fmt, "store", xd, sd, wd, n)
+    W16 = O.dequant_f16(fmt, w, k).astype(np.float64).reshape(n, k)
+    ref16 = (x16.astype(np.float64) @ W16.T) * sc[:, 1:2]
+    assert O.rel_l2(host(y), ref16) < 1e-5, O.rel_l2(host(y), ref16)
+    for _ in range(3):
+        assert torch.equal(ops.gemm(fmt, "store", xd, sd, wd, n), y)
+    assert ops.device_status() == 0

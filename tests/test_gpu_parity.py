@@ -195,19 +195,51 @@ class TestGemm:
     @pytest.mark.parametrize("fmt", ["q4_k", "q4_0", "iq4_nl"])
     @pytest.mark.parametrize("rows,n,k", [(64, 1024, 4096), (37, 512, 12288), (128, 272, 1024), (129, 256, 2048)])
     def test_short_rows_split_k(self, ops, fmt, rows, n, k):
-        # at most 128 rows: 128 x 256 tiles; few tiles: K split into ranges whose partials add into y (store zeroes
-        # y first, acc adds onto it)
+        # at most 128 rows: 128 x 256 tiles; few tiles: K split into ranges that meet in y in a fixed order (range 0
+        # stores -- acc: adds onto y -- and range s adds after range s - 1): the same bits on every run
         w = weights(fmt, n, k, 71)
         _, x16, sc = row_scaled(rows, k, 72, big=True)
-        y = host(ops.gemm(fmt, "store", dev(x16), dev(sc), dev(w), n, y=dev(np.full((rows, n), 7.0, np.float32))))
+        wd, xd, sd = dev(w), dev(x16), dev(sc)
+        y = host(ops.gemm(fmt, "store", xd, sd, wd, n, y=dev(np.full((rows, n), 7.0, np.float32))))
         ref = O.gemm_ref(fmt, w, x16, sc, n, k)
         assert O.rel_l2(y, ref) < TOL, O.rel_l2(y, ref)
+        for _ in range(4):
+            assert np.array_equal(host(ops.gemm(fmt, "store", xd, sd, wd, n)), y)
         y0 = np.random.default_rng(73).standard_normal((rows, n)).astype(np.float32)
         ya = dev(y0)
-        ops.gemm(fmt, "acc", dev(x16), dev(sc), dev(w), n, y=ya)
+        ops.gemm(fmt, "acc", xd, sd, wd, n, y=ya)
         ref_acc = O.gemm_ref(fmt, w, x16, sc, n, k, mode="acc", y_old=y0)
         assert O.rel_l2(host(ya), ref_acc) < TOL, O.rel_l2(host(ya), ref_acc)
+        for _ in range(3):
+            yb = dev(y0)
+            ops.gemm(fmt, "acc", xd, sd, wd, n, y=yb)
+            assert torch.equal(yb, ya)
         assert ops.device_status() == 0
+
+    def test_split_k_graph_replays(self, ops):
+        # the split-K turnstiles across CUDA-graph replays of one captured launch (its epoch is reused): every replay
+        # gives the eager launch's bits
+        fmt, rows, n, k = "q4_k", 64, 1024, 4096
+        w = dev(weights(fmt, n, k, 81))
+        _, x16, sc = row_scaled(rows, k, 82, big=True)
+        xd, sd = dev(x16), dev(sc)
+        y_eager = ops.gemm(fmt, "store", xd, sd, w, n)
+        y = torch.full((rows, n), float("nan"), device="cuda")
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ops.gemm(fmt, "store", xd, sd, w, n, y=y)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                ops.gemm(fmt, "store", xd, sd, w, n, y=y)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            y.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(y, y_eager)
+        assert ops.device_status() == 0
+        del g
 
     def test_empty_rows(self, ops):
         w = weights("q4_k", 256, 256, 1)
