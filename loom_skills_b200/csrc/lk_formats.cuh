@@ -39,10 +39,15 @@ __host__ __device__ constexpr int fmt_block_bytes(int fmt) {
 }
 
 LK_DEV float f16_at(const uint8_t* p) { return h2f(uint16_t(p[0] | (p[1] << 8))); }
+// the IQ4 codebook value of nibble q: a byte permute of the biased table words (no indexed array, which would live
+// in local memory)
 LK_DEV int iq4_value(int q) {
-  constexpr int kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
-  return kv[q];
+  const uint32_t lo = prmt(kIq4Biased0, kIq4Biased1, uint32_t(q & 7));
+  const uint32_t hi = prmt(kIq4Biased2, kIq4Biased3, uint32_t(q & 7));
+  return int(((q & 8) ? hi : lo) & 0xffu) - 128;
 }
+// twice the E2M1 magnitude of code bits q & 7 (0 1 2 3 4 6 8 12), by a byte permute
+LK_DEV int e2m1_x2(int q) { return int(prmt(0x03020100u, 0x0C080604u, uint32_t(q & 7)) & 0xffu); }
 
 // The 32 values of group j (0 for 32-value formats, 0..7 of a super-block) as exact integer codes and the f32
 // scale / offset they combine with: value_i = a_i * q_i - c_i. Per format: a and c are per group or per 16-value
@@ -79,11 +84,10 @@ LK_DEV void group_codes(const uint8_t* b, int j, GroupCodes& g) {
     const int e = b[0];
     // ggml_e8m0_to_fp32_half: 2^(e - 128), the e2m1 table doubled to integers (0 1 2 3 4 6 8 12)
     const float half_scale = __uint_as_float(e < 2 ? (0x00200000u << e) : (uint32_t(e - 1) << 23));
-    constexpr int kv2[8] = {0, 1, 2, 3, 4, 6, 8, 12};
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int nib = i < 16 ? (b[1 + i] & 15) : (b[1 + i - 16] >> 4);
-      g.q[i] = (nib & 8) ? -kv2[nib & 7] : kv2[nib & 7];
+      g.q[i] = (nib & 8) ? -e2m1_x2(nib) : e2m1_x2(nib);
     }
     g.a_lo = g.a_hi = half_scale;
     g.c_lo = g.c_hi = 0.f;

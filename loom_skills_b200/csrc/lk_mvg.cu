@@ -13,6 +13,14 @@
 // against every token's activations, read straight from global memory (the CTA's rows share them in L1). A warp
 // reduces its rows' partial sums by shuffles. Instruction-bound by design (the decode plus one FMA per value and
 // token): the general path, where the Q4 formats' k_mv / k_mv_q8_rows are the tuned ones.
+//
+// k_mvs, the one-token dense form (the decode step's own shape): the same arithmetic, fed through shared memory.
+// A producer warp bulk-copies stages of 8 consecutive rows -- the 16-byte-aligned window that covers the rows' bytes,
+// one copy per weight -- into a 3-slot mbarrier ring, the first stage before griddepcontrol.wait; the 8 consumer warps
+// stage x once as f32, then warp w takes row w of each stage (lane l its groups l, l + 32, ...), decoding from shared
+// memory instead of global byte loads.
+#include <mutex>
+
 #include "lk_common.cuh"
 #include "lk_formats.cuh"
 #include "lk_internal.h"
@@ -132,6 +140,171 @@ __global__ void __launch_bounds__(kGWarps * 32) k_mvg(const MvArgs a) {
   }
 }
 
+constexpr int kSRows = 8;                    // rows per stage = consumer warps
+constexpr int kSThreads = 32 * (1 + kSRows);
+constexpr int kSStages = 3;
+
+LK_DEV void sgriddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LK_DEV void sgriddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// bytes of one weight's window in a slot: 8 rows and up to 15 bytes of slack at either end, 16-byte granules
+__host__ __device__ inline int64_t mvs_window(int64_t rb) { return (kSRows * rb + 30 + 15) / 16 * 16; }
+
+template <int FMT, int XT, bool SWIGLU>
+__global__ void __launch_bounds__(kSThreads, 2) k_mvs(const MvArgs a, int nstages, int slot_bytes) {
+  constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
+  constexpr int bb = fmt_block_bytes(FMT);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int64_t win = mvs_window(a.row_bytes);
+  float* xs = reinterpret_cast<float*>(smem + kSStages * slot_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + a.k);
+  uint64_t* empty = full + kSStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kSRows);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint8_t* w2 = a.w2 ? a.w2 : a.w;
+  // the window of rows r0 .. r0 + rows of weight `src` (rows start at row_off in it): [floor16(start), ceil16(end))
+  auto window = [&](const uint8_t* base, int64_t row0, int rows, uintptr_t& lo, uint32_t& bytes) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(base + row0 * a.row_bytes);
+    lo = b & ~uintptr_t(15);
+    bytes = uint32_t(((b + uintptr_t(rows * a.row_bytes) + 15) & ~uintptr_t(15)) - lo);
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      sgriddep_launch();
+      for (int i = 0;; ++i) {
+        const int st = cta + i * G;
+        if (st >= nstages) break;
+        if (i == 1) sgriddep_wait();   // the first stage goes out before the previous grid ends
+        const int s = i % kSStages;
+        if (i >= kSStages && !mbar_wait(&empty[s], ((i / kSStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        const int r0 = st * kSRows, rows = min(kSRows, a.n - r0);
+        uintptr_t lo, lo2 = 0;
+        uint32_t bytes, bytes2 = 0;
+        window(a.w, r0, rows, lo, bytes);
+        if (SWIGLU) window(w2, int64_t(a.w2_row_offset) + r0, rows, lo2, bytes2);
+        mbar_expect_tx(&full[s], bytes + bytes2);
+        bulk_g2s(smem + s * slot_bytes, reinterpret_cast<const void*>(lo), bytes, &full[s]);
+        if (SWIGLU) bulk_g2s(smem + s * slot_bytes + win, reinterpret_cast<const void*>(lo2), bytes2, &full[s]);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  sgriddep_wait();   // x comes from the previous kernel
+  for (int i = threadIdx.x - 32; i < a.k / 4; i += kSRows * 32) {   // x as f32 into shared memory
+    float4 f;
+    if (XT == LK_F32) {
+      f = __ldg(reinterpret_cast<const float4*>(a.x) + i);
+    } else {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.x) + i);
+      if (XT == LK_BF16) {
+        f = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                        __uint_as_float(u.y & 0xffff0000u));
+      } else {
+        const float2 p0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 p1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        f = make_float4(p0.x, p0.y, p1.x, p1.y);
+      }
+    }
+    reinterpret_cast<float4*>(xs)[i] = f;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kSRows * 32) : "memory");   // consumer warps only
+  const int cw = warp - 1, groups = a.k / 32;
+  for (int i = 0;; ++i) {
+    const int st = cta + i * G;
+    if (st >= nstages) break;
+    const int s = i % kSStages;
+    if (!mbar_wait(&full[s], (i / kSStages) & 1)) atomicOr(&g_status, 1u);
+    const int row = st * kSRows + cw;
+    float acc[2] = {0.f, 0.f};
+    if (row < a.n) {
+      const uintptr_t b0 = reinterpret_cast<uintptr_t>(a.w + int64_t(st) * kSRows * a.row_bytes);
+      const uintptr_t b1 = reinterpret_cast<uintptr_t>(w2 + (int64_t(a.w2_row_offset) + int64_t(st) * kSRows) * a.row_bytes);
+      const uint8_t* rp[2] = {smem + s * slot_bytes + (b0 & 15) + int64_t(cw) * a.row_bytes,
+                              smem + s * slot_bytes + win + (b1 & 15) + int64_t(cw) * a.row_bytes};
+#pragma unroll
+      for (int wi = 0; wi < (SWIGLU ? 2 : 1); ++wi) {
+        float sacc = 0.f;
+        for (int g = lane; g < groups; g += 32) {
+          float v[32];
+          group_values<FMT>(rp[wi] + (g / gpb) * bb, g % gpb, v);
+          const float4* xp = reinterpret_cast<const float4*>(xs + g * 32);
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 xv = xp[q];
+            s0 = fmaf(v[4 * q], xv.x, s0);
+            s1 = fmaf(v[4 * q + 1], xv.y, s1);
+            s0 = fmaf(v[4 * q + 2], xv.z, s0);
+            s1 = fmaf(v[4 * q + 3], xv.w, s1);
+          }
+          sacc += s0 + s1;
+        }
+        acc[wi] = sacc;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc[0] += __shfl_xor_sync(0xFFFFFFFFu, acc[0], o);
+      if (SWIGLU) acc[1] += __shfl_xor_sync(0xFFFFFFFFu, acc[1], o);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      if (row < a.n) {
+        const float val = SWIGLU ? act_apply(a.epi.act, acc[0], acc[1], a.epi.alpha, a.epi.limit) : acc[0];
+        float* yp = a.y + row;
+        *yp = a.accumulate ? *yp + val : val;
+      }
+    }
+  }
+}
+
+// the streaming form's launch: 0 when it does not apply (the caller falls back to k_mvg)
+template <int FMT, int XT, bool SWIGLU>
+int launch_s(const MvArgs& a, cudaStream_t s, bool& done) {
+  done = false;
+  const int64_t win = mvs_window(a.row_bytes);
+  const int slot = int((win * (SWIGLU ? 2 : 1) + 127) / 128 * 128);
+  const int smem = kSStages * slot + a.k * 4 + 2 * kSStages * 8;
+  if (smem > 110 * 1024 || a.k % 4) return LK_OK;   // two CTAs per SM, or not this form
+  auto kern = k_mvs<FMT, XT, SWIGLU>;
+  static int configured[32] = {};   // the largest shared-memory size set per device
+  static std::mutex mu;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 32) return LK_OK;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[dev] < smem) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+      configured[dev] = smem;
+    }
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int nstages = (a.n + kSRows - 1) / kSRows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(min(nstages, 2 * sms), 1, 1);
+  cfg.blockDim = dim3(kSThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  done = true;
+  return cudaLaunchKernelEx(&cfg, kern, a, nstages, slot) == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
 template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
 int launch_g(const MvArgs& a, int groups, cudaStream_t s) {
   const dim3 grid((a.n + kGRows - 1) / kGRows, groups);
@@ -141,6 +314,11 @@ int launch_g(const MvArgs& a, int groups, cudaStream_t s) {
 
 template <int FMT, int XT>
 int mvg_x(const MvArgs& a, cudaStream_t s) {
+  if (!a.ids && a.tokens == 1) {   // one token, dense: the row-streaming form where its shared memory fits
+    bool done = false;
+    const int rc = a.swiglu ? launch_s<FMT, XT, true>(a, s, done) : launch_s<FMT, XT, false>(a, s, done);
+    if (done || rc != LK_OK) return rc;
+  }
   if (a.ids)
     return a.swiglu ? launch_g<FMT, XT, true, true, 1>(a, a.tokens, s) : launch_g<FMT, XT, false, true, 1>(a, a.tokens, s);
   if (a.tokens == 1)
