@@ -327,6 +327,30 @@ def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
            "data": "IQ4_NL blocks synthesised on the device (uniform indices, f16 scale 3.5e-4); bf16 N(0,1) x",
            "n_gpus": world, "scaling": "strong", "sharding": "output columns (weight rows) per rank, y all-gathered"}
     steps = max(5, min(20, args.steps // 50))
+    # the parts on their own: this rank's shard GEMMs without any exchange, and the NCCL all-gather of f32 shards of
+    # the step's output sizes without any GEMM (max over ranks, like every line)
+    ys = [torch.empty(M, w.shape[0], device=dev) for _, _, _, w, _, _ in parts]
+
+    def gemm_step():
+        for (_, _, _, w, x16, sc), y in zip(parts, ys):
+            ops.gemm("iq4_nl", "store", x16, sc, w, w.shape[0], y=y)
+    for _ in range(3):
+        gemm_step()
+    g_ms = time_steps(gemm_step, steps)
+    out["gemm_only"] = {"ms_per_step": round(g_ms, 4), "tflops_per_rank": round(flops / world / (g_ms * 1e-3) / 1e12, 1)}
+    if world > 1:
+        gbufs = [torch.empty(world * M, y.shape[1], device=dev) for y in ys]
+
+        def gather_step():
+            for y, gb in zip(ys, gbufs):
+                dist.all_gather_into_tensor(gb, y)
+        for _ in range(3):
+            gather_step()
+        a_ms = time_steps(gather_step, steps)
+        moved = sum((world - 1) * M * y.shape[1] * 4 for y in ys)
+        out["gather_only"] = {"ms_per_step": round(a_ms, 4), "recv_gbs_per_rank": round(moved / (a_ms * 1e-3) / 1e9, 1)}
+        del gbufs
+    del ys
     for exchange in ("p2p", "collective"):
         sgs = [ShardedGemm("iq4_nl", "store", w, n, k, exchange=exchange) for _, k, n, w, _, _ in parts]
 
@@ -352,6 +376,52 @@ def bench_sharded(args, torch, dist, dev, world, rank, time_steps):
     out["roofline"] = {"target_ms": round(target * 1e3, 4), "t_math_ms": round(t_math * 1e3, 4),
                        "t_link_ms": round(t_link * 1e3, 4), "frac": round(target * 1e3 / out["p2p"]["ms_per_step"], 4),
                        "peaks": "measured bf16 sustained; NVLink 770 GB/s per direction (measured peer copy)"}
+    return out
+
+
+def bench_ep_moe(args, torch, dist, dev, world, rank, time_steps):
+    """configs[2] with its experts sharded over the ranks (expert parallelism): every rank routes its own 4096 tokens,
+    the assignments are sorted by destination rank and gathered on the GPU, NCCL all-to-all moves the rows there and
+    back, the owning rank runs its experts (grouped GEMMs), and the weighted combine reads the returned rows in place.
+    Weak scaling: 4096 tokens per rank. With one GPU the same tokens run the local MoE layer (no exchange)."""
+    from loom_skills_b200 import ops
+    from loom_skills_b200.parallel import ExpertParallelMoE
+    E, ku, h, f, m = 128, 8, 2048, 768, 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(777)   # the same experts on every rank; each rank keeps its slice
+    w_gu = synth_blocks(torch, dev, E * 2 * f, h, "q4_0", gen)
+    w_dn = synth_blocks(torch, dev, E * h, f, "q4_0", gen)
+    tgen = torch.Generator(device=dev)
+    tgen.manual_seed(1000 + rank)
+    x = torch.randn(m, h, device=dev, generator=tgen).to(torch.bfloat16)
+    lg = torch.randn(m, E, device=dev, generator=tgen)
+    flops = 2.0 * m * ku * 3 * h * f
+    out = {"workload": "configs[2] Qwen3-30B-A3B-like Q4_0 MoE layer, E=128 top-8, H=2048, F=768, 4096 tokens per rank",
+           "n_gpus": world, "scaling": "weak",
+           "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits per rank"}
+    steps = max(3, min(10, args.steps // 100))
+    if world == 1:
+        fn = lambda: ops.moe_ffn("q4_0", x, lg, w_gu, w_dn, h, f, E, ku)   # noqa: E731
+        for _ in range(3):
+            fn()
+        ms = time_steps(fn, steps)
+        out["local"] = {"ms_per_step": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+        return out
+    nl = E // world
+    moe = ExpertParallelMoE("q4_0", w_gu[rank * nl * 2 * f:(rank + 1) * nl * 2 * f].contiguous(),
+                            w_dn[rank * nl * h:(rank + 1) * nl * h].contiguous(), h, f, E, ku)
+    del w_gu, w_dn
+    for _ in range(3):
+        moe(x, lg)
+    ms = time_steps(lambda: moe(x, lg), steps)
+    moe(x, lg, timed=True)   # one more call with per-stage events (the stage times are max over ranks)
+    st = {}
+    for k, v in moe.times.items():
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        st[k] = round(float(t.item()), 4)
+    out["expert_parallel"] = {"ms_per_step": round(ms, 4), "tflops": round(world * flops / (ms * 1e-3) / 1e12, 1),
+                              "stages_ms": st}
     return out
 
 
@@ -675,6 +745,8 @@ def run_ours(args):
     gemv = bench_gemv_forms(args, torch, wstack, xs, pk, time_steps) if not args.no_extra else None
     # ---- the IQ4_NL GEMMs N-sharded over the ranks, all-gather fused into the epilogue (strong scaling)
     sharded = bench_sharded(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
+    # ---- configs[2] with its experts sharded over the ranks (expert parallelism, NCCL all-to-all)
+    ep = bench_ep_moe(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
 
@@ -697,7 +769,7 @@ def run_ours(args):
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
             "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_gemv": gemv, "decode_bf16": decode_bf16,
             "decode_fused": decode_fused,
-            "sharded_iq4_nl": sharded, "moe": moe}
+            "sharded_iq4_nl": sharded, "ep_moe": ep, "moe": moe}
         print(json.dumps(line), flush=True)
     if world > 1:
         del dec, mg, fg, bf, e2e_g, scale_g, gemm_g

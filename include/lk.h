@@ -137,9 +137,10 @@ int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, 
  * Formats: every one lk_dequant decodes (MXFP4S planes: lk_gemm_mxfp4s_f8). k % 64 == 0 and a whole number of the
  * format's blocks, n % 16 == 0; x16 16-byte aligned, w 16-byte aligned for the Q4 family (2-byte otherwise, ggml
  * MXFP4 any). Any rows >= 1.
- * When store / acc has fewer output tiles than the device has SMs (few rows and narrow n), K is split into ranges
- * that meet in y in a fixed order: range 0 stores (acc: adds onto y), range s adds its partial once ranges 0..s-1
- * have, through a per-tile flag in liblk's device memory. The results are the same from run to run, bit for bit.
+ * Store / acc may split K into ranges where that shortens the persistent grid's rounds (few output tiles, or a last
+ * round that would run nearly empty). The ranges meet in y in a fixed order: range 0 stores (acc: adds onto y), and
+ * range s adds its partial once ranges 0..s-1 have, through a per-tile flag in liblk's device memory. The results are
+ * the same from run to run, bit for bit.
  */
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
             const void* w2, float* y, lk_stream_t stream);
@@ -305,9 +306,23 @@ int lk_moe_ffn_decode_noalloc(int fmt, int tokens, int h, int f, int n_experts, 
  * lk_gemm_allgather: the prefill GEMM of this rank's shard (n_local output columns from its slice of weight rows),
  *   every output tile stored to all n_dst ranks' y buffers ([rows][n_total] f32, this rank's included) at columns
  *   col_offset .. col_offset + n_local - 1: P2P stores over NVLink as each tile finishes. y_dst is a HOST array of
- *   n_dst (<= 8) device pointers. The caller orders it against readers of the y buffers (a barrier of the ranks
- *   before and after). mode LK_STORE or LK_SWIGLU (w2 = this rank's up shard).
+ *   n_dst (<= 8) device pointers, y_dst[0] this rank's own buffer: when K is split into ranges (the store case of
+ *   lk_gemm), a tile's ranges meet there in order and the last range stores the finished tile to every buffer. The
+ *   caller orders the call against readers of the y buffers (a barrier of the ranks before and after). mode LK_STORE
+ *   or LK_SWIGLU (w2 = this rank's up shard).
  */
+/* Expert-parallel dispatch (no reference counterpart). Assignment a goes to rank ids[a] / n_local.
+ * lk_moe_rank_plan: a stable sort of the assignments by destination rank: order[i] = the i-th assignment in
+ *   (rank, a) order, pos[a] = its place in order, counts[r] = the assignments for rank r. assignments <= 65536,
+ *   world <= 32. The rows of rank r are order[sum(counts[< r]) ..]; the returned results, in the same order, combine
+ *   with lk_moe_combine_sorted(pos).
+ * lk_moe_gather_rows: out[i] = x[order[i] / ku] (rows of h values, LK_F32 or LK_BF16, 16-byte aligned, h * size a
+ *   multiple of 16), eid[i] = ids[order[i]] % n_local (eid may be NULL). */
+int lk_moe_rank_plan(int assignments, int n_local, int world, const int32_t* ids, int32_t* order, int32_t* pos,
+                     int32_t* counts, lk_stream_t stream);
+int lk_moe_gather_rows(int rows, int h, int ku, int n_local, const int32_t* order, const int32_t* ids, const void* x,
+                       int x_dtype, void* out, int32_t* eid, lk_stream_t stream);
+
 int lk_peer_alloc(int64_t bytes, void** ptr, void* handle64);
 int lk_peer_open(const void* handle64, void** ptr);
 int lk_peer_close(void* ptr);

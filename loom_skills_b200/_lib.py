@@ -59,6 +59,8 @@ SIGNATURES = {
     "lk_mv_q8_fused": (_I, [_I, _I, _I, _I, _P, _I, _P, _P, _P]),
     "lk_mv_q8_fused_multi": (_I, [_I, _I, _P, _P, _P, _I, _I, _P, _I, _P]),
     "lk_moe_wscale": (_I, [_I, _I, _I, _P, _P, _P, _P]),
+    "lk_moe_rank_plan": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
+    "lk_moe_gather_rows": (_I, [_I, _I, _I, _I, _P, _P, _P, _I, _P, _P, _P]),
     "lk_moe_ffn_decode_q8": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I,
                                   _F, _F, _P, _P, _P, _P, _I, _P, _P]),
     "lk_moe_shared_gate": (_I, [_I, _I, _P, _P, _I, _P, _P]),

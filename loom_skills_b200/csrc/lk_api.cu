@@ -462,4 +462,23 @@ int lk_moe_ffn_decode_q8(int fmt, int tokens, int h, int f, int n_experts, int k
   return moe_ffn_decode_q8(fmt, p, (cudaStream_t)stream);
 }
 
+int lk_moe_rank_plan(int assignments, int n_local, int world, const int32_t* ids, int32_t* order, int32_t* pos,
+                     int32_t* counts, lk_stream_t stream) {
+  if (assignments < 0 || assignments > 65536 || n_local <= 0 || world <= 0 || world > 32) return LK_EINVAL;
+  if (!counts) return LK_EINVAL;
+  if (assignments > 0 && (!ids || !order || !pos)) return LK_EINVAL;
+  return moe_rank_plan(assignments, n_local, world, ids, order, pos, counts, (cudaStream_t)stream);
+}
+
+int lk_moe_gather_rows(int rows, int h, int ku, int n_local, const int32_t* order, const int32_t* ids, const void* x,
+                       int x_dtype, void* out, int32_t* eid, lk_stream_t stream) {
+  if (rows < 0 || h <= 0 || ku <= 0 || n_local <= 0) return LK_EINVAL;
+  if (x_dtype != LK_F32 && x_dtype != LK_BF16) return LK_EINVAL;
+  if ((int64_t(h) * (x_dtype == LK_BF16 ? 2 : 4)) % 16) return LK_EINVAL;
+  if (rows == 0) return LK_OK;
+  if (!order || !ids || !x || !out) return LK_EINVAL;
+  if (!aligned(x, 16) || !aligned(out, 16)) return LK_EALIGN;
+  return moe_gather_rows(rows, h, ku, n_local, order, ids, x, x_dtype, out, eid, (cudaStream_t)stream);
+}
+
 }  // extern "C"

@@ -187,7 +187,7 @@ constexpr int kStgBytes = kEpWarps * 32 * kStgStride * 4;
 // Split-K turnstiles: one 64-bit flag per output tile of a launch, taken from a ring of slots, so that launches in
 // flight on other streams use other flags. A flag holds epoch * 64 + (K ranges already added); every launch has its
 // own epoch, and one launch's flags end at epoch * 64 + ksplit, a value no range of a later replay waits for.
-constexpr int kKFlags = 4096;
+constexpr int kKFlags = 1 << 16;
 __device__ unsigned long long g_kflags[kKFlags];
 
 // Waits until *flag == want (acquire); false when it gave up after about 2 s (the caller records the error and carries
@@ -536,16 +536,21 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgStride + sc);
             if (col_ok && trow < store_rows) {
               const int64_t off = int64_t(m0 + trow) * p.ld + p.col_off + n0 + col + sc;
-              if (ksp && (ksi > 0 || MODE == LK_ACC)) {   // a later K range (or acc): add onto y, in range order
-                const float4 old = __ldcg(reinterpret_cast<const float4*>(p.dst[0] + off));
-                o.x += old.x;
-                o.y += old.y;
-                o.z += old.z;
-                o.w += old.w;
-                *reinterpret_cast<float4*>(p.dst[0] + off) = o;
-                continue;
-              }
-              if (MODE == LK_ACC) {
+              if (ksp) {
+                // K ranges meet in dst[0] (this rank's own y) in range order; the last range stores the finished
+                // tile to every destination
+                if (ksi > 0 || MODE == LK_ACC) {
+                  const float4 old = __ldcg(reinterpret_cast<const float4*>(p.dst[0] + off));
+                  o.x += old.x;
+                  o.y += old.y;
+                  o.z += old.z;
+                  o.w += old.w;
+                }
+                if (ksi < p.ksplit - 1) {
+                  *reinterpret_cast<float4*>(p.dst[0] + off) = o;
+                  continue;
+                }
+              } else if (MODE == LK_ACC) {
                 float4 old = *reinterpret_cast<const float4*>(p.dst[0] + off);
                 o.x += old.x;
                 o.y += old.y;
@@ -692,8 +697,8 @@ static int gemm_fmt_win(int mode, int group, bool short_m, const GemmMaps& m, co
 }
 
 // K ranges for a dense store / acc GEMM of `tiles` output tiles and kp packed stages on `sms` persistent CTAs: the
-// count whose rounds x (stages per range + 1) is least -- the + 1 stands for a tile's fill and epilogue -- with no
-// empty range; the smallest such count on ties
+// count whose rounds x (stages per range + 1, + 1 more when split: the read-add-write of y) is least -- the + 1
+// stands for a tile's fill and epilogue -- with no empty range; the smallest such count on ties
 static int choose_ksplit(int tiles, int kp, int sms) {
   int best = 1;
   int64_t best_cost = INT64_MAX;
@@ -701,7 +706,7 @@ static int choose_ksplit(int tiles, int kp, int sms) {
     const int per = (kp + sp - 1) / sp;
     if ((kp + per - 1) / per != sp) continue;
     const int64_t rounds = (int64_t(tiles) * sp + sms - 1) / sms;
-    const int64_t cost = rounds * (per + 1);
+    const int64_t cost = rounds * (per + 1 + (sp > 1 ? 1 : 0));
     if (cost < best_cost) {
       best_cost = cost;
       best = sp;
@@ -770,9 +775,10 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   const int kp = (k + 255) / 256;   // packed chunks of 256 values (the last one may be shorter)
   a.ksplit = 1;
   a.kps = kp;
-  // fewer output tiles than SMs, one destination: the K ranges may add into y
+  // dense store / acc: split K where the rounds of the persistent grid come out shorter (few tiles, or a last round
+  // that would run nearly empty); the ranges meet in dst[0] in order
   const int dense_tiles = ((rows + tm - 1) / tm) * ((n + bn - 1) / bn);
-  if (group == kDense && mode != LK_SWIGLU && !out && rows > 0 && dense_tiles < sms) {
+  if (group == kDense && mode != LK_SWIGLU && rows > 0) {
     a.ksplit = choose_ksplit(dense_tiles, kp, sms);
     a.kps = (kp + a.ksplit - 1) / a.ksplit;
   }

@@ -84,6 +84,11 @@ int moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, cons
 int moe_combine_g(int tokens, int h, int ku, const float* ys, const int32_t* pos, const float* wts, const float* sg,
                   float* y, cudaStream_t s);
 int moe_wscale(int tokens, int ku, int n_experts, const int32_t* ids, float* wts, const float* scale, cudaStream_t s);
+// expert-parallel dispatch: the stable sort of assignments by destination rank, and the gather of the send rows
+int moe_rank_plan(int assignments, int n_local, int world, const int32_t* ids, int32_t* order, int32_t* pos,
+                  int32_t* counts, cudaStream_t s);
+int moe_gather_rows(int rows, int h, int ku, int n_local, const int32_t* order, const int32_t* ids, const void* x,
+                    int x_dtype, void* out, int32_t* eid, cudaStream_t s);
 int moe_shared_gate(int tokens, int h, const float* x, const void* w, int w_dtype, float* sg, cudaStream_t s);
 
 // int8-activation decode path (xq: codes [rows][k] int8, then [rows][k/32][2] f32 meta)

@@ -14,6 +14,7 @@
 namespace lk {
 
 constexpr int kTile = 64;   // gen_moe.py:826 TILE
+constexpr int kMaxRanks = 32;   // expert-parallel dispatch: ranks of one plan
 
 // ---------------------------------------------------------------------------------------------------------------
 // router: one 256-thread block per token; thread e owns expert e
@@ -239,6 +240,92 @@ __global__ void __launch_bounds__(1024) k_bucket(int tokens, int ku, int E, int 
 int moe_bucket(int tokens, int ku, int E, int max_tiles, const int32_t* info, const int32_t* ids, int32_t* tile_info,
                int32_t* rowmap, int32_t* pos, cudaStream_t s) {
   k_bucket<<<1, 1024, 0, s>>>(tokens, ku, E, max_tiles, info, ids, tile_info, rowmap, pos);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// expert-parallel dispatch (no reference counterpart: the reference runs on one device). Assignment a goes to rank
+// ids[a] / n_local. k_rank_plan: one 1024-thread block, a stable counting sort of the assignments by rank, with
+// k_bucket's structure (warp w owns a contiguous range of assignments; per-warp counts, one scan over the warps per
+// rank, then warp-local placement rounds in ascending order): order[i] = the i-th assignment in (rank, a) order,
+// pos[a] = its place in order, counts[r] = the assignments for rank r.
+// k_gather_rows: row i of the send buffer = x[order[i] / ku] (f32 or bf16, 16-byte copies), eid[i] = the local expert
+// ids[order[i]] % n_local.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_rank_plan(int A, int n_local, int world, const int32_t* __restrict__ ids,
+                                                    int32_t* __restrict__ order, int32_t* __restrict__ pos,
+                                                    int32_t* __restrict__ counts) {
+  __shared__ int wcnt[32][kMaxRanks];
+  __shared__ int rbase[kMaxRanks + 1];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = (A + 31) / 32;
+  const int a0 = min(A, warp * chunk), a1 = min(A, a0 + chunk);
+  auto rank_of = [&](int a) { return min(max(ids[a], 0) / n_local, world - 1); };
+  if (tid < 32 * kMaxRanks) (&wcnt[0][0])[tid] = 0;
+  __syncthreads();
+  for (int a = a0 + lane; a < a1; a += 32) atomicAdd(&wcnt[warp][rank_of(a)], 1);
+  __syncthreads();
+  if (tid < world) {   // exclusive scan over the warps, per rank
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wcnt[w][tid];
+      wcnt[w][tid] = run;
+      run += c;
+    }
+    counts[tid] = run;
+    rbase[tid] = run;
+  }
+  __syncthreads();
+  if (tid == 0) {   // rank bases
+    int acc = 0;
+    for (int r = 0; r < world; ++r) {
+      const int c = rbase[r];
+      rbase[r] = acc;
+      acc += c;
+    }
+    rbase[world] = acc;
+  }
+  __syncthreads();
+  for (int b = a0; b < a1; b += 32) {   // stable placement, warp-local rounds
+    const int a = b + lane;
+    const int r = a < a1 ? rank_of(a) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, r);
+    const int rk = __popc(peers & ((1u << lane) - 1));
+    if (r >= 0) {
+      const int off = rbase[r] + wcnt[warp][r] + rk;
+      order[off] = a;
+      pos[a] = off;
+    }
+    __syncwarp();
+    if (r >= 0 && rk == 0) wcnt[warp][r] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) k_gather_rows(int rows, int h, int ku, int n_local, const int32_t* __restrict__ order,
+                                                     const int32_t* __restrict__ ids, const void* __restrict__ x,
+                                                     void* __restrict__ out, int32_t* __restrict__ eid) {
+  const int i = blockIdx.x;
+  if (i >= rows) return;
+  const int a = order[i];
+  const int64_t bytes = int64_t(h) * (BF16 ? 2 : 4);
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + int64_t(a / ku) * bytes);
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + int64_t(i) * bytes);
+  for (int j = threadIdx.x; j < bytes / 16; j += 256) dst[j] = __ldg(src + j);
+  if (threadIdx.x == 0 && eid) eid[i] = max(ids[a], 0) % n_local;
+}
+
+int moe_rank_plan(int assignments, int n_local, int world, const int32_t* ids, int32_t* order, int32_t* pos,
+                  int32_t* counts, cudaStream_t s) {
+  k_rank_plan<<<1, 1024, 0, s>>>(assignments, n_local, world, ids, order, pos, counts);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+int moe_gather_rows(int rows, int h, int ku, int n_local, const int32_t* order, const int32_t* ids, const void* x,
+                    int x_dtype, void* out, int32_t* eid, cudaStream_t s) {
+  if (x_dtype == LK_BF16) k_gather_rows<true><<<rows, 256, 0, s>>>(rows, h, ku, n_local, order, ids, x, out, eid);
+  else k_gather_rows<false><<<rows, 256, 0, s>>>(rows, h, ku, n_local, order, ids, x, out, eid);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 

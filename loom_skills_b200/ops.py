@@ -480,6 +480,32 @@ def mv_q8_fused(fmt, w, x, n, k, y=None, accumulate=False):
     return y
 
 
+def moe_rank_plan(ids, n_local, world):
+    """lk_moe_rank_plan: assignments (ids [tokens][ku]) stably sorted by destination rank ids // n_local ->
+    (order [A] int32, pos [A] int32, counts [world] int32)."""
+    _cuda(ids)
+    ids = ids.contiguous()
+    a = ids.numel()
+    order = torch.empty(a, dtype=torch.int32, device=ids.device)
+    pos = torch.empty(a, dtype=torch.int32, device=ids.device)
+    counts = torch.empty(world, dtype=torch.int32, device=ids.device)
+    L.check(L.load().lk_moe_rank_plan(a, n_local, world, _ptr(ids), _ptr(order), _ptr(pos), _ptr(counts), _stream()),
+            "lk_moe_rank_plan")
+    return order, pos, counts
+
+
+def moe_gather_rows(order, ids, x, ku, n_local):
+    """lk_moe_gather_rows: (x[order // ku] rows, ids[order] % n_local as int32)."""
+    _cuda(order, ids, x)
+    x = x.contiguous()
+    rows = order.numel()
+    out = torch.empty(rows, x.shape[1], dtype=x.dtype, device=x.device)
+    eid = torch.empty(rows, dtype=torch.int32, device=x.device)
+    L.check(L.load().lk_moe_gather_rows(rows, x.shape[1], ku, n_local, _ptr(order), _ptr(ids.contiguous()), _ptr(x),
+                                        _DT[x.dtype], _ptr(out), _ptr(eid), _stream()), "lk_moe_gather_rows")
+    return out, eid
+
+
 def moe_ffn_decode_q8(fmt, x, logits, w_gate, w_down, h, f, n_experts, ku, w_up=None, gating=1, norm=True,
                       scale=1.0, router_bias=None, down_scale=None, act="silu", alpha=1.702, limit=7.0, b_gate=None,
                       b_up=None, b_down=None, y=None, accumulate=False, sg=None, act_buf=None, routing=False):

@@ -192,6 +192,16 @@ class GpuMoEBackend:
         from . import ops
         return ops.moe_route(logits, n_experts, ku)
 
+    def plan(self, ids, n_local, world):
+        """-> (order, pos, counts): the assignments stably sorted by destination rank (lk_moe_rank_plan)."""
+        from . import ops
+        return ops.moe_rank_plan(ids, n_local, world)
+
+    def gather(self, order, ids, x, ku, n_local):
+        """-> (send rows x[order // ku], their local expert ids) (lk_moe_gather_rows)."""
+        from . import ops
+        return ops.moe_gather_rows(order, ids, x, ku, n_local)
+
     def experts(self, x, eids, w_gu, w_dn, h, f, n_local):
         """rows x [R][h], each with one local expert eids[R] -> Wd[e] (silu(Wg[e] x) * (Wu[e] x)) [R][h]."""
         from . import ops
@@ -209,16 +219,20 @@ class GpuMoEBackend:
         ones = torch.ones(r, 1, dtype=torch.float32, device=x.device)
         return ops.moe_combine_sorted(ys, pos, ones)
 
-    def combine(self, ys, wts):
+    def combine_sorted(self, ys, pos, wts):
+        """y[t] = sum_k wts[t,k] ys[pos[t,k]] in k order (lk_moe_combine_sorted)."""
         from . import ops
-        return ops.moe_combine(ys, wts)
+        return ops.moe_combine_sorted(ys, pos.view(wts.shape), wts)
 
 
 class ExpertParallelMoE:
     """The routed expert FFN with experts sharded over the ranks of `group` (E % world == 0).
 
     w_gu_local: packed rows of this rank's experts, 2f rows each (gate then up) of h values; w_dn_local: h rows each
-    of f values. Each rank passes its own tokens."""
+    of f values. Each rank passes its own tokens. The dispatch runs on the GPU: the routing, a stable sort of the
+    assignments by destination rank, the gather of the send rows, and the weighted combine of the returned rows in
+    that order; NCCL moves the counts and the rows. The counts cross to the host once per call, as NCCL's variable
+    all-to-all takes its split sizes there."""
 
     def __init__(self, fmt, w_gu_local, w_dn_local, h, f, n_experts, ku, group=None, backend=None):
         self.world, self.rank = _world(group)
@@ -228,31 +242,34 @@ class ExpertParallelMoE:
         self.h, self.f, self.E, self.ku, self.group = h, f, n_experts, ku, group
         self.w_gu, self.w_dn = w_gu_local, w_dn_local
         self.be = backend if backend is not None else GpuMoEBackend(fmt)
+        self.times = None   # per-stage device times of the last call when timed (ms), see __call__
 
-    def dispatch_plan(self, ids):
-        """-> (order: assignments sorted by destination rank, stable; send_counts [world])."""
-        dest = (ids.reshape(-1) // self.n_local).long()
-        order = torch.argsort(dest, stable=True)
-        counts = torch.bincount(dest, minlength=self.world)
-        return order, counts
-
-    def __call__(self, x, logits):
+    def __call__(self, x, logits, timed=False):
         t = x.shape[0]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timed else None
+        mark = (lambda i: ev[i].record()) if timed else (lambda i: None)
+        mark(0)
         ids, wts = self.be.route(logits, self.E, self.ku)
-        order, send_counts = self.dispatch_plan(ids)
+        order, pos, send_counts = self.be.plan(ids, self.n_local, self.world)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-        flat = ids.reshape(-1).long()
-        send_x = x.index_select(0, order // self.ku).contiguous()
-        send_e = (flat[order] % self.n_local).to(torch.int32).contiguous()
+        send_x, send_e = self.be.gather(order, ids, x, self.ku, self.n_local)
+        counts = torch.cat([send_counts, recv_counts]).tolist()   # the split sizes NCCL takes on the host
+        sc, rc = counts[:self.world], counts[self.world:]
         recv_x = torch.empty(sum(rc), self.h, dtype=x.dtype, device=x.device)
         recv_e = torch.empty(sum(rc), dtype=torch.int32, device=x.device)
+        mark(1)
         dist.all_to_all_single(recv_x, send_x, rc, sc, group=self.group)
         dist.all_to_all_single(recv_e, send_e, rc, sc, group=self.group)
+        mark(2)
         ys_recv = self.be.experts(recv_x, recv_e, self.w_gu, self.w_dn, self.h, self.f, self.n_local).contiguous()
+        mark(3)
         ys_back = torch.empty(t * self.ku, self.h, dtype=ys_recv.dtype, device=x.device)
         dist.all_to_all_single(ys_back, ys_recv, sc, rc, group=self.group)
-        ys = torch.empty_like(ys_back)
-        ys[order] = ys_back
-        return self.be.combine(ys, wts)
+        mark(4)
+        y = self.be.combine_sorted(ys_back, pos, wts)
+        if timed:
+            torch.cuda.synchronize()
+            self.times = {"route_plan_gather_ms": ev[0].elapsed_time(ev[1]), "dispatch_a2a_ms": ev[1].elapsed_time(ev[2]),
+                          "experts_ms": ev[2].elapsed_time(ev[3]), "return_a2a_ms": ev[3].elapsed_time(ev[4])}
+        return y

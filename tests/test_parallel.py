@@ -63,9 +63,20 @@ class OracleMoE:
             out[sel] = act @ dn.T.astype(np.float64)
         return torch.from_numpy(out.astype(np.float32))
 
-    def combine(self, ys, wts):
+    def plan(self, ids, n_local, world):
+        dest = (ids.reshape(-1) // n_local).long()
+        order = torch.argsort(dest, stable=True)
+        pos = torch.empty_like(order)
+        pos[order] = torch.arange(order.numel())
+        return order.to(torch.int32), pos.to(torch.int32), torch.bincount(dest, minlength=world).to(torch.int32)
+
+    def gather(self, order, ids, x, ku, n_local):
+        o = order.long()
+        return x.index_select(0, o // ku).contiguous(), (ids.reshape(-1).long()[o] % n_local).to(torch.int32)
+
+    def combine_sorted(self, ys, pos, wts):
         t, ku = wts.shape
-        return (ys.view(t, ku, -1).double() * wts.double()[:, :, None]).sum(1).float()
+        return (ys[pos.long()].view(t, ku, -1).double() * wts.double()[:, :, None]).sum(1).float()
 
 
 def _worker(rank, world, port, q):
