@@ -127,6 +127,13 @@ def synth_q4k(rng, rows, k):
     return w.reshape(rows, -1)
 
 
+def synth_q6k(rng, rows, k):
+    """Q6_K blocks (210 bytes per 256 values): uniform 6-bit codes and int8 sub-block scales, f16 d at byte 208."""
+    b = rng.integers(0, 256, (rows * k // 256, 210), dtype=np.uint8)
+    b[:, 208:210] = np.frombuffer(np.float16(2e-4).tobytes(), np.uint8)
+    return b.reshape(rows, -1)
+
+
 # ------------------------------------------------------------------------------------------------------------------
 # CPU baseline / reference arm: the reference's own CPU path for the decode matvec -- gguf's dequantize (the
 # reference's pinned third-party dequantiser, gguf 0.19.0) and a float64 numpy matvec, as make_kernel_tests.py:45-47,
@@ -261,6 +268,69 @@ def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
         if acts == "int8":
             out[label]["fused_us_per_launch"] = round(timed(True), 2)   # the row quantised in the prologue
         del ws
+    return out
+
+
+def bench_pairs(args, torch, dev, time_steps):
+    """Gate and up in two formats (Q4_K_M's Q4_K gate + Q6_K up; LK_FMT_PAIR) on a Qwen3-8B-like FFN, K=4096
+    N=12288 each: the one-token decode (bf16 x) as one pair launch and as the reference's dense fallback -- two
+    projections + g_silu_mul (gen_llm.py:6280-6283) -- over weights rotated past L2; and the prefill swiglu GEMM at
+    M=2048 as one pair launch, beside two store GEMMs + silu_mul and the one-format Q4_K swiglu GEMM."""
+    from loom_skills_b200 import ops
+    rng = np.random.default_rng(11)
+    k, n, m = 4096, 12288, 2048
+    wg = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+    wu = torch.from_numpy(synth_q6k(rng, n, k)).to(dev)
+    nbytes = wg.numel() + wu.numel()
+    copies = max(2, -(-256_000_000 // nbytes))
+    ws = [(wg, wu)] + [(wg.clone(), wu.clone()) for _ in range(copies - 1)]
+    x = torch.randn(1, k, device=dev).to(torch.bfloat16)
+    y, yu = torch.empty(1, n, device=dev), torch.empty(1, n, device=dev)
+    chain = 16
+
+    def mv_pair():
+        for i in range(chain):
+            g, u = ws[i % copies]
+            ops.mv("q4_k+q6_k", g, x, n, k, w2=u, y=y)
+
+    def mv_two():
+        for i in range(chain):
+            g, u = ws[i % copies]
+            ops.mv("q4_k", g, x, n, k, y=y)
+            ops.mv("q6_k", u, x, n, k, y=yu)
+            ops.silu_mul(y, yu)
+
+    def timed(body, steps, per):
+        g = Timed(torch, body)
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        return time_steps(g.replay, steps) / per
+
+    out = {"shape": {"k": k, "n": n, "gate": "q4_k", "up": "q6_k", "weight_mb": round(nbytes / 1e6, 1)}}
+    steps = max(5, min(args.steps, 200))
+    us_pair = timed(mv_pair, steps, chain) * 1e3
+    us_two = timed(mv_two, steps, chain) * 1e3
+    out["decode"] = {"pair_us": round(us_pair, 2), "pair_weight_gbs": round(nbytes / (us_pair * 1e-6) / 1e9, 1),
+                     "two_projections_silu_mul_us": round(us_two, 2), "weight_copies": copies,
+                     "kernel": "k_mvs<kFmtPair> (lk_mv with LK_FMT_PAIR, bf16 x)"}
+    del ws
+    x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
+    yp, yq = torch.empty(m, n, device=dev), torch.empty(m, n, device=dev)
+    wg2 = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+    flops = 2.0 * 2 * m * n * k
+    gsteps = max(3, min(args.steps, 50))
+    ms_pair = timed(lambda: ops.gemm("q4_k+q6_k", "swiglu", x16, sc, wg, n, w2=wu, y=yp), gsteps, 1)
+
+    def gemm_two():
+        ops.gemm("q4_k", "store", x16, sc, wg, n, y=yp)
+        ops.gemm("q6_k", "store", x16, sc, wu, n, y=yq)
+        ops.silu_mul(yp, yq)
+    ms_two = timed(gemm_two, gsteps, 1)
+    ms_one = timed(lambda: ops.gemm("q4_k", "swiglu", x16, sc, wg, n, w2=wg2, y=yp), gsteps, 1)
+    out["prefill"] = {"rows": m, "pair_tflops": round(flops / (ms_pair * 1e-3) / 1e12, 1),
+                      "pair_ms": round(ms_pair, 4), "two_gemms_silu_mul_ms": round(ms_two, 4),
+                      "q4_k_swiglu_ms": round(ms_one, 4),
+                      "kernel": "k_gemm_p<kFmtPair> (window form, tcgen05 kind::f16)"}
     return out
 
 
@@ -749,6 +819,8 @@ def run_ours(args):
     ep = bench_ep_moe(args, torch, dist, dev, world, rank, time_steps) if not args.no_extra else None
     # ---- the MoE layers, and the dense MXFP4 x FP8 GEMM (each rank a replica)
     moe = bench_moe(args, torch, dev, time_steps, pk) if not args.no_extra else None
+    # ---- gate and up in two formats (Q4_K_M's Q4_K + Q6_K), decode and prefill (each rank a replica)
+    pairs = bench_pairs(args, torch, dev, time_steps) if not args.no_extra else None
 
     gpu_launches = args.steps * launches_per_step   # 16 quantisations + 32 matvec launches per step
     if rank == 0:
@@ -769,7 +841,7 @@ def run_ours(args):
             "gpu_launches": gpu_launches, "clocks": clocks, "prefill": prefill, "sweep": sweep,
             "hbm_frac": round(value / world / pk["hbm_gbs"], 4), "decode_gemv": gemv, "decode_bf16": decode_bf16,
             "decode_fused": decode_fused,
-            "sharded_iq4_nl": sharded, "ep_moe": ep, "moe": moe}
+            "sharded_iq4_nl": sharded, "ep_moe": ep, "moe": moe, "gate_up_pair": pairs}
         print(json.dumps(line), flush=True)
     if world > 1:
         del dec, mg, fg, bf, e2e_g, scale_g, gemm_g
@@ -785,7 +857,8 @@ def run_profile_case(args):
     MXFP4S expert matvecs of one gpt-oss token: 4 assignments of 32 experts, h = f = 2880, bf16 x), mvf_gate_up (the
     gate_up matvec quantising its bf16 row in the prologue), mvg_q6k (the generic-format matvec, Q6_K K=4096
     N=4096, f32 x), gemm_q6k (the window-producer GEMM, Q6_K M=2048 K=4096 N=4096), moeq8 (the int8 decode MoE layer
-    of configs[2] at one token: E=128 top-8, H=2048, F=768, Q4_0)."""
+    of configs[2] at one token: E=128 top-8, H=2048, F=768, Q4_0), mvp_gate_up / gemmp_gate_up (a Q4_K gate and Q6_K
+    up pair, K=4096 N=12288: the one-token matvec on bf16 x, and the swiglu GEMM at M=2048)."""
     import torch
 
     from loom_skills_b200 import ops
@@ -798,12 +871,22 @@ def run_profile_case(args):
         x = torch.randn(1, k, device=dev).to(torch.bfloat16)
         y = torch.empty(1, n, device=dev)
         fn = lambda: ops.mv_q8_fused("q4_k", w, x, n, k, y=y)   # noqa: E731
+    elif case in ("mvp_gate_up", "gemmp_gate_up"):
+        k, n = 4096, 12288
+        wg = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+        wu = torch.from_numpy(synth_q6k(rng, n, k)).to(dev)
+        if case == "mvp_gate_up":
+            x = torch.randn(1, k, device=dev).to(torch.bfloat16)
+            y = torch.empty(1, n, device=dev)
+            fn = lambda: ops.mv("q4_k+q6_k", wg, x, n, k, w2=wu, y=y)   # noqa: E731
+        else:
+            m = 2048
+            x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
+            y = torch.empty(m, n, device=dev)
+            fn = lambda: ops.gemm("q4_k+q6_k", "swiglu", x16, sc, wg, n, w2=wu, y=y)   # noqa: E731
     elif case in ("mvg_q6k", "gemm_q6k"):
         k, n = 4096, 4096
-        # Q6_K blocks (210 bytes per 256 values): uniform 6-bit codes and int8 sub-block scales, f16 d at byte 208
-        b = rng.integers(0, 256, (n * k // 256, 210), dtype=np.uint8)
-        b[:, 208:210] = np.frombuffer(np.float16(2e-4).tobytes(), np.uint8)
-        w = torch.from_numpy(b.reshape(n, -1)).to(dev)
+        w = torch.from_numpy(synth_q6k(rng, n, k)).to(dev)
         if case == "mvg_q6k":
             x = torch.randn(1, k, device=dev)
             y = torch.empty(1, n, device=dev)

@@ -36,6 +36,14 @@ enum {
   LK_Q4_0 = 2, LK_Q5_0 = 6, LK_Q8_0 = 8, LK_Q3_K = 11, LK_Q4_K = 12, LK_Q5_K = 13, LK_Q6_K = 14, LK_IQ4_NL = 20,
   LK_IQ4_XS = 23, LK_MXFP4 = 39, LK_MXFP4S = 1039
 };
+/* Gate and up weights in two formats (Q4_K_M's Q4_K gate and Q6_K up; unsloth's mixed quants): the reference's
+ * "GATE+UP" format (gen_moe.py:537-552 expert_mv, :1129-1141 grouped_gemm; gen_gemm.py:535-545 gemm fmt2 and
+ * :1224-1251 gemm_big256 fmt2). LK_FMT_PAIR(gate, up) goes where a gate/up entry point takes `fmt`: lk_mv with w2,
+ * lk_gemm with LK_SWIGLU, lk_moe_expert_mv[_ex] mode 0 and lk_moe_grouped_gemm[_ex] with LK_SWIGLU /
+ * LK_SWIGLU_SORTED, the gate and up in separate tensors (fused = 0), each weight with its own row stride and decode.
+ * Either half is any format but LK_MXFP4S; k must be a whole number of both formats' blocks. A pair of one format is
+ * that format. Any other entry point, mode or fused = 1 with a pair: LK_EINVAL. */
+#define LK_FMT_PAIR(gate, up) ((int)(gate) | ((int)(up) << 16))
 /* element types (ggml ids where ggml has one) */
 enum { LK_F32 = 0, LK_F16 = 1, LK_BF16 = 30, LK_E4M3 = 1000 };
 /* GEMM epilogues (gen_gemm.py:535 `mode`): y = acc, y += acc, y = silu(acc_w) * acc_w2. LK_SWIGLU_SORTED (grouped
@@ -93,10 +101,16 @@ int lk_row_scale_f8(int rows, int k, const void* x, int x_dtype, float* scales, 
  * Decode matvec (tokens < 64). Replaces g_mv_{fmt}_k{K}[_t{TG}][_r{R}] and its swiglu pair (gen_llm.py:1159-1378),
  * launch(%n, %tokens, %accumulate, %x, %w [, %w2], %y): y[t][n] (+)= sum_k x[t][k] W[n][k];
  * w2 != NULL: y[t][n] (+)= silu(x.Wg[n]) * (x.Wu[n]).  x: [tokens][k] of x_dtype (LK_F32, LK_F16 or LK_BF16),
- * W: [n] packed rows. Formats Q4_0, Q4_K, IQ4_NL; k % 256 == 0; w 16-byte aligned.
+ * W: [n] packed rows. Every format lk_dequant decodes but LK_MXFP4S, and LK_FMT_PAIR(gate, up) with w2; k a whole
+ * number of the format's blocks. The Q4 family with k % 256 == 0 and 16-byte aligned w runs the tuned kernel.
  */
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w,
           const void* w2, float* y, lk_stream_t stream);
+/* lk_silu_mul: g_silu_mul (gen_llm.py:5717-5745; gen_llm.py:77, 6280-6283: the glue after two projections of a gate
+ * and up in different formats), launch(%tokens, %n, %f, %u): f[t][c] = act(f[t][c]) * u[t][c] over [tokens][n] f32,
+ * in place; act LK_ACT_SILU, or LK_ACT_GELU for the GEGLU form (gen_llm.py:5670-5716). n % 4 == 0; f, u 16-byte
+ * aligned. The LK_FMT_PAIR kernels make the two projections and this glue one launch. */
+int lk_silu_mul(int tokens, int n, float* f, const float* u, int act, lk_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Decode matvec with int8 activations: the reference's default decode numerics (ACT_Q8=1, gen_llm.py:514-518).
@@ -134,9 +148,10 @@ int lk_mv_q8_fused_multi(int fmt, int nseg, const int* n, const void* const* w, 
  * 706, 1224), launch(%rows, %k, %n, %x, %scales, %w [, %w2], %y):
  *   Y[rows][n] (+)= (X16 . W16^T) * scales[row][1]; swiglu: silu(G) * U with G, U the two weights' products.
  * x16: [rows][k] f16 (lk_row_scale_f16's output), scales: [rows][2] f32, y: [rows][n] f32.
- * Formats: every one lk_dequant decodes (MXFP4S planes: lk_gemm_mxfp4s_f8). k % 64 == 0 and a whole number of the
- * format's blocks, n % 16 == 0; x16 16-byte aligned, w 16-byte aligned for the Q4 family (2-byte otherwise, ggml
- * MXFP4 any). Any rows >= 1.
+ * Formats: every one lk_dequant decodes (MXFP4S planes: lk_gemm_mxfp4s_f8); LK_SWIGLU also LK_FMT_PAIR(gate, up),
+ * whose two weights the kernel decodes each in its own format. k % 64 == 0 and a whole number of the format's
+ * blocks, n % 16 == 0; x16 16-byte aligned; w 16-byte aligned for Q4_K outside a pair, 2-byte otherwise (ggml MXFP4
+ * any). Any rows >= 1.
  * Store / acc may split K into ranges where that shortens the persistent grid's rounds (few output tiles, or a last
  * round that would run nearly empty). The ranges meet in y in a fixed order: range 0 stores (acc: adds onto y), and
  * range s adds its partial once ranges 0..s-1 have, through a per-tile flag in liblk's device memory. The results are
@@ -189,6 +204,8 @@ int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, i
  *   y[t] (+)= sum_k wts[t][k] * ys[pos[t][k]] (pos < 0 -> 0).
  * lk_moe_expert_mv: decode expert matvecs g_moe_gu_{fmt} / g_moe_dn_{fmt} (gen_moe.py:535-727): mode 0 (gu):
  *   y[a] = silu(Wg[e] x[a/ku]) * (Wu[e] x[a/ku]); mode 1 (dn): y[a] = Wd[e] x[a]; e = ids[a].
+ * The gate/up forms of both (expert_mv mode 0, grouped LK_SWIGLU / LK_SWIGLU_SORTED) take LK_FMT_PAIR(gate, up) with
+ *   fused = 0: w the gate experts [n_experts][n] rows, w2 the up experts, each in its own format.
  * lk_moe_combine: g_moe_combine (gen_moe.py:730-762): y[t] (+)= sum_k wts[t][k] ys[t*ku + k].
  */
 int lk_moe_route(int tokens, int h, int n_experts, int ku, int gating, int norm, float scale, const float* x,

@@ -15,6 +15,13 @@ ACT_SILU, ACT_GELU, ACT_SWIGLU_OAI = 0, 1, 2
 ACT_IDS = {"silu": ACT_SILU, "gelu": ACT_GELU, "swiglu_oai": ACT_SWIGLU_OAI}
 FMT_IDS = {"q4_0": Q4_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "mxfp4": MXFP4, "mxfp4s": MXFP4S, "q5_0": Q5_0,
            "q8_0": Q8_0, "q3_k": Q3_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq4_xs": IQ4_XS}
+
+
+def fmt_pair(gate, up):
+    """LK_FMT_PAIR(gate, up): the id of gate and up weights in two formats (the reference's "GATE+UP" format)."""
+    return int(gate) | (int(up) << 16)
+
+
 MODE_IDS = {"store": STORE, "acc": ACC, "swiglu": SWIGLU, "swiglu_sorted": SWIGLU_SORTED}
 
 _P, _I, _L, _F, _U = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint
@@ -29,6 +36,7 @@ SIGNATURES = {
     "lk_row_scale_f16": (_I, [_I, _I, _P, _I, _P, _P, _P]),
     "lk_row_scale_f8": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _P]),
     "lk_mv": (_I, [_I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
+    "lk_silu_mul": (_I, [_I, _I, _P, _P, _I, _P]),
     "lk_quant_q8": (_I, [_I, _I, _P, _I, _P, _P]),
     "lk_mv_q8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "lk_mv_q8_multi": (_I, [_I, _I, _P, _P, _P, _I, _I, _I, _P, _P]),

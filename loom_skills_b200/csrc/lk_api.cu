@@ -18,6 +18,18 @@ static bool mv_format(int fmt) {
 static bool tuned_q4(int fmt, int k, const void* w, const void* w2) {
   return q4_family(fmt) && k % 256 == 0 && aligned(w, 16) && (!w2 || aligned(w2, 16));
 }
+// LK_FMT_PAIR(gate, up) ids: the gate's format in the low 16 bits, the up weight's above; a pair of one format is
+// that format
+static int pair_norm(int fmt) { return (fmt >> 16) == (fmt & 0xffff) ? (fmt & 0xffff) : fmt; }
+static bool is_pair(int fmt) { return (fmt >> 16) != 0; }
+static int gate_fmt(int fmt) { return is_pair(fmt) ? (fmt & 0xffff) : fmt; }
+static int up_fmt(int fmt) { return is_pair(fmt) ? (fmt >> 16) : fmt; }
+// both formats of a (possibly paired) id decodable, k a whole number of both formats' blocks
+static int pair_check(int fmt, int64_t k) {
+  if (!mv_format(gate_fmt(fmt)) || !mv_format(up_fmt(fmt))) return LK_EUNSUPPORTED;
+  if (k % fmt_qk(gate_fmt(fmt)) || k % fmt_qk(up_fmt(fmt))) return LK_EINVAL;
+  return LK_OK;
+}
 
 
 extern "C" {
@@ -144,11 +156,22 @@ int lk_moe_row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, cons
   return row_scale_gather(rows, k, ku, rowmap, x, x_dtype, scales, x16, x8, s8, (cudaStream_t)stream);
 }
 
+int lk_silu_mul(int tokens, int n, float* f, const float* u, int act, lk_stream_t stream) {
+  if (tokens < 0 || n <= 0 || n % 4) return LK_EINVAL;
+  if (act != LK_ACT_SILU && act != LK_ACT_GELU) return LK_EINVAL;
+  if (tokens == 0) return LK_OK;
+  if (!f || !u) return LK_EINVAL;
+  if (!aligned(f, 16) || !aligned(u, 16)) return LK_EALIGN;
+  return act_mul(tokens, n, act, f, u, (cudaStream_t)stream);
+}
+
 int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int x_dtype, const void* w, const void* w2,
           float* y, lk_stream_t stream) {
-  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
+  fmt = pair_norm(fmt);
+  if (!mv_format(gate_fmt(fmt)) || !mv_format(up_fmt(fmt))) return LK_EUNSUPPORTED;
   if (n <= 0 || k <= 0 || tokens < 0) return LK_EINVAL;
-  if (k % fmt_qk(fmt)) return LK_EINVAL;
+  if (int rc = pair_check(fmt, k)) return rc;
+  if (is_pair(fmt) && !w2) return LK_EINVAL;   // a format pair is a gate/up matvec
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
   if (!x || !w || !y) return LK_EINVAL;
@@ -163,7 +186,7 @@ int lk_mv(int fmt, int n, int k, int tokens, int accumulate, const void* x, int 
   a.tokens = tokens;
   a.accumulate = accumulate;
   a.x_dtype = x_dtype;
-  a.row_bytes = lk_row_bytes(fmt, k);
+  a.row_bytes = lk_row_bytes(gate_fmt(fmt), k);
   a.swiglu = w2 != nullptr;
   if (tuned_q4(fmt, k, w, w2)) return mv(fmt, a, (tokens + 7) / 8, (cudaStream_t)stream);
   return mv_generic(fmt, a, (cudaStream_t)stream);
@@ -200,10 +223,12 @@ int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku
                         const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2,
                         const float* bias, const float* bias2, int act, float alpha, float limit, float* y,
                         lk_stream_t stream) {
-  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
+  fmt = pair_norm(fmt);
+  if (!mv_format(gate_fmt(fmt)) || !mv_format(up_fmt(fmt))) return LK_EUNSUPPORTED;
   if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
   if (mode != 0 && mode != 1) return LK_EINVAL;
-  if (k % fmt_qk(fmt)) return LK_EINVAL;
+  if (int rc = pair_check(fmt, k)) return rc;
+  if (is_pair(fmt) && (mode != 0 || fused)) return LK_EINVAL;   // a pair: separate gate and up tensors
   if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
   if (!act_ok(act)) return LK_EINVAL;
   if (mode == 0 && (!bias) != (!bias2)) return LK_EINVAL;
@@ -220,7 +245,7 @@ int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku
   a.k = k;
   a.tokens = assignments;
   a.x_dtype = x_dtype;
-  a.row_bytes = lk_row_bytes(fmt, k);
+  a.row_bytes = lk_row_bytes(gate_fmt(fmt), k);
   a.ids = ids;
   a.x_div = mode == 0 ? ku : 1;
   a.n_experts = n_experts;
@@ -240,20 +265,23 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                              nullptr, LK_ACT_SILU, 0.f, 0.f, y, stream);
 }
 
-// the prefill GEMMs' weight contract: a whole number of 64-value stages and of the format's blocks; Q4_K keeps its
-// 16-byte aligned rows (it always takes the TMA box form), the others need 2-byte aligned blocks (MXFP4: any)
+// the prefill GEMMs' weight contract: a whole number of 64-value stages and of the format's blocks; Q4_K alone keeps
+// its 16-byte aligned rows (it takes the TMA box form), the others -- and either weight of a format pair, which takes
+// the window form -- need 2-byte aligned blocks (MXFP4: any)
 static int gemm_weight_check(int fmt, int k, const void* w, const void* w2) {
-  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
-  if (k % 64 || k % fmt_qk(fmt)) return LK_EINVAL;
-  const uintptr_t al = fmt == LK_Q4_K ? 16 : fmt == LK_MXFP4 ? 1 : 2;
-  if (!aligned(w, al) || (w2 && !aligned(w2, al))) return LK_EALIGN;
+  if (int rc = pair_check(fmt, k)) return rc;
+  if (k % 64) return LK_EINVAL;
+  auto al = [&](int f) -> uintptr_t { return (f == LK_Q4_K && !is_pair(fmt)) ? 16 : f == LK_MXFP4 ? 1 : 2; };
+  if (!aligned(w, al(gate_fmt(fmt))) || (w2 && !aligned(w2, al(up_fmt(fmt))))) return LK_EALIGN;
   return LK_OK;
 }
 
 int lk_gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
             const void* w2, float* y, lk_stream_t stream) {
-  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
+  fmt = pair_norm(fmt);
+  if (!mv_format(gate_fmt(fmt)) || !mv_format(up_fmt(fmt))) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_ACC && mode != LK_SWIGLU) return LK_EINVAL;
+  if (is_pair(fmt) && mode != LK_SWIGLU) return LK_EINVAL;
   if (rows < 0 || k <= 0 || n <= 0) return LK_EINVAL;
   if (n % 16) return LK_EINVAL;
   if (rows == 0) return LK_OK;
@@ -293,8 +321,10 @@ int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows,
                            const int32_t* tile_info, const int32_t* rowmap, const uint16_t* x16, const float* scales,
                            const void* w, const void* w2, const float* bias, const float* bias2, int act, float alpha,
                            float limit, float* y, lk_stream_t stream) {
-  if (!mv_format(fmt)) return LK_EUNSUPPORTED;
+  fmt = pair_norm(fmt);
+  if (!mv_format(gate_fmt(fmt)) || !mv_format(up_fmt(fmt))) return LK_EUNSUPPORTED;
   if (mode != LK_STORE && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
+  if (is_pair(fmt) && (mode == LK_STORE || fused)) return LK_EINVAL;   // a pair: separate gate and up tensors
   if (rows < 0 || rows % 64 || k <= 0 || n <= 0 || xrows <= 0 || ku <= 0 || n_experts <= 0 || n_experts > kMaxExperts)
     return LK_EINVAL;
   if (!act_ok(act)) return LK_EINVAL;
@@ -306,7 +336,7 @@ int lk_moe_grouped_gemm_ex(int fmt, int mode, int rows, int k, int n, int xrows,
   if (int rc = gemm_weight_check(fmt, k, w, w2)) return rc;
   if (!aligned(x16, 16) || !aligned(y, 16)) return LK_EALIGN;
   if (rows == 0) return LK_OK;
-  int64_t rb = lk_row_bytes(fmt, k);
+  int64_t rb = lk_row_bytes(gate_fmt(fmt), k);
   int64_t stride = rb * n * ((gu && fused) ? 2 : 1);
   const void* w2e = gu ? (fused ? nullptr : w2) : nullptr;
   ExpertEpi epi{bias, gu ? bias2 : nullptr, gu ? act : LK_ACT_SILU, alpha, limit};

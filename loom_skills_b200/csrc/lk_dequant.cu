@@ -3,6 +3,9 @@
 // lk_dequant   replaces the value helpers @g_<fmt>_values (quant_values.loom:18-91, 386-408; gen_llm.py:288-315,
 //              786-895) and the GEMM's f16 staging dequant16 (gen_gemm.py:281-532, moe_q4_0.py:11-38).
 // row scales   g_row_scale_f16 (gen_llm.py:1843-1912) and its fp8 twin (gen_mxfp4s.py:852-870, 887-938).
+// act * up     g_silu_mul (gen_llm.py:5717-5745) and its GEGLU form (gen_llm.py:5670-5716).
+#include <algorithm>
+
 #include "lk_common.cuh"
 #include "lk_formats.cuh"
 #include "lk_internal.h"
@@ -360,6 +363,30 @@ int row_scale_gather(int rows, int k, int ku, const int32_t* rowmap, const void*
                                   x8, s8, s) == cudaSuccess
              ? LK_OK
              : LK_ECUDA;
+}
+
+// f[t][c] = act(f[t][c]) * u[t][c] over [tokens][n] f32 rows (n % 4 == 0, 16-byte aligned), four values a thread
+__global__ void __launch_bounds__(256) k_act_mul(int64_t quads, int act, float4* __restrict__ f,
+                                                 const float4* __restrict__ u) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < quads; i += int64_t(gridDim.x) * blockDim.x) {
+    float4 g = f[i];
+    const float4 v = __ldg(u + i);
+    g.x = act_apply(act, g.x, v.x, 0.f, 0.f);
+    g.y = act_apply(act, g.y, v.y, 0.f, 0.f);
+    g.z = act_apply(act, g.z, v.z, 0.f, 0.f);
+    g.w = act_apply(act, g.w, v.w, 0.f, 0.f);
+    f[i] = g;
+  }
+}
+
+int act_mul(int tokens, int n, int act, float* f, const float* u, cudaStream_t s) {
+  const int64_t quads = int64_t(tokens) * n / 4;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = std::min<int64_t>((quads + 255) / 256, int64_t(sms) * 8);
+  k_act_mul<<<int(blocks), 256, 0, s>>>(quads, act, reinterpret_cast<float4*>(f), reinterpret_cast<const float4*>(u));
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
 }  // namespace lk

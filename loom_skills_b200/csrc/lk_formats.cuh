@@ -182,4 +182,33 @@ LK_DEV void group_f16(const uint8_t* b, int j, __half (&h)[32]) {
   }
 }
 
+// Gate and up weights in two formats (LK_FMT_PAIR(gate, up): the reference's "GATE+UP" kernels, gen_moe.py:537-552,
+// 1129-1141, and gen_gemm.py:535-545 fmt2). Kernels instantiated with kFmtPair read each weight's format at run time;
+// the switch is uniform across a warp (a warp's rows belong to one weight).
+constexpr int kFmtPair = -1;
+
+// the 32 values of group gi of a packed row (row: its first byte) in format `fmt`, chosen at run time; zeros for a
+// format without a decoder here
+LK_DEV void row_group_values(int fmt, const uint8_t* row, int gi, float (&v)[32]) {
+  switch (fmt) {
+#define LK_ROW_GROUP(F)                                                                              \
+  case F:                                                                                            \
+    group_values<F>(row + (gi / (fmt_qk(F) / 32)) * fmt_block_bytes(F), gi % (fmt_qk(F) / 32), v); \
+    return;
+    LK_ROW_GROUP(LK_Q4_0)
+    LK_ROW_GROUP(LK_IQ4_NL)
+    LK_ROW_GROUP(LK_Q4_K)
+    LK_ROW_GROUP(LK_Q5_0)
+    LK_ROW_GROUP(LK_Q8_0)
+    LK_ROW_GROUP(LK_Q5_K)
+    LK_ROW_GROUP(LK_Q6_K)
+    LK_ROW_GROUP(LK_IQ4_XS)
+    LK_ROW_GROUP(LK_Q3_K)
+    LK_ROW_GROUP(LK_MXFP4)
+#undef LK_ROW_GROUP
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = 0.f;
+}
+
 }  // namespace lk

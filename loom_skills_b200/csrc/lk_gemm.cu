@@ -57,12 +57,21 @@ struct GemmArgs {
   const uint8_t* wp;
   const uint8_t* w2p;
   int64_t rb;
+  // gate and up in two formats (kernels instantiated with kFmtPair): each weight's format, packed bytes of a
+  // 256-value chunk, and the up weight's row stride
+  int fmt, fmt2, cb, cb2;
+  int64_t rb2;
 };
 
 // packed bytes of one 256-value chunk of a row, and the bytes a window of it takes in shared memory: the chunk
 // copied from its 16-byte aligned start, so up to 15 bytes before and after it
 __host__ __device__ constexpr int chunk_bytes(int fmt) { return 256 / fmt_qk(fmt) * fmt_block_bytes(fmt); }
 __host__ __device__ constexpr int window_bytes(int fmt) { return (chunk_bytes(fmt) + 15 + 15) / 16 * 16; }
+// shared-memory bytes of one row's chunk: the TMA box form's 144, a window of the format's chunk, or for a format pair
+// the largest window of any format (Q8_0's)
+__host__ __device__ constexpr int row_slot_bytes(int fmt, bool win) {
+  return !win ? kChunkBytes : fmt == kFmtPair ? window_bytes(LK_Q8_0) : window_bytes(fmt);
+}
 
 // One 32-value group (j of the 256-value chunk) of any format into 4 swizzled 16-byte chunks of the B tile, with the
 // reference's staging (group_f16: one rounding, or the K-quants' f16 fma)
@@ -164,6 +173,22 @@ LK_DEV void dequant_group(const uint8_t* raw, int j, uint8_t* b_tile, int r, int
   }
 }
 
+// dequant_group / dequant_group_any of the format `fmt` read at run time (format pairs)
+LK_DEV void dequant_group_rt(int fmt, const uint8_t* chunk, int j, uint8_t* b_tile, int r, int c0) {
+  switch (fmt) {
+    case LK_Q4_0: dequant_group<LK_Q4_0>(chunk, j, b_tile, r, c0); return;
+    case LK_IQ4_NL: dequant_group<LK_IQ4_NL>(chunk, j, b_tile, r, c0); return;
+    case LK_Q4_K: dequant_group_any<LK_Q4_K>(chunk, j, b_tile, r, c0); return;
+    case LK_Q5_0: dequant_group_any<LK_Q5_0>(chunk, j, b_tile, r, c0); return;
+    case LK_Q8_0: dequant_group_any<LK_Q8_0>(chunk, j, b_tile, r, c0); return;
+    case LK_Q5_K: dequant_group_any<LK_Q5_K>(chunk, j, b_tile, r, c0); return;
+    case LK_Q6_K: dequant_group_any<LK_Q6_K>(chunk, j, b_tile, r, c0); return;
+    case LK_IQ4_XS: dequant_group_any<LK_IQ4_XS>(chunk, j, b_tile, r, c0); return;
+    case LK_Q3_K: dequant_group_any<LK_Q3_K>(chunk, j, b_tile, r, c0); return;
+    case LK_MXFP4: dequant_group_any<LK_MXFP4>(chunk, j, b_tile, r, c0); return;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Persistent dense GEMM: one CTA per SM walks the output tiles (tile t = blockIdx.x + i * gridDim.x; m fastest, so
 // the CTAs in flight share weight tiles in L2). The rings run on across tile boundaries, and the two TMEM
@@ -214,9 +239,19 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
   constexpr int kABytes = kTM * kBK * 2;
   constexpr int kBBytes = kRowsB * kBK * 2;
   constexpr int kCB = WIN ? chunk_bytes(FMT) : kChunkBytes;    // packed bytes of a 256-value chunk
-  constexpr int kRW = WIN ? window_bytes(FMT) : kChunkBytes;   // shared-memory bytes of one row's chunk
+  constexpr int kRW = row_slot_bytes(FMT, WIN);                // shared-memory bytes of one row's chunk
   constexpr int kRBytes = kRowsB * kRW;
   static_assert(WIN || chunk_bytes(FMT) == kChunkBytes, "the TMA box form streams 144-byte chunks");
+  static_assert(FMT != kFmtPair || (WIN && NW == 2), "a format pair is a gate/up kernel of the window form");
+  // window form: the packed source of row r's chunk of k stage ks (gate rows r < BN, up rows after them) and its length
+  auto win_src = [&](int r, int wrow, int w2row, int ks, uintptr_t& src, uint32_t& clen) {
+    const bool up = r >= BN;
+    const int cb = FMT == kFmtPair ? (up ? p.cb2 : p.cb) : kCB;
+    const int64_t rb = (FMT == kFmtPair && up) ? p.rb2 : p.rb;
+    const int64_t c0b = int64_t(ks >> 2) * cb;
+    clen = uint32_t(min(int64_t(cb), rb - c0b));
+    src = reinterpret_cast<uintptr_t>(up ? p.w2p : p.wp) + uintptr_t((int64_t(up ? w2row : wrow) + r % BN) * rb + c0b);
+  };
   constexpr int kSAp = SAP;
   constexpr int kSBp = SBP;
   constexpr uint32_t kAcc = MH * NW * BN;   // accumulator columns of one tile
@@ -326,15 +361,14 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
           if (WIN) {
             // every lane copies the chunk of rows lane, lane + 32, ... (those inside n): the 16-byte aligned window
             // around the row's chunk bytes. Lane 0 announces the stage's total bytes before any copy is issued.
-            const int64_t c0b = int64_t(ks >> 2) * kCB;
-            const uint32_t clen = uint32_t(min(int64_t(kCB), p.rb - c0b));
             uint32_t mine = 0;
 #pragma unroll
             for (int i = 0; i < kRowsB / 32; ++i) {
               const int r = lane + 32 * i, rl = r % BN;
               if (n0 + rl >= p.n) continue;
-              const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
-                                    uintptr_t((int64_t(r < BN ? wrow : w2row) + rl) * p.rb + c0b);
+              uintptr_t src;
+              uint32_t clen;
+              win_src(r, wrow, w2row, ks, src, clen);
               mine += uint32_t(((src + clen + 15) & ~uintptr_t(15)) - (src & ~uintptr_t(15)));
             }
             uint32_t total = mine;
@@ -346,8 +380,9 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
             for (int i = 0; i < kRowsB / 32; ++i) {
               const int r = lane + 32 * i, rl = r % BN;
               if (n0 + rl >= p.n) continue;
-              const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
-                                    uintptr_t((int64_t(r < BN ? wrow : w2row) + rl) * p.rb + c0b);
+              uintptr_t src;
+              uint32_t clen;
+              win_src(r, wrow, w2row, ks, src, clen);
               const uintptr_t a0 = src & ~uintptr_t(15);
               bulk_g2s(sR + sr * kRBytes + r * kRW, reinterpret_cast<const void*>(a0),
                        uint32_t(((src + clen + 15) & ~uintptr_t(15)) - a0), &full_r[sr]);
@@ -438,10 +473,12 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
           if (WIN) {
             // the row's chunk starts (src mod 16) bytes into its window; rows past n hold stale bytes whose
             // columns are never stored
-            const uintptr_t src = reinterpret_cast<uintptr_t>(r < BN ? p.wp : p.w2p) +
-                                  uintptr_t((int64_t(r < BN ? wrow : w2row) + r % BN) * p.rb + int64_t(ks >> 2) * kCB);
+            uintptr_t src;
+            uint32_t clen;
+            win_src(r, wrow, w2row, ks, src, clen);
             const uint8_t* chunk = sR + sr * kRBytes + r * kRW + (src & 15);
-            if (FMT == LK_Q4_0 || FMT == LK_IQ4_NL) dequant_group<FMT>(chunk, 2 * sub + h, bt, r, 4 * h);
+            if (FMT == kFmtPair) dequant_group_rt(r < BN ? p.fmt : p.fmt2, chunk, 2 * sub + h, bt, r, 4 * h);
+            else if (FMT == LK_Q4_0 || FMT == LK_IQ4_NL) dequant_group<FMT>(chunk, 2 * sub + h, bt, r, 4 * h);
             else dequant_group_any<FMT>(chunk, 2 * sub + h, bt, r, 4 * h);
           } else {
             dequant_group<FMT>(sR + sr * kRBytes + r * kChunkBytes, 2 * sub + h, bt, r, 4 * h);
@@ -639,7 +676,7 @@ template <int FMT, int BN, int NW, int MODE, int GROUP, int MH, int NBUF, int SA
 static int launch_gemm_p(const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
   constexpr int kRowsB = BN * NW;
   constexpr int kABytes = kBM * MH * kBK * 2, kBBytes = kRowsB * kBK * 2;
-  constexpr int kRBytes = kRowsB * (WIN ? window_bytes(FMT) : kChunkBytes);
+  constexpr int kRBytes = kRowsB * row_slot_bytes(FMT, WIN);
   constexpr int smem = 1024 + SAP * kABytes + SBP * kBBytes + SRP * kRBytes + kStgBytes +
                        (2 * (SAP + SBP + SRP) + 2 * NBUF) * 8 + 16 + 3 * kMaxExperts * 4;
   static_assert(smem <= 227 * 1024, "persistent GEMM CTA exceeds shared memory");
@@ -696,6 +733,13 @@ static int gemm_fmt_win(int mode, int group, bool short_m, const GemmMaps& m, co
   return launch_gemm_p<FMT, 128, 1, LK_STORE, kSorted, 1, 4, 4, 4, 2, true>(m, a, s);
 }
 
+// gate and up weights in two formats: the gate/up kernels of the window form, each weight decoded in its own format
+static int gemm_pair_win(int group, const GemmMaps& m, const GemmArgs& a, cudaStream_t s) {
+  if (group == kDense) return launch_gemm_p<kFmtPair, 64, 2, LK_SWIGLU, kDense, 1, 4, 4, 4, 2, true>(m, a, s);
+  if (group == kGather) return launch_gemm_p<kFmtPair, 64, 2, LK_SWIGLU, kGather, 1, 4, 4, 4, 2, true>(m, a, s);
+  return launch_gemm_p<kFmtPair, 64, 2, LK_SWIGLU, kSorted, 1, 4, 4, 4, 2, true>(m, a, s);
+}
+
 // K ranges for a dense store / acc GEMM of `tiles` output tiles and kp packed stages on `sms` persistent CTAs: the
 // count whose rounds x (stages per range + 1, + 1 more when split: the read-add-write of y) is least -- the + 1
 // stands for a tile's fill and epilogue -- with no empty range; the smallest such count on ties
@@ -735,10 +779,19 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   a.rows = rows;
   a.k = k;
   a.n = n;
-  const int64_t rb = lk_row_bytes(fmt, k);
+  // LK_FMT_PAIR(gate, up): the gate's format in the low 16 bits, the up weight's above (gate/up modes only)
+  const bool pair = (fmt >> 16) != 0;
+  a.fmt = fmt & 0xffff;
+  a.fmt2 = pair ? fmt >> 16 : a.fmt;
+  fmt = a.fmt;
+  const int64_t rb = lk_row_bytes(a.fmt, k);
+  a.rb2 = lk_row_bytes(a.fmt2, k);
+  a.cb = chunk_bytes(a.fmt);
+  a.cb2 = chunk_bytes(a.fmt2);
+  if (pair && mode != LK_SWIGLU && mode != LK_SWIGLU_SORTED) return LK_EINVAL;
   // rasterise so the larger operand is read once: n tiles of an m tile first when the activations outweigh the
   // weights (each A tile is then reused from L2 across the n tiles)
-  a.n_fast = int64_t(rows) * k * 2 > int64_t(n) * rb * (mode == LK_SWIGLU ? 2 : 1);
+  a.n_fast = int64_t(rows) * k * 2 > int64_t(n) * (mode == LK_SWIGLU ? rb + a.rb2 : rb);
   int group = kDense;
   int64_t wrows = n, w2rows = n;
   a.rows_per_expert = a.rows_per_expert2 = 0;
@@ -757,7 +810,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   }
   a.w2_row_offset = (mode != LK_STORE && mode != LK_ACC && !w2) ? int(w2_offset / rb) : 0;
   // the window producer: every format but the Q4 family's 144-byte chunks in 16-byte aligned rows
-  const bool win = !((fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL) && k % 256 == 0 &&
+  const bool win = pair || !((fmt == LK_Q4_0 || fmt == LK_Q4_K || fmt == LK_IQ4_NL) && k % 256 == 0 &&
                      (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(w2) & 15) == 0);
   a.wp = static_cast<const uint8_t*>(w);
   a.w2p = static_cast<const uint8_t*>(w2 ? w2 : w);
@@ -808,6 +861,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     a.kflags = base[dev] + s0;
     a.kepoch = ++epoch;
   }
+  if (pair) return gemm_pair_win(group, m, a, s);
   if (!win) {
     switch (fmt) {
       case LK_Q4_0: return gemm_fmt<LK_Q4_0>(mode, group, short_m, m, a, s);

@@ -44,7 +44,12 @@ struct MvArgs {
   int w2_row_offset;      // first row of the second weight inside an expert (fused gate/up: n; else 0)
   int swiglu;
   ExpertEpi epi;          // MoE mode: activation and per-expert biases (dense: SiLU, no biases)
+  // gate and up in two formats (mv_generic with an LK_FMT_PAIR id fills these): the formats and the up rows' stride
+  int fmt, fmt2;
+  int64_t row_bytes2;
 };
+// f = act(f) * u over [tokens][n] f32 (lk_silu_mul)
+int act_mul(int tokens, int n, int act, float* f, const float* u, cudaStream_t s);
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
 // every decodable format and any k of whole blocks (lk_mvg.cu): exact f32 values x f32 activations
 int mv_generic(int fmt, const MvArgs& a, cudaStream_t s);

@@ -63,11 +63,22 @@ LK_DEV void load_x32(const void* x, int64_t off, float (&xv)[32]) {
   }
 }
 
+// group gi of a packed row of weight wi (0 gate / only weight, 1 up): FMT's decoder, or for kFmtPair the weight's
+// own format read at run time
+template <int FMT>
+LK_DEV void mv_group(const MvArgs& a, int wi, const uint8_t* row, int gi, float (&v)[32]) {
+  if (FMT == kFmtPair) {
+    row_group_values(wi ? a.fmt2 : a.fmt, row, gi, v);
+  } else {
+    constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
+    group_values<FMT>(row + (gi / gpb) * fmt_block_bytes(FMT), gi % gpb, v);
+  }
+}
+
 template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
 __global__ void __launch_bounds__(kGWarps * 32) k_mvg(const MvArgs a) {
   constexpr int NW = SWIGLU ? 2 : 1;
-  constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
-  constexpr int bb = fmt_block_bytes(FMT);
+  const int64_t rb2 = FMT == kFmtPair ? a.row_bytes2 : a.row_bytes;   // the second weight's row stride
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = a.k / 32;
   int xrow0, ntok, yrow0, e = 0;
@@ -91,7 +102,7 @@ __global__ void __launch_bounds__(kGWarps * 32) k_mvg(const MvArgs a) {
   for (int rr = 0; rr < kGRowsPerWarp; ++rr) {
     const int row = blockIdx.x * kGRows + warp * kGRowsPerWarp + rr;
     if (row >= a.n) break;
-    const uint8_t* wr[2] = {a.w + (wbase + row) * a.row_bytes, w2 + (w2base + row) * a.row_bytes};
+    const uint8_t* wr[2] = {a.w + (wbase + row) * a.row_bytes, w2 + (w2base + row) * rb2};
     float acc[NW][TOK];
 #pragma unroll
     for (int wi = 0; wi < NW; ++wi)
@@ -101,7 +112,7 @@ __global__ void __launch_bounds__(kGWarps * 32) k_mvg(const MvArgs a) {
 #pragma unroll
       for (int wi = 0; wi < NW; ++wi) {
         float v[32];
-        group_values<FMT>(wr[wi] + (gi / gpb) * bb, gi % gpb, v);
+        mv_group<FMT>(a, wi, wr[wi], gi, v);
 #pragma unroll
         for (int t = 0; t < TOK; ++t) {
           if (t >= ntok) break;
@@ -152,10 +163,9 @@ __host__ __device__ inline int64_t mvs_window(int64_t rb) { return (kSRows * rb 
 
 template <int FMT, int XT, bool SWIGLU>
 __global__ void __launch_bounds__(kSThreads, 2) k_mvs(const MvArgs a, int nstages, int slot_bytes) {
-  constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
-  constexpr int bb = fmt_block_bytes(FMT);
   extern __shared__ __align__(128) uint8_t smem[];
   const int64_t win = mvs_window(a.row_bytes);
+  const int64_t rb2 = FMT == kFmtPair ? a.row_bytes2 : a.row_bytes;   // the second weight's row stride
   float* xs = reinterpret_cast<float*>(smem + kSStages * slot_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(xs + a.k);
   uint64_t* empty = full + kSStages;
@@ -171,10 +181,10 @@ __global__ void __launch_bounds__(kSThreads, 2) k_mvs(const MvArgs a, int nstage
   __syncthreads();
   const uint8_t* w2 = a.w2 ? a.w2 : a.w;
   // the window of rows r0 .. r0 + rows of weight `src` (rows start at row_off in it): [floor16(start), ceil16(end))
-  auto window = [&](const uint8_t* base, int64_t row0, int rows, uintptr_t& lo, uint32_t& bytes) {
-    const uintptr_t b = reinterpret_cast<uintptr_t>(base + row0 * a.row_bytes);
+  auto window = [&](const uint8_t* base, int64_t rb, int64_t row0, int rows, uintptr_t& lo, uint32_t& bytes) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(base + row0 * rb);
     lo = b & ~uintptr_t(15);
-    bytes = uint32_t(((b + uintptr_t(rows * a.row_bytes) + 15) & ~uintptr_t(15)) - lo);
+    bytes = uint32_t(((b + uintptr_t(rows * rb) + 15) & ~uintptr_t(15)) - lo);
   };
   if (warp == 0) {
     if (lane == 0) {
@@ -188,8 +198,8 @@ __global__ void __launch_bounds__(kSThreads, 2) k_mvs(const MvArgs a, int nstage
         const int r0 = st * kSRows, rows = min(kSRows, a.n - r0);
         uintptr_t lo, lo2 = 0;
         uint32_t bytes, bytes2 = 0;
-        window(a.w, r0, rows, lo, bytes);
-        if (SWIGLU) window(w2, int64_t(a.w2_row_offset) + r0, rows, lo2, bytes2);
+        window(a.w, a.row_bytes, r0, rows, lo, bytes);
+        if (SWIGLU) window(w2, rb2, int64_t(a.w2_row_offset) + r0, rows, lo2, bytes2);
         mbar_expect_tx(&full[s], bytes + bytes2);
         bulk_g2s(smem + s * slot_bytes, reinterpret_cast<const void*>(lo), bytes, &full[s]);
         if (SWIGLU) bulk_g2s(smem + s * slot_bytes + win, reinterpret_cast<const void*>(lo2), bytes2, &full[s]);
@@ -227,15 +237,15 @@ __global__ void __launch_bounds__(kSThreads, 2) k_mvs(const MvArgs a, int nstage
     float acc[2] = {0.f, 0.f};
     if (row < a.n) {
       const uintptr_t b0 = reinterpret_cast<uintptr_t>(a.w + int64_t(st) * kSRows * a.row_bytes);
-      const uintptr_t b1 = reinterpret_cast<uintptr_t>(w2 + (int64_t(a.w2_row_offset) + int64_t(st) * kSRows) * a.row_bytes);
+      const uintptr_t b1 = reinterpret_cast<uintptr_t>(w2 + (int64_t(a.w2_row_offset) + int64_t(st) * kSRows) * rb2);
       const uint8_t* rp[2] = {smem + s * slot_bytes + (b0 & 15) + int64_t(cw) * a.row_bytes,
-                              smem + s * slot_bytes + win + (b1 & 15) + int64_t(cw) * a.row_bytes};
+                              smem + s * slot_bytes + win + (b1 & 15) + int64_t(cw) * rb2};
 #pragma unroll
       for (int wi = 0; wi < (SWIGLU ? 2 : 1); ++wi) {
         float sacc = 0.f;
         for (int g = lane; g < groups; g += 32) {
           float v[32];
-          group_values<FMT>(rp[wi] + (g / gpb) * bb, g % gpb, v);
+          mv_group<FMT>(a, wi, rp[wi], g, v);
           const float4* xp = reinterpret_cast<const float4*>(xs + g * 32);
           float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -273,7 +283,8 @@ template <int FMT, int XT, bool SWIGLU>
 int launch_s(const MvArgs& a, cudaStream_t s, bool& done) {
   done = false;
   const int64_t win = mvs_window(a.row_bytes);
-  const int slot = int((win * (SWIGLU ? 2 : 1) + 127) / 128 * 128);
+  const int64_t win2 = SWIGLU ? mvs_window(FMT == kFmtPair ? a.row_bytes2 : a.row_bytes) : 0;
+  const int slot = int((win + win2 + 127) / 128 * 128);
   const int smem = kSStages * slot + a.k * 4 + 2 * kSStages * 8;
   if (smem > 110 * 1024 || a.k % 4) return LK_OK;   // two CTAs per SM, or not this form
   auto kern = k_mvs<FMT, XT, SWIGLU>;
@@ -340,6 +351,14 @@ int mvg_f(const MvArgs& a, cudaStream_t s) {
 }  // namespace
 
 int mv_generic(int fmt, const MvArgs& a, cudaStream_t s) {
+  if (fmt >> 16) {   // LK_FMT_PAIR(gate, up): one kernel reads each weight in its own format
+    MvArgs b = a;
+    b.fmt = fmt & 0xffff;
+    b.fmt2 = fmt >> 16;
+    b.row_bytes = lk_row_bytes(b.fmt, a.k);
+    b.row_bytes2 = lk_row_bytes(b.fmt2, a.k);
+    return mvg_f<kFmtPair>(b, s);
+  }
   switch (fmt) {
     case LK_Q4_0: return mvg_f<LK_Q4_0>(a, s);
     case LK_IQ4_NL: return mvg_f<LK_IQ4_NL>(a, s);

@@ -32,7 +32,16 @@ _DT = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}
 
 
 def _fmt(fmt):
-    return L.FMT_IDS[fmt] if isinstance(fmt, str) else int(fmt)
+    """A format name, "gate+up" (two formats: the reference's GATE+UP, e.g. "q4_k+q6_k"), or an id."""
+    if isinstance(fmt, str):
+        g, _, u = fmt.partition("+")
+        return L.fmt_pair(L.FMT_IDS[g], L.FMT_IDS[u]) if u else L.FMT_IDS[g]
+    return int(fmt)
+
+
+def _gate_fmt(fmt):
+    """The gate's format of a (possibly paired) format: the down projection's default."""
+    return fmt.partition("+")[0] if isinstance(fmt, str) else int(fmt) & 0xFFFF
 
 
 def _ptr(t):
@@ -133,6 +142,14 @@ def mv(fmt, w, x, n, k, w2=None, y=None, accumulate=False):
     L.check(L.load().lk_mv(_fmt(fmt), n, k, tokens, 1 if accumulate else 0, _ptr(x), _DT[x.dtype], _ptr(w), _ptr(w2),
                            _ptr(y), _stream()), "lk_mv")
     return y
+
+
+def silu_mul(f, u, act="silu"):
+    """g_silu_mul: f = act(f) * u in place over [tokens][n] f32 (act "silu" or "gelu"); returns f."""
+    _cuda(f, u)
+    tokens, n = f.shape
+    L.check(L.load().lk_silu_mul(tokens, n, _ptr(f), _ptr(u.contiguous()), _act(act), _stream()), "lk_silu_mul")
+    return f
 
 
 def gemm(fmt, mode, x16, scales, w, n, w2=None, y=None):
@@ -347,7 +364,8 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     x [tokens][h] (bf16 / f32), logits [tokens][n_experts]; w_gu: per expert 2f rows (gate then up) of h values --
     or, with w_up given (GGUF's separate ffn_gate_exps / ffn_up_exps), per expert f gate rows, and w_up its f up rows;
     w_dn: per expert h rows of f values, in fmt_down when it differs from fmt (GGUF quants often keep ffn_down_exps in
-    a wider format); biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
+    a wider format); fmt "gate+up" (e.g. "q4_k+q6_k", with w_up): gate and up experts in two formats, the down in
+    fmt_down or the gate's; biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
     switches to the GEMMs at 64 tokens (gen_llm.py:6107); here from 192 assignments (tokens * ku), where they
     measured faster on configs[2] shapes (top-8 of 128 experts: matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 /
     312 us). `prefill` forces either path."""
@@ -362,7 +380,8 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     if not prefill:
         act_ = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=fused, w2=w_up,
                              bias=b_gate, bias2=b_up, **ep)
-        ys = moe_expert_mv(fmt_down or fmt, "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts, bias=b_down)
+        ys = moe_expert_mv(fmt_down or _gate_fmt(fmt), "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts,
+                           bias=b_down)
         return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
     ti, rm, pos = moe_bucket(ids, n_experts)
     # the token rows row-scaled straight into bucket order: gate/up then reads plain tiles (no row gather)
@@ -370,7 +389,7 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     act_ = moe_grouped_gemm(fmt, "swiglu_sorted", ti, rm, x16, sc, w_gu, f, ku, n_experts, fused=fused, w2=w_up,
                             bias=b_gate, bias2=b_up, **ep)
     a16, asc = row_scale_f16(act_)
-    ys = moe_grouped_gemm(fmt_down or fmt, "store", ti, rm, a16, asc, w_dn, h, ku, n_experts, bias=b_down)
+    ys = moe_grouped_gemm(fmt_down or _gate_fmt(fmt), "store", ti, rm, a16, asc, w_dn, h, ku, n_experts, bias=b_down)
     return moe_combine_sorted(ys, pos, wts, y=y, accumulate=acc, sg=sg)
 
 

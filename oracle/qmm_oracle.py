@@ -451,29 +451,31 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
-def mv_ref(fmt, w, x, n, k, w2=None, y_old=None):
+def mv_ref(fmt, w, x, n, k, w2=None, y_old=None, fmt2=None):
     """Decode matvec (gen_llm.py:1159-1378; reference make_kernel_tests.py:231-238):
-    y[t, n] (+)= sum_k x[t, k] W[n, k]; with w2: y = silu(x.Wg) * (x.Wu)."""
+    y[t, n] (+)= sum_k x[t, k] W[n, k]; with w2: y = silu(x.Wg) * (x.Wu), w2 in fmt2 when the up weight's format
+    differs (gen_moe.py:537-552 "GATE+UP"; gen_llm.py:6280-6283 two projections + g_silu_mul)."""
     W = dequant(fmt, w, k).reshape(n, k).astype(np.float64)
     x = np.asarray(x, np.float64).reshape(-1, k)
     y = x @ W.T
     if w2 is not None:
-        U = dequant(fmt, w2, k).reshape(n, k).astype(np.float64)
+        U = dequant(fmt2 or fmt, w2, k).reshape(n, k).astype(np.float64)
         y = silu(y) * (x @ U.T)
     if y_old is not None:
         y = y + np.asarray(y_old, np.float64)
     return y
 
 
-def gemm_ref(fmt, w, x16, scales, n, k, mode="store", w2=None, y_old=None):
+def gemm_ref(fmt, w, x16, scales, n, k, mode="store", w2=None, y_old=None, fmt2=None):
     """Prefill GEMM (gen_gemm.py:535-704; reference make_kernel_tests.py:1860-1876):
-    Y = (X16 . W^T) * inv[row]; mode acc adds y_old; swiglu: silu(G) * U."""
+    Y = (X16 . W^T) * inv[row]; mode acc adds y_old; swiglu: silu(G) * U, w2 in fmt2 when it differs (gen_gemm.py:535-545
+    fmt2)."""
     W = dequant(fmt, w, k).reshape(n, k).astype(np.float64)
     x = np.asarray(x16, np.float64).reshape(-1, k)
     inv = np.asarray(scales, np.float64)[:, 1:2]
     y = (x @ W.T) * inv
     if mode == "swiglu":
-        U = dequant(fmt, w2, k).reshape(n, k).astype(np.float64)
+        U = dequant(fmt2 or fmt, w2, k).reshape(n, k).astype(np.float64)
         y = silu(y) * ((x @ U.T) * inv)
     elif mode == "acc":
         y = y + np.asarray(y_old, np.float64)
@@ -660,11 +662,12 @@ def check_bucket(ids, n_experts, max_tiles, tile_info, rowmap, pos, live=None, t
 
 
 def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts, act=ACT_SILU, alpha=1.702, limit=7.0, b_gate=None,
-                b_up=None, b_down=None, dsc=None, y0=None, sg=None):
+                b_up=None, b_down=None, dsc=None, y0=None, sg=None, w_up=None, fmt_up=None, fmt_down=None):
     """The routed expert FFN in float64 (kbench moe_q4_0/gen_bench.py:185-248; make_kernel_tests.py:3196-3215
     experts_ref and :3268-3271 chain): y[t] = sg[t] y0[t] + sum_k wts[t,k] dsc[e] (Wd[e] act(Wg[e] x[t] + bg[e],
     Wu[e] x[t] + bu[e]) + bd[e]), e = ids[t,k]; w_gu[e] = gate rows then up rows (packed blocks of `fmt`, or float
-    weights when fmt is None); biases [E][f] / [E][h] f32."""
+    weights when fmt is None); biases [E][f] / [E][h] f32. w_up: separate up experts [E] (f rows each, in fmt_up when it
+    differs: gen_moe.py:537-552 "GATE+UP"), w_gu then holds the f gate rows; w_dn in fmt_down when given."""
     x = np.asarray(x, np.float64)
     t, ku = ids.shape
     y = np.zeros((t, h), np.float64)
@@ -674,9 +677,13 @@ def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts, act=ACT_SILU, alp
     for e in np.unique(ids):
         if fmt is None:   # float weights [E][2f][h] / [E][h][f] (e.g. dequant_mxfp4_planar's output)
             gu, dn = np.asarray(w_gu[e], np.float64), np.asarray(w_dn[e], np.float64)
+        elif w_up is not None:
+            gu = np.concatenate([dequant(fmt, w_gu[e], h).reshape(f, h), dequant(fmt_up or fmt, w_up[e], h).reshape(f, h)])
+            gu = gu.astype(np.float64)
+            dn = dequant(fmt_down or fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
         else:
             gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
-            dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
+            dn = dequant(fmt_down or fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
         sel = np.nonzero(ids == e)
         pair = x[sel[0]] @ gu.T
         g, u = pair[:, :f], pair[:, f:]

@@ -8,6 +8,7 @@ import pytest
 from loom_skills_b200 import _lib as L
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PAIR = L.fmt_pair(L.Q4_K, L.Q6_K)
 
 
 def declared_symbols():
@@ -46,6 +47,17 @@ def test_host_only_entry_points():
     lambda lib: lib.lk_moe_route(4, 0, 300, 8, 1, 1, 1.0, 16, None, L.F32, None, 16, 16, None),  # > 256 experts
     lambda lib: lib.lk_moe_bucket(64, 8, 128, 4, None, 16, 16, 16, 16, None),          # max_tiles too small
     lambda lib: lib.lk_dequant(L.Q4_K, 16, None, 100, 16, L.F32, None),                 # not a block multiple
+    # gate/up in two formats (LK_FMT_PAIR): gate/up entry points and modes only, separate tensors, both formats' blocks
+    lambda lib: lib.lk_gemm(PAIR, L.STORE, 128, 256, 256, 16, 16, 16, 16, 16, None),     # a pair is swiglu only
+    lambda lib: lib.lk_mv(PAIR, 16, 256, 1, 0, 16, L.F32, 16, None, 32, None),           # a pair needs w2
+    lambda lib: lib.lk_mv(L.fmt_pair(L.Q4_0, L.Q6_K), 16, 704, 1, 0, 16, L.F32, 16, 16, 32, None),  # k % 256 (Q6_K)
+    lambda lib: lib.lk_mv(L.fmt_pair(L.Q4_K, L.MXFP4S), 16, 256, 1, 0, 16, L.F32, 16, 16, 32, None),  # no MXFP4S half
+    lambda lib: lib.lk_moe_expert_mv(PAIR, 1, 16, 256, 4, 2, 8, 0, 16, 16, L.F32, 16, None, 16, None),  # down mode
+    lambda lib: lib.lk_moe_expert_mv(PAIR, 0, 16, 256, 4, 2, 8, 1, 16, 16, L.F32, 16, 16, 16, None),  # fused
+    lambda lib: lib.lk_moe_grouped_gemm(PAIR, L.SWIGLU_SORTED, 64, 256, 16, 64, 2, 8, 1, 16, 16, 16, 16, 16, 16, 16,
+                                        None),                                               # fused
+    lambda lib: lib.lk_silu_mul(2, 6, 16, 16, L.ACT_SILU, None),                        # n % 4
+    lambda lib: lib.lk_silu_mul(2, 8, 16, 16, L.ACT_SWIGLU_OAI, None),                  # silu or gelu only
 ])
 def test_validation_rejects_before_any_launch(call):
     assert call(L.load()) < 0
