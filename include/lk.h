@@ -29,12 +29,12 @@ extern "C" {
 typedef struct CUstream_st* lk_stream_t;   /* == cudaStream_t */
 
 /* weight formats (ggml type ids); LK_MXFP4S = split planes (nibble plane + E8M0 scale plane), formats.py:11-14.
- * The Q4 family (Q4_0, Q4_K, IQ4_NL) and MXFP4S run on every kernel; Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS and the
- * ggml 17-byte MXFP4 blocks (the reference's remaining formats, formats.py:5-17) on lk_dequant, the decode matvecs
- * (lk_mv, lk_moe_expert_mv) and the prefill GEMMs (lk_gemm, lk_moe_grouped_gemm). */
+ * The Q4 family (Q4_0, Q4_K, IQ4_NL) and MXFP4S run on every kernel; Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS, IQ3_S
+ * and the ggml 17-byte MXFP4 blocks (the reference's remaining formats, formats.py:5-17) on lk_dequant, the decode
+ * matvecs (lk_mv, lk_moe_expert_mv) and the prefill GEMMs (lk_gemm, lk_moe_grouped_gemm). */
 enum {
   LK_Q4_0 = 2, LK_Q5_0 = 6, LK_Q8_0 = 8, LK_Q3_K = 11, LK_Q4_K = 12, LK_Q5_K = 13, LK_Q6_K = 14, LK_IQ4_NL = 20,
-  LK_IQ4_XS = 23, LK_MXFP4 = 39, LK_MXFP4S = 1039
+  LK_IQ3_S = 21, LK_IQ4_XS = 23, LK_MXFP4 = 39, LK_MXFP4S = 1039
 };
 /* Gate and up weights in two formats (Q4_K_M's Q4_K gate and Q6_K up; unsloth's mixed quants): the reference's
  * "GATE+UP" format (gen_moe.py:537-552 expert_mv, :1129-1141 grouped_gemm; gen_gemm.py:535-545 gemm fmt2 and

@@ -7,14 +7,15 @@ LIB_PATH = os.path.join(HERE, "liblk.so")
 
 # formats / dtypes / modes (include/lk.h)
 Q4_0, Q4_K, IQ4_NL, MXFP4, MXFP4S = 2, 12, 20, 39, 1039
-Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS = 6, 8, 11, 13, 14, 23
+Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS, IQ3_S = 6, 8, 11, 13, 14, 23, 21
 F32, F16, BF16, E4M3 = 0, 1, 30, 1000
 STORE, ACC, SWIGLU, SWIGLU_SORTED = 0, 1, 2, 3
 ORDER_PAIRS, ORDER_SPLIT16 = 0, 1
 ACT_SILU, ACT_GELU, ACT_SWIGLU_OAI = 0, 1, 2
 ACT_IDS = {"silu": ACT_SILU, "gelu": ACT_GELU, "swiglu_oai": ACT_SWIGLU_OAI}
 FMT_IDS = {"q4_0": Q4_0, "q4_k": Q4_K, "iq4_nl": IQ4_NL, "mxfp4": MXFP4, "mxfp4s": MXFP4S, "q5_0": Q5_0,
-           "q8_0": Q8_0, "q3_k": Q3_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq4_xs": IQ4_XS}
+           "q8_0": Q8_0, "q3_k": Q3_K, "q5_k": Q5_K, "q6_k": Q6_K, "iq4_xs": IQ4_XS,
+           "iq3_s": IQ3_S}
 
 
 def fmt_pair(gate, up):

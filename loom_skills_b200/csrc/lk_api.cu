@@ -12,6 +12,7 @@ static bool act_ok(int act) { return act == LK_ACT_SILU || act == LK_ACT_GELU ||
 // formats the decode matvecs and GEMMs take: the Q4 family on the tuned kernels, the rest on the generic ones
 static bool mv_format(int fmt) {
   return q4_family(fmt) || fmt == LK_Q5_0 || fmt == LK_Q8_0 || fmt == LK_Q3_K || fmt == LK_Q5_K || fmt == LK_Q6_K ||
+         fmt == LK_IQ3_S ||
          fmt == LK_IQ4_XS || fmt == LK_MXFP4;
 }
 // the tuned Q4 kernels stream whole 256-value chunks by TMA: k % 256, 16-byte aligned rows

@@ -79,6 +79,7 @@ int dequant(int fmt, const void* w, const void* ws, int64_t n, void* out, int ou
     case LK_Q6_K: return launch_dequant<LK_Q6_K>(w, ws, groups, out, f16, s);
     case LK_IQ4_XS: return launch_dequant<LK_IQ4_XS>(w, ws, groups, out, f16, s);
     case LK_Q3_K: return launch_dequant<LK_Q3_K>(w, ws, groups, out, f16, s);
+    case LK_IQ3_S: return launch_dequant<LK_IQ3_S>(w, ws, groups, out, f16, s);
   }
   return LK_EINVAL;
 }

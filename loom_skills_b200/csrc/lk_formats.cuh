@@ -13,17 +13,22 @@
 //   Q6_K  210 B / 256  ql[128], qh[64], int8 sc[16], d         (d sc) (q - 32)          (sub-blocks of 16)
 //   IQ4_XS 136 B / 256 d, u16 scales_h, 4 B scales_l, qs[128]  d (ls - 32) kvalue[q]    (groups of 32)
 //   Q3_K  110 B / 256  hmask[32], qs[64], 12 B scales, d       (d (ls - 32)) (q2 - 4 !hbit) (sub-blocks of 16)
+//   IQ3_S 110 B / 256  d, qs[64], qh[8], signs[32], scales[4]  (d (1 + 2 s)) (+-grid[qs | qh bit << 8][i])  (groups of 32)
 //
 // Every value is an exact f32 product (the integer factors are at most 24 significant bits together), except the
 // K-quants' d sc q - dmin m, which rounds once as gguf's does. Byte loads only: blocks of these sizes start at any
 // even (MXFP4: any) byte offset.
 #pragma once
 #include "lk_common.cuh"
+// kIq3sGrid[512]: the IQ3_S codebook, one u32 of four magnitudes per entry (written by build.py at build time)
+#include "lk_iq3s_grid.inc"
 
 namespace lk {
 
 __host__ __device__ constexpr int fmt_qk(int fmt) {
-  return (fmt == LK_Q4_K || fmt == LK_Q5_K || fmt == LK_Q6_K || fmt == LK_IQ4_XS || fmt == LK_Q3_K) ? 256 : 32;
+  return (fmt == LK_Q4_K || fmt == LK_Q5_K || fmt == LK_Q6_K || fmt == LK_IQ4_XS || fmt == LK_Q3_K || fmt == LK_IQ3_S)
+             ? 256
+             : 32;
 }
 __host__ __device__ constexpr int fmt_block_bytes(int fmt) {
   return fmt == LK_Q4_0 || fmt == LK_IQ4_NL ? 18
@@ -35,6 +40,7 @@ __host__ __device__ constexpr int fmt_block_bytes(int fmt) {
          : fmt == LK_Q6_K                  ? 210
          : fmt == LK_IQ4_XS                ? 136
          : fmt == LK_Q3_K                  ? 110
+         : fmt == LK_IQ3_S                 ? 110
                                            : 0;
 }
 
@@ -146,6 +152,25 @@ LK_DEV void group_codes(const uint8_t* b, int j, GroupCodes& g) {
     g.a_lo = a[0];
     g.a_hi = a[1];
     g.c_lo = g.c_hi = 0.f;
+  } else if (FMT == LK_IQ3_S) {
+    // group j: 8 codebook entries of 4 magnitudes, entry c = qs[8j + c] | (bit c of qh[j]) << 8; the sign of value i
+    // is bit i % 8 of signs[4j + i / 8]; the scale d (1 + 2 s), s the j-th nibble of scales[4]
+    const float d = f16_at(b);
+    const uint8_t* qs = b + 2 + 8 * j;
+    const int qh = b[66 + j];
+    const uint8_t* sg = b + 74 + 4 * j;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t e = __ldg(&kIq3sGrid[qs[c] | (((qh >> c) & 1) << 8)]);
+      const int sb = sg[c >> 1] >> (4 * (c & 1));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = int((e >> (8 * i)) & 0xffu);
+        g.q[4 * c + i] = ((sb >> i) & 1) ? -m : m;
+      }
+    }
+    g.a_lo = g.a_hi = d * float(1 + 2 * ((b[106 + (j >> 1)] >> (4 * (j & 1))) & 15));
+    g.c_lo = g.c_hi = 0.f;
   }
 }
 
@@ -204,6 +229,7 @@ LK_DEV void row_group_values(int fmt, const uint8_t* row, int gi, float (&v)[32]
     LK_ROW_GROUP(LK_Q6_K)
     LK_ROW_GROUP(LK_IQ4_XS)
     LK_ROW_GROUP(LK_Q3_K)
+    LK_ROW_GROUP(LK_IQ3_S)
     LK_ROW_GROUP(LK_MXFP4)
 #undef LK_ROW_GROUP
   }

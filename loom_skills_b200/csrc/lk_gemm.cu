@@ -185,6 +185,7 @@ LK_DEV void dequant_group_rt(int fmt, const uint8_t* chunk, int j, uint8_t* b_ti
     case LK_Q6_K: dequant_group_any<LK_Q6_K>(chunk, j, b_tile, r, c0); return;
     case LK_IQ4_XS: dequant_group_any<LK_IQ4_XS>(chunk, j, b_tile, r, c0); return;
     case LK_Q3_K: dequant_group_any<LK_Q3_K>(chunk, j, b_tile, r, c0); return;
+    case LK_IQ3_S: dequant_group_any<LK_IQ3_S>(chunk, j, b_tile, r, c0); return;
     case LK_MXFP4: dequant_group_any<LK_MXFP4>(chunk, j, b_tile, r, c0); return;
   }
 }
@@ -879,6 +880,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
     case LK_Q6_K: return gemm_fmt_win<LK_Q6_K>(mode, group, short_m, m, a, s);
     case LK_IQ4_XS: return gemm_fmt_win<LK_IQ4_XS>(mode, group, short_m, m, a, s);
     case LK_Q3_K: return gemm_fmt_win<LK_Q3_K>(mode, group, short_m, m, a, s);
+    case LK_IQ3_S: return gemm_fmt_win<LK_IQ3_S>(mode, group, short_m, m, a, s);
     case LK_MXFP4: return gemm_fmt_win<LK_MXFP4>(mode, group, short_m, m, a, s);
   }
   return LK_EUNSUPPORTED;

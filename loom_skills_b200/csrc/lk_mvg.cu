@@ -369,6 +369,7 @@ int mv_generic(int fmt, const MvArgs& a, cudaStream_t s) {
     case LK_Q6_K: return mvg_f<LK_Q6_K>(a, s);
     case LK_IQ4_XS: return mvg_f<LK_IQ4_XS>(a, s);
     case LK_Q3_K: return mvg_f<LK_Q3_K>(a, s);
+    case LK_IQ3_S: return mvg_f<LK_IQ3_S>(a, s);
     case LK_MXFP4: return mvg_f<LK_MXFP4>(a, s);
   }
   return LK_EUNSUPPORTED;

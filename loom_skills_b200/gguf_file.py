@@ -30,9 +30,9 @@ import numpy as np
 
 # ggml type id -> (values per block, bytes per block); the formats the reference decodes (formats.py:5-17)
 GGML_BLOCKS = {0: (1, 4), 1: (1, 2), 30: (1, 2), 2: (32, 18), 6: (32, 22), 8: (32, 34), 11: (256, 110),
-               12: (256, 144), 13: (256, 176), 14: (256, 210), 20: (32, 18), 23: (256, 136), 39: (32, 17)}
+               12: (256, 144), 13: (256, 176), 14: (256, 210), 20: (32, 18), 21: (256, 110), 23: (256, 136), 39: (32, 17)}
 GGML_NAMES = {0: "f32", 1: "f16", 30: "bf16", 2: "q4_0", 6: "q5_0", 8: "q8_0", 11: "q3_k", 12: "q4_k", 13: "q5_k",
-              14: "q6_k", 20: "iq4_nl", 23: "iq4_xs", 39: "mxfp4"}
+              14: "q6_k", 20: "iq4_nl", 21: "iq3_s", 23: "iq4_xs", 39: "mxfp4"}
 
 # metadata value types (GGUF specification)
 _SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}

@@ -10,6 +10,7 @@ It restates, in numpy, the numerics of loom-fun/loom-skills for this path (paths
   - Q4_0     ``skills/loom-port-llm/starter/quant_values.loom:386-408`` (@g_q4_0_values), ``formats.py:8``
   - Q4_K     ``skills/loom-port-llm/starter/gen_llm.py:234-315`` (@g_k_scale_minimum, @g_k_metadata, @g_q4_k_values)
   - IQ4_NL   ``skills/loom-port-llm/starter/quant_values.loom:18-91``
+  - IQ3_S    ``skills/loom-port-llm/starter/quant_values.loom:5-6, 243-384`` (@g_iq3s_grid, @g_iq3_s_values)
   - MXFP4    ``skills/loom-port-llm/starter/gen_llm.py:786-895`` (ggml 17-byte blocks, split16 order) and
              ``skills/loom-port-llm/starter/st_tensors.py:26-35`` (split planes, pairs order)
   The Q4_K / IQ4_NL / MXFP4 arithmetic is the third-party ``gguf`` package's (gguf-py 0.19.0, installed unpinned by
@@ -34,11 +35,19 @@ import numpy as np
 
 # values per block / bytes per block (formats.py:5-17) and gguf.GGMLQuantizationType ids
 QK = {"q4_0": 32, "q4_k": 256, "iq4_nl": 32, "mxfp4": 32, "q8_0": 32, "q5_0": 32, "q5_k": 256, "q6_k": 256,
-      "iq4_xs": 256, "q3_k": 256}
+      "iq4_xs": 256, "q3_k": 256, "iq3_s": 256}
 BLOCK_BYTES = {"q4_0": 18, "q4_k": 144, "iq4_nl": 18, "mxfp4": 17, "q8_0": 34, "q5_0": 22, "q5_k": 176, "q6_k": 210,
-               "iq4_xs": 136, "q3_k": 110}
+               "iq4_xs": 136, "q3_k": 110, "iq3_s": 110}
 GGML_TYPE = {"q4_0": 2, "q4_k": 12, "iq4_nl": 20, "mxfp4": 39, "q8_0": 8, "q5_0": 6, "q5_k": 13, "q6_k": 14,
-             "iq4_xs": 23, "q3_k": 11}
+             "iq4_xs": 23, "q3_k": 11, "iq3_s": 21}
+
+
+def iq3s_grid():
+    """The IQ3_S codebook [512][4] of odd magnitudes 1..15 (ggml's iq3s_grid; the reference embeds the same table,
+    quant_values.loom:5-6): gguf-py 0.19.0's IQ3_S grid, the format's pinned definition."""
+    from gguf.quants import IQ3_S
+    IQ3_S.init_grid()
+    return IQ3_S.grid.reshape(512, 4).astype(np.int64)
 IQ4_KVALUES = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int64)
 E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float64)
 MXFP4_F8_SHIFT = 8                      # gen_mxfp4s.py:29
@@ -271,6 +280,17 @@ def dequant(fmt, raw, k):
         hb = (hmask.reshape(-1, 1, 1, 32) >> np.arange(8, dtype=np.uint8).reshape(1, 1, 8, 1)).reshape(-1, 16, 16) & 1
         q = ql.astype(np.int64) - ((hb ^ 1).astype(np.int64) << 2)
         v = (dl * q.astype(np.float32)).reshape(-1, 256)
+    elif fmt == "iq3_s":     # gguf IQ3_S: d, qs[64], qh[8], signs[32], scales[4] (quant_values.loom:243-384)
+        d = _f16(b[:, 0:2]).astype(np.float32)
+        qs, qh, sg, sc = b[:, 2:66], b[:, 66:74], b[:, 74:106], b[:, 106:110]
+        s = (sc.reshape(-1, 4, 1) >> np.array([0, 4], np.uint8).reshape(1, 1, 2)).reshape(-1, 8) & 15
+        db = d[:, None] * (1 + 2 * s.astype(np.int64)).astype(np.float32)              # [B, 8], exact
+        hi = (qh.reshape(-1, 8, 1) >> np.arange(8, dtype=np.uint8).reshape(1, 1, 8)).reshape(-1, 64) & 1
+        idx = qs.astype(np.int64) | (hi.astype(np.int64) << 8)                          # [B, 64] codebook entries
+        mag = iq3s_grid()[idx].reshape(-1, 256)
+        neg = (sg.reshape(-1, 32, 1) >> np.arange(8, dtype=np.uint8).reshape(1, 1, 8)).reshape(-1, 256) & 1
+        q = np.where(neg == 1, -mag, mag).astype(np.float32).reshape(-1, 8, 32)
+        v = (db[:, :, None] * q).reshape(-1, 256)
     elif fmt == "mxfp4":
         e = b[:, 0].astype(np.int64)
         # ggml_e8m0_to_fp32_half: 2^(e-128) (e >= 2), subnormal encodings for e < 2; doubled e2m1 table
@@ -286,7 +306,7 @@ def dequant_f16(fmt, raw, k):
     """The f16 weights the prefill GEMM stages (one rounding of the exact value):
     Q4_0 f16(d*(q-8)) (moe_q4_0.py:36-38); IQ4_NL f16(d*kvalue) (gen_gemm.py:228-231);
     Q4_K fma_f16(q, f16(d*sc), f16(-dmin*m)) (gen_gemm.py:526-532)."""
-    if fmt in ("q4_0", "iq4_nl", "mxfp4", "mxfp4_planar", "q8_0", "q5_0", "iq4_xs", "q3_k"):
+    if fmt in ("q4_0", "iq4_nl", "mxfp4", "mxfp4_planar", "q8_0", "q5_0", "iq4_xs", "q3_k", "iq3_s"):
         # one rounding of the exact value (gen_gemm.py:352-367 for Q8_0; the @g_<fmt>_values helpers + fptrunc)
         return dequant(fmt, raw, k).astype(np.float64).astype(np.float16)
     if fmt in ("q5_k", "q6_k"):
@@ -448,7 +468,8 @@ def e5m2_values(b):
 # products (float64, as make_kernel_tests.py builds its references)
 # ------------------------------------------------------------------------------------------------------------------
 def silu(x):
-    return x / (1.0 + np.exp(-x))
+    with np.errstate(over="ignore"):   # exp(-x) = inf for very negative x: silu -> -0, as in f32
+        return x / (1.0 + np.exp(-x))
 
 
 def mv_ref(fmt, w, x, n, k, w2=None, y_old=None, fmt2=None):

@@ -298,14 +298,14 @@ def main_moe(ref):
 
 def main_formats(ref):
     """golden_formats.npz: the reference's remaining GGUF formats (formats.py:5-17: Q5_0, Q8_0, Q3_K, Q5_K, Q6_K,
-    IQ4_XS) dequantised by gguf 0.19.0 (the reference's numpy path, make_kernel_tests.py:45-47) on seeded random
+    IQ4_XS, IQ3_S) dequantised by gguf 0.19.0 (the reference's numpy path, make_kernel_tests.py:45-47) on seeded random
     blocks with finite f16 scales, and small float64 products of those values (make_kernel_tests.py:231-238)."""
     from gguf import GGMLQuantizationType as T
     from gguf.quants import dequantize
     out = {}
     rng = np.random.default_rng(77)
     spec = {"q5_0": (22, 32, [0]), "q8_0": (34, 32, [0]), "q3_k": (110, 256, [108]), "q5_k": (176, 256, [0, 2]),
-            "q6_k": (210, 256, [208]), "iq4_xs": (136, 256, [0])}
+            "q6_k": (210, 256, [208]), "iq4_xs": (136, 256, [0]), "iq3_s": (110, 256, [0])}
     for name, (bb, qk, offs) in spec.items():
         nb = 64 if qk == 256 else 512
         b = rng.integers(0, 256, (nb, bb), dtype=np.uint8)

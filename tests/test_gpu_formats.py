@@ -1,4 +1,4 @@
-"""GPU parity of the reference's remaining GGUF formats (formats.py:5-17: Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS, and
+"""GPU parity of the reference's remaining GGUF formats (formats.py:5-17: Q5_0, Q8_0, Q3_K, Q5_K, Q6_K, IQ4_XS, IQ3_S, and
 ggml 17-byte MXFP4 on the decode path) and of rows that are not a multiple of 256 values (k % 32 only):
 
 * lk_dequant against gguf 0.19.0's values bit for bit (tests/golden/golden_formats.npz) and the GEMM's f16 staging
@@ -19,8 +19,8 @@ pytestmark = pytest.mark.gpu
 from oracle import qmm_oracle as O  # noqa: E402
 
 TOL = 1e-3
-FORMATS = ["q5_0", "q8_0", "q3_k", "q5_k", "q6_k", "iq4_xs"]
-SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q3_k": [108], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0],
+FORMATS = ["q5_0", "q8_0", "q3_k", "q5_k", "q6_k", "iq4_xs", "iq3_s"]
+SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q3_k": [108], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0], "iq3_s": [0],
               "q4_0": [0], "iq4_nl": [0], "q4_k": [0, 2]}
 
 

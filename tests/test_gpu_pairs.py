@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 from oracle import qmm_oracle as O  # noqa: E402
 
 TOL = 1e-3
-SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q3_k": [108], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0],
+SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q3_k": [108], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0], "iq3_s": [0],
               "q4_0": [0], "iq4_nl": [0], "q4_k": [0, 2]}
 
 
@@ -51,7 +51,7 @@ def blocks(fmt, rows, k, seed, lo=1e-3, hi=2e-2):
 
 
 PAIRS = [("q4_k", "q6_k"), ("q6_k", "q4_k"), ("q4_0", "q8_0"), ("iq4_xs", "q5_k"), ("q5_0", "iq4_nl"),
-         ("q3_k", "q4_0")]
+         ("q3_k", "q4_0"), ("iq3_s", "q4_k")]
 
 
 @pytest.mark.parametrize("fg,fu", PAIRS)
@@ -69,14 +69,16 @@ def test_mv_pair(ops, fg, fu, tokens, xdt):
 
 @pytest.mark.parametrize("fg,fu,k", [("q4_0", "q8_0", 704), ("q4_k", "q6_k", 768)])
 def test_mv_pair_is_two_projections_and_silu_mul(ops, fg, fu, k):
-    # the pair kernel against the reference's dense fallback: gate and up projections, then g_silu_mul; and accumulate
+    # the pair kernel against the reference's dense fallback: gate and up projections, then g_silu_mul; and accumulate.
+    # A Q4_K projection alone runs the tuned kernel, which sums in another order: agreement to f32 rounding
     n = 96
     w, w2 = dev(blocks(fg, n, k, 5)), dev(blocks(fu, n, k, 6))
     x = dev(np.random.default_rng(7).standard_normal((2, k)).astype(np.float32))
     g, u = ops.mv(fg, w, x, n, k), ops.mv(fu, w2, x, n, k)
     two = host(ops.silu_mul(g, u))
     one = host(ops.mv(f"{fg}+{fu}", w, x, n, k, w2=w2))
-    np.testing.assert_allclose(one, two, rtol=1e-6, atol=1e-7)
+    assert O.rel_l2(one, two) < 1e-6
+    np.testing.assert_allclose(one, two, rtol=1e-4, atol=1e-4)
     y0 = np.random.default_rng(8).standard_normal((2, n)).astype(np.float32)
     ya = dev(y0)
     ops.mv(f"{fg}+{fu}", w, x, n, k, w2=w2, y=ya, accumulate=True)
@@ -124,7 +126,7 @@ def staged_swiglu(fg, fu, w, w2, x16, sc, n, k):
 
 
 @pytest.mark.parametrize("fg,fu", [("q4_k", "q6_k"), ("q6_k", "q4_k"), ("q4_0", "q5_k"), ("q8_0", "iq4_xs"),
-                                   ("q3_k", "q5_0")])
+                                   ("q3_k", "q5_0"), ("q5_k", "iq3_s")])
 @pytest.mark.parametrize("rows,n,k", [(200, 272, 1024), (64, 128, 2048)])
 def test_gemm_pair(ops, fg, fu, rows, n, k):
     w, w2 = blocks(fg, n, k, 41), blocks(fu, n, k, 42)

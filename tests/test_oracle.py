@@ -310,7 +310,7 @@ def gfmt():
         return {k: z[k] for k in z.files}
 
 
-@pytest.mark.parametrize("fmt", ["q5_0", "q8_0", "q3_k", "q5_k", "q6_k", "iq4_xs"])
+@pytest.mark.parametrize("fmt", ["q5_0", "q8_0", "q3_k", "q5_k", "q6_k", "iq4_xs", "iq3_s"])
 def test_remaining_formats_match_gguf(gfmt, fmt):
     # the oracle's restatement of gguf 0.19.0's dequantize_blocks, bit for bit on the golden blocks
     raw = gfmt[f"{fmt}_raw"]
