@@ -225,13 +225,16 @@ def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
     gen = torch.Generator(device=wstack[0]["o"].device)
     gen.manual_seed(7)
     q40 = synth_blocks(torch, wstack[0]["o"].device, 4096, 4096, "q4_0", gen)
+    # Q4_K_M keeps ffn_down (half the layers) and attn_v in Q6_K: the down projection's shape in Q6_K
+    q6d = torch.from_numpy(synth_q6k(np.random.default_rng(8), 4096, 12288)).to(wstack[0]["o"].device)
     x16 = xs[4096].to(torch.float16)
     forms = [("q|k|v", wstack[0]["qkv"], "q4_k", 4096, [4096, 1024, 1024], "int8"),
              ("o", wstack[0]["o"], "q4_k", 4096, [4096], "int8"),
              ("gate_up", wstack[0]["gate_up"], "q4_k", 4096, [24576], "int8"),
              ("down", wstack[0]["down"], "q4_k", 12288, [4096], "int8"),
              ("q4_0 4096x4096 fp16 (configs[0])", q40, "q4_0", 4096, [4096], "fp16"),
-             ("q4_0 4096x4096 int8 (configs[0])", q40, "q4_0", 4096, [4096], "int8")]
+             ("q4_0 4096x4096 int8 (configs[0])", q40, "q4_0", 4096, [4096], "int8"),
+             ("down q6_k (Q4_K_M)", q6d, "q6_k", 12288, [4096], "int8")]
     chain = 32
     out = {}
     xq = {k: ops.quant_q8(xs[k]) for k in xs}
@@ -264,8 +267,10 @@ def bench_gemv_forms(args, torch, wstack, xs, pk, time_steps):
         out[label] = {"format": fmt, "activations": acts, "us_per_launch": round(us, 2),
                       "weight_mb": round(nbytes / 1e6, 1), "weight_gbs": round(gbs, 1),
                       "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies,
-                      "kernel": "k_mv (lk_mv.cu)" if acts == "fp16" else "k_mv_q8_rows on lk_quant_q8 codes"}
-        if acts == "int8":
+                      "kernel": "k_mv (lk_mv.cu)" if acts == "fp16" else
+                                "k_mv_q8_rows on lk_quant_q8 codes" if fmt in ("q4_0", "q4_k") else
+                                "k_mvq8g on lk_quant_q8 codes (lk_mvq8g.cu)"}
+        if acts == "int8" and fmt in ("q4_0", "q4_k"):
             out[label]["fused_us_per_launch"] = round(timed(True), 2)   # the row quantised in the prologue
         del ws
     return out
@@ -858,7 +863,8 @@ def run_profile_case(args):
     gate_up matvec quantising its bf16 row in the prologue), mvg_q6k (the generic-format matvec, Q6_K K=4096
     N=4096, f32 x), gemm_q6k (the window-producer GEMM, Q6_K M=2048 K=4096 N=4096), moeq8 (the int8 decode MoE layer
     of configs[2] at one token: E=128 top-8, H=2048, F=768, Q4_0), mvp_gate_up / gemmp_gate_up (a Q4_K gate and Q6_K
-    up pair, K=4096 N=12288: the one-token matvec on bf16 x, and the swiglu GEMM at M=2048)."""
+    up pair, K=4096 N=12288: the one-token matvec on bf16 x, and the swiglu GEMM at M=2048), mvq8_q6k_down (the int8
+    matvec over Q6_K, K=12288 N=4096)."""
     import torch
 
     from loom_skills_b200 import ops
@@ -907,6 +913,12 @@ def run_profile_case(args):
         y = torch.empty(1, h, device=dev)
         act = torch.empty(ku, f, device=dev)
         fn = lambda: ops.moe_ffn_decode_q8("q4_0", x, lg, wgu, wdn, h, f, E, ku, y=y, act_buf=act)   # noqa: E731
+    elif case == "mvq8_q6k_down":
+        k, n = 12288, 4096
+        w = torch.from_numpy(synth_q6k(rng, n, k)).to(dev)
+        xq = ops.quant_q8(torch.randn(1, k, device=dev))
+        y = torch.empty(1, n, device=dev)
+        fn = lambda: ops.mv_q8("q6_k", w, xq, n, k, 1, y=y)   # noqa: E731
     elif case.startswith("mv"):
         k, n = (12288, 4096) if case == "mv_down" else (4096, 24576)
         t = 8 if case == "mv8_gate_up" else 1

@@ -118,10 +118,14 @@ int lk_silu_mul(int tokens, int n, float* f, const float* u, int act, lk_stream_
  *   q = round(x/d) (halves away from zero; 0 for an all-zero group); xq = codes int8 [rows][k], then at byte rows*k
  *   the meta [rows][k/32][2] f32 = (d rounded to f16, sum of the group's codes). x_dtype LK_F32 or LK_BF16, k % 32 == 0.
  *   xq holds rows*k + rows*(k/32)*8 bytes.
- * lk_mv_q8: g_mv_{fmt}_k{K}[_t{TG}]_q8 (gen_llm.py:1159-1378 with @g_q4_0_icodes / @g_q4_k_icodes, :521-680),
- *   launch(%n, %tokens, %accumulate, %xq, %w, %y): y[t][n] (+)= sum_k dequant(W)[n][k] * xcode[t][k] * d[t][k/32],
- *   the weight codes contracted with the activation codes in integer arithmetic per 32-group. xq: lk_quant_q8's
- *   output for `tokens` rows. Formats Q4_0 and Q4_K (IQ4_NL: LK_EUNSUPPORTED); k % 256 == 0.
+ * lk_mv_q8: g_mv_{fmt}_k{K}[_t{TG}]_q8 (gen_llm.py:1159-1378 with the @g_<fmt>_icodes helpers, :521-680, 898-1000,
+ *   and the dot of iq_dot, :1017-1050), launch(%n, %tokens, %accumulate, %xq, %w, %y):
+ *   y[t][n] (+)= sum_k dequant(W)[n][k] * xcode[t][k] * d[t][k/32], the weight codes contracted with the activation
+ *   codes in integer arithmetic per 32-group, then scaled in f32 as the reference does per format. xq: lk_quant_q8's
+ *   output for `tokens` rows. Formats: Q4_0 and Q4_K (k % 256 == 0, w 16-byte aligned) on the tuned kernels; Q8_0,
+ *   Q5_0, Q5_K, Q6_K (the reference's ICODES set, formats.py:22-31) and IQ4_NL, IQ4_XS (its IQ4_Q8 choice) with k a
+ *   whole number of blocks and of 32-value groups, w 2-byte aligned. Other decodable formats (Q3_K, IQ3_S, MXFP4):
+ *   LK_EUNSUPPORTED, as the reference has no integer codes for them.
  */
 int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_stream_t stream);
 int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,

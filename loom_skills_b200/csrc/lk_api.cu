@@ -70,29 +70,47 @@ int lk_quant_q8(int rows, int k, const void* x, int x_dtype, uint8_t* xq, lk_str
   return quant_q8(rows, k, x, x_dtype, xq, (cudaStream_t)stream);
 }
 
+// the int8-activation matvec's formats: the Q4 pair on the tuned kernels (k % 256, 16-byte aligned rows), the other
+// integer-code formats on k_mvq8g (k a whole number of blocks and of 32-value groups, 2-byte aligned blocks)
+static int mv_q8_check(int fmt, int k, const void* w) {
+  const bool gen = mv_q8_generic_format(fmt);
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K && !gen) return mv_format(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (k <= 0 || k % (gen ? fmt_qk(fmt) : 256) || k % 32) return LK_EINVAL;
+  if (w && !aligned(w, gen ? 2 : 16)) return LK_EALIGN;
+  return LK_OK;
+}
+
 int lk_mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
              lk_stream_t stream) {
-  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return q4_family(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
-  if (n <= 0 || k <= 0 || tokens < 0 || k % 256) return LK_EINVAL;
+  if (int rc = mv_q8_check(fmt, k, nullptr)) return rc;
+  if (n <= 0 || tokens < 0) return LK_EINVAL;
   if (tokens == 0) return LK_OK;
   if (!xq || !w || !y) return LK_EINVAL;
-  if (!aligned(xq, 16) || !aligned(w, 16)) return LK_EALIGN;
+  if (int rc = mv_q8_check(fmt, k, w)) return rc;
+  if (!aligned(xq, 16)) return LK_EALIGN;
+  if (mv_q8_generic_format(fmt)) return mv_q8_generic(fmt, n, k, tokens, accumulate, xq, w, y, (cudaStream_t)stream);
   return mv_q8(fmt, n, k, tokens, accumulate, xq, w, y, (cudaStream_t)stream);
 }
 
 int lk_mv_q8_multi(int fmt, int nseg, const int* n, const void* const* w, float* const* y, int k, int tokens,
                    int accumulate, const uint8_t* xq, lk_stream_t stream) {
-  if (fmt != LK_Q4_0 && fmt != LK_Q4_K) return q4_family(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (int rc = mv_q8_check(fmt, k, nullptr)) return rc;
   if (nseg <= 0 || nseg > 4 || !n || !w || !y) return LK_EINVAL;
-  if (k <= 0 || tokens < 0 || k % 256) return LK_EINVAL;
+  if (tokens < 0) return LK_EINVAL;
   for (int g = 0; g < nseg; ++g) {
     if (n[g] <= 0) return LK_EINVAL;
     if (tokens > 0 && (!w[g] || !y[g])) return LK_EINVAL;
-    if (tokens > 0 && !aligned(w[g], 16)) return LK_EALIGN;
+    if (tokens > 0)
+      if (int rc = mv_q8_check(fmt, k, w[g])) return rc;
   }
   if (tokens == 0) return LK_OK;
   if (!xq) return LK_EINVAL;
   if (!aligned(xq, 16)) return LK_EALIGN;
+  if (mv_q8_generic_format(fmt)) {   // one launch per segment
+    for (int g = 0; g < nseg; ++g)
+      if (int rc = mv_q8_generic(fmt, n[g], k, tokens, accumulate, xq, w[g], y[g], (cudaStream_t)stream)) return rc;
+    return LK_OK;
+  }
   return mv_q8_multi(fmt, nseg, n, w, y, k, tokens, accumulate, xq, (cudaStream_t)stream);
 }
 

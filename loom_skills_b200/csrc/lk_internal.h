@@ -102,6 +102,10 @@ int mv_q8(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, 
           cudaStream_t s);
 int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int tokens,
                 int accumulate, const uint8_t* xq, cudaStream_t s);
+// the other formats with integer weight codes (Q8_0, Q5_0, Q5_K, Q6_K, IQ4_NL, IQ4_XS; lk_mvq8g.cu)
+bool mv_q8_generic_format(int fmt);
+int mv_q8_generic(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+                  cudaStream_t s);
 // one token: the activation row quantised inside the row-streaming matvec (no xq buffer); LK_EUNSUPPORTED off its
 // shapes (Q4_0 / Q4_K, k % 4096 == 0, k <= 12288)
 int mv_q8_fused(int fmt, int nseg, const int* ns, const void* const* ws, float* const* ys, int k, int accumulate,

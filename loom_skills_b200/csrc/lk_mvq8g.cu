@@ -1,0 +1,333 @@
+// Decode matvec on int8 activations for the formats with integer weight codes beyond the Q4 pair: the reference's
+// ICODES set (formats.py:22-31: Q8_0, Q5_0, Q5_K, Q6_K by default; IQ4_NL and IQ4_XS under its IQ4_Q8 choice), each
+// format's @g_<fmt>_icodes helper (gen_llm.py:521-680, 898-1000) with the dot of iq_dot (gen_llm.py:1017-1050):
+//
+//   per 32-value group, the weight codes (int8) . the activation codes (lk_quant_q8's) as an exact integer dot, then
+//     ONE_SCALE (Q8_0, IQ4_NL, IQ4_XS)   (scale * d_x) * dot
+//     with a minimum (Q5_0, Q5_K)        (dot * scale - sum_x * minimum) * d_x
+//     Q6_K (a scale per 16 values)        fma(dot_hi, scale_hi, dot_lo * scale_lo) * d_x
+//
+// k_mvq8g: a producer warp streams stages of (8 rows) x (a chunk of 2048 values) into a 4-slot shared-memory ring --
+// one bulk copy per row of the 16-byte-aligned window around the row's chunk bytes, since these blocks (34, 22, 176,
+// 210, 18, 136 bytes) start at any even offset -- and 8 consumer warps take one row each: lane l decodes the groups
+// l, l + 32, ... of the chunk from shared memory (2-byte loads), reads the activation codes of up to 8 tokens from
+// global memory (the whole row of codes is shared by every warp: it stays in L1), and runs 8 dp4a per group and token.
+// A CTA walks whole row blocks (all chunks of 8 rows) so each row's sum stays in registers; the first stage is
+// requested before griddepcontrol.wait (the weights never depend on the previous kernel).
+#include <mutex>
+
+#include "lk_common.cuh"
+#include "lk_formats.cuh"
+#include "lk_internal.h"
+
+namespace lk {
+namespace {
+
+constexpr int kGRows = 8;                    // rows per stage = consumer warps
+constexpr int kGThreads = 32 * (1 + kGRows);
+constexpr int kGStages = 4;
+constexpr int kGChunk = 2048;                // values of a row per stage
+
+LK_DEV void gq_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LK_DEV void gq_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// a little-endian word from a 2-byte aligned address in shared memory
+LK_DEV uint32_t ld32_2a(const uint8_t* p) {
+  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+  return uint32_t(q[0]) | (uint32_t(q[1]) << 16);
+}
+LK_DEV float f16_2a(const uint8_t* p) { return h2f(*reinterpret_cast<const uint16_t*>(p)); }
+
+// The int8 codes of one 32-value group (word i = values 4i..4i+3, one per byte) and its factors: sc the scale, mn
+// the minimum (Q5_0, Q5_K) or the second 16 values' scale (Q6_K)
+struct ICodes {
+  uint32_t w[8];
+  float sc, mn;
+};
+
+enum { kOneScale = 0, kMinimum = 1, kTwoScales = 2 };
+__host__ __device__ constexpr int icode_kind(int fmt) {
+  return fmt == LK_Q6_K ? kTwoScales : (fmt == LK_Q5_0 || fmt == LK_Q5_K) ? kMinimum : kOneScale;
+}
+
+// group j of the block at b (@g_<fmt>_icodes)
+template <int FMT>
+LK_DEV void group_icodes(const uint8_t* b, int j, ICodes& o) {
+  if (FMT == LK_Q8_0) {   // gen_llm.py:523-534: int8 codes, scale d
+    o.sc = f16_2a(b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o.w[i] = ld32_2a(b + 2 + 4 * i);
+    o.mn = 0.f;
+  } else if (FMT == LK_Q5_0) {   // gen_llm.py:943-985: nibble | bit i of qh << 4 (0..31), minimum 16 d
+    const float d = f16_2a(b);
+    const uint32_t qh = ld32_2a(b + 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t q = ld32_2a(b + 6 + 4 * (i & 3));
+      const uint32_t hb = (qh >> (4 * i)) & 15u;
+      o.w[i] = ((i < 4 ? q : q >> 4) & 0x0F0F0F0Fu) |
+               ((hb & 1u) << 4) | ((hb & 2u) << 11) | ((hb & 4u) << 18) | ((hb & 8u) << 25);
+    }
+    o.sc = d;
+    o.mn = 16.0f * d;
+  } else if (FMT == LK_Q5_K) {   // gen_llm.py:579-615: Q4_K's nibbles | bit j of qh[l] << 4, scale d sc, minimum dmin m
+    uint32_t sc, m;
+    q4k_scale_min_w(ld32_2a(b + 4), ld32_2a(b + 8), ld32_2a(b + 12), j, sc, m);
+    o.sc = f16_2a(b) * float(sc);
+    o.mn = f16_2a(b + 2) * float(m);
+    const uint8_t* qs = b + 48 + 32 * (j >> 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      o.w[i] = ((ld32_2a(qs + 4 * i) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
+               (((ld32_2a(b + 16 + 4 * i) >> j) & 0x01010101u) << 4);
+  } else if (FMT == LK_Q6_K) {   // gen_llm.py:617-680: signed (q - 32), d sc of each 16 values
+    const int half = j >> 2, jj = j & 3;
+    const uint8_t* ql = b + 64 * half + 32 * (jj & 1);
+    const uint8_t* qh = b + 128 + 32 * half;
+    const uint8_t* sc = b + 192 + 8 * half + 2 * jj;
+    const float d = f16_2a(b + 208);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t c = ((ld32_2a(ql + 4 * i) >> (4 * (jj >> 1))) & 0x0F0F0F0Fu) |
+                         (((ld32_2a(qh + 4 * i) >> (2 * jj)) & 0x03030303u) << 4);   // 0..63 per byte
+      // c - 32 per byte: flip bit 5; bytes below 32 also get bits 6 and 7 (their two's complement)
+      o.w[i] = (c ^ 0x20202020u) | ((~c & 0x20202020u) * 7u);
+    }
+    o.sc = float(int8_t(sc[0])) * d;
+    o.mn = float(int8_t(sc[1])) * d;
+  } else if (FMT == LK_IQ4_NL || FMT == LK_IQ4_XS) {   // gen_llm.py:898-940: codebook values, one scale
+    const uint8_t* qs;
+    if (FMT == LK_IQ4_NL) {
+      o.sc = f16_2a(b);
+      qs = b + 2;
+    } else {
+      const int sh = *reinterpret_cast<const uint16_t*>(b + 2);
+      const int ls = ((b[4 + (j >> 1)] >> (4 * (j & 1))) & 15) | (((sh >> (2 * j)) & 3) << 4);
+      o.sc = f16_2a(b) * float(ls - 32);
+      qs = b + 8 + 16 * j;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t q = ld32_2a(qs + 4 * (i & 3));
+      o.w[i] = iq4_lookup4((i < 4 ? q : q >> 4) & 0x0F0F0F0Fu) ^ 0x80808080u;   // biased table bytes -> int8
+    }
+    o.mn = 0.f;
+  }
+}
+
+// the group's contribution for one token: x codes xw[8], the activation group's f16-rounded d and code sum
+template <int FMT>
+LK_DEV float group_dot(const ICodes& c, const uint32_t (&xw)[8], float dx, float xsum) {
+  if (icode_kind(FMT) == kTwoScales) {
+    int lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      lo = __dp4a(int(c.w[i]), int(xw[i]), lo);
+      hi = __dp4a(int(c.w[4 + i]), int(xw[4 + i]), hi);
+    }
+    return fmaf(__int2float_rn(hi), c.mn, __int2float_rn(lo) * c.sc) * dx;
+  }
+  int s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = __dp4a(int(c.w[i]), int(xw[i]), s);
+  if (icode_kind(FMT) == kOneScale) return (c.sc * dx) * __int2float_rn(s);
+  return (__int2float_rn(s) * c.sc - xsum * c.mn) * dx;
+}
+
+struct GqArgs {
+  const uint8_t* w;
+  const uint8_t* codes;   // [tokens][k] int8
+  const float* meta;      // [tokens][k/32][2]
+  float* y;
+  int n, k, ntok, accumulate;
+  int64_t rb;             // packed bytes of a row
+  int cb;                 // packed bytes of a full chunk (kGChunk values)
+  int nkc;                // chunks per row
+  int row_slot;           // shared-memory bytes of one row's window
+};
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
+  constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
+  constexpr int bb = fmt_block_bytes(FMT);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int slot = kGRows * a.row_slot;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * slot);
+  uint64_t* empty = full + kGStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+  const int nblk = (a.n + kGRows - 1) / kGRows;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGRows);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // row r's chunk kc: its packed source and length
+  auto src_of = [&](int r, int kc, uintptr_t& src, uint32_t& len) {
+    const int64_t c0 = int64_t(kc) * a.cb;
+    len = uint32_t(min(int64_t(a.cb), a.rb - c0));
+    src = reinterpret_cast<uintptr_t>(a.w + int64_t(r) * a.rb + c0);
+  };
+  if (warp == 0) {
+    gq_launch();
+    int i = 0;
+    for (int blk = cta; blk < nblk; blk += G) {
+      for (int kc = 0; kc < a.nkc; ++kc, ++i) {
+        if (i == 1) gq_wait();   // the first stage goes out before the previous grid ends
+        const int s = i % kGStages;
+        if (i >= kGStages && !mbar_wait(&empty[s], ((i / kGStages) - 1) & 1)) atomicOr(&g_status, 1u);
+        const int r = blk * kGRows + lane;
+        uintptr_t src = 0;
+        uint32_t len = 0, bytes = 0;
+        if (lane < kGRows && r < a.n) {
+          src_of(r, kc, src, len);
+          bytes = uint32_t(((src + len + 15) & ~uintptr_t(15)) - (src & ~uintptr_t(15)));
+        }
+        uint32_t total = bytes;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xFFFFFFFFu, total, o);
+        if (lane == 0) mbar_expect_tx(&full[s], total);
+        __syncwarp();
+        if (bytes)
+          bulk_g2s(smem + s * slot + lane * a.row_slot, reinterpret_cast<const void*>(src & ~uintptr_t(15)), bytes,
+                   &full[s]);
+        __syncwarp();
+      }
+    }
+    return;
+  }
+  gq_wait();   // the activation codes come from the previous kernel
+  const int cw = warp - 1, groups = a.k / 32;
+  int i = 0;
+  for (int blk = cta; blk < nblk; blk += G) {
+    const int r = blk * kGRows + cw;
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    for (int kc = 0; kc < a.nkc; ++kc, ++i) {
+      const int s = i % kGStages;
+      if (!mbar_wait(&full[s], (i / kGStages) & 1)) atomicOr(&g_status, 1u);
+      if (r < a.n) {
+        uintptr_t src;
+        uint32_t len;
+        src_of(r, kc, src, len);
+        const uint8_t* chunk = smem + s * slot + cw * a.row_slot + (src & 15);
+        const int gc = min(kGChunk, a.k - kc * kGChunk) / 32, g0 = kc * (kGChunk / 32);
+        for (int g = lane; g < gc; g += 32) {
+          ICodes c;
+          group_icodes<FMT>(chunk + (g / gpb) * bb, g % gpb, c);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t >= a.ntok) break;
+            const uint4* xp = reinterpret_cast<const uint4*>(a.codes + int64_t(t) * a.k + int64_t(g0 + g) * 32);
+            const uint4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+            const float2 m = __ldg(reinterpret_cast<const float2*>(a.meta) + int64_t(t) * groups + g0 + g);
+            const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            acc[t] += group_dot<FMT>(c, xw, m.x, m.y);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xFFFFFFFFu, acc[t], o);
+    if (lane == 0 && r < a.n) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t >= a.ntok) break;
+        float* yp = a.y + int64_t(t) * a.n + r;
+        *yp = a.accumulate ? *yp + acc[t] : acc[t];
+      }
+    }
+  }
+}
+
+template <int FMT, int NT>
+int launch_gq(const GqArgs& a, cudaStream_t s) {
+  const int smem = kGStages * kGRows * a.row_slot + 2 * kGStages * 8;
+  auto kern = k_mvq8g<FMT, NT>;
+  static int configured[32] = {};   // the largest shared-memory size set per device
+  static std::mutex mu;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 32) return LK_EUNSUPPORTED;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[dev] < smem) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+      configured[dev] = smem;
+    }
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGThreads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int nblk = (a.n + kGRows - 1) / kGRows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(min(nblk, per_sm * sms), 1, 1);
+  cfg.blockDim = dim3(kGThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
+template <int FMT>
+int mvq8g_f(GqArgs a, int tokens, cudaStream_t s) {
+  a.rb = lk_row_bytes(FMT, a.k);
+  a.cb = kGChunk / fmt_qk(FMT) * fmt_block_bytes(FMT);
+  a.nkc = (a.k + kGChunk - 1) / kGChunk;
+  a.row_slot = (a.cb + 15 + 15) / 16 * 16;
+  float* y = a.y;
+  const uint8_t* codes = a.codes;
+  const float* meta = a.meta;
+  for (int t0 = 0; t0 < tokens; t0 += 8) {   // token tiles of 8 (one launch each; one token: the NT = 1 kernel)
+    a.ntok = min(8, tokens - t0);
+    a.y = y + int64_t(t0) * a.n;
+    a.codes = codes + int64_t(t0) * a.k;
+    a.meta = meta + int64_t(t0) * (a.k / 32) * 2;
+    const int rc = a.ntok == 1 ? launch_gq<FMT, 1>(a, s) : launch_gq<FMT, 8>(a, s);
+    if (rc != LK_OK) return rc;
+  }
+  return LK_OK;
+}
+
+}  // namespace
+
+bool mv_q8_generic_format(int fmt) {
+  return fmt == LK_Q8_0 || fmt == LK_Q5_0 || fmt == LK_Q5_K || fmt == LK_Q6_K || fmt == LK_IQ4_NL ||
+         fmt == LK_IQ4_XS;
+}
+
+int mv_q8_generic(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
+                  cudaStream_t s) {
+  GqArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
+  a.codes = xq;
+  a.meta = reinterpret_cast<const float*>(xq + int64_t(tokens) * k);
+  a.y = y;
+  a.n = n;
+  a.k = k;
+  a.accumulate = accumulate;
+  switch (fmt) {
+    case LK_Q8_0: return mvq8g_f<LK_Q8_0>(a, tokens, s);
+    case LK_Q5_0: return mvq8g_f<LK_Q5_0>(a, tokens, s);
+    case LK_Q5_K: return mvq8g_f<LK_Q5_K>(a, tokens, s);
+    case LK_Q6_K: return mvq8g_f<LK_Q6_K>(a, tokens, s);
+    case LK_IQ4_NL: return mvq8g_f<LK_IQ4_NL>(a, tokens, s);
+    case LK_IQ4_XS: return mvq8g_f<LK_IQ4_XS>(a, tokens, s);
+  }
+  return LK_EUNSUPPORTED;
+}
+
+}  // namespace lk

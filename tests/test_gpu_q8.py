@@ -85,11 +85,80 @@ class TestMvQ8:
         assert O.rel_l2(host(ops.mv_q8(fmt, dev(w), xq, n, k, x.shape[0])), golden[f"mv_{fmt}_y"]) < 2e-2
 
     def test_unsupported_and_empty(self, ops):
+        # no integer codes for Q3_K / IQ3_S / MXFP4 (formats.py:22-31)
         xq = torch.zeros(256 + 8 * 8, dtype=torch.uint8, device="cuda")
         w = torch.zeros(4, 144, dtype=torch.uint8, device="cuda")
-        with pytest.raises(ops.L.LkError):
-            ops.mv_q8("iq4_nl", w, xq, 4, 256, 1)
+        for fmt in ("q3_k", "iq3_s", "mxfp4"):
+            with pytest.raises(ops.L.LkError):
+                ops.mv_q8(fmt, w, xq, 4, 256, 1)
         assert ops.mv_q8("q4_k", w, xq, 4, 256, 0).shape == (0, 4)
+
+
+SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0], "iq4_nl": [0]}
+GENERIC = ["q8_0", "q5_0", "q5_k", "q6_k", "iq4_nl", "iq4_xs"]
+
+
+def blocks(fmt, rows, k, seed, lo=1e-3, hi=2e-2):
+    """Random blocks of `fmt` (every code and sub-block scale) with finite f16 scales of both signs."""
+    rng = np.random.default_rng(seed)
+    nb = rows * k // O.QK[fmt]
+    b = rng.integers(0, 256, (nb, O.BLOCK_BYTES[fmt]), dtype=np.uint8)
+    for o in SCALE_OFFS[fmt]:
+        b[:, o:o + 2] = (rng.uniform(lo, hi, nb) * rng.choice([-1, 1], nb)).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    return b.reshape(rows, -1)
+
+
+class TestMvQ8Generic:
+    """k_mvq8g: the reference's other integer-code formats (formats.py:22-31 ICODES, @g_<fmt>_icodes
+    gen_llm.py:521-680, 898-1000) on lk_quant_q8 codes: exact integer dots, f32 scaling per format."""
+
+    @pytest.mark.parametrize("fmt", GENERIC)
+    @pytest.mark.parametrize("n,k,tokens", [(200, 2048, 1), (4096, 4096, 1), (130, 12288, 1), (300, 4096, 3),
+                                            (96, 1024, 9), (1000, 2560, 8)])
+    def test_vs_oracle(self, ops, fmt, n, k, tokens):
+        rng = np.random.default_rng(n + k + tokens)
+        w = blocks(fmt, n, k, n + tokens)
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        xq = ops.quant_q8(dev(x))
+        codes, meta = ops.q8_views(xq, tokens, k)
+        y = host(ops.mv_q8(fmt, dev(w), xq, n, k, tokens))
+        ref = O.mv_ref(fmt, w, O.dequant_q8(host(codes), host(meta)), n, k)
+        assert O.rel_l2(y, ref) < 1e-5, O.rel_l2(y, ref)
+        assert ops.device_status() == 0
+
+    @pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "iq4_nl"])
+    def test_rows_of_32_value_blocks_and_accumulate(self, ops, fmt):
+        # k = 704 (22 blocks of 32: the kbench down projection's width) at an odd 2-byte offset of 16 (w + 2 bytes)
+        n, k, tokens = 77, 704, 2
+        w = blocks(fmt, n, k, 5)
+        buf = torch.zeros(w.size + 16, dtype=torch.uint8, device="cuda")
+        buf[2:2 + w.size] = dev(w.reshape(-1))
+        x = np.random.default_rng(6).standard_normal((tokens, k)).astype(np.float32)
+        xq = ops.quant_q8(dev(x))
+        codes, meta = ops.q8_views(xq, tokens, k)
+        y0 = np.random.default_rng(7).standard_normal((tokens, n)).astype(np.float32)
+        y = host(ops.mv_q8(fmt, buf[2:2 + w.size], xq, n, k, tokens, y=dev(y0), accumulate=True))
+        ref = O.mv_ref(fmt, w, O.dequant_q8(host(codes), host(meta)), n, k, y_old=y0)
+        assert O.rel_l2(y, ref) < 1e-5
+
+    @pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q5_k", "q6_k"])
+    def test_golden_within_the_q8_tolerance(self, ops, fmt):
+        # gguf 0.19.0's float64 product of the golden blocks (tests/golden/golden_formats.npz): the int8 activations
+        # stay within the reference's q8 tolerance of it
+        import os
+        with np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_formats.npz")) as z:
+            w, x, yref = z[f"mv_{fmt}_w"], z[f"mv_{fmt}_x"], z[f"mv_{fmt}_y"]
+        xq = ops.quant_q8(dev(x))
+        y = host(ops.mv_q8(fmt, dev(w), xq, w.shape[0], x.shape[1], x.shape[0]))
+        assert O.rel_l2(y, yref) < 2e-2
+
+    def test_multi_segments(self, ops):
+        k, tokens, ns = 4096, 1, [512, 128, 130]
+        ws = [dev(blocks("q6_k", n, k, 30 + i)) for i, n in enumerate(ns)]
+        xq = ops.quant_q8(dev(np.random.default_rng(31).standard_normal((tokens, k)).astype(np.float32)))
+        ys = ops.mv_q8_multi("q6_k", ws, xq, ns, k, tokens)
+        for w, n, y in zip(ws, ns, ys):
+            assert torch.equal(y, ops.mv_q8("q6_k", w, xq, n, k, tokens))
 
 
 class TestMvQ8Multi:
