@@ -305,6 +305,15 @@ def bench_pairs(args, torch, dev, time_steps):
             ops.mv("q6_k", u, x, n, k, y=yu)
             ops.silu_mul(y, yu)
 
+    xq = ops.quant_q8(x)
+
+    def mv_q8_two():   # the reference's default decode of a mixed layer: two int8 projections + g_silu_mul
+        for i in range(chain):
+            g, u = ws[i % copies]
+            ops.mv_q8("q4_k", g, xq, n, k, 1, y=y)
+            ops.mv_q8("q6_k", u, xq, n, k, 1, y=yu)
+            ops.silu_mul(y, yu)
+
     def timed(body, steps, per):
         g = Timed(torch, body)
         for _ in range(max(3, args.warmup)):
@@ -315,9 +324,13 @@ def bench_pairs(args, torch, dev, time_steps):
     steps = max(5, min(args.steps, 200))
     us_pair = timed(mv_pair, steps, chain) * 1e3
     us_two = timed(mv_two, steps, chain) * 1e3
+    us_q8 = timed(mv_q8_two, steps, chain) * 1e3
     out["decode"] = {"pair_us": round(us_pair, 2), "pair_weight_gbs": round(nbytes / (us_pair * 1e-6) / 1e9, 1),
-                     "two_projections_silu_mul_us": round(us_two, 2), "weight_copies": copies,
-                     "kernel": "k_mvs<kFmtPair> (lk_mv with LK_FMT_PAIR, bf16 x)"}
+                     "two_projections_silu_mul_us": round(us_two, 2),
+                     "int8_two_projections_silu_mul_us": round(us_q8, 2),
+                     "int8_weight_gbs": round(nbytes / (us_q8 * 1e-6) / 1e9, 1), "weight_copies": copies,
+                     "kernel": "k_mvs<kFmtPair> (lk_mv with LK_FMT_PAIR, bf16 x); int8: k_mv_q8_rows<Q4_K> + "
+                               "k_mvq8g<Q6_K> on one lk_quant_q8 row, then lk_silu_mul"}
     del ws
     x16, sc = ops.row_scale_f16(torch.randn(m, k, device=dev).to(torch.bfloat16))
     yp, yq = torch.empty(m, n, device=dev), torch.empty(m, n, device=dev)
@@ -335,7 +348,8 @@ def bench_pairs(args, torch, dev, time_steps):
     out["prefill"] = {"rows": m, "pair_tflops": round(flops / (ms_pair * 1e-3) / 1e12, 1),
                       "pair_ms": round(ms_pair, 4), "two_gemms_silu_mul_ms": round(ms_two, 4),
                       "q4_k_swiglu_ms": round(ms_one, 4),
-                      "kernel": "k_gemm_p<kFmtPair> (window form, tcgen05 kind::f16)"}
+                      "kernel": "two passes of k_gemm_p (tcgen05 kind::f16): Q4_K store, Q6_K store with the act "
+                                "epilogue against the stored gate"}
     return out
 
 

@@ -61,6 +61,9 @@ struct GemmArgs {
   // 256-value chunk, and the up weight's row stride
   int fmt, fmt2, cb, cb2;
   int64_t rb2;
+  // store modes: y = act(y, acc * scale + bias) -- the second pass of a gate/up pair in two formats, whose first pass
+  // stored the gate's products (plus its bias) in y (epi.act / alpha / limit choose the activation)
+  int act_mul;
 };
 
 // packed bytes of one 256-value chunk of a row, and the bytes a window of it takes in shared memory: the chunk
@@ -72,20 +75,6 @@ __host__ __device__ constexpr int window_bytes(int fmt) { return (chunk_bytes(fm
 __host__ __device__ constexpr int row_slot_bytes(int fmt, bool win) {
   return !win ? kChunkBytes : fmt == kFmtPair ? window_bytes(LK_Q8_0) : window_bytes(fmt);
 }
-
-// One 32-value group (j of the 256-value chunk) of any format into 4 swizzled 16-byte chunks of the B tile, with the
-// reference's staging (group_f16: one rounding, or the K-quants' f16 fma)
-template <int FMT>
-LK_DEV void dequant_group_any(const uint8_t* chunk, int j, uint8_t* b_tile, int r, int c0) {
-  __half h[32];
-  if (fmt_qk(FMT) == 32) group_f16<FMT>(chunk + j * fmt_block_bytes(FMT), 0, h);
-  else group_f16<FMT>(chunk, j, h);
-#pragma unroll
-  for (int cc = 0; cc < 4; ++cc)
-    *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = reinterpret_cast<const uint4*>(h)[cc];
-}
-
-// 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
 
 LK_DEV uint32_t hsub2u(uint32_t a, uint32_t b) {
   __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
@@ -99,6 +88,115 @@ LK_DEV uint32_t hfma2u(uint32_t a, __half2 b, __half2 c) {
   __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), b, c);
   return *reinterpret_cast<uint32_t*>(&r);
 }
+
+// N little-endian words from a 2-byte aligned shared-memory address: N + 1 aligned loads and funnel shifts (the
+// load past the end stays inside the CTA's shared memory: the row windows are followed by the staging buffers)
+template <int N>
+LK_DEV void ld_words_2a(const uint8_t* p, uint32_t (&w)[N]) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+  const uint32_t sh = uint32_t(reinterpret_cast<uintptr_t>(p) & 3u) * 8u;
+  uint32_t v[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; ++i) v[i] = q[i];
+#pragma unroll
+  for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
+}
+
+// Word-wise f16 staging of one 32-value group for the formats whose codes sit in whole bytes or nibble/bit planes
+// (Q8_0, Q5_0, Q5_K, Q6_K): 4 codes per 32-bit word, f16(1024 + code) by a byte permute, the exact code (or centred
+// code) by one f16 subtraction, then the reference's single rounding -- one f16 multiply by d (Q8_0, Q5_0), or the
+// f16 fma of the K-quants with f16(d sc) and f16(-dmin m) / f16(-32 d sc) -- the same operations group_f16 does value
+// by value. words[i] = codes of values 4i..4i+3; s / o: the scale and offset of values 0..15 (s[0], o[0]) and 16..31.
+LK_DEV void stage_words(const uint32_t (&c)[8], uint32_t bias, const __half2 (&s)[2], const __half2 (&o)[2], bool fma,
+                        uint8_t* b_tile, int r, int c0) {
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    const __half2 sc = s[cc >> 1], of = o[cc >> 1];
+    uint32_t h[4] = {prmt(c[2 * cc], 0x64646464u, 0x4140u), prmt(c[2 * cc], 0x64646464u, 0x4342u),
+                     prmt(c[2 * cc + 1], 0x64646464u, 0x4140u), prmt(c[2 * cc + 1], 0x64646464u, 0x4342u)};
+    uint4 out;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) po[t] = fma ? hfma2u(hsub2u(h[t], bias), sc, of) : hmul2u(hsub2u(h[t], bias), sc);
+    *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = out;
+  }
+}
+
+template <int FMT>
+LK_DEV void dequant_group_words(const uint8_t* chunk, int j, uint8_t* b_tile, int r, int c0) {
+  uint32_t c[8];
+  __half2 s[2], o[2];
+  if (FMT == LK_Q8_0) {   // int8 codes: code ^ 0x80 = code + 128; f16(1152 + code) - 1152 = code; f16(d code)
+    const uint8_t* b = chunk + 34 * j;
+    ld_words_2a(b + 2, c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] ^= 0x80808080u;
+    const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t*>(b));
+    s[0] = s[1] = __halves2half2(d, d);
+    stage_words(c, 0x64806480u, s, s, false, b_tile, r, c0);
+  } else if (FMT == LK_Q5_0) {   // nibble | bit i of qh << 4; f16(1024 + code) - 1040 = code - 16; f16(d (code - 16))
+    const uint8_t* b = chunk + 22 * j;
+    uint32_t qh[1], qs[4];
+    ld_words_2a(b + 2, qh);
+    ld_words_2a(b + 6, qs);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t hb = (qh[0] >> (4 * i)) & 15u;
+      c[i] = ((i < 4 ? qs[i] : qs[i - 4] >> 4) & 0x0F0F0F0Fu) |
+             ((hb & 1u) << 4) | ((hb & 2u) << 11) | ((hb & 4u) << 18) | ((hb & 8u) << 25);
+    }
+    const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t*>(b));
+    s[0] = s[1] = __halves2half2(d, d);
+    stage_words(c, 0x64106410u, s, s, false, b_tile, r, c0);
+  } else if (FMT == LK_Q5_K) {   // Q4_K's nibble pages | bit j of qh[l] << 4; fma(code, f16(d sc), f16(-dmin m))
+    int sc, m;
+    q4k_scale_min(chunk + 4, j, sc, m);
+    uint32_t qs[8], qh[8];
+    ld_words_2a(chunk + 48 + 32 * (j >> 1), qs);
+    ld_words_2a(chunk + 16, qh);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      c[i] = ((qs[i] >> (4 * (j & 1))) & 0x0F0F0F0Fu) | (((qh[i] >> j) & 0x01010101u) << 4);
+    s[0] = s[1] = __float2half2_rn(f16_at(chunk) * float(sc));
+    o[0] = o[1] = __float2half2_rn(-(f16_at(chunk + 2) * float(m)));
+    stage_words(c, 0x64006400u, s, o, true, b_tile, r, c0);
+  } else {   // Q6_K: ql nibble | 2 bits of qh << 4 (0..63); fma(code, f16(d sc), f16(-32 d sc)) per 16 values
+    const int h = j >> 2, jj = j & 3;
+    uint32_t ql[8], qh[8];
+    ld_words_2a(chunk + 64 * h + 32 * (jj & 1), ql);
+    ld_words_2a(chunk + 128 + 32 * h, qh);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      c[i] = ((ql[i] >> (4 * (jj >> 1))) & 0x0F0F0F0Fu) | (((qh[i] >> (2 * jj)) & 0x03030303u) << 4);
+    const float d = f16_at(chunk + 208);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float a = d * float(int8_t(chunk[192 + 2 * j + t]));
+      s[t] = __float2half2_rn(a);
+      o[t] = __float2half2_rn(-32.0f * a);
+    }
+    stage_words(c, 0x64006400u, s, o, true, b_tile, r, c0);
+  }
+}
+
+// One 32-value group (j of the 256-value chunk) of any format into 4 swizzled 16-byte chunks of the B tile, with the
+// reference's staging (group_f16: one rounding, or the K-quants' f16 fma)
+template <int FMT>
+LK_DEV void dequant_group_any(const uint8_t* chunk, int j, uint8_t* b_tile, int r, int c0) {
+  if (FMT == LK_Q8_0 || FMT == LK_Q5_0 || FMT == LK_Q5_K || FMT == LK_Q6_K) {
+    dequant_group_words<FMT>(chunk, j, b_tile, r, c0);
+    return;
+  }
+  __half h[32];
+  if (fmt_qk(FMT) == 32) group_f16<FMT>(chunk + j * fmt_block_bytes(FMT), 0, h);
+  else group_f16<FMT>(chunk, j, h);
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc)
+    *reinterpret_cast<uint4*>(b_tile + sw128(r, c0 + cc)) = reinterpret_cast<const uint4*>(h)[cc];
+}
+
+// 16-byte chunk `c` of row `r` of a K-major 128-byte-swizzled tile
+
 
 // 8 codes (bytes of t0, t1; low nibble only) -> 8 f16 (1024 + code), natural k order
 LK_DEV void magic8(uint32_t t0, uint32_t t1, uint32_t (&h)[4]) {
@@ -178,7 +276,10 @@ LK_DEV void dequant_group_rt(int fmt, const uint8_t* chunk, int j, uint8_t* b_ti
   switch (fmt) {
     case LK_Q4_0: dequant_group<LK_Q4_0>(chunk, j, b_tile, r, c0); return;
     case LK_IQ4_NL: dequant_group<LK_IQ4_NL>(chunk, j, b_tile, r, c0); return;
-    case LK_Q4_K: dequant_group_any<LK_Q4_K>(chunk, j, b_tile, r, c0); return;
+    case LK_Q4_K:   // the box form's register decode where the window left the 144-byte chunk 16-byte aligned
+      if ((reinterpret_cast<uintptr_t>(chunk) & 15) == 0) dequant_group<LK_Q4_K>(chunk, j, b_tile, r, c0);
+      else dequant_group_any<LK_Q4_K>(chunk, j, b_tile, r, c0);
+      return;
     case LK_Q5_0: dequant_group_any<LK_Q5_0>(chunk, j, b_tile, r, c0); return;
     case LK_Q8_0: dequant_group_any<LK_Q8_0>(chunk, j, b_tile, r, c0); return;
     case LK_Q5_K: dequant_group_any<LK_Q5_K>(chunk, j, b_tile, r, c0); return;
@@ -594,6 +695,12 @@ __global__ void __launch_bounds__(kGemmPThreads, 1)
                 o.y += old.y;
                 o.z += old.z;
                 o.w += old.w;
+              } else if (MODE == LK_STORE && p.act_mul) {
+                const float4 g = *reinterpret_cast<const float4*>(p.dst[0] + off);
+                o.x = act_apply(p.epi.act, g.x, o.x, p.epi.alpha, p.epi.limit);
+                o.y = act_apply(p.epi.act, g.y, o.y, p.epi.alpha, p.epi.limit);
+                o.z = act_apply(p.epi.act, g.z, o.z, p.epi.alpha, p.epi.limit);
+                o.w = act_apply(p.epi.act, g.w, o.w, p.epi.alpha, p.epi.limit);
               }
 #pragma unroll
               for (int d = 0; d < kMaxPeers; ++d)
@@ -762,8 +869,28 @@ static int choose_ksplit(int tiles, int kp, int sms) {
 
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
-         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out, const ExpertEpi* epi) {
+         int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out, const ExpertEpi* epi,
+         bool act_mul) {
+  if ((fmt >> 16) && !out && (mode == LK_SWIGLU ? !tile_info : mode == LK_SWIGLU_SORTED)) {
+    // a gate/up pair on dense or bucket-sorted rows: two passes of the single-format kernels -- the gate's products
+    // (+ its bias) stored in y, then the up weight's with the activation applied against them in the epilogue --
+    // where each weight can take its own kernel (a Q4_K one keeps its 16-byte aligned rows); else the pair kernel
+    const int fg = fmt & 0xffff, fu = fmt >> 16;
+    auto own = [&](int f, const void* p) { return f != LK_Q4_K || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (own(fg, w) && own(fu, w2)) {
+      const ExpertEpi e0 = epi ? *epi : ExpertEpi{};
+      const ExpertEpi eg{e0.bias, nullptr, LK_ACT_SILU, 0.f, 0.f}, eu{e0.bias2, nullptr, e0.act, e0.alpha, e0.limit};
+      // LK_STORE: dense rows, or with a schedule the sorted-row store the down projection uses (A = x16[r], scales[r])
+      int rc = gemm(fg, LK_STORE, rows, k, n, x16, scales, w, nullptr, y, s, tile_info, rowmap, xrows, ku, n_experts,
+                    lk_row_bytes(fg, k) * n, 0, nullptr, &eg);
+      if (rc == LK_OK)
+        rc = gemm(fu, LK_STORE, rows, k, n, x16, scales, w2, nullptr, y, s, tile_info, rowmap, xrows, ku, n_experts,
+                  lk_row_bytes(fu, k) * n, 0, nullptr, &eu, true);
+      return rc;
+    }
+  }
   GemmArgs a{};
+  a.act_mul = act_mul;
   a.scales = scales;
   if (epi) a.epi = *epi;
   if (out) {
@@ -832,7 +959,7 @@ int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const f
   // dense store / acc: split K where the rounds of the persistent grid come out shorter (few tiles, or a last round
   // that would run nearly empty); the ranges meet in dst[0] in order
   const int dense_tiles = ((rows + tm - 1) / tm) * ((n + bn - 1) / bn);
-  if (group == kDense && mode != LK_SWIGLU && rows > 0) {
+  if (group == kDense && mode != LK_SWIGLU && rows > 0 && !act_mul) {
     a.ksplit = choose_ksplit(dense_tiles, kp, sms);
     a.kps = (kp + a.ksplit - 1) / a.ksplit;
   }

@@ -64,7 +64,7 @@ struct OutSpec {
 int gemm(int fmt, int mode, int rows, int k, int n, const uint16_t* x16, const float* scales, const void* w,
          const void* w2, float* y, cudaStream_t s, const int32_t* tile_info, const int32_t* rowmap, int xrows, int ku,
          int n_experts, int64_t expert_stride, int64_t w2_offset, const OutSpec* out = nullptr,
-         const ExpertEpi* epi = nullptr);
+         const ExpertEpi* epi = nullptr, bool act_mul = false);
 
 int gemm_mxfp4s(int mode, int order, int rows, int k, int n, const uint8_t* x8, const float* s8, const uint8_t* w,
                 const uint8_t* ws, const uint8_t* w2, const uint8_t* w2s, float* y, cudaStream_t s);
