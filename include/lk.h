@@ -234,6 +234,16 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                      lk_stream_t stream);
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream);
+/* lk_moe_expert_mv_q8: the decode expert matvecs on int8 activations, g_moe_gu_{fmt}_q8 / g_moe_dn_{fmt}_q8
+ * (MOE_Q8, gen_llm.py:5290-5302; gen_moe.py:535-727 with iq): xq is lk_quant_q8's output for the activation rows --
+ * mode 0 (gu): the tokens' rows (assignment a reads row a / ku; assignments % ku == 0), y[a] = act(Wg[e] x, Wu[e] x)
+ * with w / w2 / fused as lk_moe_expert_mv; mode 1 (dn): one row per assignment (the quantised activations),
+ * y[a] = Wd[e] x[a]; e = ids[a]. Per 32-value group an exact integer dot of the weight and activation codes, scaled in
+ * f32 as lk_mv_q8 does. Formats: Q4_0, Q4_K, Q8_0, Q5_0, Q5_K, Q6_K (the reference's MoE int8 formats; no IQ4, no
+ * biases); k a whole number of blocks and of 32-value groups; xq 16-byte, w 2-byte aligned. */
+int lk_moe_expert_mv_q8(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                        const int32_t* ids, const uint8_t* xq, const void* w, const void* w2, int act, float alpha,
+                        float limit, float* y, lk_stream_t stream);
 /* lk_moe_expert_mv_mxfp4s: lk_moe_expert_mv over MXFP4S experts (the reference's expert_mv, gen_moe.py:535-727, with
  * the split-plane MXFP4S format of gen_llm.py:844-895; the MoE counterpart of lk_moe_grouped_gemm_mxfp4s_f8 at decode
  * sizes). w / ws: nibble plane [rows][k/2] and E8M0 plane [rows][k/32] of the stacked experts -- mode 0 (gu): per

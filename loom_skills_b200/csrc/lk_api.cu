@@ -277,6 +277,25 @@ int lk_moe_expert_mv_ex(int fmt, int mode, int n, int k, int assignments, int ku
   return mv_generic(fmt, a, (cudaStream_t)stream);
 }
 
+int lk_moe_expert_mv_q8(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                        const int32_t* ids, const uint8_t* xq, const void* w, const void* w2, int act, float alpha,
+                        float limit, float* y, lk_stream_t stream) {
+  if (fmt != LK_Q4_0 && fmt != LK_Q4_K && fmt != LK_Q8_0 && fmt != LK_Q5_0 && fmt != LK_Q5_K && fmt != LK_Q6_K)
+    return mv_format(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (n <= 0 || k <= 0 || assignments < 0 || ku <= 0 || n_experts <= 0) return LK_EINVAL;
+  if (mode != 0 && mode != 1) return LK_EINVAL;
+  if (k % fmt_qk(fmt) || k % 32) return LK_EINVAL;
+  if (mode == 0 && assignments % ku) return LK_EINVAL;   // whole tokens of ku assignments
+  if (!act_ok(act)) return LK_EINVAL;
+  if (assignments == 0) return LK_OK;
+  if (!ids || !xq || !w || !y) return LK_EINVAL;
+  if (mode == 0 && !fused && !w2) return LK_EINVAL;
+  if (!aligned(xq, 16) || !aligned(w, 2) || (mode == 0 && !fused && !aligned(w2, 2))) return LK_EALIGN;
+  const int xrows = mode == 0 ? assignments / ku : assignments;
+  return moe_expert_mv_q8(fmt, mode, n, k, assignments, ku, n_experts, fused, ids, xq, xrows, w, w2, act, alpha,
+                          limit, y, (cudaStream_t)stream);
+}
+
 int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
                      const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
                      lk_stream_t stream) {

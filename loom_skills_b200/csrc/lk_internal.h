@@ -104,6 +104,11 @@ int mv_q8_multi(int fmt, int nseg, const int* ns, const void* const* ws, float* 
                 int accumulate, const uint8_t* xq, cudaStream_t s);
 // the other formats with integer weight codes (Q8_0, Q5_0, Q5_K, Q6_K, IQ4_NL, IQ4_XS; lk_mvq8g.cu)
 bool mv_q8_generic_format(int fmt);
+// per-assignment expert matvecs on int8 activation codes (MOE_Q8; lk_mvq8g.cu): mode 0 gate/up with act, 1 down;
+// xq holds xrows rows of lk_quant_q8 output
+int moe_expert_mv_q8(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                     const int32_t* ids, const uint8_t* xq, int xrows, const void* w, const void* w2, int act,
+                     float alpha, float limit, float* y, cudaStream_t s);
 int mv_q8_generic(int fmt, int n, int k, int tokens, int accumulate, const uint8_t* xq, const void* w, float* y,
                   cudaStream_t s);
 // one token: the activation row quantised inside the row-streaming matvec (no xq buffer); LK_EUNSUPPORTED off its

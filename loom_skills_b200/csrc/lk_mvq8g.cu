@@ -47,13 +47,32 @@ struct ICodes {
 
 enum { kOneScale = 0, kMinimum = 1, kTwoScales = 2 };
 __host__ __device__ constexpr int icode_kind(int fmt) {
-  return fmt == LK_Q6_K ? kTwoScales : (fmt == LK_Q5_0 || fmt == LK_Q5_K) ? kMinimum : kOneScale;
+  return fmt == LK_Q6_K ? kTwoScales
+         : (fmt == LK_Q5_0 || fmt == LK_Q5_K || fmt == LK_Q4_0 || fmt == LK_Q4_K) ? kMinimum
+                                                                                   : kOneScale;
 }
 
 // group j of the block at b (@g_<fmt>_icodes)
 template <int FMT>
 LK_DEV void group_icodes(const uint8_t* b, int j, ICodes& o) {
-  if (FMT == LK_Q8_0) {   // gen_llm.py:523-534: int8 codes, scale d
+  if (FMT == LK_Q4_0) {   // gen_llm.py:536-552: nibbles 0..15, minimum 8 d
+    const float d = f16_2a(b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t q = ld32_2a(b + 2 + 4 * (i & 3));
+      o.w[i] = (i < 4 ? q : q >> 4) & 0x0F0F0F0Fu;
+    }
+    o.sc = d;
+    o.mn = 8.0f * d;
+  } else if (FMT == LK_Q4_K) {   // gen_llm.py:554-577: the nibble page of group j, scale d sc, minimum dmin m
+    uint32_t sc, m;
+    q4k_scale_min_w(ld32_2a(b + 4), ld32_2a(b + 8), ld32_2a(b + 12), j, sc, m);
+    o.sc = f16_2a(b) * float(sc);
+    o.mn = f16_2a(b + 2) * float(m);
+    const uint8_t* qs = b + 16 + 32 * (j >> 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o.w[i] = (ld32_2a(qs + 4 * i) >> (4 * (j & 1))) & 0x0F0F0F0Fu;
+  } else if (FMT == LK_Q8_0) {   // gen_llm.py:523-534: int8 codes, scale d
     o.sc = f16_2a(b);
 #pragma unroll
     for (int i = 0; i < 8; ++i) o.w[i] = ld32_2a(b + 2 + 4 * i);
@@ -144,19 +163,31 @@ struct GqArgs {
   int cb;                 // packed bytes of a full chunk (kGChunk values)
   int nkc;                // chunks per row
   int row_slot;           // shared-memory bytes of one row's window
+  // per MoE assignment a (kGMoeDn / kGMoeGu): expert ids[a], activation row a / x_div, output row a; the second
+  // weight's rows (gate/up) at e * rows_per_expert2 + w2_row_offset of w2
+  const int32_t* ids;
+  const uint8_t* w2;
+  int assignments, x_div, n_experts, rows_per_expert, rows_per_expert2, w2_row_offset;
+  int act;
+  float alpha, limit;
 };
 
-template <int FMT, int NT>
+enum { kGDense = 0, kGMoeDn = 1, kGMoeGu = 2 };
+
+template <int FMT, int NT, int MODE>
 __global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
   constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
   constexpr int bb = fmt_block_bytes(FMT);
+  constexpr int NW = MODE == kGMoeGu ? 2 : 1;   // weights per row block (gate and up)
+  static_assert(MODE == kGDense || NT == 1, "one activation row per MoE assignment");
   extern __shared__ __align__(128) uint8_t smem[];
-  const int slot = kGRows * a.row_slot;
+  const int slot = NW * kGRows * a.row_slot;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * slot);
   uint64_t* empty = full + kGStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x, G = gridDim.x;
-  const int nblk = (a.n + kGRows - 1) / kGRows;
+  const int nrb = (a.n + kGRows - 1) / kGRows;   // row blocks of one output row
+  const int nblk = MODE == kGDense ? nrb : a.assignments * nrb;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGStages; ++i) {
       mbar_init(&full[i], 1);
@@ -165,25 +196,31 @@ __global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
     fence_mbar_init();
   }
   __syncthreads();
-  // row r's chunk kc: its packed source and length
-  auto src_of = [&](int r, int kc, uintptr_t& src, uint32_t& len) {
+  // output row r (of n) of row block blk in weight wi: its packed chunk kc's source and length
+  auto src_of = [&](int blk, int r, int wi, int kc, uintptr_t& src, uint32_t& len) {
     const int64_t c0 = int64_t(kc) * a.cb;
     len = uint32_t(min(int64_t(a.cb), a.rb - c0));
-    src = reinterpret_cast<uintptr_t>(a.w + int64_t(r) * a.rb + c0);
+    int64_t wr = r;
+    if (MODE != kGDense) {
+      const int e = min(max(__ldg(a.ids + blk / nrb), 0), a.n_experts - 1);
+      wr = wi ? int64_t(e) * a.rows_per_expert2 + a.w2_row_offset + r : int64_t(e) * a.rows_per_expert + r;
+    }
+    src = reinterpret_cast<uintptr_t>((wi ? a.w2 : a.w) + wr * a.rb + c0);
   };
   if (warp == 0) {
     gq_launch();
+    if (MODE != kGDense) gq_wait();   // the expert ids come from the previous kernel
     int i = 0;
     for (int blk = cta; blk < nblk; blk += G) {
       for (int kc = 0; kc < a.nkc; ++kc, ++i) {
         if (i == 1) gq_wait();   // the first stage goes out before the previous grid ends
         const int s = i % kGStages;
         if (i >= kGStages && !mbar_wait(&empty[s], ((i / kGStages) - 1) & 1)) atomicOr(&g_status, 1u);
-        const int r = blk * kGRows + lane;
+        const int r = (blk % nrb) * kGRows + (lane % kGRows);   // lanes 0-7 the first weight's rows, 8-15 the second's
         uintptr_t src = 0;
         uint32_t len = 0, bytes = 0;
-        if (lane < kGRows && r < a.n) {
-          src_of(r, kc, src, len);
+        if (lane < NW * kGRows && r < a.n) {
+          src_of(blk, r, lane / kGRows, kc, src, len);
           bytes = uint32_t(((src + len + 15) & ~uintptr_t(15)) - (src & ~uintptr_t(15)));
         }
         uint32_t total = bytes;
@@ -203,30 +240,37 @@ __global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
   const int cw = warp - 1, groups = a.k / 32;
   int i = 0;
   for (int blk = cta; blk < nblk; blk += G) {
-    const int r = blk * kGRows + cw;
-    float acc[NT];
+    const int r = (blk % nrb) * kGRows + cw;
+    const int xrow = MODE == kGDense ? 0 : (blk / nrb) / a.x_div;   // the assignment's activation row
+    float acc[NW][NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    for (int wi = 0; wi < NW; ++wi)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[wi][t] = 0.f;
     for (int kc = 0; kc < a.nkc; ++kc, ++i) {
       const int s = i % kGStages;
       if (!mbar_wait(&full[s], (i / kGStages) & 1)) atomicOr(&g_status, 1u);
       if (r < a.n) {
-        uintptr_t src;
-        uint32_t len;
-        src_of(r, kc, src, len);
-        const uint8_t* chunk = smem + s * slot + cw * a.row_slot + (src & 15);
         const int gc = min(kGChunk, a.k - kc * kGChunk) / 32, g0 = kc * (kGChunk / 32);
-        for (int g = lane; g < gc; g += 32) {
-          ICodes c;
-          group_icodes<FMT>(chunk + (g / gpb) * bb, g % gpb, c);
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t >= a.ntok) break;
-            const uint4* xp = reinterpret_cast<const uint4*>(a.codes + int64_t(t) * a.k + int64_t(g0 + g) * 32);
-            const uint4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
-            const float2 m = __ldg(reinterpret_cast<const float2*>(a.meta) + int64_t(t) * groups + g0 + g);
-            const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            acc[t] += group_dot<FMT>(c, xw, m.x, m.y);
+        for (int wi = 0; wi < NW; ++wi) {
+          uintptr_t src;
+          uint32_t len;
+          src_of(blk, r, wi, kc, src, len);
+          const uint8_t* chunk = smem + s * slot + (wi * kGRows + cw) * a.row_slot + (src & 15);
+          for (int g = lane; g < gc; g += 32) {
+            ICodes c;
+            group_icodes<FMT>(chunk + (g / gpb) * bb, g % gpb, c);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              if (t >= a.ntok) break;
+              const int64_t xr = MODE == kGDense ? t : xrow;
+              const uint4* xp = reinterpret_cast<const uint4*>(a.codes + xr * a.k + int64_t(g0 + g) * 32);
+              const uint4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+              const float2 m = __ldg(reinterpret_cast<const float2*>(a.meta) + xr * groups + g0 + g);
+              const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+              acc[wi][t] += group_dot<FMT>(c, xw, m.x, m.y);
+            }
           }
         }
       }
@@ -234,24 +278,31 @@ __global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+    for (int wi = 0; wi < NW; ++wi)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xFFFFFFFFu, acc[t], o);
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[wi][t] += __shfl_xor_sync(0xFFFFFFFFu, acc[wi][t], o);
     if (lane == 0 && r < a.n) {
+      if (MODE == kGDense) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t >= a.ntok) break;
-        float* yp = a.y + int64_t(t) * a.n + r;
-        *yp = a.accumulate ? *yp + acc[t] : acc[t];
+        for (int t = 0; t < NT; ++t) {
+          if (t >= a.ntok) break;
+          float* yp = a.y + int64_t(t) * a.n + r;
+          *yp = a.accumulate ? *yp + acc[0][t] : acc[0][t];
+        }
+      } else {
+        a.y[int64_t(blk / nrb) * a.n + r] =
+            MODE == kGMoeGu ? act_apply(a.act, acc[0][0], acc[NW - 1][0], a.alpha, a.limit) : acc[0][0];
       }
     }
   }
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int MODE>
 int launch_gq(const GqArgs& a, cudaStream_t s) {
-  const int smem = kGStages * kGRows * a.row_slot + 2 * kGStages * 8;
-  auto kern = k_mvq8g<FMT, NT>;
+  const int smem = kGStages * (MODE == kGMoeGu ? 2 : 1) * kGRows * a.row_slot + 2 * kGStages * 8;
+  auto kern = k_mvq8g<FMT, NT, MODE>;
   static int configured[32] = {};   // the largest shared-memory size set per device
   static std::mutex mu;
   int dev = 0, sms = 0;
@@ -268,7 +319,7 @@ int launch_gq(const GqArgs& a, cudaStream_t s) {
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGThreads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
-  const int nblk = (a.n + kGRows - 1) / kGRows;
+  const int nblk = (a.n + kGRows - 1) / kGRows * (MODE == kGDense ? 1 : a.assignments);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(min(nblk, per_sm * sms), 1, 1);
   cfg.blockDim = dim3(kGThreads, 1, 1);
@@ -283,11 +334,23 @@ int launch_gq(const GqArgs& a, cudaStream_t s) {
 }
 
 template <int FMT>
-int mvq8g_f(GqArgs a, int tokens, cudaStream_t s) {
+void chunk_geometry(GqArgs& a) {
   a.rb = lk_row_bytes(FMT, a.k);
   a.cb = kGChunk / fmt_qk(FMT) * fmt_block_bytes(FMT);
   a.nkc = (a.k + kGChunk - 1) / kGChunk;
   a.row_slot = (a.cb + 15 + 15) / 16 * 16;
+}
+
+template <int FMT>
+int mvq8g_moe(GqArgs a, int mode, cudaStream_t s) {
+  chunk_geometry<FMT>(a);
+  a.ntok = 1;
+  return mode == 0 ? launch_gq<FMT, 1, kGMoeGu>(a, s) : launch_gq<FMT, 1, kGMoeDn>(a, s);
+}
+
+template <int FMT>
+int mvq8g_f(GqArgs a, int tokens, cudaStream_t s) {
+  chunk_geometry<FMT>(a);
   float* y = a.y;
   const uint8_t* codes = a.codes;
   const float* meta = a.meta;
@@ -296,13 +359,45 @@ int mvq8g_f(GqArgs a, int tokens, cudaStream_t s) {
     a.y = y + int64_t(t0) * a.n;
     a.codes = codes + int64_t(t0) * a.k;
     a.meta = meta + int64_t(t0) * (a.k / 32) * 2;
-    const int rc = a.ntok == 1 ? launch_gq<FMT, 1>(a, s) : launch_gq<FMT, 8>(a, s);
+    const int rc = a.ntok == 1 ? launch_gq<FMT, 1, kGDense>(a, s) : launch_gq<FMT, 8, kGDense>(a, s);
     if (rc != LK_OK) return rc;
   }
   return LK_OK;
 }
 
 }  // namespace
+
+int moe_expert_mv_q8(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
+                     const int32_t* ids, const uint8_t* xq, int xrows, const void* w, const void* w2, int act,
+                     float alpha, float limit, float* y, cudaStream_t s) {
+  GqArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
+  a.w2 = static_cast<const uint8_t*>(mode == 0 && !fused ? w2 : w);
+  a.codes = xq;
+  a.meta = reinterpret_cast<const float*>(xq + int64_t(xrows) * k);
+  a.y = y;
+  a.n = n;
+  a.k = k;
+  a.ids = ids;
+  a.assignments = assignments;
+  a.x_div = mode == 0 ? ku : 1;
+  a.n_experts = n_experts;
+  a.rows_per_expert = n * (mode == 0 && fused ? 2 : 1);
+  a.rows_per_expert2 = mode == 0 && fused ? 2 * n : n;
+  a.w2_row_offset = mode == 0 && fused ? n : 0;
+  a.act = act;
+  a.alpha = alpha;
+  a.limit = limit;
+  switch (fmt) {
+    case LK_Q4_0: return mvq8g_moe<LK_Q4_0>(a, mode, s);
+    case LK_Q4_K: return mvq8g_moe<LK_Q4_K>(a, mode, s);
+    case LK_Q8_0: return mvq8g_moe<LK_Q8_0>(a, mode, s);
+    case LK_Q5_0: return mvq8g_moe<LK_Q5_0>(a, mode, s);
+    case LK_Q5_K: return mvq8g_moe<LK_Q5_K>(a, mode, s);
+    case LK_Q6_K: return mvq8g_moe<LK_Q6_K>(a, mode, s);
+  }
+  return LK_EUNSUPPORTED;
+}
 
 bool mv_q8_generic_format(int fmt) {
   return fmt == LK_Q8_0 || fmt == LK_Q5_0 || fmt == LK_Q5_K || fmt == LK_Q6_K || fmt == LK_IQ4_NL ||

@@ -268,6 +268,21 @@ def moe_combine_sorted(ys, pos, wts, y=None, accumulate=False, sg=None):
     return y
 
 
+def moe_expert_mv_q8(fmt, mode, ids, xq, w, n, k, ku, n_experts, fused=True, w2=None, y=None, act="silu", alpha=1.702,
+                     limit=7.0):
+    """Decode expert matvecs on int8 activations (MOE_Q8): xq = quant_q8 of the tokens' rows (mode 'gu') or of one
+    row per assignment ('dn'); 'gu' -> act(Wg x, Wu x), 'dn' -> Wd x."""
+    _cuda(ids, xq, w, w2, y)
+    a = ids.numel()
+    if y is None:
+        y = torch.empty(a, n, dtype=torch.float32, device=xq.device)
+    md = 0 if mode == "gu" else 1
+    L.check(L.load().lk_moe_expert_mv_q8(_fmt(fmt), md, n, k, a, ku, n_experts, 1 if fused else 0,
+                                         _ptr(ids.contiguous()), _ptr(xq), _ptr(w), _ptr(w2), _act(act), alpha, limit,
+                                         _ptr(y), _stream()), "lk_moe_expert_mv_q8")
+    return y
+
+
 def moe_expert_mv(fmt, mode, ids, x, w, n, k, ku, n_experts, fused=True, w2=None, y=None, act="silu", bias=None,
                   bias2=None, alpha=1.702, limit=7.0):
     """Decode expert matvecs per assignment: mode 'gu' -> act(Wg x + bg, Wu x + bu); 'dn' -> Wd x (+ bd)."""
@@ -355,7 +370,7 @@ def _combine_out(tokens, h, x, y_shared):
 
 def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None, gating=1, router_bias=None,
             scale=1.0, act="silu", b_gate=None, b_up=None, b_down=None, down_scale=None, y_shared=None,
-            shared_gate_w=None, alpha=1.702, limit=7.0, w_up=None, fmt_down=None):
+            shared_gate_w=None, alpha=1.702, limit=7.0, w_up=None, fmt_down=None, act_q8=False):
     """The routed expert FFN of one MoE layer (wiring of gen_llm.py:5324-5386): route (gating 1/2/3, router bias,
     expert_weights_scale) -> per-expert down scale folded into the weights (g_moe_wscale) -> bucket -> grouped gate/up
     (act + biases) -> row scale -> grouped down (+ bias) -> weighted combine (prefill), or per-assignment expert
@@ -368,7 +383,9 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     fmt_down or the gate's; biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
     switches to the GEMMs at 64 tokens (gen_llm.py:6107); here from 192 assignments (tokens * ku), where they
     measured faster on configs[2] shapes (top-8 of 128 experts: matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 /
-    312 us). `prefill` forces either path."""
+    312 us). `prefill` forces either path. act_q8 (decode only; the reference's MOE_Q8 numerics, gen_llm.py:5290-5302):
+    x and the activations quantised to int8 codes (quant_q8) for the expert matvecs -- formats with integer codes,
+    one format for gate and up, no biases."""
     tokens = x.shape[0]
     ids, wts, sg = _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale,
                                     shared_gate_w)
@@ -377,6 +394,13 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     if prefill is None:
         prefill = tokens * ku >= 192
     fused = w_up is None
+    if not prefill and act_q8:
+        if b_gate is not None or b_up is not None or b_down is not None or "+" in str(fmt):
+            raise L.LkError("the int8 expert matvecs take one gate/up format and no biases (gen_llm.py:5300-5302)")
+        fi = ids.reshape(-1)
+        act_ = moe_expert_mv_q8(fmt, "gu", fi, quant_q8(x), w_gu, f, h, ku, n_experts, fused=fused, w2=w_up, **ep)
+        ys = moe_expert_mv_q8(fmt_down or fmt, "dn", fi, quant_q8(act_), w_dn, h, f, ku, n_experts)
+        return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
     if not prefill:
         act_ = moe_expert_mv(fmt, "gu", ids.reshape(-1), x, w_gu, f, h, ku, n_experts, fused=fused, w2=w_up,
                              bias=b_gate, bias2=b_up, **ep)

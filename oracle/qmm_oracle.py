@@ -719,12 +719,13 @@ def moe_ffn_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, n_experts, act=ACT_SILU, alp
 
 
 def moe_ffn_q8_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, act=ACT_SILU, alpha=1.702, limit=7.0, b_gate=None,
-                   b_up=None, b_down=None, dsc=None, y0=None, sg=None):
+                   b_up=None, b_down=None, dsc=None, y0=None, sg=None, fmt_down=None):
     """The decode expert FFN on int8 activations, MOE_Q8=1 (gen_llm.py:5290-5302): x is quantised by g_quant_q8
     (quant_q8 above, gen_llm.py:683-750), the gate/up products of those codes with the dequantised weights are taken
     in float64, act = act(g + bg, u + bu) is rounded to f32 and quantised again per assignment row (the g_quant_q8
     launch on the gate/up output), the down products likewise (+ bd), then the weighted combine
-    y[t] = sg[t] y0[t] + sum_k wts[t,k] dsc[e] ys. w_gu[e] = the expert's gate rows then up rows (packed blocks)."""
+    y[t] = sg[t] y0[t] + sum_k wts[t,k] dsc[e] ys. w_gu[e] = the expert's gate rows then up rows (packed blocks);
+    w_dn in fmt_down when given."""
     xq = dequant_q8(*quant_q8(np.asarray(x, np.float32))).astype(np.float64)
     t, ku = ids.shape
     y = np.zeros((t, h), np.float64)
@@ -733,7 +734,7 @@ def moe_ffn_q8_ref(x, ids, wts, w_gu, w_dn, fmt, h, f, act=ACT_SILU, alpha=1.702
     w_eff = np.asarray(wts, np.float64) if dsc is None else wscale_ref(ids, wts, dsc).astype(np.float64)
     for e in np.unique(ids):
         gu = dequant(fmt, w_gu[e], h).reshape(2 * f, h).astype(np.float64)
-        dn = dequant(fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
+        dn = dequant(fmt_down or fmt, w_dn[e], f).reshape(h, f).astype(np.float64)
         for i, j in zip(*np.nonzero(ids == e)):
             pair = gu @ xq[i]
             g, u = pair[:f], pair[f:]

@@ -94,7 +94,8 @@ class TestMvQ8:
         assert ops.mv_q8("q4_k", w, xq, 4, 256, 0).shape == (0, 4)
 
 
-SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0], "iq4_nl": [0]}
+SCALE_OFFS = {"q5_0": [0], "q8_0": [0], "q5_k": [0, 2], "q6_k": [208], "iq4_xs": [0], "iq4_nl": [0], "q4_0": [0],
+              "q4_k": [0, 2]}
 GENERIC = ["q8_0", "q5_0", "q5_k", "q6_k", "iq4_nl", "iq4_xs"]
 
 
@@ -159,6 +160,44 @@ class TestMvQ8Generic:
         ys = ops.mv_q8_multi("q6_k", ws, xq, ns, k, tokens)
         for w, n, y in zip(ws, ns, ys):
             assert torch.equal(y, ops.mv_q8("q6_k", w, xq, n, k, tokens))
+
+
+class TestMoeExpertMvQ8:
+    """lk_moe_expert_mv_q8 (MOE_Q8 for every format with integer codes) through ops.moe_ffn(act_q8=True): routing,
+    quant_q8 of x, int8 gate/up with the activation, quant_q8 of the activations, int8 down, combine -- against the
+    float64 oracle of the same numerics (moe_ffn_q8_ref)."""
+
+    @pytest.mark.parametrize("fmt,fmt_down,fused,act", [("q6_k", None, True, "silu"), ("q4_k", "q6_k", False, "silu"),
+                                                        ("q5_k", "q8_0", True, "gelu"), ("q8_0", "q5_0", False, "silu"),
+                                                        ("q4_0", None, True, "swiglu_oai"), ("q5_0", "q4_k", True, "silu")])
+    @pytest.mark.parametrize("tokens", [1, 3])
+    def test_layer_vs_oracle(self, ops, fmt, fmt_down, fused, act, tokens):
+        E, ku, H, F = 8, 4, 512, 256
+        rng = np.random.default_rng(tokens * 10 + len(fmt))
+        fd = fmt_down or fmt
+        wg = np.stack([blocks(fmt, F, H, 100 + e) for e in range(E)])
+        wu = np.stack([blocks(fmt, F, H, 200 + e) for e in range(E)])
+        wd = np.stack([blocks(fd, H, F, 300 + e) for e in range(E)])
+        w_gu = np.concatenate([wg, wu], axis=1)   # per expert F gate rows then F up rows
+        x = rng.standard_normal((tokens, H)).astype(np.float32)
+        lg = rng.standard_normal((tokens, E)).astype(np.float32)
+        kw = dict(w_up=dev(wu)) if not fused else {}
+        y = host(ops.moe_ffn(fmt, dev(x), dev(lg), dev(wg if not fused else w_gu), dev(wd), H, F, E, ku,
+                             prefill=False, act=act, fmt_down=fmt_down, act_q8=True, **kw))
+        ids, wts = O.route_ref(lg, ku)
+        ref = O.moe_ffn_q8_ref(x, ids, wts, w_gu, wd, fmt, H, F, act={"silu": O.ACT_SILU, "gelu": O.ACT_GELU,
+                               "swiglu_oai": O.ACT_SWIGLU_OAI}[act], fmt_down=fd)
+        assert O.rel_l2(y, ref) < 1e-3, O.rel_l2(y, ref)
+        assert ops.device_status() == 0
+
+    def test_refusals(self, ops):
+        ids = torch.zeros(4, dtype=torch.int32, device="cuda")
+        xq = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+        w = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+        with pytest.raises(ops.L.LkError):   # no integer codes for IQ4 in the MoE (gen_llm.py:5300-5301)
+            ops.moe_expert_mv_q8("iq4_nl", "dn", ids, xq, w, 32, 256, 4, 8)
+        with pytest.raises(ops.L.LkError):   # gate/up: whole tokens of ku assignments
+            ops.moe_expert_mv_q8("q6_k", "gu", ids[:3], xq, w, 32, 256, 2, 8)
 
 
 class TestMvQ8Multi:
