@@ -385,6 +385,16 @@ def synth_blocks(torch, dev, rows, k, fmt, gen):
     return w.view(rows, -1)
 
 
+def synth_kquant(torch, dev, rows, k, fmt, gen):
+    """Q4_K / Q6_K super-blocks synthesised on the device: uniform bytes, the f16 scale(s) of the host forms."""
+    bb, offs = {"q4_k": (144, [(0, Q4K_D)]), "q6_k": (210, [(208, np.frombuffer(np.float16(2e-4).tobytes(), np.uint8))])}[fmt]
+    w = torch.randint(0, 256, (rows, k // 256, bb), dtype=torch.uint8, device=dev, generator=gen)
+    for o, b in offs:
+        for i, v in enumerate(b):
+            w[:, :, o + i] = int(v)
+    return w.view(rows, -1)
+
+
 def synth_mxfp4(torch, dev, rows, k, gen):
     """MXFP4 split planes synthesised on the device: uniform nibbles, E8M0 exponents 119..121 (N(0, 0.02) blocks)."""
     nib = torch.randint(0, 256, (rows, k // 2), dtype=torch.uint8, device=dev, generator=gen)
@@ -547,6 +557,28 @@ def bench_moe(args, torch, dev, time_steps, pk):
                      **moe_path(ops, torch, lg, E, ku, m, 3 * h * f * 18 // 32, ms, 192 // ku)}
     out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
                              "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
+    del w_gu, w_dn
+    # the same layer in a Q4_K_M-like mix (Q4_K gate/up, Q6_K down) at decode sizes: the reference's default MOE_Q8
+    # numerics (int8 expert matvecs, lk_moe_expert_mv_q8) beside the f32-activation expert matvecs
+    w_gu = synth_kquant(torch, dev, E * 2 * f, h, "q4_k", gen)
+    w_dn = synth_kquant(torch, dev, E * h, f, "q6_k", gen)
+    kq = {}
+    ebytes = 2 * f * h // 256 * 144 + h * f // 256 * 210
+    for m in (1, 4):
+        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
+        lg = torch.randn(m, E, device=dev, generator=gen)
+        row = {}
+        for name, q8 in (("int8", True), ("f32", False)):
+            g = Timed(torch, lambda: ops.moe_ffn("q4_k", x, lg, w_gu, w_dn, h, f, E, ku, prefill=False,
+                                                 fmt_down="q6_k", act_q8=q8))
+            for _ in range(3):
+                g.replay()
+            ms = time_steps(g.replay, 20)
+            row[name] = {"ms": round(ms, 4), **moe_path(ops, torch, lg, E, ku, m, ebytes, ms, 1 << 30)}
+        kq[str(m)] = row
+    out["q4_k_m_mix_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "gate_up": "q4_k",
+                                   "down": "q6_k", "by_tokens": kq,
+                                   "data": "Q4_K / Q6_K blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
     del w_gu, w_dn
     E, ku, h, f = 32, 4, 2880, 2880
     gu, gus = synth_mxfp4(torch, dev, E * 2 * f, h, gen)
