@@ -3,9 +3,10 @@
 // Replaces g_mv_{fmt}_k{K}[_t{TG}][_r{R}] and its swiglu pair (gen_llm.py:1159-1378) and the MoE expert matvecs
 // g_moe_gu_/g_moe_dn_ (gen_moe.py:535-727).
 //
-// Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, four 2-D TMA
-// boxes of the rows' packed bytes (16 rows x 144 bytes = 256 k each, 1024 k per stage) plus the matching slice of
-// each token's activations (1-D bulk copies) into a 4-stage shared-memory ring. Four consumer warps each take one 256-value chunk of every
+// Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, one 2-D TMA
+// box of the rows' packed bytes per consumer warp (16 rows x 144 bytes = 256 k each; 8 consumers for one token, 4 for
+// token tiles of 8) plus the matching slice of each token's activations (1-D bulk copies) into a 4-stage shared-memory
+// ring. Each consumer warp takes one 256-value chunk of every
 // stage: they convert their activation slice to f16 once (with per-32-value group sums), then unpack nibbles in
 // registers straight into the A fragments of warp-level f16 MMAs (16 rows x 16 k x 8 tokens) -- the weights never
 // go back to shared memory. Codes enter the MMA as exact small-integer f16 values, made from a (1024 + code) bit
@@ -19,14 +20,13 @@
 
 namespace lk {
 
-constexpr int kMvConsumers = 4;
-constexpr int kMvThreads = (kMvConsumers + 1) * 32;
+// consumer warps per CTA (CONS below; one 256-value chunk of each stage apiece): 8 for one token -- more warps in
+// flight per SM hide the TMA and decode latency -- and 4 for token tiles of 8, whose larger stages must fit
+constexpr int mv_consumers(int tok) { return tok == 1 ? 8 : 4; }
 constexpr int kMvRows = 16;
-constexpr int kMvStageChunks = 4;                               // 256-value chunks per stage, one per consumer
 // ring depth: 4 stages, or 2 when a stage is large (two weights and 8 f32 tokens) so the CTA fits shared memory
 constexpr int mv_stages(int stage_bytes) { return 4 * stage_bytes <= 150 * 1024 ? 4 : 2; }
 constexpr int kMvChunkTile = kMvRows * kChunkBytes;             // 2304: 16 rows x 144 bytes (one TMA box)
-constexpr int kMvWBytes = kMvStageChunks * kMvChunkTile;        // 9216: one weight's 4 chunk tiles per stage
 constexpr int kAcStride = 10;                                   // float2 stride of a row of the (a, c') table
 constexpr int kXStride = 272;                                   // f16 row stride of a consumer's x tile
 
@@ -269,9 +269,11 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
   }
 }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
-__global__ void __launch_bounds__(kMvThreads) k_mv(const __grid_constant__ CUtensorMap wmap,
-                                                   const __grid_constant__ CUtensorMap w2map, MvArgs a) {
+template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK, int CONS = mv_consumers(TOK)>
+__global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 : 2) k_mv(const __grid_constant__ CUtensorMap wmap,
+                                                        const __grid_constant__ CUtensorMap w2map, MvArgs a) {
+  constexpr int kMvConsumers = CONS, kMvStageChunks = CONS;
+  constexpr int kMvWBytes = kMvStageChunks * kMvChunkTile;   // one weight's chunk tiles per stage
   constexpr int NW = SWIGLU ? 2 : 1;
   constexpr int XE = XT == LK_F32 ? 4 : 2;                          // activation element bytes
   constexpr int kXStageBytes = TOK * kMvStageChunks * 256 * XE;     // raw activations per stage
@@ -409,6 +411,8 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int ele
 
 template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
 static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
+  constexpr int kMvConsumers = mv_consumers(TOK), kMvStageChunks = kMvConsumers;
+  constexpr int kMvWBytes = kMvStageChunks * kMvChunkTile;
   constexpr int NW = SWIGLU ? 2 : 1;
   constexpr int XE = XT == LK_F32 ? 4 : 2;
   constexpr int kStageBytes = NW * kMvWBytes + TOK * kMvStageChunks * 256 * XE;
@@ -421,7 +425,7 @@ static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs
   static unsigned configured = 0;
   if (!once_per_device(configured)) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((a.n + kMvRows - 1) / kMvRows, groups);
-  kern<<<grid, kMvThreads, smem, s>>>(wm, w2m, a);
+  kern<<<grid, (kMvConsumers + 1) * 32, smem, s>>>(wm, w2m, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
