@@ -4,8 +4,8 @@
 // g_moe_gu_/g_moe_dn_ (gen_moe.py:535-727).
 //
 // Design (HBM-bound). A CTA owns 16 weight rows and up to 8 tokens. A producer warp streams, per stage, one 2-D TMA
-// box of the rows' packed bytes per consumer warp (16 rows x 144 bytes = 256 k each; 8 consumers for one token, 4 for
-// token tiles of 8) plus the matching slice of each token's activations (1-D bulk copies) into a 4-stage shared-memory
+// box of the rows' packed bytes per consumer warp (16 rows x 144 bytes = 256 k each; 8 consumers for one dense token,
+// 4 otherwise) plus the matching slice of each token's activations (1-D bulk copies) into a 4-stage shared-memory
 // ring. Each consumer warp takes one 256-value chunk of every
 // stage: they convert their activation slice to f16 once (with per-32-value group sums), then unpack nibbles in
 // registers straight into the A fragments of warp-level f16 MMAs (16 rows x 16 k x 8 tokens) -- the weights never
@@ -20,9 +20,11 @@
 
 namespace lk {
 
-// consumer warps per CTA (CONS below; one 256-value chunk of each stage apiece): 8 for one token -- more warps in
-// flight per SM hide the TMA and decode latency -- and 4 for token tiles of 8, whose larger stages must fit
-constexpr int mv_consumers(int tok) { return tok == 1 ? 8 : 4; }
+// consumer warps per CTA (CONS below; one 256-value chunk of each stage apiece): 8 for one token of a dense matvec --
+// more warps in flight per SM hide the TMA and decode latency (measured: Q4_0 4096 x 4096 fp16 6.83 -> 5.98 us, the
+// bf16 decode step 1885 -> 1982 GB/s) -- and 4 for token tiles of 8, whose larger stages must fit, and for the MoE
+// expert matvecs, whose short rows (one stage at K = 2048) ran slower with 8 (27 -> 31 us for configs[2] at M = 1)
+constexpr int mv_consumers(int tok, bool moe) { return tok == 1 && !moe ? 8 : 4; }
 constexpr int kMvRows = 16;
 // ring depth: 4 stages, or 2 when a stage is large (two weights and 8 f32 tokens) so the CTA fits shared memory
 constexpr int mv_stages(int stage_bytes) { return 4 * stage_bytes <= 150 * 1024 ? 4 : 2; }
@@ -269,7 +271,7 @@ LK_DEV void mv_chunk(const uint8_t* rb0, const uint8_t* rb1, const __half* xt, c
   }
 }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK, int CONS = mv_consumers(TOK)>
+template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK, int CONS = mv_consumers(TOK, MOE)>
 __global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 : 2) k_mv(const __grid_constant__ CUtensorMap wmap,
                                                         const __grid_constant__ CUtensorMap w2map, MvArgs a) {
   constexpr int kMvConsumers = CONS, kMvStageChunks = CONS;
@@ -411,7 +413,7 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int ele
 
 template <int FMT, int XT, bool SWIGLU, bool MOE, int TOK>
 static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
-  constexpr int kMvConsumers = mv_consumers(TOK), kMvStageChunks = kMvConsumers;
+  constexpr int kMvConsumers = mv_consumers(TOK, MOE), kMvStageChunks = kMvConsumers;
   constexpr int kMvWBytes = kMvStageChunks * kMvChunkTile;
   constexpr int NW = SWIGLU ? 2 : 1;
   constexpr int XE = XT == LK_F32 ? 4 : 2;
