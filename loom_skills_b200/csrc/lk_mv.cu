@@ -15,6 +15,8 @@
 //     Q4_0 / IQ4_NL: sum_k d v_k x_k = d * D;   Q4_K: sum_k (a q_k - c) x_k = a * D - c * S,   S = sum x_k
 // with a = d*sc, c = dmin*m per group. Centred codes keep D free of the cancellation a (1024 + q) offset would cause:
 // the f32 accumulation of exact codes is as precise as the reference's f32 dequant-then-dot (gen_llm.py:1281-1357).
+#include <mutex>
+
 #include "lk_common.cuh"
 #include "lk_internal.h"
 
@@ -408,6 +410,119 @@ __global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Persistent one-token dense form (the decode step's shape): the same chunk math, with the activation row converted to
+// its f16 chunk tiles (and group sums) once per CTA instead of once per stage, and the CTAs walking 16-row blocks
+// round-robin, so the producer's TMA ring runs on across row blocks while the consumers finish the previous one.
+// Per row block the 8 consumer warps' partial sums meet in shared memory; warp 0 stores the 16 outputs.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kRowsCons = 8;
+template <bool SWIGLU>
+constexpr int rows_stages() { return SWIGLU ? 2 : 3; }
+
+template <int FMT, int XT, bool SWIGLU>
+__global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
+    k_mv_rows(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap w2map, MvArgs a) {
+  constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
+  constexpr int kWB = kRowsCons * kMvChunkTile;                     // one weight's chunk tiles per stage
+  constexpr int kStageBytes = NW * kWB;
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kXStride;            // f16 elements of one chunk's x tile(s)
+  constexpr int XE = XT == LK_F32 ? 4 : 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * kStageBytes);
+  uint64_t* empty = full + NST;
+  float2* actab_all = reinterpret_cast<float2*>(empty + NST);                                  // [cons][NW][16][st]
+  float* red = reinterpret_cast<float*>(actab_all + kRowsCons * NW * 16 * kAcStride);        // [cons][NW][32][4]
+  float* S_all = red + kRowsCons * NW * 32 * 4;                                               // [kchunks][8]
+  const int kchunks = a.k / kChunkValues;
+  __half* xt_all = reinterpret_cast<__half*>(S_all + kchunks * 8);                          // [kchunks][kXT]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nblk = (a.n + kMvRows - 1) / kMvRows;
+  const int nstages = (kchunks + kRowsCons - 1) / kRowsCons;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRowsCons);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == kRowsCons) {   // producer: stage (block, st) = chunks [8 st, 8 st + 8) of the block's 16 rows
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+      int i = 0;
+      for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        for (int st = 0; st < nstages; ++st, ++i) {
+          const int s = i % NST;
+          if (i >= NST && !mbar_wait(&empty[s], ((i / NST) - 1) & 1)) atomicOr(&g_status, 1u);
+          const int c0 = st * kRowsCons, nch = min(kRowsCons, kchunks - c0);
+          mbar_expect_tx(&full[s], uint32_t(NW * nch * kMvChunkTile));
+          uint8_t* stg = smem + s * kStageBytes;
+          for (int c = 0; c < nch; ++c) {
+            tma_load_2d(stg + c * kMvChunkTile, &wmap, (c0 + c) * (kChunkBytes / 4), blk * kMvRows, &full[s]);
+            if (NW == 2)
+              tma_load_2d(stg + kWB + c * kMvChunkTile, &w2map, (c0 + c) * (kChunkBytes / 4),
+                          a.w2_row_offset + blk * kMvRows, &full[s]);
+          }
+        }
+      }
+    }
+    return;
+  }
+  // consumers: the activation row as f16 chunk tiles and group sums, once
+  for (int c = warp; c < kchunks; c += kRowsCons)
+    stage_x<XT, 1>(static_cast<const uint8_t*>(a.x) + int64_t(c) * 256 * XE, 0, 1, lane, xt_all + c * kXT,
+                   xt_all + c * kXT + kXStride, S_all + c * 8);
+  asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+  const int g = lane >> 2, tig = lane & 3;
+  float2* actab = actab_all + warp * NW * 16 * kAcStride;
+  int i = 0;
+  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    float acc[NW][4];
+#pragma unroll
+    for (int wi = 0; wi < NW; ++wi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[wi][e] = 0.f;
+    for (int st = 0; st < nstages; ++st, ++i) {
+      const int s = i % NST;
+      if (!mbar_wait(&full[s], (i / NST) & 1)) atomicOr(&g_status, 1u);
+      const int c = st * kRowsCons + warp;
+      if (c < kchunks) {
+        const uint8_t* rb0 = smem + s * kStageBytes + warp * kMvChunkTile;
+        mv_chunk<FMT, XT, NW, 1>(rb0, rb0 + kWB, xt_all + c * kXT, xt_all + c * kXT + kXStride, S_all + c * 8, g == 0,
+                                 g, tig, lane, actab, acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int wi = 0; wi < NW; ++wi)
+      *reinterpret_cast<float4*>(red + ((warp * NW + wi) * 32 + lane) * 4) =
+          make_float4(acc[wi][0], acc[wi][1], acc[wi][2], acc[wi][3]);
+    asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+    if (warp == 0 && tig == 0) {   // token 0: elements 0 (row g) and 2 (row g + 8)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = blk * kMvRows + g + 8 * h;
+        float out[NW];
+#pragma unroll
+        for (int wi = 0; wi < NW; ++wi) {
+          float sum = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRowsCons; ++w) sum += red[((w * NW + wi) * 32 + lane) * 4 + 2 * h];
+          out[wi] = sum;
+        }
+        if (row < a.n) {
+          const float v = SWIGLU ? act_apply(a.epi.act, out[0], out[NW - 1], a.epi.alpha, a.epi.limit) : out[0];
+          a.y[row] = a.accumulate ? a.y[row] + v : v;
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");   // red is rewritten by the next block
+  }
+}
+
 int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, int64_t rows, int64_t cols,
              int box_cols, int box_rows, CUtensorMapSwizzle swz);
 
@@ -431,8 +546,43 @@ static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
+template <int FMT, int XT, bool SWIGLU>
+static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, cudaStream_t s) {
+  constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kXStride;
+  const int kchunks = a.k / kChunkValues;
+  const int smem = NST * NW * kRowsCons * kMvChunkTile + 2 * NST * 8 + kRowsCons * NW * 16 * kAcStride * 8 +
+                   kRowsCons * NW * 32 * 4 * 4 + kchunks * 8 * 4 + kchunks * kXT * 2;
+  if (smem > 200 * 1024) return LK_EUNSUPPORTED;   // rows past ~40k values: the per-stage form below
+  auto kern = k_mv_rows<FMT, XT, SWIGLU>;
+  static int configured[32] = {};   // the largest shared-memory size set per device
+  static std::mutex mu;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 32) return LK_EUNSUPPORTED;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[dev] < smem) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+      configured[dev] = smem;
+    }
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (kRowsCons + 1) * 32, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int nblk = (a.n + kMvRows - 1) / kMvRows;
+  kern<<<min(nblk, per_sm * sms), (kRowsCons + 1) * 32, smem, s>>>(wm, w2m, a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
 template <int FMT, int XT>
 static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
+  if (!a.ids && a.tokens == 1) {   // the decode step's shape: the persistent form where its shared memory fits
+    const int rc = a.swiglu ? launch_mv_rows<FMT, XT, true>(wm, w2m, a, s) : launch_mv_rows<FMT, XT, false>(wm, w2m, a, s);
+    if (rc != LK_EUNSUPPORTED) return rc;
+  }
   if (a.ids) {
     if (a.swiglu) return launch_mv<FMT, XT, true, true, 1>(wm, w2m, a, groups, s);
     return launch_mv<FMT, XT, false, true, 1>(wm, w2m, a, groups, s);

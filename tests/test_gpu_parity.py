@@ -146,6 +146,23 @@ class TestMv:
             y = host(ops.mv("q4_k", dev(w), xt, n, k))
             assert O.rel_l2(y, O.mv_ref("q4_k", w, xt.float().cpu().numpy(), n, k)) < TOL
 
+    @pytest.mark.parametrize("fmt,xdt,n,k", [("q4_k", "f32", 1000, 12288), ("q4_0", "bf16", 4104, 4096),
+                                             ("iq4_nl", "f16", 130, 2304), ("q4_k", "bf16", 24576, 4096)])
+    def test_one_token_row_blocks(self, ops, fmt, xdt, n, k):
+        # the persistent one-token form: several 16-row blocks per CTA, a last partial block and a partial last stage,
+        # swiglu with accumulate, and the plain product
+        w, w2 = weights(fmt, n, k, 41), weights(fmt, n, k, 42)
+        x = np.random.default_rng(43).standard_normal((1, k)).astype(np.float32)
+        xt = dev(x).to({"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[xdt])
+        xh = xt.float().cpu().numpy()
+        y = host(ops.mv(fmt, dev(w), xt, n, k))
+        assert O.rel_l2(y, O.mv_ref(fmt, w, xh, n, k)) < TOL
+        y0 = np.random.default_rng(44).standard_normal((1, n)).astype(np.float32)
+        yt = dev(y0)
+        ops.mv(fmt, dev(w), xt, n, k, w2=dev(w2), y=yt, accumulate=True)
+        assert O.rel_l2(host(yt), O.mv_ref(fmt, w, xh, n, k, w2=w2, y_old=y0)) < TOL
+        assert ops.device_status() == 0
+
     def test_device_status_clear(self, ops):
         assert ops.device_status() == 0
 
