@@ -910,7 +910,8 @@ def run_profile_case(args):
     N=4096, f32 x), gemm_q6k (the window-producer GEMM, Q6_K M=2048 K=4096 N=4096), moeq8 (the int8 decode MoE layer
     of configs[2] at one token: E=128 top-8, H=2048, F=768, Q4_0), mvp_gate_up / gemmp_gate_up (a Q4_K gate and Q6_K
     up pair, K=4096 N=12288: the one-token matvec on bf16 x, and the swiglu GEMM at M=2048), mvq8_q6k_down (the int8
-    matvec over Q6_K, K=12288 N=4096)."""
+    matvec over Q6_K, K=12288 N=4096), mv_bf16_gate_up (the persistent one-token matvec on bf16 x, Q4_K K=4096
+    N=24576)."""
     import torch
 
     from loom_skills_b200 import ops
@@ -959,6 +960,12 @@ def run_profile_case(args):
         y = torch.empty(1, h, device=dev)
         act = torch.empty(ku, f, device=dev)
         fn = lambda: ops.moe_ffn_decode_q8("q4_0", x, lg, wgu, wdn, h, f, E, ku, y=y, act_buf=act)   # noqa: E731
+    elif case == "mv_bf16_gate_up":
+        k, n = 4096, 24576
+        w = torch.from_numpy(synth_q4k(rng, n, k)).to(dev)
+        x = torch.randn(1, k, device=dev).to(torch.bfloat16)
+        y = torch.empty(1, n, device=dev)
+        fn = lambda: ops.mv("q4_k", w, x, n, k, y=y)   # noqa: E731
     elif case == "mvq8_q6k_down":
         k, n = 12288, 4096
         w = torch.from_numpy(synth_q6k(rng, n, k)).to(dev)

@@ -93,11 +93,12 @@ LK_DEV uint32_t hfma2u(uint32_t a, __half2 b, __half2 c) {
 // load past the end stays inside the CTA's shared memory: the row windows are followed by the staging buffers)
 template <int N>
 LK_DEV void ld_words_2a(const uint8_t* p, uint32_t (&w)[N]) {
-  const uint32_t* q = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
-  const uint32_t sh = uint32_t(reinterpret_cast<uintptr_t>(p) & 3u) * 8u;
+  // explicit shared-memory loads: the aligned address is formed as an integer, and a generic load through it would
+  // not be known to be shared
+  const uint32_t a = smem_u32(p), base = a & ~3u, sh = (a & 3u) * 8u;
   uint32_t v[N + 1];
 #pragma unroll
-  for (int i = 0; i <= N; ++i) v[i] = q[i];
+  for (int i = 0; i <= N; ++i) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v[i]) : "r"(base + 4u * i));
 #pragma unroll
   for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
 }

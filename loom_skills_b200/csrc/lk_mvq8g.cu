@@ -10,7 +10,7 @@
 // k_mvq8g: a producer warp streams stages of (8 rows) x (a chunk of 2048 values) into a 4-slot shared-memory ring --
 // one bulk copy per row of the 16-byte-aligned window around the row's chunk bytes, since these blocks (34, 22, 176,
 // 210, 18, 136 bytes) start at any even offset -- and 8 consumer warps take one row each: lane l decodes the groups
-// l, l + 32, ... of the chunk from shared memory (2-byte loads), reads the activation codes of up to 8 tokens from
+// l, l + 32, ... of the chunk from shared memory (aligned word loads realigned by funnel shifts), reads the activation codes of up to 8 tokens from
 // global memory (the whole row of codes is shared by every warp: it stays in L1), and runs 8 dp4a per group and token.
 // A CTA walks whole row blocks (all chunks of 8 rows) so each row's sum stays in registers; the first stage is
 // requested before griddepcontrol.wait (the weights never depend on the previous kernel).
@@ -31,12 +31,19 @@ constexpr int kGChunk = 2048;                // values of a row per stage
 LK_DEV void gq_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 LK_DEV void gq_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// a little-endian word from a 2-byte aligned address in shared memory
-LK_DEV uint32_t ld32_2a(const uint8_t* p) {
-  const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-  return uint32_t(q[0]) | (uint32_t(q[1]) << 16);
-}
 LK_DEV float f16_2a(const uint8_t* p) { return h2f(*reinterpret_cast<const uint16_t*>(p)); }
+// N little-endian words from a 2-byte aligned shared-memory address: N + 1 explicit shared loads of the aligned words
+// around them and funnel shifts (the load past the end stays inside the CTA's shared memory: every row window has
+// slack behind it, then the barriers)
+template <int N>
+LK_DEV void ldw(const uint8_t* p, uint32_t (&w)[N]) {
+  const uint32_t a = smem_u32(p), base = a & ~3u, sh = (a & 3u) * 8u;
+  uint32_t v[N + 1];
+#pragma unroll
+  for (int i = 0; i <= N; ++i) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v[i]) : "r"(base + 4u * i));
+#pragma unroll
+  for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(v[i], v[i + 1], sh);
+}
 
 // The int8 codes of one 32-value group (word i = values 4i..4i+3, one per byte) and its factors: sc the scale, mn
 // the minimum (Q5_0, Q5_K) or the second 16 values' scale (Q6_K)
@@ -57,32 +64,33 @@ template <int FMT>
 LK_DEV void group_icodes(const uint8_t* b, int j, ICodes& o) {
   if (FMT == LK_Q4_0) {   // gen_llm.py:536-552: nibbles 0..15, minimum 8 d
     const float d = f16_2a(b);
+    uint32_t q[4];
+    ldw(b + 2, q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t q = ld32_2a(b + 2 + 4 * (i & 3));
-      o.w[i] = (i < 4 ? q : q >> 4) & 0x0F0F0F0Fu;
-    }
+    for (int i = 0; i < 8; ++i) o.w[i] = (i < 4 ? q[i] : q[i - 4] >> 4) & 0x0F0F0F0Fu;
     o.sc = d;
     o.mn = 8.0f * d;
   } else if (FMT == LK_Q4_K) {   // gen_llm.py:554-577: the nibble page of group j, scale d sc, minimum dmin m
-    uint32_t sc, m;
-    q4k_scale_min_w(ld32_2a(b + 4), ld32_2a(b + 8), ld32_2a(b + 12), j, sc, m);
-    o.sc = f16_2a(b) * float(sc);
-    o.mn = f16_2a(b + 2) * float(m);
-    const uint8_t* qs = b + 16 + 32 * (j >> 1);
+    uint32_t sc, m, hd[4], qs[8];
+    ldw(b, hd);
+    q4k_scale_min_w(hd[1], hd[2], hd[3], j, sc, m);
+    o.sc = h2f(uint16_t(hd[0] & 0xffffu)) * float(sc);
+    o.mn = h2f(uint16_t(hd[0] >> 16)) * float(m);
+    ldw(b + 16 + 32 * (j >> 1), qs);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o.w[i] = (ld32_2a(qs + 4 * i) >> (4 * (j & 1))) & 0x0F0F0F0Fu;
+    for (int i = 0; i < 8; ++i) o.w[i] = (qs[i] >> (4 * (j & 1))) & 0x0F0F0F0Fu;
   } else if (FMT == LK_Q8_0) {   // gen_llm.py:523-534: int8 codes, scale d
     o.sc = f16_2a(b);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o.w[i] = ld32_2a(b + 2 + 4 * i);
+    ldw(b + 2, o.w);
     o.mn = 0.f;
   } else if (FMT == LK_Q5_0) {   // gen_llm.py:943-985: nibble | bit i of qh << 4 (0..31), minimum 16 d
     const float d = f16_2a(b);
-    const uint32_t qh = ld32_2a(b + 2);
+    uint32_t hq[5];   // qh, then the 16 nibble bytes
+    ldw(b + 2, hq);
+    const uint32_t qh = hq[0];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t q = ld32_2a(b + 6 + 4 * (i & 3));
+      const uint32_t q = hq[1 + (i & 3)];
       const uint32_t hb = (qh >> (4 * i)) & 15u;
       o.w[i] = ((i < 4 ? q : q >> 4) & 0x0F0F0F0Fu) |
                ((hb & 1u) << 4) | ((hb & 2u) << 11) | ((hb & 4u) << 18) | ((hb & 8u) << 25);
@@ -90,25 +98,29 @@ LK_DEV void group_icodes(const uint8_t* b, int j, ICodes& o) {
     o.sc = d;
     o.mn = 16.0f * d;
   } else if (FMT == LK_Q5_K) {   // gen_llm.py:579-615: Q4_K's nibbles | bit j of qh[l] << 4, scale d sc, minimum dmin m
-    uint32_t sc, m;
-    q4k_scale_min_w(ld32_2a(b + 4), ld32_2a(b + 8), ld32_2a(b + 12), j, sc, m);
-    o.sc = f16_2a(b) * float(sc);
-    o.mn = f16_2a(b + 2) * float(m);
-    const uint8_t* qs = b + 48 + 32 * (j >> 1);
+    uint32_t sc, m, hd[4], qh[8], qs[8];
+    ldw(b, hd);
+    q4k_scale_min_w(hd[1], hd[2], hd[3], j, sc, m);
+    o.sc = h2f(uint16_t(hd[0] & 0xffffu)) * float(sc);
+    o.mn = h2f(uint16_t(hd[0] >> 16)) * float(m);
+    ldw(b + 16, qh);
+    ldw(b + 48 + 32 * (j >> 1), qs);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      o.w[i] = ((ld32_2a(qs + 4 * i) >> (4 * (j & 1))) & 0x0F0F0F0Fu) |
-               (((ld32_2a(b + 16 + 4 * i) >> j) & 0x01010101u) << 4);
+      o.w[i] = ((qs[i] >> (4 * (j & 1))) & 0x0F0F0F0Fu) | (((qh[i] >> j) & 0x01010101u) << 4);
   } else if (FMT == LK_Q6_K) {   // gen_llm.py:617-680: signed (q - 32), d sc of each 16 values
     const int half = j >> 2, jj = j & 3;
     const uint8_t* ql = b + 64 * half + 32 * (jj & 1);
     const uint8_t* qh = b + 128 + 32 * half;
     const uint8_t* sc = b + 192 + 8 * half + 2 * jj;
     const float d = f16_2a(b + 208);
+    uint32_t wl[8], wh[8];
+    ldw(ql, wl);
+    ldw(qh, wh);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t c = ((ld32_2a(ql + 4 * i) >> (4 * (jj >> 1))) & 0x0F0F0F0Fu) |
-                         (((ld32_2a(qh + 4 * i) >> (2 * jj)) & 0x03030303u) << 4);   // 0..63 per byte
+      const uint32_t c = ((wl[i] >> (4 * (jj >> 1))) & 0x0F0F0F0Fu) |
+                         (((wh[i] >> (2 * jj)) & 0x03030303u) << 4);   // 0..63 per byte
       // c - 32 per byte: flip bit 5; bytes below 32 also get bits 6 and 7 (their two's complement)
       o.w[i] = (c ^ 0x20202020u) | ((~c & 0x20202020u) * 7u);
     }
@@ -125,11 +137,11 @@ LK_DEV void group_icodes(const uint8_t* b, int j, ICodes& o) {
       o.sc = f16_2a(b) * float(ls - 32);
       qs = b + 8 + 16 * j;
     }
+    uint32_t q[4];
+    ldw(qs, q);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t q = ld32_2a(qs + 4 * (i & 3));
-      o.w[i] = iq4_lookup4((i < 4 ? q : q >> 4) & 0x0F0F0F0Fu) ^ 0x80808080u;   // biased table bytes -> int8
-    }
+    for (int i = 0; i < 8; ++i)
+      o.w[i] = iq4_lookup4((i < 4 ? q[i] : q[i - 4] >> 4) & 0x0F0F0F0Fu) ^ 0x80808080u;   // biased bytes -> int8
     o.mn = 0.f;
   }
 }
