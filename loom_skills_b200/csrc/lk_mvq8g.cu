@@ -187,7 +187,7 @@ struct GqArgs {
 enum { kGDense = 0, kGMoeDn = 1, kGMoeGu = 2 };
 
 template <int FMT, int NT, int MODE>
-__global__ void __launch_bounds__(kGThreads, 3) k_mvq8g(const GqArgs a) {
+__global__ void __launch_bounds__(kGThreads, 4) k_mvq8g(const GqArgs a) {
   constexpr int gpb = fmt_qk(FMT) / 32;   // 32-value groups per block
   constexpr int bb = fmt_block_bytes(FMT);
   constexpr int NW = MODE == kGMoeGu ? 2 : 1;   // weights per row block (gate and up)
