@@ -535,6 +535,23 @@ def moe_path(ops, torch, lg, E, ku, m, expert_bytes, ms, matvec_below=64):
             "weight_gbs": round(eu * expert_bytes / (ms * 1e-3) / 1e9, 1)}
 
 
+def moe_inputs(torch, dev, gen, m, h, E):
+    """The (x, logits) pairs one timed MoE step walks: at decode sizes (m <= 32) 8 different routings, so the experts a
+    step touches (8 x the routing's) exceed the L2 and every expert streams from HBM; one pair for larger m, where
+    all experts are touched."""
+    r = 8 if m <= 32 else 1
+    return [(torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16), torch.randn(m, E, device=dev, generator=gen))
+            for _ in range(r)]
+
+
+def timed_layers(torch, time_steps, pairs, layer):
+    """ms per MoE layer over the pairs (one CUDA graph runs `layer` once per pair)."""
+    g = Timed(torch, lambda: [layer(x, lg) for x, lg in pairs])
+    for _ in range(3):
+        g.replay()
+    return time_steps(g.replay, 20) / len(pairs)
+
+
 def bench_moe(args, torch, dev, time_steps, pk):
     """configs[2] (Q4_0 MoE, Qwen3-30B-A3B-like) and configs[3] (MXFP4 x e4m3 MoE, gpt-oss-20b-like): one MoE layer
     (route, schedule, expert GEMMs / matvecs, combine) per step as a CUDA graph; plus the dense MXFP4 x FP8 GEMM."""
@@ -547,14 +564,11 @@ def bench_moe(args, torch, dev, time_steps, pk):
     w_dn = synth_blocks(torch, dev, E * h, f, "q4_0", gen)
     q = {}
     for m in (1, 16, 256, 4096):
-        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
-        lg = torch.randn(m, E, device=dev, generator=gen)
-        g = Timed(torch, lambda: ops.moe_ffn("q4_0", x, lg, w_gu, w_dn, h, f, E, ku))
-        for _ in range(3):
-            g.replay()
-        ms = time_steps(g.replay, 20)
+        pairs = moe_inputs(torch, dev, gen, m, h, E)
+        ms = timed_layers(torch, time_steps, pairs, lambda x, lg: ops.moe_ffn("q4_0", x, lg, w_gu, w_dn, h, f, E, ku))
         q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
-                     **moe_path(ops, torch, lg, E, ku, m, 3 * h * f * 18 // 32, ms, 192 // ku)}
+                     "routings_per_step": len(pairs),
+                     **moe_path(ops, torch, pairs[0][1], E, ku, m, 3 * h * f * 18 // 32, ms, 192 // ku)}
     out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
                              "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
     del w_gu, w_dn
@@ -565,16 +579,13 @@ def bench_moe(args, torch, dev, time_steps, pk):
     kq = {}
     ebytes = 2 * f * h // 256 * 144 + h * f // 256 * 210
     for m in (1, 4):
-        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
-        lg = torch.randn(m, E, device=dev, generator=gen)
-        row = {}
+        pairs = moe_inputs(torch, dev, gen, m, h, E)
+        row = {"routings_per_step": len(pairs)}
         for name, q8 in (("int8", True), ("f32", False)):
-            g = Timed(torch, lambda: ops.moe_ffn("q4_k", x, lg, w_gu, w_dn, h, f, E, ku, prefill=False,
-                                                 fmt_down="q6_k", act_q8=q8))
-            for _ in range(3):
-                g.replay()
-            ms = time_steps(g.replay, 20)
-            row[name] = {"ms": round(ms, 4), **moe_path(ops, torch, lg, E, ku, m, ebytes, ms, 1 << 30)}
+            ms = timed_layers(torch, time_steps, pairs,
+                              lambda x, lg: ops.moe_ffn("q4_k", x, lg, w_gu, w_dn, h, f, E, ku, prefill=False,
+                                                        fmt_down="q6_k", act_q8=q8))
+            row[name] = {"ms": round(ms, 4), **moe_path(ops, torch, pairs[0][1], E, ku, m, ebytes, ms, 1 << 30)}
         kq[str(m)] = row
     out["q4_k_m_mix_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "gate_up": "q4_k",
                                    "down": "q6_k", "by_tokens": kq,
@@ -590,14 +601,12 @@ def bench_moe(args, torch, dev, time_steps, pk):
     oai = dict(gating=3, router_bias=rbias, norm=False, act="swiglu_oai", b_gate=bg, b_up=bu, b_down=bd)
     mx = {}
     for m in (1, 32, 1024, 8192):
-        x = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
-        lg = torch.randn(m, E, device=dev, generator=gen)
-        g = Timed(torch, lambda: ops.moe_ffn_mxfp4s(x, lg, gu, gus, dn, dns, h, f, E, ku, **oai))
-        for _ in range(3):
-            g.replay()
-        ms = time_steps(g.replay, 20)
+        pairs = moe_inputs(torch, dev, gen, m, h, E)
+        ms = timed_layers(torch, time_steps, pairs,
+                          lambda x, lg: ops.moe_ffn_mxfp4s(x, lg, gu, gus, dn, dns, h, f, E, ku, **oai))
         mx[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
-                      **moe_path(ops, torch, lg, E, ku, m, 3 * h * f // 2 + 3 * h * f // 32, ms, 16 // ku + 1)}
+                      "routings_per_step": len(pairs),
+                      **moe_path(ops, torch, pairs[0][1], E, ku, m, 3 * h * f // 2 + 3 * h * f // 32, ms, 16 // ku + 1)}
     # the dense kernel alone: fused gate/up shape, M=8192
     M = 8192
     x8, s8 = ops.row_scale_f8(torch.randn(M, h, device=dev, generator=gen))
