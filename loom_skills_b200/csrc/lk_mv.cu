@@ -415,12 +415,16 @@ __global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 
 // its f16 chunk tiles (and group sums) once per CTA instead of once per stage, and the CTAs walking 16-row blocks
 // round-robin, so the producer's TMA ring runs on across row blocks while the consumers finish the previous one.
 // Per row block the 8 consumer warps' partial sums meet in shared memory; warp 0 stores the 16 outputs.
+// MOE: per-assignment expert matvecs: the blocks are (assignment, 16-row block) pairs, each block's rows taken from
+// its assignment's expert, with the expert epilogue (biases, activation). The activation row is the one token's for
+// every assignment (the gate/up matvecs of one decode token), or with XPER the assignment's own row (the down
+// matvecs), converted again whenever a CTA's next block belongs to another assignment.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRowsCons = 8;
 template <bool SWIGLU>
 constexpr int rows_stages() { return SWIGLU ? 2 : 3; }
 
-template <int FMT, int XT, bool SWIGLU>
+template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER>
 __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
     k_mv_rows(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap w2map, MvArgs a) {
   constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
@@ -437,8 +441,15 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
   const int kchunks = a.k / kChunkValues;
   __half* xt_all = reinterpret_cast<__half*>(S_all + kchunks * 8);                          // [kchunks][kXT]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nblk = (a.n + kMvRows - 1) / kMvRows;
+  const int nrb = (a.n + kMvRows - 1) / kMvRows;           // 16-row blocks of one output row
+  const int nblk = MOE ? a.tokens * nrb : nrb;              // MoE: a.tokens = assignments
   const int nstages = (kchunks + kRowsCons - 1) / kRowsCons;
+  // block blk: its expert (MoE), first weight row in w and w2, first output row
+  auto expert_of = [&](int blk) { return MOE ? min(max(__ldg(a.ids + blk / nrb), 0), a.n_experts - 1) : 0; };
+  auto wrow_of = [&](int blk) { return expert_of(blk) * a.rows_per_expert + (blk % nrb) * kMvRows; };
+  auto w2row_of = [&](int blk) {
+    return expert_of(blk) * a.rows_per_expert2 + a.w2_row_offset + (blk % nrb) * kMvRows;
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
@@ -453,6 +464,7 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
       if (NW == 2) prefetch_tensormap(&w2map);
       int i = 0;
       for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        const int wr = wrow_of(blk), w2r = NW == 2 ? w2row_of(blk) : 0;
         for (int st = 0; st < nstages; ++st, ++i) {
           const int s = i % NST;
           if (i >= NST && !mbar_wait(&empty[s], ((i / NST) - 1) & 1)) atomicOr(&g_status, 1u);
@@ -460,25 +472,32 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
           mbar_expect_tx(&full[s], uint32_t(NW * nch * kMvChunkTile));
           uint8_t* stg = smem + s * kStageBytes;
           for (int c = 0; c < nch; ++c) {
-            tma_load_2d(stg + c * kMvChunkTile, &wmap, (c0 + c) * (kChunkBytes / 4), blk * kMvRows, &full[s]);
+            tma_load_2d(stg + c * kMvChunkTile, &wmap, (c0 + c) * (kChunkBytes / 4), wr, &full[s]);
             if (NW == 2)
-              tma_load_2d(stg + kWB + c * kMvChunkTile, &w2map, (c0 + c) * (kChunkBytes / 4),
-                          a.w2_row_offset + blk * kMvRows, &full[s]);
+              tma_load_2d(stg + kWB + c * kMvChunkTile, &w2map, (c0 + c) * (kChunkBytes / 4), w2r, &full[s]);
           }
         }
       }
     }
     return;
   }
-  // consumers: the activation row as f16 chunk tiles and group sums, once
-  for (int c = warp; c < kchunks; c += kRowsCons)
-    stage_x<XT, 1>(static_cast<const uint8_t*>(a.x) + int64_t(c) * 256 * XE, 0, 1, lane, xt_all + c * kXT,
-                   xt_all + c * kXT + kXStride, S_all + c * 8);
-  asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+  // consumers: the activation row as f16 chunk tiles and group sums (once, or per assignment with XPER)
+  auto stage_row = [&](int xrow) {
+    for (int c = warp; c < kchunks; c += kRowsCons)
+      stage_x<XT, 1>(static_cast<const uint8_t*>(a.x) + (int64_t(xrow) * a.k + int64_t(c) * 256) * XE, 0, 1, lane,
+                     xt_all + c * kXT, xt_all + c * kXT + kXStride, S_all + c * 8);
+    asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+  };
+  if (!XPER) stage_row(0);
+  int staged = -1;   // the assignment whose row the tiles hold (XPER)
   const int g = lane >> 2, tig = lane & 3;
   float2* actab = actab_all + warp * NW * 16 * kAcStride;
   int i = 0;
   for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    if (XPER && blk / nrb != staged) {   // the previous block's last bar.sync has every warp done with the old tiles
+      staged = blk / nrb;
+      stage_row(staged);
+    }
     float acc[NW][4];
 #pragma unroll
     for (int wi = 0; wi < NW; ++wi)
@@ -504,7 +523,7 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
     if (warp == 0 && tig == 0) {   // token 0: elements 0 (row g) and 2 (row g + 8)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int row = blk * kMvRows + g + 8 * h;
+        const int row = (blk % nrb) * kMvRows + g + 8 * h;
         float out[NW];
 #pragma unroll
         for (int wi = 0; wi < NW; ++wi) {
@@ -514,8 +533,14 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
           out[wi] = sum;
         }
         if (row < a.n) {
+          if (MOE && a.epi.bias) {   // per-expert output biases (gen_moe.py:535 expert_mv bias=True)
+            const int e = expert_of(blk);
+            out[0] += __ldg(a.epi.bias + int64_t(e) * a.n + row);
+            if (SWIGLU) out[NW - 1] += __ldg(a.epi.bias2 + int64_t(e) * a.n + row);
+          }
           const float v = SWIGLU ? act_apply(a.epi.act, out[0], out[NW - 1], a.epi.alpha, a.epi.limit) : out[0];
-          a.y[row] = a.accumulate ? a.y[row] + v : v;
+          float* yp = a.y + (MOE ? int64_t(blk / nrb) * a.n : 0) + row;
+          *yp = a.accumulate ? *yp + v : v;
         }
       }
     }
@@ -546,7 +571,7 @@ static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
-template <int FMT, int XT, bool SWIGLU>
+template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER = false>
 static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, cudaStream_t s) {
   constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
   constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kXStride;
@@ -554,7 +579,7 @@ static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const M
   const int smem = NST * NW * kRowsCons * kMvChunkTile + 2 * NST * 8 + kRowsCons * NW * 16 * kAcStride * 8 +
                    kRowsCons * NW * 32 * 4 * 4 + kchunks * 8 * 4 + kchunks * kXT * 2;
   if (smem > 200 * 1024) return LK_EUNSUPPORTED;   // rows past ~40k values: the per-stage form below
-  auto kern = k_mv_rows<FMT, XT, SWIGLU>;
+  auto kern = k_mv_rows<FMT, XT, SWIGLU, MOE, XPER>;
   static int configured[32] = {};   // the largest shared-memory size set per device
   static std::mutex mu;
   int dev = 0, sms = 0;
@@ -572,7 +597,7 @@ static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const M
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (kRowsCons + 1) * 32, smem) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
-  const int nblk = (a.n + kMvRows - 1) / kMvRows;
+  const int nblk = (a.n + kMvRows - 1) / kMvRows * (MOE ? a.tokens : 1);
   kern<<<min(nblk, per_sm * sms), (kRowsCons + 1) * 32, smem, s>>>(wm, w2m, a);
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
@@ -580,7 +605,16 @@ static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const M
 template <int FMT, int XT>
 static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
   if (!a.ids && a.tokens == 1) {   // the decode step's shape: the persistent form where its shared memory fits
-    const int rc = a.swiglu ? launch_mv_rows<FMT, XT, true>(wm, w2m, a, s) : launch_mv_rows<FMT, XT, false>(wm, w2m, a, s);
+    const int rc = a.swiglu ? launch_mv_rows<FMT, XT, true, false>(wm, w2m, a, s)
+                            : launch_mv_rows<FMT, XT, false, false>(wm, w2m, a, s);
+    if (rc != LK_EUNSUPPORTED) return rc;
+  }
+  if (a.ids && a.swiglu && a.x_div == a.tokens) {   // the gate/up expert matvecs of one token: all read x row 0
+    const int rc = launch_mv_rows<FMT, XT, true, true>(wm, w2m, a, s);
+    if (rc != LK_EUNSUPPORTED) return rc;
+  }
+  if (a.ids && !a.swiglu && a.x_div == 1 && a.tokens <= 64) {   // the down matvecs at decode sizes: row a of x each
+    const int rc = launch_mv_rows<FMT, XT, false, true, true>(wm, w2m, a, s);
     if (rc != LK_EUNSUPPORTED) return rc;
   }
   if (a.ids) {
