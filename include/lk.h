@@ -234,6 +234,17 @@ int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, i
                      lk_stream_t stream);
 int lk_moe_combine(int tokens, int h, int ku, int accumulate, const float* ys, const float* wts, float* y,
                    lk_stream_t stream);
+/* lk_moe_gate_up_routed: lk_moe_route (over the given logits) and lk_moe_expert_mv_ex mode 0 of ONE decode token in
+ * one launch (g_moe_route + g_moe_gu_{fmt}, gen_moe.py:116-253, 535-727): every CTA routes the token with the router's
+ * own code, then runs its gate/up expert rows; ids [ku] and wts [ku] receive the routing, bit for bit lk_moe_route's,
+ * and y [ku][f] = act(Wg[e] x + bias, Wu[e] x + bias2) as lk_moe_expert_mv_ex gives. logits [n_experts] f32,
+ * router_bias as lk_moe_route's (gating 2 / 3), x [h] of x_dtype; w / w2 / fused / biases as lk_moe_expert_mv_ex.
+ * Formats Q4_0, Q4_K, IQ4_NL with h % 256 == 0 and 16-byte aligned x and weights; n_experts <= 256, ku <= 8
+ * (LK_ERANGE beyond). A per-expert down scale (lk_moe_wscale) applies to wts afterwards as it does after the router. */
+int lk_moe_gate_up_routed(int fmt, int h, int f, int n_experts, int ku, int gating, int norm, float scale,
+                          const float* logits, const float* router_bias, const void* x, int x_dtype, const void* w,
+                          const void* w2, int fused, const float* bias, const float* bias2, int act, float alpha,
+                          float limit, int32_t* ids, float* wts, float* y, lk_stream_t stream);
 /* lk_moe_expert_mv_q8: the decode expert matvecs on int8 activations, g_moe_gu_{fmt}_q8 / g_moe_dn_{fmt}_q8
  * (MOE_Q8, gen_llm.py:5290-5302; gen_moe.py:535-727 with iq): xq is lk_quant_q8's output for the activation rows --
  * mode 0 (gu): the tokens' rows (assignment a reads row a / ku; assignments % ku == 0), y[a] = act(Wg[e] x, Wu[e] x)

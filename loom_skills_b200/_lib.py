@@ -38,6 +38,8 @@ SIGNATURES = {
     "lk_row_scale_f8": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _P]),
     "lk_mv": (_I, [_I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
     "lk_silu_mul": (_I, [_I, _I, _P, _P, _I, _P]),
+    "lk_moe_gate_up_routed": (_I, [_I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P, _P, _I, _P, _P, _I, _F, _F, _P,
+                                   _P, _P, _P]),
     "lk_moe_expert_mv_q8": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _F, _P, _P]),
     "lk_quant_q8": (_I, [_I, _I, _P, _I, _P, _P]),
     "lk_mv_q8": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P]),

@@ -296,6 +296,45 @@ int lk_moe_expert_mv_q8(int fmt, int mode, int n, int k, int assignments, int ku
                           limit, y, (cudaStream_t)stream);
 }
 
+int lk_moe_gate_up_routed(int fmt, int h, int f, int n_experts, int ku, int gating, int norm, float scale,
+                          const float* logits, const float* router_bias, const void* x, int x_dtype, const void* w,
+                          const void* w2, int fused, const float* bias, const float* bias2, int act, float alpha,
+                          float limit, int32_t* ids, float* wts, float* y, lk_stream_t stream) {
+  if (!q4_family(fmt)) return mv_format(fmt) ? LK_EUNSUPPORTED : LK_EINVAL;
+  if (h <= 0 || f <= 0 || n_experts <= 0 || ku <= 0 || h % 256) return LK_EINVAL;
+  if (gating < 1 || gating > 3 || !act_ok(act)) return LK_EINVAL;
+  if (n_experts > 256 || ku > 8 || ku > n_experts) return LK_ERANGE;
+  if (x_dtype != LK_F32 && x_dtype != LK_F16 && x_dtype != LK_BF16) return LK_EINVAL;
+  if (!logits || !x || !w || !ids || !wts || !y || (!fused && !w2)) return LK_EINVAL;
+  if ((!bias) != (!bias2)) return LK_EINVAL;
+  if (!aligned(x, 16) || !aligned(w, 16) || (!fused && !aligned(w2, 16))) return LK_EALIGN;
+  MvArgs a{};
+  a.w = (const uint8_t*)w;
+  a.w2 = fused ? (const uint8_t*)w : (const uint8_t*)w2;
+  a.x = x;
+  a.y = y;
+  a.n = f;
+  a.k = h;
+  a.tokens = ku;   // the token's assignments
+  a.x_dtype = x_dtype;
+  a.row_bytes = lk_row_bytes(fmt, h);
+  a.x_div = ku;
+  a.n_experts = n_experts;
+  a.rows_per_expert = fused ? 2 * f : f;
+  a.rows_per_expert2 = fused ? 2 * f : f;
+  a.w2_row_offset = fused ? f : 0;
+  a.swiglu = 1;
+  a.epi = ExpertEpi{bias, bias2, act, alpha, limit};
+  a.logits = logits;
+  a.rbias = router_bias;
+  a.ids_out = ids;
+  a.wts_out = wts;
+  a.gating = gating;
+  a.norm = norm;
+  a.rscale = scale;
+  return mv_routed(fmt, a, (cudaStream_t)stream);
+}
+
 int lk_moe_expert_mv(int fmt, int mode, int n, int k, int assignments, int ku, int n_experts, int fused,
                      const int32_t* ids, const void* x, int x_dtype, const void* w, const void* w2, float* y,
                      lk_stream_t stream) {

@@ -47,12 +47,22 @@ struct MvArgs {
   // gate and up in two formats (mv_generic with an LK_FMT_PAIR id fills these): the formats and the up rows' stride
   int fmt, fmt2;
   int64_t row_bytes2;
+  // the router folded into a one-token gate/up launch (mv_routed): the token's logits, router bias and settings;
+  // ids_out / wts_out receive the routing (n_experts experts, top x_div)
+  const float* logits;
+  const float* rbias;
+  int32_t* ids_out;
+  float* wts_out;
+  int gating, norm;
+  float rscale;
 };
 // f = act(f) * u over [tokens][n] f32 (lk_silu_mul)
 int act_mul(int tokens, int n, int act, float* f, const float* u, cudaStream_t s);
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s);
 // every decodable format and any k of whole blocks (lk_mvg.cu): exact f32 values x f32 activations
 int mv_generic(int fmt, const MvArgs& a, cudaStream_t s);
+// the router and the gate/up expert matvecs of one decode token in one launch (Q4 formats, tuned layout)
+int mv_routed(int fmt, const MvArgs& a, cudaStream_t s);
 
 // where a GEMM stores its tile: dst[d][row * ld + col_off + col] for d < ndst (at most 8)
 struct OutSpec {

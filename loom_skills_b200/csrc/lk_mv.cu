@@ -19,6 +19,7 @@
 
 #include "lk_common.cuh"
 #include "lk_internal.h"
+#include "lk_route.cuh"
 
 namespace lk {
 
@@ -424,7 +425,7 @@ constexpr int kRowsCons = 8;
 template <bool SWIGLU>
 constexpr int rows_stages() { return SWIGLU ? 2 : 3; }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER>
+template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER, bool ROUTE>
 __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
     k_mv_rows(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap w2map, MvArgs a) {
   constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
@@ -444,8 +445,22 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
   const int nrb = (a.n + kMvRows - 1) / kMvRows;           // 16-row blocks of one output row
   const int nblk = MOE ? a.tokens * nrb : nrb;              // MoE: a.tokens = assignments
   const int nstages = (kchunks + kRowsCons - 1) / kRowsCons;
+  // ROUTE: every CTA routes the token itself (one warp, the router's own code) before anything else; CTA 0 stores
+  // the routing for the launches after this one
+  __shared__ int32_t s_ids[8];
+  __shared__ float s_wts[8];
+  if (ROUTE && warp == 0) {
+    route_token(lane, a.n_experts, a.x_div, a.gating, a.norm, a.rscale, a.logits, a.rbias, s_ids, s_wts);
+    __syncwarp();
+    if (blockIdx.x == 0 && lane < a.x_div) {
+      a.ids_out[lane] = s_ids[lane];
+      a.wts_out[lane] = s_wts[lane];
+    }
+  }
   // block blk: its expert (MoE), first weight row in w and w2, first output row
-  auto expert_of = [&](int blk) { return MOE ? min(max(__ldg(a.ids + blk / nrb), 0), a.n_experts - 1) : 0; };
+  auto expert_of = [&](int blk) {
+    return MOE ? min(max(ROUTE ? s_ids[blk / nrb] : __ldg(a.ids + blk / nrb), 0), a.n_experts - 1) : 0;
+  };
   auto wrow_of = [&](int blk) { return expert_of(blk) * a.rows_per_expert + (blk % nrb) * kMvRows; };
   auto w2row_of = [&](int blk) {
     return expert_of(blk) * a.rows_per_expert2 + a.w2_row_offset + (blk % nrb) * kMvRows;
@@ -571,7 +586,7 @@ static int launch_mv(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
-template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER = false>
+template <int FMT, int XT, bool SWIGLU, bool MOE, bool XPER = false, bool ROUTE = false>
 static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, cudaStream_t s) {
   constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
   constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kXStride;
@@ -579,7 +594,7 @@ static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const M
   const int smem = NST * NW * kRowsCons * kMvChunkTile + 2 * NST * 8 + kRowsCons * NW * 16 * kAcStride * 8 +
                    kRowsCons * NW * 32 * 4 * 4 + kchunks * 8 * 4 + kchunks * kXT * 2;
   if (smem > 200 * 1024) return LK_EUNSUPPORTED;   // rows past ~40k values: the per-stage form below
-  auto kern = k_mv_rows<FMT, XT, SWIGLU, MOE, XPER>;
+  auto kern = k_mv_rows<FMT, XT, SWIGLU, MOE, XPER, ROUTE>;
   static int configured[32] = {};   // the largest shared-memory size set per device
   static std::mutex mu;
   int dev = 0, sms = 0;
@@ -637,6 +652,32 @@ static int mv_f(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, 
     case LK_F32: return mv_x<FMT, LK_F32>(wm, w2m, a, groups, s);
   }
   return LK_EINVAL;
+}
+
+template <int FMT>
+static int routed_f(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, cudaStream_t s) {
+  switch (a.x_dtype) {
+    case LK_F16: return launch_mv_rows<FMT, LK_F16, true, true, false, true>(wm, w2m, a, s);
+    case LK_BF16: return launch_mv_rows<FMT, LK_BF16, true, true, false, true>(wm, w2m, a, s);
+    case LK_F32: return launch_mv_rows<FMT, LK_F32, true, true, false, true>(wm, w2m, a, s);
+  }
+  return LK_EINVAL;
+}
+
+int mv_routed(int fmt, const MvArgs& a, cudaStream_t s) {
+  CUtensorMap wm, w2m;
+  int rc = make_map(&wm, a.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, int64_t(a.n_experts) * a.rows_per_expert,
+                    a.row_bytes / 4, kChunkBytes / 4, kMvRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == LK_OK)
+    rc = make_map(&w2m, a.w2, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, int64_t(a.n_experts) * a.rows_per_expert2,
+                  a.row_bytes / 4, kChunkBytes / 4, kMvRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc != LK_OK) return rc;
+  switch (fmt) {
+    case LK_Q4_0: return routed_f<LK_Q4_0>(wm, w2m, a, s);
+    case LK_Q4_K: return routed_f<LK_Q4_K>(wm, w2m, a, s);
+    case LK_IQ4_NL: return routed_f<LK_IQ4_NL>(wm, w2m, a, s);
+  }
+  return LK_EUNSUPPORTED;
 }
 
 int mv(int fmt, const MvArgs& a, int groups, cudaStream_t s) {

@@ -190,6 +190,24 @@ def moe_route(x, n_experts, ku, router_w=None, gating=1, norm=True, scale=1.0, b
     return ids, wts
 
 
+def moe_gate_up_routed(fmt, x, logits, w, n, n_experts, ku, fused=True, w2=None, gating=1, norm=True, scale=1.0,
+                       router_bias=None, act="silu", bias=None, bias2=None, alpha=1.702, limit=7.0):
+    """The router and the gate/up expert matvecs of one decode token in one launch (lk_moe_gate_up_routed): returns
+    (ids [1][ku], wts [1][ku], act [ku][n]) -- the routing bit for bit moe_route's, act as moe_expert_mv 'gu' gives."""
+    _cuda(x, logits, w, w2, router_bias, bias, bias2)
+    x = x.contiguous()
+    h = x.shape[1]
+    ids = torch.empty(1, ku, dtype=torch.int32, device=x.device)
+    wts = torch.empty(1, ku, dtype=torch.float32, device=x.device)
+    y = torch.empty(ku, n, dtype=torch.float32, device=x.device)
+    L.check(L.load().lk_moe_gate_up_routed(_fmt(fmt), h, n, n_experts, ku, gating, 1 if norm else 0, scale,
+                                           _ptr(logits.contiguous().float()), _ptr(_f32c(router_bias)), _ptr(x),
+                                           _DT[x.dtype], _ptr(w), _ptr(w2), 1 if fused else 0, _ptr(_f32c(bias)),
+                                           _ptr(_f32c(bias2)), _act(act), alpha, limit, _ptr(ids), _ptr(wts), _ptr(y),
+                                           _stream()), "lk_moe_gate_up_routed")
+    return ids, wts, y
+
+
 def moe_max_tiles(tokens, ku, n_experts):
     """Worst-case schedule size (gen_llm.py:5406-5411)."""
     a = tokens * ku
@@ -387,13 +405,27 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     x and the activations quantised to int8 codes (quant_q8) for the expert matvecs -- formats with integer codes,
     one format for gate and up, no biases."""
     tokens = x.shape[0]
-    ids, wts, sg = _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale,
-                                    shared_gate_w)
-    y, acc = _combine_out(tokens, h, x, y_shared)
     ep = dict(act=act, alpha=alpha, limit=limit)
     if prefill is None:
         prefill = tokens * ku >= 192
     fused = w_up is None
+    aligned = all(t is None or t.data_ptr() % 16 == 0 for t in (x, w_gu, w_up))
+    if (not prefill and not act_q8 and tokens == 1 and fmt in ("q4_0", "q4_k", "iq4_nl") and h % 256 == 0
+            and n_experts <= 256 and ku <= 8 and aligned and x.is_contiguous()):
+        # one decode token: the router folded into the gate/up launch
+        ids, wts, act_ = moe_gate_up_routed(fmt, x, logits, w_gu, f, n_experts, ku, fused=fused, w2=w_up,
+                                            gating=gating, norm=norm, scale=scale, router_bias=router_bias,
+                                            bias=b_gate, bias2=b_up, **ep)
+        if down_scale is not None:
+            moe_wscale(ids, wts, down_scale)
+        sg = moe_shared_gate(x.float(), shared_gate_w) if shared_gate_w is not None else None
+        y, acc = _combine_out(tokens, h, x, y_shared)
+        ys = moe_expert_mv(fmt_down or _gate_fmt(fmt), "dn", ids.reshape(-1), act_, w_dn, h, f, ku, n_experts,
+                           bias=b_down)
+        return moe_combine(ys, wts, y=y, accumulate=acc, sg=sg)
+    ids, wts, sg = _route_and_gates(x, logits, n_experts, ku, norm, gating, router_bias, scale, down_scale,
+                                    shared_gate_w)
+    y, acc = _combine_out(tokens, h, x, y_shared)
     if not prefill and act_q8:
         if b_gate is not None or b_up is not None or b_down is not None or "+" in str(fmt):
             raise L.LkError("the int8 expert matvecs take one gate/up format and no biases (gen_llm.py:5300-5302)")
