@@ -418,8 +418,8 @@ __global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 
 // Per row block the 8 consumer warps' partial sums meet in shared memory; warp 0 stores the 16 outputs.
 // MOE: per-assignment expert matvecs: the blocks are (assignment, 16-row block) pairs, each block's rows taken from
 // its assignment's expert, with the expert epilogue (biases, activation). The activation row is the one token's for
-// every assignment (the gate/up matvecs of one decode token), or with XPER the assignment's own row (the down
-// matvecs), converted again whenever a CTA's next block belongs to another assignment.
+// every assignment (the gate/up matvecs of one decode token), or with XPER row a / x_div of the assignment a (its
+// token's row for gate/up, its own for down), converted again whenever a CTA's next block needs another row.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRowsCons = 8;
 template <bool SWIGLU>
@@ -509,8 +509,8 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
   float2* actab = actab_all + warp * NW * 16 * kAcStride;
   int i = 0;
   for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
-    if (XPER && blk / nrb != staged) {   // the previous block's last bar.sync has every warp done with the old tiles
-      staged = blk / nrb;
+    if (XPER && (blk / nrb) / a.x_div != staged) {   // the previous block's last bar.sync has every warp done
+      staged = (blk / nrb) / a.x_div;                  // with the old tiles
       stage_row(staged);
     }
     float acc[NW][4];
@@ -628,7 +628,11 @@ static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, 
     const int rc = launch_mv_rows<FMT, XT, true, true>(wm, w2m, a, s);
     if (rc != LK_EUNSUPPORTED) return rc;
   }
-  if (a.ids && !a.swiglu && a.x_div == 1 && a.tokens <= 64) {   // the down matvecs at decode sizes: row a of x each
+  if (a.ids && a.swiglu && a.tokens <= 256) {   // gate/up of a few tokens: row a / ku of x
+    const int rc = launch_mv_rows<FMT, XT, true, true, true>(wm, w2m, a, s);
+    if (rc != LK_EUNSUPPORTED) return rc;
+  }
+  if (a.ids && !a.swiglu && a.x_div == 1 && a.tokens <= 256) {   // the down matvecs at decode sizes: row a of x
     const int rc = launch_mv_rows<FMT, XT, false, true, true>(wm, w2m, a, s);
     if (rc != LK_EUNSUPPORTED) return rc;
   }
