@@ -525,8 +525,9 @@ def bench_ep_moe(args, torch, dist, dev, world, rank, time_steps):
 
 
 def moe_path(ops, torch, lg, E, ku, m, expert_bytes, ms, matvec_below=64):
-    """Which pipeline a MoE layer of m tokens runs (Q4: GEMMs from 192 assignments; MXFP4: matvecs for at most 16
-    assignments), and for the matvecs the weight GB/s over the experts the routing touches."""
+    """Which pipeline a MoE layer of m tokens runs (Q4 on these shapes: expert matvecs up to 1024 assignments, grouped
+    by expert from 128; MXFP4: matvecs for at most 16 assignments), and for the matvecs the weight GB/s over the
+    experts the routing touches."""
     if m >= matvec_below:
         return {"path": "grouped GEMMs"}
     ids, _ = ops.moe_route(lg, E, ku)
@@ -563,12 +564,12 @@ def bench_moe(args, torch, dev, time_steps, pk):
     w_gu = synth_blocks(torch, dev, E * 2 * f, h, "q4_0", gen)
     w_dn = synth_blocks(torch, dev, E * h, f, "q4_0", gen)
     q = {}
-    for m in (1, 16, 256, 4096):
+    for m in (1, 16, 64, 256, 4096):
         pairs = moe_inputs(torch, dev, gen, m, h, E)
         ms = timed_layers(torch, time_steps, pairs, lambda x, lg: ops.moe_ffn("q4_0", x, lg, w_gu, w_dn, h, f, E, ku))
         q[str(m)] = {"ms": round(ms, 4), "tflops": round(2.0 * m * ku * 3 * h * f / (ms * 1e-3) / 1e12, 2),
                      "routings_per_step": len(pairs),
-                     **moe_path(ops, torch, pairs[0][1], E, ku, m, 3 * h * f * 18 // 32, ms, 192 // ku)}
+                     **moe_path(ops, torch, pairs[0][1], E, ku, m, 3 * h * f * 18 // 32, ms, 1024 // ku + 1)}
     out["q4_0_qwen3_30b"] = {"experts": E, "top_k": ku, "hidden": h, "intermediate": f, "by_tokens": q,
                              "data": "Q4_0 blocks synthesised on the device; bf16 N(0,1) x, N(0,1) logits"}
     del w_gu, w_dn

@@ -109,51 +109,71 @@ LK_DEV void bfrag(const __half* xt, int g, int kk, bool valid, uint32_t& b0, uin
   }
 }
 
+// A lane's 8 activations of a 256-value chunk as f32, from the raw words it loaded (f32: two uint4, else one).
+template <int XT>
+LK_DEV void x8_f32(const uint4* r, float (&f)[8]) {
+  if (XT == LK_F32) {
+    f[0] = __uint_as_float(r[0].x); f[1] = __uint_as_float(r[0].y);
+    f[2] = __uint_as_float(r[0].z); f[3] = __uint_as_float(r[0].w);
+    f[4] = __uint_as_float(r[1].x); f[5] = __uint_as_float(r[1].y);
+    f[6] = __uint_as_float(r[1].z); f[7] = __uint_as_float(r[1].w);
+  } else {
+    uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (XT == LK_BF16) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      } else {
+        float2 h = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
+        f[2 * i] = h.x;
+        f[2 * i + 1] = h.y;
+      }
+    }
+  }
+}
+
+// One token of a chunk: the lane's 8 f32 activations into the f16 tile (and, for f32, the residual tile) and the
+// token's per-group sums S[8].
+template <int XT>
+LK_DEV void put_x8(const float (&f)[8], int lane, __half* xt, __half* xl, float* S);
+
 // Convert this chunk's activations (ntok tokens x 256 values) to the f16 tile(s) and per-group sums S[t][8].
 template <int XT, int TOK>
 LK_DEV void stage_x(const uint8_t* xraw, int xraw_stride, int ntok, int lane, __half* xt, __half* xl, float* S) {
 #pragma unroll
   for (int t = 0; t < TOK; ++t) {
     if (t >= ntok) break;
+    constexpr int NR = XT == LK_F32 ? 2 : 1;
+    const uint4* p = reinterpret_cast<const uint4*>(xraw + t * xraw_stride) + NR * lane;
+    uint4 r[NR];
+#pragma unroll
+    for (int j = 0; j < NR; ++j) r[j] = p[j];
     float f[8];
-    if (XT == LK_F32) {
-      const float4* p = reinterpret_cast<const float4*>(xraw + t * xraw_stride) + 2 * lane;
-      float4 u = p[0], v = p[1];
-      f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w; f[4] = v.x; f[5] = v.y; f[6] = v.z; f[7] = v.w;
-    } else {
-      uint4 u = reinterpret_cast<const uint4*>(xraw + t * xraw_stride)[lane];
-      uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (XT == LK_BF16) {
-          f[2 * i] = __uint_as_float(w[i] << 16);
-          f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-        } else {
-          float2 h = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
-          f[2 * i] = h.x;
-          f[2 * i + 1] = h.y;
-        }
-      }
-    }
-    uint32_t hp[4], lp[4];
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-      hp[i] = h2u(h);
-      if (XT == LK_F32) {
-        float2 hf = __half22float2(h);
-        lp[i] = h2u(__floats2half2_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y));
-      }
-      s += f[2 * i] + f[2 * i + 1];
-    }
-    *reinterpret_cast<uint4*>(xt + t * kXStride + 8 * lane) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
-    if (XT == LK_F32)
-      *reinterpret_cast<uint4*>(xl + t * kXStride + 8 * lane) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    if ((lane & 3) == 0) S[t * 8 + (lane >> 2)] = s;   // group lane/4 of token t
+    x8_f32<XT>(r, f);
+    put_x8<XT>(f, lane, xt + t * kXStride, xl + t * kXStride, S + t * 8);
   }
+}
+
+template <int XT>
+LK_DEV void put_x8(const float (&f)[8], int lane, __half* xt, __half* xl, float* S) {
+  uint32_t hp[4], lp[4];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    hp[i] = h2u(h);
+    if (XT == LK_F32) {
+      float2 hf = __half22float2(h);
+      lp[i] = h2u(__floats2half2_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y));
+    }
+    s += f[2 * i] + f[2 * i + 1];
+  }
+  *reinterpret_cast<uint4*>(xt + 8 * lane) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+  if (XT == LK_F32) *reinterpret_cast<uint4*>(xl + 8 * lane) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if ((lane & 3) == 0) S[lane >> 2] = s;   // group lane/4
 }
 
 // One 256-value chunk of 16 rows (row r at rb + r*144, one TMA box) against the staged x tile.
@@ -419,7 +439,8 @@ __global__ void __launch_bounds__((CONS + 1) * 32, (SWIGLU && XT == LK_F32) ? 1 
 // MOE: per-assignment expert matvecs: the blocks are (assignment, 16-row block) pairs, each block's rows taken from
 // its assignment's expert, with the expert epilogue (biases, activation). The activation row is the one token's for
 // every assignment (the gate/up matvecs of one decode token), or with XPER row a / x_div of the assignment a (its
-// token's row for gate/up, its own for down), converted again whenever a CTA's next block needs another row.
+// token's row for gate/up, its own for down), each CTA then walking a contiguous range of blocks and converting the
+// row again where its range crosses into another assignment.
 // ---------------------------------------------------------------------------------------------------------------
 constexpr int kRowsCons = 8;
 template <bool SWIGLU>
@@ -445,6 +466,10 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
   const int nrb = (a.n + kMvRows - 1) / kMvRows;           // 16-row blocks of one output row
   const int nblk = MOE ? a.tokens * nrb : nrb;              // MoE: a.tokens = assignments
   const int nstages = (kchunks + kRowsCons - 1) / kRowsCons;
+  // blocks of this CTA: round-robin, or with XPER a contiguous range (fewer activation rows to restage)
+  const int b0 = XPER ? int(int64_t(blockIdx.x) * nblk / gridDim.x) : blockIdx.x;
+  const int b1 = XPER ? int(int64_t(blockIdx.x + 1) * nblk / gridDim.x) : nblk;
+  const int bstep = XPER ? 1 : gridDim.x;
   // ROUTE: every CTA routes the token itself (one warp, the router's own code) before anything else; CTA 0 stores
   // the routing for the launches after this one
   __shared__ int32_t s_ids[8];
@@ -478,7 +503,7 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
       prefetch_tensormap(&wmap);
       if (NW == 2) prefetch_tensormap(&w2map);
       int i = 0;
-      for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+      for (int blk = b0; blk < b1; blk += bstep) {
         const int wr = wrow_of(blk), w2r = NW == 2 ? w2row_of(blk) : 0;
         for (int st = 0; st < nstages; ++st, ++i) {
           const int s = i % NST;
@@ -508,7 +533,7 @@ __global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
   const int g = lane >> 2, tig = lane & 3;
   float2* actab = actab_all + warp * NW * 16 * kAcStride;
   int i = 0;
-  for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+  for (int blk = b0; blk < b1; blk += bstep) {
     if (XPER && (blk / nrb) / a.x_div != staged) {   // the previous block's last bar.sync has every warp done
       staged = (blk / nrb) / a.x_div;                  // with the old tiles
       stage_row(staged);
@@ -617,6 +642,243 @@ static int launch_mv_rows(const CUtensorMap& wm, const CUtensorMap& w2m, const M
   return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Expert-grouped form of the per-assignment expert matvecs (MoE decode at several tokens). The assignments are grouped
+// by expert, at most 8 to a group, so a 16-row block of an expert's weights is read once for all the assignments of
+// its group: the group's activation rows fill the MMA's 8 token columns, which the per-assignment form leaves empty.
+// Every CTA groups the assignments itself and deterministically (warp 0 in rounds of 32 over the assignments: counts
+// per expert, one scan, stable placement), so all CTAs see the same groups without scratch memory or another launch.
+// The work items are (group, 16-row block) pairs, a contiguous range of them per CTA, so a CTA restages the activation
+// tiles only where its range crosses into another group (the rows of a group loaded together, then converted). Each assignment's outputs are its own row y[a][n], computed by
+// the same chunk math as the per-assignment form (an MMA column depends on its own activations only).
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kGrpTok = 8;      // assignments of one group (the MMA's token columns)
+constexpr int kGrpMaxA = 1024;  // assignments one launch can group
+constexpr int kGrpMinA = 128;   // below this the per-assignment form measured faster (configs[2] shapes)
+template <int FMT, int XT, bool SWIGLU>
+__global__ void __launch_bounds__((kRowsCons + 1) * 32, SWIGLU ? 1 : 2)
+    k_mv_grp(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap w2map, MvArgs a) {
+  constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
+  constexpr int kWB = kRowsCons * kMvChunkTile;
+  constexpr int kStageBytes = NW * kWB;
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kGrpTok * kXStride;   // f16 elements of one chunk's x tiles
+  constexpr int XE = XT == LK_F32 ? 4 : 2;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * kStageBytes);
+  uint64_t* empty = full + NST;
+  float2* actab_all = reinterpret_cast<float2*>(empty + NST);                                  // [cons][NW][16][st]
+  float* red = reinterpret_cast<float*>(actab_all + kRowsCons * NW * 16 * kAcStride);        // [cons][NW][32][4]
+  float* S_all = red + kRowsCons * NW * 32 * 4;                                               // [kchunks][8][8]
+  const int kchunks = a.k / kChunkValues;
+  __half* xt_all = reinterpret_cast<__half*>(S_all + kchunks * kGrpTok * 8);                // [kchunks][kXT]
+  __shared__ int s_cnt[256];            // assignments per expert, then the placement cursor
+  __shared__ int s_order[kGrpMaxA];     // the assignments in (expert, assignment) order
+  __shared__ int s_grp[kGrpMaxA];       // group: expert | count << 8 | first place in s_order << 12
+  __shared__ int s_ngrp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int A = a.tokens, E = a.n_experts;
+  if (warp == 0) {
+    auto expert_at = [&](int i) { return i < A ? min(max(__ldg(a.ids + i), 0), E - 1) : -1; };
+    for (int e = lane; e < E; e += 32) s_cnt[e] = 0;
+    __syncwarp();
+    for (int b = 0; b < A; b += 32) {   // counts: the first lane of each expert's peers adds them
+      const int e = expert_at(b + lane);
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (peers & ((1u << lane) - 1)) == 0) s_cnt[e] += __popc(peers);
+      __syncwarp();
+    }
+    const int per = (E + 31) / 32;   // lane owns experts [lane * per, lane * per + per)
+    int pos = 0, grp = 0;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < E) {
+        pos += s_cnt[e];
+        grp += (s_cnt[e] + kGrpTok - 1) / kGrpTok;
+      }
+    }
+    int pinc = pos, ginc = grp;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int p = __shfl_up_sync(0xffffffffu, pinc, o), q = __shfl_up_sync(0xffffffffu, ginc, o);
+      if (lane >= o) {
+        pinc += p;
+        ginc += q;
+      }
+    }
+    int pb = pinc - pos, gb = ginc - grp;
+    if (lane == 31) s_ngrp = ginc;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < E) {
+        const int c = s_cnt[e];
+        for (int q = 0; q < c; q += kGrpTok) s_grp[gb++] = e | (min(kGrpTok, c - q) << 8) | ((pb + q) << 12);
+        s_cnt[e] = pb;
+        pb += c;
+      }
+    }
+    __syncwarp();
+    for (int b = 0; b < A; b += 32) {   // stable placement, in assignment order within each expert
+      const int e = expert_at(b + lane);
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << lane) - 1));
+      if (e >= 0) s_order[s_cnt[e] + rank] = b + lane;
+      __syncwarp();
+      if (e >= 0 && rank == 0) s_cnt[e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRowsCons);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int nrb = (a.n + kMvRows - 1) / kMvRows;
+  const int nitems = s_ngrp * nrb;
+  const int it0 = int(int64_t(blockIdx.x) * nitems / gridDim.x), it1 = int(int64_t(blockIdx.x + 1) * nitems / gridDim.x);
+  const int nstages = (kchunks + kRowsCons - 1) / kRowsCons;
+  if (warp == kRowsCons) {   // producer: stage (item, st) = chunks [8 st, 8 st + 8) of the item's 16 expert rows
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      if (NW == 2) prefetch_tensormap(&w2map);
+      int i = 0;
+      for (int it = it0; it < it1; ++it) {
+        const int e = s_grp[it / nrb] & 0xff, r0 = (it % nrb) * kMvRows;
+        const int wr = e * a.rows_per_expert + r0, w2r = e * a.rows_per_expert2 + a.w2_row_offset + r0;
+        for (int st = 0; st < nstages; ++st, ++i) {
+          const int s = i % NST;
+          if (i >= NST && !mbar_wait(&empty[s], ((i / NST) - 1) & 1)) atomicOr(&g_status, 1u);
+          const int c0 = st * kRowsCons, nch = min(kRowsCons, kchunks - c0);
+          mbar_expect_tx(&full[s], uint32_t(NW * nch * kMvChunkTile));
+          uint8_t* stg = smem + s * kStageBytes;
+          for (int c = 0; c < nch; ++c) {
+            tma_load_2d(stg + c * kMvChunkTile, &wmap, (c0 + c) * (kChunkBytes / 4), wr, &full[s]);
+            if (NW == 2)
+              tma_load_2d(stg + kWB + c * kMvChunkTile, &w2map, (c0 + c) * (kChunkBytes / 4), w2r, &full[s]);
+          }
+        }
+      }
+    }
+    return;
+  }
+  const int g = lane >> 2, tig = lane & 3;
+  float2* actab = actab_all + warp * NW * 16 * kAcStride;
+  int staged = -1, i = 0;
+  for (int it = it0; it < it1; ++it) {
+    const int gi = it / nrb, gw = s_grp[gi], e = gw & 0xff, ng = (gw >> 8) & 15, first = gw >> 12;
+    if (gi != staged) {   // the previous item's last bar.sync has every warp done with the old tiles
+      staged = gi;
+      constexpr int NR = XT == LK_F32 ? 2 : 1, TB = kGrpTok / NR;   // rows loaded together: 8 words per lane
+      for (int c = warp; c < kchunks; c += kRowsCons) {
+        __half* xt = xt_all + c * kXT;
+        for (int t0 = 0; t0 < ng; t0 += TB) {
+          uint4 r[TB][NR];
+#pragma unroll
+          for (int t = 0; t < TB; ++t)
+            if (t0 + t < ng) {
+              const int xrow = s_order[first + t0 + t] / a.x_div;
+              const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) +
+                                                              (int64_t(xrow) * a.k + int64_t(c) * 256) * XE) +
+                               NR * lane;
+#pragma unroll
+              for (int j = 0; j < NR; ++j) r[t][j] = __ldg(p + j);
+            }
+#pragma unroll
+          for (int t = 0; t < TB; ++t)
+            if (t0 + t < ng) {
+              const int u = t0 + t;
+              float f[8];
+              x8_f32<XT>(r[t], f);
+              put_x8<XT>(f, lane, xt + u * kXStride, xt + (kGrpTok + u) * kXStride, S_all + (c * kGrpTok + u) * 8);
+            }
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+    }
+    float acc[NW][4];
+#pragma unroll
+    for (int wi = 0; wi < NW; ++wi)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[wi][q] = 0.f;
+    for (int st = 0; st < nstages; ++st, ++i) {
+      const int s = i % NST;
+      if (!mbar_wait(&full[s], (i / NST) & 1)) atomicOr(&g_status, 1u);
+      const int c = st * kRowsCons + warp;
+      if (c < kchunks) {
+        const uint8_t* rb0 = smem + s * kStageBytes + warp * kMvChunkTile;
+        const __half* xt = xt_all + c * kXT;
+        mv_chunk<FMT, XT, NW, kGrpTok>(rb0, rb0 + kWB, xt, xt + kGrpTok * kXStride, S_all + c * kGrpTok * 8, g < ng,
+                                       g, tig, lane, actab, acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int wi = 0; wi < NW; ++wi)
+      *reinterpret_cast<float4*>(red + ((warp * NW + wi) * 32 + lane) * 4) =
+          make_float4(acc[wi][0], acc[wi][1], acc[wi][2], acc[wi][3]);
+    asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");
+    if (warp == 0) {   // element q: row g (q < 2) or g + 8, token column 2 tig + (q & 1)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = (it % nrb) * kMvRows + g + (q >= 2 ? 8 : 0), tok = 2 * tig + (q & 1);
+        float out[NW];
+#pragma unroll
+        for (int wi = 0; wi < NW; ++wi) {
+          float sum = 0.f;
+#pragma unroll
+          for (int w = 0; w < kRowsCons; ++w) sum += red[((w * NW + wi) * 32 + lane) * 4 + q];
+          out[wi] = sum;
+        }
+        if (row < a.n && tok < ng) {
+          if (a.epi.bias) {   // per-expert output biases (gen_moe.py:535 expert_mv bias=True)
+            out[0] += __ldg(a.epi.bias + int64_t(e) * a.n + row);
+            if (SWIGLU) out[NW - 1] += __ldg(a.epi.bias2 + int64_t(e) * a.n + row);
+          }
+          const float v = SWIGLU ? act_apply(a.epi.act, out[0], out[NW - 1], a.epi.alpha, a.epi.limit) : out[0];
+          float* yp = a.y + int64_t(s_order[first + tok]) * a.n + row;
+          *yp = a.accumulate ? *yp + v : v;
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kRowsCons * 32) : "memory");   // red and the x tiles are rewritten next
+  }
+}
+
+template <int FMT, int XT, bool SWIGLU>
+static int launch_mv_grp(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, cudaStream_t s) {
+  constexpr int NW = SWIGLU ? 2 : 1, NST = rows_stages<SWIGLU>();
+  constexpr int kXT = (XT == LK_F32 ? 2 : 1) * kGrpTok * kXStride;
+  const int kchunks = a.k / kChunkValues;
+  const int smem = NST * NW * kRowsCons * kMvChunkTile + 2 * NST * 8 + kRowsCons * NW * 16 * kAcStride * 8 +
+                   kRowsCons * NW * 32 * 4 * 4 + kchunks * kGrpTok * 8 * 4 + kchunks * kXT * 2;
+  if (smem > 200 * 1024 || a.n_experts > 256 || a.tokens > kGrpMaxA) return LK_EUNSUPPORTED;
+  auto kern = k_mv_grp<FMT, XT, SWIGLU>;
+  static int configured[32] = {};
+  static std::mutex mu;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 32) return LK_EUNSUPPORTED;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[dev] < smem) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return LK_ECUDA;
+      configured[dev] = smem;
+    }
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, (kRowsCons + 1) * 32, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  // at most min(A, E + A / 8) groups
+  const int max_items = min(a.tokens, a.n_experts + a.tokens / kGrpTok) * ((a.n + kMvRows - 1) / kMvRows);
+  kern<<<min(max_items, per_sm * sms), (kRowsCons + 1) * 32, smem, s>>>(wm, w2m, a);
+  return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ECUDA;
+}
+
 template <int FMT, int XT>
 static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, int groups, cudaStream_t s) {
   if (!a.ids && a.tokens == 1) {   // the decode step's shape: the persistent form where its shared memory fits
@@ -626,6 +888,10 @@ static int mv_x(const CUtensorMap& wm, const CUtensorMap& w2m, const MvArgs& a, 
   }
   if (a.ids && a.swiglu && a.x_div == a.tokens) {   // the gate/up expert matvecs of one token: all read x row 0
     const int rc = launch_mv_rows<FMT, XT, true, true>(wm, w2m, a, s);
+    if (rc != LK_EUNSUPPORTED) return rc;
+  }
+  if (a.ids && a.x_div < a.tokens && a.tokens >= kGrpMinA && a.tokens <= kGrpMaxA) {   // several tokens: by expert
+    const int rc = a.swiglu ? launch_mv_grp<FMT, XT, true>(wm, w2m, a, s) : launch_mv_grp<FMT, XT, false>(wm, w2m, a, s);
     if (rc != LK_EUNSUPPORTED) return rc;
   }
   if (a.ids && a.swiglu && a.tokens <= 256) {   // gate/up of a few tokens: row a / ku of x

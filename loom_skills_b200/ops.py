@@ -386,6 +386,17 @@ def _combine_out(tokens, h, x, y_shared):
     return torch.empty(tokens, h, dtype=torch.float32, device=x.device), False
 
 
+def _grouped_decode(fmt, fmt_down, x_dtype, h, f, n_experts):
+    """Whether the expert-grouped matvecs (lk_mv.cu k_mv_grp: up to 1024 assignments, grouped by expert inside the
+    launch) take both the gate/up and the down expert matvecs of a decode MoE layer: the tuned Q4 formats, at most 256
+    experts, and the staged activation rows within the kernel's shared memory (gate/up: h values of x; down: f of the
+    f32 activations)."""
+    q4 = ("q4_0", "q4_k", "iq4_nl")
+    if str(fmt) not in q4 or (fmt_down is not None and str(fmt_down) not in q4) or n_experts > 256:
+        return False
+    return h % 256 == 0 and f % 256 == 0 and h <= (2816 if x_dtype == torch.float32 else 5632) and f <= 3840
+
+
 def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=None, gating=1, router_bias=None,
             scale=1.0, act="silu", b_gate=None, b_up=None, b_down=None, down_scale=None, y_shared=None,
             shared_gate_w=None, alpha=1.702, limit=7.0, w_up=None, fmt_down=None, act_q8=False):
@@ -399,15 +410,17 @@ def moe_ffn(fmt, x, logits, w_gu, w_dn, h, f, n_experts, ku, norm=True, prefill=
     w_dn: per expert h rows of f values, in fmt_down when it differs from fmt (GGUF quants often keep ffn_down_exps in
     a wider format); fmt "gate+up" (e.g. "q4_k+q6_k", with w_up): gate and up experts in two formats, the down in
     fmt_down or the gate's; biases [n_experts][f] (gate, up) / [n_experts][h] (down). The reference
-    switches to the GEMMs at 64 tokens (gen_llm.py:6107); here from 192 assignments (tokens * ku), where they
-    measured faster on configs[2] shapes (top-8 of 128 experts: matvecs 209 / 388 us at 16 / 32 tokens, GEMMs 265 /
-    312 us). `prefill` forces either path. act_q8 (decode only; the reference's MOE_Q8 numerics, gen_llm.py:5290-5302):
+    switches to the GEMMs at 64 tokens (gen_llm.py:6107). Here the switch is at 192 assignments (tokens * ku), or at
+    1024 where the expert-grouped matvecs take both projections (Q4_0 / Q4_K / IQ4_NL experts, see _grouped_decode):
+    on configs[2] shapes (top-8 of 128 experts, bf16 x) those measured 143 / 191 / 224 / 314 us at 16 / 32 / 64 / 128
+    tokens against 291 / 351 / 394 / 396 us for the GEMMs. `prefill` forces either path. act_q8 (decode only; the reference's MOE_Q8 numerics, gen_llm.py:5290-5302):
     x and the activations quantised to int8 codes (quant_q8) for the expert matvecs -- formats with integer codes,
     one format for gate and up, no biases."""
     tokens = x.shape[0]
     ep = dict(act=act, alpha=alpha, limit=limit)
     if prefill is None:
-        prefill = tokens * ku >= 192
+        grouped = not act_q8 and _grouped_decode(fmt, fmt_down, x.dtype, h, f, n_experts)
+        prefill = tokens * ku > (1024 if grouped else 191)
     fused = w_up is None
     aligned = all(t is None or t.data_ptr() % 16 == 0 for t in (x, w_gu, w_up))
     if (not prefill and not act_q8 and tokens == 1 and fmt in ("q4_0", "q4_k", "iq4_nl") and h % 256 == 0

@@ -208,7 +208,8 @@ class GpuMoEBackend:
         r = x.shape[0]
         if r == 0:
             return torch.zeros(0, h, dtype=torch.float32, device=x.device)
-        if r < 192:   # decode-sized: per-row expert matvecs (the crossover ops.moe_ffn measured)
+        # decode-sized: per-row expert matvecs (the crossover ops.moe_ffn measured; grouped by expert up to 1024 rows)
+        if r < 192 or (r <= 1024 and ops._grouped_decode(self.fmt, None, x.dtype, h, f, n_local)):
             act = ops.moe_expert_mv(self.fmt, "gu", eids, x, w_gu, f, h, 1, n_local, fused=True)
             return ops.moe_expert_mv(self.fmt, "dn", eids, act, w_dn, h, f, 1, n_local)
         ti, rm, pos = ops.moe_bucket(eids.view(r, 1), n_local)
