@@ -207,7 +207,10 @@ int lk_moe_grouped_gemm_mxfp4s_f8(int mode, int order, int rows, int k, int n, i
  * lk_moe_combine_sorted: g_moe_combine_sorted (gen_moe.py:1231-1280), launch(%tokens, %rows, %ys, %pos, %wts, %y):
  *   y[t] (+)= sum_k wts[t][k] * ys[pos[t][k]] (pos < 0 -> 0).
  * lk_moe_expert_mv: decode expert matvecs g_moe_gu_{fmt} / g_moe_dn_{fmt} (gen_moe.py:535-727): mode 0 (gu):
- *   y[a] = silu(Wg[e] x[a/ku]) * (Wu[e] x[a/ku]); mode 1 (dn): y[a] = Wd[e] x[a]; e = ids[a].
+ *   y[a] = silu(Wg[e] x[a/ku]) * (Wu[e] x[a/ku]); mode 1 (dn): y[a] = Wd[e] x[a]; e = ids[a]. With Q4_0 / Q4_K /
+ *   IQ4_NL experts, 128 to 1024 assignments over at most 256 experts (several decode tokens), the launch groups the
+ *   assignments by expert and reads an expert's rows once for up to 8 of them; every y[a] is bit for bit the
+ *   per-assignment result, and no scratch memory is used.
  * The gate/up forms of both (expert_mv mode 0, grouped LK_SWIGLU / LK_SWIGLU_SORTED) take LK_FMT_PAIR(gate, up) with
  *   fused = 0: w the gate experts [n_experts][n] rows, w2 the up experts, each in its own format.
  * lk_moe_combine: g_moe_combine (gen_moe.py:730-762): y[t] (+)= sum_k wts[t][k] ys[t*ku + k].
