@@ -15,6 +15,10 @@
 //     Q4_0 / IQ4_NL: sum_k d v_k x_k = d * D;   Q4_K: sum_k (a q_k - c) x_k = a * D - c * S,   S = sum x_k
 // with a = d*sc, c = dmin*m per group. Centred codes keep D free of the cancellation a (1024 + q) offset would cause:
 // the f32 accumulation of exact codes is as precise as the reference's f32 dequant-then-dot (gen_llm.py:1281-1357).
+//
+// Kernels: k_mv (token tiles of up to 8, one CTA per 16 rows), k_mv_rows (persistent: one dense token, or MoE expert
+// matvecs per assignment, optionally with the router folded in), k_mv_grp (persistent: MoE expert matvecs of 128 to
+// 1024 assignments grouped by expert, 8 to the MMA's token columns). mv_x picks one by shape.
 #include <mutex>
 
 #include "lk_common.cuh"
